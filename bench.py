@@ -1,0 +1,263 @@
+"""Decode-throughput benchmark of the B200 backend (BASELINE metric: decode tok/s, Qwen3.5-style Q4_K_M).
+
+Workload: BASELINE config 3 (~2B-class hybrid, 28 layers = 21 Gated-DeltaNet + 7 gated GQA, E=2048,
+FFN 6144, vocab 151936, Q4_K_M with Q6_K head/embeddings), random-init N(0, 0.02) weights written as a
+synthetic GGUF from a fixed seed, a 512-token seeded prompt, greedy decode at batch 1 per sequence.
+A "step" is one greedy decode step of every sequence this rank owns (embedding lookup, 28 layers, LM
+head, on-device argmax). Multi-GPU (torchrun): each rank owns its own independent sequences on its own
+GPU (batch sharding, weak scaling, no collective on the data path).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Prints one JSON line (rank 0).
+"""
+from __future__ import annotations
+
+import argparse
+import importlib.util
+import json
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = pathlib.Path(__file__).resolve().parent
+PEAKS = ROOT / "MEASURED_PEAKS.json"
+FALLBACK_HBM_GBS = 6650.0
+METRIC = "decode tok/s at batch 1 & 64 (Qwen3.5-style Q4_K_M); GEMV HBM GB/s vs 8 TB/s"
+
+
+def load_pkg():
+    if "xjb200" in sys.modules:
+        return sys.modules["xjb200"]
+    spec = importlib.util.spec_from_file_location("xjb200", ROOT / "meta-work_b200" / "__init__.py",
+                                                  submodule_search_locations=[str(ROOT / "meta-work_b200")])
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules["xjb200"] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def dist_env():
+    return int(os.environ.get("RANK", 0)), int(os.environ.get("LOCAL_RANK", 0)), int(os.environ.get("WORLD_SIZE", 1))
+
+
+def hbm_peak():
+    try:
+        p = json.loads(PEAKS.read_text())
+        return float(p["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+class Clocks:
+    """nvidia-smi sampling during the timed region (SM clock, throttle reasons)."""
+
+    def __init__(self, gpu: int):
+        self.f = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+             "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+             "clocks_event_reasons.sw_power_cap")
+        try:
+            self.p = subprocess.Popen(["nvidia-smi", "-i", str(gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
+                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.p = None
+
+    def stop(self):
+        if self.p is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.p.terminate()
+        self.p.wait()
+        self.f.seek(0)
+        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        os.unlink(self.f.name)
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v.strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def step_bytes(cfg, pos: int, kv_bytes: int = 2) -> dict:
+    """Algorithmic HBM bytes of one batch-1 decode step at KV length `pos` (weights of all layers and the
+    head read once, KV cache read + one position written, GDN + conv state read + written)."""
+    from xjb200 import synth
+    E, FF, V, L = cfg.n_embd, cfg.n_ff, cfg.n_vocab, cfg.n_layer
+    H, Hkv, D = cfg.n_head, cfg.n_head_kv, cfg.head_dim
+    S, Hk, Hv = cfg.s_k, cfg.h_k, cfg.h_v
+    DI, KD = Hv * S, Hk * S
+    CD = 2 * KD + DI
+    bpw = {synth.Q4_K: 144 / 256, synth.Q6_K: 210 / 256, synth.Q8_0: 34 / 32, synth.F32: 4}
+
+    def more_bits(i):
+        return i < L // 8 or i >= 7 * L // 8 or (i - L // 8) % 3 == 2
+
+    w = 0.0
+    n_full = 0
+    for i in range(L):
+        down_t = synth.Q6_K if (cfg.wtype == synth.Q4_K and more_bits(i)) else cfg.wtype
+        w += (2 * E * FF) * bpw[cfg.wtype] + FF * E * bpw[down_t] + 2 * E * 4
+        if (i + 1) % cfg.full_attn_interval:
+            w += (E * CD + E * DI + 2 * E * Hv + DI * E) * bpw[cfg.wtype] + (CD * cfg.conv_k + 3 * Hv + S) * 4
+        else:
+            n_full += 1
+            v_t = synth.Q6_K if (cfg.wtype == synth.Q4_K and more_bits(i)) else cfg.wtype
+            w += (E * 2 * H * D + E * Hkv * D + H * D * E) * bpw[cfg.wtype] + E * Hkv * D * bpw[v_t] + 2 * D * 4
+    io_t = synth.Q6_K if cfg.wtype == synth.Q4_K else cfg.wtype
+    head = E * V * bpw[io_t] + E * 4 + E * bpw[io_t]
+    kv = n_full * 2 * Hkv * D * kv_bytes * (pos + 1)
+    n_rec = L - n_full
+    state = n_rec * (2 * Hv * S * S * 4 + 2 * CD * (cfg.conv_k - 1) * 4)
+    return {"weights": w + head, "kv": kv, "state": state, "total": w + head + kv + state}
+
+
+def run_reference(args, rank, world):
+    """--impl reference: the reference CPU path (oracle/_ref, the reference's own core/*.c) on the host cores."""
+    if rank != 0:
+        return
+    from xjb200 import synth
+    sys.path.insert(0, str(ROOT))
+    from oracle import ref
+    if not ref.available():
+        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libxjref.so was not built"}))
+        return
+    cfg = synth.CONFIG3
+    path = synth.cached_gguf(cfg)
+    m = ref.Model(path)
+    threads = os.cpu_count() or 1
+    ref.set_threads(threads)
+    n_prompt = 32
+    K = min(args.steps, 48)
+    p = np.random.default_rng(1234).integers(0, cfg.n_vocab, n_prompt)
+    m.greedy(p, 2, max_batch=8, n_ctx=2048)                         # warm-up: pages the weights in
+    _, _, _, times = m.greedy(p, K + 1, max_batch=8, n_ctx=2048)
+    v = K / times[1]
+    sample = f"{cfg.name}: {n_prompt}-token prompt, {K} greedy decode steps at batch 1, {threads} threads"
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": world,
+        "steps": K, "warmup": args.warmup, "ms_per_step": round(1e3 / v, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": cfg.name + " decode, batch 1", "prompt": n_prompt, "batch": 1},
+        "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample},
+        "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }))
+
+
+def cpu_baseline(K_cap=24):
+    """Reference CPU path timed on this host on a bounded sample of the workload."""
+    from xjb200 import synth
+    sys.path.insert(0, str(ROOT))
+    from oracle import ref
+    if not ref.available():
+        return None
+    cfg = synth.CONFIG3
+    m = ref.Model(synth.cached_gguf(cfg))
+    threads = os.cpu_count() or 1
+    ref.set_threads(threads)
+    p = np.random.default_rng(1234).integers(0, cfg.n_vocab, 32)
+    _, _, _, times = m.greedy(p, K_cap + 1, max_batch=8, n_ctx=2048)
+    v = K_cap / times[1]
+    return {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "reference",
+            "sample": f"{cfg.name}: 32-token prompt, {K_cap} greedy decode steps at batch 1 (oracle/_ref, {threads} threads)"}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=8)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--prompt", type=int, default=512)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    rank, local, world = dist_env()
+    load_pkg()
+    if args.impl == "reference":
+        return run_reference(args, rank, world)
+
+    import torch
+    torch.cuda.set_device(local)
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=torch.device("cuda", local))
+    from xjb200 import synth, xjcuda
+    cfg = synth.CONFIG3
+    path = synth.cached_gguf(cfg, os.environ.get("XJ_MODEL_DIR", f"/tmp/xj_models_r{local}"))
+    model = xjcuda.Model(path)
+    n_ctx = args.prompt + args.warmup + args.steps + 8
+    stage = xjcuda.Stage(model, 0, model.n_layer, n_ctx, 8)
+    prompt = np.random.default_rng(1234 + rank).integers(0, cfg.n_vocab, args.prompt).astype(np.int32)
+
+    def barrier():
+        torch.cuda.synchronize()
+        if world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+
+    # prefill + warm-up decode steps (untimed)
+    toks, _, _ = stage.decode(prompt, max(args.warmup, 3))
+    last = toks[-1:]
+    pos0 = stage.n_past
+    # timed region: exactly K decode steps, device-timed with CUDA events on the stage stream
+    barrier()
+    clocks = Clocks(local)
+    toks, _, ms = stage.decode(last, args.steps)
+    barrier()
+    clk = clocks.stop()
+    dev_ms = float(ms[0] + ms[1])
+    last = toks[-1:]
+    # end to end through the public C ABI with host buffers (token ids in, ids out), host wall clock
+    barrier()
+    t0 = time.perf_counter()
+    toks2, _, _ = stage.decode(last, args.steps)
+    torch.cuda.synchronize()
+    e2e_ms = (time.perf_counter() - t0) * 1e3
+    t_max = dev_ms
+    e2e_max = e2e_ms
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([dev_ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_max, e2e_max = float(t[0]), float(t[1])
+    value = world * args.steps / (t_max / 1e3)
+    e2e = world * args.steps / (e2e_max / 1e3)
+    kernels = int(xjcuda.lib().xj_cuda_graph_kernels(stage.addr)) if hasattr(xjcuda.lib(), "xj_cuda_graph_kernels") else None
+    if rank == 0:
+        peak, peak_kind = hbm_peak()
+        b = step_bytes(cfg, pos0 + args.steps // 2)
+        achieved = b["total"] / (t_max / args.steps / 1e3) / 1e9
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(t_max / args.steps, 4), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "q4_k/q6_k weights, f32 accumulate", "data": "synthetic",
+            "config": {"workload": f"{cfg.name} greedy decode, batch 1 per GPU", "prompt": args.prompt,
+                       "batch_per_gpu": 1, "kv_cache": "f16", "parallelism": f"batch-shard x{world}",
+                       "l2": "weights 1.2 GB per step > 126 MB L2"},
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": round(4 / args.steps, 3),
+                    "d2h_bytes_per_step": 4},
+            "roofline": {"bound": "hbm", "kernel": "whole decode step", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                         "bytes_per_step": round(b["total"]), "peak_kind": peak_kind},
+            "clocks": clk,
+            "gpu_launches": kernels * args.steps if kernels else None,
+            "tokens_check": int(toks[0]),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline()
+        print(json.dumps(line))
+    stage.close()
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,69 @@
+// B200 (sm_100a) CUDA backend for the xiaoju-pipe decode loop: public C ABI of libxj_cuda.so.
+//
+// Drop-in entry points (same signature and semantics as the runtime's other backends):
+//
+//   xj_cuda_stage_new      replaces xj_metal_stage_new / xj_cpu_stage_new
+//                          (src/xiaoju-pipe/core/xj_stage.h:42-47; Metal: metal/xj_metal.m:554-664,
+//                          CPU: core/xj_cpu.c:375-418). Returns an xj_stage whose function pointers
+//                          (forward, logits, rollback, reset, destroy) follow core/xj_stage.h:28-37.
+//   xj_cuda_device_name    replaces xj_metal_device_name (core/xj_stage.h:48).
+//   xjc_model_load / xjc_model_free / xjc_embed / xjc_stage_state_bytes
+//                          a loader and helpers with the semantics of xj_model_load
+//                          (core/xj_model.c:204-210), xj_model_free (:289-294), xj_embed
+//                          (core/xj_cpu.c:369-373) and xj_stage_state_bytes (core/xj_cpu.c:356-367),
+//                          for hosts that do not link the runtime's own core/. Models from either
+//                          loader are accepted by xj_cuda_stage_new (same struct layout, xj_abi.h).
+//
+// Additive extensions (no counterpart in the reference; the vtable is unchanged):
+//
+//   xj_cuda_decode         device-resident greedy decode on a full-model stage: token ids in, token
+//                          ids out; embedding lookup, all layers, the LM head and the argmax run on
+//                          the GPU and one decode step is replayed as a CUDA graph.
+//   xj_cuda_set_options    backend switches (KV-cache precision, GEMV path) for tests.
+//
+// Error convention (as the runtime's): functions return 0 (or a pointer) on success and -1 (or
+// NULL) on failure with a NUL-terminated message in err[errlen]. A stage is single-threaded; it runs
+// on the CUDA device that was current when it was created.
+#pragma once
+#include "xj_abi.h"
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+xj_stage *xj_cuda_stage_new(const xj_model *m, int l0, int l1, int n_ctx, int max_batch, bool has_head,
+                            char *err, size_t errlen);
+const char *xj_cuda_device_name(void);
+
+xj_model *xjc_model_load(const char *path, char *err, size_t errlen);
+void xjc_model_free(xj_model *m);
+void xjc_embed(const xj_model *m, int32_t token, float *out);
+uint64_t xjc_stage_state_bytes(const xj_model *m, int l0, int l1, int n_ctx, int max_batch);
+
+// Options (process-wide, read when a stage is created):
+//   XJC_OPT_KV_F32   1 = float32 KV cache (matches the CPU oracle's cache), 0 = float16 (default,
+//                    the Metal backend's and the BASELINE precision).
+//   XJC_OPT_GEMV     0 = fastest path per type (default), 1 = generic per-element path for every type.
+enum { XJC_OPT_KV_F32 = 1, XJC_OPT_GEMV = 2 };
+int xj_cuda_set_options(int which, int value);
+
+// Greedy decode on a stage covering [0, n_layer) with the head. Feeds n_prompt ids (prefill in
+// chunks of max_batch, continuing from the stage's n_past), then emits n_gen ids into out (out[0] is
+// the argmax after the prompt). Each emitted id except the last is fed back, so the stage's n_past
+// grows by n_prompt + n_gen - 1. margins (may be NULL) receives each step's top-2 logit gap.
+// gpu_ms (may be NULL) receives [prefill ms, decode ms] measured with CUDA events on the stage stream.
+int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, int32_t *out, float *margins,
+                   float *gpu_ms, char *err, size_t errlen);
+
+// Number of kernel launches in one replay of the stage's cached decode-step graph (0 before the first
+// xj_cuda_decode call that generated more than one token).
+int xj_cuda_graph_kernels(const xj_stage *s);
+
+// Dequantise n_rows rows of k elements of GGUF type `type` (host bytes in, host fp32 out) with the
+// device decoder the GEMV kernels use; for checking bit-exactness against xj_dequant_row
+// (core/xj_quant.h:55-122). Runs on the current device.
+int xj_cuda_dequant_rows(int type, const void *src, int k, int n_rows, float *out, char *err, size_t errlen);
+
+#ifdef __cplusplus
+}
+#endif

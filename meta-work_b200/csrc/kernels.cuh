@@ -1,0 +1,362 @@
+// Layer kernels of the xj CUDA backend (everything except the fast GEMV paths, gemv_mma.cuh).
+//
+// Token positions are read from device memory (*npast), so a decode step does not depend on any
+// host-side scalar and can be captured once as a CUDA graph and replayed.
+#pragma once
+#include "common.cuh"
+
+namespace xjk {
+
+constexpr int MAXT = 16;   // tokens per forward handled by the CUDA-core GEMV
+
+// ---------------------------------------------------------------- dequant / embed
+// out[r][K] = rows [row0, row0+nrows) of W in fp32 (bit-exact with core/xj_quant.h).
+__global__ void k_dequant(DevMat w, int row0, int nrows, float *out) {
+    const long long total = (long long)nrows * (w.K / 8);
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
+        const int r = (int)(i / (w.K / 8)), e0 = (int)(i % (w.K / 8)) * 8;
+        float y[8];
+        dequant8(w.type, w.p + (row0 + r) * w.ld, e0, y);
+        float *o = out + (size_t)r * w.K + e0;
+#pragma unroll
+        for (int l = 0; l < 8; l++) o[l] = y[l];
+    }
+}
+
+// x[t] = row tok[t] of the embedding table; out-of-range ids give zeros (core/xj_cpu.c:369-373).
+__global__ void k_embed(DevMat w, const int32_t *tok, int T, float *x, int ldx) {
+    const int t = blockIdx.y;
+    if (t >= T) return;
+    const int id = tok[t];
+    for (int e0 = (blockIdx.x * blockDim.x + threadIdx.x) * 8; e0 < w.K; e0 += gridDim.x * blockDim.x * 8) {
+        float y[8];
+        if (id >= 0 && id < w.N) dequant8(w.type, w.p + id * w.ld, e0, y);
+        else {
+#pragma unroll
+            for (int l = 0; l < 8; l++) y[l] = 0.0f;
+        }
+#pragma unroll
+        for (int l = 0; l < 8; l++) x[(size_t)t * ldx + e0 + l] = y[l];
+    }
+}
+
+// ---------------------------------------------------------------- norms
+// y[r] = x[r] * w / sqrt(mean(x[r]^2) + eps), sum in double (core/xj_cpu.c:56-61). One block per row.
+__global__ void k_rmsnorm(const float *x, long long ldx, const float *w, float *y, long long ldy, int n, float eps) {
+    __shared__ double red[32];
+    const float *xr = x + blockIdx.x * ldx;
+    float *yr = y + blockIdx.x * ldy;
+    double ss = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) ss += (double)xr[i] * xr[i];
+    ss = block_sum_d(ss, red);
+    const float sc = 1.0f / sqrtf((float)(ss / n) + eps);
+    for (int i = threadIdx.x; i < n; i += blockDim.x) yr[i] = xr[i] * sc * (w ? w[i] : 1.0f);
+}
+
+// ---------------------------------------------------------------- generic GEMV
+// y[t][r] (+)= dot(W[r], x[t]) for up to 4 matrices sharing the input x[T][K]: one warp per row,
+// each lane dequantises 8 consecutive elements at a time with the reference formulas and keeps T fp32
+// partial sums. Used for every type when XJC_OPT_GEMV=1 and for the small/odd types otherwise.
+struct GemvJob {
+    DevMat w;
+    float *y;
+    long long ldy;       // floats between tokens in y
+    int accumulate;      // y += W x (residual add, core/xj_cpu.c:268,275)
+};
+struct GemvArgs {
+    GemvJob job[4];
+    int njob;
+    int row_start[5];    // prefix sums of rows over jobs
+    const float *x;
+    long long ldx;
+    int T;
+};
+
+__global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a) {
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int grow = blockIdx.x * 8 + warp;
+    if (grow >= a.row_start[a.njob]) return;
+    int j = 0;
+    while (grow >= a.row_start[j + 1]) j++;
+    const GemvJob &jb = a.job[j];
+    const int r = grow - a.row_start[j];
+    const int K = jb.w.K, T = a.T;
+    const uint8_t *row = jb.w.p + r * jb.w.ld;
+    float acc[MAXT];
+#pragma unroll
+    for (int t = 0; t < MAXT; t++) acc[t] = 0.0f;
+    for (int e0 = lane * 8; e0 < K; e0 += 256) {
+        float wv[8];
+        dequant8(jb.w.type, row, e0, wv);
+#pragma unroll
+        for (int t = 0; t < MAXT; t++) {
+            if (t < T) {
+                const float4 *xp = reinterpret_cast<const float4 *>(a.x + t * a.ldx + e0);
+                float4 x0 = __ldg(xp), x1 = __ldg(xp + 1);
+                float s = acc[t];
+                s = fmaf(wv[0], x0.x, s); s = fmaf(wv[1], x0.y, s); s = fmaf(wv[2], x0.z, s); s = fmaf(wv[3], x0.w, s);
+                s = fmaf(wv[4], x1.x, s); s = fmaf(wv[5], x1.y, s); s = fmaf(wv[6], x1.z, s); s = fmaf(wv[7], x1.w, s);
+                acc[t] = s;
+            }
+        }
+    }
+#pragma unroll
+    for (int t = 0; t < MAXT; t++) {
+        if (t < T) {
+            float s = warp_sum(acc[t]);
+            if (lane == 0) {
+                float *yp = jb.y + t * jb.ldy + r;
+                *yp = jb.accumulate ? *yp + s : s;
+            }
+        }
+    }
+}
+
+// ---------------------------------------------------------------- Gated DeltaNet
+// Causal depthwise conv (kernel KC) with a rolling state, then SiLU, in place on qkv[T][CD]
+// (core/xj_cpu.c:172-182). One thread per channel, tokens in order. With ck != nullptr the state
+// after token t (t < T-1) is saved to ck[t][CD][KC-1] (core/xj_cpu.c:220).
+__global__ void k_conv_silu(float *qkv, long long ldq, int T, int CD, int KC, float *state, const float *cw, float *ck) {
+    const int c = blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= CD) return;
+    float cs[8];
+    const float *wc = cw + (size_t)c * KC;
+    for (int k = 0; k < KC - 1; k++) cs[k] = state[(size_t)c * (KC - 1) + k];
+    for (int t = 0; t < T; t++) {
+        float *xp = qkv + t * ldq + c;
+        float acc = 0.0f;
+        for (int k = 0; k < KC - 1; k++) acc = fmaf(cs[k], wc[k], acc);
+        acc = fmaf(*xp, wc[KC - 1], acc);
+        for (int k = 0; k < KC - 2; k++) cs[k] = cs[k + 1];
+        cs[KC - 2] = *xp;
+        *xp = silu_f(acc);
+        if (ck && t < T - 1)
+            for (int k = 0; k < KC - 1; k++) ck[((size_t)t * CD + c) * (KC - 1) + k] = cs[k];
+    }
+    for (int k = 0; k < KC - 1; k++) state[(size_t)c * (KC - 1) + k] = cs[k];
+}
+
+// One block per value head hv, S threads; thread j owns row j of the head's state M (value dim j,
+// S key dims) in registers for all T tokens (core/xj_cpu.c:194-219):
+//   q, k <- L2-normalised key head hv % Hk;  b = sigmoid(beta);  g = softplus(alpha + dt) * A
+//   M *= exp(g);  delta_j = (v_j - M_j.k) * b;  M_j += delta_j k;  o_j = M_j.q / sqrt(S)
+//   out = rmsnorm(o) * norm_w * silu(z)
+// State layout [Hv][S(j)][S(i)] as the CPU oracle. ck_ssm != nullptr saves M after token t < T-1.
+template <int S>
+__global__ void __launch_bounds__(S < 32 ? 32 : S) k_gdn(const float *qkv, long long ldq, const float *z, long long ldz,
+                                                         const float *beta, const float *alpha, long long ldg,
+                                                         const float *dt, const float *A, const float *nw,
+                                                         float *ssm, float *ck_ssm, float *out, long long ldo,
+                                                         int T, int Hk, int Hv, int key_dim, float eps) {
+    __shared__ float qs[S], ks[S];
+    __shared__ double red[32];
+    const int hv = blockIdx.x, hk = hv % Hk, j = threadIdx.x;
+    const bool active = j < S;
+    float row[S];
+    float *M = ssm + (size_t)hv * S * S;
+    if (active) {
+#pragma unroll
+        for (int i = 0; i < S; i++) row[i] = M[(size_t)j * S + i];
+    }
+    const float qscale = 1.0f / sqrtf((float)S);
+    for (int t = 0; t < T; t++) {
+        const float *x = qkv + t * ldq;
+        float qv = active ? x[hk * S + j] : 0.0f, kv = active ? x[key_dim + hk * S + j] : 0.0f;
+        double sq = block_sum_d((double)qv * qv, red);
+        double sk2 = block_sum_d((double)kv * kv, red);
+        if (active) {
+            qs[j] = qv * (1.0f / sqrtf((float)sq + eps));
+            ks[j] = kv * (1.0f / sqrtf((float)sk2 + eps));
+        }
+        __syncthreads();
+        const float b = sigm_f(beta[t * ldg + hv]);
+        const float g = softplus_f(alpha[t * ldg + hv] + dt[hv]) * A[hv];
+        const float eg = expf(g);
+        float o = 0.0f;
+        if (active) {
+            const float vj = x[2 * key_dim + hv * S + j];
+            float sk = 0.0f;
+#pragma unroll
+            for (int i = 0; i < S; i++) { row[i] *= eg; sk = fmaf(row[i], ks[i], sk); }
+            const float delta = (vj - sk) * b;
+            float acc = 0.0f;
+#pragma unroll
+            for (int i = 0; i < S; i++) { row[i] = fmaf(ks[i], delta, row[i]); acc = fmaf(row[i], qs[i], acc); }
+            o = acc * qscale;
+        }
+        double so = block_sum_d((double)o * o, red);
+        if (active) {
+            const float sc = 1.0f / sqrtf((float)(so / S) + eps);
+            const float zj = z[t * ldz + hv * S + j];
+            out[t * ldo + hv * S + j] = o * sc * nw[j] * silu_f(zj);
+            if (ck_ssm && t < T - 1) {
+                float *C = ck_ssm + ((size_t)t * Hv + hv) * S * S + (size_t)j * S;
+#pragma unroll
+                for (int i = 0; i < S; i++) C[i] = row[i];
+            }
+        }
+        __syncthreads();
+    }
+    if (active) {
+#pragma unroll
+        for (int i = 0; i < S; i++) M[(size_t)j * S + i] = row[i];
+    }
+}
+
+// ---------------------------------------------------------------- gated full attention
+// Per token t and head slot: q heads get RMSNorm(q_norm) + NeoX RoPE into qrot[t][h][D]; KV heads get
+// RMSNorm(k_norm) + RoPE and are stored with v at position npast+t (core/xj_cpu.c:107-116).
+// Grid (H + Hkv, T), D threads.
+template <typename KV>
+XJ_DEV void store_kv(KV *p, float v);
+template <> XJ_DEV void store_kv<float>(float *p, float v) { *p = v; }
+template <> XJ_DEV void store_kv<__half>(__half *p, float v) { *p = __float2half_rn(v); }
+XJ_DEV float load_kv(const float *p) { return *p; }
+XJ_DEV float load_kv(const __half *p) { return __half2float(*p); }
+
+template <typename KV>
+__global__ void k_attn_prep(const float *q, long long ldq, const float *k, const float *v, long long ldkv,
+                            const float *qn, const float *kn, float *qrot, KV *kc, KV *vc, const int *npast,
+                            int H, int Hkv, int D, int n_rot, float base, float eps) {
+    extern __shared__ float sh[];
+    __shared__ double red[32];
+    const int t = blockIdx.y, slot = blockIdx.x, i = threadIdx.x;
+    const int pos = *npast + t;
+    const bool isq = slot < H;
+    const int hh = isq ? slot : slot - H;
+    const float *src = isq ? q + t * ldq + (size_t)hh * 2 * D : k + t * ldkv + (size_t)hh * D;
+    const float xi = i < D ? src[i] : 0.0f;
+    double ss = block_sum_d((double)xi * xi, red);
+    const float sc = 1.0f / sqrtf((float)(ss / D) + eps);
+    const float *nw = isq ? qn : kn;
+    if (i < D) sh[i] = xi * sc * nw[i];
+    __syncthreads();
+    float r = i < D ? sh[i] : 0.0f;
+    const int half = n_rot / 2;
+    if (i < n_rot) {
+        const int p = i < half ? i : i - half;
+        const float theta = (float)pos * powf(base, -2.0f * (float)p / (float)n_rot);
+        const float c = cosf(theta), s = sinf(theta);
+        const float x0 = sh[p], x1 = sh[p + half];
+        r = i < half ? x0 * c - x1 * s : x0 * s + x1 * c;
+    }
+    if (i < D) {
+        if (isq) qrot[((size_t)t * H + hh) * D + i] = r;
+        else {
+            const size_t o = (size_t)pos * Hkv * D + (size_t)hh * D + i;
+            store_kv<KV>(kc + o, r);
+            store_kv<KV>(vc + o, v[t * ldkv + (size_t)hh * D + i]);
+        }
+    }
+}
+
+// Attention of query (t, h) over positions 0..npast+t of its KV head, online softmax, then the
+// sigmoid output gate: out[t][h*D + i] = (sum_j p_j v_j[i]) * sigmoid(gate[i]) (core/xj_cpu.c:118-150).
+// One block of 4 warps per (h, t); lanes split the head dim (D <= 256, D % 32 == 0).
+template <typename KV, int DPL>
+__global__ void __launch_bounds__(128) k_attn(const float *qrot, const float *qg, long long ldq, const KV *kc, const KV *vc,
+                                              const int *npast, float *out, long long ldo, int H, int Hkv, int D) {
+    __shared__ float sm_m[4], sm_l[4];
+    __shared__ float sm_o[4][256];
+    const int h = blockIdx.x, t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int n = *npast + t + 1, kvh = h / (H / Hkv), kvd = Hkv * D;
+    const float scale = 1.0f / sqrtf((float)D);
+    float qv[DPL], o[DPL];
+    const float *qp = qrot + ((size_t)t * H + h) * D;
+#pragma unroll
+    for (int d = 0; d < DPL; d++) { qv[d] = qp[lane * DPL + d]; o[d] = 0.0f; }
+    float m = -INFINITY, l = 0.0f;
+    for (int j = warp; j < n; j += 4) {
+        const KV *kr = kc + (size_t)j * kvd + (size_t)kvh * D + lane * DPL;
+        float s = 0.0f;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) s = fmaf(qv[d], load_kv(kr + d), s);
+        s = warp_sum(s) * scale;
+        const float mn = fmaxf(m, s);
+        const float corr = expf(m - mn), p = expf(s - mn);
+        l = l * corr + p;
+        const KV *vr = vc + (size_t)j * kvd + (size_t)kvh * D + lane * DPL;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) o[d] = fmaf(p, load_kv(vr + d), o[d] * corr);
+        m = mn;
+    }
+    if (lane == 0) { sm_m[warp] = m; sm_l[warp] = l; }
+#pragma unroll
+    for (int d = 0; d < DPL; d++) sm_o[warp][lane * DPL + d] = o[d];
+    __syncthreads();
+    if (warp == 0) {
+        float M = fmaxf(fmaxf(sm_m[0], sm_m[1]), fmaxf(sm_m[2], sm_m[3]));
+        float L = 0.0f, c[4];
+#pragma unroll
+        for (int w = 0; w < 4; w++) { c[w] = sm_m[w] == -INFINITY ? 0.0f : expf(sm_m[w] - M); L += sm_l[w] * c[w]; }
+        const float *gate = qg + t * ldq + (size_t)h * 2 * D + D;
+#pragma unroll
+        for (int d = 0; d < DPL; d++) {
+            const int i = lane * DPL + d;
+            float acc = 0.0f;
+#pragma unroll
+            for (int w = 0; w < 4; w++) acc = fmaf(sm_o[w][i], c[w], acc);
+            out[t * ldo + (size_t)h * D + i] = (acc / L) * sigm_f(gate[i]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------- FFN / misc
+// g = silu(g) * u (core/xj_cpu.c:273).
+__global__ void k_swiglu(float *g, const float *u, long long n) {
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
+        g[i] = silu_f(g[i]) * u[i];
+}
+
+__global__ void k_advance(int *npast, int T) {
+    if (threadIdx.x == 0 && blockIdx.x == 0) *npast += T;
+}
+
+// Greedy pick over logits[V]: largest value, lowest index on ties (core/xj_spec.c:12-16); also the
+// gap to the runner-up. Writes the id to out_tok[*step] and to *cur (the next step's input), the gap
+// to margin[*step], then advances *step. One block of 1024 threads.
+__global__ void __launch_bounds__(1024) k_argmax(const float *logits, int V, int32_t *out_tok, float *margin,
+                                                 int32_t *cur, int *step) {
+    __shared__ float sv[32], sv2[32];
+    __shared__ int si[32];
+    float b = -INFINITY, b2 = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = logits[i];
+        if (v > b || (v == b && i < bi)) { b2 = fmaxf(b2, b); b = v; bi = i; }
+        else b2 = fmaxf(b2, v);
+    }
+    // warp reduce (value desc, index asc), keeping the runner-up value
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, b, o), ov2 = __shfl_xor_sync(0xffffffffu, b2, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > b || (ov == b && oi < bi)) { b2 = fmaxf(b, ov2); b = ov; bi = oi; }
+        else b2 = fmaxf(b2, ov);
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sv[w] = b; sv2[w] = b2; si[w] = bi; }
+    __syncthreads();
+    if (w == 0) {
+        const int nw = blockDim.x >> 5;
+        b = lane < nw ? sv[lane] : -INFINITY;
+        b2 = lane < nw ? sv2[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, b, o), ov2 = __shfl_xor_sync(0xffffffffu, b2, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > b || (ov == b && oi < bi)) { b2 = fmaxf(b, ov2); b = ov; bi = oi; }
+            else b2 = fmaxf(b2, ov);
+        }
+        if (lane == 0) {
+            const int s = *step;
+            out_tok[s] = bi;
+            if (margin) margin[s] = b - b2;
+            *cur = bi;
+            *step = s + 1;
+        }
+    }
+}
+
+}  // namespace xjk

@@ -1,0 +1,637 @@
+// xj_cuda_stage_new: the CUDA implementation of the runtime's stage vtable (include/xj_abi.h).
+//
+// State machine and error behaviour follow the reference CPU stage (src/xiaoju-pipe/core/xj_cpu.c):
+//   forward   :244-280  (T checks, keep one-shot, ck_start/ck_T, n_past += T)
+//   logits    :282-291  (output_norm or the MTP shared_head_norm, then the LM head)
+//   rollback  :293-319  (KV-only stages truncate; recurrent stages restore checkpoint j)
+//   reset     :321-330  (zero conv + recurrent state, n_past = 0)
+//   ctor      :375-418  (layer-range / MTP-range validation)
+// and the device-side structure follows the Metal stage's (metal/xj_metal.m:422-534): weights are
+// uploaded once per stage, the KV cache is fp16 (fp32 on request), recurrent state fp32, and one
+// forward is one stream of kernels with a single host synchronisation at the end.
+#include <cuda_runtime.h>
+
+#include <cstdarg>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <map>
+#include <vector>
+
+#include "../../include/xj_cuda.h"
+#include "kernels.cuh"
+#include "gemv_mma.cuh"
+
+using namespace xjk;
+
+namespace {
+
+int g_opt_kv_f32 = 0;
+int g_opt_gemv = 0;
+
+void seterr(char *err, size_t errlen, const char *fmt, ...) {
+    if (!err || !errlen) return;
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(err, errlen, fmt, ap);
+    va_end(ap);
+}
+
+struct Layer {
+    bool rec = false;
+    float *attn_norm = nullptr, *post_norm = nullptr;
+    DevMat ffn_gate{}, ffn_up{}, ffn_down{};
+    // Gated DeltaNet
+    DevMat qkv{}, gate{}, beta{}, alpha{}, out{};
+    float *conv_w = nullptr, *dt = nullptr, *A = nullptr, *ssm_norm = nullptr;
+    float *conv = nullptr, *ssm = nullptr, *ck_conv = nullptr, *ck_ssm = nullptr;
+    // full attention
+    bool fused = false;
+    DevMat wqkv{}, wq{}, wk{}, wv{}, wo{};
+    float *q_norm = nullptr, *k_norm = nullptr;
+    void *kc = nullptr, *vc = nullptr;
+};
+
+struct Impl {
+    int dev = 0;
+    cudaStream_t st = nullptr;
+    cudaEvent_t ev[3] = {};
+    std::vector<Layer> L;
+    std::map<const void *, DevMat> uploaded;   // host weight pointer -> device copy
+    std::vector<void *> allocs;
+    bool kv_f32 = false;
+    int gemv_mode = 0;
+    int n_ck = 0;
+    size_t state_bytes = 0;
+    DevMat tok_embd{}, output{}, mtp_eh{};
+    float *output_norm = nullptr, *mtp_enorm = nullptr, *mtp_hnorm = nullptr, *mtp_head_norm = nullptr;
+    // activations (device)
+    float *x = nullptr, *xin = nullptr, *h = nullptr, *qkvb = nullptr, *z = nullptr, *beta = nullptr, *alpha = nullptr;
+    float *o = nullptr, *qrot = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
+    float *q = nullptr, *k = nullptr, *v = nullptr;
+    int *npast = nullptr, *step = nullptr;
+    int32_t *tok = nullptr, *cur = nullptr, *out_tok = nullptr;
+    float *margin = nullptr;
+    int out_cap = 0;
+    // pinned host staging
+    float *hx = nullptr, *hlogits = nullptr;
+    // decode-step graph
+    cudaGraphExec_t step_graph = nullptr;
+    int step_kernels = 0;
+};
+
+Impl *I(xj_stage *s) { return (Impl *)s->impl; }
+
+#define CK(call) do { cudaError_t e_ = (call); if (e_ != cudaSuccess) { seterr(err, errlen, "CUDA error %s at %s:%d", cudaGetErrorString(e_), __FILE__, __LINE__); return -1; } } while (0)
+
+struct DevGuard {
+    int prev = -1;
+    explicit DevGuard(int d) { cudaGetDevice(&prev); if (prev != d) cudaSetDevice(d); }
+    ~DevGuard() { int cur; cudaGetDevice(&cur); if (prev >= 0 && cur != prev) cudaSetDevice(prev); }
+};
+
+template <typename T>
+int dalloc(Impl *im, T **p, size_t n, char *err, size_t errlen) {
+    void *q = nullptr;
+    cudaError_t e = cudaMalloc(&q, n ? n * sizeof(T) : 16);
+    if (e != cudaSuccess) { seterr(err, errlen, "cudaMalloc(%zu bytes) failed: %s", n * sizeof(T), cudaGetErrorString(e)); return -1; }
+    im->allocs.push_back(q);
+    *p = (T *)q;
+    return 0;
+}
+
+uint64_t row_bytes(uint32_t type, int64_t n) {
+    switch (type) {
+    case XJ_F32: return (uint64_t)n * 4;
+    case XJ_F16: case XJ_BF16: return (uint64_t)n * 2;
+    case XJ_Q8_0: return (uint64_t)(n / 32) * 34;
+    case XJ_Q4_K: return (uint64_t)(n / 256) * 144;
+    case XJ_Q5_K: return (uint64_t)(n / 256) * 176;
+    case XJ_Q6_K: return (uint64_t)(n / 256) * 210;
+    default: return 0;
+    }
+}
+
+// Upload one weight (once per host pointer) in its GGUF block layout.
+int upload(Impl *im, const xj_w &w, DevMat *out, char *err, size_t errlen) {
+    if (!w.data || !w.nbytes) { seterr(err, errlen, "weight is not mapped"); return -1; }
+    auto it = im->uploaded.find(w.data);
+    if (it != im->uploaded.end()) { *out = it->second; return 0; }
+    uint8_t *p;
+    if (dalloc(im, &p, (size_t)w.nbytes, err, errlen)) return -1;
+    CK(cudaMemcpy(p, w.data, (size_t)w.nbytes, cudaMemcpyHostToDevice));
+    DevMat d{p, (int)w.type, (int)w.ne0, (int)w.ne1, (long long)row_bytes(w.type, w.ne0)};
+    im->uploaded[w.data] = d;
+    *out = d;
+    return 0;
+}
+
+int upload_f32(Impl *im, const xj_w &w, float **out, char *err, size_t errlen) {
+    if (w.type != XJ_F32) { seterr(err, errlen, "expected an F32 tensor"); return -1; }
+    DevMat d;
+    if (upload(im, w, &d, err, errlen)) return -1;
+    *out = (float *)d.p;
+    return 0;
+}
+
+// ------------------------------------------------------------------ launches
+void gemv(Impl *im, const float *x, long long ldx, int T, std::initializer_list<GemvJob> jobs) {
+    // Fast tensor-core path for the block types it supports, generic path for the rest.
+    GemvArgs a{};
+    a.x = x; a.ldx = ldx; a.T = T;
+    std::vector<GemvJob> slow;
+    for (const GemvJob &j : jobs) {
+        if (im->gemv_mode == 0 && T <= MMA_MAXT && mma_supported(j.w))
+            launch_gemv_mma(j, x, ldx, T, im->st);
+        else
+            slow.push_back(j);
+    }
+    for (size_t i0 = 0; i0 < slow.size(); i0 += 4) {
+        a.njob = 0;
+        a.row_start[0] = 0;
+        for (size_t i = i0; i < slow.size() && a.njob < 4; i++) {
+            a.job[a.njob] = slow[i];
+            a.row_start[a.njob + 1] = a.row_start[a.njob] + slow[i].w.N;
+            a.njob++;
+        }
+        for (int t0 = 0; t0 < T; t0 += MAXT) {
+            GemvArgs b = a;
+            b.T = T - t0 < MAXT ? T - t0 : MAXT;
+            b.x = x + t0 * ldx;
+            for (int j = 0; j < b.njob; j++) b.job[j].y = a.job[j].y + t0 * a.job[j].ldy;
+            k_gemv_generic<<<(b.row_start[b.njob] + 7) / 8, 256, 0, im->st>>>(b);
+        }
+    }
+}
+
+void rmsnorm(Impl *im, const float *x, long long ldx, const float *w, float *y, long long ldy, int n, int rows, float eps) {
+    k_rmsnorm<<<rows, 256, 0, im->st>>>(x, ldx, w, y, ldy, n, eps);
+}
+
+void launch_gdn(Impl *im, const xj_hparams *hp, Layer &Ly, int T, bool ck) {
+    const int S = hp->s_k;
+    const long long ldq = hp->conv_dim;
+#define GDN(SS) k_gdn<SS><<<hp->h_v, SS < 32 ? 32 : SS, 0, im->st>>>(im->qkvb, ldq, im->z, hp->d_inner, im->beta, im->alpha, \
+        hp->h_v, Ly.dt, Ly.A, Ly.ssm_norm, Ly.ssm, ck ? Ly.ck_ssm : nullptr, im->o, hp->d_inner, T, hp->h_k, hp->h_v, \
+        hp->key_dim, hp->eps)
+    switch (S) {
+    case 16: GDN(16); break;
+    case 32: GDN(32); break;
+    case 64: GDN(64); break;
+    case 128: GDN(128); break;
+    case 256: GDN(256); break;
+    default: break;
+    }
+#undef GDN
+}
+
+template <typename KV>
+void launch_attn(Impl *im, const xj_hparams *hp, Layer &Ly, int T, const float *q, long long ldq, const float *k,
+                 const float *v, long long ldkv) {
+    const int H = hp->n_head, Hkv = hp->n_head_kv, D = hp->head_dim;
+    const int thr = (D + 31) / 32 * 32;
+    k_attn_prep<KV><<<dim3(H + Hkv, T), thr, D * sizeof(float), im->st>>>(q, ldq, k, v, ldkv, Ly.q_norm, Ly.k_norm, im->qrot,
+                                                                         (KV *)Ly.kc, (KV *)Ly.vc, im->npast, H, Hkv, D,
+                                                                         hp->n_rot, hp->rope_base, hp->eps);
+    const long long ldo = (long long)H * D;
+    switch ((D + 31) / 32) {
+    case 1: k_attn<KV, 1><<<dim3(H, T), 128, 0, im->st>>>(im->qrot, q, ldq, (KV *)Ly.kc, (KV *)Ly.vc, im->npast, im->o, ldo, H, Hkv, D); break;
+    case 2: k_attn<KV, 2><<<dim3(H, T), 128, 0, im->st>>>(im->qrot, q, ldq, (KV *)Ly.kc, (KV *)Ly.vc, im->npast, im->o, ldo, H, Hkv, D); break;
+    case 4: k_attn<KV, 4><<<dim3(H, T), 128, 0, im->st>>>(im->qrot, q, ldq, (KV *)Ly.kc, (KV *)Ly.vc, im->npast, im->o, ldo, H, Hkv, D); break;
+    case 8: k_attn<KV, 8><<<dim3(H, T), 128, 0, im->st>>>(im->qrot, q, ldq, (KV *)Ly.kc, (KV *)Ly.vc, im->npast, im->o, ldo, H, Hkv, D); break;
+    default: break;
+    }
+}
+
+// All layers of the stage on im->x[T][E] (device), positions *npast .. *npast+T-1; advances *npast.
+void run_layers(xj_stage *s, int T, bool keep) {
+    Impl *im = I(s);
+    const xj_hparams *hp = &s->m->hp;
+    const int E = hp->n_embd, FF = hp->n_ff;
+    for (int il = s->l0; il < s->l1; il++) {
+        Layer &Ly = im->L[il - s->l0];
+        rmsnorm(im, im->x, E, Ly.attn_norm, im->h, E, E, T, hp->eps);
+        if (Ly.rec) {
+            const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v;
+            gemv(im, im->h, E, T, {{Ly.qkv, im->qkvb, CD, 0}, {Ly.gate, im->z, DI, 0}, {Ly.beta, im->beta, Hv, 0},
+                                   {Ly.alpha, im->alpha, Hv, 0}});
+            k_conv_silu<<<(CD + 127) / 128, 128, 0, im->st>>>(im->qkvb, CD, T, CD, hp->conv_k, Ly.conv, Ly.conv_w,
+                                                            keep ? Ly.ck_conv : nullptr);
+            launch_gdn(im, hp, Ly, T, keep);
+            gemv(im, im->o, DI, T, {{Ly.out, im->x, E, 1}});
+        } else {
+            const int H = hp->n_head, Hkv = hp->n_head_kv, D = hp->head_dim, nq = 2 * H * D, nk = Hkv * D;
+            const float *q, *k, *v;
+            long long ldq, ldkv;
+            if (Ly.fused) {
+                gemv(im, im->h, E, T, {{Ly.wqkv, im->qkvb, nq + 2 * nk, 0}});
+                q = im->qkvb; k = im->qkvb + nq; v = im->qkvb + nq + nk; ldq = ldkv = nq + 2 * nk;
+            } else {
+                gemv(im, im->h, E, T, {{Ly.wq, im->q, nq, 0}, {Ly.wk, im->k, nk, 0}, {Ly.wv, im->v, nk, 0}});
+                q = im->q; k = im->k; v = im->v; ldq = nq; ldkv = nk;
+            }
+            if (im->kv_f32) launch_attn<float>(im, hp, Ly, T, q, ldq, k, v, ldkv);
+            else launch_attn<__half>(im, hp, Ly, T, q, ldq, k, v, ldkv);
+            gemv(im, im->o, (long long)H * D, T, {{Ly.wo, im->x, E, 1}});
+        }
+        rmsnorm(im, im->x, E, Ly.post_norm, im->h, E, E, T, hp->eps);
+        gemv(im, im->h, E, T, {{Ly.ffn_gate, im->g, FF, 0}, {Ly.ffn_up, im->u, FF, 0}});
+        const long long n = (long long)T * FF;
+        k_swiglu<<<(int)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184), 256, 0, im->st>>>(im->g, im->u, n);
+        gemv(im, im->g, FF, T, {{Ly.ffn_down, im->x, E, 1}});
+    }
+    k_advance<<<1, 32, 0, im->st>>>(im->npast, T);
+}
+
+// MTP prefix (core/xj_cpu.c:253-261): x[T][E] = eh_proj([enorm(emb) | hnorm(hid)]), input in im->xin[T][2E].
+void run_mtp_prefix(xj_stage *s, int T) {
+    Impl *im = I(s);
+    const xj_hparams *hp = &s->m->hp;
+    const int E = hp->n_embd;
+    rmsnorm(im, im->xin, 2 * E, im->mtp_enorm, im->h, 2 * E, E, T, hp->eps);
+    rmsnorm(im, im->xin + E, 2 * E, im->mtp_hnorm, im->h + E, 2 * E, E, T, hp->eps);
+    gemv(im, im->h, 2 * E, T, {{im->mtp_eh, im->x, E, 0}});
+}
+
+void head(xj_stage *s, const float *x, int T) {
+    Impl *im = I(s);
+    const xj_hparams *hp = &s->m->hp;
+    const int E = hp->n_embd;
+    rmsnorm(im, x, E, s->mtp ? im->mtp_head_norm : im->output_norm, im->h, E, E, T, hp->eps);
+    gemv(im, im->h, E, T, {{im->output, im->logits, im->output.N, 0}});
+}
+
+int sync_check(Impl *im, char *err, size_t errlen) {
+    cudaError_t e = cudaGetLastError();
+    if (e == cudaSuccess) e = cudaStreamSynchronize(im->st);
+    if (e != cudaSuccess) { seterr(err, errlen, "GPU error: %s", cudaGetErrorString(e)); return -1; }
+    return 0;
+}
+
+// Checkpoint slots for speculative rollback (core/xj_cpu.c:228-242).
+int ensure_ck(xj_stage *s, int n, char *err, size_t errlen) {
+    Impl *im = I(s);
+    const xj_hparams *hp = &s->m->hp;
+    if (n <= im->n_ck) return 0;
+    for (auto &Ly : im->L) {
+        if (!Ly.rec) continue;
+        float *a, *b;
+        if (dalloc(im, &a, (size_t)n * hp->conv_dim * (hp->conv_k - 1), err, errlen)) return -1;
+        if (dalloc(im, &b, (size_t)n * hp->h_v * hp->s_v * hp->s_k, err, errlen)) return -1;
+        Ly.ck_conv = a; Ly.ck_ssm = b;
+    }
+    im->n_ck = n;
+    return 0;
+}
+
+// ------------------------------------------------------------------ vtable
+int cuda_forward(xj_stage *s, float *x, int T, char *err, size_t errlen) {
+    Impl *im = I(s);
+    DevGuard dg(im->dev);
+    const int E = s->m->hp.n_embd;
+    if (T <= 0 || T > s->max_batch) { seterr(err, errlen, "%d tokens in one forward exceeds the limit %d", T, s->max_batch); s->keep = 0; return -1; }
+    if (s->n_past + T > s->n_ctx) { seterr(err, errlen, "context is full (%d)", s->n_ctx); s->keep = 0; return -1; }
+    if (s->keep && ensure_ck(s, T - 1, err, errlen)) { s->keep = 0; return -1; }
+    s->ck_start = s->n_past;
+    s->ck_T = s->keep ? T : 0;
+    const bool keep = s->keep != 0;
+    const int in_w = s->mtp ? 2 * E : E;
+    memcpy(im->hx, x, sizeof(float) * (size_t)T * in_w);
+    if (cudaMemcpyAsync(s->mtp ? im->xin : im->x, im->hx, sizeof(float) * (size_t)T * in_w, cudaMemcpyHostToDevice, im->st) != cudaSuccess) {
+        seterr(err, errlen, "host-to-device copy failed"); s->keep = 0; return -1;
+    }
+    if (s->mtp) run_mtp_prefix(s, T);
+    run_layers(s, T, keep);
+    cudaMemcpyAsync(im->hx, im->x, sizeof(float) * (size_t)T * E, cudaMemcpyDeviceToHost, im->st);
+    if (sync_check(im, err, errlen)) { s->keep = 0; return -1; }
+    memcpy(x, im->hx, sizeof(float) * (size_t)T * E);
+    s->n_past += T;
+    s->keep = 0;
+    return 0;
+}
+
+int cuda_logits(xj_stage *s, const float *x, int T, float *logits, char *err, size_t errlen) {
+    Impl *im = I(s);
+    DevGuard dg(im->dev);
+    const int E = s->m->hp.n_embd, V = im->output.N;
+    if (!s->has_head) { seterr(err, errlen, "this stage has no output head"); return -1; }
+    if (T < 1 || T > s->max_batch) { seterr(err, errlen, "%d tokens for the output head exceeds the limit", T); return -1; }
+    memcpy(im->hx, x, sizeof(float) * (size_t)T * E);
+    CK(cudaMemcpyAsync(im->xin, im->hx, sizeof(float) * (size_t)T * E, cudaMemcpyHostToDevice, im->st));
+    head(s, im->xin, T);
+    cudaMemcpyAsync(im->hlogits, im->logits, sizeof(float) * (size_t)T * V, cudaMemcpyDeviceToHost, im->st);
+    if (sync_check(im, err, errlen)) return -1;
+    memcpy(logits, im->hlogits, sizeof(float) * (size_t)T * V);
+    return 0;
+}
+
+int cuda_rollback(xj_stage *s, int n_past, char *err, size_t errlen) {
+    Impl *im = I(s);
+    DevGuard dg(im->dev);
+    const xj_hparams *hp = &s->m->hp;
+    if (n_past == s->n_past) { s->ck_T = 0; return 0; }
+    bool recurrent = false;
+    for (auto &Ly : im->L) if (Ly.rec) recurrent = true;
+    if (!recurrent) {
+        if (n_past < 0 || n_past > s->n_past) { seterr(err, errlen, "cannot roll back to position %d", n_past); return -1; }
+    } else {
+        const int j = n_past - s->ck_start - 1;
+        if (!s->ck_T || s->n_past != s->ck_start + s->ck_T || j < 0 || j >= s->ck_T - 1) {
+            seterr(err, errlen, "cannot roll back to position %d (checkpoints %d+%d, now %d)", n_past, s->ck_start, s->ck_T, s->n_past);
+            return -1;
+        }
+        const size_t nc = (size_t)hp->conv_dim * (hp->conv_k - 1), ns = (size_t)hp->h_v * hp->s_v * hp->s_k;
+        for (auto &Ly : im->L) {
+            if (!Ly.rec) continue;
+            CK(cudaMemcpyAsync(Ly.conv, Ly.ck_conv + (size_t)j * nc, nc * 4, cudaMemcpyDeviceToDevice, im->st));
+            CK(cudaMemcpyAsync(Ly.ssm, Ly.ck_ssm + (size_t)j * ns, ns * 4, cudaMemcpyDeviceToDevice, im->st));
+        }
+        s->ck_T = 0;
+    }
+    int np = n_past;
+    CK(cudaMemcpyAsync(im->npast, &np, sizeof(int), cudaMemcpyHostToDevice, im->st));
+    if (sync_check(im, err, errlen)) return -1;
+    s->n_past = n_past;
+    return 0;
+}
+
+void cuda_reset(xj_stage *s) {
+    Impl *im = I(s);
+    DevGuard dg(im->dev);
+    const xj_hparams *hp = &s->m->hp;
+    for (auto &Ly : im->L) {
+        if (!Ly.rec) continue;
+        cudaMemsetAsync(Ly.conv, 0, sizeof(float) * hp->conv_dim * (hp->conv_k - 1), im->st);
+        cudaMemsetAsync(Ly.ssm, 0, sizeof(float) * (size_t)hp->h_v * hp->s_v * hp->s_k, im->st);
+    }
+    cudaMemsetAsync(im->npast, 0, sizeof(int), im->st);
+    cudaStreamSynchronize(im->st);
+    s->n_past = 0;
+}
+
+void cuda_destroy(xj_stage *s) {
+    if (!s) return;
+    Impl *im = I(s);
+    if (im) {
+        DevGuard dg(im->dev);
+        if (im->st) cudaStreamSynchronize(im->st);
+        if (im->step_graph) cudaGraphExecDestroy(im->step_graph);
+        for (void *p : im->allocs) cudaFree(p);
+        if (im->hx) cudaFreeHost(im->hx);
+        if (im->hlogits) cudaFreeHost(im->hlogits);
+        for (auto &e : im->ev) if (e) cudaEventDestroy(e);
+        if (im->st) cudaStreamDestroy(im->st);
+        delete im;
+    }
+    free(s);
+}
+
+size_t scratch_floats(const xj_hparams *hp) {
+    size_t n = (size_t)hp->n_ff;
+    const size_t qkv = 2 * (size_t)hp->n_head * hp->head_dim + 2 * (size_t)hp->n_head_kv * hp->head_dim;
+    if (qkv > n) n = qkv;
+    if ((size_t)hp->conv_dim > n) n = hp->conv_dim;
+    if ((size_t)hp->n_embd * 2 > n) n = 2 * (size_t)hp->n_embd;
+    return n;
+}
+
+int build(xj_stage *s, char *err, size_t errlen) {
+    Impl *im = I(s);
+    const xj_model *m = s->m;
+    const xj_hparams *hp = &m->hp;
+    const int E = hp->n_embd, B = s->max_batch;
+    CK(cudaStreamCreateWithFlags(&im->st, cudaStreamNonBlocking));
+    for (auto &e : im->ev) CK(cudaEventCreate(&e));
+    im->kv_f32 = g_opt_kv_f32 != 0;
+    im->gemv_mode = g_opt_gemv;
+    im->L.resize((size_t)(s->l1 - s->l0));
+    for (int il = s->l0; il < s->l1; il++) {
+        const xj_layer &X = m->layers[il];
+        Layer &Ly = im->L[il - s->l0];
+        Ly.rec = il < hp->n_layer && X.recurrent;
+        if (upload_f32(im, X.attn_norm, &Ly.attn_norm, err, errlen) || upload_f32(im, X.post_norm, &Ly.post_norm, err, errlen) ||
+            upload(im, X.ffn_gate, &Ly.ffn_gate, err, errlen) || upload(im, X.ffn_up, &Ly.ffn_up, err, errlen) ||
+            upload(im, X.ffn_down, &Ly.ffn_down, err, errlen)) return -1;
+        if (Ly.rec) {
+            if (upload(im, X.ssm_qkv, &Ly.qkv, err, errlen) || upload(im, X.ssm_gate, &Ly.gate, err, errlen) ||
+                upload(im, X.ssm_beta, &Ly.beta, err, errlen) || upload(im, X.ssm_alpha, &Ly.alpha, err, errlen) ||
+                upload(im, X.ssm_out, &Ly.out, err, errlen) || upload_f32(im, X.ssm_conv1d, &Ly.conv_w, err, errlen) ||
+                upload_f32(im, X.ssm_dt, &Ly.dt, err, errlen) || upload_f32(im, X.ssm_a, &Ly.A, err, errlen) ||
+                upload_f32(im, X.ssm_norm, &Ly.ssm_norm, err, errlen)) return -1;
+            const size_t nc = (size_t)hp->conv_dim * (hp->conv_k - 1), ns = (size_t)hp->h_v * hp->s_v * hp->s_k;
+            if (dalloc(im, &Ly.conv, nc, err, errlen) || dalloc(im, &Ly.ssm, ns, err, errlen)) return -1;
+            CK(cudaMemset(Ly.conv, 0, nc * 4));
+            CK(cudaMemset(Ly.ssm, 0, ns * 4));
+            im->state_bytes += (nc + ns) * 4;
+        } else {
+            Ly.fused = X.wqkv.nbytes != 0;
+            if (Ly.fused) { if (upload(im, X.wqkv, &Ly.wqkv, err, errlen)) return -1; }
+            else if (upload(im, X.wq, &Ly.wq, err, errlen) || upload(im, X.wk, &Ly.wk, err, errlen) ||
+                     upload(im, X.wv, &Ly.wv, err, errlen)) return -1;
+            if (upload(im, X.wo, &Ly.wo, err, errlen) || upload_f32(im, X.q_norm, &Ly.q_norm, err, errlen) ||
+                upload_f32(im, X.k_norm, &Ly.k_norm, err, errlen)) return -1;
+            const size_t n = (size_t)s->n_ctx * hp->n_head_kv * hp->head_dim, es = im->kv_f32 ? 4 : 2;
+            uint8_t *a, *b;
+            if (dalloc(im, &a, n * es, err, errlen) || dalloc(im, &b, n * es, err, errlen)) return -1;
+            Ly.kc = a; Ly.vc = b;
+            im->state_bytes += 2 * n * es;
+        }
+    }
+    if (s->mtp) {
+        if (upload(im, m->mtp_eh, &im->mtp_eh, err, errlen) || upload_f32(im, m->mtp_enorm, &im->mtp_enorm, err, errlen) ||
+            upload_f32(im, m->mtp_hnorm, &im->mtp_hnorm, err, errlen) ||
+            upload_f32(im, m->mtp_head_norm, &im->mtp_head_norm, err, errlen)) return -1;
+    }
+    if (s->has_head) {
+        if (upload(im, m->output, &im->output, err, errlen) || upload_f32(im, m->output_norm, &im->output_norm, err, errlen)) return -1;
+    }
+    const size_t sf = scratch_floats(hp) * (size_t)B;
+    const size_t V = s->has_head ? (size_t)m->output.ne1 : 1;
+    if (dalloc(im, &im->x, (size_t)B * E, err, errlen) || dalloc(im, &im->xin, (size_t)B * 2 * E, err, errlen) ||
+        dalloc(im, &im->h, (size_t)B * 2 * E, err, errlen) || dalloc(im, &im->qkvb, sf, err, errlen) ||
+        dalloc(im, &im->z, sf, err, errlen) || dalloc(im, &im->beta, (size_t)B * hp->h_v + 16, err, errlen) ||
+        dalloc(im, &im->alpha, (size_t)B * hp->h_v + 16, err, errlen) || dalloc(im, &im->o, sf, err, errlen) ||
+        dalloc(im, &im->qrot, (size_t)B * hp->n_head * hp->head_dim, err, errlen) || dalloc(im, &im->g, sf, err, errlen) ||
+        dalloc(im, &im->u, sf, err, errlen) || dalloc(im, &im->q, sf, err, errlen) || dalloc(im, &im->k, sf, err, errlen) ||
+        dalloc(im, &im->v, sf, err, errlen) || dalloc(im, &im->logits, V * (size_t)B, err, errlen) ||
+        dalloc(im, &im->npast, 4, err, errlen) || dalloc(im, &im->step, 4, err, errlen) ||
+        dalloc(im, &im->tok, (size_t)B, err, errlen) || dalloc(im, &im->cur, 4, err, errlen)) return -1;
+    CK(cudaMemset(im->npast, 0, 16));
+    CK(cudaMallocHost(&im->hx, sizeof(float) * (size_t)B * 2 * E));
+    CK(cudaMallocHost(&im->hlogits, sizeof(float) * V * (size_t)B));
+    im->state_bytes += sizeof(float) * (sf * 7 + (size_t)B * 4 * E + V * B);
+    CK(cudaDeviceSynchronize());
+    return 0;
+}
+
+int count_kernels(cudaGraph_t g) {
+    size_t n = 0;
+    if (cudaGraphGetNodes(g, nullptr, &n) != cudaSuccess || !n) return 0;
+    std::vector<cudaGraphNode_t> nodes(n);
+    cudaGraphGetNodes(g, nodes.data(), &n);
+    int k = 0;
+    for (auto nd : nodes) {
+        cudaGraphNodeType t;
+        if (cudaGraphNodeGetType(nd, &t) == cudaSuccess && t == cudaGraphNodeTypeKernel) k++;
+    }
+    return k;
+}
+
+// One decode step on device: x = embed(*cur); layers; head on the last row; argmax -> out_tok[*step], *cur.
+void decode_step(xj_stage *s) {
+    Impl *im = I(s);
+    const int E = s->m->hp.n_embd;
+    k_embed<<<dim3((E / 8 + 127) / 128, 1), 128, 0, im->st>>>(im->tok_embd, im->cur, 1, im->x, E);
+    run_layers(s, 1, false);
+    head(s, im->x, 1);
+    k_argmax<<<1, 1024, 0, im->st>>>(im->logits, im->output.N, im->out_tok, im->margin, im->cur, im->step);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *xj_cuda_device_name(void) {
+    static char name[256];
+    int d = 0;
+    cudaDeviceProp p;
+    if (cudaGetDevice(&d) != cudaSuccess || cudaGetDeviceProperties(&p, d) != cudaSuccess) return "CUDA";
+    snprintf(name, sizeof name, "%s", p.name);
+    return name;
+}
+
+int xj_cuda_set_options(int which, int value) {
+    switch (which) {
+    case XJC_OPT_KV_F32: g_opt_kv_f32 = value; return 0;
+    case XJC_OPT_GEMV: g_opt_gemv = value; return 0;
+    default: return -1;
+    }
+}
+
+xj_stage *xj_cuda_stage_new(const xj_model *m, int l0, int l1, int n_ctx, int max_batch, bool has_head, char *err,
+                            size_t errlen) {
+    const xj_hparams *hp = &m->hp;
+    const bool mtp = m->has_mtp && l0 == hp->n_layer && l1 == hp->n_layer + 1;
+    if (l0 < 0 || (l1 > hp->n_layer && !mtp) || l0 > l1) { seterr(err, errlen, "bad layer range [%d,%d)", l0, l1); return nullptr; }
+    if (hp->head_dim > 256 || hp->head_dim % 8) { seterr(err, errlen, "head dim %d not supported", hp->head_dim); return nullptr; }
+    if (hp->s_k != 16 && hp->s_k != 32 && hp->s_k != 64 && hp->s_k != 128 && hp->s_k != 256) {
+        seterr(err, errlen, "linear-attention head dim %d not supported", hp->s_k); return nullptr;
+    }
+    if (hp->conv_k < 2 || hp->conv_k > 9) { seterr(err, errlen, "conv kernel %d not supported", hp->conv_k); return nullptr; }
+    if (n_ctx <= 0 || max_batch <= 0) { seterr(err, errlen, "n_ctx and max_batch must be positive"); return nullptr; }
+    for (int il = l0; il < l1; il++)
+        if (!m->layers[il].ffn_down.data) { seterr(err, errlen, "layer %d weights are not mapped", il); return nullptr; }
+    if (has_head && !m->output.data) { seterr(err, errlen, "output head is not mapped"); return nullptr; }
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) { seterr(err, errlen, "no CUDA device"); return nullptr; }
+    xj_stage *s = (xj_stage *)calloc(1, sizeof(xj_stage));
+    Impl *im = new Impl();
+    im->dev = dev;
+    s->m = m; s->l0 = l0; s->l1 = l1; s->n_ctx = n_ctx; s->max_batch = max_batch; s->has_head = has_head; s->mtp = mtp;
+    s->backend = "cuda";
+    s->forward = cuda_forward; s->logits = cuda_logits; s->rollback = cuda_rollback; s->reset = cuda_reset;
+    s->destroy = cuda_destroy;
+    s->impl = im;
+    if (build(s, err, errlen)) { cuda_destroy(s); return nullptr; }
+    return s;
+}
+
+int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, int32_t *out, float *margins,
+                   float *gpu_ms, char *err, size_t errlen) {
+    if (!s || s->backend == nullptr || strcmp(s->backend, "cuda") != 0) { seterr(err, errlen, "not a CUDA stage"); return -1; }
+    Impl *im = I(s);
+    DevGuard dg(im->dev);
+    const xj_model *m = s->m;
+    const int E = m->hp.n_embd;
+    if (s->mtp || s->l0 != 0 || s->l1 != m->hp.n_layer || !s->has_head) {
+        seterr(err, errlen, "decode needs a stage over all layers with the head"); return -1;
+    }
+    if (n_prompt <= 0 || n_gen <= 0) { seterr(err, errlen, "need at least one prompt token and one generated token"); return -1; }
+    if (s->n_past + n_prompt + n_gen - 1 > s->n_ctx) { seterr(err, errlen, "context is full (%d)", s->n_ctx); return -1; }
+    if (!im->tok_embd.p && upload(im, m->tok_embd, &im->tok_embd, err, errlen)) return -1;
+    if (n_gen > im->out_cap) {
+        // the step graph writes through these pointers, so it is rebuilt after a reallocation
+        if (im->step_graph) { cudaGraphExecDestroy(im->step_graph); im->step_graph = nullptr; }
+        const int cap = n_gen > 4096 ? n_gen : 4096;
+        if (dalloc(im, &im->out_tok, (size_t)cap, err, errlen) || dalloc(im, &im->margin, (size_t)cap, err, errlen)) return -1;
+        im->out_cap = cap;
+    }
+    CK(cudaMemsetAsync(im->step, 0, sizeof(int), im->st));
+    CK(cudaEventRecord(im->ev[0], im->st));
+    const int B = s->max_batch;
+    for (int i = 0; i < n_prompt; i += B) {
+        const int T = n_prompt - i < B ? n_prompt - i : B;
+        CK(cudaMemcpyAsync(im->tok, prompt + i, sizeof(int32_t) * T, cudaMemcpyHostToDevice, im->st));
+        k_embed<<<dim3((E / 8 + 127) / 128, T), 128, 0, im->st>>>(im->tok_embd, im->tok, T, im->x, E);
+        run_layers(s, T, false);
+        if (i + T == n_prompt) {
+            head(s, im->x + (size_t)(T - 1) * E, 1);
+            k_argmax<<<1, 1024, 0, im->st>>>(im->logits, im->output.N, im->out_tok, im->margin, im->cur, im->step);
+        }
+    }
+    CK(cudaEventRecord(im->ev[1], im->st));
+    if (n_gen > 1) {
+        if (!im->step_graph) {
+            cudaGraph_t g;
+            CK(cudaStreamBeginCapture(im->st, cudaStreamCaptureModeThreadLocal));
+            decode_step(s);
+            CK(cudaStreamEndCapture(im->st, &g));
+            im->step_kernels = count_kernels(g);
+            cudaError_t e = cudaGraphInstantiate(&im->step_graph, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) { seterr(err, errlen, "graph instantiate: %s", cudaGetErrorString(e)); im->step_graph = nullptr; return -1; }
+        }
+        for (int i = 1; i < n_gen; i++) CK(cudaGraphLaunch(im->step_graph, im->st));
+    }
+    CK(cudaEventRecord(im->ev[2], im->st));
+    CK(cudaMemcpyAsync(out, im->out_tok, sizeof(int32_t) * n_gen, cudaMemcpyDeviceToHost, im->st));
+    if (margins) CK(cudaMemcpyAsync(margins, im->margin, sizeof(float) * n_gen, cudaMemcpyDeviceToHost, im->st));
+    if (sync_check(im, err, errlen)) return -1;
+    if (gpu_ms) {
+        cudaEventElapsedTime(&gpu_ms[0], im->ev[0], im->ev[1]);
+        cudaEventElapsedTime(&gpu_ms[1], im->ev[1], im->ev[2]);
+    }
+    s->n_past += n_prompt + n_gen - 1;
+    return 0;
+}
+
+int xj_cuda_graph_kernels(const xj_stage *s) {
+    const Impl *im = (const Impl *)s->impl;
+    return im ? im->step_kernels : 0;
+}
+
+int xj_cuda_dequant_rows(int type, const void *src, int k, int n_rows, float *out, char *err, size_t errlen) {
+    const uint64_t rb = row_bytes((uint32_t)type, k);
+    if (!rb || k % 8 || n_rows <= 0) { seterr(err, errlen, "unsupported type %d or row length %d", type, k); return -1; }
+    uint8_t *d_src = nullptr;
+    float *d_out = nullptr;
+    cudaError_t e = cudaMalloc(&d_src, rb * n_rows);
+    if (e == cudaSuccess) e = cudaMalloc(&d_out, sizeof(float) * (size_t)k * n_rows);
+    if (e == cudaSuccess) e = cudaMemcpy(d_src, src, rb * n_rows, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        DevMat w{d_src, type, k, n_rows, (long long)rb};
+        k_dequant<<<148, 256>>>(w, 0, n_rows, d_out);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(out, d_out, sizeof(float) * (size_t)k * n_rows, cudaMemcpyDeviceToHost);
+    cudaFree(d_src);
+    cudaFree(d_out);
+    if (e != cudaSuccess) { seterr(err, errlen, "CUDA error: %s", cudaGetErrorString(e)); return -1; }
+    return 0;
+}
+
+uint64_t xjc_stage_state_bytes(const xj_model *m, int l0, int l1, int n_ctx, int max_batch) {
+    const xj_hparams *hp = &m->hp;
+    uint64_t b = 0;
+    const uint64_t kv_es = g_opt_kv_f32 ? 4 : 2;
+    for (int il = l0; il < l1; il++) {
+        if (il < hp->n_layer && m->layers[il].recurrent)
+            b += 4ull * ((uint64_t)hp->conv_dim * (hp->conv_k - 1) + (uint64_t)hp->h_v * hp->s_v * hp->s_k);
+        else
+            b += 2ull * kv_es * n_ctx * hp->n_head_kv * hp->head_dim;
+    }
+    b += 7ull * 4 * max_batch * scratch_floats(hp);
+    return b;
+}
+
+}  // extern "C"

@@ -1,0 +1,260 @@
+"""Python front end of libxj_cuda.so (C ABI in include/xj_cuda.h), used by tests and bench.py.
+
+Everything goes through the library's exported C functions and the xj_stage function pointers the
+library fills in, exactly as a C host (or the runtime's own pipeline code) would call them. There is
+no Python or CPU fallback: if the library or a GPU is missing, the calls fail.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import pathlib
+import subprocess
+
+import numpy as np
+
+HERE = pathlib.Path(__file__).resolve().parent
+LIB = HERE / "csrc" / "libxj_cuda.so"
+
+_lib = None
+
+F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 8, 12, 13, 14, 30
+OPT_KV_F32, OPT_GEMV = 1, 2
+
+
+class XjError(RuntimeError):
+    pass
+
+
+# ---- ABI mirror of include/xj_abi.h (only what Python touches) ----
+FORWARD = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t)
+LOGITS = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_char_p,
+                          ctypes.c_size_t)
+ROLLBACK = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t)
+VOIDFN = ctypes.CFUNCTYPE(None, ctypes.c_void_p)
+
+
+class _Stage(ctypes.Structure):
+    _fields_ = [
+        ("m", ctypes.c_void_p), ("l0", ctypes.c_int), ("l1", ctypes.c_int), ("n_ctx", ctypes.c_int),
+        ("max_batch", ctypes.c_int), ("n_past", ctypes.c_int), ("has_head", ctypes.c_bool), ("mtp", ctypes.c_bool),
+        ("backend", ctypes.c_char_p), ("keep", ctypes.c_int), ("ck_start", ctypes.c_int), ("ck_T", ctypes.c_int),
+        ("forward", FORWARD), ("logits", LOGITS), ("rollback", ROLLBACK), ("reset", VOIDFN), ("destroy", VOIDFN),
+        ("impl", ctypes.c_void_p),
+    ]
+
+
+class _HParams(ctypes.Structure):
+    _fields_ = [(n, ctypes.c_int) for n in ("n_layer", "n_embd", "n_ff", "n_vocab", "n_head", "n_head_kv", "head_dim",
+                                             "n_rot")] + \
+               [("rope_base", ctypes.c_float), ("eps", ctypes.c_float)] + \
+               [(n, ctypes.c_int) for n in ("conv_k", "d_inner", "s_k", "h_k", "h_v", "s_v", "key_dim", "conv_dim",
+                                             "full_attn_interval")] + \
+               [("eos", ctypes.c_uint32), ("eot", ctypes.c_uint32)]
+
+
+class _W(ctypes.Structure):
+    _fields_ = [("data", ctypes.c_void_p), ("file_off", ctypes.c_uint64), ("nbytes", ctypes.c_uint64),
+                ("type", ctypes.c_uint32), ("ne0", ctypes.c_int64), ("ne1", ctypes.c_int64)]
+
+
+class _Layer(ctypes.Structure):
+    _fields_ = [("recurrent", ctypes.c_bool)] + [(n, _W) for n in (
+        "attn_norm", "post_norm", "wqkv", "wq", "wk", "wv", "wo", "q_norm", "k_norm", "ssm_qkv", "ssm_gate",
+        "ssm_conv1d", "ssm_dt", "ssm_a", "ssm_beta", "ssm_alpha", "ssm_norm", "ssm_out", "ffn_gate", "ffn_up",
+        "ffn_down")]
+
+
+class _Model(ctypes.Structure):
+    _fields_ = [("gguf", ctypes.c_void_p), ("hp", _HParams), ("tok_embd", _W), ("output_norm", _W), ("output", _W),
+                ("layers", _Layer * 128), ("fingerprint", ctypes.c_uint64), ("has_mtp", ctypes.c_bool),
+                ("mtp_eh", _W), ("mtp_enorm", _W), ("mtp_hnorm", _W), ("mtp_head_norm", _W),
+                ("mtp_gguf", ctypes.c_void_p)]
+
+
+def build(quiet: bool = True) -> None:
+    """Compile csrc/libxj_cuda.so (nvcc, sm_100a)."""
+    r = subprocess.run(["make", "-C", str(LIB.parent)], capture_output=True, text=True)
+    if r.returncode != 0:
+        raise XjError("build failed:\n" + r.stdout[-4000:] + r.stderr[-4000:])
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIB.exists():
+        build()
+    L = ctypes.CDLL(str(LIB))
+    vp, ip, sz, cp = ctypes.c_void_p, ctypes.c_int, ctypes.c_size_t, ctypes.c_char_p
+    sig = {
+        "xj_cuda_stage_new": (ctypes.POINTER(_Stage), [vp, ip, ip, ip, ip, ctypes.c_bool, cp, sz]),
+        "xj_cuda_device_name": (cp, []),
+        "xjc_model_load": (vp, [cp, cp, sz]),
+        "xjc_model_free": (None, [vp]),
+        "xjc_embed": (None, [vp, ctypes.c_int32, vp]),
+        "xjc_stage_state_bytes": (ctypes.c_uint64, [vp, ip, ip, ip, ip]),
+        "xj_cuda_set_options": (ip, [ip, ip]),
+        "xj_cuda_decode": (ip, [vp, vp, ip, ip, vp, vp, vp, cp, sz]),
+        "xj_cuda_dequant_rows": (ip, [ip, vp, ip, ip, vp, cp, sz]),
+        "xj_cuda_graph_kernels": (ip, [vp]),
+    }
+    for name, (res, args) in sig.items():
+        f = getattr(L, name)
+        f.restype = res
+        f.argtypes = args
+    _lib = L
+    return L
+
+
+def ctor_address() -> int:
+    """Address of xj_cuda_stage_new, for hosts that take a stage constructor (same signature as xj_cpu_stage_new)."""
+    return ctypes.cast(lib().xj_cuda_stage_new, ctypes.c_void_p).value
+
+
+def set_option(which: int, value: int) -> None:
+    if lib().xj_cuda_set_options(which, value) != 0:
+        raise XjError(f"unknown option {which}")
+
+
+def device_name() -> str:
+    return lib().xj_cuda_device_name().decode()
+
+
+def dequant_rows(type_id: int, raw: bytes, k: int, n_rows: int) -> np.ndarray:
+    """GPU block decoder on host bytes -> fp32 [n_rows][k] (xj_cuda_dequant_rows)."""
+    src = np.frombuffer(bytes(raw), np.uint8).copy()
+    out = np.zeros((n_rows, k), np.float32)
+    e = _err()
+    if lib().xj_cuda_dequant_rows(type_id, src.ctypes.data, k, n_rows, out.ctypes.data, e, 512):
+        _raise(e)
+    return out
+
+
+def _err():
+    return ctypes.create_string_buffer(512)
+
+
+def _raise(e):
+    raise XjError(e.value.decode(errors="replace"))
+
+
+class Model:
+    """A qwen35 GGUF loaded by the library's loader (xjc_model_load), or wrapping a pointer to an xj_model
+    produced by any loader with the runtime's layout (e.g. the runtime's own xj_model_load)."""
+
+    def __init__(self, path: str | os.PathLike | None = None, ptr: int | None = None):
+        self.owned = ptr is None
+        if ptr is None:
+            e = _err()
+            ptr = lib().xjc_model_load(str(path).encode(), e, 512)
+            if not ptr:
+                _raise(e)
+        self.ptr = ptr
+        self.m = _Model.from_address(ptr)
+        self.hp = self.m.hp
+        self.n_embd, self.n_vocab, self.n_layer = self.hp.n_embd, self.hp.n_vocab, self.hp.n_layer
+
+    def embed(self, tok: int) -> np.ndarray:
+        out = np.zeros(self.n_embd, np.float32)
+        lib().xjc_embed(self.ptr, int(tok), out.ctypes.data)
+        return out
+
+    def embed_many(self, toks) -> np.ndarray:
+        return np.stack([self.embed(int(t)) for t in toks])
+
+    def close(self):
+        if self.ptr and self.owned:
+            lib().xjc_model_free(self.ptr)
+        self.ptr = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Stage:
+    """xj_cuda_stage_new(m, l0, l1, n_ctx, max_batch, has_head) and its vtable."""
+
+    def __init__(self, model: Model, l0: int, l1: int, n_ctx: int = 256, max_batch: int = 16, has_head: bool = True):
+        e = _err()
+        p = lib().xj_cuda_stage_new(model.ptr, l0, l1, n_ctx, max_batch, has_head, e, 512)
+        if not p:
+            _raise(e)
+        self.model, self.p, self.s = model, p, p.contents
+        self.E = model.n_embd
+
+    @property
+    def addr(self) -> int:
+        return ctypes.cast(self.p, ctypes.c_void_p).value
+
+    def forward(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32).copy()
+        T = x.shape[0]
+        e = _err()
+        if self.s.forward(self.addr, x.ctypes.data, T, e, 512):
+            _raise(e)
+        return x.reshape(-1)[:T * self.E].reshape(T, self.E).copy()
+
+    def logits(self, x: np.ndarray) -> np.ndarray:
+        x = np.ascontiguousarray(x, dtype=np.float32)
+        T = x.shape[0]
+        out = np.zeros((T, self.model.n_vocab), np.float32)
+        e = _err()
+        if self.s.logits(self.addr, x.ctypes.data, T, out.ctypes.data, e, 512):
+            _raise(e)
+        return out
+
+    def rollback(self, n_past: int) -> None:
+        e = _err()
+        if self.s.rollback(self.addr, n_past, e, 512):
+            _raise(e)
+
+    def reset(self) -> None:
+        self.s.reset(self.addr)
+
+    @property
+    def keep(self) -> int:
+        return self.s.keep
+
+    @keep.setter
+    def keep(self, v: int) -> None:
+        self.s.keep = v
+
+    @property
+    def n_past(self) -> int:
+        return self.s.n_past
+
+    @property
+    def ck(self):
+        return self.s.ck_start, self.s.ck_T
+
+    @property
+    def backend(self) -> str:
+        return self.s.backend.decode()
+
+    def decode(self, prompt, n_gen: int, want_margins: bool = False):
+        """Device-resident greedy decode (xj_cuda_decode). Returns (ids, margins or None, gpu_ms[2])."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(n_gen, np.int32)
+        mar = np.zeros(n_gen, np.float32) if want_margins else None
+        ms = np.zeros(2, np.float32)
+        e = _err()
+        rc = lib().xj_cuda_decode(self.addr, p.ctypes.data, p.size, n_gen, out.ctypes.data,
+                                  mar.ctypes.data if mar is not None else None, ms.ctypes.data, e, 512)
+        if rc:
+            _raise(e)
+        return out, mar, ms
+
+    def close(self):
+        if self.p:
+            self.s.destroy(self.addr)
+            self.p = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
