@@ -192,7 +192,7 @@ def main():
     cfg = synth.CONFIG3
     path = synth.cached_gguf(cfg, os.environ.get("XJ_MODEL_DIR", f"/tmp/xj_models_r{local}"))
     model = xjcuda.Model(path)
-    n_ctx = args.prompt + args.warmup + args.steps + 8
+    n_ctx = args.prompt + max(args.warmup, 3) + 2 * args.steps + 16   # prefill + warm-up + timed + e2e runs
     stage = xjcuda.Stage(model, 0, model.n_layer, n_ctx, 8)
     prompt = np.random.default_rng(1234 + rank).integers(0, cfg.n_vocab, args.prompt).astype(np.int32)
 

@@ -263,26 +263,31 @@ __global__ void __launch_bounds__(128) k_attn(const float *qrot, const float *qg
     const float scale = 1.0f / sqrtf((float)D);
     float qv[DPL], o[DPL];
     const float *qp = qrot + ((size_t)t * H + h) * D;
+    const bool on = lane * DPL < D;   // head dims below 32 leave the upper lanes idle
 #pragma unroll
-    for (int d = 0; d < DPL; d++) { qv[d] = qp[lane * DPL + d]; o[d] = 0.0f; }
+    for (int d = 0; d < DPL; d++) { qv[d] = on ? qp[lane * DPL + d] : 0.0f; o[d] = 0.0f; }
     float m = -INFINITY, l = 0.0f;
     for (int j = warp; j < n; j += 4) {
         const KV *kr = kc + (size_t)j * kvd + (size_t)kvh * D + lane * DPL;
         float s = 0.0f;
+        if (on) {
 #pragma unroll
-        for (int d = 0; d < DPL; d++) s = fmaf(qv[d], load_kv(kr + d), s);
+            for (int d = 0; d < DPL; d++) s = fmaf(qv[d], load_kv(kr + d), s);
+        }
         s = warp_sum(s) * scale;
         const float mn = fmaxf(m, s);
         const float corr = expf(m - mn), p = expf(s - mn);
         l = l * corr + p;
-        const KV *vr = vc + (size_t)j * kvd + (size_t)kvh * D + lane * DPL;
+        if (on) {
+            const KV *vr = vc + (size_t)j * kvd + (size_t)kvh * D + lane * DPL;
 #pragma unroll
-        for (int d = 0; d < DPL; d++) o[d] = fmaf(p, load_kv(vr + d), o[d] * corr);
+            for (int d = 0; d < DPL; d++) o[d] = fmaf(p, load_kv(vr + d), o[d] * corr);
+        }
         m = mn;
     }
     if (lane == 0) { sm_m[warp] = m; sm_l[warp] = l; }
 #pragma unroll
-    for (int d = 0; d < DPL; d++) sm_o[warp][lane * DPL + d] = o[d];
+    for (int d = 0; d < DPL; d++) sm_o[warp][lane * DPL + d] = o[d];   // lane*DPL + d < 32*DPL <= 256
     __syncthreads();
     if (warp == 0) {
         float M = fmaxf(fmaxf(sm_m[0], sm_m[1]), fmaxf(sm_m[2], sm_m[3]));
@@ -293,6 +298,7 @@ __global__ void __launch_bounds__(128) k_attn(const float *qrot, const float *qg
 #pragma unroll
         for (int d = 0; d < DPL; d++) {
             const int i = lane * DPL + d;
+            if (i >= D) break;
             float acc = 0.0f;
 #pragma unroll
             for (int w = 0; w < 4; w++) acc = fmaf(sm_o[w][i], c[w], acc);

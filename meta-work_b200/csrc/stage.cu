@@ -519,8 +519,16 @@ xj_stage *xj_cuda_stage_new(const xj_model *m, int l0, int l1, int n_ctx, int ma
     }
     if (hp->conv_k < 2 || hp->conv_k > 9) { seterr(err, errlen, "conv kernel %d not supported", hp->conv_k); return nullptr; }
     if (n_ctx <= 0 || max_batch <= 0) { seterr(err, errlen, "n_ctx and max_batch must be positive"); return nullptr; }
-    for (int il = l0; il < l1; il++)
-        if (!m->layers[il].ffn_down.data) { seterr(err, errlen, "layer %d weights are not mapped", il); return nullptr; }
+    for (int il = l0; il < l1; il++) {
+        const xj_layer &X = m->layers[il];
+        if (!X.ffn_down.data) { seterr(err, errlen, "layer %d weights are not mapped", il); return nullptr; }
+        // every matrix-vector product reads its input 8 elements at a time
+        const xj_w *mats[] = {&X.ffn_gate, &X.ffn_up, &X.ffn_down, &X.ssm_qkv, &X.ssm_gate, &X.ssm_beta, &X.ssm_alpha,
+                              &X.ssm_out, &X.wqkv, &X.wq, &X.wk, &X.wv, &X.wo};
+        for (const xj_w *w : mats)
+            if (w->nbytes && w->ne0 % 8) { seterr(err, errlen, "layer %d: row length %lld is not a multiple of 8", il, (long long)w->ne0); return nullptr; }
+    }
+    if (n_ctx > (1 << 24)) { seterr(err, errlen, "n_ctx %d too large", n_ctx); return nullptr; }
     if (has_head && !m->output.data) { seterr(err, errlen, "output head is not mapped"); return nullptr; }
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) { seterr(err, errlen, "no CUDA device"); return nullptr; }
