@@ -44,7 +44,9 @@ uint64_t xjc_stage_state_bytes(const xj_model *m, int l0, int l1, int n_ctx, int
 //   XJC_OPT_KV_F32   1 = float32 KV cache (matches the CPU oracle's cache), 0 = float16 (default,
 //                    the Metal backend's and the BASELINE precision).
 //   XJC_OPT_GEMV     0 = fastest path per type (default), 1 = generic per-element path for every type.
-enum { XJC_OPT_KV_F32 = 1, XJC_OPT_GEMV = 2 };
+//   XJC_OPT_PDL      1 = kernels of a step overlap through programmatic dependent launch (default),
+//                    0 = each kernel starts after its predecessor completes.
+enum { XJC_OPT_KV_F32 = 1, XJC_OPT_GEMV = 2, XJC_OPT_PDL = 3 };
 int xj_cuda_set_options(int which, int value);
 
 // Greedy decode on a stage covering [0, n_layer) with the head. Feeds n_prompt ids (prefill in
@@ -54,6 +56,16 @@ int xj_cuda_set_options(int which, int value);
 // gpu_ms (may be NULL) receives [prefill ms, decode ms] measured with CUDA events on the stage stream.
 int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, int32_t *out, float *margins,
                    float *gpu_ms, char *err, size_t errlen);
+
+// Matrix-vector product on host buffers with the decode kernels: y[t][n] = W[n] . x[t] for t < T
+// (1 <= T <= 16), W an [n][k] matrix in GGUF block layout of `type`. path 0 = fastest available
+// kernel, 1 = generic per-element kernel. For parity tests of the kernel that dominates decode.
+int xj_cuda_gemv(int type, const void *w, int k, int n, const float *x, int T, float *y, int path, char *err,
+                 size_t errlen);
+// Average device time (ms) of one such launch over `iters` launches that rotate through `copies`
+// distinct device copies of W, so the last-level cache cannot serve the weights (GEMV microbenchmark).
+int xj_cuda_gemv_time(int type, const void *w, int k, int n, int T, int copies, int iters, int path, float *ms,
+                      char *err, size_t errlen);
 
 // Number of kernel launches in one replay of the stage's cached decode-step graph (0 before the first
 // xj_cuda_decode call that generated more than one token).

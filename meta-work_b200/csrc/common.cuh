@@ -8,12 +8,14 @@
 
 #define XJ_DEV __device__ __forceinline__
 
-// A weight matrix resident in HBM in the GGUF block layout: N rows of K elements, row r at p + r*ld.
+// A weight matrix resident in HBM: N rows of K elements. Row-major GGUF block layout (row r at
+// p + r*ld) and/or the tensor-core tiled layout (tq/th/ts/td, see gemv_mma.cuh); either may be absent.
 struct DevMat {
     const uint8_t *p;
     int type;        // enum xj_type
     int K, N;
-    long long ld;    // bytes between rows
+    long long ld;    // bytes between rows (row-major layout)
+    const uint8_t *tq = nullptr, *th = nullptr, *ts = nullptr, *td = nullptr;
 };
 
 XJ_DEV float warp_sum(float v) {

@@ -1,9 +1,697 @@
-// Tensor-core GEMV path (placeholder until the mma kernels land): nothing is routed here yet.
+// Tensor-core decode GEMV for Q4_K / Q6_K / Q8_0 weights: y[t][r] (+)= W[r] . f(x[t]), T <= 4 tokens.
+//
+// The arithmetic is the reference matmul (core/xj_cpu.c:36-54: dequantise, fp32 dot product) reorganised
+// so the tensor cores do the multiply-adds without losing fp32 accuracy:
+//
+//   * weights enter the MMA as their exact small integer codes (Q4_K q in 0..15, Q6_K q-32 as
+//     lo + 16*hi - 32, Q8_0 q in -127..127), which fp16 represents exactly;
+//   * each activation is split into two fp16 values x = hi + lo (after an exact power-of-two range
+//     scaling), so the pair carries ~22 mantissa bits; the two halves are separate MMA columns;
+//   * the per-block scales (d*sc, dmin*m, d) multiply the fp32 MMA partial sums of each 16- or 32-wide
+//     block, and the Q4_K "- dmin*m" term is applied once per block via the block sums of x.
+//
+// mma.sync.m16n8k16 (f16 inputs, f32 accumulate): A = 16 weight rows x 16 codes, B = 16 codes x 8
+// columns where column n = 2*token + split. The weights are re-laid-out at upload ("tiled" layout, same
+// byte count, bit-exact re-encoding of the GGUF blocks): for every 16-row tile the payload of each warp
+// k-step is stored in the exact register order of the A fragment, and every (tile, unit) is contiguous.
+//
+// Streaming: at most one CTA per SM; each CTA owns a contiguous range of tiles and streams their
+// weights through a ring of shared-memory stages filled by bulk asynchronous copies (cp.async.bulk with
+// an mbarrier per stage; no multicast). The first stages are requested before griddepcontrol.wait, so
+// under programmatic dependent launch a kernel's weight stream starts while its predecessor finishes;
+// registers stay free, so the two kernels' CTAs fit on an SM together.
+//
+// Fused prologues f: RMSNorm (core/xj_cpu.c:56-61), SwiGLU silu(g)*u (:273). Fused epilogues:
+// store, residual add (:268,275), causal conv + SiLU over the T tokens of each channel (:172-182, the
+// GDN qkv rows), per-tile argmax partials of the LM head (core/xj_spec.c:12-16).
+//
+// Every token column is computed independently in a fixed order, so a token's result does not depend
+// on how many other tokens share the launch (decode T=1 and speculative verify T>1 agree bit for bit).
 #pragma once
+#include <vector>
+
 #include "kernels.cuh"
 
 namespace xjk {
-constexpr int MMA_MAXT = 0;
-inline bool mma_supported(const DevMat &) { return false; }
-inline void launch_gemv_mma(const GemvJob &, const float *, long long, int, cudaStream_t) {}
+
+constexpr int MMA_MAXT = 4;
+constexpr int MMA_WARPS = 16;
+constexpr int MMA_KMAX_PT = 12;   // prologue elements per thread: K <= 12 * 512
+
+enum { PRO_NONE = 0, PRO_NORM = 1, PRO_SWIGLU = 2 };
+enum { EPI_STORE = 0, EPI_ADD = 1, EPI_CONV = 2, EPI_ARGMAX = 3 };
+
+// Tiled weight (see repack_tiled below).
+struct Tiled {
+    const uint8_t *q = nullptr;   // fragment-ordered codes
+    const uint8_t *h = nullptr;   // Q6_K high 2-bit planes
+    const uint8_t *s = nullptr;   // per-row block headers (scales)
+    const uint8_t *d = nullptr;   // Q6_K / Q8_0 fp16 d per row-block
+    int type = 0, K = 0, N = 0;
+    int nu = 0;                   // units per row: Q4_K/Q6_K super-blocks (K/256), Q8_0 blocks (K/32)
+};
+
+inline Tiled tiled_of(const DevMat &m) {
+    Tiled t;
+    t.q = m.tq; t.h = m.th; t.s = m.ts; t.d = m.td; t.type = m.type; t.K = m.K; t.N = m.N;
+    t.nu = m.type == XJ_Q8_0 ? m.K / 32 : m.K / 256;
+    return t;
+}
+
+struct MmaJob {
+    Tiled w;
+    float *y;              // output rows (may be null for EPI_ARGMAX)
+    long long ldy;
+    int epi;
+    // EPI_CONV: rows are conv channels; state [N][kc-1], weights [N][kc], checkpoints [T-1][N][kc-1]
+    float *conv_state;
+    const float *conv_w;
+    float *conv_ck;
+    int kc;
+    // EPI_ARGMAX (T = 1): per-tile best value, runner-up value, best index
+    float *pbest, *psecond;
+    int *pidx;
+};
+
+struct MmaArgs {
+    MmaJob job[4];
+    int njob;
+    int tile_start[5];     // prefix sums of 16-row tiles over jobs
+    int tiles_per_cta;     // each CTA owns tiles [blockIdx.x * tiles_per_cta, ...)
+    const float *x;        // input [T][K] (PRO_SWIGLU: gate values)
+    const float *x2;       // PRO_SWIGLU: up values
+    long long ldx;
+    int T, K;
+    int pro;
+    const float *norm_w;   // PRO_NORM weights
+    float eps;
+    int *err;              // set to 1 when a wait for the weight stream gives up
+};
+
+// Bytes per unit in each tiled region, units per streamed chunk, ring depth.
+template <int TYPE> struct Geo;
+// A ring of ~54 KB per CTA keeps enough bytes in flight per SM for HBM bandwidth while leaving room
+// for the next kernel's CTA on the same SM.
+template <> struct Geo<XJ_Q4_K> { static constexpr int QB = 2048, HB = 0, SB = 256, DB = 0, CU = 8, STAGES = 3; };
+template <> struct Geo<XJ_Q6_K> { static constexpr int QB = 2048, HB = 1024, SB = 256, DB = 32, CU = 8, STAGES = 2; };
+template <> struct Geo<XJ_Q8_0> { static constexpr int QB = 512, HB = 0, SB = 0, DB = 32, CU = 32, STAGES = 3; };
+template <int TYPE> constexpr int unit_bytes() { return Geo<TYPE>::QB + Geo<TYPE>::HB + Geo<TYPE>::SB + Geo<TYPE>::DB; }
+template <int TYPE> constexpr int stage_bytes() { return Geo<TYPE>::CU * unit_bytes<TYPE>(); }
+
+// ------------------------------------------------------------------ PTX helpers
+XJ_DEV uint32_t smem_u32(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+XJ_DEV void mbar_init(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(smem_u32(bar)), "r"(count) : "memory");
+}
+XJ_DEV void mbar_expect_tx(uint64_t *bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(smem_u32(bar)), "r"(bytes) : "memory");
+}
+XJ_DEV bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
+// Bounded wait: gives up after a fixed number of polls (each poll may suspend the thread briefly),
+// records the failure in *err and returns false instead of hanging.
+XJ_DEV bool mbar_wait(uint64_t *bar, uint32_t parity, int *err) {
+    for (int it = 0; it < (1 << 22); it++)
+        if (mbar_try_wait(bar, parity)) return true;
+    if (err) atomicExch(err, 1);
+    return false;
+}
+XJ_DEV void bulk_g2s(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(smem_u32(dst)), "l"(src), "r"(bytes), "r"(smem_u32(bar)) : "memory");
+}
+
+XJ_DEV uint32_t lop3_and_or(uint32_t a, uint32_t mask, uint32_t magic) {
+    uint32_t r;
+    asm("lop3.b32 %0, %1, %2, %3, 0xEA;" : "=r"(r) : "r"(a), "r"(mask), "r"(magic));   // (a & b) | c
+    return r;
+}
+
+XJ_DEV uint32_t hsub2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("sub.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
+XJ_DEV uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
+    uint32_t r;
+    asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
+    return r;
+}
+
+XJ_DEV void mma16816(float *d, const uint32_t *a, uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Q4_K / Q6_K low nibbles of one k-step word -> exact fp16 codes in A-fragment order.
+// Word bits: a0 at 0-3 / 16-19, a1 at 4-7 / 20-23, a2 at 8-11 / 24-27, a3 at 12-15 / 28-31.
+XJ_DEV void nib_frag(uint32_t w, uint32_t *a) {
+    const uint32_t w8 = w >> 8;
+    a[0] = hsub2(lop3_and_or(w, 0x000F000Fu, 0x64006400u), 0x64006400u);    // 1024 + q - 1024
+    a[1] = hsub2(lop3_and_or(w, 0x00F000F0u, 0x54005400u), 0x54005400u);    //   64 + q - 64
+    a[2] = hsub2(lop3_and_or(w8, 0x000F000Fu, 0x64006400u), 0x64006400u);
+    a[3] = hsub2(lop3_and_or(w8, 0x00F000F0u, 0x54005400u), 0x54005400u);
+}
+
+// Q6_K high 2-bit fields (bits 2r..2r+1 of each half of hw) -> 16*h - 32, exact in fp16.
+XJ_DEV void hi_frag(uint32_t hw, uint32_t *a) {
+    a[0] = hfma2(lop3_and_or(hw, 0x00030003u, 0x64006400u), 0x4C004C00u, 0xF402F402u);   // (1024+h)*16 - 16416
+    a[1] = hfma2(lop3_and_or(hw, 0x000C000Cu, 0x5C005C00u), 0x4C004C00u, 0xEC08EC08u);   // ( 256+h)*16 -  4128
+    a[2] = hfma2(lop3_and_or(hw, 0x00300030u, 0x54005400u), 0x4C004C00u, 0xE420E420u);   // (  64+h)*16 -  1056
+    a[3] = hfma2(lop3_and_or(hw, 0x00C000C0u, 0x4C004C00u), 0x4C004C00u, 0xDC80DC80u);   // (  16+h)*16 -   288
+}
+
+// Q8_0 signed bytes [p0 p1 p2 p3] -> fp16 pairs (p0, p1) and (p2, p3), exact.
+XJ_DEV void q8_frag(uint32_t w0, uint32_t w1, uint32_t *a) {
+    const uint32_t u0 = w0 ^ 0x80808080u, u1 = w1 ^ 0x80808080u;                 // q + 128
+    a[0] = hsub2(__byte_perm(u0, 0x64646464u, 0x4140), 0x64806480u);             // 1024 + 128 + q - 1152
+    a[1] = hsub2(__byte_perm(u0, 0x64646464u, 0x4342), 0x64806480u);
+    a[2] = hsub2(__byte_perm(u1, 0x64646464u, 0x4140), 0x64806480u);
+    a[3] = hsub2(__byte_perm(u1, 0x64646464u, 0x4342), 0x64806480u);
+}
+
+XJ_DEV uint32_t word_of(const uint4 &v, int i) { return i == 0 ? v.x : i == 1 ? v.y : i == 2 ? v.z : v.w; }
+XJ_DEV uint32_t byte_of(const uint4 &v, int i) { return (word_of(v, i >> 2) >> (8 * (i & 3))) & 0xffu; }
+
+// Q4_K codes of one k-step word as fp16 (64 + q), exact; the constant 64 is removed through the
+// block-sum term (d*sc*(D - 64*S) - dmin*m*S = d*sc*D - (64*d*sc + dmin*m)*S).
+XJ_DEV void nib_frag64(uint32_t w, uint32_t *a) {
+    a[0] = lop3_and_or(w << 4, 0x00F000F0u, 0x54005400u);
+    a[1] = lop3_and_or(w, 0x00F000F0u, 0x54005400u);
+    a[2] = lop3_and_or(w >> 4, 0x00F000F0u, 0x54005400u);
+    a[3] = lop3_and_or(w >> 8, 0x00F000F0u, 0x54005400u);
+}
+
+// Position of column k (0..15) of a k-step in the staged activations: lane quad c finds columns
+// 2c, 2c+1, 2c+8, 2c+9 (its two B-fragment registers) as 4 adjacent halves.
+__host__ __device__ inline int bperm(int k) { return ((k & 7) >> 1) * 4 + (k >> 3) * 2 + (k & 1); }
+
+// ------------------------------------------------------------------ one unit from a shared-memory stage
+// Accumulate into (yg, yg8) (rows g, g+8 of the tile, token c) unit ui of the staged chunk (global unit
+// u of its tile). K-quant units are shared by two warps: half hh takes k-steps 8hh..8hh+7. xb: this
+// lane's B-fragment row (column g), valid when bcol; xsum_t: 32-wide block sums of token c (Q4_K);
+// scw: this warp's 128-float scale scratch.
+template <int TYPE>
+XJ_DEV void unit_compute(const uint8_t *stage, int ui, int u, int hh, int lane, bool bcol, const __half *xb,
+                         const float *xsum_t, float *scw, float &yg, float &yg8) {
+    using G = Geo<TYPE>;
+    const int g = lane >> 2;
+    const uint8_t *qs = stage + ui * G::QB;
+    if constexpr (TYPE == XJ_Q4_K) {
+        const uint8_t *ss = stage + G::CU * G::QB + ui * G::SB;
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh) * 32 + lane) * 16);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh + 1) * 32 + lane) * 16);
+        {   // (d*sc, 64*d*sc + dmin*m) for row r, sub-blocks 4hh + 2*(lane>>4) + {0,1} (core/xj_quant.h:49-52)
+            const int r = lane & 15;
+            const uint4 hdr = *reinterpret_cast<const uint4 *>(ss + r * 16);
+            const float d = h2f((uint16_t)(hdr.x & 0xffff)), dmin = h2f((uint16_t)(hdr.x >> 16));
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int sbl = 2 * (lane >> 4) + e, sb = 4 * hh + sbl;
+                int s_, m_;
+                if (sb < 4) { s_ = byte_of(hdr, 4 + sb) & 63; m_ = byte_of(hdr, 8 + sb) & 63; }
+                else {
+                    s_ = (byte_of(hdr, 8 + sb) & 0xF) | ((byte_of(hdr, sb) >> 6) << 4);
+                    m_ = (byte_of(hdr, 8 + sb) >> 4) | ((byte_of(hdr, 4 + sb) >> 6) << 4);
+                }
+                const float d1 = d * (float)s_, m1 = dmin * (float)m_;
+                float *o = scw + ((sbl * 8 + (r & 7)) * 4 + (r >> 3) * 2);
+                o[0] = d1;
+                o[1] = 64.0f * d1 + m1;
+            }
+        }
+        __syncwarp();
+        const int kb = u * 256;
+#pragma unroll
+        for (int sbl = 0; sbl < 4; sbl++) {
+            float d4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int s = 8 * hh + 2 * sbl + e;            // k-step within the super-block
+                uint32_t af[4];
+                nib_frag64(word_of(e + 2 * sbl < 4 ? q0 : q1, (2 * sbl + e) & 3), af);
+                uint2 bv = make_uint2(0u, 0u);
+                if (bcol) bv = *reinterpret_cast<const uint2 *>(xb + kb + 16 * s);
+                mma16816(d4, af, bv.x, bv.y);
+            }
+            const float4 sc4 = *reinterpret_cast<const float4 *>(scw + (sbl * 8 + g) * 4);
+            const float S = xsum_t ? xsum_t[(kb >> 5) + 4 * hh + sbl] : 0.0f;
+            yg = fmaf(sc4.x, d4[0] + d4[1], yg);
+            yg = fmaf(-sc4.y, S, yg);
+            yg8 = fmaf(sc4.z, d4[2] + d4[3], yg8);
+            yg8 = fmaf(-sc4.w, S, yg8);
+        }
+        __syncwarp();
+    } else if constexpr (TYPE == XJ_Q6_K) {
+        const uint8_t *hs = stage + G::CU * G::QB + ui * G::HB;
+        const uint8_t *ss = stage + G::CU * (G::QB + G::HB) + ui * G::SB;
+        const uint8_t *ds = stage + G::CU * (G::QB + G::HB + G::SB) + ui * G::DB;
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh) * 32 + lane) * 16);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh + 1) * 32 + lane) * 16);
+        const uint4 hq = *reinterpret_cast<const uint4 *>(hs + (hh * 32 + lane) * 16);
+        {   // d*sc for row r, k-steps 8hh + 4*(lane>>4) + {0..3} (core/xj_quant.h:106-118)
+            const int r = lane & 15;
+            const uint4 sc = *reinterpret_cast<const uint4 *>(ss + r * 16);
+            const float d = h2f(*reinterpret_cast<const uint16_t *>(ds + r * 2));
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int sl = 4 * (lane >> 4) + e;
+                scw[(sl * 8 + (r & 7)) * 2 + (r >> 3)] = d * (float)(int8_t)byte_of(sc, 8 * hh + sl);
+            }
+        }
+        __syncwarp();
+        const int kb = u * 256;
+#pragma unroll
+        for (int sl = 0; sl < 8; sl++) {
+            const int s = 8 * hh + sl;
+            float d4[4] = {0.f, 0.f, 0.f, 0.f};
+            uint32_t af[4], ah[4];
+            nib_frag(word_of(sl < 4 ? q0 : q1, sl & 3), af);
+            uint32_t hw = word_of(hq, sl >> 1);
+            if (sl & 1) hw >>= 8;
+            hi_frag(hw, ah);
+            uint2 bv = make_uint2(0u, 0u);
+            if (bcol) bv = *reinterpret_cast<const uint2 *>(xb + kb + 16 * s);
+            mma16816(d4, af, bv.x, bv.y);
+            mma16816(d4, ah, bv.x, bv.y);
+            const float2 sc2 = *reinterpret_cast<const float2 *>(scw + (sl * 8 + g) * 2);
+            yg = fmaf(sc2.x, d4[0] + d4[1], yg);
+            yg8 = fmaf(sc2.y, d4[2] + d4[3], yg8);
+        }
+        __syncwarp();
+    } else {
+        const uint8_t *ds = stage + G::CU * G::QB + ui * G::DB;
+        const uint4 q = *reinterpret_cast<const uint4 *>(qs + lane * 16);
+        const float dv = lane < 16 ? h2f(*reinterpret_cast<const uint16_t *>(ds + lane * 2)) : 0.0f;
+        const float dg = __shfl_sync(0xffffffffu, dv, g), dg8 = __shfl_sync(0xffffffffu, dv, g + 8);
+        float d4[4] = {0.f, 0.f, 0.f, 0.f};
+        const int kb = u * 32;
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            uint32_t af[4];
+            q8_frag(word_of(q, 2 * e), word_of(q, 2 * e + 1), af);
+            uint2 bv = make_uint2(0u, 0u);
+            if (bcol) bv = *reinterpret_cast<const uint2 *>(xb + kb + 16 * e);
+            mma16816(d4, af, bv.x, bv.y);
+        }
+        yg = fmaf(dg, d4[0] + d4[1], yg);
+        yg8 = fmaf(dg8, d4[2] + d4[3], yg8);
+    }
+}
+
+// ------------------------------------------------------------------ shared-memory layout
+struct MmaSmem {
+    int T, K, xstride;        // halves per activation column (row of the staged B operand)
+    size_t off_ring, off_xs, off_sum, off_sc, off_red, bytes;
+    __host__ __device__ MmaSmem(int T_, int K_, int ring_bytes) : T(T_), K(K_) {
+        xstride = K + 16;                                   // 16-half pad: conflict-free 8-byte B loads
+        off_ring = 0;                                       // weight stages (16-byte aligned)
+        off_xs = off_ring + (size_t)ring_bytes;
+        off_sum = off_xs + (size_t)2 * T * xstride * 2;     // fp16 columns 2t (hi) and 2t+1 (lo)
+        off_sum = (off_sum + 15) & ~(size_t)15;
+        off_sc = off_sum + (size_t)T * (K / 32) * 4;        // fp32 sums of hi+lo per 32-wide block
+        off_sc = (off_sc + 15) & ~(size_t)15;
+        off_red = off_sc + (size_t)MMA_WARPS * 128 * 4;     // per-warp staged scales
+        bytes = off_red + (size_t)MMA_WARPS * 16 * 4 * 4 + 64;
+    }
+};
+
+// ------------------------------------------------------------------ kernel
+template <int TYPE>
+__global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
+    using G = Geo<TYPE>;
+    constexpr int SB = stage_bytes<TYPE>(), NS = G::STAGES;
+    constexpr bool KQ = TYPE != XJ_Q8_0;                 // K-quant units are split over two warps
+    extern __shared__ __align__(128) uint8_t smem[];
+    const MmaSmem L(a.T, a.K, SB * NS);
+    uint8_t *ring = smem + L.off_ring;
+    __half *xs = reinterpret_cast<__half *>(smem + L.off_xs);
+    float *xsum = reinterpret_cast<float *>(smem + L.off_sum);
+    float *scs = reinterpret_cast<float *>(smem + L.off_sc);
+    float *red = reinterpret_cast<float *>(smem + L.off_red);
+    __shared__ __align__(8) uint64_t bars[NS];
+    __shared__ float tok_scale[MMA_MAXT], tok_nsc[MMA_MAXT];
+    __shared__ float pred[MMA_WARPS][MMA_MAXT][2];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+    const int T = a.T, K = a.K;
+    const int total = a.tile_start[a.njob];
+    const int ta = blockIdx.x * a.tiles_per_cta;
+    const int tb = ta + a.tiles_per_cta < total ? ta + a.tiles_per_cta : total;
+    const int nu = a.job[0].w.nu;                       // all jobs of a launch share K
+    const int nch = (nu + G::CU - 1) / G::CU;           // chunks per tile
+    const int nchunks = (tb - ta) * nch;
+
+    // chunk i -> (job, tile within job, first unit, units)
+    auto chunk_of = [&](int i, int &j, int &tile, int &u0, int &cu) {
+        const int tg = ta + i / nch, ci = i % nch;
+        j = 0;
+        while (tg >= a.tile_start[j + 1]) j++;
+        tile = tg - a.tile_start[j];
+        u0 = ci * G::CU;
+        cu = nu - u0 < G::CU ? nu - u0 : G::CU;
+    };
+    auto issue = [&](int i) {   // one thread: request chunk i into stage i % NS
+        int j, tile, u0, cu;
+        chunk_of(i, j, tile, u0, cu);
+        const Tiled &W = a.job[j].w;
+        uint8_t *st = ring + (size_t)(i % NS) * SB;
+        uint64_t *bar = &bars[i % NS];
+        const size_t tu0 = (size_t)tile * nu + u0;
+        mbar_expect_tx(bar, (uint32_t)(cu * unit_bytes<TYPE>()));
+        bulk_g2s(st, W.q + tu0 * G::QB, cu * G::QB, bar);
+        if (G::HB) bulk_g2s(st + G::CU * G::QB, W.h + tu0 * G::HB, cu * G::HB, bar);
+        if (G::SB) bulk_g2s(st + G::CU * (G::QB + G::HB), W.s + tu0 * G::SB, cu * G::SB, bar);
+        if (G::DB) bulk_g2s(st + G::CU * (G::QB + G::HB + G::SB), W.d + tu0 * G::DB, cu * G::DB, bar);
+    };
+
+    // ---- 1. request the first stages of weights (independent of the producer kernel)
+    if (tid == 0) {
+        for (int s = 0; s < NS; s++) mbar_init(&bars[s], 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int i = 0; i < NS && i < nchunks; i++) issue(i);
+    }
+    griddep_launch();
+    griddep_wait();
+
+    // ---- 2. prologue: f(x) -> range scale -> fp16 hi/lo columns (+ Q4_K block sums); x read once
+    constexpr int XPT = MMA_KMAX_PT;
+    for (int t = 0; t < T; t++) {
+        const float *xr = a.x + t * a.ldx;
+        float v[XPT];
+        float ss = 0.0f, am = 0.0f;
+#pragma unroll
+        for (int k = 0; k < XPT; k++) {
+            const int i = tid + k * MMA_WARPS * 32;
+            float val = 0.0f;
+            if (i < K) {
+                const float xv = xr[i];
+                if (a.pro == PRO_NORM) { ss = fmaf(xv, xv, ss); val = xv * a.norm_w[i]; }
+                else if (a.pro == PRO_SWIGLU) val = silu_f(xv) * a.x2[t * a.ldx + i];
+                else val = xv;
+                v[k] = a.pro == PRO_NORM ? xv : val;
+            }
+            am = fmaxf(am, fabsf(val));
+        }
+        ss = warp_sum(ss);
+        am = warp_max(am);
+        if (lane == 0) { pred[warp][t][0] = ss; pred[warp][t][1] = am; }
+        __syncthreads();
+        if (tid == 0) {
+            double tss = 0;
+            float tam = 0.0f;
+            for (int w = 0; w < MMA_WARPS; w++) { tss += pred[w][t][0]; tam = fmaxf(tam, pred[w][t][1]); }
+            float nsc = 1.0f;
+            if (a.pro == PRO_NORM) nsc = 1.0f / sqrtf((float)(tss / K) + a.eps);
+            // the largest |f(x)| lands in [2^14, 2^15): fp16 hi/lo stay finite with full relative precision
+            const float m = tam * nsc;
+            tok_nsc[t] = nsc;
+            tok_scale[t] = ldexpf(1.0f, 14 - (m > 0.0f ? ilogbf(m) : 0));
+        }
+        __syncthreads();
+        const float sc = tok_scale[t], nsc = tok_nsc[t];
+        __half *col_hi = xs + (size_t)(2 * t) * L.xstride, *col_lo = xs + (size_t)(2 * t + 1) * L.xstride;
+#pragma unroll
+        for (int k = 0; k < XPT; k++) {
+            const int i = tid + k * MMA_WARPS * 32;
+            if (i < K) {
+                // PRO_NORM: (x * nsc) * w as core/xj_cpu.c:60, then the exact power-of-two scale
+                const float val = (a.pro == PRO_NORM ? (v[k] * nsc) * a.norm_w[i] : v[k]) * sc;
+                const __half hi = __float2half_rn(val);
+                const __half lo = __float2half_rn(val - __half2float(hi));
+                const int pos = (i & ~15) + bperm(i & 15);
+                col_hi[pos] = hi;
+                col_lo[pos] = lo;
+                if (TYPE == XJ_Q4_K) {
+                    // elements i..i+31 of a warp form one 32-wide block; sum what the MMA multiplies
+                    const float bs = warp_sum(__half2float(hi) + __half2float(lo));
+                    if (lane == 0) xsum[t * (K / 32) + (i >> 5)] = bs;
+                }
+            }
+        }
+    }
+    __syncthreads();
+
+    // ---- 3. stream the chunks: wait for the stage, compute, release, refill
+    const bool bcol = g < 2 * T;
+    const __half *xb = xs + (size_t)g * L.xstride + 4 * c;
+    const float *xsum_t = (TYPE == XJ_Q4_K && c < T) ? xsum + c * (K / 32) : nullptr;
+    float *scw = scs + warp * 128;
+    float yg = 0.0f, yg8 = 0.0f;
+    for (int i = 0; i < nchunks; i++) {
+        int j, tile, u0, cu;
+        chunk_of(i, j, tile, u0, cu);
+        mbar_wait(&bars[i % NS], (uint32_t)((i / NS) & 1), a.err);
+        const uint8_t *st = ring + (size_t)(i % NS) * SB;
+        if (KQ) {
+            const int ui = warp >> 1;
+            if (ui < cu) unit_compute<TYPE>(st, ui, u0 + ui, warp & 1, lane, bcol, xb, xsum_t, scw, yg, yg8);
+        } else {
+#pragma unroll
+            for (int k = 0; k < G::CU / MMA_WARPS; k++) {
+                const int ui = warp + k * MMA_WARPS;
+                if (ui < cu) unit_compute<TYPE>(st, ui, u0 + ui, 0, lane, bcol, xb, xsum_t, scw, yg, yg8);
+            }
+        }
+        const bool tile_end = (i % nch) == nch - 1;
+        if (tile_end) {
+            red[(warp * 16 + g) * 4 + c] = yg;
+            red[(warp * 16 + g + 8) * 4 + c] = yg8;
+            yg = 0.0f; yg8 = 0.0f;
+        }
+        __syncthreads();   // stage i % NS is free; red holds the tile's per-warp partials
+        if (tid == 0 && i + NS < nchunks) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue(i + NS);
+        }
+        if (!tile_end) continue;
+        // ---- 4. epilogue of the tile: fixed-order sum over warps
+        const MmaJob &jb = a.job[j];
+        if (jb.epi == EPI_CONV) {
+            // one thread per channel: the T tokens in order through the rolling conv state
+            if (tid < 16) {
+                const int ch = tile * 16 + tid, kc = jb.kc;
+                float cs[8];
+                for (int k = 0; k < kc - 1; k++) cs[k] = jb.conv_state[(size_t)ch * (kc - 1) + k];
+                const float *wc = jb.conv_w + (size_t)ch * kc;
+                for (int t = 0; t < T; t++) {
+                    float s = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + tid) * 4 + t];
+                    s /= tok_scale[t];
+                    float acc = 0.0f;
+                    for (int k = 0; k < kc - 1; k++) acc = fmaf(cs[k], wc[k], acc);
+                    acc = fmaf(s, wc[kc - 1], acc);
+                    for (int k = 0; k < kc - 2; k++) cs[k] = cs[k + 1];
+                    cs[kc - 2] = s;
+                    jb.y[t * jb.ldy + ch] = silu_f(acc);
+                    if (jb.conv_ck && t < T - 1)
+                        for (int k = 0; k < kc - 1; k++) jb.conv_ck[((size_t)t * jb.w.N + ch) * (kc - 1) + k] = cs[k];
+                }
+                for (int k = 0; k < kc - 1; k++) jb.conv_state[(size_t)ch * (kc - 1) + k] = cs[k];
+            }
+        } else if (jb.epi == EPI_ARGMAX) {
+            if (tid < 32) {
+                const int row = tid & 15;
+                float s = 0.0f;
+#pragma unroll
+                for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + row) * 4 + 0];
+                s /= tok_scale[0];
+                if (jb.y && tid < 16) jb.y[(size_t)tile * 16 + row] = s;
+                // best / runner-up / lowest index of the tile's 16 rows (lanes 16..31 mirror 0..15)
+                float b = s, b2 = -INFINITY;
+                int bi = tile * 16 + row;
+#pragma unroll
+                for (int o = 8; o; o >>= 1) {
+                    const float ov = __shfl_xor_sync(0xffffffffu, b, o), ov2 = __shfl_xor_sync(0xffffffffu, b2, o);
+                    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+                    if (ov > b || (ov == b && oi < bi)) { b2 = fmaxf(b, ov2); b = ov; bi = oi; }
+                    else b2 = fmaxf(b2, ov);
+                }
+                if (tid == 0) { jb.pbest[tile] = b; jb.psecond[tile] = b2; jb.pidx[tile] = bi; }
+            }
+        } else if (tid < 64) {
+            const int row = tid >> 2, t = tid & 3;
+            if (t < T) {
+                float s = 0.0f;
+#pragma unroll
+                for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + row) * 4 + t];
+                s /= tok_scale[t];
+                float *yp = jb.y + t * jb.ldy + (size_t)tile * 16 + row;
+                *yp = jb.epi == EPI_ADD ? *yp + s : s;
+            }
+        }
+        __syncthreads();   // red is reused by the next tile
+    }
+}
+
+// ------------------------------------------------------------------ host: launch
+constexpr size_t MMA_SMEM_MAX = 200 * 1024;
+constexpr int MMA_KMAX = MMA_KMAX_PT * MMA_WARPS * 32;   // longest row the prologue stages
+
+inline int ring_bytes(int type) {
+    switch (type) {
+    case XJ_Q4_K: return stage_bytes<XJ_Q4_K>() * Geo<XJ_Q4_K>::STAGES;
+    case XJ_Q6_K: return stage_bytes<XJ_Q6_K>() * Geo<XJ_Q6_K>::STAGES;
+    default: return stage_bytes<XJ_Q8_0>() * Geo<XJ_Q8_0>::STAGES;
+    }
+}
+inline size_t mma_smem_bytes(int type, int T, int K) { return MmaSmem(T, K, ring_bytes(type)).bytes; }
+
+// Matrices the tensor-core path can take (at up to MMA_MAXT tokens).
+inline bool tiled_ok(int type, int K, int N) {
+    if (N % 16 || K > MMA_KMAX) return false;
+    if (type == XJ_Q4_K || type == XJ_Q6_K) { if (K % 256) return false; }
+    else if (type == XJ_Q8_0) { if (K % 32) return false; }
+    else return false;
+    return mma_smem_bytes(type, MMA_MAXT, K) <= MMA_SMEM_MAX;
+}
+
+// Programmatic dependent launch: the kernel may start while its stream predecessor runs; it calls
+// griddepcontrol.wait before touching anything the predecessor writes. g_pdl = 0 launches plainly.
+inline int g_pdl = 1;
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t st, Args... args) {
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[1];
+    at[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    at[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = at;
+    cfg.numAttrs = g_pdl ? 1 : 0;
+    return cudaLaunchKernelEx(&cfg, kern, args...);
+}
+
+// Per-device, once: allow the kernel's dynamic shared memory; returns the SM count.
+template <int TYPE>
+inline int mma_setup() {
+    constexpr int MAXDEV = 64;
+    static int sms[MAXDEV] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= MAXDEV) dev = 0;
+    if (!sms[dev]) {
+        cudaFuncSetAttribute(k_gemv_mma<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM_MAX);
+        cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
+    }
+    return sms[dev];
+}
+
+// One launch for up to 4 same-type matrices sharing the input x[T][K] (T <= MMA_MAXT): at most one CTA
+// per SM, each owning a contiguous, balanced range of tiles.
+template <int TYPE>
+inline cudaError_t launch_mma_t(MmaArgs a, cudaStream_t st) {
+    const int sms = mma_setup<TYPE>();
+    const int tiles = a.tile_start[a.njob];
+    const int ctas = tiles < sms ? tiles : sms;
+    a.tiles_per_cta = (tiles + ctas - 1) / ctas;
+    const dim3 grid((tiles + a.tiles_per_cta - 1) / a.tiles_per_cta), block(MMA_WARPS * 32);
+    return launch_pdl(k_gemv_mma<TYPE>, grid, block, mma_smem_bytes(TYPE, a.T, a.K), st, a);
+}
+
+inline cudaError_t launch_mma(const MmaArgs &a, int type, cudaStream_t st) {
+    switch (type) {
+    case XJ_Q4_K: return launch_mma_t<XJ_Q4_K>(a, st);
+    case XJ_Q6_K: return launch_mma_t<XJ_Q6_K>(a, st);
+    case XJ_Q8_0: return launch_mma_t<XJ_Q8_0>(a, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+
+// ------------------------------------------------------------------ host: tiled re-encoding
+// Host bytes of the tiled layout for an [N][K] GGUF matrix (N % 16 == 0): q, h, s, d regions.
+struct TiledHost {
+    std::vector<uint8_t> q, h, s, d;
+};
+
+inline uint8_t q4k_code(const uint8_t *blk, int col) {   // Q4_K code of column col (0..255) of a super-block
+    const int j = col / 32, l = col % 32;
+    const uint8_t b = blk[16 + 32 * (j / 2) + l];
+    return (j & 1) ? (b >> 4) : (b & 0xF);
+}
+
+inline uint8_t q6k_code(const uint8_t *blk, int col) {   // Q6_K code 0..63 (value + 32)
+    const int h = col / 128, r = col % 128, part = r / 32, l = r % 32;
+    const uint8_t ql = blk[64 * h + (part & 1) * 32 + l], qh = blk[128 + 32 * h + l];
+    return (uint8_t)(((ql >> ((part >> 1) * 4)) & 0xF) | (((qh >> (2 * part)) & 3) << 4));
+}
+
+// Column (0..15 within the k-step) / row (0..15 within the tile) of A-fragment register r, half e.
+inline int frag_col(int r, int e, int c) { return 2 * c + e + 8 * (r >> 1); }
+inline int frag_row(int r, int g) { return g + 8 * (r & 1); }
+
+inline void repack_tiled(int type, const uint8_t *src, int K, int N, TiledHost &o) {
+    const int tiles = N / 16;
+    if (type == XJ_Q4_K || type == XJ_Q6_K) {
+        const int nu = K / 256, bb = type == XJ_Q4_K ? 144 : 210;
+        const size_t rb = (size_t)nu * bb;
+        o.q.assign((size_t)tiles * nu * 2048, 0);
+        o.s.assign((size_t)tiles * nu * 16 * 16, 0);
+        if (type == XJ_Q6_K) { o.h.assign((size_t)tiles * nu * 1024, 0); o.d.assign((size_t)tiles * nu * 16 * 2, 0); }
+        for (int t = 0; t < tiles; t++)
+            for (int u = 0; u < nu; u++) {
+                const size_t tu = (size_t)t * nu + u;
+                const uint8_t *blk[16];
+                for (int i = 0; i < 16; i++) blk[i] = src + (size_t)(16 * t + i) * rb + (size_t)u * bb;
+                for (int i = 0; i < 16; i++) {
+                    if (type == XJ_Q4_K) memcpy(&o.s[(tu * 16 + i) * 16], blk[i], 16);
+                    else { memcpy(&o.s[(tu * 16 + i) * 16], blk[i] + 192, 16); memcpy(&o.d[(tu * 16 + i) * 2], blk[i] + 208, 2); }
+                }
+                for (int lane = 0; lane < 32; lane++) {
+                    const int g = lane >> 2, c = lane & 3;
+                    for (int s = 0; s < 16; s++) {
+                        uint32_t w = 0, hw = 0;
+                        for (int r = 0; r < 4; r++)
+                            for (int e = 0; e < 2; e++) {
+                                const int row = frag_row(r, g), col = 16 * s + frag_col(r, e, c);
+                                const uint8_t code = type == XJ_Q4_K ? q4k_code(blk[row], col) : q6k_code(blk[row], col);
+                                w |= (uint32_t)(code & 0xF) << (4 * r + 16 * e);
+                                hw |= (uint32_t)(code >> 4) << (2 * r + 16 * e);
+                            }
+                        memcpy(&o.q[((tu * 4 + s / 4) * 32 + lane) * 16 + (s % 4) * 4], &w, 4);
+                        if (type == XJ_Q6_K) {
+                            // two k-steps share one word: odd k-step in the upper byte of each half
+                            uint32_t cur;
+                            uint8_t *p = &o.h[((tu * 2 + s / 8) * 32 + lane) * 16 + ((s / 2) % 4) * 4];
+                            memcpy(&cur, p, 4);
+                            cur |= hw << ((s & 1) * 8);
+                            memcpy(p, &cur, 4);
+                        }
+                    }
+                }
+            }
+    } else {   // Q8_0
+        const int nu = K / 32;
+        const size_t rb = (size_t)nu * 34;
+        o.q.assign((size_t)tiles * nu * 512, 0);
+        o.d.assign((size_t)tiles * nu * 16 * 2, 0);
+        for (int t = 0; t < tiles; t++)
+            for (int u = 0; u < nu; u++) {
+                const size_t tu = (size_t)t * nu + u;
+                for (int i = 0; i < 16; i++) memcpy(&o.d[(tu * 16 + i) * 2], src + (size_t)(16 * t + i) * rb + (size_t)u * 34, 2);
+                for (int lane = 0; lane < 32; lane++) {
+                    const int g = lane >> 2, c = lane & 3;
+                    uint8_t out[16];
+                    for (int ss = 0; ss < 2; ss++)
+                        for (int hw = 0; hw < 2; hw++)        // word: hw=0 -> a0,a1 ; hw=1 -> a2,a3
+                            for (int b = 0; b < 4; b++) {     // byte b: (r = 2*hw + b/2, e = b%2)
+                                const int r = 2 * hw + b / 2, e = b % 2;
+                                const int row = frag_row(r, g), col = 16 * ss + frag_col(r, e, c);
+                                out[ss * 8 + hw * 4 + b] = src[(size_t)(16 * t + row) * rb + (size_t)u * 34 + 2 + col];
+                            }
+                    memcpy(&o.q[(tu * 32 + lane) * 16], out, 16);
+                }
+            }
+    }
+}
+
 }  // namespace xjk

@@ -7,11 +7,17 @@
 
 namespace xjk {
 
+// Programmatic dependent launch: every kernel waits for its stream predecessor's results before
+// touching activations or state (a no-op when launched without the programmatic attribute).
+XJ_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+XJ_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
+
 constexpr int MAXT = 16;   // tokens per forward handled by the CUDA-core GEMV
 
 // ---------------------------------------------------------------- dequant / embed
 // out[r][K] = rows [row0, row0+nrows) of W in fp32 (bit-exact with core/xj_quant.h).
 __global__ void k_dequant(DevMat w, int row0, int nrows, float *out) {
+    griddep_wait();
     const long long total = (long long)nrows * (w.K / 8);
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
         const int r = (int)(i / (w.K / 8)), e0 = (int)(i % (w.K / 8)) * 8;
@@ -25,6 +31,7 @@ __global__ void k_dequant(DevMat w, int row0, int nrows, float *out) {
 
 // x[t] = row tok[t] of the embedding table; out-of-range ids give zeros (core/xj_cpu.c:369-373).
 __global__ void k_embed(DevMat w, const int32_t *tok, int T, float *x, int ldx) {
+    griddep_wait();
     const int t = blockIdx.y;
     if (t >= T) return;
     const int id = tok[t];
@@ -43,6 +50,7 @@ __global__ void k_embed(DevMat w, const int32_t *tok, int T, float *x, int ldx) 
 // ---------------------------------------------------------------- norms
 // y[r] = x[r] * w / sqrt(mean(x[r]^2) + eps), sum in double (core/xj_cpu.c:56-61). One block per row.
 __global__ void k_rmsnorm(const float *x, long long ldx, const float *w, float *y, long long ldy, int n, float eps) {
+    griddep_wait();
     __shared__ double red[32];
     const float *xr = x + blockIdx.x * ldx;
     float *yr = y + blockIdx.x * ldy;
@@ -73,6 +81,7 @@ struct GemvArgs {
 };
 
 __global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a) {
+    griddep_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grow = blockIdx.x * 8 + warp;
     if (grow >= a.row_start[a.njob]) return;
@@ -117,6 +126,7 @@ __global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a) {
 // (core/xj_cpu.c:172-182). One thread per channel, tokens in order. With ck != nullptr the state
 // after token t (t < T-1) is saved to ck[t][CD][KC-1] (core/xj_cpu.c:220).
 __global__ void k_conv_silu(float *qkv, long long ldq, int T, int CD, int KC, float *state, const float *cw, float *ck) {
+    griddep_wait();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= CD) return;
     float cs[8];
@@ -136,37 +146,47 @@ __global__ void k_conv_silu(float *qkv, long long ldq, int T, int CD, int KC, fl
     for (int k = 0; k < KC - 1; k++) state[(size_t)c * (KC - 1) + k] = cs[k];
 }
 
-// One block per value head hv, S threads; thread j owns row j of the head's state M (value dim j,
-// S key dims) in registers for all T tokens (core/xj_cpu.c:194-219):
+// One block per value head hv, 4 threads per value row j (thread (j, q) keeps key dims
+// [q*S/4, (q+1)*S/4) of row j of the head's state M in registers for all T tokens) (core/xj_cpu.c:194-219):
 //   q, k <- L2-normalised key head hv % Hk;  b = sigmoid(beta);  g = softplus(alpha + dt) * A
 //   M *= exp(g);  delta_j = (v_j - M_j.k) * b;  M_j += delta_j k;  o_j = M_j.q / sqrt(S)
 //   out = rmsnorm(o) * norm_w * silu(z)
-// State layout [Hv][S(j)][S(i)] as the CPU oracle. ck_ssm != nullptr saves M after token t < T-1.
+// State layout [Hv][S(j)][S(i)] as the CPU oracle; each thread's slice is 4*S/4 contiguous bytes.
+// ck_ssm != nullptr saves M after token t < T-1 into ck_ssm[t][Hv][S][S].
 template <int S>
-__global__ void __launch_bounds__(S < 32 ? 32 : S) k_gdn(const float *qkv, long long ldq, const float *z, long long ldz,
-                                                         const float *beta, const float *alpha, long long ldg,
-                                                         const float *dt, const float *A, const float *nw,
-                                                         float *ssm, float *ck_ssm, float *out, long long ldo,
-                                                         int T, int Hk, int Hv, int key_dim, float eps) {
+__global__ void __launch_bounds__(4 * S < 64 ? 64 : 4 * S) k_gdn(const float *qkv, long long ldq, const float *z,
+                                                                  long long ldz, const float *beta, const float *alpha,
+                                                                  long long ldg, const float *dt, const float *A,
+                                                                  const float *nw, float *ssm, float *ck_ssm, float *out,
+                                                                  long long ldo, int T, int Hk, int Hv, int key_dim,
+                                                                  float eps) {
+    constexpr int Q = 4, P = S / Q;          // threads per row, key dims per thread
     __shared__ float qs[S], ks[S];
     __shared__ double red[32];
-    const int hv = blockIdx.x, hk = hv % Hk, j = threadIdx.x;
+    griddep_wait();
+    const int hv = blockIdx.x, hk = hv % Hk;
+    const int j = threadIdx.x >> 2, qq = threadIdx.x & 3;
     const bool active = j < S;
-    float row[S];
-    float *M = ssm + (size_t)hv * S * S;
+    float row[P];
+    float *M = ssm + (size_t)hv * S * S + (size_t)j * S + qq * P;
     if (active) {
 #pragma unroll
-        for (int i = 0; i < S; i++) row[i] = M[(size_t)j * S + i];
+        for (int i = 0; i < P; i += 4) {
+            const float4 v4 = *reinterpret_cast<const float4 *>(M + i);
+            row[i] = v4.x; row[i + 1] = v4.y; row[i + 2] = v4.z; row[i + 3] = v4.w;
+        }
     }
     const float qscale = 1.0f / sqrtf((float)S);
     for (int t = 0; t < T; t++) {
         const float *x = qkv + t * ldq;
-        float qv = active ? x[hk * S + j] : 0.0f, kv = active ? x[key_dim + hk * S + j] : 0.0f;
-        double sq = block_sum_d((double)qv * qv, red);
-        double sk2 = block_sum_d((double)kv * kv, red);
-        if (active) {
-            qs[j] = qv * (1.0f / sqrtf((float)sq + eps));
-            ks[j] = kv * (1.0f / sqrtf((float)sk2 + eps));
+        // L2 norms of q and k (sums in double, core/xj_cpu.c:185-193)
+        const int e = threadIdx.x;
+        const float qv = e < S ? x[hk * S + e] : 0.0f, kv = e < S ? x[key_dim + hk * S + e] : 0.0f;
+        const double sq = block_sum_d((double)qv * qv, red);
+        const double sk2 = block_sum_d((double)kv * kv, red);
+        if (e < S) {
+            qs[e] = qv * (1.0f / sqrtf((float)sq + eps));
+            ks[e] = kv * (1.0f / sqrtf((float)sk2 + eps));
         }
         __syncthreads();
         const float b = sigm_f(beta[t * ldg + hv]);
@@ -174,32 +194,36 @@ __global__ void __launch_bounds__(S < 32 ? 32 : S) k_gdn(const float *qkv, long 
         const float eg = expf(g);
         float o = 0.0f;
         if (active) {
-            const float vj = x[2 * key_dim + hv * S + j];
             float sk = 0.0f;
 #pragma unroll
-            for (int i = 0; i < S; i++) { row[i] *= eg; sk = fmaf(row[i], ks[i], sk); }
-            const float delta = (vj - sk) * b;
+            for (int i = 0; i < P; i++) { row[i] *= eg; sk = fmaf(row[i], ks[qq * P + i], sk); }
+            sk += __shfl_xor_sync(0xffffffffu, sk, 1);
+            sk += __shfl_xor_sync(0xffffffffu, sk, 2);
+            const float delta = (x[2 * key_dim + hv * S + j] - sk) * b;
             float acc = 0.0f;
 #pragma unroll
-            for (int i = 0; i < S; i++) { row[i] = fmaf(ks[i], delta, row[i]); acc = fmaf(row[i], qs[i], acc); }
+            for (int i = 0; i < P; i++) { row[i] = fmaf(ks[qq * P + i], delta, row[i]); acc = fmaf(row[i], qs[qq * P + i], acc); }
+            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
             o = acc * qscale;
         }
-        double so = block_sum_d((double)o * o, red);
+        const double so = block_sum_d(active && qq == 0 ? (double)o * o : 0.0, red);
         if (active) {
-            const float sc = 1.0f / sqrtf((float)(so / S) + eps);
-            const float zj = z[t * ldz + hv * S + j];
-            out[t * ldo + hv * S + j] = o * sc * nw[j] * silu_f(zj);
+            if (qq == 0) {
+                const float sc = 1.0f / sqrtf((float)(so / S) + eps);
+                out[t * ldo + hv * S + j] = o * sc * nw[j] * silu_f(z[t * ldz + hv * S + j]);
+            }
             if (ck_ssm && t < T - 1) {
-                float *C = ck_ssm + ((size_t)t * Hv + hv) * S * S + (size_t)j * S;
+                float *C = ck_ssm + ((size_t)t * Hv + hv) * S * S + (size_t)j * S + qq * P;
 #pragma unroll
-                for (int i = 0; i < S; i++) C[i] = row[i];
+                for (int i = 0; i < P; i += 4) *reinterpret_cast<float4 *>(C + i) = make_float4(row[i], row[i + 1], row[i + 2], row[i + 3]);
             }
         }
         __syncthreads();
     }
     if (active) {
 #pragma unroll
-        for (int i = 0; i < S; i++) M[(size_t)j * S + i] = row[i];
+        for (int i = 0; i < P; i += 4) *reinterpret_cast<float4 *>(M + i) = make_float4(row[i], row[i + 1], row[i + 2], row[i + 3]);
     }
 }
 
@@ -220,6 +244,7 @@ __global__ void k_attn_prep(const float *q, long long ldq, const float *k, const
                             int H, int Hkv, int D, int n_rot, float base, float eps) {
     extern __shared__ float sh[];
     __shared__ double red[32];
+    griddep_wait();
     const int t = blockIdx.y, slot = blockIdx.x, i = threadIdx.x;
     const int pos = *npast + t;
     const bool isq = slot < H;
@@ -258,6 +283,7 @@ __global__ void __launch_bounds__(128) k_attn(const float *qrot, const float *qg
                                               const int *npast, float *out, long long ldo, int H, int Hkv, int D) {
     __shared__ float sm_m[4], sm_l[4];
     __shared__ float sm_o[4][256];
+    griddep_wait();
     const int h = blockIdx.x, t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int n = *npast + t + 1, kvh = h / (H / Hkv), kvd = Hkv * D;
     const float scale = 1.0f / sqrtf((float)D);
@@ -308,13 +334,15 @@ __global__ void __launch_bounds__(128) k_attn(const float *qrot, const float *qg
 }
 
 // ---------------------------------------------------------------- FFN / misc
-// g = silu(g) * u (core/xj_cpu.c:273).
-__global__ void k_swiglu(float *g, const float *u, long long n) {
+// out = silu(g) * u (core/xj_cpu.c:273).
+__global__ void k_swiglu(const float *g, const float *u, float *out, long long n) {
+    griddep_wait();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
-        g[i] = silu_f(g[i]) * u[i];
+        out[i] = silu_f(g[i]) * u[i];
 }
 
 __global__ void k_advance(int *npast, int T) {
+    griddep_wait();
     if (threadIdx.x == 0 && blockIdx.x == 0) *npast += T;
 }
 
@@ -325,6 +353,7 @@ __global__ void __launch_bounds__(1024) k_argmax(const float *logits, int V, int
                                                  int32_t *cur, int *step) {
     __shared__ float sv[32], sv2[32];
     __shared__ int si[32];
+    griddep_wait();
     float b = -INFINITY, b2 = -INFINITY;
     int bi = 0x7fffffff;
     for (int i = threadIdx.x; i < V; i += blockDim.x) {
@@ -362,6 +391,88 @@ __global__ void __launch_bounds__(1024) k_argmax(const float *logits, int V, int
             *cur = bi;
             *step = s + 1;
         }
+    }
+}
+
+// Per 16-row tile of logits[V]: best value, runner-up, lowest best index (the partials the fused
+// LM-head epilogue produces, for heads that are not on the tensor-core path). One warp per tile.
+__global__ void k_argmax_rows(const float *logits, int V, float *pbest, float *psecond, int *pidx) {
+    griddep_wait();
+    const int tile = blockIdx.x, row = threadIdx.x & 15, r = tile * 16 + row;
+    float b = r < V ? logits[r] : -INFINITY, b2 = -INFINITY;
+    int bi = r < V ? r : 0x7fffffff;
+#pragma unroll
+    for (int o = 8; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, b, o), ov2 = __shfl_xor_sync(0xffffffffu, b2, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > b || (ov == b && oi < bi)) { b2 = fmaxf(b, ov2); b = ov; bi = oi; }
+        else b2 = fmaxf(b2, ov);
+    }
+    if (threadIdx.x == 0) { pbest[tile] = b; psecond[tile] = b2; pidx[tile] = bi; }
+}
+
+// Greedy pick from the LM head's per-tile partials (best, runner-up, lowest index of each 16 rows):
+// token = largest value, lowest index on ties (core/xj_spec.c:12-16). Writes out_tok[*step], the
+// runner-up gap to margin[*step], the token to *cur, then the token's embedding row into x (the next
+// decode step's input, core/xj_cpu.c:369-373), advances *npast by one and *step by one. One block.
+__global__ void __launch_bounds__(1024) k_argmax_final(const float *pbest, const float *psecond, const int *pidx,
+                                                       int ntiles, int32_t *out_tok, float *margin, int32_t *cur,
+                                                       int *step, DevMat emb, float *x, int *npast) {
+    __shared__ float sv[32], sv2[32];
+    __shared__ int si[32];
+    __shared__ int s_tok;
+    griddep_wait();
+    float b = -INFINITY, b2 = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < ntiles; i += blockDim.x) {
+        const float v = pbest[i], v2 = psecond[i];
+        const int vi = pidx[i];
+        if (v > b || (v == b && vi < bi)) { b2 = fmaxf(fmaxf(b, b2), v2); b = v; bi = vi; }
+        else b2 = fmaxf(b2, v);                      // the tile's runner-up is <= its best
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, b, o), ov2 = __shfl_xor_sync(0xffffffffu, b2, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > b || (ov == b && oi < bi)) { b2 = fmaxf(b, ov2); b = ov; bi = oi; }
+        else b2 = fmaxf(b2, ov);
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sv[w] = b; sv2[w] = b2; si[w] = bi; }
+    __syncthreads();
+    if (w == 0) {
+        const int nw = blockDim.x >> 5;
+        b = lane < nw ? sv[lane] : -INFINITY;
+        b2 = lane < nw ? sv2[lane] : -INFINITY;
+        bi = lane < nw ? si[lane] : 0x7fffffff;
+#pragma unroll
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, b, o), ov2 = __shfl_xor_sync(0xffffffffu, b2, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > b || (ov == b && oi < bi)) { b2 = fmaxf(b, ov2); b = ov; bi = oi; }
+            else b2 = fmaxf(b2, ov);
+        }
+        if (lane == 0) {
+            const int s = *step;
+            out_tok[s] = bi;
+            if (margin) margin[s] = b - b2;
+            *cur = bi;
+            *step = s + 1;
+            *npast += 1;
+            s_tok = bi;
+        }
+    }
+    __syncthreads();
+    const int id = s_tok;
+    for (int e0 = threadIdx.x * 8; e0 < emb.K; e0 += blockDim.x * 8) {
+        float y[8];
+        if (id >= 0 && id < emb.N) dequant8(emb.type, emb.p + id * emb.ld, e0, y);
+        else {
+#pragma unroll
+            for (int l = 0; l < 8; l++) y[l] = 0.0f;
+        }
+#pragma unroll
+        for (int l = 0; l < 8; l++) x[e0 + l] = y[l];
     }
 }
 

@@ -68,7 +68,10 @@ struct Impl {
     // activations (device)
     float *x = nullptr, *xin = nullptr, *h = nullptr, *qkvb = nullptr, *z = nullptr, *beta = nullptr, *alpha = nullptr;
     float *o = nullptr, *qrot = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
-    float *q = nullptr, *k = nullptr, *v = nullptr;
+    float *q = nullptr, *k = nullptr, *v = nullptr, *hn = nullptr;
+    float *pbest = nullptr, *psecond = nullptr;
+    int *pidx = nullptr;
+    int *derr = nullptr;       // device error word: set when a kernel's bounded wait gives up
     int *npast = nullptr, *step = nullptr;
     int32_t *tok = nullptr, *cur = nullptr, *out_tok = nullptr;
     float *margin = nullptr;
@@ -112,15 +115,37 @@ uint64_t row_bytes(uint32_t type, int64_t n) {
     }
 }
 
-// Upload one weight (once per host pointer) in its GGUF block layout.
-int upload(Impl *im, const xj_w &w, DevMat *out, char *err, size_t errlen) {
-    if (!w.data || !w.nbytes) { seterr(err, errlen, "weight is not mapped"); return -1; }
-    auto it = im->uploaded.find(w.data);
-    if (it != im->uploaded.end()) { *out = it->second; return 0; }
+template <typename T>
+int dput(Impl *im, const std::vector<T> &v, const uint8_t **dst, char *err, size_t errlen) {
+    if (v.empty()) { *dst = nullptr; return 0; }
     uint8_t *p;
-    if (dalloc(im, &p, (size_t)w.nbytes, err, errlen)) return -1;
-    CK(cudaMemcpy(p, w.data, (size_t)w.nbytes, cudaMemcpyHostToDevice));
-    DevMat d{p, (int)w.type, (int)w.ne0, (int)w.ne1, (long long)row_bytes(w.type, w.ne0)};
+    if (dalloc(im, &p, v.size() * sizeof(T), err, errlen)) return -1;
+    CK(cudaMemcpy(p, v.data(), v.size() * sizeof(T), cudaMemcpyHostToDevice));
+    *dst = p;
+    return 0;
+}
+
+// Upload one weight once per host pointer: in the tensor-core tiled layout when the fast GEMV can
+// take it, and/or in the GGUF row-major layout (always for the embedding table, which is read by row,
+// and for everything the fast path cannot take).
+int upload(Impl *im, const xj_w &w, DevMat *out, char *err, size_t errlen, bool need_rowmajor = false) {
+    if (!w.data || !w.nbytes) { seterr(err, errlen, "weight is not mapped"); return -1; }
+    DevMat d{nullptr, (int)w.type, (int)w.ne0, (int)w.ne1, (long long)row_bytes(w.type, w.ne0)};
+    auto it = im->uploaded.find(w.data);
+    if (it != im->uploaded.end()) d = it->second;
+    const bool want_tiled = im->gemv_mode == 0 && w.ne1 > 1 && tiled_ok((int)w.type, (int)w.ne0, (int)w.ne1);
+    if (want_tiled && !d.tq) {
+        TiledHost th;
+        repack_tiled((int)w.type, (const uint8_t *)w.data, (int)w.ne0, (int)w.ne1, th);
+        if (dput(im, th.q, &d.tq, err, errlen) || dput(im, th.h, &d.th, err, errlen) ||
+            dput(im, th.s, &d.ts, err, errlen) || dput(im, th.d, &d.td, err, errlen)) return -1;
+    }
+    if ((need_rowmajor || !want_tiled) && !d.p) {
+        uint8_t *p;
+        if (dalloc(im, &p, (size_t)w.nbytes, err, errlen)) return -1;
+        CK(cudaMemcpy(p, w.data, (size_t)w.nbytes, cudaMemcpyHostToDevice));
+        d.p = p;
+    }
     im->uploaded[w.data] = d;
     *out = d;
     return 0;
@@ -135,22 +160,103 @@ int upload_f32(Impl *im, const xj_w &w, float **out, char *err, size_t errlen) {
 }
 
 // ------------------------------------------------------------------ launches
-void gemv(Impl *im, const float *x, long long ldx, int T, std::initializer_list<GemvJob> jobs) {
-    // Fast tensor-core path for the block types it supports, generic path for the rest.
+// One matrix of a GEMV group: y (+)= W f(x), with an epilogue (see gemv_mma.cuh).
+struct Job {
+    DevMat w;
+    float *y;
+    long long ldy;
+    int epi = EPI_STORE;
+    float *conv_state = nullptr;
+    const float *conv_w = nullptr;
+    float *conv_ck = nullptr;
+    int kc = 0;
+    float *pbest = nullptr, *psecond = nullptr;
+    int *pidx = nullptr;
+};
+
+template <typename... KArgs, typename... Args>
+void launch(Impl *im, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
+    launch_pdl(kern, grid, block, smem, im->st, args...);
+}
+
+void rmsnorm(Impl *im, const float *x, long long ldx, const float *w, float *y, long long ldy, int n, int rows, float eps) {
+    launch(im, k_rmsnorm, dim3(rows), dim3(256), 0, x, ldx, w, y, ldy, n, eps);
+}
+
+// y_j[t] (+)= W_j . f(x[t]) for a group of matrices sharing the input x[T][K]; f = identity, RMSNorm
+// (norm_w) or SwiGLU silu(x) * x2. Tiled matrices go to the tensor-core kernel (one launch per weight
+// type, f and the epilogues fused); the rest to the generic kernel with f and the epilogues as passes.
+void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int pro, const float *norm_w, float eps,
+          std::initializer_list<Job> jobs) {
+    const int K = jobs.begin()->w.K;
+    std::vector<Job> fast, slow;
+    for (const Job &j : jobs) {
+        // a tiled matrix has no row-major copy: it always takes the tensor-core kernel
+        if (j.w.tq && !(j.epi == EPI_ARGMAX && T != 1)) fast.push_back(j);
+        else slow.push_back(j);
+    }
+    std::vector<char> done(fast.size(), 0);
+    for (size_t i = 0; i < fast.size(); i++) {
+        if (done[i]) continue;
+        MmaArgs m{};
+        m.ldx = ldx; m.K = K; m.pro = pro; m.norm_w = norm_w; m.eps = eps; m.err = im->derr;
+        const int type = fast[i].w.type;
+        m.tile_start[0] = 0;
+        for (size_t k = i; k < fast.size() && m.njob < 4; k++) {
+            if (done[k] || fast[k].w.type != type) continue;
+            const Job &f = fast[k];
+            MmaJob &mj = m.job[m.njob];
+            mj.w = tiled_of(f.w); mj.y = f.y; mj.ldy = f.ldy; mj.epi = f.epi;
+            mj.conv_state = f.conv_state; mj.conv_w = f.conv_w; mj.conv_ck = f.conv_ck; mj.kc = f.kc;
+            mj.pbest = f.pbest; mj.psecond = f.psecond; mj.pidx = f.pidx;
+            m.tile_start[m.njob + 1] = m.tile_start[m.njob] + f.w.N / 16;
+            m.njob++;
+            done[k] = 1;
+        }
+        // tokens in chunks of MMA_MAXT; each token's result does not depend on the chunking (the conv
+        // epilogue carries its state across chunks, its checkpoints are indexed by absolute token)
+        for (int t0 = 0; t0 < T; t0 += MMA_MAXT) {
+            MmaArgs c = m;
+            c.T = T - t0 < MMA_MAXT ? T - t0 : MMA_MAXT;
+            c.x = x + t0 * ldx;
+            c.x2 = x2 ? x2 + t0 * ldx : nullptr;
+            for (int j = 0; j < c.njob; j++) {
+                if (c.job[j].y) c.job[j].y = m.job[j].y + t0 * m.job[j].ldy;
+                if (c.job[j].conv_ck) {
+                    // the chunk saves the states after its tokens t0..t0+c.T-2; the one after t0+c.T-1
+                    // (when that is not the last token) is saved by the next chunk as its "previous" state
+                    c.job[j].conv_ck = m.job[j].conv_ck + (size_t)t0 * m.job[j].w.N * (m.job[j].kc - 1);
+                }
+            }
+            launch_mma(c, type, im->st);
+            for (int j = 0; j < c.njob; j++)
+                if (m.job[j].conv_ck && t0 + c.T < T) {
+                    // state after token t0+c.T-1 = current conv state: copy it into its checkpoint slot
+                    const size_t n = (size_t)m.job[j].w.N * (m.job[j].kc - 1);
+                    cudaMemcpyAsync(m.job[j].conv_ck + (size_t)(t0 + c.T - 1) * n, m.job[j].conv_state, n * 4,
+                                    cudaMemcpyDeviceToDevice, im->st);
+                }
+        }
+    }
+    if (slow.empty()) return;
+    if (pro == PRO_NORM) {
+        rmsnorm(im, x, ldx, norm_w, im->hn, K, K, T, eps);
+        x = im->hn;
+        ldx = K;
+    } else if (pro == PRO_SWIGLU) {
+        for (int t = 0; t < T; t++)
+            launch(im, k_swiglu, dim3((K + 255) / 256), dim3(256), 0, (const float *)(x + t * ldx),
+                   (const float *)(x2 + t * ldx), im->hn + (size_t)t * K, (long long)K);
+        x = im->hn;
+        ldx = K;
+    }
     GemvArgs a{};
     a.x = x; a.ldx = ldx; a.T = T;
-    std::vector<GemvJob> slow;
-    for (const GemvJob &j : jobs) {
-        if (im->gemv_mode == 0 && T <= MMA_MAXT && mma_supported(j.w))
-            launch_gemv_mma(j, x, ldx, T, im->st);
-        else
-            slow.push_back(j);
-    }
     for (size_t i0 = 0; i0 < slow.size(); i0 += 4) {
         a.njob = 0;
         a.row_start[0] = 0;
         for (size_t i = i0; i < slow.size() && a.njob < 4; i++) {
-            a.job[a.njob] = slow[i];
+            a.job[a.njob] = {slow[i].w, slow[i].y, slow[i].ldy, slow[i].epi == EPI_ADD ? 1 : 0};
             a.row_start[a.njob + 1] = a.row_start[a.njob] + slow[i].w.N;
             a.njob++;
         }
@@ -159,21 +265,25 @@ void gemv(Impl *im, const float *x, long long ldx, int T, std::initializer_list<
             b.T = T - t0 < MAXT ? T - t0 : MAXT;
             b.x = x + t0 * ldx;
             for (int j = 0; j < b.njob; j++) b.job[j].y = a.job[j].y + t0 * a.job[j].ldy;
-            k_gemv_generic<<<(b.row_start[b.njob] + 7) / 8, 256, 0, im->st>>>(b);
+            launch(im, k_gemv_generic, dim3((b.row_start[b.njob] + 7) / 8), dim3(256), 0, b);
         }
     }
-}
-
-void rmsnorm(Impl *im, const float *x, long long ldx, const float *w, float *y, long long ldy, int n, int rows, float eps) {
-    k_rmsnorm<<<rows, 256, 0, im->st>>>(x, ldx, w, y, ldy, n, eps);
+    for (const Job &j : slow) {
+        if (j.epi == EPI_CONV)
+            launch(im, k_conv_silu, dim3((j.w.N + 127) / 128), dim3(128), 0, j.y, j.ldy, T, j.w.N, j.kc, j.conv_state,
+                   j.conv_w, j.conv_ck);
+        else if (j.epi == EPI_ARGMAX)
+            launch(im, k_argmax_rows, dim3((j.w.N + 15) / 16), dim3(32), 0, (const float *)j.y, j.w.N, j.pbest, j.psecond, j.pidx);
+    }
 }
 
 void launch_gdn(Impl *im, const xj_hparams *hp, Layer &Ly, int T, bool ck) {
     const int S = hp->s_k;
     const long long ldq = hp->conv_dim;
-#define GDN(SS) k_gdn<SS><<<hp->h_v, SS < 32 ? 32 : SS, 0, im->st>>>(im->qkvb, ldq, im->z, hp->d_inner, im->beta, im->alpha, \
-        hp->h_v, Ly.dt, Ly.A, Ly.ssm_norm, Ly.ssm, ck ? Ly.ck_ssm : nullptr, im->o, hp->d_inner, T, hp->h_k, hp->h_v, \
-        hp->key_dim, hp->eps)
+#define GDN(SS) launch(im, k_gdn<SS>, dim3(hp->h_v), dim3(4 * SS < 64 ? 64 : 4 * SS), 0, (const float *)im->qkvb, ldq, \
+        (const float *)im->z, (long long)hp->d_inner, (const float *)im->beta, (const float *)im->alpha, (long long)hp->h_v, \
+        (const float *)Ly.dt, (const float *)Ly.A, (const float *)Ly.ssm_norm, Ly.ssm, ck ? Ly.ck_ssm : (float *)nullptr, \
+        im->o, (long long)hp->d_inner, T, hp->h_k, hp->h_v, hp->key_dim, hp->eps)
     switch (S) {
     case 16: GDN(16); break;
     case 32: GDN(32); break;
@@ -190,57 +300,66 @@ void launch_attn(Impl *im, const xj_hparams *hp, Layer &Ly, int T, const float *
                  const float *v, long long ldkv) {
     const int H = hp->n_head, Hkv = hp->n_head_kv, D = hp->head_dim;
     const int thr = (D + 31) / 32 * 32;
-    k_attn_prep<KV><<<dim3(H + Hkv, T), thr, D * sizeof(float), im->st>>>(q, ldq, k, v, ldkv, Ly.q_norm, Ly.k_norm, im->qrot,
-                                                                         (KV *)Ly.kc, (KV *)Ly.vc, im->npast, H, Hkv, D,
-                                                                         hp->n_rot, hp->rope_base, hp->eps);
+    launch(im, k_attn_prep<KV>, dim3(H + Hkv, T), dim3(thr), D * sizeof(float), q, ldq, k, v, ldkv,
+           (const float *)Ly.q_norm, (const float *)Ly.k_norm, im->qrot, (KV *)Ly.kc, (KV *)Ly.vc,
+           (const int *)im->npast, H, Hkv, D, hp->n_rot, hp->rope_base, hp->eps);
     const long long ldo = (long long)H * D;
+#define ATT(DPL) launch(im, k_attn<KV, DPL>, dim3(H, T), dim3(128), 0, (const float *)im->qrot, q, ldq, (const KV *)Ly.kc, \
+        (const KV *)Ly.vc, (const int *)im->npast, im->o, ldo, H, Hkv, D)
     switch ((D + 31) / 32) {
-    case 1: k_attn<KV, 1><<<dim3(H, T), 128, 0, im->st>>>(im->qrot, q, ldq, (KV *)Ly.kc, (KV *)Ly.vc, im->npast, im->o, ldo, H, Hkv, D); break;
-    case 2: k_attn<KV, 2><<<dim3(H, T), 128, 0, im->st>>>(im->qrot, q, ldq, (KV *)Ly.kc, (KV *)Ly.vc, im->npast, im->o, ldo, H, Hkv, D); break;
-    case 4: k_attn<KV, 4><<<dim3(H, T), 128, 0, im->st>>>(im->qrot, q, ldq, (KV *)Ly.kc, (KV *)Ly.vc, im->npast, im->o, ldo, H, Hkv, D); break;
-    case 8: k_attn<KV, 8><<<dim3(H, T), 128, 0, im->st>>>(im->qrot, q, ldq, (KV *)Ly.kc, (KV *)Ly.vc, im->npast, im->o, ldo, H, Hkv, D); break;
+    case 1: ATT(1); break;
+    case 2: ATT(2); break;
+    case 4: ATT(4); break;
+    case 8: ATT(8); break;
     default: break;
     }
+#undef ATT
 }
 
-// All layers of the stage on im->x[T][E] (device), positions *npast .. *npast+T-1; advances *npast.
-void run_layers(xj_stage *s, int T, bool keep) {
+// All layers of the stage on im->x[T][E] (device) at positions *npast .. *npast+T-1, then a last kernel
+// moves *npast forward by `advance` (the decode step's argmax kernel does its own +1).
+void run_layers(xj_stage *s, int T, bool keep, int advance) {
     Impl *im = I(s);
     const xj_hparams *hp = &s->m->hp;
     const int E = hp->n_embd, FF = hp->n_ff;
+    const float eps = hp->eps;
     for (int il = s->l0; il < s->l1; il++) {
         Layer &Ly = im->L[il - s->l0];
-        rmsnorm(im, im->x, E, Ly.attn_norm, im->h, E, E, T, hp->eps);
         if (Ly.rec) {
             const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v;
-            gemv(im, im->h, E, T, {{Ly.qkv, im->qkvb, CD, 0}, {Ly.gate, im->z, DI, 0}, {Ly.beta, im->beta, Hv, 0},
-                                   {Ly.alpha, im->alpha, Hv, 0}});
-            k_conv_silu<<<(CD + 127) / 128, 128, 0, im->st>>>(im->qkvb, CD, T, CD, hp->conv_k, Ly.conv, Ly.conv_w,
-                                                            keep ? Ly.ck_conv : nullptr);
+            Job qkv{Ly.qkv, im->qkvb, CD};
+            qkv.epi = EPI_CONV; qkv.conv_state = Ly.conv; qkv.conv_w = Ly.conv_w; qkv.kc = hp->conv_k;
+            qkv.conv_ck = keep ? Ly.ck_conv : nullptr;
+            gemv(im, im->x, nullptr, E, T, PRO_NORM, Ly.attn_norm, eps,
+                 {qkv, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
             launch_gdn(im, hp, Ly, T, keep);
-            gemv(im, im->o, DI, T, {{Ly.out, im->x, E, 1}});
+            Job out{Ly.out, im->x, E};
+            out.epi = EPI_ADD;
+            gemv(im, im->o, nullptr, DI, T, PRO_NONE, nullptr, eps, {out});
         } else {
             const int H = hp->n_head, Hkv = hp->n_head_kv, D = hp->head_dim, nq = 2 * H * D, nk = Hkv * D;
             const float *q, *k, *v;
             long long ldq, ldkv;
             if (Ly.fused) {
-                gemv(im, im->h, E, T, {{Ly.wqkv, im->qkvb, nq + 2 * nk, 0}});
+                gemv(im, im->x, nullptr, E, T, PRO_NORM, Ly.attn_norm, eps, {{Ly.wqkv, im->qkvb, nq + 2 * nk}});
                 q = im->qkvb; k = im->qkvb + nq; v = im->qkvb + nq + nk; ldq = ldkv = nq + 2 * nk;
             } else {
-                gemv(im, im->h, E, T, {{Ly.wq, im->q, nq, 0}, {Ly.wk, im->k, nk, 0}, {Ly.wv, im->v, nk, 0}});
+                gemv(im, im->x, nullptr, E, T, PRO_NORM, Ly.attn_norm, eps,
+                     {{Ly.wq, im->q, nq}, {Ly.wk, im->k, nk}, {Ly.wv, im->v, nk}});
                 q = im->q; k = im->k; v = im->v; ldq = nq; ldkv = nk;
             }
             if (im->kv_f32) launch_attn<float>(im, hp, Ly, T, q, ldq, k, v, ldkv);
             else launch_attn<__half>(im, hp, Ly, T, q, ldq, k, v, ldkv);
-            gemv(im, im->o, (long long)H * D, T, {{Ly.wo, im->x, E, 1}});
+            Job o{Ly.wo, im->x, E};
+            o.epi = EPI_ADD;
+            gemv(im, im->o, nullptr, (long long)H * D, T, PRO_NONE, nullptr, eps, {o});
         }
-        rmsnorm(im, im->x, E, Ly.post_norm, im->h, E, E, T, hp->eps);
-        gemv(im, im->h, E, T, {{Ly.ffn_gate, im->g, FF, 0}, {Ly.ffn_up, im->u, FF, 0}});
-        const long long n = (long long)T * FF;
-        k_swiglu<<<(int)((n + 255) / 256 < 1184 ? (n + 255) / 256 : 1184), 256, 0, im->st>>>(im->g, im->u, n);
-        gemv(im, im->g, FF, T, {{Ly.ffn_down, im->x, E, 1}});
+        gemv(im, im->x, nullptr, E, T, PRO_NORM, Ly.post_norm, eps, {{Ly.ffn_gate, im->g, FF}, {Ly.ffn_up, im->u, FF}});
+        Job down{Ly.ffn_down, im->x, E};
+        down.epi = EPI_ADD;
+        gemv(im, im->g, im->u, FF, T, PRO_SWIGLU, nullptr, eps, {down});
     }
-    k_advance<<<1, 32, 0, im->st>>>(im->npast, T);
+    if (advance) launch(im, k_advance, dim3(1), dim3(32), 0, im->npast, advance);
 }
 
 // MTP prefix (core/xj_cpu.c:253-261): x[T][E] = eh_proj([enorm(emb) | hnorm(hid)]), input in im->xin[T][2E].
@@ -250,21 +369,40 @@ void run_mtp_prefix(xj_stage *s, int T) {
     const int E = hp->n_embd;
     rmsnorm(im, im->xin, 2 * E, im->mtp_enorm, im->h, 2 * E, E, T, hp->eps);
     rmsnorm(im, im->xin + E, 2 * E, im->mtp_hnorm, im->h + E, 2 * E, E, T, hp->eps);
-    gemv(im, im->h, 2 * E, T, {{im->mtp_eh, im->x, E, 0}});
+    gemv(im, im->h, nullptr, 2 * E, T, PRO_NONE, nullptr, hp->eps, {{im->mtp_eh, im->x, E}});
 }
 
+// Output norm + LM head: logits[T][V] (core/xj_cpu.c:282-291).
 void head(xj_stage *s, const float *x, int T) {
     Impl *im = I(s);
     const xj_hparams *hp = &s->m->hp;
-    const int E = hp->n_embd;
-    rmsnorm(im, x, E, s->mtp ? im->mtp_head_norm : im->output_norm, im->h, E, E, T, hp->eps);
-    gemv(im, im->h, E, T, {{im->output, im->logits, im->output.N, 0}});
+    gemv(im, x, nullptr, hp->n_embd, T, PRO_NORM, s->mtp ? im->mtp_head_norm : im->output_norm, hp->eps,
+         {{im->output, im->logits, im->output.N}});
+}
+
+// Output norm + LM head for one row with the greedy pick fused (per-tile partials, then one small
+// kernel that also embeds the picked token into x and advances the position).
+void head_argmax(xj_stage *s, const float *x) {
+    Impl *im = I(s);
+    const xj_hparams *hp = &s->m->hp;
+    Job h{im->output, im->logits, im->output.N};
+    h.epi = EPI_ARGMAX; h.pbest = im->pbest; h.psecond = im->psecond; h.pidx = im->pidx;
+    gemv(im, x, nullptr, hp->n_embd, 1, PRO_NORM, im->output_norm, hp->eps, {h});
+    const int ntiles = (im->output.N + 15) / 16;
+    launch(im, k_argmax_final, dim3(1), dim3(1024), 0, (const float *)im->pbest, (const float *)im->psecond,
+           (const int *)im->pidx, ntiles, im->out_tok, im->margin, im->cur, im->step, im->tok_embd, im->x, im->npast);
 }
 
 int sync_check(Impl *im, char *err, size_t errlen) {
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaStreamSynchronize(im->st);
     if (e != cudaSuccess) { seterr(err, errlen, "GPU error: %s", cudaGetErrorString(e)); return -1; }
+    int flag = 0;
+    if (im->derr && cudaMemcpy(&flag, im->derr, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && flag) {
+        cudaMemset(im->derr, 0, sizeof(int));
+        seterr(err, errlen, "GPU wait for the weight stream timed out");
+        return -1;
+    }
     return 0;
 }
 
@@ -301,7 +439,7 @@ int cuda_forward(xj_stage *s, float *x, int T, char *err, size_t errlen) {
         seterr(err, errlen, "host-to-device copy failed"); s->keep = 0; return -1;
     }
     if (s->mtp) run_mtp_prefix(s, T);
-    run_layers(s, T, keep);
+    run_layers(s, T, keep, T);
     cudaMemcpyAsync(im->hx, im->x, sizeof(float) * (size_t)T * E, cudaMemcpyDeviceToHost, im->st);
     if (sync_check(im, err, errlen)) { s->keep = 0; return -1; }
     memcpy(x, im->hx, sizeof(float) * (size_t)T * E);
@@ -454,9 +592,17 @@ int build(xj_stage *s, char *err, size_t errlen) {
         dalloc(im, &im->qrot, (size_t)B * hp->n_head * hp->head_dim, err, errlen) || dalloc(im, &im->g, sf, err, errlen) ||
         dalloc(im, &im->u, sf, err, errlen) || dalloc(im, &im->q, sf, err, errlen) || dalloc(im, &im->k, sf, err, errlen) ||
         dalloc(im, &im->v, sf, err, errlen) || dalloc(im, &im->logits, V * (size_t)B, err, errlen) ||
+        dalloc(im, &im->hn, sf, err, errlen) ||
         dalloc(im, &im->npast, 4, err, errlen) || dalloc(im, &im->step, 4, err, errlen) ||
+        dalloc(im, &im->derr, 4, err, errlen) ||
         dalloc(im, &im->tok, (size_t)B, err, errlen) || dalloc(im, &im->cur, 4, err, errlen)) return -1;
+    if (s->has_head) {
+        const size_t nt = (size_t)(m->output.ne1 + 15) / 16;
+        if (dalloc(im, &im->pbest, nt, err, errlen) || dalloc(im, &im->psecond, nt, err, errlen) ||
+            dalloc(im, &im->pidx, nt, err, errlen)) return -1;
+    }
     CK(cudaMemset(im->npast, 0, 16));
+    CK(cudaMemset(im->derr, 0, sizeof(int)));
     CK(cudaMallocHost(&im->hx, sizeof(float) * (size_t)B * 2 * E));
     CK(cudaMallocHost(&im->hlogits, sizeof(float) * V * (size_t)B));
     im->state_bytes += sizeof(float) * (sf * 7 + (size_t)B * 4 * E + V * B);
@@ -480,11 +626,8 @@ int count_kernels(cudaGraph_t g) {
 // One decode step on device: x = embed(*cur); layers; head on the last row; argmax -> out_tok[*step], *cur.
 void decode_step(xj_stage *s) {
     Impl *im = I(s);
-    const int E = s->m->hp.n_embd;
-    k_embed<<<dim3((E / 8 + 127) / 128, 1), 128, 0, im->st>>>(im->tok_embd, im->cur, 1, im->x, E);
-    run_layers(s, 1, false);
-    head(s, im->x, 1);
-    k_argmax<<<1, 1024, 0, im->st>>>(im->logits, im->output.N, im->out_tok, im->margin, im->cur, im->step);
+    run_layers(s, 1, false, 0);
+    head_argmax(s, im->x);
 }
 
 }  // namespace
@@ -504,6 +647,7 @@ int xj_cuda_set_options(int which, int value) {
     switch (which) {
     case XJC_OPT_KV_F32: g_opt_kv_f32 = value; return 0;
     case XJC_OPT_GEMV: g_opt_gemv = value; return 0;
+    case XJC_OPT_PDL: g_pdl = value ? 1 : 0; return 0;
     default: return -1;
     }
 }
@@ -556,7 +700,7 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
     }
     if (n_prompt <= 0 || n_gen <= 0) { seterr(err, errlen, "need at least one prompt token and one generated token"); return -1; }
     if (s->n_past + n_prompt + n_gen - 1 > s->n_ctx) { seterr(err, errlen, "context is full (%d)", s->n_ctx); return -1; }
-    if (!im->tok_embd.p && upload(im, m->tok_embd, &im->tok_embd, err, errlen)) return -1;
+    if (!im->tok_embd.p && upload(im, m->tok_embd, &im->tok_embd, err, errlen, true)) return -1;
     if (n_gen > im->out_cap) {
         // the step graph writes through these pointers, so it is rebuilt after a reallocation
         if (im->step_graph) { cudaGraphExecDestroy(im->step_graph); im->step_graph = nullptr; }
@@ -570,12 +714,10 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
     for (int i = 0; i < n_prompt; i += B) {
         const int T = n_prompt - i < B ? n_prompt - i : B;
         CK(cudaMemcpyAsync(im->tok, prompt + i, sizeof(int32_t) * T, cudaMemcpyHostToDevice, im->st));
-        k_embed<<<dim3((E / 8 + 127) / 128, T), 128, 0, im->st>>>(im->tok_embd, im->tok, T, im->x, E);
-        run_layers(s, T, false);
-        if (i + T == n_prompt) {
-            head(s, im->x + (size_t)(T - 1) * E, 1);
-            k_argmax<<<1, 1024, 0, im->st>>>(im->logits, im->output.N, im->out_tok, im->margin, im->cur, im->step);
-        }
+        launch(im, k_embed, dim3((E / 8 + 127) / 128, T), dim3(128), 0, im->tok_embd, (const int32_t *)im->tok, T, im->x, E);
+        const bool last = i + T == n_prompt;
+        run_layers(s, T, false, last ? T - 1 : T);
+        if (last) head_argmax(s, im->x + (size_t)(T - 1) * E);   // picks out[0], embeds it, position +1
     }
     CK(cudaEventRecord(im->ev[1], im->st));
     if (n_gen > 1) {
@@ -601,6 +743,75 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
     }
     s->n_past += n_prompt + n_gen - 1;
     return 0;
+}
+
+// Diagnostic GEMV on host buffers: y[t][n] = W[n] . x[t] with the decode-path kernels (path 0 = fastest
+// available, 1 = generic), or average device time per launch over `iters` launches rotating through
+// `copies` device copies of W (so L2 cannot serve the weights) when ms != nullptr.
+static int gemv_diag(int type, const void *w, int k, int n, const float *x, int t, float *y, int path, int copies,
+                     int iters, float *ms, char *err, size_t errlen) {
+    if (t < 1 || t > MAXT) { seterr(err, errlen, "t must be in 1..%d", MAXT); return -1; }
+    if (k % 8) { seterr(err, errlen, "k must be a multiple of 8"); return -1; }
+    Impl tmp;
+    Impl *im = &tmp;
+    im->gemv_mode = path;
+    CK(cudaStreamCreateWithFlags(&im->st, cudaStreamNonBlocking));
+    int rc = -1;
+    float *dx = nullptr, *dy = nullptr;
+    std::vector<DevMat> mats;
+    const uint64_t nbytes = row_bytes((uint32_t)type, k) * (uint64_t)n;
+    if (!nbytes) { seterr(err, errlen, "unsupported type %d", type); goto done; }
+    if (copies < 1) copies = 1;
+    {
+        std::vector<uint8_t> buf((const uint8_t *)w, (const uint8_t *)w + nbytes);
+        for (int c = 0; c < copies; c++) {
+            xj_w hw{};
+            if (c) buf[0] ^= 0;   // identical bytes, distinct device copies
+            hw.data = buf.data() + 0; hw.nbytes = nbytes; hw.type = (uint32_t)type; hw.ne0 = k; hw.ne1 = n;
+            im->uploaded.clear();
+            DevMat d;
+            if (upload(im, hw, &d, err, errlen)) goto done;
+            mats.push_back(d);
+        }
+    }
+    if (dalloc(im, &dx, (size_t)t * k, err, errlen) || dalloc(im, &dy, (size_t)t * n, err, errlen) ||
+        dalloc(im, &im->hn, (size_t)t * k, err, errlen) || dalloc(im, &im->derr, 1, err, errlen)) goto done;
+    cudaMemset(im->derr, 0, sizeof(int));
+    if (cudaMemcpy(dx, x, sizeof(float) * (size_t)t * k, cudaMemcpyHostToDevice) != cudaSuccess) { seterr(err, errlen, "copy failed"); goto done; }
+    gemv(im, dx, nullptr, k, t, PRO_NONE, nullptr, 0.0f, {{mats[0], dy, n}});
+    if (ms) {
+        cudaEvent_t e0, e1;
+        cudaEventCreate(&e0); cudaEventCreate(&e1);
+        for (int i = 0; i < 3; i++) gemv(im, dx, nullptr, k, t, PRO_NONE, nullptr, 0.0f, {{mats[i % copies], dy, n}});
+        cudaEventRecord(e0, im->st);
+        for (int i = 0; i < iters; i++) gemv(im, dx, nullptr, k, t, PRO_NONE, nullptr, 0.0f, {{mats[i % copies], dy, n}});
+        cudaEventRecord(e1, im->st);
+        cudaEventSynchronize(e1);
+        cudaEventElapsedTime(ms, e0, e1);
+        *ms /= iters;
+        cudaEventDestroy(e0); cudaEventDestroy(e1);
+    }
+    if (y && cudaMemcpyAsync(y, dy, sizeof(float) * (size_t)t * n, cudaMemcpyDeviceToHost, im->st) != cudaSuccess) {
+        seterr(err, errlen, "copy failed"); goto done;
+    }
+    if (sync_check(im, err, errlen)) goto done;
+    rc = 0;
+done:
+    cudaStreamSynchronize(im->st);
+    for (void *p : im->allocs) cudaFree(p);
+    im->allocs.clear();
+    cudaStreamDestroy(im->st);
+    return rc;
+}
+
+int xj_cuda_gemv(int type, const void *w, int k, int n, const float *x, int t, float *y, int path, char *err, size_t errlen) {
+    return gemv_diag(type, w, k, n, x, t, y, path, 1, 0, nullptr, err, errlen);
+}
+
+int xj_cuda_gemv_time(int type, const void *w, int k, int n, int t, int copies, int iters, int path, float *ms,
+                      char *err, size_t errlen) {
+    std::vector<float> x((size_t)t * k, 0.5f);
+    return gemv_diag(type, w, k, n, x.data(), t, nullptr, path, copies, iters, ms, err, errlen);
 }
 
 int xj_cuda_graph_kernels(const xj_stage *s) {

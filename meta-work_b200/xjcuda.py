@@ -19,7 +19,7 @@ LIB = HERE / "csrc" / "libxj_cuda.so"
 _lib = None
 
 F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 8, 12, 13, 14, 30
-OPT_KV_F32, OPT_GEMV = 1, 2
+OPT_KV_F32, OPT_GEMV, OPT_PDL = 1, 2, 3
 
 
 class XjError(RuntimeError):
@@ -98,6 +98,8 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_decode": (ip, [vp, vp, ip, ip, vp, vp, vp, cp, sz]),
         "xj_cuda_dequant_rows": (ip, [ip, vp, ip, ip, vp, cp, sz]),
         "xj_cuda_graph_kernels": (ip, [vp]),
+        "xj_cuda_gemv": (ip, [ip, vp, ip, ip, vp, ip, vp, ip, cp, sz]),
+        "xj_cuda_gemv_time": (ip, [ip, vp, ip, ip, ip, ip, ip, ip, vp, cp, sz]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -129,6 +131,28 @@ def dequant_rows(type_id: int, raw: bytes, k: int, n_rows: int) -> np.ndarray:
     if lib().xj_cuda_dequant_rows(type_id, src.ctypes.data, k, n_rows, out.ctypes.data, e, 512):
         _raise(e)
     return out
+
+
+def gemv(type_id: int, raw: bytes, k: int, n: int, x: np.ndarray, path: int = 0) -> np.ndarray:
+    """y[T][n] = W x with the decode GEMV kernels (xj_cuda_gemv)."""
+    w = np.frombuffer(bytes(raw), np.uint8).copy()
+    x = np.ascontiguousarray(x, np.float32).reshape(-1, k)
+    y = np.zeros((x.shape[0], n), np.float32)
+    e = _err()
+    if lib().xj_cuda_gemv(type_id, w.ctypes.data, k, n, x.ctypes.data, x.shape[0], y.ctypes.data, path, e, 512):
+        _raise(e)
+    return y
+
+
+def gemv_time(type_id: int, raw: bytes, k: int, n: int, T: int = 1, copies: int = 4, iters: int = 50,
+              path: int = 0) -> float:
+    """Average ms per GEMV launch with weights rotated over `copies` device copies (xj_cuda_gemv_time)."""
+    w = np.frombuffer(bytes(raw), np.uint8).copy()
+    ms = ctypes.c_float(0)
+    e = _err()
+    if lib().xj_cuda_gemv_time(type_id, w.ctypes.data, k, n, T, copies, iters, path, ctypes.byref(ms), e, 512):
+        _raise(e)
+    return ms.value
 
 
 def _err():

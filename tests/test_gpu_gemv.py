@@ -1,0 +1,83 @@
+"""The decode GEMV (y = W x, the reference matmul core/xj_cpu.c:36-54) on the GPU through the C ABI.
+
+Checks, per weight type and shape (BASELINE config-1 shapes included): fp32-level agreement with a
+float64 product of the reference-exact dequantised weights (bound 1e-5 of max|y|: fp32 accumulation,
+plus the Q4_K path's codes enter the MMA as 64+q with 64*sum(x) removed afterwards, which costs a few
+fp32 ulps of that sum); the tensor-core path equals the generic
+path to fp32 rounding; each token's result is bit-identical whatever the number of tokens in the launch
+(so decode and speculative verify agree exactly); activations over a wide dynamic range stay exact.
+"""
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from oracle import xj_oracle as xo
+
+pytestmark = pytest.mark.gpu
+
+SHAPES = [(256, 16), (512, 48), (2048, 2048), (2048, 6144), (6144, 2048)]
+TYPES = [xo.Q4_K, xo.Q6_K, xo.Q8_0, xo.Q5_K, xo.F16, xo.BF16, xo.F32]
+
+
+def _w(t, k, n, seed):
+    from xjb200 import synth
+    rng = np.random.default_rng(seed)
+    x = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    return b"".join(synth.quantize_row(t, x[r]) for r in range(n)) if t != xo.F32 else x.tobytes()
+
+
+def _ref(t, raw, k, n, x):
+    W = xo.dequant(t, raw, k, n).astype(np.float64)
+    return x.astype(np.float64) @ W.T
+
+
+@pytest.mark.parametrize("t", TYPES)
+@pytest.mark.parametrize("k,n", SHAPES)
+def test_gemv_matches_float64(t, k, n):
+    from xjb200 import xjcuda
+    if t in (xo.Q4_K, xo.Q6_K, xo.Q5_K) and k % 256:
+        pytest.skip("K-quant rows are whole super-blocks")
+    raw = _w(t, k, n, k * 7 + n + t)
+    rng = np.random.default_rng(1)
+    for T in (1, 3, 4):
+        x = rng.standard_normal((T, k)).astype(np.float32)
+        want = _ref(t, raw, k, n, x)
+        for path in (0, 1):
+            y = xjcuda.gemv(t, raw, k, n, x, path)
+            err = np.abs(y - want).max() / np.abs(want).max()
+            assert err < 1e-5, (t, k, n, T, path, err)
+
+
+@pytest.mark.parametrize("t", [xo.Q4_K, xo.Q6_K, xo.Q8_0])
+def test_token_results_independent_of_batch(t):
+    from xjb200 import xjcuda
+    k, n = 2048, 512
+    raw = _w(t, k, n, 3)
+    x = np.random.default_rng(2).standard_normal((4, k)).astype(np.float32)
+    y4 = xjcuda.gemv(t, raw, k, n, x)
+    for i in range(4):
+        y1 = xjcuda.gemv(t, raw, k, n, x[i:i + 1])
+        assert y1[0].view(np.uint32).tolist() == y4[i].view(np.uint32).tolist()
+
+
+@pytest.mark.parametrize("t", [xo.Q4_K, xo.Q6_K, xo.Q8_0])
+def test_wide_dynamic_range(t):
+    from xjb200 import xjcuda
+    k, n = 1024, 64
+    raw = _w(t, k, n, 5)
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((2, k)).astype(np.float32)
+    x[0] *= 3e4                                    # beyond fp16 range before scaling
+    x[1] *= np.exp(rng.uniform(-20, 5, k)).astype(np.float32)   # tiny and large mixed
+    want = _ref(t, raw, k, n, x)
+    y = xjcuda.gemv(t, raw, k, n, x)
+    for r in range(2):
+        assert np.abs(y[r] - want[r]).max() / np.abs(want[r]).max() < 1e-5
+
+
+def test_gemv_microbench_runs():
+    from xjb200 import xjcuda
+    raw = _w(xo.Q4_K, 2048, 2048, 9)
+    ms = xjcuda.gemv_time(xo.Q4_K, raw, 2048, 2048, T=1, copies=4, iters=20)
+    assert 0 < ms < 5
