@@ -76,6 +76,21 @@ int xj_cuda_graph_kernels(const xj_stage *s);
 // (core/xj_quant.h:55-122). Runs on the current device.
 int xj_cuda_dequant_rows(int type, const void *src, int k, int n_rows, float *out, char *err, size_t errlen);
 
+// Capacity, in floats, of the fixed device scratch used by xj_cuda_norm_gemv_noalloc (256 KiB).
+#define XJC_NOALLOC_MAX_FLOATS 65536
+
+// No counterpart in the reference. y[t] = W . (rmsnorm(x[t]) * norm_w) for t < T without allocating
+// anything, for callers that cannot call cudaMalloc where they need it (a process whose device memory
+// is a fixed pool owned by another component, or a thread on which allocation is not allowed). Every
+// pointer is a DEVICE pointer on the current device: w_dev = n rows of k elements in GGUF block layout
+// of `type` (F32/F16/BF16/Q8_0/Q4_K/Q5_K/Q6_K), x_dev [T][k], norm_w_dev [k] fp32, y_dev [T][n].
+// 1 <= T <= 16 and T*k <= XJC_NOALLOC_MAX_FLOATS, else -1 with a message. The normalised rows live
+// in a fixed device array shared by all calls on a device: calls that overlap on the GPU race. The
+// first call on a device sets up that array's address; make it before any stream capture. Runs on
+// the legacy default stream and returns after the GPU has finished.
+int xj_cuda_norm_gemv_noalloc(int type, const void *w_dev, int k, int n, const float *x_dev, const float *norm_w_dev,
+                              float eps, int T, float *y_dev, char *err, size_t errlen);
+
 #ifdef __cplusplus
 }
 #endif

@@ -7,7 +7,8 @@
 
 namespace xjk {
 
-// Programmatic dependent launch: every kernel waits for its stream predecessor's results before
+// Kernels in this header have internal linkage (static): each translation unit that includes it
+// gets its own copies. Programmatic dependent launch: every kernel waits for its stream predecessor's results before
 // touching activations or state (a no-op when launched without the programmatic attribute).
 XJ_DEV void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 XJ_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" :::); }
@@ -16,7 +17,7 @@ constexpr int MAXT = 16;   // tokens per forward handled by the CUDA-core GEMV
 
 // ---------------------------------------------------------------- dequant / embed
 // out[r][K] = rows [row0, row0+nrows) of W in fp32 (bit-exact with core/xj_quant.h).
-__global__ void k_dequant(DevMat w, int row0, int nrows, float *out) {
+static __global__ void k_dequant(DevMat w, int row0, int nrows, float *out) {
     griddep_wait();
     const long long total = (long long)nrows * (w.K / 8);
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < total; i += (long long)gridDim.x * blockDim.x) {
@@ -30,7 +31,7 @@ __global__ void k_dequant(DevMat w, int row0, int nrows, float *out) {
 }
 
 // x[t] = row tok[t] of the embedding table; out-of-range ids give zeros (core/xj_cpu.c:369-373).
-__global__ void k_embed(DevMat w, const int32_t *tok, int T, float *x, int ldx) {
+static __global__ void k_embed(DevMat w, const int32_t *tok, int T, float *x, int ldx) {
     griddep_wait();
     const int t = blockIdx.y;
     if (t >= T) return;
@@ -49,7 +50,7 @@ __global__ void k_embed(DevMat w, const int32_t *tok, int T, float *x, int ldx) 
 
 // ---------------------------------------------------------------- norms
 // y[r] = x[r] * w / sqrt(mean(x[r]^2) + eps), sum in double (core/xj_cpu.c:56-61). One block per row.
-__global__ void k_rmsnorm(const float *x, long long ldx, const float *w, float *y, long long ldy, int n, float eps) {
+static __global__ void k_rmsnorm(const float *x, long long ldx, const float *w, float *y, long long ldy, int n, float eps) {
     griddep_wait();
     __shared__ double red[32];
     const float *xr = x + blockIdx.x * ldx;
@@ -80,7 +81,7 @@ struct GemvArgs {
     int T;
 };
 
-__global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a) {
+static __global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a) {
     griddep_wait();
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int grow = blockIdx.x * 8 + warp;
@@ -125,7 +126,7 @@ __global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a) {
 // Causal depthwise conv (kernel KC) with a rolling state, then SiLU, in place on qkv[T][CD]
 // (core/xj_cpu.c:172-182). One thread per channel, tokens in order. With ck != nullptr the state
 // after token t (t < T-1) is saved to ck[t][CD][KC-1] (core/xj_cpu.c:220).
-__global__ void k_conv_silu(float *qkv, long long ldq, int T, int CD, int KC, float *state, const float *cw, float *ck) {
+static __global__ void k_conv_silu(float *qkv, long long ldq, int T, int CD, int KC, float *state, const float *cw, float *ck) {
     griddep_wait();
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= CD) return;
@@ -154,7 +155,7 @@ __global__ void k_conv_silu(float *qkv, long long ldq, int T, int CD, int KC, fl
 // State layout [Hv][S(j)][S(i)] as the CPU oracle; each thread's slice is 4*S/4 contiguous bytes.
 // ck_ssm != nullptr saves M after token t < T-1 into ck_ssm[t][Hv][S][S].
 template <int S>
-__global__ void __launch_bounds__(4 * S < 64 ? 64 : 4 * S) k_gdn(const float *qkv, long long ldq, const float *z,
+static __global__ void __launch_bounds__(4 * S < 64 ? 64 : 4 * S) k_gdn(const float *qkv, long long ldq, const float *z,
                                                                   long long ldz, const float *beta, const float *alpha,
                                                                   long long ldg, const float *dt, const float *A,
                                                                   const float *nw, float *ssm, float *ck_ssm, float *out,
@@ -239,7 +240,7 @@ XJ_DEV float load_kv(const float *p) { return *p; }
 XJ_DEV float load_kv(const __half *p) { return __half2float(*p); }
 
 template <typename KV>
-__global__ void k_attn_prep(const float *q, long long ldq, const float *k, const float *v, long long ldkv,
+static __global__ void k_attn_prep(const float *q, long long ldq, const float *k, const float *v, long long ldkv,
                             const float *qn, const float *kn, float *qrot, KV *kc, KV *vc, const int *npast,
                             int H, int Hkv, int D, int n_rot, float base, float eps) {
     extern __shared__ float sh[];
@@ -279,7 +280,7 @@ __global__ void k_attn_prep(const float *q, long long ldq, const float *k, const
 // sigmoid output gate: out[t][h*D + i] = (sum_j p_j v_j[i]) * sigmoid(gate[i]) (core/xj_cpu.c:118-150).
 // One block of 4 warps per (h, t); lanes split the head dim (D <= 256, D % 32 == 0).
 template <typename KV, int DPL>
-__global__ void __launch_bounds__(128) k_attn(const float *qrot, const float *qg, long long ldq, const KV *kc, const KV *vc,
+static __global__ void __launch_bounds__(128) k_attn(const float *qrot, const float *qg, long long ldq, const KV *kc, const KV *vc,
                                               const int *npast, float *out, long long ldo, int H, int Hkv, int D) {
     __shared__ float sm_m[4], sm_l[4];
     __shared__ float sm_o[4][256];
@@ -335,13 +336,13 @@ __global__ void __launch_bounds__(128) k_attn(const float *qrot, const float *qg
 
 // ---------------------------------------------------------------- FFN / misc
 // out = silu(g) * u (core/xj_cpu.c:273).
-__global__ void k_swiglu(const float *g, const float *u, float *out, long long n) {
+static __global__ void k_swiglu(const float *g, const float *u, float *out, long long n) {
     griddep_wait();
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         out[i] = silu_f(g[i]) * u[i];
 }
 
-__global__ void k_advance(int *npast, int T) {
+static __global__ void k_advance(int *npast, int T) {
     griddep_wait();
     if (threadIdx.x == 0 && blockIdx.x == 0) *npast += T;
 }
@@ -349,7 +350,7 @@ __global__ void k_advance(int *npast, int T) {
 // Greedy pick over logits[V]: largest value, lowest index on ties (core/xj_spec.c:12-16); also the
 // gap to the runner-up. Writes the id to out_tok[*step] and to *cur (the next step's input), the gap
 // to margin[*step], then advances *step. One block of 1024 threads.
-__global__ void __launch_bounds__(1024) k_argmax(const float *logits, int V, int32_t *out_tok, float *margin,
+static __global__ void __launch_bounds__(1024) k_argmax(const float *logits, int V, int32_t *out_tok, float *margin,
                                                  int32_t *cur, int *step) {
     __shared__ float sv[32], sv2[32];
     __shared__ int si[32];
@@ -396,7 +397,7 @@ __global__ void __launch_bounds__(1024) k_argmax(const float *logits, int V, int
 
 // Per 16-row tile of logits[V]: best value, runner-up, lowest best index (the partials the fused
 // LM-head epilogue produces, for heads that are not on the tensor-core path). One warp per tile.
-__global__ void k_argmax_rows(const float *logits, int V, float *pbest, float *psecond, int *pidx) {
+static __global__ void k_argmax_rows(const float *logits, int V, float *pbest, float *psecond, int *pidx) {
     griddep_wait();
     const int tile = blockIdx.x, row = threadIdx.x & 15, r = tile * 16 + row;
     float b = r < V ? logits[r] : -INFINITY, b2 = -INFINITY;
@@ -415,7 +416,7 @@ __global__ void k_argmax_rows(const float *logits, int V, float *pbest, float *p
 // token = largest value, lowest index on ties (core/xj_spec.c:12-16). Writes out_tok[*step], the
 // runner-up gap to margin[*step], the token to *cur, then the token's embedding row into x (the next
 // decode step's input, core/xj_cpu.c:369-373), advances *npast by one and *step by one. One block.
-__global__ void __launch_bounds__(1024) k_argmax_final(const float *pbest, const float *psecond, const int *pidx,
+static __global__ void __launch_bounds__(1024) k_argmax_final(const float *pbest, const float *psecond, const int *pidx,
                                                        int ntiles, int32_t *out_tok, float *margin, int32_t *cur,
                                                        int *step, DevMat emb, float *x, int *npast) {
     __shared__ float sv[32], sv2[32];

@@ -100,6 +100,7 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_graph_kernels": (ip, [vp]),
         "xj_cuda_gemv": (ip, [ip, vp, ip, ip, vp, ip, vp, ip, cp, sz]),
         "xj_cuda_gemv_time": (ip, [ip, vp, ip, ip, ip, ip, ip, ip, vp, cp, sz]),
+        "xj_cuda_norm_gemv_noalloc": (ip, [ip, vp, ip, ip, vp, vp, ctypes.c_float, ip, vp, cp, sz]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
