@@ -15,6 +15,29 @@ XJ_DEV void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" 
 
 constexpr int MAXT = 16;   // tokens per forward handled by the CUDA-core GEMV
 
+// Barriers for the device functions below: the whole block (standalone kernels), or a named
+// barrier over the first N threads (the persistent decode kernel, whose last warp streams weights).
+struct BarBlock { XJ_DEV static void sync() { __syncthreads(); } };
+template <int ID, int N> struct BarNamed {
+    XJ_DEV static void sync() { asm volatile("bar.sync %0, %1;" :: "n"(ID), "n"(N) : "memory"); }
+};
+
+// Sum over nthr threads (tid < nthr) in double; `red` holds one double per warp. All get the result.
+template <class Bar>
+XJ_DEV double group_sum_d(double v, double *red, int tid, int nthr) {
+    const int lane = tid & 31, w = tid >> 5, nw = (nthr + 31) >> 5;
+    v = warp_sum_d(v);
+    Bar::sync();
+    if (lane == 0) red[w] = v;
+    Bar::sync();
+    double t = 0;
+    for (int i = 0; i < nw; i++) t += red[i];
+    return t;
+}
+
+// Activations written by other blocks are read through L2 only (never a stale L1 line).
+XJ_DEV float lda(const float *p) { return __ldcg(p); }
+
 // ---------------------------------------------------------------- dequant / embed
 // out[r][K] = rows [row0, row0+nrows) of W in fp32 (bit-exact with core/xj_quant.h).
 static __global__ void k_dequant(DevMat w, int row0, int nrows, float *out) {
@@ -147,152 +170,169 @@ static __global__ void k_conv_silu(float *qkv, long long ldq, int T, int CD, int
     for (int k = 0; k < KC - 1; k++) state[(size_t)c * (KC - 1) + k] = cs[k];
 }
 
-// One block per value head hv, 4 threads per value row j (thread (j, q) keeps key dims
-// [q*S/4, (q+1)*S/4) of row j of the head's state M in registers for all T tokens) (core/xj_cpu.c:194-219):
+struct GdnArgs {
+    const float *qkv; long long ldq;
+    const float *z; long long ldz;
+    const float *beta, *alpha; long long ldg;
+    const float *dt, *A, *nw;
+    float *ssm, *ck_ssm, *out; long long ldo;
+    int T, Hk, Hv, key_dim;
+    float eps;
+};
+
+// Gated DeltaNet for value head hv over T tokens, 4*S threads (tid < 4*S); thread (j, q) keeps key
+// dims [q*S/4, (q+1)*S/4) of row j of the head's state M in registers (core/xj_cpu.c:194-219):
 //   q, k <- L2-normalised key head hv % Hk;  b = sigmoid(beta);  g = softplus(alpha + dt) * A
 //   M *= exp(g);  delta_j = (v_j - M_j.k) * b;  M_j += delta_j k;  o_j = M_j.q / sqrt(S)
 //   out = rmsnorm(o) * norm_w * silu(z)
-// State layout [Hv][S(j)][S(i)] as the CPU oracle; each thread's slice is 4*S/4 contiguous bytes.
+// State layout [Hv][S(j)][S(i)] as the CPU oracle; each thread's slice is contiguous.
 // ck_ssm != nullptr saves M after token t < T-1 into ck_ssm[t][Hv][S][S].
-template <int S>
-static __global__ void __launch_bounds__(4 * S < 64 ? 64 : 4 * S) k_gdn(const float *qkv, long long ldq, const float *z,
-                                                                  long long ldz, const float *beta, const float *alpha,
-                                                                  long long ldg, const float *dt, const float *A,
-                                                                  const float *nw, float *ssm, float *ck_ssm, float *out,
-                                                                  long long ldo, int T, int Hk, int Hv, int key_dim,
-                                                                  float eps) {
-    constexpr int Q = 4, P = S / Q;          // threads per row, key dims per thread
+template <int S, class Bar>
+XJ_DEV void gdn_head(const GdnArgs &a, int hv, int tid) {
+    constexpr int P = S / 4, NT = 4 * S;
     __shared__ float qs[S], ks[S];
     __shared__ double red[32];
-    griddep_wait();
-    const int hv = blockIdx.x, hk = hv % Hk;
-    const int j = threadIdx.x >> 2, qq = threadIdx.x & 3;
-    const bool active = j < S;
+    const int hk = hv % a.Hk;
+    const int j = tid >> 2, qq = tid & 3;
     float row[P];
-    float *M = ssm + (size_t)hv * S * S + (size_t)j * S + qq * P;
-    if (active) {
+    float *M = a.ssm + (size_t)hv * S * S + (size_t)j * S + qq * P;
 #pragma unroll
-        for (int i = 0; i < P; i += 4) {
-            const float4 v4 = *reinterpret_cast<const float4 *>(M + i);
-            row[i] = v4.x; row[i + 1] = v4.y; row[i + 2] = v4.z; row[i + 3] = v4.w;
-        }
+    for (int i = 0; i < P; i += 4) {
+        const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(M + i));
+        row[i] = v4.x; row[i + 1] = v4.y; row[i + 2] = v4.z; row[i + 3] = v4.w;
     }
     const float qscale = 1.0f / sqrtf((float)S);
-    for (int t = 0; t < T; t++) {
-        const float *x = qkv + t * ldq;
+    for (int t = 0; t < a.T; t++) {
+        const float *x = a.qkv + t * a.ldq;
         // L2 norms of q and k (sums in double, core/xj_cpu.c:185-193)
-        const int e = threadIdx.x;
-        const float qv = e < S ? x[hk * S + e] : 0.0f, kv = e < S ? x[key_dim + hk * S + e] : 0.0f;
-        const double sq = block_sum_d((double)qv * qv, red);
-        const double sk2 = block_sum_d((double)kv * kv, red);
-        if (e < S) {
-            qs[e] = qv * (1.0f / sqrtf((float)sq + eps));
-            ks[e] = kv * (1.0f / sqrtf((float)sk2 + eps));
+        const float qv = tid < S ? lda(x + hk * S + tid) : 0.0f, kv = tid < S ? lda(x + a.key_dim + hk * S + tid) : 0.0f;
+        const double sq = group_sum_d<Bar>((double)qv * qv, red, tid, NT);
+        const double sk2 = group_sum_d<Bar>((double)kv * kv, red, tid, NT);
+        if (tid < S) {
+            qs[tid] = qv * (1.0f / sqrtf((float)sq + a.eps));
+            ks[tid] = kv * (1.0f / sqrtf((float)sk2 + a.eps));
         }
-        __syncthreads();
-        const float b = sigm_f(beta[t * ldg + hv]);
-        const float g = softplus_f(alpha[t * ldg + hv] + dt[hv]) * A[hv];
+        Bar::sync();
+        const float b = sigm_f(lda(a.beta + t * a.ldg + hv));
+        const float g = softplus_f(lda(a.alpha + t * a.ldg + hv) + a.dt[hv]) * a.A[hv];
         const float eg = expf(g);
-        float o = 0.0f;
-        if (active) {
-            float sk = 0.0f;
+        float sk = 0.0f;
 #pragma unroll
-            for (int i = 0; i < P; i++) { row[i] *= eg; sk = fmaf(row[i], ks[qq * P + i], sk); }
-            sk += __shfl_xor_sync(0xffffffffu, sk, 1);
-            sk += __shfl_xor_sync(0xffffffffu, sk, 2);
-            const float delta = (x[2 * key_dim + hv * S + j] - sk) * b;
-            float acc = 0.0f;
+        for (int i = 0; i < P; i++) { row[i] *= eg; sk = fmaf(row[i], ks[qq * P + i], sk); }
+        sk += __shfl_xor_sync(0xffffffffu, sk, 1);
+        sk += __shfl_xor_sync(0xffffffffu, sk, 2);
+        const float delta = (lda(x + 2 * a.key_dim + hv * S + j) - sk) * b;
+        float acc = 0.0f;
 #pragma unroll
-            for (int i = 0; i < P; i++) { row[i] = fmaf(ks[qq * P + i], delta, row[i]); acc = fmaf(row[i], qs[qq * P + i], acc); }
-            acc += __shfl_xor_sync(0xffffffffu, acc, 1);
-            acc += __shfl_xor_sync(0xffffffffu, acc, 2);
-            o = acc * qscale;
+        for (int i = 0; i < P; i++) { row[i] = fmaf(ks[qq * P + i], delta, row[i]); acc = fmaf(row[i], qs[qq * P + i], acc); }
+        acc += __shfl_xor_sync(0xffffffffu, acc, 1);
+        acc += __shfl_xor_sync(0xffffffffu, acc, 2);
+        const float o = acc * qscale;
+        const double so = group_sum_d<Bar>(qq == 0 ? (double)o * o : 0.0, red, tid, NT);
+        if (qq == 0) {
+            const float sc = 1.0f / sqrtf((float)(so / S) + a.eps);
+            a.out[t * a.ldo + hv * S + j] = o * sc * a.nw[j] * silu_f(lda(a.z + t * a.ldz + hv * S + j));
         }
-        const double so = block_sum_d(active && qq == 0 ? (double)o * o : 0.0, red);
-        if (active) {
-            if (qq == 0) {
-                const float sc = 1.0f / sqrtf((float)(so / S) + eps);
-                out[t * ldo + hv * S + j] = o * sc * nw[j] * silu_f(z[t * ldz + hv * S + j]);
-            }
-            if (ck_ssm && t < T - 1) {
-                float *C = ck_ssm + ((size_t)t * Hv + hv) * S * S + (size_t)j * S + qq * P;
+        if (a.ck_ssm && t < a.T - 1) {
+            float *C = a.ck_ssm + ((size_t)t * a.Hv + hv) * S * S + (size_t)j * S + qq * P;
 #pragma unroll
-                for (int i = 0; i < P; i += 4) *reinterpret_cast<float4 *>(C + i) = make_float4(row[i], row[i + 1], row[i + 2], row[i + 3]);
-            }
+            for (int i = 0; i < P; i += 4) *reinterpret_cast<float4 *>(C + i) = make_float4(row[i], row[i + 1], row[i + 2], row[i + 3]);
         }
-        __syncthreads();
+        Bar::sync();
     }
-    if (active) {
 #pragma unroll
-        for (int i = 0; i < P; i += 4) *reinterpret_cast<float4 *>(M + i) = make_float4(row[i], row[i + 1], row[i + 2], row[i + 3]);
-    }
+    for (int i = 0; i < P; i += 4) *reinterpret_cast<float4 *>(M + i) = make_float4(row[i], row[i + 1], row[i + 2], row[i + 3]);
+}
+
+// One block of 4*S threads per value head.
+template <int S>
+__global__ void __launch_bounds__(4 * S) k_gdn(GdnArgs a) {
+    griddep_wait();
+    gdn_head<S, BarBlock>(a, blockIdx.x, threadIdx.x);
 }
 
 // ---------------------------------------------------------------- gated full attention
-// Per token t and head slot: q heads get RMSNorm(q_norm) + NeoX RoPE into qrot[t][h][D]; KV heads get
-// RMSNorm(k_norm) + RoPE and are stored with v at position npast+t (core/xj_cpu.c:107-116).
-// Grid (H + Hkv, T), D threads.
 template <typename KV>
 XJ_DEV void store_kv(KV *p, float v);
 template <> XJ_DEV void store_kv<float>(float *p, float v) { *p = v; }
 template <> XJ_DEV void store_kv<__half>(__half *p, float v) { *p = __float2half_rn(v); }
-XJ_DEV float load_kv(const float *p) { return *p; }
-XJ_DEV float load_kv(const __half *p) { return __half2float(*p); }
+// KV rows may have been written by another block this step: read them through L2.
+XJ_DEV float load_kv(const float *p) { return __ldcg(p); }
+XJ_DEV float load_kv(const __half *p) { return __half2float(__ushort_as_half(__ldcg(reinterpret_cast<const unsigned short *>(p)))); }
 
-template <typename KV>
-static __global__ void k_attn_prep(const float *q, long long ldq, const float *k, const float *v, long long ldkv,
-                            const float *qn, const float *kn, float *qrot, KV *kc, KV *vc, const int *npast,
-                            int H, int Hkv, int D, int n_rot, float base, float eps) {
-    extern __shared__ float sh[];
+struct AttnArgs {
+    const float *q; long long ldq;       // [T][H][q(D) | gate(D)]
+    const float *k, *v; long long ldkv;  // [T][Hkv*D]
+    const float *qn, *kn;                // per-head RMSNorm weights
+    float *qrot;                         // [T][H][D]
+    void *kc, *vc;                       // [n_ctx][Hkv*D]
+    const int *npast;
+    float *out; long long ldo;           // [T][H*D]
+    int H, Hkv, D, n_rot;
+    float base, eps;
+};
+
+// Token t, head slot `slot` (q heads, then KV heads): q heads get RMSNorm(q_norm) + NeoX RoPE into
+// qrot[t][h][D]; KV heads get RMSNorm(k_norm) + RoPE and are stored with v at position npast+t
+// (core/xj_cpu.c:107-116). Threads tid < ceil32(D) take part (Bar spans exactly those).
+template <typename KV, class Bar>
+XJ_DEV void attn_prep_slot(const AttnArgs &a, int slot, int t, int tid) {
+    __shared__ float sh[256];
     __shared__ double red[32];
-    griddep_wait();
-    const int t = blockIdx.y, slot = blockIdx.x, i = threadIdx.x;
-    const int pos = *npast + t;
-    const bool isq = slot < H;
-    const int hh = isq ? slot : slot - H;
-    const float *src = isq ? q + t * ldq + (size_t)hh * 2 * D : k + t * ldkv + (size_t)hh * D;
-    const float xi = i < D ? src[i] : 0.0f;
-    double ss = block_sum_d((double)xi * xi, red);
-    const float sc = 1.0f / sqrtf((float)(ss / D) + eps);
-    const float *nw = isq ? qn : kn;
-    if (i < D) sh[i] = xi * sc * nw[i];
-    __syncthreads();
-    float r = i < D ? sh[i] : 0.0f;
-    const int half = n_rot / 2;
-    if (i < n_rot) {
-        const int p = i < half ? i : i - half;
-        const float theta = (float)pos * powf(base, -2.0f * (float)p / (float)n_rot);
+    const int D = a.D, nthr = (D + 31) / 32 * 32;
+    const int pos = __ldcg(a.npast) + t;
+    const bool isq = slot < a.H;
+    const int hh = isq ? slot : slot - a.H;
+    const float *src = isq ? a.q + t * a.ldq + (size_t)hh * 2 * D : a.k + t * a.ldkv + (size_t)hh * D;
+    const float xi = tid < D ? lda(src + tid) : 0.0f;
+    const double ss = group_sum_d<Bar>((double)xi * xi, red, tid, nthr);
+    const float sc = 1.0f / sqrtf((float)(ss / D) + a.eps);
+    const float *nw = isq ? a.qn : a.kn;
+    if (tid < D) sh[tid] = xi * sc * nw[tid];
+    Bar::sync();
+    float r = tid < D ? sh[tid] : 0.0f;
+    const int half = a.n_rot / 2;
+    if (tid < a.n_rot) {
+        const int p = tid < half ? tid : tid - half;
+        const float theta = (float)pos * powf(a.base, -2.0f * (float)p / (float)a.n_rot);
         const float c = cosf(theta), s = sinf(theta);
         const float x0 = sh[p], x1 = sh[p + half];
-        r = i < half ? x0 * c - x1 * s : x0 * s + x1 * c;
+        r = tid < half ? x0 * c - x1 * s : x0 * s + x1 * c;
     }
-    if (i < D) {
-        if (isq) qrot[((size_t)t * H + hh) * D + i] = r;
+    if (tid < D) {
+        if (isq) a.qrot[((size_t)t * a.H + hh) * D + tid] = r;
         else {
-            const size_t o = (size_t)pos * Hkv * D + (size_t)hh * D + i;
-            store_kv<KV>(kc + o, r);
-            store_kv<KV>(vc + o, v[t * ldkv + (size_t)hh * D + i]);
+            const size_t o = (size_t)pos * a.Hkv * D + (size_t)hh * D + tid;
+            store_kv<KV>((KV *)a.kc + o, r);
+            store_kv<KV>((KV *)a.vc + o, lda(a.v + t * a.ldkv + (size_t)hh * D + tid));
         }
     }
+    Bar::sync();   // sh / red are reused by the caller's next slot
+}
+
+// Grid (H + Hkv, T), ceil32(D) threads.
+template <typename KV>
+static __global__ void k_attn_prep(AttnArgs a) {
+    griddep_wait();
+    attn_prep_slot<KV, BarBlock>(a, blockIdx.x, blockIdx.y, threadIdx.x);
 }
 
 // Attention of query (t, h) over positions 0..npast+t of its KV head, online softmax, then the
 // sigmoid output gate: out[t][h*D + i] = (sum_j p_j v_j[i]) * sigmoid(gate[i]) (core/xj_cpu.c:118-150).
-// One block of 4 warps per (h, t); lanes split the head dim (D <= 256, D % 32 == 0).
-template <typename KV, int DPL>
-static __global__ void __launch_bounds__(128) k_attn(const float *qrot, const float *qg, long long ldq, const KV *kc, const KV *vc,
-                                              const int *npast, float *out, long long ldo, int H, int Hkv, int D) {
+// 4 warps (tid < 128); lanes split the head dim (D <= 256).
+template <typename KV, int DPL, class Bar>
+XJ_DEV void attn_head(const AttnArgs &a, int h, int t, int tid) {
     __shared__ float sm_m[4], sm_l[4];
     __shared__ float sm_o[4][256];
-    griddep_wait();
-    const int h = blockIdx.x, t = blockIdx.y, warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n = *npast + t + 1, kvh = h / (H / Hkv), kvd = Hkv * D;
+    const int warp = tid >> 5, lane = tid & 31, D = a.D;
+    const int n = __ldcg(a.npast) + t + 1, kvh = h / (a.H / a.Hkv), kvd = a.Hkv * D;
     const float scale = 1.0f / sqrtf((float)D);
+    const KV *kc = (const KV *)a.kc, *vc = (const KV *)a.vc;
     float qv[DPL], o[DPL];
-    const float *qp = qrot + ((size_t)t * H + h) * D;
+    const float *qp = a.qrot + ((size_t)t * a.H + h) * D;
     const bool on = lane * DPL < D;   // head dims below 32 leave the upper lanes idle
 #pragma unroll
-    for (int d = 0; d < DPL; d++) { qv[d] = on ? qp[lane * DPL + d] : 0.0f; o[d] = 0.0f; }
+    for (int d = 0; d < DPL; d++) { qv[d] = on ? lda(qp + lane * DPL + d) : 0.0f; o[d] = 0.0f; }
     float m = -INFINITY, l = 0.0f;
     for (int j = warp; j < n; j += 4) {
         const KV *kr = kc + (size_t)j * kvd + (size_t)kvh * D + lane * DPL;
@@ -315,13 +355,13 @@ static __global__ void __launch_bounds__(128) k_attn(const float *qrot, const fl
     if (lane == 0) { sm_m[warp] = m; sm_l[warp] = l; }
 #pragma unroll
     for (int d = 0; d < DPL; d++) sm_o[warp][lane * DPL + d] = o[d];   // lane*DPL + d < 32*DPL <= 256
-    __syncthreads();
+    Bar::sync();
     if (warp == 0) {
         float M = fmaxf(fmaxf(sm_m[0], sm_m[1]), fmaxf(sm_m[2], sm_m[3]));
         float L = 0.0f, c[4];
 #pragma unroll
         for (int w = 0; w < 4; w++) { c[w] = sm_m[w] == -INFINITY ? 0.0f : expf(sm_m[w] - M); L += sm_l[w] * c[w]; }
-        const float *gate = qg + t * ldq + (size_t)h * 2 * D + D;
+        const float *gate = a.q + t * a.ldq + (size_t)h * 2 * D + D;
 #pragma unroll
         for (int d = 0; d < DPL; d++) {
             const int i = lane * DPL + d;
@@ -329,9 +369,17 @@ static __global__ void __launch_bounds__(128) k_attn(const float *qrot, const fl
             float acc = 0.0f;
 #pragma unroll
             for (int w = 0; w < 4; w++) acc = fmaf(sm_o[w][i], c[w], acc);
-            out[t * ldo + (size_t)h * D + i] = (acc / L) * sigm_f(gate[i]);
+            a.out[t * a.ldo + (size_t)h * D + i] = (acc / L) * sigm_f(lda(gate + i));
         }
     }
+    Bar::sync();   // sm_* are reused by the caller's next head
+}
+
+// Grid (H, T), 128 threads.
+template <typename KV, int DPL>
+static __global__ void __launch_bounds__(128) k_attn(AttnArgs a) {
+    griddep_wait();
+    attn_head<KV, DPL, BarBlock>(a, blockIdx.x, blockIdx.y, threadIdx.x);
 }
 
 // ---------------------------------------------------------------- FFN / misc
@@ -412,22 +460,34 @@ static __global__ void k_argmax_rows(const float *logits, int V, float *pbest, f
     if (threadIdx.x == 0) { pbest[tile] = b; psecond[tile] = b2; pidx[tile] = bi; }
 }
 
+struct ArgmaxArgs {
+    const float *pbest, *psecond;
+    const int *pidx;
+    int ntiles;
+    int32_t *out_tok;
+    float *margin;
+    int32_t *cur;
+    int *step;
+    DevMat emb;
+    float *x;
+    int *npast;
+};
+
 // Greedy pick from the LM head's per-tile partials (best, runner-up, lowest index of each 16 rows):
 // token = largest value, lowest index on ties (core/xj_spec.c:12-16). Writes out_tok[*step], the
 // runner-up gap to margin[*step], the token to *cur, then the token's embedding row into x (the next
-// decode step's input, core/xj_cpu.c:369-373), advances *npast by one and *step by one. One block.
-static __global__ void __launch_bounds__(1024) k_argmax_final(const float *pbest, const float *psecond, const int *pidx,
-                                                       int ntiles, int32_t *out_tok, float *margin, int32_t *cur,
-                                                       int *step, DevMat emb, float *x, int *npast) {
+// decode step's input, core/xj_cpu.c:369-373), advances *npast by one and *step by one.
+// nthr threads (a multiple of 32, at most 1024); Bar spans exactly those.
+template <class Bar>
+XJ_DEV void argmax_final_dev(const ArgmaxArgs &a, int tid, int nthr) {
     __shared__ float sv[32], sv2[32];
     __shared__ int si[32];
     __shared__ int s_tok;
-    griddep_wait();
     float b = -INFINITY, b2 = -INFINITY;
     int bi = 0x7fffffff;
-    for (int i = threadIdx.x; i < ntiles; i += blockDim.x) {
-        const float v = pbest[i], v2 = psecond[i];
-        const int vi = pidx[i];
+    for (int i = tid; i < a.ntiles; i += nthr) {
+        const float v = __ldcg(a.pbest + i), v2 = __ldcg(a.psecond + i);
+        const int vi = __ldcg(a.pidx + i);
         if (v > b || (v == b && vi < bi)) { b2 = fmaxf(fmaxf(b, b2), v2); b = v; bi = vi; }
         else b2 = fmaxf(b2, v);                      // the tile's runner-up is <= its best
     }
@@ -438,11 +498,11 @@ static __global__ void __launch_bounds__(1024) k_argmax_final(const float *pbest
         if (ov > b || (ov == b && oi < bi)) { b2 = fmaxf(b, ov2); b = ov; bi = oi; }
         else b2 = fmaxf(b2, ov);
     }
-    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int w = tid >> 5, lane = tid & 31;
     if (lane == 0) { sv[w] = b; sv2[w] = b2; si[w] = bi; }
-    __syncthreads();
+    Bar::sync();
     if (w == 0) {
-        const int nw = blockDim.x >> 5;
+        const int nw = nthr >> 5;
         b = lane < nw ? sv[lane] : -INFINITY;
         b2 = lane < nw ? sv2[lane] : -INFINITY;
         bi = lane < nw ? si[lane] : 0x7fffffff;
@@ -454,18 +514,19 @@ static __global__ void __launch_bounds__(1024) k_argmax_final(const float *pbest
             else b2 = fmaxf(b2, ov);
         }
         if (lane == 0) {
-            const int s = *step;
-            out_tok[s] = bi;
-            if (margin) margin[s] = b - b2;
-            *cur = bi;
-            *step = s + 1;
-            *npast += 1;
+            const int s = *a.step;
+            a.out_tok[s] = bi;
+            if (a.margin) a.margin[s] = b - b2;
+            *a.cur = bi;
+            *a.step = s + 1;
+            *a.npast += 1;
             s_tok = bi;
         }
     }
-    __syncthreads();
+    Bar::sync();
     const int id = s_tok;
-    for (int e0 = threadIdx.x * 8; e0 < emb.K; e0 += blockDim.x * 8) {
+    const DevMat &emb = a.emb;
+    for (int e0 = tid * 8; e0 < emb.K; e0 += nthr * 8) {
         float y[8];
         if (id >= 0 && id < emb.N) dequant8(emb.type, emb.p + id * emb.ld, e0, y);
         else {
@@ -473,8 +534,14 @@ static __global__ void __launch_bounds__(1024) k_argmax_final(const float *pbest
             for (int l = 0; l < 8; l++) y[l] = 0.0f;
         }
 #pragma unroll
-        for (int l = 0; l < 8; l++) x[e0 + l] = y[l];
+        for (int l = 0; l < 8; l++) a.x[e0 + l] = y[l];
     }
+}
+
+// One block of 1024 threads.
+static __global__ void __launch_bounds__(1024) k_argmax_final(ArgmaxArgs a) {
+    griddep_wait();
+    argmax_final_dev<BarBlock>(a, threadIdx.x, blockDim.x);
 }
 
 }  // namespace xjk

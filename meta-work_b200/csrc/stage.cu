@@ -277,43 +277,52 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
     }
 }
 
+GdnArgs gdn_args(Impl *im, const xj_hparams *hp, Layer &Ly, int T, bool ck) {
+    GdnArgs g;
+    g.qkv = im->qkvb; g.ldq = hp->conv_dim; g.z = im->z; g.ldz = hp->d_inner;
+    g.beta = im->beta; g.alpha = im->alpha; g.ldg = hp->h_v;
+    g.dt = Ly.dt; g.A = Ly.A; g.nw = Ly.ssm_norm;
+    g.ssm = Ly.ssm; g.ck_ssm = ck ? Ly.ck_ssm : nullptr; g.out = im->o; g.ldo = hp->d_inner;
+    g.T = T; g.Hk = hp->h_k; g.Hv = hp->h_v; g.key_dim = hp->key_dim; g.eps = hp->eps;
+    return g;
+}
+
 void launch_gdn(Impl *im, const xj_hparams *hp, Layer &Ly, int T, bool ck) {
-    const int S = hp->s_k;
-    const long long ldq = hp->conv_dim;
-#define GDN(SS) launch(im, k_gdn<SS>, dim3(hp->h_v), dim3(4 * SS < 64 ? 64 : 4 * SS), 0, (const float *)im->qkvb, ldq, \
-        (const float *)im->z, (long long)hp->d_inner, (const float *)im->beta, (const float *)im->alpha, (long long)hp->h_v, \
-        (const float *)Ly.dt, (const float *)Ly.A, (const float *)Ly.ssm_norm, Ly.ssm, ck ? Ly.ck_ssm : (float *)nullptr, \
-        im->o, (long long)hp->d_inner, T, hp->h_k, hp->h_v, hp->key_dim, hp->eps)
-    switch (S) {
-    case 16: GDN(16); break;
-    case 32: GDN(32); break;
-    case 64: GDN(64); break;
-    case 128: GDN(128); break;
-    case 256: GDN(256); break;
+    const GdnArgs g = gdn_args(im, hp, Ly, T, ck);
+    switch (hp->s_k) {
+    case 16: launch(im, k_gdn<16>, dim3(hp->h_v), dim3(64), 0, g); break;
+    case 32: launch(im, k_gdn<32>, dim3(hp->h_v), dim3(128), 0, g); break;
+    case 64: launch(im, k_gdn<64>, dim3(hp->h_v), dim3(256), 0, g); break;
+    case 128: launch(im, k_gdn<128>, dim3(hp->h_v), dim3(512), 0, g); break;
+    case 256: launch(im, k_gdn<256>, dim3(hp->h_v), dim3(1024), 0, g); break;
     default: break;
     }
-#undef GDN
+}
+
+AttnArgs attn_args(Impl *im, const xj_hparams *hp, Layer &Ly, const float *q, long long ldq, const float *k,
+                   const float *v, long long ldkv) {
+    AttnArgs a;
+    a.q = q; a.ldq = ldq; a.k = k; a.v = v; a.ldkv = ldkv;
+    a.qn = Ly.q_norm; a.kn = Ly.k_norm; a.qrot = im->qrot; a.kc = Ly.kc; a.vc = Ly.vc; a.npast = im->npast;
+    a.out = im->o; a.ldo = (long long)hp->n_head * hp->head_dim;
+    a.H = hp->n_head; a.Hkv = hp->n_head_kv; a.D = hp->head_dim; a.n_rot = hp->n_rot;
+    a.base = hp->rope_base; a.eps = hp->eps;
+    return a;
 }
 
 template <typename KV>
 void launch_attn(Impl *im, const xj_hparams *hp, Layer &Ly, int T, const float *q, long long ldq, const float *k,
                  const float *v, long long ldkv) {
+    const AttnArgs a = attn_args(im, hp, Ly, q, ldq, k, v, ldkv);
     const int H = hp->n_head, Hkv = hp->n_head_kv, D = hp->head_dim;
-    const int thr = (D + 31) / 32 * 32;
-    launch(im, k_attn_prep<KV>, dim3(H + Hkv, T), dim3(thr), D * sizeof(float), q, ldq, k, v, ldkv,
-           (const float *)Ly.q_norm, (const float *)Ly.k_norm, im->qrot, (KV *)Ly.kc, (KV *)Ly.vc,
-           (const int *)im->npast, H, Hkv, D, hp->n_rot, hp->rope_base, hp->eps);
-    const long long ldo = (long long)H * D;
-#define ATT(DPL) launch(im, k_attn<KV, DPL>, dim3(H, T), dim3(128), 0, (const float *)im->qrot, q, ldq, (const KV *)Ly.kc, \
-        (const KV *)Ly.vc, (const int *)im->npast, im->o, ldo, H, Hkv, D)
+    launch(im, k_attn_prep<KV>, dim3(H + Hkv, T), dim3((D + 31) / 32 * 32), 0, a);
     switch ((D + 31) / 32) {
-    case 1: ATT(1); break;
-    case 2: ATT(2); break;
-    case 4: ATT(4); break;
-    case 8: ATT(8); break;
+    case 1: launch(im, k_attn<KV, 1>, dim3(H, T), dim3(128), 0, a); break;
+    case 2: launch(im, k_attn<KV, 2>, dim3(H, T), dim3(128), 0, a); break;
+    case 4: launch(im, k_attn<KV, 4>, dim3(H, T), dim3(128), 0, a); break;
+    case 8: launch(im, k_attn<KV, 8>, dim3(H, T), dim3(128), 0, a); break;
     default: break;
     }
-#undef ATT
 }
 
 // All layers of the stage on im->x[T][E] (device) at positions *npast .. *npast+T-1, then a last kernel
@@ -380,6 +389,14 @@ void head(xj_stage *s, const float *x, int T) {
          {{im->output, im->logits, im->output.N}});
 }
 
+ArgmaxArgs argmax_args(Impl *im) {
+    ArgmaxArgs a;
+    a.pbest = im->pbest; a.psecond = im->psecond; a.pidx = im->pidx; a.ntiles = (im->output.N + 15) / 16;
+    a.out_tok = im->out_tok; a.margin = im->margin; a.cur = im->cur; a.step = im->step;
+    a.emb = im->tok_embd; a.x = im->x; a.npast = im->npast;
+    return a;
+}
+
 // Output norm + LM head for one row with the greedy pick fused (per-tile partials, then one small
 // kernel that also embeds the picked token into x and advances the position).
 void head_argmax(xj_stage *s, const float *x) {
@@ -388,9 +405,7 @@ void head_argmax(xj_stage *s, const float *x) {
     Job h{im->output, im->logits, im->output.N};
     h.epi = EPI_ARGMAX; h.pbest = im->pbest; h.psecond = im->psecond; h.pidx = im->pidx;
     gemv(im, x, nullptr, hp->n_embd, 1, PRO_NORM, im->output_norm, hp->eps, {h});
-    const int ntiles = (im->output.N + 15) / 16;
-    launch(im, k_argmax_final, dim3(1), dim3(1024), 0, (const float *)im->pbest, (const float *)im->psecond,
-           (const int *)im->pidx, ntiles, im->out_tok, im->margin, im->cur, im->step, im->tok_embd, im->x, im->npast);
+    launch(im, k_argmax_final, dim3(1), dim3(1024), 0, argmax_args(im));
 }
 
 int sync_check(Impl *im, char *err, size_t errlen) {
