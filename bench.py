@@ -229,7 +229,7 @@ def main():
         t_max, e2e_max = float(t[0]), float(t[1])
     value = world * args.steps / (t_max / 1e3)
     e2e = world * args.steps / (e2e_max / 1e3)
-    kernels = int(xjcuda.lib().xj_cuda_graph_kernels(stage.addr)) if hasattr(xjcuda.lib(), "xj_cuda_graph_kernels") else None
+    launches = sum(stage.last_decode_launches())   # of the timed call: its 1-token prompt + the steps
     if rank == 0:
         peak, peak_kind = hbm_peak()
         b = step_bytes(cfg, pos0 + args.steps // 2)
@@ -247,7 +247,7 @@ def main():
                          "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                          "bytes_per_step": round(b["total"]), "peak_kind": peak_kind},
             "clocks": clk,
-            "gpu_launches": kernels * args.steps if kernels else None,
+            "gpu_launches": launches,
             "tokens_check": int(toks[0]),
         }
         if world == 1 and not args.no_cpu_baseline:

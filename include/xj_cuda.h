@@ -46,7 +46,10 @@ uint64_t xjc_stage_state_bytes(const xj_model *m, int l0, int l1, int n_ctx, int
 //   XJC_OPT_GEMV     0 = fastest path per type (default), 1 = generic per-element path for every type.
 //   XJC_OPT_PDL      1 = kernels of a step overlap through programmatic dependent launch (default),
 //                    0 = each kernel starts after its predecessor completes.
-enum { XJC_OPT_KV_F32 = 1, XJC_OPT_GEMV = 2, XJC_OPT_PDL = 3 };
+//   XJC_OPT_PERSIST  1 = xj_cuda_decode runs all decode steps after the prompt in one persistent
+//                    cooperative kernel when every matrix of the stage is in the tensor-core layout
+//                    (default), 0 = one CUDA-graph replay of the per-phase kernels per step.
+enum { XJC_OPT_KV_F32 = 1, XJC_OPT_GEMV = 2, XJC_OPT_PDL = 3, XJC_OPT_PERSIST = 4 };
 int xj_cuda_set_options(int which, int value);
 
 // Greedy decode on a stage covering [0, n_layer) with the head. Feeds n_prompt ids (prefill in
@@ -70,6 +73,11 @@ int xj_cuda_gemv_time(int type, const void *w, int k, int n, int T, int copies, 
 // Number of kernel launches in one replay of the stage's cached decode-step graph (0 before the first
 // xj_cuda_decode call that generated more than one token).
 int xj_cuda_graph_kernels(const xj_stage *s);
+
+// Kernel launches made by the last xj_cuda_decode call: launches[0] for the prompt (prefill chunks and
+// the first pick), launches[1] for the decode steps after it (one per 8192 steps when the persistent
+// kernel ran them, else steps x xj_cuda_graph_kernels). Returns launches[0] + launches[1].
+long long xj_cuda_last_decode_launches(const xj_stage *s, long long *launches);
 
 // Dequantise n_rows rows of k elements of GGUF type `type` (host bytes in, host fp32 out) with the
 // device decoder the GEMV kernels use; for checking bit-exactness against xj_dequant_row

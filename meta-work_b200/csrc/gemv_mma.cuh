@@ -28,6 +28,7 @@
 // Every token column is computed independently in a fixed order, so a token's result does not depend
 // on how many other tokens share the launch (decode T=1 and speculative verify T>1 agree bit for bit).
 #pragma once
+#include <cstring>
 #include <vector>
 
 #include "kernels.cuh"
@@ -475,7 +476,7 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
         const MmaJob &jb = a.job[j];
         if (jb.epi == EPI_CONV) {
             // one thread per channel: the T tokens in order through the rolling conv state
-            if (tid < 16) {
+            if (tid < 16 && tile * 16 + tid < jb.w.N) {
                 const int ch = tile * 16 + tid, kc = jb.kc;
                 float cs[8];
                 for (int k = 0; k < kc - 1; k++) cs[k] = jb.conv_state[(size_t)ch * (kc - 1) + k];
@@ -503,7 +504,9 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
 #pragma unroll
                 for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + row) * 4 + 0];
                 s /= tok_scale[0];
-                if (jb.y && tid < 16) jb.y[(size_t)tile * 16 + row] = s;
+                const bool real = tile * 16 + row < jb.w.N;   // rows past N pad the last tile
+                if (jb.y && tid < 16 && real) jb.y[(size_t)tile * 16 + row] = s;
+                if (!real) s = -INFINITY;
                 // best / runner-up / lowest index of the tile's 16 rows (lanes 16..31 mirror 0..15)
                 float b = s, b2 = -INFINITY;
                 int bi = tile * 16 + row;
@@ -518,7 +521,7 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
             }
         } else if (tid < 64) {
             const int row = tid >> 2, t = tid & 3;
-            if (t < T) {
+            if (t < T && tile * 16 + row < jb.w.N) {
                 float s = 0.0f;
 #pragma unroll
                 for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + row) * 4 + t];
@@ -546,7 +549,7 @@ inline size_t mma_smem_bytes(int type, int T, int K) { return MmaSmem(T, K, ring
 
 // Matrices the tensor-core path can take (at up to MMA_MAXT tokens).
 inline bool tiled_ok(int type, int K, int N) {
-    if (N % 16 || K > MMA_KMAX) return false;
+    if (N < 1 || K > MMA_KMAX) return false;
     if (type == XJ_Q4_K || type == XJ_Q6_K) { if (K % 256) return false; }
     else if (type == XJ_Q8_0) { if (K % 32) return false; }
     else return false;
@@ -608,7 +611,8 @@ inline cudaError_t launch_mma(const MmaArgs &a, int type, cudaStream_t st) {
 }
 
 // ------------------------------------------------------------------ host: tiled re-encoding
-// Host bytes of the tiled layout for an [N][K] GGUF matrix (N % 16 == 0): q, h, s, d regions.
+// Host bytes of the tiled layout for an [N][K] GGUF matrix: q, h, s, d regions. The last tile is padded
+// to 16 rows with all-zero blocks (scale 0: every padded row's product is exactly 0).
 struct TiledHost {
     std::vector<uint8_t> q, h, s, d;
 };
@@ -629,8 +633,16 @@ inline uint8_t q6k_code(const uint8_t *blk, int col) {   // Q6_K code 0..63 (val
 inline int frag_col(int r, int e, int c) { return 2 * c + e + 8 * (r >> 1); }
 inline int frag_row(int r, int g) { return g + 8 * (r & 1); }
 
-inline void repack_tiled(int type, const uint8_t *src, int K, int N, TiledHost &o) {
-    const int tiles = N / 16;
+inline void repack_tiled(int type, const uint8_t *src_rows, int K, int N, TiledHost &o) {
+    const int tiles = (N + 15) / 16;
+    const size_t rb0 = type == XJ_Q8_0 ? (size_t)(K / 32) * 34 : (size_t)(K / 256) * (type == XJ_Q4_K ? 144 : 210);
+    std::vector<uint8_t> padded;
+    const uint8_t *src = src_rows;
+    if (N % 16) {
+        padded.assign((size_t)tiles * 16 * rb0, 0);
+        memcpy(padded.data(), src_rows, (size_t)N * rb0);
+        src = padded.data();
+    }
     if (type == XJ_Q4_K || type == XJ_Q6_K) {
         const int nu = K / 256, bb = type == XJ_Q4_K ? 144 : 210;
         const size_t rb = (size_t)nu * bb;

@@ -21,6 +21,7 @@
 #include "../../include/xj_cuda.h"
 #include "kernels.cuh"
 #include "gemv_mma.cuh"
+#include "decode_mk.cuh"
 
 using namespace xjk;
 
@@ -28,6 +29,7 @@ namespace {
 
 int g_opt_kv_f32 = 0;
 int g_opt_gemv = 0;
+int g_opt_persist = 1;
 
 void seterr(char *err, size_t errlen, const char *fmt, ...) {
     if (!err || !errlen) return;
@@ -81,6 +83,15 @@ struct Impl {
     // decode-step graph
     cudaGraphExec_t step_graph = nullptr;
     int step_kernels = 0;
+    // persistent decode kernel: phase program (device), barrier counter, attention split scratch
+    int mk_state = 0;          // 0: not built, 1: built, -1: this stage cannot use it
+    MkPhase *mk_prog = nullptr;
+    int mk_nphase = 0, mk_ctas = 0, mk_max_split = 1;
+    unsigned *mk_bar = nullptr;
+    float *mk_apart = nullptr;
+    int *mk_acnt = nullptr;
+    long long nlaunch = 0;                   // kernels launched on the stage stream so far
+    long long last_launches[2] = {0, 0};     // last xj_cuda_decode: prompt, decode steps
 };
 
 Impl *I(xj_stage *s) { return (Impl *)s->impl; }
@@ -177,6 +188,7 @@ struct Job {
 template <typename... KArgs, typename... Args>
 void launch(Impl *im, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, Args... args) {
     launch_pdl(kern, grid, block, smem, im->st, args...);
+    im->nlaunch++;
 }
 
 void rmsnorm(Impl *im, const float *x, long long ldx, const float *w, float *y, long long ldy, int n, int rows, float eps) {
@@ -209,7 +221,7 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
             mj.w = tiled_of(f.w); mj.y = f.y; mj.ldy = f.ldy; mj.epi = f.epi;
             mj.conv_state = f.conv_state; mj.conv_w = f.conv_w; mj.conv_ck = f.conv_ck; mj.kc = f.kc;
             mj.pbest = f.pbest; mj.psecond = f.psecond; mj.pidx = f.pidx;
-            m.tile_start[m.njob + 1] = m.tile_start[m.njob] + f.w.N / 16;
+            m.tile_start[m.njob + 1] = m.tile_start[m.njob] + (f.w.N + 15) / 16;
             m.njob++;
             done[k] = 1;
         }
@@ -229,6 +241,7 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
                 }
             }
             launch_mma(c, type, im->st);
+            im->nlaunch++;
             for (int j = 0; j < c.njob; j++)
                 if (m.job[j].conv_ck && t0 + c.T < T) {
                     // state after token t0+c.T-1 = current conv state: copy it into its checkpoint slot
@@ -316,13 +329,12 @@ void launch_attn(Impl *im, const xj_hparams *hp, Layer &Ly, int T, const float *
     const AttnArgs a = attn_args(im, hp, Ly, q, ldq, k, v, ldkv);
     const int H = hp->n_head, Hkv = hp->n_head_kv, D = hp->head_dim;
     launch(im, k_attn_prep<KV>, dim3(H + Hkv, T), dim3((D + 31) / 32 * 32), 0, a);
-    switch ((D + 31) / 32) {
-    case 1: launch(im, k_attn<KV, 1>, dim3(H, T), dim3(128), 0, a); break;
-    case 2: launch(im, k_attn<KV, 2>, dim3(H, T), dim3(128), 0, a); break;
-    case 4: launch(im, k_attn<KV, 4>, dim3(H, T), dim3(128), 0, a); break;
-    case 8: launch(im, k_attn<KV, 8>, dim3(H, T), dim3(128), 0, a); break;
-    default: break;
-    }
+    // lanes cover the head dim DPL elements each: DPL = 1, 2, 4 or 8 (head dims up to 256)
+    const int dpl = (D + 31) / 32;
+    if (dpl == 1) launch(im, k_attn<KV, 1>, dim3(H, T), dim3(128), 0, a);
+    else if (dpl == 2) launch(im, k_attn<KV, 2>, dim3(H, T), dim3(128), 0, a);
+    else if (dpl <= 4) launch(im, k_attn<KV, 4>, dim3(H, T), dim3(128), 0, a);
+    else launch(im, k_attn<KV, 8>, dim3(H, T), dim3(128), 0, a);
 }
 
 // All layers of the stage on im->x[T][E] (device) at positions *npast .. *npast+T-1, then a last kernel
@@ -415,7 +427,7 @@ int sync_check(Impl *im, char *err, size_t errlen) {
     int flag = 0;
     if (im->derr && cudaMemcpy(&flag, im->derr, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && flag) {
         cudaMemset(im->derr, 0, sizeof(int));
-        seterr(err, errlen, "GPU wait for the weight stream timed out");
+        seterr(err, errlen, "a bounded wait on the GPU gave up (%s)", flag == 2 ? "grid barrier" : "weight stream");
         return -1;
     }
     return 0;
@@ -645,6 +657,117 @@ void decode_step(xj_stage *s) {
     head_argmax(s, im->x);
 }
 
+// ------------------------------------------------------------------ persistent decode kernel
+// The phase program of one decode step: the same layer sequence as decode_step (run_layers at T = 1,
+// then the head with the fused greedy pick), expressed for k_decode_persistent. Returns false when a
+// matrix is not in the tiled layout (the persistent kernel has only the tensor-core GEMV).
+bool mk_gemv(std::vector<MkPhase> &prog, int K, int pro, const float *x, const float *x2, const float *norm_w,
+             float eps, int gs, std::initializer_list<Job> jobs) {
+    MkPhase p{};
+    p.op = MK_GEMV; p.K = K; p.pro = pro; p.x = x; p.x2 = x2; p.norm_w = norm_w; p.eps = eps; p.gs = gs;
+    if (K > MK_KMAX || K % 32) return false;
+    p.tile_start[0] = 0;
+    for (const Job &f : jobs) {
+        if (!f.w.tq || p.njob == 4 || f.w.K != K) return false;
+        MmaJob &mj = p.job[p.njob];
+        mj.w = tiled_of(f.w); mj.y = f.y; mj.ldy = f.ldy; mj.epi = f.epi;
+        mj.conv_state = f.conv_state; mj.conv_w = f.conv_w; mj.conv_ck = nullptr; mj.kc = f.kc;
+        mj.pbest = f.pbest; mj.psecond = f.psecond; mj.pidx = f.pidx;
+        p.tile_start[p.njob + 1] = p.tile_start[p.njob] + (f.w.N + 15) / 16;
+        p.njob++;
+    }
+    p.ntiles = p.tile_start[p.njob];
+    prog.push_back(p);
+    return true;
+}
+
+// 1: built, -1: unsupported for this stage, with the reason in err.
+int mk_build(xj_stage *s, char *err, size_t errlen) {
+    Impl *im = I(s);
+    if (im->mk_state) return im->mk_state;
+    const xj_hparams *hp = &s->m->hp;
+    const int E = hp->n_embd, FF = hp->n_ff;
+    const float eps = hp->eps;
+    std::vector<MkPhase> prog;
+    bool ok = hp->s_k == hp->s_v && hp->head_dim <= 256 && hp->n_head % hp->n_head_kv == 0;
+    for (int il = s->l0; ok && il < s->l1; il++) {
+        Layer &Ly = im->L[il - s->l0];
+        if (Ly.rec) {
+            const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v;
+            Job qkv{Ly.qkv, im->qkvb, CD};
+            qkv.epi = EPI_CONV; qkv.conv_state = Ly.conv; qkv.conv_w = Ly.conv_w; qkv.kc = hp->conv_k;
+            ok = ok && mk_gemv(prog, E, PRO_NORM, im->x, nullptr, Ly.attn_norm, eps, 0,
+                               {qkv, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
+            MkPhase g{};
+            g.op = MK_GDN; g.gdn = gdn_args(im, hp, Ly, 1, false); g.gs = hp->s_k;
+            prog.push_back(g);
+            Job out{Ly.out, im->x, E};
+            out.epi = EPI_ADD;
+            ok = ok && mk_gemv(prog, DI, PRO_GNORM, im->o, im->z, Ly.ssm_norm, eps, hp->s_k, {out});
+        } else {
+            const int H = hp->n_head, Hkv = hp->n_head_kv, D = hp->head_dim, nq = 2 * H * D, nk = Hkv * D;
+            const float *q, *k, *v;
+            long long ldq, ldkv;
+            if (Ly.fused) {
+                ok = ok && mk_gemv(prog, E, PRO_NORM, im->x, nullptr, Ly.attn_norm, eps, 0, {{Ly.wqkv, im->qkvb, nq + 2 * nk}});
+                q = im->qkvb; k = im->qkvb + nq; v = im->qkvb + nq + nk; ldq = ldkv = nq + 2 * nk;
+            } else {
+                ok = ok && mk_gemv(prog, E, PRO_NORM, im->x, nullptr, Ly.attn_norm, eps, 0,
+                                   {{Ly.wq, im->q, nq}, {Ly.wk, im->k, nk}, {Ly.wv, im->v, nk}});
+                q = im->q; k = im->k; v = im->v; ldq = nq; ldkv = nk;
+            }
+            MkPhase a{};
+            a.op = MK_ATTN; a.attn = attn_args(im, hp, Ly, q, ldq, k, v, ldkv);
+            prog.push_back(a);
+            Job o{Ly.wo, im->x, E};
+            o.epi = EPI_ADD;
+            ok = ok && mk_gemv(prog, H * D, PRO_NONE, im->o, nullptr, nullptr, eps, 0, {o});
+        }
+        ok = ok && mk_gemv(prog, E, PRO_NORM, im->x, nullptr, Ly.post_norm, eps, 0, {{Ly.ffn_gate, im->g, FF}, {Ly.ffn_up, im->u, FF}});
+        Job down{Ly.ffn_down, im->x, E};
+        down.epi = EPI_ADD;
+        ok = ok && mk_gemv(prog, FF, PRO_SWIGLU, im->g, im->u, nullptr, eps, 0, {down});
+    }
+    Job h{im->output, nullptr, im->output.N};
+    h.epi = EPI_ARGMAX; h.pbest = im->pbest; h.psecond = im->psecond; h.pidx = im->pidx;
+    ok = ok && mk_gemv(prog, E, PRO_NORM, im->x, nullptr, im->output_norm, eps, 0, {h});
+    if (!ok) { im->mk_state = -1; seterr(err, errlen, "persistent decode needs every matrix in the tiled layout"); return -1; }
+    MkPhase am{};
+    am.op = MK_ARGMAX; am.am = argmax_args(im);
+    prog.push_back(am);
+
+    // one CTA per SM, all resident (cooperative launch)
+    int sms = 0, per_sm = 0, coop = 0;
+    CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, im->dev));
+    CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, im->dev));
+    CK(cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent, MK_THREADS, MK_SMEM));
+    if (!coop || per_sm < 1) { im->mk_state = -1; seterr(err, errlen, "cooperative launch of the persistent decode kernel is not possible"); return -1; }
+    im->mk_ctas = sms;
+    im->mk_max_split = sms / hp->n_head > 0 ? sms / hp->n_head : 1;
+    if (dalloc(im, &im->mk_prog, prog.size(), err, errlen) || dalloc(im, &im->mk_bar, 4, err, errlen) ||
+        dalloc(im, &im->mk_acnt, (size_t)hp->n_head, err, errlen) ||
+        dalloc(im, &im->mk_apart, (size_t)hp->n_head * im->mk_max_split * (hp->head_dim + 2), err, errlen)) return -1;
+    CK(cudaMemcpy(im->mk_prog, prog.data(), prog.size() * sizeof(MkPhase), cudaMemcpyHostToDevice));
+    im->mk_nphase = (int)prog.size();
+    im->mk_state = 1;
+    return 1;
+}
+
+// n decode steps in one cooperative launch (k_decode_persistent).
+int mk_launch(xj_stage *s, int n, char *err, size_t errlen) {
+    Impl *im = I(s);
+    MkArgs a{};
+    a.prog = im->mk_prog; a.nphase = im->mk_nphase; a.nsteps = n;
+    a.bar = im->mk_bar; a.err = im->derr; a.apart = im->mk_apart; a.acnt = im->mk_acnt;
+    a.max_split = im->mk_max_split; a.kv_f32 = im->kv_f32 ? 1 : 0;
+    CK(cudaMemsetAsync(im->mk_bar, 0, sizeof(unsigned), im->st));
+    CK(cudaMemsetAsync(im->mk_acnt, 0, sizeof(int) * (size_t)s->m->hp.n_head, im->st));
+    void *args[] = {&a};
+    CK(cudaLaunchCooperativeKernel((const void *)k_decode_persistent, dim3(im->mk_ctas), dim3(MK_THREADS), args, MK_SMEM, im->st));
+    return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -663,6 +786,7 @@ int xj_cuda_set_options(int which, int value) {
     case XJC_OPT_KV_F32: g_opt_kv_f32 = value; return 0;
     case XJC_OPT_GEMV: g_opt_gemv = value; return 0;
     case XJC_OPT_PDL: g_pdl = value ? 1 : 0; return 0;
+    case XJC_OPT_PERSIST: g_opt_persist = value; return 0;
     default: return -1;
     }
 }
@@ -725,6 +849,7 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
     }
     CK(cudaMemsetAsync(im->step, 0, sizeof(int), im->st));
     CK(cudaEventRecord(im->ev[0], im->st));
+    const long long nl0 = im->nlaunch;
     const int B = s->max_batch;
     for (int i = 0; i < n_prompt; i += B) {
         const int T = n_prompt - i < B ? n_prompt - i : B;
@@ -735,7 +860,20 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
         if (last) head_argmax(s, im->x + (size_t)(T - 1) * E);   // picks out[0], embeds it, position +1
     }
     CK(cudaEventRecord(im->ev[1], im->st));
-    if (n_gen > 1) {
+    im->last_launches[0] = im->nlaunch - nl0;
+    im->last_launches[1] = 0;
+    int persist = 0;
+    if (n_gen > 1 && g_opt_persist) {
+        char why[256];
+        persist = mk_build(s, why, sizeof why) == 1;
+    }
+    if (n_gen > 1 && persist) {
+        // segments of at most 8192 steps keep the grid barrier's 32-bit counter far from wrapping
+        for (int done = 0; done < n_gen - 1; done += 8192) {
+            if (mk_launch(s, n_gen - 1 - done < 8192 ? n_gen - 1 - done : 8192, err, errlen)) return -1;
+            im->last_launches[1]++;
+        }
+    } else if (n_gen > 1) {
         if (!im->step_graph) {
             cudaGraph_t g;
             CK(cudaStreamBeginCapture(im->st, cudaStreamCaptureModeThreadLocal));
@@ -747,6 +885,7 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
             if (e != cudaSuccess) { seterr(err, errlen, "graph instantiate: %s", cudaGetErrorString(e)); im->step_graph = nullptr; return -1; }
         }
         for (int i = 1; i < n_gen; i++) CK(cudaGraphLaunch(im->step_graph, im->st));
+        im->last_launches[1] = (long long)(n_gen - 1) * im->step_kernels;
     }
     CK(cudaEventRecord(im->ev[2], im->st));
     CK(cudaMemcpyAsync(out, im->out_tok, sizeof(int32_t) * n_gen, cudaMemcpyDeviceToHost, im->st));
@@ -832,6 +971,13 @@ int xj_cuda_gemv_time(int type, const void *w, int k, int n, int t, int copies, 
 int xj_cuda_graph_kernels(const xj_stage *s) {
     const Impl *im = (const Impl *)s->impl;
     return im ? im->step_kernels : 0;
+}
+
+long long xj_cuda_last_decode_launches(const xj_stage *s, long long *launches) {
+    const Impl *im = (const Impl *)s->impl;
+    if (!im) return 0;
+    if (launches) { launches[0] = im->last_launches[0]; launches[1] = im->last_launches[1]; }
+    return im->last_launches[0] + im->last_launches[1];
 }
 
 int xj_cuda_dequant_rows(int type, const void *src, int k, int n_rows, float *out, char *err, size_t errlen) {

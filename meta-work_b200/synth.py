@@ -8,6 +8,8 @@ The named configurations are the workloads of the decode benchmark suite:
   GDN 16 x 128, FFN 6144, vocab 151936, Q4_K_M policy (Q6_K embeddings/head, Q6_K ffn_down and
   attn_v on the "more bits" layers).
 - ``DRAFT``: the config-0 architecture widened to E=1024 / 8 layers, Q8_0, vocab of CONFIG3.
+- ``MID``: CONFIG3's head shapes and Q4_K_M policy at test size: 8 layers (6 GDN + 2 GQA), E=512,
+  4 q / 2 KV heads x 128, GDN 4 x 128, FFN 1536, vocab 4096.
 """
 from __future__ import annotations
 
@@ -80,6 +82,8 @@ CONFIG0 = ModelConfig("config0-tiny-q8_0")
 CONFIG3 = ModelConfig(
     "config3-2b-q4_k_m", n_layer=28, n_embd=2048, n_ff=6144, n_vocab=151936, n_head=16, n_head_kv=4,
     head_dim=128, n_rot=32, s_k=128, h_k=16, h_v=16, wtype=Q4_K)
+MID = ModelConfig("mid-q4_k_m", n_layer=8, n_embd=512, n_ff=1536, n_vocab=4096, n_head=4, n_head_kv=2,
+                  head_dim=128, n_rot=32, s_k=128, h_k=4, h_v=4, wtype=Q4_K)
 DRAFT = ModelConfig("draft-1024-q8_0", n_layer=8, n_embd=1024, n_ff=2816, n_vocab=151936, n_head=8,
                     n_head_kv=2, head_dim=128, n_rot=32, s_k=128, h_k=4, h_v=8, wtype=Q8_0)
 

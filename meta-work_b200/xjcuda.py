@@ -19,7 +19,7 @@ LIB = HERE / "csrc" / "libxj_cuda.so"
 _lib = None
 
 F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 8, 12, 13, 14, 30
-OPT_KV_F32, OPT_GEMV, OPT_PDL = 1, 2, 3
+OPT_KV_F32, OPT_GEMV, OPT_PDL, OPT_PERSIST = 1, 2, 3, 4
 
 
 class XjError(RuntimeError):
@@ -98,6 +98,7 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_decode": (ip, [vp, vp, ip, ip, vp, vp, vp, cp, sz]),
         "xj_cuda_dequant_rows": (ip, [ip, vp, ip, ip, vp, cp, sz]),
         "xj_cuda_graph_kernels": (ip, [vp]),
+        "xj_cuda_last_decode_launches": (ctypes.c_longlong, [vp, vp]),
         "xj_cuda_gemv": (ip, [ip, vp, ip, ip, vp, ip, vp, ip, cp, sz]),
         "xj_cuda_gemv_time": (ip, [ip, vp, ip, ip, ip, ip, ip, ip, vp, cp, sz]),
         "xj_cuda_norm_gemv_noalloc": (ip, [ip, vp, ip, ip, vp, vp, ctypes.c_float, ip, vp, cp, sz]),
@@ -272,6 +273,13 @@ class Stage:
         if rc:
             _raise(e)
         return out, mar, ms
+
+    def last_decode_launches(self) -> tuple[int, int]:
+        """Kernel launches of the last decode() call: (prompt, decode steps after it); the persistent
+        kernel runs up to 8192 steps per launch."""
+        v = (ctypes.c_longlong * 2)()
+        lib().xj_cuda_last_decode_launches(self.addr, v)
+        return int(v[0]), int(v[1])
 
     def close(self):
         if self.p:

@@ -10,7 +10,8 @@ Writes, next to this script:
                   F32 / Q8_0 weights, vocab 288, one MTP layer, seed 20261107).
   golden.npz      outputs of the reference CPU path (oracle/_ref/libxjref.so, built from the
                   reference's own core/*.c by oracle/Makefile) on that model and on the synthetic
-                  config-0 model, plus row dequantisation known answers for every supported type.
+                  config-0 (Q8_0) and mid (Q4_K_M, config-3 head shapes) models, plus row
+                  dequantisation known answers for every supported type.
 The GPU box has no reference tree, so the tests read these files instead of re-running the reference.
 """
 from __future__ import annotations
@@ -43,6 +44,7 @@ def load_pkg():
 # Seeds and shapes of every golden case (tests import these so they never drift apart).
 TINY_PROMPT_SEED, TINY_N_PROMPT, TINY_N_GEN = 7, 24, 48
 C0_PROMPT_SEED, C0_N_PROMPT, C0_N_GEN = 1, 32, 64
+MID_PROMPT_SEED, MID_N_PROMPT, MID_N_GEN = 3, 40, 64
 TRACE_CHUNKS = (12, 1, 1, 1)      # tools/xjpipe-check.c:61 (prefill 12, then 3 single tokens)
 DQ_ROWS, DQ_K = 4, 512
 
@@ -120,6 +122,15 @@ def main():
     hid0, lg0 = m0.layer_trace(p0[:sum(TRACE_CHUNKS)], TRACE_CHUNKS, max_batch=16, n_ctx=128)
     g.update(config0_prompt=p0, config0_tokens=tok0, config0_margins=mar0, config0_first_logits=first0,
              config0_trace_hid=hid0, config0_trace_logits=lg0, config0_fingerprint=np.uint64(m0.fingerprint))
+    # ---- synthetic mid model (Q4_K / Q6_K, 128-wide heads) ----
+    cm = HERE.parent.parent / "_work" / "golden_mid.gguf"
+    synth.write_gguf(cm, synth.MID)
+    g["mid_sha256"] = np.frombuffer(hashlib.sha256(cm.read_bytes()).digest(), np.uint8)
+    mm = ref.Model(cm)
+    pm = prompt(MID_PROMPT_SEED, MID_N_PROMPT, mm.n_vocab)
+    tokm, marm, firstm, _ = mm.greedy(pm, MID_N_GEN, max_batch=8, n_ctx=512)
+    g.update(mid_prompt=pm, mid_tokens=tokm, mid_margins=marm, mid_first_logits=firstm,
+             mid_fingerprint=np.uint64(mm.fingerprint))
     # ---- dequant known answers ----
     for t, (raw, dq) in dequant_cases(synth).items():
         g[f"dq_{t}_raw"] = raw

@@ -11,7 +11,7 @@ import numpy as np
 import pytest
 
 from conftest import rel_err
-from make_golden import C0_N_GEN, DQ_K, DQ_ROWS, TINY_N_GEN, TRACE_CHUNKS
+from make_golden import C0_N_GEN, DQ_K, DQ_ROWS, MID_N_GEN, TINY_N_GEN, TRACE_CHUNKS
 from oracle import xj_oracle as xo
 
 pytestmark = pytest.mark.gpu
@@ -26,10 +26,11 @@ def xc():
     yield xjcuda
     xjcuda.set_option(xjcuda.OPT_KV_F32, 0)
     xjcuda.set_option(xjcuda.OPT_GEMV, 0)
+    xjcuda.set_option(xjcuda.OPT_PERSIST, 1)
 
 
-def model_path(which, tiny_path, config0_path):
-    return tiny_path if which == "tiny" else config0_path
+def model_path(which, tiny_path, config0_path, mid_path=None):
+    return {"tiny": tiny_path, "config0": config0_path, "mid": mid_path}[which]
 
 
 @pytest.mark.parametrize("t", TYPES)
@@ -84,21 +85,69 @@ def test_greedy_tokens_identical_vtable(xc, golden, tiny_path, config0_path, whi
     assert s.n_past == len(p) + n_gen - 1
 
 
-@pytest.mark.parametrize("which", ["tiny", "config0"])
-def test_greedy_tokens_identical_device_decode(xc, golden, tiny_path, config0_path, which):
+@pytest.mark.parametrize("persist", [0, 1])
+@pytest.mark.parametrize("which", ["tiny", "config0", "mid"])
+def test_greedy_tokens_identical_device_decode(xc, golden, tiny_path, config0_path, mid_path, which, persist):
+    """xj_cuda_decode against the reference's greedy tokens, through the per-step graph (persist=0) and
+    the persistent kernel (persist=1; the tiny model's F32 matrices keep it on the graph path)."""
     xc.set_option(xc.OPT_KV_F32, 0)
-    m = xc.Model(model_path(which, tiny_path, config0_path))
+    xc.set_option(xc.OPT_PERSIST, persist)
+    m = xc.Model(model_path(which, tiny_path, config0_path, mid_path))
     s = xc.Stage(m, 0, m.n_layer, 512, 8)
     p = golden[f"{which}_prompt"]
-    n_gen = TINY_N_GEN if which == "tiny" else C0_N_GEN
+    n_gen = {"tiny": TINY_N_GEN, "config0": C0_N_GEN, "mid": MID_N_GEN}[which]
     toks, margins, ms = s.decode(p, n_gen, want_margins=True)
     assert toks.tolist() == golden[f"{which}_tokens"].tolist()
     assert np.allclose(margins, golden[f"{which}_margins"], rtol=0.05, atol=2e-3)
     assert s.n_past == len(p) + n_gen - 1 and ms[1] > 0
+    pre, launches = s.last_decode_launches()
+    assert pre > 0
+    if persist and which != "tiny":
+        assert launches == 1
+    else:
+        assert launches == (n_gen - 1) * xc.lib().xj_cuda_graph_kernels(s.addr) > n_gen
     # a second call continues the same sequence; reset starts over and reproduces the first call
     s.reset()
     toks2, _, _ = s.decode(p, n_gen)
     assert toks2.tolist() == toks.tolist()
+
+
+@pytest.mark.parametrize("which", ["config0", "mid"])
+def test_persistent_decode_kv_f32_and_continuation(xc, golden, config0_path, mid_path, which):
+    """The persistent kernel with the fp32 KV cache, and a decode split into two calls (the second call
+    continues from the first one's position and state) against the reference's tokens."""
+    xc.set_option(xc.OPT_PERSIST, 1)
+    xc.set_option(xc.OPT_KV_F32, 1)
+    m = xc.Model(model_path(which, None, config0_path, mid_path))
+    s = xc.Stage(m, 0, m.n_layer, 512, 8)
+    xc.set_option(xc.OPT_KV_F32, 0)
+    p = golden[f"{which}_prompt"]
+    want = golden[f"{which}_tokens"].tolist()
+    a, _, _ = s.decode(p, 20)
+    assert s.last_decode_launches()[1] == 1
+    # the last emitted id is not fed back: passing it as a one-token prompt continues the sequence
+    b, _, _ = s.decode(a[-1:], len(want) - 20)
+    assert a.tolist() + b.tolist() == want
+
+
+def test_persistent_matches_graph_path_long_context(xc, mid_path):
+    """Long run (attention over up to ~1000 positions, split across CTAs) through both CUDA paths: the
+    ids agree until the first step whose top-2 gap is a near tie (the two paths sum GDN and attention
+    in different orders)."""
+    m = xc.Model(mid_path)
+    p = np.random.default_rng(5).integers(0, m.n_vocab, 700).astype(np.int32)
+    out = {}
+    for persist in (0, 1):
+        xc.set_option(xc.OPT_PERSIST, persist)
+        s = xc.Stage(m, 0, m.n_layer, 1100, 64)
+        out[persist] = s.decode(p, 300, want_margins=True)
+        assert s.last_decode_launches()[1] == (1 if persist else 299 * xc.lib().xj_cuda_graph_kernels(s.addr))
+        s.close()
+    (t0, m0, _), (t1, m1, _) = out[0], out[1]
+    diff = np.nonzero(t0 != t1)[0]
+    first = int(diff[0]) if diff.size else len(t0)
+    assert first >= 100 or m0[first] < 5e-3, (first, m0[first])
+    assert np.allclose(m0[:first], m1[:first], rtol=0.05, atol=2e-3)
 
 
 def test_reference_driver_runs_cuda_stage(xc, ref_lib, golden, tiny_path, config0_path):
