@@ -49,7 +49,9 @@ uint64_t xjc_stage_state_bytes(const xj_model *m, int l0, int l1, int n_ctx, int
 //   XJC_OPT_PERSIST  1 = xj_cuda_decode runs all decode steps after the prompt in one persistent
 //                    cooperative kernel when every matrix of the stage is in the tensor-core layout
 //                    (default), 0 = one CUDA-graph replay of the per-phase kernels per step.
-enum { XJC_OPT_KV_F32 = 1, XJC_OPT_GEMV = 2, XJC_OPT_PDL = 3, XJC_OPT_PERSIST = 4 };
+//   XJC_OPT_TRACE    1 = the persistent kernel records when each CTA starts and ends each phase of
+//                    its last step (read with xj_cuda_phase_trace), 0 = off (default).
+enum { XJC_OPT_KV_F32 = 1, XJC_OPT_GEMV = 2, XJC_OPT_PDL = 3, XJC_OPT_PERSIST = 4, XJC_OPT_TRACE = 5 };
 int xj_cuda_set_options(int which, int value);
 
 // Greedy decode on a stage covering [0, n_layer) with the head. Feeds n_prompt ids (prefill in
@@ -78,6 +80,14 @@ int xj_cuda_graph_kernels(const xj_stage *s);
 // the first pick), launches[1] for the decode steps after it (one per 8192 steps when the persistent
 // kernel ran them, else steps x xj_cuda_graph_kernels). Returns launches[0] + launches[1].
 long long xj_cuda_last_decode_launches(const xj_stage *s, long long *launches);
+
+// Phase timing of the persistent kernel's last traced step (XJC_OPT_TRACE): for each phase p < cap,
+// out[9p..9p+8] = {kind (0 matrix-vector, 1 Gated DeltaNet, 2 attention, 3 token pick), longest CTA
+// time in the phase (us), mean CTA time (us), first start to last end over CTAs (us), first start
+// (us, device clock), mean time a CTA's consumers waited for weight chunks (us), mean lead of the
+// first chunk request before the phase started (us), mean prologue time (us), mean time of the first
+// tile after the prologue (us)}. Returns the number of phases, or -1.
+int xj_cuda_phase_trace(const xj_stage *s, double *out, int cap);
 
 // Dequantise n_rows rows of k elements of GGUF type `type` (host bytes in, host fp32 out) with the
 // device decoder the GEMV kernels use; for checking bit-exactness against xj_dequant_row

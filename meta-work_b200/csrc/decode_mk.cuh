@@ -38,12 +38,14 @@ constexpr int MK_SLOT = 26880;                   // largest chunk: 8 Q6_K units
 constexpr int MK_NS = 6;                         // ring slots
 constexpr int MK_KMAX = MMA_KMAX_PT * MK_CTHREADS;
 constexpr int MK_XS_BYTES = 2 * (MK_KMAX + 16) * 2;   // hi/lo fp16 columns (also GDN / attention scratch)
+constexpr int MK_ATTN_SCR = 5440;                     // floats of attention scratch (split merge: nsplit*(D+2))
+static_assert(MK_ATTN_SCR * 4 <= MK_XS_BYTES, "attention scratch lives in the activation staging area");
 using BarC = BarNamed<1, MK_CTHREADS>;           // the consumer warps only
 
 enum { MK_GEMV = 0, MK_GDN = 1, MK_ATTN = 2, MK_ARGMAX = 3 };
 enum { PRO_GNORM = 3 };                          // per-head RMSNorm(ssm_norm) * silu(z), core/xj_cpu.c:218-224
 
-struct MkPhase {
+struct alignas(16) MkPhase {
     int op;
     // MK_GEMV
     int njob, ntiles;
@@ -59,15 +61,32 @@ struct MkPhase {
     ArgmaxArgs am;
 };
 
+// One GEMV phase as the producer streams it (the weight regions of each job's tiled layout).
+struct alignas(16) MkStream {
+    int ntiles, njob, ph;         // ph: index of the phase in the program
+    int tile_start[5];
+    int type[4], nu[4];
+    const uint8_t *q[4], *h[4], *s[4], *d[4];
+    // side data of this phase and of the non-GEMV phase after it (norm and conv weights, recurrent
+    // state), prefetched into L2 when the producer reaches this phase: a 1/G slice per CTA
+    const uint8_t *pf[6];
+    unsigned pf_bytes[6];
+};
+
 struct MkArgs {
     const MkPhase *prog;
-    int nphase, nsteps;
+    const MkStream *stream;      // the GEMV phases of prog, in order
+    int nphase, nstream, nsteps;
+    unsigned long long *trace;   // optional, per CTA and phase of the last step (ns): start, end, time the
+                                 // consumers waited for weights, first and last chunk request, end of
+                                 // the prologue, end of the first tile, tiles
     unsigned *bar;               // grid barrier counter, zero at launch
     int *err;                    // 1: weight stream wait gave up, 2: grid barrier wait gave up
     float *apart;                // attention split partials [H][max_split][D + 2]
     int *acnt;                   // per-head split counters, zero at launch
     int max_split;
     int kv_f32;
+    int *diag;                   // first wait that gave up: kind, cta, tid, step, phase, index, extra
 };
 
 constexpr size_t MK_SMEM = (size_t)MK_NS * MK_SLOT + MK_XS_BYTES + (MK_KMAX / 32) * 4 + MK_CWARPS * 128 * 4 +
@@ -99,23 +118,36 @@ XJ_DEV void mbar_arrive(uint64_t *bar) {
 
 constexpr unsigned long long MK_WAIT_NS = 2000000000ull;   // 2 s: no legitimate wait comes near it
 
-// Wait for an mbarrier phase; gives up (recording `code`) after MK_WAIT_NS (or 2^30 polls, should the
-// clock not advance) or as soon as another part of the grid has recorded an error.
-XJ_DEV bool mk_wait(uint64_t *bar, uint32_t parity, int *err, int code) {
+// Where the first wait that gave up was (read by the host after an error).
+XJ_DEV void mk_record(int *diag, int kind, int step, int ph, int idx, int extra) {
+    if (diag && atomicCAS(diag, 0, kind) == 0) {
+        diag[1] = blockIdx.x; diag[2] = threadIdx.x; diag[3] = step; diag[4] = ph; diag[5] = idx; diag[6] = extra;
+        __threadfence();
+    }
+}
+
+// Wait for an mbarrier phase; gives up (recording `code`) after MK_WAIT_NS (or 2^24 rounds of polls,
+// should the clock not advance) or as soon as another part of the grid has recorded an error. Between
+// rounds of polls the thread sleeps `nap` ns, so a waiting warp does not take issue slots from the
+// warps that compute.
+XJ_DEV bool mk_wait(uint64_t *bar, uint32_t parity, int *err, int code, int *diag = nullptr, int step = 0,
+                    int ph = 0, int idx = 0, int nap = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
     for (int it = 0; it < (1 << 24); it++) {
-        for (int i = 0; i < 64; i++)
+        for (int i = 0; i < 4; i++)
             if (mbar_try_wait(bar, parity)) return true;
+        if (nap) __nanosleep(nap);
         if (ld_volatile(err)) return false;
         if (globaltimer() - t0 > MK_WAIT_NS) break;
     }
+    mk_record(diag, code == 1 ? 10 + (int)parity : code, step, ph, idx, (int)(globaltimer() - t0) / 1000);
     atomicExch(err, code);
     return false;
 }
 
 // All consumer threads of all CTAs: returns false (uniformly) when the grid records an error.
-XJ_DEV bool mk_grid_sync(unsigned *bar, unsigned target, int *err, int tid) {
+XJ_DEV bool mk_grid_sync(unsigned *bar, unsigned target, int *err, int tid, int *diag, int step, int ph) {
     __shared__ int s_ok;
     BarC::sync();
     if (tid == 0) {
@@ -125,7 +157,12 @@ XJ_DEV bool mk_grid_sync(unsigned *bar, unsigned target, int *err, int tid) {
         const unsigned long long t0 = globaltimer();
         for (int it = 0; ld_acquire(bar) < target; it++) {
             if (ld_volatile(err)) { ok = 0; break; }
-            if (globaltimer() - t0 > MK_WAIT_NS || it > (1 << 27)) { atomicExch(err, 2); ok = 0; break; }
+            if (globaltimer() - t0 > MK_WAIT_NS || it > (1 << 27)) {
+                mk_record(diag, 2, step, ph, (int)target, (int)ld_acquire(bar));
+                atomicExch(err, 2);
+                ok = 0;
+                break;
+            }
             __nanosleep(20);
         }
         __threadfence();
@@ -134,6 +171,23 @@ XJ_DEV bool mk_grid_sync(unsigned *bar, unsigned target, int *err, int tid) {
     }
     BarC::sync();
     return s_ok != 0;
+}
+
+// Asynchronous 16-byte global -> shared copies (L2 only) for the phase descriptors.
+XJ_DEV void cp_async16(void *dst, const void *src) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" :: "r"(smem_u32(dst)), "l"(src) : "memory");
+}
+XJ_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+XJ_DEV void prefetch_l2(const void *p, unsigned bytes) {   // p 16-byte aligned, bytes a multiple of 16
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" :: "l"(p), "r"(bytes) : "memory");
+}
+XJ_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Threads tid < bytes/16 start copying `bytes` (a multiple of 16) from src to dst.
+XJ_DEV void copy_desc_async(void *dst, const void *src, int bytes, int tid) {
+    if (tid < bytes / 16) {
+        cp_async16(reinterpret_cast<uint8_t *>(dst) + tid * 16, reinterpret_cast<const uint8_t *>(src) + tid * 16);
+        cp_async_commit();
+    }
 }
 
 // ------------------------------------------------------------------ matrix-vector phases
@@ -145,100 +199,167 @@ XJ_DEV int mk_job_of(const MkPhase &p, int tg) {
 }
 
 template <int TYPE>
-XJ_DEV void mk_issue_t(const Tiled &W, int tile, int u0, int cu, uint8_t *st, uint64_t *bar) {
+XJ_DEV void mk_issue_t(const MkStream &S, int j, int tile, int u0, int cu, uint8_t *st, uint64_t *bar) {
     using G = Geo<TYPE>;
-    const size_t tu0 = (size_t)tile * W.nu + u0;
+    const size_t tu0 = (size_t)tile * S.nu[j] + u0;
     mbar_expect_tx(bar, (uint32_t)(cu * unit_bytes<TYPE>()));
-    bulk_g2s(st, W.q + tu0 * G::QB, cu * G::QB, bar);
-    if (G::HB) bulk_g2s(st + G::CU * G::QB, W.h + tu0 * G::HB, cu * G::HB, bar);
-    if (G::SB) bulk_g2s(st + G::CU * (G::QB + G::HB), W.s + tu0 * G::SB, cu * G::SB, bar);
-    if (G::DB) bulk_g2s(st + G::CU * (G::QB + G::HB + G::SB), W.d + tu0 * G::DB, cu * G::DB, bar);
+    bulk_g2s(st, S.q[j] + tu0 * G::QB, cu * G::QB, bar);
+    if (G::HB) bulk_g2s(st + G::CU * G::QB, S.h[j] + tu0 * G::HB, cu * G::HB, bar);
+    if (G::SB) bulk_g2s(st + G::CU * (G::QB + G::HB), S.s[j] + tu0 * G::SB, cu * G::SB, bar);
+    if (G::DB) bulk_g2s(st + G::CU * (G::QB + G::HB + G::SB), S.d[j] + tu0 * G::DB, cu * G::DB, bar);
 }
 
 // f(x) for one token -> exact power-of-two range scale -> fp16 hi/lo columns (B operand) + 32-wide block
-// sums; the same arithmetic as k_gemv_mma's prologue at T = 1. Returns the range scale.
+// sums, as k_gemv_mma's prologue at T = 1 computes them. Thread t takes the 4 consecutive elements
+// 2048r + 4t .. +3 (r < 3): one vector load per operand (all issued before the first use, so the
+// prologue costs one memory round trip), two half2 stores per column, and block sums over 8 lanes.
+// Sums of squares are accumulated in double, where they are exact, so their order does not matter.
+// Returns the range scale.
+XJ_DEV float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
+XJ_DEV float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
+XJ_DEV float f4(const float4 &v, int e) { return e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w; }
+XJ_DEV void f4set(float4 &v, int e, float x) { if (e == 0) v.x = x; else if (e == 1) v.y = x; else if (e == 2) v.z = x; else v.w = x; }
+
 XJ_DEV float mk_prologue(const MkPhase &p, __half *xs, float *xsum, int tid) {
-    __shared__ float s_ss[MK_CWARPS], s_am[MK_CWARPS];
-    __shared__ double s_hg[MK_KMAX / 32];
-    const int lane = tid & 31, warp = tid >> 5, K = p.K, xstride = K + 16;
-    constexpr int XPT = MMA_KMAX_PT;
-    float v[XPT];
-    float ss = 0.0f, am = 0.0f;
+    __shared__ double s_ss[MK_CWARPS];
+    __shared__ float s_am[MK_CWARPS];
+    __shared__ double s_hd[MK_KMAX / 128];
+    const int lane = tid & 31, warp = tid >> 5, K = p.K, xstride = K + 16, pro = p.pro, gs = p.gs;
+    const float *px = p.x, *px2 = p.x2, *pw = p.norm_w;
+    const float eps = p.eps;
+    constexpr int NG = MK_KMAX / (4 * MK_CTHREADS);   // groups of 2048 elements
+    const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    float4 v[NG], w[NG], v2[NG];
 #pragma unroll
-    for (int k = 0; k < XPT; k++) {
-        const int i = tid + k * MK_CTHREADS;
-        v[k] = 0.0f;
-        if (i < K) {
-            const float xv = lda(p.x + i);
-            if (p.pro == PRO_NORM) { ss = fmaf(xv, xv, ss); am = fmaxf(am, fabsf(xv * p.norm_w[i])); v[k] = xv; }
-            else if (p.pro == PRO_SWIGLU) { v[k] = silu_f(xv) * lda(p.x2 + i); am = fmaxf(am, fabsf(v[k])); }
-            else if (p.pro == PRO_GNORM) v[k] = xv;
-            else { v[k] = xv; am = fmaxf(am, fabsf(xv)); }
+    for (int r = 0; r < NG; r++) {
+        const int i = r * 4 * MK_CTHREADS + 4 * tid;
+        const bool in = i < K;
+        v[r] = in ? ldcg4(px + i) : z4;
+        w[r] = in && pro == PRO_NORM ? ld4(pw + i) : in && pro == PRO_GNORM ? ld4(pw + i % gs) : z4;
+        v2[r] = in && (pro == PRO_SWIGLU || pro == PRO_GNORM) ? ldcg4(px2 + i) : z4;
+    }
+    double ss = 0.0;
+    float am = 0.0f;
+#pragma unroll
+    for (int r = 0; r < NG; r++) {
+        if (r * 4 * MK_CTHREADS + 4 * tid >= K) continue;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float xv = f4(v[r], e);
+            if (pro == PRO_NORM) { ss += (double)xv * xv; am = fmaxf(am, fabsf(xv * f4(w[r], e))); }
+            else if (pro == PRO_SWIGLU) { const float y = silu_f(xv) * f4(v2[r], e); f4set(v[r], e, y); am = fmaxf(am, fabsf(y)); }
+            else if (pro != PRO_GNORM) am = fmaxf(am, fabsf(xv));
         }
     }
-    if (p.pro == PRO_GNORM) {
-        // o * (1/sqrt(mean_head(o^2) + eps)) * w[j] * silu(z), head sums in double
-        const int gs = p.gs;
-        double hd[XPT];
+    if (pro == PRO_GNORM) {
+        // o * (1/sqrt(mean_head(o^2) + eps)) * w[j] * silu(z): head sums (exact, in double) over the
+        // gs/4 lanes of a head, across warps through shared memory for heads wider than 128
+        double hd[NG];
 #pragma unroll
-        for (int k = 0; k < XPT; k++) {
-            const int i = tid + k * MK_CTHREADS;   // K is a multiple of 32: warp-uniform
-            double d = i < K ? (double)v[k] * v[k] : 0.0;
-            if (gs >= 32) {
-                d = warp_sum_d(d);
-                if (lane == 0 && i < K) s_hg[i >> 5] = d;
+        for (int r = 0; r < NG; r++) {
+            double d = 0.0;
+#pragma unroll
+            for (int e = 0; e < 4; e++) d += (double)f4(v[r], e) * f4(v[r], e);
+            if (gs <= 128) {
+                for (int o = gs >> 3; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
             } else {
-                for (int o = gs >> 1; o; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+                d = warp_sum_d(d);
+                const int i = r * 4 * MK_CTHREADS + 4 * tid;
+                if (lane == 0 && i < K) s_hd[i >> 7] = d;
             }
-            hd[k] = d;
+            hd[r] = d;
         }
-        if (gs >= 32) BarC::sync();
+        if (gs > 128) BarC::sync();
 #pragma unroll
-        for (int k = 0; k < XPT; k++) {
-            const int i = tid + k * MK_CTHREADS;
-            if (i < K) {
-                double so = hd[k];
-                if (gs >= 32) {
-                    so = 0.0;
-                    const int c0 = (i / gs) * (gs >> 5);
-                    for (int c = 0; c < (gs >> 5); c++) so += s_hg[c0 + c];
-                }
-                const float sc = 1.0f / sqrtf((float)(so / gs) + p.eps);
-                v[k] = v[k] * sc * p.norm_w[i % gs] * silu_f(lda(p.x2 + i));
-                am = fmaxf(am, fabsf(v[k]));
+        for (int r = 0; r < NG; r++) {
+            const int i = r * 4 * MK_CTHREADS + 4 * tid;
+            if (i >= K) continue;
+            double so = hd[r];
+            if (gs > 128) {
+                so = 0.0;
+                for (int c = 0; c < (gs >> 7); c++) so += s_hd[(i / gs) * (gs >> 7) + c];
+            }
+            const float sc = 1.0f / sqrtf((float)(so / gs) + eps);
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const float y = f4(v[r], e) * sc * f4(w[r], e) * silu_f(f4(v2[r], e));
+                f4set(v[r], e, y);
+                am = fmaxf(am, fabsf(y));
             }
         }
     }
-    ss = warp_sum(ss);
+    ss = warp_sum_d(ss);
     am = warp_max(am);
     if (lane == 0) { s_ss[warp] = ss; s_am[warp] = am; }
     BarC::sync();
-    double tss = 0;
-    float tam = 0.0f;
-    for (int w = 0; w < MK_CWARPS; w++) { tss += s_ss[w]; tam = fmaxf(tam, s_am[w]); }
-    const float nsc = p.pro == PRO_NORM ? 1.0f / sqrtf((float)(tss / K) + p.eps) : 1.0f;
+    double tss = lane < MK_CWARPS ? s_ss[lane] : 0.0;
+    float tam = lane < MK_CWARPS ? s_am[lane] : 0.0f;
+    tss = warp_sum_d(tss);
+    tam = warp_max(tam);
+    const float nsc = pro == PRO_NORM ? 1.0f / sqrtf((float)(tss / K) + eps) : 1.0f;
     const float m = tam * nsc;
     const float sc = ldexpf(1.0f, 14 - (m > 0.0f ? ilogbf(m) : 0));
 #pragma unroll
-    for (int k = 0; k < XPT; k++) {
-        const int i = tid + k * MK_CTHREADS;
+    for (int r = 0; r < NG; r++) {
+        const int i = r * 4 * MK_CTHREADS + 4 * tid;
+        if (r * 4 * MK_CTHREADS >= K) break;          // uniform: whole groups beyond K
+        float bs = 0.0f;
+        __half hi[4], lo[4];
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const float val = (pro == PRO_NORM ? (f4(v[r], e) * nsc) * f4(w[r], e) : f4(v[r], e)) * sc;
+            hi[e] = __float2half_rn(val);
+            lo[e] = __float2half_rn(val - __half2float(hi[e]));
+            bs += __half2float(hi[e]) + __half2float(lo[e]);
+        }
+        // block sums of the 32 elements of 8 consecutive lanes
+        bs += __shfl_xor_sync(0xffffffffu, bs, 1);
+        bs += __shfl_xor_sync(0xffffffffu, bs, 2);
+        bs += __shfl_xor_sync(0xffffffffu, bs, 4);
         if (i < K) {
-            const float val = (p.pro == PRO_NORM ? (v[k] * nsc) * p.norm_w[i] : v[k]) * sc;
-            const __half hi = __float2half_rn(val);
-            const __half lo = __float2half_rn(val - __half2float(hi));
-            const int pos = (i & ~15) + bperm(i & 15);
-            xs[pos] = hi;
-            xs[xstride + pos] = lo;
-            const float bs = warp_sum(__half2float(hi) + __half2float(lo));
-            if (lane == 0) xsum[i >> 5] = bs;
+            const int pos = (i & ~15) + bperm(i & 15);       // elements i, i+1 -> pos, pos+1; i+2, i+3 -> pos+4, pos+5
+            *reinterpret_cast<__half2 *>(xs + pos) = __halves2half2(hi[0], hi[1]);
+            *reinterpret_cast<__half2 *>(xs + pos + 4) = __halves2half2(hi[2], hi[3]);
+            *reinterpret_cast<__half2 *>(xs + xstride + pos) = __halves2half2(lo[0], lo[1]);
+            *reinterpret_cast<__half2 *>(xs + xstride + pos + 4) = __halves2half2(lo[2], lo[3]);
+            if ((lane & 7) == 0) xsum[i >> 5] = bs;
         }
     }
     BarC::sync();
     return sc;
 }
 
+// Global operands of a tile's epilogue, loaded when the tile starts so the load latency overlaps the
+// tile's tensor-core work (threads tid < 16, one output row each).
+struct EpiPre {
+    float y;          // EPI_ADD: current value of the output row
+    float cs[8];      // EPI_CONV: the channel's rolling state (kc - 1 values)
+    float wc[9];      // EPI_CONV: the channel's kc conv weights
+};
+
+XJ_DEV void mk_epi_load(const MmaJob &jb, int tile, int tid, EpiPre &e) {
+    const int row = tile * 16 + tid;
+    if (tid >= 16 || row >= jb.w.N) return;
+    if (jb.epi == EPI_ADD) e.y = __ldcg(jb.y + row);
+    else if (jb.epi == EPI_CONV) {
+        const int kc = jb.kc;
+        const float *st = jb.conv_state + (size_t)row * (kc - 1);
+        const float *wc = jb.conv_w + (size_t)row * kc;
+#pragma unroll
+        for (int k = 0; k < 8; k++) e.cs[k] = k < kc - 1 ? __ldcg(st + k) : 0.0f;
+#pragma unroll
+        for (int k = 0; k < 9; k++) e.wc[k] = k < kc ? wc[k] : 0.0f;
+    }
+}
+
+// Running greedy pick of one CTA over its LM-head tiles (warp 0): best value, runner-up, lowest index.
+struct ArgRun {
+    float b = -INFINITY, b2 = -INFINITY;
+    int bi = 0x7fffffff;
+};
+
 // Epilogue of one 16-row tile from the per-warp partials red[warp][16] (fixed-order sum over warps).
-XJ_DEV void mk_epilogue(const MmaJob &jb, int tile, const float *red, float tscale, int tid) {
+XJ_DEV void mk_epilogue(const MmaJob &jb, int tile, const float *red, float tscale, int tid, const EpiPre &e, ArgRun &ar) {
     const bool real = tile * 16 + (tid & 15) < jb.w.N;   // rows past N pad the last tile
     if (jb.epi == EPI_CONV) {
         if (tid < 16 && real) {
@@ -247,14 +368,19 @@ XJ_DEV void mk_epilogue(const MmaJob &jb, int tile, const float *red, float tsca
 #pragma unroll
             for (int w = 0; w < MK_CWARPS; w++) s += red[w * 16 + tid];
             s /= tscale;
-            float cs[8];
-            float *st = jb.conv_state + (size_t)ch * (kc - 1);
-            for (int k = 0; k < kc - 1; k++) cs[k] = __ldcg(st + k);
-            const float *wc = jb.conv_w + (size_t)ch * kc;
             float acc = 0.0f;
-            for (int k = 0; k < kc - 1; k++) acc = fmaf(cs[k], wc[k], acc);
-            acc = fmaf(s, wc[kc - 1], acc);
-            for (int k = 0; k < kc - 2; k++) st[k] = cs[k + 1];
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (k < kc - 1) acc = fmaf(e.cs[k], e.wc[k], acc);
+            float wl = e.wc[0];
+#pragma unroll
+            for (int k = 1; k < 9; k++)
+                if (k == kc - 1) wl = e.wc[k];
+            acc = fmaf(s, wl, acc);
+            float *st = jb.conv_state + (size_t)ch * (kc - 1);
+#pragma unroll
+            for (int k = 0; k < 7; k++)
+                if (k < kc - 2) st[k] = e.cs[k + 1];
             st[kc - 2] = s;
             jb.y[ch] = silu_f(acc);
         }
@@ -276,15 +402,16 @@ XJ_DEV void mk_epilogue(const MmaJob &jb, int tile, const float *red, float tsca
                 if (ov > b || (ov == b && oi < bi)) { b2 = fmaxf(b, ov2); b = ov; bi = oi; }
                 else b2 = fmaxf(b2, ov);
             }
-            if (tid == 0) { jb.pbest[tile] = b; jb.psecond[tile] = b2; jb.pidx[tile] = bi; }
+            // merge the tile into the CTA's running pick (same rule as argmax_final_dev)
+            if (b > ar.b || (b == ar.b && bi < ar.bi)) { ar.b2 = fmaxf(fmaxf(ar.b, ar.b2), b2); ar.b = b; ar.bi = bi; }
+            else ar.b2 = fmaxf(ar.b2, b);
         }
     } else if (tid < 16 && real) {
         float s = 0.0f;
 #pragma unroll
         for (int w = 0; w < MK_CWARPS; w++) s += red[w * 16 + tid];
         s /= tscale;
-        float *yp = jb.y + (size_t)tile * 16 + tid;
-        *yp = jb.epi == EPI_ADD ? __ldcg(yp) + s : s;
+        jb.y[(size_t)tile * 16 + tid] = jb.epi == EPI_ADD ? e.y + s : s;
     }
 }
 
@@ -310,9 +437,20 @@ XJ_DEV void mk_gdn_item(const GdnArgs &a, int item, float *scr, int tid) {
     const int j = r0 + tid / TPR, qq = tid % TPR;
     const bool act = tid < RPI * TPR;                                    // warp-uniform
     const float *x = a.qkv;
-    // L2 norms of q (threads 0..S-1) and k (threads 256..256+S-1), sums in double
+    // every global operand first (one memory round trip): q, k, the state row slice, v, gates
     const float qv = tid < S ? lda(x + hk * S + tid) : 0.0f;
     const float kv = (tid >= 256 && tid - 256 < S) ? lda(x + a.key_dim + hk * S + tid - 256) : 0.0f;
+    float *M = a.ssm + ((size_t)hv * S + (act ? j : 0)) * S + qq * P;
+    float row[P];
+#pragma unroll
+    for (int i = 0; i < P; i += 4) {
+        float4 v4 = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (act) v4 = __ldcg(reinterpret_cast<const float4 *>(M + i));
+        row[i] = v4.x; row[i + 1] = v4.y; row[i + 2] = v4.z; row[i + 3] = v4.w;
+    }
+    const float vj = act ? lda(x + 2 * a.key_dim + hv * S + j) : 0.0f;
+    const float bb = lda(a.beta + hv), al = lda(a.alpha + hv), dt = a.dt[hv], Ah = a.A[hv];
+    // L2 norms of q (threads 0..S-1) and k (threads 256..256+S-1), sums in double
     const double d = warp_sum_d(tid < 256 ? (double)qv * qv : (double)kv * kv);
     if (lane == 0) red[warp] = d;
     BarC::sync();
@@ -322,22 +460,15 @@ XJ_DEV void mk_gdn_item(const GdnArgs &a, int item, float *scr, int tid) {
     if (tid >= 256 && tid - 256 < S) ks[tid - 256] = kv * (1.0f / sqrtf((float)sk2 + a.eps));
     BarC::sync();
     if (act) {
-        float *M = a.ssm + ((size_t)hv * S + j) * S + qq * P;
-        float row[P];
-#pragma unroll
-        for (int i = 0; i < P; i += 4) {
-            const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(M + i));
-            row[i] = v4.x; row[i + 1] = v4.y; row[i + 2] = v4.z; row[i + 3] = v4.w;
-        }
-        const float b = sigm_f(lda(a.beta + hv));
-        const float g = softplus_f(lda(a.alpha + hv) + a.dt[hv]) * a.A[hv];
+        const float b = sigm_f(bb);
+        const float g = softplus_f(al + dt) * Ah;
         const float eg = expf(g);
         float sk = 0.0f;
 #pragma unroll
         for (int i = 0; i < P; i++) { row[i] *= eg; sk = fmaf(row[i], ks[qq * P + i], sk); }
 #pragma unroll
         for (int o = TPR >> 1; o; o >>= 1) sk += __shfl_xor_sync(0xffffffffu, sk, o);
-        const float delta = (lda(x + 2 * a.key_dim + hv * S + j) - sk) * b;
+        const float delta = (vj - sk) * b;
         float acc = 0.0f;
 #pragma unroll
         for (int i = 0; i < P; i++) { row[i] = fmaf(ks[qq * P + i], delta, row[i]); acc = fmaf(row[i], qs[qq * P + i], acc); }
@@ -359,54 +490,57 @@ template <> XJ_DEV float kv_round<__half>(float v) { return __half2float(__float
 // arithmetic of attn_prep_slot), the new K/V row stored at position npast by one item per KV head, and
 // online-softmax attention over positions [sp*n/nsplit, (sp+1)*n/nsplit) of n = npast + 1 (the new row
 // is taken from shared memory, rounded as the cache stores it). One split writes the gated output
-// directly; otherwise the last split of the head to finish merges all splits (core/xj_cpu.c:118-150).
+// directly; otherwise the last split of a head to finish merges all splits (core/xj_cpu.c:118-150).
+// Global operands are loaded in as few round trips as possible: all per-head vectors at once, then
+// the cache rows of MK_CWARPS * PB positions per batch.
 template <typename KV, int DPL>
 XJ_DEV void mk_attn_item(const AttnArgs &a, int h, int sp, int nsplit, float *apart, int *acnt, float *scr, int tid) {
+    constexpr int PB = DPL >= 8 ? 2 : 4;   // positions per warp per batch of loads
     __shared__ int s_last;
     const int D = a.D, group = a.H / a.Hkv, kvh = h / group, lane = tid & 31, warp = tid >> 5;
     float *nq = scr, *rq = scr + 256, *nk = scr + 512, *rk = scr + 768, *rv = scr + 1024;
     double *red = reinterpret_cast<double *>(scr + 1280);
     float *sm_m = scr + 1312, *sm_l = scr + 1328, *sm_o = scr + 1344;      // [16][256]
     const int pos = __ldcg(a.npast), n = pos + 1;
-    const float qv = tid < D ? lda(a.q + (size_t)h * 2 * D + tid) : 0.0f;
-    const float kv = (tid >= 256 && tid - 256 < D) ? lda(a.k + (size_t)kvh * D + tid - 256) : 0.0f;
-    const double d = warp_sum_d(tid < 256 ? (double)qv * qv : (double)kv * kv);
+    const bool isq = tid < 256;
+    const int i = isq ? tid : tid - 256;
+    const bool in = i < D;
+    const float *gate = a.q + (size_t)h * 2 * D + D;
+    const float xv = in ? lda(isq ? a.q + (size_t)h * 2 * D + i : a.k + (size_t)kvh * D + i) : 0.0f;
+    const float nw = in ? (isq ? a.qn[i] : a.kn[i]) : 0.0f;
+    const float vv = in && !isq ? lda(a.v + (size_t)kvh * D + i) : 0.0f;
+    const float gv = in && isq ? lda(gate + i) : 0.0f;
+    const double d = warp_sum_d((double)xv * xv);
     if (lane == 0) red[warp] = d;
     BarC::sync();
     double ssq = 0, ssk = 0;
     for (int w = 0; w < 8; w++) { ssq += red[w]; ssk += red[8 + w]; }
-    if (tid < D) nq[tid] = qv * (1.0f / sqrtf((float)(ssq / D) + a.eps)) * a.qn[tid];
-    if (tid >= 256 && tid - 256 < D) nk[tid - 256] = kv * (1.0f / sqrtf((float)(ssk / D) + a.eps)) * a.kn[tid - 256];
+    float *src = isq ? nq : nk;
+    if (in) src[i] = xv * (1.0f / sqrtf((float)((isq ? ssq : ssk) / D) + a.eps)) * nw;
     BarC::sync();
-    {
-        const bool isq = tid < 256;
-        const int i = isq ? tid : tid - 256;
-        if (i < D) {
-            const float *src = isq ? nq : nk;
-            float r = src[i];
-            const int half = a.n_rot / 2;
-            if (i < a.n_rot) {
-                const int p = i < half ? i : i - half;
-                const float theta = (float)pos * powf(a.base, -2.0f * (float)p / (float)a.n_rot);
-                const float c = cosf(theta), s = sinf(theta);
-                const float x0 = src[p], x1 = src[p + half];
-                r = i < half ? x0 * c - x1 * s : x0 * s + x1 * c;
-            }
-            if (isq) rq[i] = r;
-            else {
-                const float vv = lda(a.v + (size_t)kvh * D + i);
-                rk[i] = kv_round<KV>(r);
-                rv[i] = kv_round<KV>(vv);
-                if (sp == nsplit - 1 && h % group == 0) {
-                    const size_t o = (size_t)pos * a.Hkv * D + (size_t)kvh * D + i;
-                    store_kv<KV>((KV *)a.kc + o, r);
-                    store_kv<KV>((KV *)a.vc + o, vv);
-                }
+    if (in) {
+        float r = src[i];
+        const int half = a.n_rot / 2;
+        if (i < a.n_rot) {
+            const int p = i < half ? i : i - half;
+            const float theta = (float)pos * powf(a.base, -2.0f * (float)p / (float)a.n_rot);
+            const float c = cosf(theta), s = sinf(theta);
+            const float x0 = src[p], x1 = src[p + half];
+            r = i < half ? x0 * c - x1 * s : x0 * s + x1 * c;
+        }
+        if (isq) rq[i] = r;
+        else {
+            rk[i] = kv_round<KV>(r);
+            rv[i] = kv_round<KV>(vv);
+            if (sp == nsplit - 1 && h % group == 0) {
+                const size_t o = (size_t)pos * a.Hkv * D + (size_t)kvh * D + i;
+                store_kv<KV>((KV *)a.kc + o, r);
+                store_kv<KV>((KV *)a.vc + o, vv);
             }
         }
     }
     BarC::sync();
-    // online softmax over this split's positions, 16 warps interleaved
+    // online softmax over this split's positions: warp w takes j0 + w, j0 + w + 16, ... in order
     const int j0 = (int)((long long)sp * n / nsplit), j1 = (int)((long long)(sp + 1) * n / nsplit);
     const int kvd = a.Hkv * D;
     const float scale = 1.0f / sqrtf((float)D);
@@ -416,34 +550,41 @@ XJ_DEV void mk_attn_item(const AttnArgs &a, int h, int sp, int nsplit, float *ap
 #pragma unroll
     for (int e = 0; e < DPL; e++) { qr[e] = on ? rq[lane * DPL + e] : 0.0f; o[e] = 0.0f; }
     float m = -INFINITY, l = 0.0f;
-    for (int j = j0 + warp; j < j1; j += MK_CWARPS) {
-        float kr[DPL], vr[DPL];
-        if (j == pos) {
+    for (int jb = j0 + warp; jb < j1; jb += MK_CWARPS * PB) {
+        float kr[PB][DPL], vr[PB][DPL];
 #pragma unroll
-            for (int e = 0; e < DPL; e++) { kr[e] = on ? rk[lane * DPL + e] : 0.0f; vr[e] = on ? rv[lane * DPL + e] : 0.0f; }
-        } else {
-            const KV *kp = kc + (size_t)j * kvd + (size_t)kvh * D + lane * DPL;
-            const KV *vp = vc + (size_t)j * kvd + (size_t)kvh * D + lane * DPL;
+        for (int b = 0; b < PB; b++) {
+            const int j = jb + b * MK_CWARPS;
+            const bool fromsm = j == pos;
+            const bool ld = on && j < j1 && !fromsm;
+            const KV *kp = kc + (size_t)(ld ? j : 0) * kvd + (size_t)kvh * D + lane * DPL;
+            const KV *vp = vc + (size_t)(ld ? j : 0) * kvd + (size_t)kvh * D + lane * DPL;
 #pragma unroll
-            for (int e = 0; e < DPL; e++) { kr[e] = on ? load_kv(kp + e) : 0.0f; vr[e] = on ? load_kv(vp + e) : 0.0f; }
+            for (int e = 0; e < DPL; e++) {
+                kr[b][e] = ld ? load_kv(kp + e) : (on && fromsm ? rk[lane * DPL + e] : 0.0f);
+                vr[b][e] = ld ? load_kv(vp + e) : (on && fromsm ? rv[lane * DPL + e] : 0.0f);
+            }
         }
-        float s = 0.0f;
 #pragma unroll
-        for (int e = 0; e < DPL; e++) s = fmaf(qr[e], kr[e], s);
-        s = warp_sum(s) * scale;
-        const float mn = fmaxf(m, s);
-        const float corr = expf(m - mn), p = expf(s - mn);
-        l = l * corr + p;
+        for (int b = 0; b < PB; b++) {
+            if (jb + b * MK_CWARPS >= j1) break;
+            float s = 0.0f;
 #pragma unroll
-        for (int e = 0; e < DPL; e++) o[e] = fmaf(p, vr[e], o[e] * corr);
-        m = mn;
+            for (int e = 0; e < DPL; e++) s = fmaf(qr[e], kr[b][e], s);
+            s = warp_sum(s) * scale;
+            const float mn = fmaxf(m, s);
+            const float corr = expf(m - mn), p = expf(s - mn);
+            l = l * corr + p;
+#pragma unroll
+            for (int e = 0; e < DPL; e++) o[e] = fmaf(p, vr[b][e], o[e] * corr);
+            m = mn;
+        }
     }
     if (lane == 0) { sm_m[warp] = m; sm_l[warp] = l; }
 #pragma unroll
     for (int e = 0; e < DPL; e++) sm_o[warp * 256 + lane * DPL + e] = o[e];
     BarC::sync();
     float *part = apart + ((size_t)h * nsplit + sp) * (D + 2);
-    const float *gate = a.q + (size_t)h * 2 * D + D;
     if (tid < D) {
         float M = -INFINITY;
         for (int w = 0; w < MK_CWARPS; w++) M = fmaxf(M, sm_m[w]);
@@ -453,7 +594,7 @@ XJ_DEV void mk_attn_item(const AttnArgs &a, int h, int sp, int nsplit, float *ap
             L += sm_l[w] * c;
             acc = fmaf(sm_o[w * 256 + tid], c, acc);
         }
-        if (nsplit == 1) a.out[(size_t)h * D + tid] = (acc / L) * sigm_f(lda(gate + tid));
+        if (nsplit == 1) a.out[(size_t)h * D + tid] = (acc / L) * sigm_f(gv);
         else {
             part[tid] = acc;
             if (tid == 0) { part[D] = M; part[D + 1] = L; }
@@ -470,18 +611,21 @@ XJ_DEV void mk_attn_item(const AttnArgs &a, int h, int sp, int nsplit, float *ap
         BarC::sync();
         if (s_last) {
             __threadfence();
+            // all splits' partials into shared memory (one round trip), then the merge per dim
+            const float *p0 = apart + (size_t)h * nsplit * (D + 2);
+            const int np = nsplit * (D + 2);                  // <= MK_ATTN_SCR floats (host cap)
+            for (int q = tid; q < np; q += MK_CTHREADS) scr[q] = __ldcg(p0 + q);
+            BarC::sync();
             if (tid < D) {
-                const float *p0 = apart + (size_t)h * nsplit * (D + 2);
                 float M = -INFINITY;
-                for (int s = 0; s < nsplit; s++) M = fmaxf(M, __ldcg(p0 + (size_t)s * (D + 2) + D));
+                for (int s = 0; s < nsplit; s++) M = fmaxf(M, scr[s * (D + 2) + D]);
                 float L = 0.0f, acc = 0.0f;
                 for (int s = 0; s < nsplit; s++) {
-                    const float *ps = p0 + (size_t)s * (D + 2);
-                    const float c = expf(__ldcg(ps + D) - M);
-                    L += __ldcg(ps + D + 1) * c;
-                    acc = fmaf(__ldcg(ps + tid), c, acc);
+                    const float c = expf(scr[s * (D + 2) + D] - M);
+                    L += scr[s * (D + 2) + D + 1] * c;
+                    acc = fmaf(scr[s * (D + 2) + tid], c, acc);
                 }
-                a.out[(size_t)h * D + tid] = (acc / L) * sigm_f(lda(gate + tid));
+                a.out[(size_t)h * D + tid] = (acc / L) * sigm_f(gv);
             }
             if (tid == 0) atomicExch(acnt + h, 0);
         }
@@ -490,7 +634,7 @@ XJ_DEV void mk_attn_item(const AttnArgs &a, int h, int sp, int nsplit, float *ap
 }
 
 XJ_DEV int mk_nsplit(int n, int H, int max_split) {
-    int ns = (n + 31) / 32;
+    int ns = (n + 63) / 64;                    // one batch of loads per warp up to 64 positions a split
     if (ns > max_split) ns = max_split;
     return ns < 1 ? 1 : ns;
 }
@@ -521,6 +665,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[MK_NS], empty[MK_NS];
     __shared__ unsigned s_issued;
+    __shared__ MkPhase sph[2];     // consumers: this phase's descriptor and the next one (prefetched)
+    __shared__ MkStream sst[2];    // producer: same for its GEMV stream
     uint8_t *ring = smem;
     __half *xs = reinterpret_cast<__half *>(smem + (size_t)MK_NS * MK_SLOT);
     float *xsum = reinterpret_cast<float *>(smem + (size_t)MK_NS * MK_SLOT + MK_XS_BYTES);
@@ -539,44 +685,77 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
 
     if (warp == MK_CWARPS) {
         // ---------------- producer: this CTA's weight chunks of every GEMV phase, in program order
-        if (lane == 0) {
-            unsigned i = 0;
-            bool ok = true;
-            for (int step = 0; ok && step < A.nsteps; step++)
-                for (int ph = 0; ok && ph < A.nphase; ph++) {
-                    const MkPhase &p = A.prog[ph];
-                    if (p.op != MK_GEMV) continue;
-                    for (int tg = cta; ok && tg < p.ntiles; tg += G) {
-                        const int j = mk_job_of(p, tg);
-                        const Tiled &W = p.job[j].w;
-                        const int tile = tg - p.tile_start[j], CU = mk_cu(W.type);
-                        for (int u0 = 0; u0 < W.nu; u0 += CU, i++) {
+        copy_desc_async(&sst[0], &A.stream[0], (int)sizeof(MkStream), lane);
+        cp_async_wait_all();
+        __syncwarp();
+        unsigned i = 0;
+        int gk = 0;                 // GEMV phases streamed so far
+        bool ok = true;
+        for (int step = 0; ok && step < A.nsteps; step++)
+            for (int k = 0; ok && k < A.nstream; k++, gk++) {
+                const MkStream &S = sst[gk & 1];
+                const int kn = k + 1 < A.nstream ? k + 1 : 0;
+                copy_desc_async(&sst[(gk + 1) & 1], &A.stream[kn], (int)sizeof(MkStream), lane);
+                unsigned long long *trp = A.trace && step == A.nsteps - 1 ? A.trace + ((size_t)cta * A.nphase + S.ph) * 8 : nullptr;
+                if (lane < 6 && S.pf[lane]) {
+                    // this CTA's slice of the side-data range (16-byte granules)
+                    const unsigned bytes = S.pf_bytes[lane];
+                    const unsigned chunk = ((bytes + G - 1) / G + 15u) & ~15u, off = (unsigned)cta * chunk;
+                    if (off < bytes) prefetch_l2(S.pf[lane] + off, bytes - off < chunk ? bytes - off : chunk);
+                }
+                if (lane == 0) {
+                    for (int tg = cta; ok && tg < S.ntiles; tg += G) {
+                        int j = 0;
+                        while (j + 1 < S.njob && tg >= S.tile_start[j + 1]) j++;
+                        const int type = S.type[j], nu = S.nu[j];
+                        const int tile = tg - S.tile_start[j], CU = mk_cu(type);
+                        for (int u0 = 0; u0 < nu; u0 += CU, i++) {
                             const int slot = i % MK_NS;
-                            if (i >= MK_NS && !mk_wait(&empty[slot], ((i / MK_NS) - 1) & 1, A.err, 1)) { ok = false; break; }
+                            if (i >= MK_NS && !mk_wait(&empty[slot], ((i / MK_NS) - 1) & 1, A.err, 1, A.diag, step, k, (int)i, 128)) { ok = false; break; }
                             asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
-                            const int cu = W.nu - u0 < CU ? W.nu - u0 : CU;
+                            const int cu = nu - u0 < CU ? nu - u0 : CU;
                             uint8_t *st = ring + (size_t)slot * MK_SLOT;
-                            if (W.type == XJ_Q4_K) mk_issue_t<XJ_Q4_K>(W, tile, u0, cu, st, &full[slot]);
-                            else if (W.type == XJ_Q6_K) mk_issue_t<XJ_Q6_K>(W, tile, u0, cu, st, &full[slot]);
-                            else mk_issue_t<XJ_Q8_0>(W, tile, u0, cu, st, &full[slot]);
+                            if (type == XJ_Q4_K) mk_issue_t<XJ_Q4_K>(S, j, tile, u0, cu, st, &full[slot]);
+                            else if (type == XJ_Q6_K) mk_issue_t<XJ_Q6_K>(S, j, tile, u0, cu, st, &full[slot]);
+                            else mk_issue_t<XJ_Q8_0>(S, j, tile, u0, cu, st, &full[slot]);
                             *(volatile unsigned *)&s_issued = i + 1;
+                            if (trp) {
+                                const unsigned long long now = globaltimer();
+                                if (tg == cta && u0 == 0) trp[3] = now;
+                                trp[4] = now;
+                            }
                         }
                     }
                 }
-        }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                cp_async_wait_all();
+                __syncwarp();
+            }
+        cp_async_wait_all();
         __syncwarp();
     } else {
         // ---------------- consumers
         const int g = lane >> 2, c = lane & 3;
         float *scw = scs + warp * 128;
         unsigned nbar = 0;
-        int rb = 0;
+        int rb = 0, gp = 0;         // gp: phases run so far (selects the descriptor buffer)
+        copy_desc_async(&sph[0], &A.prog[0], (int)sizeof(MkPhase), tid);
+        cp_async_wait_all();
+        BarC::sync();
         for (int step = 0; step < A.nsteps; step++) {
             bool ok = true;
-            for (int ph = 0; ph < A.nphase; ph++) {
-                const MkPhase &p = A.prog[ph];
+            for (int ph = 0; ph < A.nphase; ph++, gp++) {
+                const MkPhase &p = sph[gp & 1];
+                const int pn = ph + 1 < A.nphase ? ph + 1 : 0;
+                copy_desc_async(&sph[(gp + 1) & 1], &A.prog[pn], (int)sizeof(MkPhase), tid);
+                const bool tr = A.trace && step == A.nsteps - 1 && tid == 0;
+                unsigned long long wait_ns = 0;
+                if (tr) A.trace[((size_t)cta * A.nphase + ph) * 8] = globaltimer();
                 if (p.op == MK_GEMV && cta < p.ntiles) {
+                    ArgRun ar;
                     const float tsc = mk_prologue(p, xs, xsum, tid);
+                    if (tr) A.trace[((size_t)cta * A.nphase + ph) * 8 + 5] = globaltimer();
+                    int ntile_done = 0;
                     const int xstride = p.K + 16;
                     const bool bcol = g < 2;
                     const __half *xb = xs + (size_t)g * xstride + 4 * c;
@@ -587,9 +766,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                         const Tiled &W = jb.w;
                         const int tile = tg - p.tile_start[j], CU = mk_cu(W.type);
                         float yg = 0.0f, yg8 = 0.0f;
+                        EpiPre e;
+                        mk_epi_load(jb, tile, tid, e);
                         for (int u0 = 0; u0 < W.nu; u0 += CU, consumed++) {
                             const int slot = consumed % MK_NS;
-                            const bool got = mk_wait(&full[slot], (consumed / MK_NS) & 1, A.err, 1);
+                            const unsigned long long w0 = tr ? globaltimer() : 0;
+                            const bool got = mk_wait(&full[slot], (consumed / MK_NS) & 1, A.err, 1, A.diag, step, ph, (int)consumed, 32);
+                            if (tr) wait_ns += globaltimer() - w0;
                             const uint8_t *st = ring + (size_t)slot * MK_SLOT;
                             const int cu = W.nu - u0 < CU ? W.nu - u0 : CU;
                             if (W.type == XJ_Q4_K) {
@@ -612,8 +795,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                         float *rr = red + rb * (MK_CWARPS * 16);
                         if (c == 0) { rr[warp * 16 + g] = yg; rr[warp * 16 + g + 8] = yg8; }
                         BarC::sync();
-                        mk_epilogue(jb, tile, rr, tsc, tid);
+                        mk_epilogue(jb, tile, rr, tsc, tid, e, ar);
                         rb ^= 1;
+                        if (tr && ntile_done == 0) A.trace[((size_t)cta * A.nphase + ph) * 8 + 6] = globaltimer();
+                        ntile_done++;
+                    }
+                    if (tr) A.trace[((size_t)cta * A.nphase + ph) * 8 + 7] = ntile_done;
+                    if (tid == 0 && p.job[0].epi == EPI_ARGMAX) {
+                        // one greedy-pick partial per CTA (CTA c holds tiles c, c + G, ...)
+                        p.job[0].pbest[cta] = ar.b; p.job[0].psecond[cta] = ar.b2; p.job[0].pidx[cta] = ar.bi;
                     }
                 } else if (p.op == MK_GDN) {
                     switch (p.gs) {
@@ -630,12 +820,18 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                 } else if (p.op == MK_ARGMAX) {
                     if (cta == 0) argmax_final_dev<BarC>(p.am, tid, MK_CTHREADS);
                 }
+                if (tr) {
+                    A.trace[((size_t)cta * A.nphase + ph) * 8 + 1] = globaltimer();
+                    A.trace[((size_t)cta * A.nphase + ph) * 8 + 2] = wait_ns;
+                }
+                cp_async_wait_all();   // the next descriptor has landed (visible after the barrier below)
                 if (step == A.nsteps - 1 && ph == A.nphase - 1) break;
                 nbar++;
-                if (!mk_grid_sync(A.bar, nbar * (unsigned)G, A.err, tid)) { ok = false; break; }
+                if (!mk_grid_sync(A.bar, nbar * (unsigned)G, A.err, tid, A.diag, step, ph)) { ok = false; break; }
             }
             if (!ok) break;
         }
+        cp_async_wait_all();
     }
     __syncthreads();
     // chunks requested but never consumed (only after an error): let their copies land before exiting

@@ -30,6 +30,7 @@ namespace {
 int g_opt_kv_f32 = 0;
 int g_opt_gemv = 0;
 int g_opt_persist = 1;
+int g_opt_trace = 0;
 
 void seterr(char *err, size_t errlen, const char *fmt, ...) {
     if (!err || !errlen) return;
@@ -86,8 +87,12 @@ struct Impl {
     // persistent decode kernel: phase program (device), barrier counter, attention split scratch
     int mk_state = 0;          // 0: not built, 1: built, -1: this stage cannot use it
     MkPhase *mk_prog = nullptr;
-    int mk_nphase = 0, mk_ctas = 0, mk_max_split = 1;
+    MkStream *mk_stream = nullptr;
+    int mk_nphase = 0, mk_nstream = 0, mk_ctas = 0, mk_max_split = 1;
+    unsigned long long *mk_trace = nullptr;   // per CTA and phase: start, end (last step of a traced launch)
+    std::vector<int> mk_ops;
     unsigned *mk_bar = nullptr;
+    int *mk_diag = nullptr;
     float *mk_apart = nullptr;
     int *mk_acnt = nullptr;
     long long nlaunch = 0;                   // kernels launched on the stage stream so far
@@ -661,9 +666,10 @@ void decode_step(xj_stage *s) {
 // The phase program of one decode step: the same layer sequence as decode_step (run_layers at T = 1,
 // then the head with the fused greedy pick), expressed for k_decode_persistent. Returns false when a
 // matrix is not in the tiled layout (the persistent kernel has only the tensor-core GEMV).
-bool mk_gemv(std::vector<MkPhase> &prog, int K, int pro, const float *x, const float *x2, const float *norm_w,
-             float eps, int gs, std::initializer_list<Job> jobs) {
+bool mk_gemv(std::vector<MkPhase> &prog, std::vector<MkStream> &stream, int K, int pro, const float *x,
+             const float *x2, const float *norm_w, float eps, int gs, std::initializer_list<Job> jobs) {
     MkPhase p{};
+    MkStream ms{};
     p.op = MK_GEMV; p.K = K; p.pro = pro; p.x = x; p.x2 = x2; p.norm_w = norm_w; p.eps = eps; p.gs = gs;
     if (K > MK_KMAX || K % 32) return false;
     p.tile_start[0] = 0;
@@ -673,11 +679,16 @@ bool mk_gemv(std::vector<MkPhase> &prog, int K, int pro, const float *x, const f
         mj.w = tiled_of(f.w); mj.y = f.y; mj.ldy = f.ldy; mj.epi = f.epi;
         mj.conv_state = f.conv_state; mj.conv_w = f.conv_w; mj.conv_ck = nullptr; mj.kc = f.kc;
         mj.pbest = f.pbest; mj.psecond = f.psecond; mj.pidx = f.pidx;
+        ms.type[p.njob] = mj.w.type; ms.nu[p.njob] = mj.w.nu;
+        ms.q[p.njob] = mj.w.q; ms.h[p.njob] = mj.w.h; ms.s[p.njob] = mj.w.s; ms.d[p.njob] = mj.w.d;
         p.tile_start[p.njob + 1] = p.tile_start[p.njob] + (f.w.N + 15) / 16;
         p.njob++;
     }
     p.ntiles = p.tile_start[p.njob];
+    ms.ntiles = p.ntiles; ms.njob = p.njob; ms.ph = (int)prog.size();
+    for (int j = 0; j < 5; j++) ms.tile_start[j] = p.tile_start[j];
     prog.push_back(p);
+    stream.push_back(ms);
     return true;
 }
 
@@ -689,6 +700,7 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
     const int E = hp->n_embd, FF = hp->n_ff;
     const float eps = hp->eps;
     std::vector<MkPhase> prog;
+    std::vector<MkStream> stream;
     bool ok = hp->s_k == hp->s_v && hp->head_dim <= 256 && hp->n_head % hp->n_head_kv == 0;
     for (int il = s->l0; ok && il < s->l1; il++) {
         Layer &Ly = im->L[il - s->l0];
@@ -696,23 +708,23 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
             const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v;
             Job qkv{Ly.qkv, im->qkvb, CD};
             qkv.epi = EPI_CONV; qkv.conv_state = Ly.conv; qkv.conv_w = Ly.conv_w; qkv.kc = hp->conv_k;
-            ok = ok && mk_gemv(prog, E, PRO_NORM, im->x, nullptr, Ly.attn_norm, eps, 0,
+            ok = ok && mk_gemv(prog, stream, E, PRO_NORM, im->x, nullptr, Ly.attn_norm, eps, 0,
                                {qkv, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
             MkPhase g{};
             g.op = MK_GDN; g.gdn = gdn_args(im, hp, Ly, 1, false); g.gs = hp->s_k;
             prog.push_back(g);
             Job out{Ly.out, im->x, E};
             out.epi = EPI_ADD;
-            ok = ok && mk_gemv(prog, DI, PRO_GNORM, im->o, im->z, Ly.ssm_norm, eps, hp->s_k, {out});
+            ok = ok && mk_gemv(prog, stream, DI, PRO_GNORM, im->o, im->z, Ly.ssm_norm, eps, hp->s_k, {out});
         } else {
             const int H = hp->n_head, Hkv = hp->n_head_kv, D = hp->head_dim, nq = 2 * H * D, nk = Hkv * D;
             const float *q, *k, *v;
             long long ldq, ldkv;
             if (Ly.fused) {
-                ok = ok && mk_gemv(prog, E, PRO_NORM, im->x, nullptr, Ly.attn_norm, eps, 0, {{Ly.wqkv, im->qkvb, nq + 2 * nk}});
+                ok = ok && mk_gemv(prog, stream, E, PRO_NORM, im->x, nullptr, Ly.attn_norm, eps, 0, {{Ly.wqkv, im->qkvb, nq + 2 * nk}});
                 q = im->qkvb; k = im->qkvb + nq; v = im->qkvb + nq + nk; ldq = ldkv = nq + 2 * nk;
             } else {
-                ok = ok && mk_gemv(prog, E, PRO_NORM, im->x, nullptr, Ly.attn_norm, eps, 0,
+                ok = ok && mk_gemv(prog, stream, E, PRO_NORM, im->x, nullptr, Ly.attn_norm, eps, 0,
                                    {{Ly.wq, im->q, nq}, {Ly.wk, im->k, nk}, {Ly.wv, im->v, nk}});
                 q = im->q; k = im->k; v = im->v; ldq = nq; ldkv = nk;
             }
@@ -721,20 +733,47 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
             prog.push_back(a);
             Job o{Ly.wo, im->x, E};
             o.epi = EPI_ADD;
-            ok = ok && mk_gemv(prog, H * D, PRO_NONE, im->o, nullptr, nullptr, eps, 0, {o});
+            ok = ok && mk_gemv(prog, stream, H * D, PRO_NONE, im->o, nullptr, nullptr, eps, 0, {o});
         }
-        ok = ok && mk_gemv(prog, E, PRO_NORM, im->x, nullptr, Ly.post_norm, eps, 0, {{Ly.ffn_gate, im->g, FF}, {Ly.ffn_up, im->u, FF}});
+        ok = ok && mk_gemv(prog, stream, E, PRO_NORM, im->x, nullptr, Ly.post_norm, eps, 0, {{Ly.ffn_gate, im->g, FF}, {Ly.ffn_up, im->u, FF}});
         Job down{Ly.ffn_down, im->x, E};
         down.epi = EPI_ADD;
-        ok = ok && mk_gemv(prog, FF, PRO_SWIGLU, im->g, im->u, nullptr, eps, 0, {down});
+        ok = ok && mk_gemv(prog, stream, FF, PRO_SWIGLU, im->g, im->u, nullptr, eps, 0, {down});
     }
     Job h{im->output, nullptr, im->output.N};
     h.epi = EPI_ARGMAX; h.pbest = im->pbest; h.psecond = im->psecond; h.pidx = im->pidx;
-    ok = ok && mk_gemv(prog, E, PRO_NORM, im->x, nullptr, im->output_norm, eps, 0, {h});
+    ok = ok && mk_gemv(prog, stream, E, PRO_NORM, im->x, nullptr, im->output_norm, eps, 0, {h});
     if (!ok) { im->mk_state = -1; seterr(err, errlen, "persistent decode needs every matrix in the tiled layout"); return -1; }
     MkPhase am{};
     am.op = MK_ARGMAX; am.am = argmax_args(im);
     prog.push_back(am);
+    // side data each GEMV phase (and the GDN / attention phase after it) reads, for the producer's
+    // L2 prefetch
+    for (MkStream &ms : stream) {
+        int n = 0;
+        auto add = [&](const void *ptr, size_t bytes) {
+            if (ptr && bytes >= 16 && n < 6) { ms.pf[n] = (const uint8_t *)ptr; ms.pf_bytes[n] = (unsigned)(bytes & ~(size_t)15); n++; }
+        };
+        const MkPhase &g = prog[ms.ph];
+        if (g.pro == PRO_NORM) add(g.norm_w, (size_t)g.K * 4);
+        if (g.pro == PRO_GNORM) add(g.norm_w, (size_t)g.gs * 4);
+        for (int j = 0; j < g.njob; j++)
+            if (g.job[j].epi == EPI_CONV) {
+                add(g.job[j].conv_w, (size_t)g.job[j].w.N * g.job[j].kc * 4);
+                add(g.job[j].conv_state, (size_t)g.job[j].w.N * (g.job[j].kc - 1) * 4);
+            }
+        if (ms.ph + 1 < (int)prog.size() && prog[ms.ph + 1].op == MK_GDN) {
+            const GdnArgs &d = prog[ms.ph + 1].gdn;
+            add(d.ssm, (size_t)d.Hv * hp->s_k * hp->s_k * 4);
+            add(d.dt, (size_t)d.Hv * 4);
+            add(d.A, (size_t)d.Hv * 4);
+        }
+        if (ms.ph + 1 < (int)prog.size() && prog[ms.ph + 1].op == MK_ATTN) {
+            const AttnArgs &t = prog[ms.ph + 1].attn;
+            add(t.qn, (size_t)t.D * 4);
+            add(t.kn, (size_t)t.D * 4);
+        }
+    }
 
     // one CTA per SM, all resident (cooperative launch)
     int sms = 0, per_sm = 0, coop = 0;
@@ -744,12 +783,27 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent, MK_THREADS, MK_SMEM));
     if (!coop || per_sm < 1) { im->mk_state = -1; seterr(err, errlen, "cooperative launch of the persistent decode kernel is not possible"); return -1; }
     im->mk_ctas = sms;
-    im->mk_max_split = sms / hp->n_head > 0 ? sms / hp->n_head : 1;
-    if (dalloc(im, &im->mk_prog, prog.size(), err, errlen) || dalloc(im, &im->mk_bar, 4, err, errlen) ||
-        dalloc(im, &im->mk_acnt, (size_t)hp->n_head, err, errlen) ||
-        dalloc(im, &im->mk_apart, (size_t)hp->n_head * im->mk_max_split * (hp->head_dim + 2), err, errlen)) return -1;
+    // the head phase leaves one greedy-pick partial per CTA that holds LM-head tiles
+    prog.back().am.ntiles = prog[prog.size() - 2].ntiles < sms ? prog[prog.size() - 2].ntiles : sms;
+    // splits per head: at most one work item per CTA, and the merge fits the attention scratch
+    int ms = sms / hp->n_head;
+    if (ms > MK_ATTN_SCR / (hp->head_dim + 2)) ms = MK_ATTN_SCR / (hp->head_dim + 2);
+    im->mk_max_split = ms > 0 ? ms : 1;
+    // the program's size is fixed for a stage: a rebuild (after the output buffers moved) reuses these
+    if (!im->mk_prog &&
+        (dalloc(im, &im->mk_prog, prog.size(), err, errlen) || dalloc(im, &im->mk_stream, stream.size(), err, errlen) ||
+         dalloc(im, &im->mk_trace, (size_t)sms * prog.size() * 8, err, errlen) || dalloc(im, &im->mk_bar, 4, err, errlen) ||
+         dalloc(im, &im->mk_diag, 8, err, errlen) || dalloc(im, &im->mk_acnt, (size_t)hp->n_head, err, errlen) ||
+         dalloc(im, &im->mk_apart, (size_t)hp->n_head * im->mk_max_split * (hp->head_dim + 2), err, errlen))) return -1;
     CK(cudaMemcpy(im->mk_prog, prog.data(), prog.size() * sizeof(MkPhase), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(im->mk_stream, stream.data(), stream.size() * sizeof(MkStream), cudaMemcpyHostToDevice));
+    // a pageable host-to-device cudaMemcpy may return before its DMA lands, and the stage stream does
+    // not wait for the legacy stream: the program must be complete before the kernel reads it
+    CK(cudaDeviceSynchronize());
     im->mk_nphase = (int)prog.size();
+    im->mk_nstream = (int)stream.size();
+    im->mk_ops.clear();
+    for (const MkPhase &q : prog) im->mk_ops.push_back(q.op);
     im->mk_state = 1;
     return 1;
 }
@@ -758,10 +812,13 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
 int mk_launch(xj_stage *s, int n, char *err, size_t errlen) {
     Impl *im = I(s);
     MkArgs a{};
-    a.prog = im->mk_prog; a.nphase = im->mk_nphase; a.nsteps = n;
+    a.prog = im->mk_prog; a.stream = im->mk_stream; a.nphase = im->mk_nphase; a.nstream = im->mk_nstream;
+    a.nsteps = n;
+    a.trace = g_opt_trace ? im->mk_trace : nullptr;
     a.bar = im->mk_bar; a.err = im->derr; a.apart = im->mk_apart; a.acnt = im->mk_acnt;
-    a.max_split = im->mk_max_split; a.kv_f32 = im->kv_f32 ? 1 : 0;
+    a.max_split = im->mk_max_split; a.kv_f32 = im->kv_f32 ? 1 : 0; a.diag = im->mk_diag;
     CK(cudaMemsetAsync(im->mk_bar, 0, sizeof(unsigned), im->st));
+    CK(cudaMemsetAsync(im->mk_diag, 0, sizeof(int) * 8, im->st));
     CK(cudaMemsetAsync(im->mk_acnt, 0, sizeof(int) * (size_t)s->m->hp.n_head, im->st));
     void *args[] = {&a};
     CK(cudaLaunchCooperativeKernel((const void *)k_decode_persistent, dim3(im->mk_ctas), dim3(MK_THREADS), args, MK_SMEM, im->st));
@@ -787,6 +844,7 @@ int xj_cuda_set_options(int which, int value) {
     case XJC_OPT_GEMV: g_opt_gemv = value; return 0;
     case XJC_OPT_PDL: g_pdl = value ? 1 : 0; return 0;
     case XJC_OPT_PERSIST: g_opt_persist = value; return 0;
+    case XJC_OPT_TRACE: g_opt_trace = value; return 0;
     default: return -1;
     }
 }
@@ -839,10 +897,14 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
     }
     if (n_prompt <= 0 || n_gen <= 0) { seterr(err, errlen, "need at least one prompt token and one generated token"); return -1; }
     if (s->n_past + n_prompt + n_gen - 1 > s->n_ctx) { seterr(err, errlen, "context is full (%d)", s->n_ctx); return -1; }
-    if (!im->tok_embd.p && upload(im, m->tok_embd, &im->tok_embd, err, errlen, true)) return -1;
+    if (!im->tok_embd.p) {
+        if (upload(im, m->tok_embd, &im->tok_embd, err, errlen, true)) return -1;
+        CK(cudaDeviceSynchronize());   // the upload's DMA must land before the stage stream reads it
+    }
     if (n_gen > im->out_cap) {
-        // the step graph writes through these pointers, so it is rebuilt after a reallocation
+        // the step graph and the persistent kernel's program write through these pointers: rebuild them
         if (im->step_graph) { cudaGraphExecDestroy(im->step_graph); im->step_graph = nullptr; }
+        if (im->mk_state == 1) im->mk_state = 0;
         const int cap = n_gen > 4096 ? n_gen : 4096;
         if (dalloc(im, &im->out_tok, (size_t)cap, err, errlen) || dalloc(im, &im->margin, (size_t)cap, err, errlen)) return -1;
         im->out_cap = cap;
@@ -890,7 +952,16 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
     CK(cudaEventRecord(im->ev[2], im->st));
     CK(cudaMemcpyAsync(out, im->out_tok, sizeof(int32_t) * n_gen, cudaMemcpyDeviceToHost, im->st));
     if (margins) CK(cudaMemcpyAsync(margins, im->margin, sizeof(float) * n_gen, cudaMemcpyDeviceToHost, im->st));
-    if (sync_check(im, err, errlen)) return -1;
+    if (sync_check(im, err, errlen)) {
+        int d[8] = {0};
+        if (persist && im->mk_diag && cudaMemcpy(d, im->mk_diag, sizeof d, cudaMemcpyDeviceToHost) == cudaSuccess && d[0]) {
+            const size_t n = strlen(err);
+            snprintf(err + n, errlen > n ? errlen - n : 0,
+                     " [persistent kernel: wait kind %d, cta %d, thread %d, step %d, phase %d, index %d, extra %d]",
+                     d[0], d[1], d[2], d[3], d[4], d[5], d[6]);
+        }
+        return -1;
+    }
     if (gpu_ms) {
         cudaEventElapsedTime(&gpu_ms[0], im->ev[0], im->ev[1]);
         cudaEventElapsedTime(&gpu_ms[1], im->ev[1], im->ev[2]);
@@ -931,7 +1002,8 @@ static int gemv_diag(int type, const void *w, int k, int n, const float *x, int 
     if (dalloc(im, &dx, (size_t)t * k, err, errlen) || dalloc(im, &dy, (size_t)t * n, err, errlen) ||
         dalloc(im, &im->hn, (size_t)t * k, err, errlen) || dalloc(im, &im->derr, 1, err, errlen)) goto done;
     cudaMemset(im->derr, 0, sizeof(int));
-    if (cudaMemcpy(dx, x, sizeof(float) * (size_t)t * k, cudaMemcpyHostToDevice) != cudaSuccess) { seterr(err, errlen, "copy failed"); goto done; }
+    if (cudaMemcpy(dx, x, sizeof(float) * (size_t)t * k, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaDeviceSynchronize() != cudaSuccess) { seterr(err, errlen, "copy failed"); goto done; }
     gemv(im, dx, nullptr, k, t, PRO_NONE, nullptr, 0.0f, {{mats[0], dy, n}});
     if (ms) {
         cudaEvent_t e0, e1;
@@ -971,6 +1043,42 @@ int xj_cuda_gemv_time(int type, const void *w, int k, int n, int t, int copies, 
 int xj_cuda_graph_kernels(const xj_stage *s) {
     const Impl *im = (const Impl *)s->impl;
     return im ? im->step_kernels : 0;
+}
+
+int xj_cuda_phase_trace(const xj_stage *s, double *out, int cap) {
+    Impl *im = (Impl *)s->impl;
+    if (!im || im->mk_state != 1 || !g_opt_trace) return -1;
+    DevGuard dg(im->dev);
+    const int np = im->mk_nphase, G = im->mk_ctas;
+    std::vector<unsigned long long> t((size_t)G * np * 8);
+    if (cudaMemcpy(t.data(), im->mk_trace, t.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
+    for (int ph = 0; ph < np && ph < cap; ph++) {
+        unsigned long long s0 = ~0ull, e1 = 0;
+        double wmax = 0, wsum = 0, wait = 0, lead = 0, pro = 0, first = 0;
+        int nlead = 0, ntl = 0;
+        for (int c = 0; c < G; c++) {
+            const unsigned long long *r = &t[((size_t)c * np + ph) * 8];
+            if (r[7]) { pro += ((double)r[5] - (double)r[0]) * 1e-3; first += ((double)r[6] - (double)r[5]) * 1e-3; ntl++; }
+            if (r[0] < s0) s0 = r[0];
+            if (r[1] > e1) e1 = r[1];
+            const double w = r[1] > r[0] ? (double)(r[1] - r[0]) * 1e-3 : 0.0;
+            wsum += w;
+            if (w > wmax) wmax = w;
+            wait += (double)r[2] * 1e-3;
+            if (r[3]) { lead += ((double)r[0] - (double)r[3]) * 1e-3; nlead++; }
+        }
+        double *o = out + (size_t)ph * 9;
+        o[0] = im->mk_ops[ph];
+        o[1] = wmax;
+        o[2] = wsum / G;
+        o[3] = e1 > s0 ? (double)(e1 - s0) * 1e-3 : 0.0;
+        o[4] = (double)s0 * 1e-3;
+        o[5] = wait / G;
+        o[6] = nlead ? lead / nlead : 0.0;
+        o[7] = ntl ? pro / ntl : 0.0;
+        o[8] = ntl ? first / ntl : 0.0;
+    }
+    return np;
 }
 
 long long xj_cuda_last_decode_launches(const xj_stage *s, long long *launches) {

@@ -19,7 +19,7 @@ LIB = HERE / "csrc" / "libxj_cuda.so"
 _lib = None
 
 F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 8, 12, 13, 14, 30
-OPT_KV_F32, OPT_GEMV, OPT_PDL, OPT_PERSIST = 1, 2, 3, 4
+OPT_KV_F32, OPT_GEMV, OPT_PDL, OPT_PERSIST, OPT_TRACE = 1, 2, 3, 4, 5
 
 
 class XjError(RuntimeError):
@@ -99,6 +99,7 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_dequant_rows": (ip, [ip, vp, ip, ip, vp, cp, sz]),
         "xj_cuda_graph_kernels": (ip, [vp]),
         "xj_cuda_last_decode_launches": (ctypes.c_longlong, [vp, vp]),
+        "xj_cuda_phase_trace": (ip, [vp, vp, ip]),
         "xj_cuda_gemv": (ip, [ip, vp, ip, ip, vp, ip, vp, ip, cp, sz]),
         "xj_cuda_gemv_time": (ip, [ip, vp, ip, ip, ip, ip, ip, ip, vp, cp, sz]),
         "xj_cuda_norm_gemv_noalloc": (ip, [ip, vp, ip, ip, vp, vp, ctypes.c_float, ip, vp, cp, sz]),
@@ -280,6 +281,16 @@ class Stage:
         v = (ctypes.c_longlong * 2)()
         lib().xj_cuda_last_decode_launches(self.addr, v)
         return int(v[0]), int(v[1])
+
+    def phase_trace(self):
+        """Per-phase timing of the last traced persistent decode (OPT_TRACE): array [phases, 5] of
+        kind, max CTA us, mean CTA us, span us, start us, mean weight wait us, mean request lead us,
+        mean prologue us, mean first-tile us."""
+        out = np.zeros((4096, 9), np.float64)
+        n = lib().xj_cuda_phase_trace(self.addr, out.ctypes.data, 4096)
+        if n < 0:
+            raise XjError("no phase trace (enable OPT_TRACE before decode)")
+        return out[:n]
 
     def close(self):
         if self.p:

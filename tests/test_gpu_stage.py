@@ -91,6 +91,7 @@ def test_greedy_tokens_identical_device_decode(xc, golden, tiny_path, config0_pa
     """xj_cuda_decode against the reference's greedy tokens, through the per-step graph (persist=0) and
     the persistent kernel (persist=1; the tiny model's F32 matrices keep it on the graph path)."""
     xc.set_option(xc.OPT_KV_F32, 0)
+    xc.set_option(xc.OPT_GEMV, 0)
     xc.set_option(xc.OPT_PERSIST, persist)
     m = xc.Model(model_path(which, tiny_path, config0_path, mid_path))
     s = xc.Stage(m, 0, m.n_layer, 512, 8)
@@ -117,6 +118,7 @@ def test_persistent_decode_kv_f32_and_continuation(xc, golden, config0_path, mid
     """The persistent kernel with the fp32 KV cache, and a decode split into two calls (the second call
     continues from the first one's position and state) against the reference's tokens."""
     xc.set_option(xc.OPT_PERSIST, 1)
+    xc.set_option(xc.OPT_GEMV, 0)
     xc.set_option(xc.OPT_KV_F32, 1)
     m = xc.Model(model_path(which, None, config0_path, mid_path))
     s = xc.Stage(m, 0, m.n_layer, 512, 8)
@@ -134,6 +136,8 @@ def test_persistent_matches_graph_path_long_context(xc, mid_path):
     """Long run (attention over up to ~1000 positions, split across CTAs) through both CUDA paths: the
     ids agree until the first step whose top-2 gap is a near tie (the two paths sum GDN and attention
     in different orders)."""
+    xc.set_option(xc.OPT_GEMV, 0)
+    xc.set_option(xc.OPT_KV_F32, 0)
     m = xc.Model(mid_path)
     p = np.random.default_rng(5).integers(0, m.n_vocab, 700).astype(np.int32)
     out = {}
