@@ -28,6 +28,9 @@ import numpy as np
 
 ROOT = pathlib.Path(__file__).resolve().parent
 PEAKS = ROOT / "MEASURED_PEAKS.json"
+# DRAM bytes (read + write) per decode step of k_decode_persistent on this workload, from an ncu capture
+# of a 3-step launch (profiles/k_decode_persistent_config3.md); a launch of n steps moves n times this.
+TRAFFIC_PER_STEP = 1.2557e9
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "decode tok/s at batch 1 & 64 (Qwen3.5-style Q4_K_M); GEMV HBM GB/s vs 8 TB/s"
 
@@ -213,6 +216,8 @@ def main():
     barrier()
     clk = clocks.stop()
     dev_ms = float(ms[0] + ms[1])
+    kern_ms = float(ms[1])                     # the decode steps after the 1-token prompt (one launch)
+    launches = stage.last_decode_launches()
     last = toks[-1:]
     # end to end through the public C ABI with host buffers (token ids in, ids out), host wall clock
     barrier()
@@ -229,25 +234,31 @@ def main():
         t_max, e2e_max = float(t[0]), float(t[1])
     value = world * args.steps / (t_max / 1e3)
     e2e = world * args.steps / (e2e_max / 1e3)
-    launches = sum(stage.last_decode_launches())   # of the timed call: its 1-token prompt + the steps
     if rank == 0:
         peak, peak_kind = hbm_peak()
         b = step_bytes(cfg, pos0 + args.steps // 2)
-        achieved = b["total"] / (t_max / args.steps / 1e3) / 1e9
+        n_kern = args.steps - 1
+        persistent = launches[1] == 1
+        achieved = b["total"] * n_kern / (kern_ms / 1e3) / 1e9
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(t_max / args.steps, 4), "higher_is_better": True,
             "scaling": "weak", "vs_baseline": None, "dtype": "q4_k/q6_k weights, f32 accumulate", "data": "synthetic",
             "config": {"workload": f"{cfg.name} greedy decode, batch 1 per GPU", "prompt": args.prompt,
                        "batch_per_gpu": 1, "kv_cache": "f16", "parallelism": f"batch-shard x{world}",
+                       "decode_kernel": "persistent" if launches[1] == 1 else "graph",
                        "l2": "weights 1.2 GB per step > 126 MB L2"},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": round(4 / args.steps, 3),
                     "d2h_bytes_per_step": 4},
-            "roofline": {"bound": "hbm", "kernel": "whole decode step", "achieved": round(achieved, 1),
-                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
-                         "bytes_per_step": round(b["total"]), "peak_kind": peak_kind},
+            "roofline": {"bound": "hbm",
+                         "kernel": "k_decode_persistent" if persistent else "decode-step CUDA graph",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4),
+                         "traffic": round(TRAFFIC_PER_STEP * n_kern) if persistent else None,
+                         "algorithmic_bytes": round(b["total"] * n_kern), "units": f"{n_kern} decode steps",
+                         "launch_ms": round(kern_ms, 4), "peak_kind": peak_kind},
             "clocks": clk,
-            "gpu_launches": launches,
+            "gpu_launches": int(sum(launches)),
             "tokens_check": int(toks[0]),
         }
         if world == 1 and not args.no_cpu_baseline:

@@ -331,10 +331,11 @@ XJ_DEV float mk_prologue(const MkPhase &p, __half *xs, float *xsum, int tid) {
 
 // Global operands of a tile's epilogue, loaded when the tile starts so the load latency overlaps the
 // tile's tensor-core work (threads tid < 16, one output row each).
+constexpr int MK_KC = 4;   // longest causal conv the persistent kernel takes (the models' conv_k)
 struct EpiPre {
-    float y;          // EPI_ADD: current value of the output row
-    float cs[8];      // EPI_CONV: the channel's rolling state (kc - 1 values)
-    float wc[9];      // EPI_CONV: the channel's kc conv weights
+    float y;                // EPI_ADD: current value of the output row
+    float cs[MK_KC - 1];    // EPI_CONV: the channel's rolling state (kc - 1 values)
+    float wc[MK_KC];        // EPI_CONV: the channel's kc conv weights
 };
 
 XJ_DEV void mk_epi_load(const MmaJob &jb, int tile, int tid, EpiPre &e) {
@@ -346,9 +347,9 @@ XJ_DEV void mk_epi_load(const MmaJob &jb, int tile, int tid, EpiPre &e) {
         const float *st = jb.conv_state + (size_t)row * (kc - 1);
         const float *wc = jb.conv_w + (size_t)row * kc;
 #pragma unroll
-        for (int k = 0; k < 8; k++) e.cs[k] = k < kc - 1 ? __ldcg(st + k) : 0.0f;
+        for (int k = 0; k < MK_KC - 1; k++) e.cs[k] = k < kc - 1 ? __ldcg(st + k) : 0.0f;
 #pragma unroll
-        for (int k = 0; k < 9; k++) e.wc[k] = k < kc ? wc[k] : 0.0f;
+        for (int k = 0; k < MK_KC; k++) e.wc[k] = k < kc ? wc[k] : 0.0f;
     }
 }
 
@@ -370,16 +371,16 @@ XJ_DEV void mk_epilogue(const MmaJob &jb, int tile, const float *red, float tsca
             s /= tscale;
             float acc = 0.0f;
 #pragma unroll
-            for (int k = 0; k < 8; k++)
+            for (int k = 0; k < MK_KC - 1; k++)
                 if (k < kc - 1) acc = fmaf(e.cs[k], e.wc[k], acc);
             float wl = e.wc[0];
 #pragma unroll
-            for (int k = 1; k < 9; k++)
+            for (int k = 1; k < MK_KC; k++)
                 if (k == kc - 1) wl = e.wc[k];
             acc = fmaf(s, wl, acc);
             float *st = jb.conv_state + (size_t)ch * (kc - 1);
 #pragma unroll
-            for (int k = 0; k < 7; k++)
+            for (int k = 0; k < MK_KC - 2; k++)
                 if (k < kc - 2) st[k] = e.cs[k + 1];
             st[kc - 2] = s;
             jb.y[ch] = silu_f(acc);

@@ -701,7 +701,7 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
     const float eps = hp->eps;
     std::vector<MkPhase> prog;
     std::vector<MkStream> stream;
-    bool ok = hp->s_k == hp->s_v && hp->head_dim <= 256 && hp->n_head % hp->n_head_kv == 0;
+    bool ok = hp->s_k == hp->s_v && hp->head_dim <= 256 && hp->n_head % hp->n_head_kv == 0 && hp->conv_k <= MK_KC;
     for (int il = s->l0; ok && il < s->l1; il++) {
         Layer &Ly = im->L[il - s->l0];
         if (Ly.rec) {
@@ -845,6 +845,7 @@ int xj_cuda_set_options(int which, int value) {
     case XJC_OPT_PDL: g_pdl = value ? 1 : 0; return 0;
     case XJC_OPT_PERSIST: g_opt_persist = value; return 0;
     case XJC_OPT_TRACE: g_opt_trace = value; return 0;
+    case XJC_OPT_GEMV_CTAS: if (value < 1 || value > 2) return -1; g_mma_ctas_per_sm = value; return 0;
     default: return -1;
     }
 }
