@@ -68,9 +68,19 @@ class Clocks:
              "clocks_event_reasons.sw_power_cap")
         try:
             self.p = subprocess.Popen(["nvidia-smi", "-i", str(gpu), f"--query-gpu={q}", "--format=csv,noheader,nounits",
-                                       "-lms", "100"], stdout=self.f, stderr=subprocess.DEVNULL)
+                                       "-lms", "20"], stdout=self.f, stderr=subprocess.DEVNULL)
         except FileNotFoundError:
             self.p = None
+            return
+        # the sampler takes a moment to start: wait (up to 10 s) for its first row so that the samples
+        # cover the timed region that follows
+        t0 = time.time()
+        while time.time() - t0 < 10 and self.p.poll() is None:
+            self.f.flush()
+            if os.path.getsize(self.f.name) > 0:
+                break
+            time.sleep(0.05)
+        self.skip = sum(1 for _ in open(self.f.name))
 
     def stop(self):
         if self.p is None:
@@ -78,7 +88,8 @@ class Clocks:
         self.p.terminate()
         self.p.wait()
         self.f.seek(0)
-        rows = [r.split(",") for r in self.f.read().strip().splitlines() if r.count(",") >= 8]
+        lines = self.f.read().strip().splitlines()[getattr(self, "skip", 0):]   # rows from the timed region on
+        rows = [r.split(",") for r in lines if r.count(",") >= 8]
         os.unlink(self.f.name)
         sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
         mx = [float(r[2]) for r in rows if r[2].strip().replace(".", "").isdigit()]
