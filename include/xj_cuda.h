@@ -96,6 +96,28 @@ int xj_cuda_phase_trace(const xj_stage *s, double *out, int cap);
 // (core/xj_quant.h:55-122). Runs on the current device.
 int xj_cuda_dequant_rows(int type, const void *src, int k, int n_rows, float *out, char *err, size_t errlen);
 
+// Batch of n_seq independent sequences decoded in lockstep (no counterpart in the reference, which has
+// no multi-sequence API; additive). The batch owns a stage over all layers with the head (weights,
+// n_seq-row activation buffers) plus each sequence's KV caches, Gated-DeltaNet/conv states and
+// position; the current device at creation is the batch's device.
+typedef struct xj_cuda_batch xj_cuda_batch;
+xj_cuda_batch *xj_cuda_batch_new(const xj_model *m, int n_seq, int n_ctx, char *err, size_t errlen);
+void xj_cuda_batch_free(xj_cuda_batch *b);
+// Forget every sequence (positions 0, states zero).
+int xj_cuda_batch_reset(xj_cuda_batch *b, char *err, size_t errlen);
+// Common position of the sequences (they advance in lockstep).
+int xj_cuda_batch_n_past(const xj_cuda_batch *b);
+// Greedy decode of every sequence: feeds prompts[b][0..n_prompt) (one token of each sequence per step,
+// continuing from n_past), then emits n_gen ids per sequence into out[b][0..n_gen) (out[b][0] is the
+// argmax after the prompt; every id but the last is fed back); margins[b][..] (may be NULL) receives
+// the top-2 logit gaps, gpu_ms (may be NULL) [prompt ms, decode ms]. Sequence b's ids are the ones
+// xj_cuda_decode gives for that sequence alone.
+int xj_cuda_batch_decode(xj_cuda_batch *b, const int32_t *prompts, int n_prompt, int n_gen, int32_t *out, float *margins,
+                         float *gpu_ms, char *err, size_t errlen);
+// Kernel launches of the last xj_cuda_batch_decode: launches[0] for the prompt steps, launches[1] for
+// the decode steps after them. Returns their sum.
+long long xj_cuda_batch_last_launches(const xj_cuda_batch *b, long long *launches);
+
 // Capacity, in floats, of the fixed device scratch used by xj_cuda_norm_gemv_noalloc (256 KiB).
 #define XJC_NOALLOC_MAX_FLOATS 65536
 

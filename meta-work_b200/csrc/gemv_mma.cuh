@@ -69,6 +69,7 @@ struct MmaJob {
     const float *conv_w;
     float *conv_ck;
     int kc;
+    long long conv_bstride;   // nonzero: token t is its own sequence, with its state at conv_state + t*conv_bstride
     // EPI_ARGMAX (T = 1): per-tile best value, runner-up value, best index
     float *pbest, *psecond;
     int *pidx;
@@ -232,8 +233,7 @@ XJ_DEV void unit_compute(const uint8_t *stage, int ui, int u, int hh, int lane, 
         const int kb = u * 256;
 #pragma unroll
         for (int sbl = 0; sbl < 4; sbl++) {
-            // the two k-steps of a 32-wide sub-block accumulate separately: two independent MMAs
-            float d4[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            float d4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
             for (int e = 0; e < 2; e++) {
                 const int s = 8 * hh + 2 * sbl + e;            // k-step within the super-block
@@ -241,13 +241,13 @@ XJ_DEV void unit_compute(const uint8_t *stage, int ui, int u, int hh, int lane, 
                 nib_frag64(word_of(e + 2 * sbl < 4 ? q0 : q1, (2 * sbl + e) & 3), af);
                 uint2 bv = make_uint2(0u, 0u);
                 if (bcol) bv = *reinterpret_cast<const uint2 *>(xb + kb + 16 * s);
-                mma16816(d4[e], af, bv.x, bv.y);
+                mma16816(d4, af, bv.x, bv.y);
             }
             const float4 sc4 = *reinterpret_cast<const float4 *>(scw + (sbl * 8 + g) * 4);
             const float S = xsum_t ? xsum_t[(kb >> 5) + 4 * hh + sbl] : 0.0f;
-            yg = fmaf(sc4.x, (d4[0][0] + d4[0][1]) + (d4[1][0] + d4[1][1]), yg);
+            yg = fmaf(sc4.x, d4[0] + d4[1], yg);
             yg = fmaf(-sc4.y, S, yg);
-            yg8 = fmaf(sc4.z, (d4[0][2] + d4[0][3]) + (d4[1][2] + d4[1][3]), yg8);
+            yg8 = fmaf(sc4.z, d4[2] + d4[3], yg8);
             yg8 = fmaf(-sc4.w, S, yg8);
         }
         __syncwarp();
@@ -281,12 +281,11 @@ XJ_DEV void unit_compute(const uint8_t *stage, int ui, int u, int hh, int lane, 
             hi_frag(hw, ah);
             uint2 bv = make_uint2(0u, 0u);
             if (bcol) bv = *reinterpret_cast<const uint2 *>(xb + kb + 16 * s);
-            float d5[4] = {0.f, 0.f, 0.f, 0.f};   // low nibbles and high bits: independent MMAs
             mma16816(d4, af, bv.x, bv.y);
-            mma16816(d5, ah, bv.x, bv.y);
+            mma16816(d4, ah, bv.x, bv.y);
             const float2 sc2 = *reinterpret_cast<const float2 *>(scw + (sl * 8 + g) * 2);
-            yg = fmaf(sc2.x, (d4[0] + d4[1]) + (d5[0] + d5[1]), yg);
-            yg8 = fmaf(sc2.y, (d4[2] + d4[3]) + (d5[2] + d5[3]), yg8);
+            yg = fmaf(sc2.x, d4[0] + d4[1], yg);
+            yg8 = fmaf(sc2.y, d4[2] + d4[3], yg8);
         }
         __syncwarp();
     } else {
@@ -309,11 +308,139 @@ XJ_DEV void unit_compute(const uint8_t *stage, int ui, int u, int hh, int lane, 
     }
 }
 
+// The same unit for up to 4*NT tokens: the A fragment is decoded once per k-step and multiplied with
+// NT B fragments (8 columns each: tokens 4n..4n+3, hi and lo). Column by column the arithmetic is
+// unit_compute's, so a token's result does not depend on NT or on the other tokens of the launch.
+// xb: this lane's B-fragment row of n-tile 0 (column g); the row of n-tile n is 8n columns further.
+template <int TYPE, int NT>
+XJ_DEV void unit_compute_n(const uint8_t *stage, int ui, int u, int hh, int lane, int T, const __half *xb,
+                           int xstride, const float *xsum, int nblk, float *scw, float (&yg)[NT], float (&yg8)[NT]) {
+    using G = Geo<TYPE>;
+    const int g = lane >> 2, c = lane & 3;
+    const uint8_t *qs = stage + ui * G::QB;
+    if constexpr (TYPE == XJ_Q4_K) {
+        const uint8_t *ss = stage + G::CU * G::QB + ui * G::SB;
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh) * 32 + lane) * 16);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh + 1) * 32 + lane) * 16);
+        {
+            const int r = lane & 15;
+            const uint4 hdr = *reinterpret_cast<const uint4 *>(ss + r * 16);
+            const float d = h2f((uint16_t)(hdr.x & 0xffff)), dmin = h2f((uint16_t)(hdr.x >> 16));
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int sbl = 2 * (lane >> 4) + e, sb = 4 * hh + sbl;
+                int s_, m_;
+                if (sb < 4) { s_ = byte_of(hdr, 4 + sb) & 63; m_ = byte_of(hdr, 8 + sb) & 63; }
+                else {
+                    s_ = (byte_of(hdr, 8 + sb) & 0xF) | ((byte_of(hdr, sb) >> 6) << 4);
+                    m_ = (byte_of(hdr, 8 + sb) >> 4) | ((byte_of(hdr, 4 + sb) >> 6) << 4);
+                }
+                const float d1 = d * (float)s_, m1 = dmin * (float)m_;
+                float *o = scw + ((sbl * 8 + (r & 7)) * 4 + (r >> 3) * 2);
+                o[0] = d1;
+                o[1] = 64.0f * d1 + m1;
+            }
+        }
+        __syncwarp();
+        const int kb = u * 256;
+#pragma unroll
+        for (int sbl = 0; sbl < 4; sbl++) {
+            float d4[NT][4];
+#pragma unroll
+            for (int n = 0; n < NT; n++) { d4[n][0] = d4[n][1] = d4[n][2] = d4[n][3] = 0.0f; }
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int s = 8 * hh + 2 * sbl + e;
+                uint32_t af[4];
+                nib_frag64(word_of(e + 2 * sbl < 4 ? q0 : q1, (2 * sbl + e) & 3), af);
+#pragma unroll
+                for (int n = 0; n < NT; n++) {
+                    uint2 bv = make_uint2(0u, 0u);
+                    if (8 * n + g < 2 * T) bv = *reinterpret_cast<const uint2 *>(xb + (size_t)(8 * n) * xstride + kb + 16 * s);
+                    mma16816(d4[n], af, bv.x, bv.y);
+                }
+            }
+            const float4 sc4 = *reinterpret_cast<const float4 *>(scw + (sbl * 8 + g) * 4);
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+                const int t = 4 * n + c;
+                const float S = t < T ? xsum[t * nblk + (kb >> 5) + 4 * hh + sbl] : 0.0f;
+                yg[n] = fmaf(sc4.x, d4[n][0] + d4[n][1], yg[n]);
+                yg[n] = fmaf(-sc4.y, S, yg[n]);
+                yg8[n] = fmaf(sc4.z, d4[n][2] + d4[n][3], yg8[n]);
+                yg8[n] = fmaf(-sc4.w, S, yg8[n]);
+            }
+        }
+        __syncwarp();
+    } else if constexpr (TYPE == XJ_Q6_K) {
+        const uint8_t *hs = stage + G::CU * G::QB + ui * G::HB;
+        const uint8_t *ss = stage + G::CU * (G::QB + G::HB) + ui * G::SB;
+        const uint8_t *ds = stage + G::CU * (G::QB + G::HB + G::SB) + ui * G::DB;
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh) * 32 + lane) * 16);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh + 1) * 32 + lane) * 16);
+        const uint4 hq = *reinterpret_cast<const uint4 *>(hs + (hh * 32 + lane) * 16);
+        {
+            const int r = lane & 15;
+            const uint4 sc = *reinterpret_cast<const uint4 *>(ss + r * 16);
+            const float d = h2f(*reinterpret_cast<const uint16_t *>(ds + r * 2));
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int sl = 4 * (lane >> 4) + e;
+                scw[(sl * 8 + (r & 7)) * 2 + (r >> 3)] = d * (float)(int8_t)byte_of(sc, 8 * hh + sl);
+            }
+        }
+        __syncwarp();
+        const int kb = u * 256;
+#pragma unroll
+        for (int sl = 0; sl < 8; sl++) {
+            const int s = 8 * hh + sl;
+            uint32_t af[4], ah[4];
+            nib_frag(word_of(sl < 4 ? q0 : q1, sl & 3), af);
+            uint32_t hw = word_of(hq, sl >> 1);
+            if (sl & 1) hw >>= 8;
+            hi_frag(hw, ah);
+            const float2 sc2 = *reinterpret_cast<const float2 *>(scw + (sl * 8 + g) * 2);
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+                float d4[4] = {0.f, 0.f, 0.f, 0.f};
+                uint2 bv = make_uint2(0u, 0u);
+                if (8 * n + g < 2 * T) bv = *reinterpret_cast<const uint2 *>(xb + (size_t)(8 * n) * xstride + kb + 16 * s);
+                mma16816(d4, af, bv.x, bv.y);
+                mma16816(d4, ah, bv.x, bv.y);
+                yg[n] = fmaf(sc2.x, d4[0] + d4[1], yg[n]);
+                yg8[n] = fmaf(sc2.y, d4[2] + d4[3], yg8[n]);
+            }
+        }
+        __syncwarp();
+    } else {
+        const uint8_t *ds = stage + G::CU * G::QB + ui * G::DB;
+        const uint4 q = *reinterpret_cast<const uint4 *>(qs + lane * 16);
+        const float dv = lane < 16 ? h2f(*reinterpret_cast<const uint16_t *>(ds + lane * 2)) : 0.0f;
+        const float dg = __shfl_sync(0xffffffffu, dv, g), dg8 = __shfl_sync(0xffffffffu, dv, g + 8);
+        const int kb = u * 32;
+        uint32_t af[2][4];
+#pragma unroll
+        for (int e = 0; e < 2; e++) q8_frag(word_of(q, 2 * e), word_of(q, 2 * e + 1), af[e]);
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+            float d4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                uint2 bv = make_uint2(0u, 0u);
+                if (8 * n + g < 2 * T) bv = *reinterpret_cast<const uint2 *>(xb + (size_t)(8 * n) * xstride + kb + 16 * e);
+                mma16816(d4, af[e], bv.x, bv.y);
+            }
+            yg[n] = fmaf(dg, d4[0] + d4[1], yg[n]);
+            yg8[n] = fmaf(dg8, d4[2] + d4[3], yg8[n]);
+        }
+    }
+}
+
 // ------------------------------------------------------------------ shared-memory layout
 struct MmaSmem {
     int T, K, xstride;        // halves per activation column (row of the staged B operand)
     size_t off_ring, off_xs, off_sum, off_sc, off_red, bytes;
-    __host__ __device__ MmaSmem(int T_, int K_, int ring_bytes) : T(T_), K(K_) {
+    __host__ __device__ MmaSmem(int T_, int K_, int ring_bytes, int tmax = MMA_MAXT) : T(T_), K(K_) {
         xstride = K + 16;                                   // 16-half pad: conflict-free 8-byte B loads
         off_ring = 0;                                       // weight stages (16-byte aligned)
         off_xs = off_ring + (size_t)ring_bytes;
@@ -322,26 +449,26 @@ struct MmaSmem {
         off_sc = off_sum + (size_t)T * (K / 32) * 4;        // fp32 sums of hi+lo per 32-wide block
         off_sc = (off_sc + 15) & ~(size_t)15;
         off_red = off_sc + (size_t)MMA_WARPS * 128 * 4;     // per-warp staged scales
-        bytes = off_red + (size_t)MMA_WARPS * 16 * 4 * 4 + 64;
+        bytes = off_red + (size_t)MMA_WARPS * 16 * tmax * 4 + 64;
     }
 };
 
 // ------------------------------------------------------------------ kernel
-template <int TYPE>
-__global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
+template <int TYPE, int NT>
+__global__ void __launch_bounds__(MMA_WARPS * 32, NT == 1 ? 2 : 1) k_gemv_mma(MmaArgs a) {
     using G = Geo<TYPE>;
-    constexpr int SB = stage_bytes<TYPE>(), NS = G::STAGES;
+    constexpr int SB = stage_bytes<TYPE>(), NS = G::STAGES, TMAX = 4 * NT;
     constexpr bool KQ = TYPE != XJ_Q8_0;                 // K-quant units are split over two warps
     extern __shared__ __align__(128) uint8_t smem[];
-    const MmaSmem L(a.T, a.K, SB * NS);
+    const MmaSmem L(a.T, a.K, SB * NS, TMAX);
     uint8_t *ring = smem + L.off_ring;
     __half *xs = reinterpret_cast<__half *>(smem + L.off_xs);
     float *xsum = reinterpret_cast<float *>(smem + L.off_sum);
     float *scs = reinterpret_cast<float *>(smem + L.off_sc);
     float *red = reinterpret_cast<float *>(smem + L.off_red);
     __shared__ __align__(8) uint64_t bars[NS];
-    __shared__ float tok_scale[MMA_MAXT], tok_nsc[MMA_MAXT];
-    __shared__ float pred[MMA_WARPS][MMA_MAXT][2];
+    __shared__ float tok_scale[TMAX], tok_nsc[TMAX];
+    __shared__ float pred[MMA_WARPS][2];
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
     const int T = a.T, K = a.K;
     const int total = a.tile_start[a.njob];
@@ -404,12 +531,12 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
         }
         ss = warp_sum(ss);
         am = warp_max(am);
-        if (lane == 0) { pred[warp][t][0] = ss; pred[warp][t][1] = am; }
+        if (lane == 0) { pred[warp][0] = ss; pred[warp][1] = am; }
         __syncthreads();
         if (tid == 0) {
             double tss = 0;
             float tam = 0.0f;
-            for (int w = 0; w < MMA_WARPS; w++) { tss += pred[w][t][0]; tam = fmaxf(tam, pred[w][t][1]); }
+            for (int w = 0; w < MMA_WARPS; w++) { tss += pred[w][0]; tam = fmaxf(tam, pred[w][1]); }
             float nsc = 1.0f;
             if (a.pro == PRO_NORM) nsc = 1.0f / sqrtf((float)(tss / K) + a.eps);
             // the largest |f(x)| lands in [2^14, 2^15): fp16 hi/lo stay finite with full relative precision
@@ -442,11 +569,11 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
     __syncthreads();
 
     // ---- 3. stream the chunks: wait for the stage, compute, release, refill
-    const bool bcol = g < 2 * T;
     const __half *xb = xs + (size_t)g * L.xstride + 4 * c;
-    const float *xsum_t = (TYPE == XJ_Q4_K && c < T) ? xsum + c * (K / 32) : nullptr;
     float *scw = scs + warp * 128;
-    float yg = 0.0f, yg8 = 0.0f;
+    float yg[NT], yg8[NT];
+#pragma unroll
+    for (int n = 0; n < NT; n++) { yg[n] = 0.0f; yg8[n] = 0.0f; }
     for (int i = 0; i < nchunks; i++) {
         int j, tile, u0, cu;
         chunk_of(i, j, tile, u0, cu);
@@ -454,19 +581,22 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
         const uint8_t *st = ring + (size_t)(i % NS) * SB;
         if (KQ) {
             const int ui = warp >> 1;
-            if (ui < cu) unit_compute<TYPE>(st, ui, u0 + ui, warp & 1, lane, bcol, xb, xsum_t, scw, yg, yg8);
+            if (ui < cu) unit_compute_n<TYPE, NT>(st, ui, u0 + ui, warp & 1, lane, T, xb, L.xstride, xsum, K / 32, scw, yg, yg8);
         } else {
 #pragma unroll
             for (int k = 0; k < G::CU / MMA_WARPS; k++) {
                 const int ui = warp + k * MMA_WARPS;
-                if (ui < cu) unit_compute<TYPE>(st, ui, u0 + ui, 0, lane, bcol, xb, xsum_t, scw, yg, yg8);
+                if (ui < cu) unit_compute_n<TYPE, NT>(st, ui, u0 + ui, 0, lane, T, xb, L.xstride, xsum, K / 32, scw, yg, yg8);
             }
         }
         const bool tile_end = (i % nch) == nch - 1;
         if (tile_end) {
-            red[(warp * 16 + g) * 4 + c] = yg;
-            red[(warp * 16 + g + 8) * 4 + c] = yg8;
-            yg = 0.0f; yg8 = 0.0f;
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+                red[(warp * 16 + g) * TMAX + 4 * n + c] = yg[n];
+                red[(warp * 16 + g + 8) * TMAX + 4 * n + c] = yg8[n];
+                yg[n] = 0.0f; yg8[n] = 0.0f;
+            }
         }
         __syncthreads();   // stage i % NS is free; red holds the tile's per-warp partials
         if (tid == 0 && i + NS < nchunks) {
@@ -476,7 +606,28 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
         if (!tile_end) continue;
         // ---- 4. epilogue of the tile: fixed-order sum over warps
         const MmaJob &jb = a.job[j];
-        if (jb.epi == EPI_CONV) {
+        if (jb.epi == EPI_CONV && jb.conv_bstride) {
+            // batch of sequences: each token through its own sequence's conv state, no checkpoints
+            if (tid < 16 && tile * 16 + tid < jb.w.N) {
+                const int ch = tile * 16 + tid, kc = jb.kc;
+                const float *wc = jb.conv_w + (size_t)ch * kc;
+                for (int t = 0; t < T; t++) {
+                    float *st = jb.conv_state + t * jb.conv_bstride + (size_t)ch * (kc - 1);
+                    float cs[8];
+                    for (int k = 0; k < kc - 1; k++) cs[k] = st[k];
+                    float s = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + tid) * TMAX + t];
+                    s /= tok_scale[t];
+                    float acc = 0.0f;
+                    for (int k = 0; k < kc - 1; k++) acc = fmaf(cs[k], wc[k], acc);
+                    acc = fmaf(s, wc[kc - 1], acc);
+                    for (int k = 0; k < kc - 2; k++) st[k] = cs[k + 1];
+                    st[kc - 2] = s;
+                    jb.y[t * jb.ldy + ch] = silu_f(acc);
+                }
+            }
+        } else if (jb.epi == EPI_CONV) {
             // one thread per channel: the T tokens in order through the rolling conv state
             if (tid < 16 && tile * 16 + tid < jb.w.N) {
                 const int ch = tile * 16 + tid, kc = jb.kc;
@@ -486,7 +637,7 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
                 for (int t = 0; t < T; t++) {
                     float s = 0.0f;
 #pragma unroll
-                    for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + tid) * 4 + t];
+                    for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + tid) * TMAX + t];
                     s /= tok_scale[t];
                     float acc = 0.0f;
                     for (int k = 0; k < kc - 1; k++) acc = fmaf(cs[k], wc[k], acc);
@@ -504,7 +655,7 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
                 const int row = tid & 15;
                 float s = 0.0f;
 #pragma unroll
-                for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + row) * 4 + 0];
+                for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + row) * TMAX + 0];
                 s /= tok_scale[0];
                 const bool real = tile * 16 + row < jb.w.N;   // rows past N pad the last tile
                 if (jb.y && tid < 16 && real) jb.y[(size_t)tile * 16 + row] = s;
@@ -521,12 +672,12 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
                 }
                 if (tid == 0) { jb.pbest[tile] = b; jb.psecond[tile] = b2; jb.pidx[tile] = bi; }
             }
-        } else if (tid < 64) {
-            const int row = tid >> 2, t = tid & 3;
+        } else if (tid < 16 * TMAX) {
+            const int row = tid / TMAX, t = tid % TMAX;
             if (t < T && tile * 16 + row < jb.w.N) {
                 float s = 0.0f;
 #pragma unroll
-                for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + row) * 4 + t];
+                for (int w = 0; w < MMA_WARPS; w++) s += red[(w * 16 + row) * TMAX + t];
                 s /= tok_scale[t];
                 float *yp = jb.y + t * jb.ldy + (size_t)tile * 16 + row;
                 *yp = jb.epi == EPI_ADD ? *yp + s : s;
@@ -537,7 +688,9 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 2) k_gemv_mma(MmaArgs a) {
 }
 
 // ------------------------------------------------------------------ host: launch
-constexpr size_t MMA_SMEM_MAX = 200 * 1024;
+constexpr size_t MMA_SMEM_MAX = 200 * 1024;              // 4-token launches
+constexpr size_t MMA_SMEM_MAX_WIDE = 222 * 1024;         // 16-token launches (one CTA per SM)
+constexpr int MMA_WIDE_T = 16;                           // tokens of a wide launch (NT = 4 n-tiles)
 constexpr int MMA_KMAX = MMA_KMAX_PT * MMA_WARPS * 32;   // longest row the prologue stages
 
 inline int ring_bytes(int type) {
@@ -547,7 +700,10 @@ inline int ring_bytes(int type) {
     default: return stage_bytes<XJ_Q8_0>() * Geo<XJ_Q8_0>::STAGES;
     }
 }
-inline size_t mma_smem_bytes(int type, int T, int K) { return MmaSmem(T, K, ring_bytes(type)).bytes; }
+inline size_t mma_smem_bytes(int type, int T, int K, int tmax = MMA_MAXT) { return MmaSmem(T, K, ring_bytes(type), tmax).bytes; }
+
+// Whether a 16-token launch fits for this weight type and row length (its activations are staged whole).
+inline bool wide_ok(int type, int K) { return mma_smem_bytes(type, MMA_WIDE_T, K, MMA_WIDE_T) <= MMA_SMEM_MAX_WIDE; }
 
 // Matrices the tensor-core path can take (at up to MMA_MAXT tokens).
 inline bool tiled_ok(int type, int K, int N) {
@@ -580,7 +736,7 @@ inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, siz
 }
 
 // Per-device, once: allow the kernel's dynamic shared memory; returns the SM count.
-template <int TYPE>
+template <int TYPE, int NT>
 inline int mma_setup() {
     constexpr int MAXDEV = 64;
     static int sms[MAXDEV] = {0};
@@ -588,22 +744,30 @@ inline int mma_setup() {
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= MAXDEV) dev = 0;
     if (!sms[dev]) {
-        cudaFuncSetAttribute(k_gemv_mma<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM_MAX);
+        cudaFuncSetAttribute(k_gemv_mma<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)(NT == 1 ? MMA_SMEM_MAX : MMA_SMEM_MAX_WIDE));
         cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
     }
     return sms[dev];
 }
 
-// One launch for up to 4 same-type matrices sharing the input x[T][K] (T <= MMA_MAXT): up to
-// g_mma_ctas_per_sm CTAs per SM, each owning a contiguous, balanced range of tiles.
-template <int TYPE>
-inline cudaError_t launch_mma_t(MmaArgs a, cudaStream_t st) {
-    const int sms = mma_setup<TYPE>() * g_mma_ctas_per_sm;
+// One launch for up to 4 same-type matrices sharing the input x[T][K]: T <= 4 with up to
+// g_mma_ctas_per_sm CTAs per SM, or 4 < T <= 16 (wide: four n-tiles per decoded weight fragment) with
+// one CTA per SM; each CTA owns a contiguous, balanced range of tiles.
+template <int TYPE, int NT>
+inline cudaError_t launch_mma_nt(MmaArgs a, cudaStream_t st) {
+    const int sms = mma_setup<TYPE, NT>() * (NT == 1 ? g_mma_ctas_per_sm : 1);
     const int tiles = a.tile_start[a.njob];
     const int ctas = tiles < sms ? tiles : sms;
     a.tiles_per_cta = (tiles + ctas - 1) / ctas;
     const dim3 grid((tiles + a.tiles_per_cta - 1) / a.tiles_per_cta), block(MMA_WARPS * 32);
-    return launch_pdl(k_gemv_mma<TYPE>, grid, block, mma_smem_bytes(TYPE, a.T, a.K), st, a);
+    return launch_pdl(k_gemv_mma<TYPE, NT>, grid, block, mma_smem_bytes(TYPE, a.T, a.K, 4 * NT), st, a);
+}
+template <int TYPE>
+inline cudaError_t launch_mma_t(MmaArgs a, cudaStream_t st) {
+    if (a.T <= MMA_MAXT) return launch_mma_nt<TYPE, 1>(a, st);
+    if (a.T <= MMA_WIDE_T && wide_ok(TYPE, a.K)) return launch_mma_nt<TYPE, 4>(a, st);
+    return cudaErrorInvalidValue;
 }
 
 inline cudaError_t launch_mma(const MmaArgs &a, int type, cudaStream_t st) {

@@ -395,6 +395,12 @@ static __global__ void k_advance(int *npast, int T) {
     if (threadIdx.x == 0 && blockIdx.x == 0) *npast += T;
 }
 
+// Positions of B sequences: npast[b] += T.
+static __global__ void k_advance_batch(int *npast, int B, int T) {
+    griddep_wait();
+    for (int b = threadIdx.x; b < B; b += blockDim.x) npast[b] += T;
+}
+
 // Greedy pick over logits[V]: largest value, lowest index on ties (core/xj_spec.c:12-16); also the
 // gap to the runner-up. Writes the id to out_tok[*step] and to *cur (the next step's input), the gap
 // to margin[*step], then advances *step. One block of 1024 threads.
@@ -542,6 +548,80 @@ XJ_DEV void argmax_final_dev(const ArgmaxArgs &a, int tid, int nthr) {
 static __global__ void __launch_bounds__(1024) k_argmax_final(ArgmaxArgs a) {
     griddep_wait();
     argmax_final_dev<BarBlock>(a, threadIdx.x, blockDim.x);
+}
+
+// ---------------------------------------------------------------- batch of independent sequences
+// One token of each of B sequences per launch: the single-sequence device functions with the
+// operands of sequence b = blockIdx.y (its activation row, recurrent state, KV cache, position,
+// output slots). The arithmetic per sequence is exactly the single-sequence kernels' at T = 1.
+
+// Grid (Hv, B), 4*S threads; state of sequence b at ssm + b*state_stride.
+template <int S>
+__global__ void __launch_bounds__(4 * S) k_gdn_batch(GdnArgs a, long long state_stride) {
+    griddep_wait();
+    const int b = blockIdx.y;
+    GdnArgs c = a;
+    c.qkv += b * a.ldq; c.z += b * a.ldz; c.beta += b * a.ldg; c.alpha += b * a.ldg;
+    c.ssm += b * state_stride; c.out += b * a.ldo; c.T = 1; c.ck_ssm = nullptr;
+    gdn_head<S, BarBlock>(c, blockIdx.x, threadIdx.x);
+}
+
+template <typename KV>
+XJ_DEV AttnArgs attn_seq(const AttnArgs &a, const int *npast_b, long long kv_stride, int b) {
+    AttnArgs c = a;
+    c.q += b * a.ldq; c.k += b * a.ldkv; c.v += b * a.ldkv;
+    c.qrot += (size_t)b * a.H * a.D;
+    c.kc = (KV *)a.kc + b * kv_stride; c.vc = (KV *)a.vc + b * kv_stride;
+    c.npast = npast_b + b;
+    c.out += b * a.ldo;
+    return c;
+}
+
+// Grid (H + Hkv, B), ceil32(D) threads; KV cache of sequence b at kc/vc + b*kv_stride elements.
+template <typename KV>
+static __global__ void k_attn_prep_batch(AttnArgs a, const int *npast_b, long long kv_stride) {
+    griddep_wait();
+    attn_prep_slot<KV, BarBlock>(attn_seq<KV>(a, npast_b, kv_stride, blockIdx.y), blockIdx.x, 0, threadIdx.x);
+}
+
+// Grid (H, B), 128 threads.
+template <typename KV, int DPL>
+static __global__ void __launch_bounds__(128) k_attn_batch(AttnArgs a, const int *npast_b, long long kv_stride) {
+    griddep_wait();
+    attn_head<KV, DPL, BarBlock>(attn_seq<KV>(a, npast_b, kv_stride, blockIdx.y), blockIdx.x, 0, threadIdx.x);
+}
+
+// Grid (ceil(V/16), B), 32 threads: per-tile argmax partials of each sequence's logits row.
+static __global__ void k_argmax_rows_batch(const float *logits, int V, float *pbest, float *psecond, int *pidx, int ntiles) {
+    griddep_wait();
+    const int b = blockIdx.y, tile = blockIdx.x, row = threadIdx.x & 15, r = tile * 16 + row;
+    const float *lg = logits + (size_t)b * V;
+    float v = r < V ? lg[r] : -INFINITY, v2 = -INFINITY;
+    int vi = r < V ? r : 0x7fffffff;
+#pragma unroll
+    for (int o = 8; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, v, o), ov2 = __shfl_xor_sync(0xffffffffu, v2, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, vi, o);
+        if (ov > v || (ov == v && oi < vi)) { v2 = fmaxf(v, ov2); v = ov; vi = oi; }
+        else v2 = fmaxf(v2, ov);
+    }
+    if (threadIdx.x == 0) {
+        const size_t o = (size_t)b * ntiles + tile;
+        pbest[o] = v; psecond[o] = v2; pidx[o] = vi;
+    }
+}
+
+// Grid (B), 1024 threads: the greedy pick of each sequence (argmax_final_dev on its partials),
+// written to out_tok[b*out_stride + step_b], with the next token's embedding into row b of x.
+static __global__ void __launch_bounds__(1024) k_argmax_final_batch(ArgmaxArgs a, long long out_stride, int E) {
+    griddep_wait();
+    const int b = blockIdx.x;
+    ArgmaxArgs c = a;
+    c.pbest += (size_t)b * a.ntiles; c.psecond += (size_t)b * a.ntiles; c.pidx += (size_t)b * a.ntiles;
+    c.out_tok += b * out_stride;
+    if (c.margin) c.margin += b * out_stride;
+    c.cur += b; c.step += b; c.x += (size_t)b * E; c.npast += b;
+    argmax_final_dev<BarBlock>(c, threadIdx.x, blockDim.x);
 }
 
 }  // namespace xjk

@@ -186,6 +186,7 @@ struct Job {
     const float *conv_w = nullptr;
     float *conv_ck = nullptr;
     int kc = 0;
+    long long conv_bstride = 0;   // batch of sequences: token t's conv state at conv_state + t*conv_bstride
     float *pbest = nullptr, *psecond = nullptr;
     int *pidx = nullptr;
 };
@@ -225,20 +226,24 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
             MmaJob &mj = m.job[m.njob];
             mj.w = tiled_of(f.w); mj.y = f.y; mj.ldy = f.ldy; mj.epi = f.epi;
             mj.conv_state = f.conv_state; mj.conv_w = f.conv_w; mj.conv_ck = f.conv_ck; mj.kc = f.kc;
+            mj.conv_bstride = f.conv_bstride;
             mj.pbest = f.pbest; mj.psecond = f.psecond; mj.pidx = f.pidx;
             m.tile_start[m.njob + 1] = m.tile_start[m.njob] + (f.w.N + 15) / 16;
             m.njob++;
             done[k] = 1;
         }
-        // tokens in chunks of MMA_MAXT; each token's result does not depend on the chunking (the conv
-        // epilogue carries its state across chunks, its checkpoints are indexed by absolute token)
-        for (int t0 = 0; t0 < T; t0 += MMA_MAXT) {
+        // tokens in chunks of 16 (wide launches) or 4; each token's result does not depend on the
+        // chunking (the conv epilogue carries its state across chunks, its checkpoints are indexed by
+        // absolute token)
+        const int tch = T > MMA_MAXT && wide_ok(type, K) ? MMA_WIDE_T : MMA_MAXT;
+        for (int t0 = 0; t0 < T; t0 += tch) {
             MmaArgs c = m;
-            c.T = T - t0 < MMA_MAXT ? T - t0 : MMA_MAXT;
+            c.T = T - t0 < tch ? T - t0 : tch;
             c.x = x + t0 * ldx;
             c.x2 = x2 ? x2 + t0 * ldx : nullptr;
             for (int j = 0; j < c.njob; j++) {
                 if (c.job[j].y) c.job[j].y = m.job[j].y + t0 * m.job[j].ldy;
+                if (c.job[j].conv_bstride) c.job[j].conv_state = m.job[j].conv_state + t0 * m.job[j].conv_bstride;
                 if (c.job[j].conv_ck) {
                     // the chunk saves the states after its tokens t0..t0+c.T-2; the one after t0+c.T-1
                     // (when that is not the last token) is saved by the next chunk as its "previous" state
@@ -248,7 +253,7 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
             launch_mma(c, type, im->st);
             im->nlaunch++;
             for (int j = 0; j < c.njob; j++)
-                if (m.job[j].conv_ck && t0 + c.T < T) {
+                if (m.job[j].conv_ck && !m.job[j].conv_bstride && t0 + c.T < T) {
                     // state after token t0+c.T-1 = current conv state: copy it into its checkpoint slot
                     const size_t n = (size_t)m.job[j].w.N * (m.job[j].kc - 1);
                     cudaMemcpyAsync(m.job[j].conv_ck + (size_t)(t0 + c.T - 1) * n, m.job[j].conv_state, n * 4,
@@ -825,6 +830,126 @@ int mk_launch(xj_stage *s, int n, char *err, size_t errlen) {
     return 0;
 }
 
+// ------------------------------------------------------------------ batch of independent sequences
+// B sequences decoded in lockstep, one token of each per step (the reference has no multi-sequence API;
+// this is additive). Weights and activation buffers are those of an ordinary stage with max_batch = B;
+// each sequence has its own KV caches, Gated-DeltaNet and conv states and position. Matrix-vector
+// products take the B tokens as one batch (each token's column is computed independently, so a
+// sequence's result is bitwise the single-sequence one); attention, GDN and the greedy pick run one
+// CUDA block per (head, sequence).
+struct BatchImpl {
+    xj_stage *s = nullptr;
+    int B = 0, n_ctx = 0, n_past = 0;
+    std::vector<float *> ssm, conv;        // per layer: [B][h_v][s_v][s_k], [B][conv_dim][conv_k-1]
+    std::vector<void *> kc, vc;            // per layer: [B][n_ctx][n_head_kv * head_dim]
+    int *npast = nullptr, *step = nullptr;
+    int32_t *cur = nullptr, *prompts = nullptr, *out_tok = nullptr;
+    float *margin = nullptr, *pbest = nullptr, *psecond = nullptr;
+    int *pidx = nullptr;
+    int ntiles = 0, out_cap = 0, prompt_cap = 0;
+    cudaGraphExec_t step_graph = nullptr;
+    int step_kernels = 0;
+    long long last_launches[2] = {0, 0};
+};
+
+void run_layers_batch(BatchImpl *bi) {
+    xj_stage *s = bi->s;
+    Impl *im = I(s);
+    const xj_hparams *hp = &s->m->hp;
+    const int E = hp->n_embd, FF = hp->n_ff, B = bi->B;
+    const float eps = hp->eps;
+    for (int il = s->l0; il < s->l1; il++) {
+        Layer &Ly = im->L[il - s->l0];
+        const int li = il - s->l0;
+        if (Ly.rec) {
+            const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v;
+            Job qkv{Ly.qkv, im->qkvb, CD};
+            qkv.epi = EPI_CONV; qkv.conv_state = bi->conv[li]; qkv.conv_w = Ly.conv_w; qkv.kc = hp->conv_k;
+            qkv.conv_bstride = (long long)CD * (hp->conv_k - 1);
+            gemv(im, im->x, nullptr, E, B, PRO_NORM, Ly.attn_norm, eps,
+                 {qkv, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
+            GdnArgs g = gdn_args(im, hp, Ly, 1, false);
+            g.ssm = bi->ssm[li];
+            const long long ss = (long long)hp->h_v * hp->s_v * hp->s_k;
+            switch (hp->s_k) {
+            case 16: launch(im, k_gdn_batch<16>, dim3(Hv, B), dim3(64), 0, g, ss); break;
+            case 32: launch(im, k_gdn_batch<32>, dim3(Hv, B), dim3(128), 0, g, ss); break;
+            case 64: launch(im, k_gdn_batch<64>, dim3(Hv, B), dim3(256), 0, g, ss); break;
+            case 128: launch(im, k_gdn_batch<128>, dim3(Hv, B), dim3(512), 0, g, ss); break;
+            default: launch(im, k_gdn_batch<256>, dim3(Hv, B), dim3(1024), 0, g, ss); break;
+            }
+            Job out{Ly.out, im->x, E};
+            out.epi = EPI_ADD;
+            gemv(im, im->o, nullptr, DI, B, PRO_NONE, nullptr, eps, {out});
+        } else {
+            const int H = hp->n_head, Hkv = hp->n_head_kv, D = hp->head_dim, nq = 2 * H * D, nk = Hkv * D;
+            const float *q, *k, *v;
+            long long ldq, ldkv;
+            if (Ly.fused) {
+                gemv(im, im->x, nullptr, E, B, PRO_NORM, Ly.attn_norm, eps, {{Ly.wqkv, im->qkvb, nq + 2 * nk}});
+                q = im->qkvb; k = im->qkvb + nq; v = im->qkvb + nq + nk; ldq = ldkv = nq + 2 * nk;
+            } else {
+                gemv(im, im->x, nullptr, E, B, PRO_NORM, Ly.attn_norm, eps,
+                     {{Ly.wq, im->q, nq}, {Ly.wk, im->k, nk}, {Ly.wv, im->v, nk}});
+                q = im->q; k = im->k; v = im->v; ldq = nq; ldkv = nk;
+            }
+            AttnArgs a = attn_args(im, hp, Ly, q, ldq, k, v, ldkv);
+            a.kc = bi->kc[li]; a.vc = bi->vc[li];
+            const long long kvs = (long long)bi->n_ctx * nk;
+            const int dpl = (D + 31) / 32;
+            if (im->kv_f32) {
+                launch(im, k_attn_prep_batch<float>, dim3(H + Hkv, B), dim3((D + 31) / 32 * 32), 0, a, (const int *)bi->npast, kvs);
+                if (dpl == 1) launch(im, k_attn_batch<float, 1>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                else if (dpl == 2) launch(im, k_attn_batch<float, 2>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                else if (dpl <= 4) launch(im, k_attn_batch<float, 4>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                else launch(im, k_attn_batch<float, 8>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+            } else {
+                launch(im, k_attn_prep_batch<__half>, dim3(H + Hkv, B), dim3((D + 31) / 32 * 32), 0, a, (const int *)bi->npast, kvs);
+                if (dpl == 1) launch(im, k_attn_batch<__half, 1>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                else if (dpl == 2) launch(im, k_attn_batch<__half, 2>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                else if (dpl <= 4) launch(im, k_attn_batch<__half, 4>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                else launch(im, k_attn_batch<__half, 8>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+            }
+            Job o{Ly.wo, im->x, E};
+            o.epi = EPI_ADD;
+            gemv(im, im->o, nullptr, (long long)H * D, B, PRO_NONE, nullptr, eps, {o});
+        }
+        gemv(im, im->x, nullptr, E, B, PRO_NORM, Ly.post_norm, eps, {{Ly.ffn_gate, im->g, FF}, {Ly.ffn_up, im->u, FF}});
+        Job down{Ly.ffn_down, im->x, E};
+        down.epi = EPI_ADD;
+        gemv(im, im->g, im->u, FF, B, PRO_SWIGLU, nullptr, eps, {down});
+    }
+}
+
+// Output norm + LM head for all B rows, then each sequence's greedy pick: out_tok[b][step_b], the next
+// token's embedding into row b of x, position + 1.
+void head_batch(BatchImpl *bi) {
+    xj_stage *s = bi->s;
+    Impl *im = I(s);
+    const xj_hparams *hp = &s->m->hp;
+    const int V = im->output.N, B = bi->B;
+    gemv(im, im->x, nullptr, hp->n_embd, B, PRO_NORM, im->output_norm, hp->eps, {{im->output, im->logits, V}});
+    launch(im, k_argmax_rows_batch, dim3(bi->ntiles, B), dim3(32), 0, (const float *)im->logits, V, bi->pbest, bi->psecond,
+           bi->pidx, bi->ntiles);
+    ArgmaxArgs a;
+    a.pbest = bi->pbest; a.psecond = bi->psecond; a.pidx = bi->pidx; a.ntiles = bi->ntiles;
+    a.out_tok = bi->out_tok; a.margin = bi->margin; a.cur = bi->cur; a.step = bi->step;
+    a.emb = im->tok_embd; a.x = im->x; a.npast = bi->npast;
+    launch(im, k_argmax_final_batch, dim3(B), dim3(1024), 0, a, (long long)bi->out_cap, hp->n_embd);
+}
+
+int batch_reset_state(BatchImpl *bi, char *err, size_t errlen) {
+    Impl *im = I(bi->s);
+    const xj_hparams *hp = &bi->s->m->hp;
+    const size_t ns = (size_t)bi->B * hp->h_v * hp->s_v * hp->s_k, nc = (size_t)bi->B * hp->conv_dim * (hp->conv_k - 1);
+    for (float *p : bi->ssm) if (p) CK(cudaMemsetAsync(p, 0, ns * 4, im->st));     // GDN layers only
+    for (float *p : bi->conv) if (p) CK(cudaMemsetAsync(p, 0, nc * 4, im->st));
+    CK(cudaMemsetAsync(bi->npast, 0, sizeof(int) * bi->B, im->st));
+    CK(cudaStreamSynchronize(im->st));
+    bi->n_past = 0;
+    return 0;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1121,6 +1246,142 @@ uint64_t xjc_stage_state_bytes(const xj_model *m, int l0, int l1, int n_ctx, int
     }
     b += 7ull * 4 * max_batch * scratch_floats(hp);
     return b;
+}
+
+
+// ------------------------------------------------------------------ batch API (additive)
+struct xj_cuda_batch {
+    BatchImpl impl;
+};
+
+xj_cuda_batch *xj_cuda_batch_new(const xj_model *m, int n_seq, int n_ctx, char *err, size_t errlen) {
+    if (!m || n_seq < 1 || n_seq > 1024 || n_ctx < 1) { seterr(err, errlen, "need 1 <= n_seq <= 1024 and n_ctx >= 1"); return nullptr; }
+    // the stage holds the weights and B-row activation buffers; its own single-sequence state is minimal
+    xj_stage *s = xj_cuda_stage_new(m, 0, m->hp.n_layer, 1, n_seq, true, err, errlen);
+    if (!s) return nullptr;
+    xj_cuda_batch *b = new xj_cuda_batch();
+    BatchImpl *bi = &b->impl;
+    bi->s = s;
+    bi->B = n_seq;
+    bi->n_ctx = n_ctx;
+    Impl *im = I(s);
+    DevGuard dg(im->dev);
+    const xj_hparams *hp = &m->hp;
+    auto fail = [&]() { cuda_destroy(s); delete b; return (xj_cuda_batch *)nullptr; };
+    const size_t ns = (size_t)n_seq * hp->h_v * hp->s_v * hp->s_k, nc = (size_t)n_seq * hp->conv_dim * (hp->conv_k - 1);
+    const size_t nkv = (size_t)n_seq * n_ctx * hp->n_head_kv * hp->head_dim, es = im->kv_f32 ? 4 : 2;
+    for (int il = 0; il < hp->n_layer; il++) {
+        float *a = nullptr, *c = nullptr;
+        uint8_t *k = nullptr, *v = nullptr;
+        if (im->L[il].rec) {
+            if (dalloc(im, &a, ns, err, errlen) || dalloc(im, &c, nc, err, errlen)) return fail();
+        } else if (dalloc(im, &k, nkv * es, err, errlen) || dalloc(im, &v, nkv * es, err, errlen)) return fail();
+        bi->ssm.push_back(a); bi->conv.push_back(c); bi->kc.push_back(k); bi->vc.push_back(v);
+    }
+    bi->ntiles = (im->output.N + 15) / 16;
+    if (dalloc(im, &bi->npast, (size_t)n_seq, err, errlen) || dalloc(im, &bi->step, (size_t)n_seq, err, errlen) ||
+        dalloc(im, &bi->cur, (size_t)n_seq, err, errlen) ||
+        dalloc(im, &bi->pbest, (size_t)n_seq * bi->ntiles, err, errlen) ||
+        dalloc(im, &bi->psecond, (size_t)n_seq * bi->ntiles, err, errlen) ||
+        dalloc(im, &bi->pidx, (size_t)n_seq * bi->ntiles, err, errlen)) return fail();
+    if (!im->tok_embd.p && upload(im, m->tok_embd, &im->tok_embd, err, errlen, true)) return fail();
+    if (cudaDeviceSynchronize() != cudaSuccess) { seterr(err, errlen, "CUDA error while creating the batch"); return fail(); }
+    if (batch_reset_state(bi, err, errlen)) return fail();
+    return b;
+}
+
+void xj_cuda_batch_free(xj_cuda_batch *b) {
+    if (!b) return;
+    BatchImpl *bi = &b->impl;
+    if (bi->s) {
+        DevGuard dg(I(bi->s)->dev);
+        if (bi->step_graph) cudaGraphExecDestroy(bi->step_graph);
+        cuda_destroy(bi->s);
+    }
+    delete b;
+}
+
+int xj_cuda_batch_reset(xj_cuda_batch *b, char *err, size_t errlen) {
+    if (!b) { seterr(err, errlen, "null batch"); return -1; }
+    DevGuard dg(I(b->impl.s)->dev);
+    return batch_reset_state(&b->impl, err, errlen);
+}
+
+int xj_cuda_batch_n_past(const xj_cuda_batch *b) { return b ? b->impl.n_past : -1; }
+
+int xj_cuda_batch_decode(xj_cuda_batch *b, const int32_t *prompts, int n_prompt, int n_gen, int32_t *out, float *margins,
+                         float *gpu_ms, char *err, size_t errlen) {
+    if (!b || !prompts || !out) { seterr(err, errlen, "null argument"); return -1; }
+    BatchImpl *bi = &b->impl;
+    xj_stage *s = bi->s;
+    Impl *im = I(s);
+    DevGuard dg(im->dev);
+    const int B = bi->B, E = s->m->hp.n_embd;
+    if (n_prompt <= 0 || n_gen <= 0) { seterr(err, errlen, "need at least one prompt token and one generated token"); return -1; }
+    if (bi->n_past + n_prompt + n_gen - 1 > bi->n_ctx) { seterr(err, errlen, "context is full (%d)", bi->n_ctx); return -1; }
+    if (n_gen > bi->out_cap) {
+        if (bi->step_graph) { cudaGraphExecDestroy(bi->step_graph); bi->step_graph = nullptr; }
+        const int cap = n_gen > 1024 ? n_gen : 1024;
+        if (dalloc(im, &bi->out_tok, (size_t)B * cap, err, errlen) || dalloc(im, &bi->margin, (size_t)B * cap, err, errlen)) return -1;
+        bi->out_cap = cap;
+    }
+    if (n_prompt > bi->prompt_cap) {
+        if (dalloc(im, &bi->prompts, (size_t)B * n_prompt, err, errlen)) return -1;
+        bi->prompt_cap = n_prompt;
+    }
+    // prompts [B][n_prompt] -> device [n_prompt][B]: the tokens of step i are contiguous (the pageable
+    // source is consumed before the call returns; the copy is ordered on the stage stream)
+    std::vector<int32_t> tp((size_t)B * n_prompt);
+    for (int bq = 0; bq < B; bq++)
+        for (int i = 0; i < n_prompt; i++) tp[(size_t)i * B + bq] = prompts[(size_t)bq * n_prompt + i];
+    CK(cudaMemcpyAsync(bi->prompts, tp.data(), tp.size() * sizeof(int32_t), cudaMemcpyHostToDevice, im->st));
+    CK(cudaMemsetAsync(bi->step, 0, sizeof(int) * B, im->st));
+    CK(cudaEventRecord(im->ev[0], im->st));
+    const long long nl0 = im->nlaunch;
+    for (int i = 0; i < n_prompt; i++) {
+        launch(im, k_embed, dim3((E / 8 + 127) / 128, B), dim3(128), 0, im->tok_embd, (const int32_t *)(bi->prompts + (size_t)i * B), B,
+               im->x, E);
+        run_layers_batch(bi);
+        if (i + 1 < n_prompt) launch(im, k_advance_batch, dim3(1), dim3(256), 0, bi->npast, B, 1);
+        else head_batch(bi);   // out[:, 0], its embedding into x, position + 1
+    }
+    CK(cudaEventRecord(im->ev[1], im->st));
+    bi->last_launches[0] = im->nlaunch - nl0;
+    bi->last_launches[1] = 0;
+    if (n_gen > 1) {
+        if (!bi->step_graph) {
+            cudaGraph_t g;
+            CK(cudaStreamBeginCapture(im->st, cudaStreamCaptureModeThreadLocal));
+            run_layers_batch(bi);
+            head_batch(bi);
+            CK(cudaStreamEndCapture(im->st, &g));
+            bi->step_kernels = count_kernels(g);
+            cudaError_t e = cudaGraphInstantiate(&bi->step_graph, g, 0);
+            cudaGraphDestroy(g);
+            if (e != cudaSuccess) { seterr(err, errlen, "graph instantiate: %s", cudaGetErrorString(e)); bi->step_graph = nullptr; return -1; }
+        }
+        for (int i = 1; i < n_gen; i++) CK(cudaGraphLaunch(bi->step_graph, im->st));
+        bi->last_launches[1] = (long long)(n_gen - 1) * bi->step_kernels;
+    }
+    CK(cudaEventRecord(im->ev[2], im->st));
+    CK(cudaMemcpy2DAsync(out, sizeof(int32_t) * n_gen, bi->out_tok, sizeof(int32_t) * bi->out_cap, sizeof(int32_t) * n_gen, B,
+                         cudaMemcpyDeviceToHost, im->st));
+    if (margins)
+        CK(cudaMemcpy2DAsync(margins, sizeof(float) * n_gen, bi->margin, sizeof(float) * bi->out_cap, sizeof(float) * n_gen, B,
+                             cudaMemcpyDeviceToHost, im->st));
+    if (sync_check(im, err, errlen)) return -1;
+    if (gpu_ms) {
+        cudaEventElapsedTime(&gpu_ms[0], im->ev[0], im->ev[1]);
+        cudaEventElapsedTime(&gpu_ms[1], im->ev[1], im->ev[2]);
+    }
+    bi->n_past += n_prompt + n_gen - 1;
+    return 0;
+}
+
+long long xj_cuda_batch_last_launches(const xj_cuda_batch *b, long long *launches) {
+    if (!b) return 0;
+    if (launches) { launches[0] = b->impl.last_launches[0]; launches[1] = b->impl.last_launches[1]; }
+    return b->impl.last_launches[0] + b->impl.last_launches[1];
 }
 
 }  // extern "C"

@@ -100,6 +100,12 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_graph_kernels": (ip, [vp]),
         "xj_cuda_last_decode_launches": (ctypes.c_longlong, [vp, vp]),
         "xj_cuda_phase_trace": (ip, [vp, vp, ip]),
+        "xj_cuda_batch_new": (vp, [vp, ip, ip, cp, sz]),
+        "xj_cuda_batch_free": (None, [vp]),
+        "xj_cuda_batch_reset": (ip, [vp, cp, sz]),
+        "xj_cuda_batch_n_past": (ip, [vp]),
+        "xj_cuda_batch_decode": (ip, [vp, vp, ip, ip, vp, vp, vp, cp, sz]),
+        "xj_cuda_batch_last_launches": (ctypes.c_longlong, [vp, vp]),
         "xj_cuda_gemv": (ip, [ip, vp, ip, ip, vp, ip, vp, ip, cp, sz]),
         "xj_cuda_gemv_time": (ip, [ip, vp, ip, ip, ip, ip, ip, ip, vp, cp, sz]),
         "xj_cuda_norm_gemv_noalloc": (ip, [ip, vp, ip, ip, vp, vp, ctypes.c_float, ip, vp, cp, sz]),
@@ -295,6 +301,56 @@ class Stage:
     def close(self):
         if self.p:
             self.s.destroy(self.addr)
+            self.p = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Batch:
+    """n_seq independent sequences decoded in lockstep on one GPU (xj_cuda_batch_*)."""
+
+    def __init__(self, model: Model, n_seq: int, n_ctx: int = 256):
+        e = _err()
+        p = lib().xj_cuda_batch_new(model.ptr, n_seq, n_ctx, e, 512)
+        if not p:
+            _raise(e)
+        self.model, self.p, self.n_seq = model, p, n_seq
+
+    @property
+    def n_past(self) -> int:
+        return int(lib().xj_cuda_batch_n_past(self.p))
+
+    def reset(self):
+        e = _err()
+        if lib().xj_cuda_batch_reset(self.p, e, 512):
+            _raise(e)
+
+    def decode(self, prompts, n_gen: int, want_margins: bool = False):
+        """prompts [n_seq][n_prompt] -> (ids [n_seq][n_gen], margins or None, gpu_ms[2])."""
+        p = np.ascontiguousarray(prompts, dtype=np.int32)
+        assert p.ndim == 2 and p.shape[0] == self.n_seq
+        out = np.zeros((self.n_seq, n_gen), np.int32)
+        mar = np.zeros((self.n_seq, n_gen), np.float32) if want_margins else None
+        ms = np.zeros(2, np.float32)
+        e = _err()
+        rc = lib().xj_cuda_batch_decode(self.p, p.ctypes.data, p.shape[1], n_gen, out.ctypes.data,
+                                        mar.ctypes.data if mar is not None else None, ms.ctypes.data, e, 512)
+        if rc:
+            _raise(e)
+        return out, mar, ms
+
+    def last_launches(self) -> tuple[int, int]:
+        v = (ctypes.c_longlong * 2)()
+        lib().xj_cuda_batch_last_launches(self.p, v)
+        return int(v[0]), int(v[1])
+
+    def close(self):
+        if self.p:
+            lib().xj_cuda_batch_free(self.p)
             self.p = None
 
     def __del__(self):
