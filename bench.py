@@ -182,6 +182,53 @@ def cpu_baseline(K_cap=24):
             "sample": f"{cfg.name}: 32-token prompt, {K_cap} greedy decode steps at batch 1 (oracle/_ref, {threads} threads)"}
 
 
+def run_batch(args, cfg, model, rank, world, barrier, xjcuda):
+    """Batched greedy decode: args.batch independent sequences per GPU in lockstep (xj_cuda_batch_*),
+    each with its own seeded prompt of args.prompt tokens; K timed steps = one token of every sequence."""
+    import torch
+    B = args.batch
+    n_ctx = args.prompt + max(args.warmup, 3) + 2 * args.steps + 16
+    bt = xjcuda.Batch(model, B, n_ctx)
+    P = np.random.default_rng(4321 + rank).integers(0, cfg.n_vocab, (B, args.prompt)).astype(np.int32)
+    toks, _, ms_pre = bt.decode(P, max(args.warmup, 3))          # prompt + warm-up steps (untimed)
+    last = toks[:, -1:]
+    pos0 = bt.n_past
+    barrier()
+    toks, _, ms = bt.decode(last, args.steps)
+    barrier()
+    dev_ms = float(ms[0] + ms[1])
+    launches = bt.last_launches()
+    last = toks[:, -1:]
+    barrier()
+    t0 = time.perf_counter()
+    bt.decode(last, args.steps)
+    torch.cuda.synchronize()
+    e2e_ms = (time.perf_counter() - t0) * 1e3
+    t_max, e2e_max = dev_ms, e2e_ms
+    if world > 1:
+        import torch.distributed as dist
+        t = torch.tensor([dev_ms, e2e_ms], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        t_max, e2e_max = float(t[0]), float(t[1])
+    bt.close()
+    if rank != 0:
+        return None
+    b = step_bytes(cfg, pos0 + args.steps // 2)
+    step_total = b["weights"] + B * (b["kv"] + b["state"])
+    peak, peak_kind = hbm_peak()
+    achieved = step_total / (t_max / args.steps / 1e3) / 1e9
+    return {
+        "value": round(world * B * args.steps / (t_max / 1e3), 1), "unit": "tok/s", "sequences_per_gpu": B,
+        "ms_per_step": round(t_max / args.steps, 4), "steps": args.steps, "prompt": args.prompt,
+        "e2e": {"value": round(world * B * args.steps / (e2e_max / 1e3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": round(4 * B / args.steps, 3), "d2h_bytes_per_step": 4 * B},
+        "roofline": {"bound": "hbm", "kernel": "decode-step CUDA graph (batched)", "achieved": round(achieved, 1),
+                     "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
+                     "bytes_per_step": round(step_total), "peak_kind": peak_kind},
+        "gpu_launches": int(sum(launches)), "prompt_ms": round(float(ms_pre[0]), 1),
+    }
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -190,6 +237,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--batch", type=int, default=64, help="sequences of the batched-decode measurement (0: skip)")
     args = ap.parse_args()
     rank, local, world = dist_env()
     load_pkg()
@@ -245,6 +293,8 @@ def main():
         t_max, e2e_max = float(t[0]), float(t[1])
     value = world * args.steps / (t_max / 1e3)
     e2e = world * args.steps / (e2e_max / 1e3)
+    stage.close()
+    batch_line = run_batch(args, cfg, model, rank, world, barrier, xjcuda) if args.batch > 0 else None
     if rank == 0:
         peak, peak_kind = hbm_peak()
         b = step_bytes(cfg, pos0 + args.steps // 2)
@@ -272,10 +322,11 @@ def main():
             "gpu_launches": int(sum(launches)),
             "tokens_check": int(toks[0]),
         }
+        if batch_line:
+            line["batch"] = batch_line
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line))
-    stage.close()
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()

@@ -36,6 +36,7 @@
 namespace xjk {
 
 constexpr int MMA_MAXT = 4;
+constexpr int MMA_WIDE_T = 16;    // tokens of a wide launch (k_gemv_wide: 4 n-tiles per decoded fragment)
 constexpr int MMA_WARPS = 16;
 constexpr int MMA_KMAX_PT = 12;   // prologue elements per thread: K <= 12 * 512
 
@@ -687,10 +688,292 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, NT == 1 ? 2 : 1) k_gemv_mma(Mm
     }
 }
 
+// ------------------------------------------------------------------ wide launches (5..16 tokens)
+// Activations for a wide launch are prepared once per GEMV by k_prep_x (one block per token, the same
+// arithmetic as k_gemv_mma's prologue: identical hi/lo values, block sums and range scales) into a
+// global buffer laid out as k_gemv_mma stages them: per token, columns hi and lo of xstride = K + 16
+// halves (bperm order within each 16), then the 32-wide block sums, then the range scales.
+struct WideX {
+    __half *cols;        // [T][2][xstride]
+    float *xsum;         // [T][sstride]: K/32 block sums, rows padded to 16 bytes (bulk-copy granularity)
+    float *scale;        // [T]
+    int sstride;
+};
+__host__ __device__ inline int wide_sstride(int K) { return (K / 32 + 3) & ~3; }
+inline size_t wide_x_bytes(int T, int K) {
+    return ((size_t)T * 2 * (K + 16) * 2 + 255) / 256 * 256 + ((size_t)T * wide_sstride(K) * 4 + 255) / 256 * 256 + 256;
+}
+__host__ __device__ inline WideX wide_x_of(void *buf, int T, int K) {
+    WideX w;
+    uint8_t *p = (uint8_t *)buf;
+    w.cols = (__half *)p;
+    p += ((size_t)T * 2 * (K + 16) * 2 + 255) / 256 * 256;
+    w.xsum = (float *)p;
+    w.sstride = wide_sstride(K);
+    p += ((size_t)T * w.sstride * 4 + 255) / 256 * 256;
+    w.scale = (float *)p;
+    return w;
+}
+
+// Grid T, MMA_WARPS*32 threads: f(x[t]) -> range scale -> hi/lo columns + block sums of token t.
+static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_x(const float *x, const float *x2, long long ldx, int K, int pro,
+                                                                  const float *norm_w, float eps, void *buf, int T) {
+    griddep_wait();
+    __shared__ float pred[MMA_WARPS][2];
+    __shared__ float s_scale, s_nsc;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = blockIdx.x;
+    const WideX W = wide_x_of(buf, T, K);
+    const int xstride = K + 16;
+    constexpr int XPT = MMA_KMAX_PT;
+    const float *xr = x + t * ldx;
+    float v[XPT];
+    float ss = 0.0f, am = 0.0f;
+#pragma unroll
+    for (int k = 0; k < XPT; k++) {
+        const int i = tid + k * MMA_WARPS * 32;
+        float val = 0.0f;
+        if (i < K) {
+            const float xv = xr[i];
+            if (pro == PRO_NORM) { ss = fmaf(xv, xv, ss); val = xv * norm_w[i]; }
+            else if (pro == PRO_SWIGLU) val = silu_f(xv) * x2[t * ldx + i];
+            else val = xv;
+            v[k] = pro == PRO_NORM ? xv : val;
+        }
+        am = fmaxf(am, fabsf(val));
+    }
+    ss = warp_sum(ss);
+    am = warp_max(am);
+    if (lane == 0) { pred[warp][0] = ss; pred[warp][1] = am; }
+    __syncthreads();
+    if (tid == 0) {
+        double tss = 0;
+        float tam = 0.0f;
+        for (int w = 0; w < MMA_WARPS; w++) { tss += pred[w][0]; tam = fmaxf(tam, pred[w][1]); }
+        float nsc = 1.0f;
+        if (pro == PRO_NORM) nsc = 1.0f / sqrtf((float)(tss / K) + eps);
+        const float m = tam * nsc;
+        s_nsc = nsc;
+        s_scale = ldexpf(1.0f, 14 - (m > 0.0f ? ilogbf(m) : 0));
+        W.scale[t] = s_scale;
+    }
+    __syncthreads();
+    const float sc = s_scale, nsc = s_nsc;
+    __half *col_hi = W.cols + (size_t)(2 * t) * xstride, *col_lo = W.cols + (size_t)(2 * t + 1) * xstride;
+#pragma unroll
+    for (int k = 0; k < XPT; k++) {
+        const int i = tid + k * MMA_WARPS * 32;
+        if (i < K) {
+            const float val = (pro == PRO_NORM ? (v[k] * nsc) * norm_w[i] : v[k]) * sc;
+            const __half hi = __float2half_rn(val);
+            const __half lo = __float2half_rn(val - __half2float(hi));
+            const int pos = (i & ~15) + bperm(i & 15);
+            col_hi[pos] = hi;
+            col_lo[pos] = lo;
+            const float bs = warp_sum(__half2float(hi) + __half2float(lo));
+            if (lane == 0) W.xsum[t * W.sstride + (i >> 5)] = bs;
+        }
+    }
+}
+
+constexpr int WIDE_SLICE = 2048;          // largest K per staged activation slice (one chunk of units)
+constexpr int WIDE_MAXTILES = 4;          // tiles a CTA may own when a tile spans several slices
+struct WideSmem {
+    size_t off_ring, off_xs, off_sum, off_sc, off_red, bytes;
+    int xstride;
+    __host__ __device__ WideSmem(int ring_bytes) {
+        xstride = WIDE_SLICE + 16;
+        off_ring = 0;
+        off_xs = (size_t)ring_bytes;
+        off_sum = off_xs + (size_t)2 * MMA_WIDE_T * xstride * 2;
+        off_sc = off_sum + (size_t)MMA_WIDE_T * (WIDE_SLICE / 32) * 4;
+        off_red = off_sc + (size_t)MMA_WARPS * 128 * 4;
+        bytes = off_red + (size_t)MMA_WARPS * 16 * MMA_WIDE_T * 4 + 64;
+    }
+};
+
+// 5..16 tokens: each CTA owns a contiguous range of tiles; the activations arrive one K-slice at a
+// time (bulk copies of the prepared columns), the weights through the same chunk ring as k_gemv_mma in
+// slice-major order; each tile's partial rows are carried across slices in registers, so a tile's
+// arithmetic is k_gemv_mma's (same units in the same order per warp, same fixed-order epilogue).
+template <int TYPE>
+__global__ void __launch_bounds__(MMA_WARPS * 32, 1) k_gemv_wide(MmaArgs a, const void *xbuf) {
+    using G = Geo<TYPE>;
+    constexpr int SB = stage_bytes<TYPE>(), NS = G::STAGES, NT = MMA_WIDE_T / 4, TMAX = MMA_WIDE_T;
+    constexpr bool KQ = TYPE != XJ_Q8_0;
+    constexpr int USL = G::CU;                                  // units per slice: one chunk
+    constexpr int SLK = USL * (TYPE == XJ_Q8_0 ? 32 : 256);     // K per slice
+    static_assert(SLK <= WIDE_SLICE, "slice fits the staging area");
+    extern __shared__ __align__(128) uint8_t smem[];
+    const WideSmem L(SB * NS);
+    uint8_t *ring = smem + L.off_ring;
+    __half *xs = reinterpret_cast<__half *>(smem + L.off_xs);
+    float *xsum = reinterpret_cast<float *>(smem + L.off_sum);
+    float *scs = reinterpret_cast<float *>(smem + L.off_sc);
+    float *red = reinterpret_cast<float *>(smem + L.off_red);
+    __shared__ __align__(8) uint64_t bars[NS];
+    __shared__ __align__(8) uint64_t xbar;
+    __shared__ float tok_scale[TMAX];
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+    const int T = a.T, K = a.K;
+    const WideX X = wide_x_of(const_cast<void *>(xbuf), T, K);
+    const int total = a.tile_start[a.njob];
+    const int ta = blockIdx.x * a.tiles_per_cta;
+    const int tb = ta + a.tiles_per_cta < total ? ta + a.tiles_per_cta : total;
+    const int ntl = tb - ta;
+    const int nu = a.job[0].w.nu;
+    const int nsl = (nu + USL - 1) / USL;                   // slices (chunks per tile)
+    const int nchunks = ntl * nsl;
+    // chunk i (slice-major: i = s * ntl + tile) -> (job, tile, first unit, units)
+    auto chunk_of = [&](int i, int &j, int &tile, int &u0, int &cu) {
+        const int s = i / ntl, tg = ta + i % ntl;
+        j = 0;
+        while (tg >= a.tile_start[j + 1]) j++;
+        tile = tg - a.tile_start[j];
+        u0 = s * USL;
+        cu = nu - u0 < USL ? nu - u0 : USL;
+    };
+    auto issue = [&](int i) {
+        int j, tile, u0, cu;
+        chunk_of(i, j, tile, u0, cu);
+        const Tiled &W = a.job[j].w;
+        uint8_t *st = ring + (size_t)(i % NS) * SB;
+        uint64_t *bar = &bars[i % NS];
+        const size_t tu0 = (size_t)tile * nu + u0;
+        mbar_expect_tx(bar, (uint32_t)(cu * unit_bytes<TYPE>()));
+        bulk_g2s(st, W.q + tu0 * G::QB, cu * G::QB, bar);
+        if (G::HB) bulk_g2s(st + G::CU * G::QB, W.h + tu0 * G::HB, cu * G::HB, bar);
+        if (G::SB) bulk_g2s(st + G::CU * (G::QB + G::HB), W.s + tu0 * G::SB, cu * G::SB, bar);
+        if (G::DB) bulk_g2s(st + G::CU * (G::QB + G::HB + G::SB), W.d + tu0 * G::DB, cu * G::DB, bar);
+    };
+    if (tid == 0) {
+        for (int q = 0; q < NS; q++) mbar_init(&bars[q], 1);
+        mbar_init(&xbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        for (int i = 0; i < NS && i < nchunks; i++) issue(i);
+    }
+    griddep_launch();
+    griddep_wait();
+    if (tid < T) tok_scale[tid] = X.scale[tid];
+    const __half *xb = xs + (size_t)g * L.xstride + 4 * c;
+    float *scw = scs + warp * 128;
+    float yg[WIDE_MAXTILES][NT], yg8[WIDE_MAXTILES][NT];
+#pragma unroll
+    for (int q = 0; q < WIDE_MAXTILES; q++)
+#pragma unroll
+        for (int n = 0; n < NT; n++) { yg[q][n] = 0.0f; yg8[q][n] = 0.0f; }
+    for (int sl = 0; sl < nsl; sl++) {
+        // ---- activation slice sl of every token (columns hi, lo; block sums)
+        const int k0 = sl * SLK, kl = K - k0 < SLK ? K - k0 : SLK;
+        __syncthreads();                                   // the previous slice is no longer read
+        if (tid == 0) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            const int nb4 = ((kl / 32) + 3) & ~3;              // block sums copied, rounded up to 16 bytes
+            mbar_expect_tx(&xbar, (uint32_t)(2 * T * kl * 2 + T * nb4 * 4));
+            for (int col = 0; col < 2 * T; col++)
+                bulk_g2s(xs + (size_t)col * L.xstride, X.cols + (size_t)col * (K + 16) + k0, kl * 2, &xbar);
+            for (int t = 0; t < T; t++)
+                bulk_g2s(xsum + t * (WIDE_SLICE / 32), X.xsum + (size_t)t * X.sstride + k0 / 32, nb4 * 4, &xbar);
+        }
+        mbar_wait(&xbar, (uint32_t)(sl & 1), a.err);
+        for (int tl = 0; tl < ntl; tl++) {
+            const int i = sl * ntl + tl;
+            int j, tile, u0, cu;
+            chunk_of(i, j, tile, u0, cu);
+            mbar_wait(&bars[i % NS], (uint32_t)((i / NS) & 1), a.err);
+            const uint8_t *st = ring + (size_t)(i % NS) * SB;
+            float zg[NT], zg8[NT];
+            const int q = nsl > 1 ? tl : 0;                 // carried accumulators when a tile spans slices
+#pragma unroll
+            for (int n = 0; n < NT; n++) { zg[n] = yg[q][n]; zg8[n] = yg8[q][n]; }
+            if (KQ) {
+                const int ui = warp >> 1;
+                if (ui < cu) unit_compute_n<TYPE, NT>(st, ui, ui, warp & 1, lane, T, xb, L.xstride, xsum, WIDE_SLICE / 32, scw, zg, zg8);
+            } else {
+#pragma unroll
+                for (int k = 0; k < G::CU / MMA_WARPS; k++) {
+                    const int ui = warp + k * MMA_WARPS;
+                    if (ui < cu) unit_compute_n<TYPE, NT>(st, ui, ui, 0, lane, T, xb, L.xstride, xsum, WIDE_SLICE / 32, scw, zg, zg8);
+                }
+            }
+            __syncthreads();                               // the stage is free
+            if (tid == 0 && i + NS < nchunks) {
+                asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+                issue(i + NS);
+            }
+            if (sl < nsl - 1) {
+#pragma unroll
+                for (int n = 0; n < NT; n++) { yg[q][n] = zg[n]; yg8[q][n] = zg8[n]; }
+                continue;
+            }
+            // ---- last slice of the tile: fixed-order sum over warps, epilogue
+#pragma unroll
+            for (int n = 0; n < NT; n++) {
+                red[(warp * 16 + g) * TMAX + 4 * n + c] = zg[n];
+                red[(warp * 16 + g + 8) * TMAX + 4 * n + c] = zg8[n];
+                yg[q][n] = 0.0f; yg8[q][n] = 0.0f;
+            }
+            __syncthreads();
+            const MmaJob &jb = a.job[j];
+            if (jb.epi == EPI_CONV && jb.conv_bstride) {
+                if (tid < 16 && tile * 16 + tid < jb.w.N) {
+                    const int ch = tile * 16 + tid, kc = jb.kc;
+                    const float *wc = jb.conv_w + (size_t)ch * kc;
+                    for (int t = 0; t < T; t++) {
+                        float *stt = jb.conv_state + t * jb.conv_bstride + (size_t)ch * (kc - 1);
+                        float cs[8];
+                        for (int k = 0; k < kc - 1; k++) cs[k] = stt[k];
+                        float sv = 0.0f;
+#pragma unroll
+                        for (int w = 0; w < MMA_WARPS; w++) sv += red[(w * 16 + tid) * TMAX + t];
+                        sv /= tok_scale[t];
+                        float acc = 0.0f;
+                        for (int k = 0; k < kc - 1; k++) acc = fmaf(cs[k], wc[k], acc);
+                        acc = fmaf(sv, wc[kc - 1], acc);
+                        for (int k = 0; k < kc - 2; k++) stt[k] = cs[k + 1];
+                        stt[kc - 2] = sv;
+                        jb.y[t * jb.ldy + ch] = silu_f(acc);
+                    }
+                }
+            } else if (jb.epi == EPI_CONV) {
+                if (tid < 16 && tile * 16 + tid < jb.w.N) {
+                    const int ch = tile * 16 + tid, kc = jb.kc;
+                    float cs[8];
+                    for (int k = 0; k < kc - 1; k++) cs[k] = jb.conv_state[(size_t)ch * (kc - 1) + k];
+                    const float *wc = jb.conv_w + (size_t)ch * kc;
+                    for (int t = 0; t < T; t++) {
+                        float sv = 0.0f;
+#pragma unroll
+                        for (int w = 0; w < MMA_WARPS; w++) sv += red[(w * 16 + tid) * TMAX + t];
+                        sv /= tok_scale[t];
+                        float acc = 0.0f;
+                        for (int k = 0; k < kc - 1; k++) acc = fmaf(cs[k], wc[k], acc);
+                        acc = fmaf(sv, wc[kc - 1], acc);
+                        for (int k = 0; k < kc - 2; k++) cs[k] = cs[k + 1];
+                        cs[kc - 2] = sv;
+                        jb.y[t * jb.ldy + ch] = silu_f(acc);
+                        if (jb.conv_ck && t < T - 1)
+                            for (int k = 0; k < kc - 1; k++) jb.conv_ck[((size_t)t * jb.w.N + ch) * (kc - 1) + k] = cs[k];
+                    }
+                    for (int k = 0; k < kc - 1; k++) jb.conv_state[(size_t)ch * (kc - 1) + k] = cs[k];
+                }
+            } else if (tid < 16 * TMAX) {
+                const int row = tid / TMAX, t = tid % TMAX;
+                if (t < T && tile * 16 + row < jb.w.N) {
+                    float sv = 0.0f;
+#pragma unroll
+                    for (int w = 0; w < MMA_WARPS; w++) sv += red[(w * 16 + row) * TMAX + t];
+                    sv /= tok_scale[t];
+                    float *yp = jb.y + t * jb.ldy + (size_t)tile * 16 + row;
+                    *yp = jb.epi == EPI_ADD ? *yp + sv : sv;
+                }
+            }
+            __syncthreads();   // red is reused by the next tile
+        }
+    }
+}
+
 // ------------------------------------------------------------------ host: launch
 constexpr size_t MMA_SMEM_MAX = 200 * 1024;              // 4-token launches
-constexpr size_t MMA_SMEM_MAX_WIDE = 222 * 1024;         // 16-token launches (one CTA per SM)
-constexpr int MMA_WIDE_T = 16;                           // tokens of a wide launch (NT = 4 n-tiles)
 constexpr int MMA_KMAX = MMA_KMAX_PT * MMA_WARPS * 32;   // longest row the prologue stages
 
 inline int ring_bytes(int type) {
@@ -702,8 +985,7 @@ inline int ring_bytes(int type) {
 }
 inline size_t mma_smem_bytes(int type, int T, int K, int tmax = MMA_MAXT) { return MmaSmem(T, K, ring_bytes(type), tmax).bytes; }
 
-// Whether a 16-token launch fits for this weight type and row length (its activations are staged whole).
-inline bool wide_ok(int type, int K) { return mma_smem_bytes(type, MMA_WIDE_T, K, MMA_WIDE_T) <= MMA_SMEM_MAX_WIDE; }
+
 
 // Matrices the tensor-core path can take (at up to MMA_MAXT tokens).
 inline bool tiled_ok(int type, int K, int N) {
@@ -744,16 +1026,14 @@ inline int mma_setup() {
     cudaGetDevice(&dev);
     if (dev < 0 || dev >= MAXDEV) dev = 0;
     if (!sms[dev]) {
-        cudaFuncSetAttribute(k_gemv_mma<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             (int)(NT == 1 ? MMA_SMEM_MAX : MMA_SMEM_MAX_WIDE));
+        cudaFuncSetAttribute(k_gemv_mma<TYPE, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MMA_SMEM_MAX);
         cudaDeviceGetAttribute(&sms[dev], cudaDevAttrMultiProcessorCount, dev);
     }
     return sms[dev];
 }
 
-// One launch for up to 4 same-type matrices sharing the input x[T][K]: T <= 4 with up to
-// g_mma_ctas_per_sm CTAs per SM, or 4 < T <= 16 (wide: four n-tiles per decoded weight fragment) with
-// one CTA per SM; each CTA owns a contiguous, balanced range of tiles.
+// One launch for up to 4 same-type matrices sharing the input x[T][K], T <= 4: up to
+// g_mma_ctas_per_sm CTAs per SM, each owning a contiguous, balanced range of tiles.
 template <int TYPE, int NT>
 inline cudaError_t launch_mma_nt(MmaArgs a, cudaStream_t st) {
     const int sms = mma_setup<TYPE, NT>() * (NT == 1 ? g_mma_ctas_per_sm : 1);
@@ -766,8 +1046,37 @@ inline cudaError_t launch_mma_nt(MmaArgs a, cudaStream_t st) {
 template <int TYPE>
 inline cudaError_t launch_mma_t(MmaArgs a, cudaStream_t st) {
     if (a.T <= MMA_MAXT) return launch_mma_nt<TYPE, 1>(a, st);
-    if (a.T <= MMA_WIDE_T && wide_ok(TYPE, a.K)) return launch_mma_nt<TYPE, 4>(a, st);
-    return cudaErrorInvalidValue;
+    return cudaErrorInvalidValue;   // 5..16 tokens: launch_wide
+}
+
+// Wide launch (5..16 tokens) on activations prepared by k_prep_x into xbuf.
+template <int TYPE>
+inline cudaError_t launch_wide_t(MmaArgs a, const void *xbuf, cudaStream_t st) {
+    constexpr int MAXDEV = 64;
+    static int sms_dev[MAXDEV] = {0};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= MAXDEV) dev = 0;
+    const size_t smem = WideSmem(ring_bytes(TYPE)).bytes;
+    if (!sms_dev[dev]) {
+        cudaFuncSetAttribute(k_gemv_wide<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaDeviceGetAttribute(&sms_dev[dev], cudaDevAttrMultiProcessorCount, dev);
+    }
+    const int tiles = a.tile_start[a.njob];
+    const int cu = Geo<TYPE>::CU, nsl = (a.job[0].w.nu + cu - 1) / cu;
+    const int ctas = tiles < sms_dev[dev] ? tiles : sms_dev[dev];
+    a.tiles_per_cta = (tiles + ctas - 1) / ctas;
+    if (nsl > 1 && a.tiles_per_cta > WIDE_MAXTILES) a.tiles_per_cta = WIDE_MAXTILES;   // carried accumulators
+    const dim3 grid((tiles + a.tiles_per_cta - 1) / a.tiles_per_cta), block(MMA_WARPS * 32);
+    return launch_pdl(k_gemv_wide<TYPE>, grid, block, smem, st, a, xbuf);
+}
+inline cudaError_t launch_wide(const MmaArgs &a, int type, const void *xbuf, cudaStream_t st) {
+    switch (type) {
+    case XJ_Q4_K: return launch_wide_t<XJ_Q4_K>(a, xbuf, st);
+    case XJ_Q6_K: return launch_wide_t<XJ_Q6_K>(a, xbuf, st);
+    case XJ_Q8_0: return launch_wide_t<XJ_Q8_0>(a, xbuf, st);
+    default: return cudaErrorInvalidValue;
+    }
 }
 
 inline cudaError_t launch_mma(const MmaArgs &a, int type, cudaStream_t st) {

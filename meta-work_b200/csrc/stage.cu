@@ -72,6 +72,7 @@ struct Impl {
     float *x = nullptr, *xin = nullptr, *h = nullptr, *qkvb = nullptr, *z = nullptr, *beta = nullptr, *alpha = nullptr;
     float *o = nullptr, *qrot = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
     float *q = nullptr, *k = nullptr, *v = nullptr, *hn = nullptr;
+    void *wide_buf = nullptr;   // activations of a wide (5..16-token) GEMV launch, prepared by k_prep_x
     float *pbest = nullptr, *psecond = nullptr;
     int *pidx = nullptr;
     int *derr = nullptr;       // device error word: set when a kernel's bounded wait gives up
@@ -213,6 +214,9 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
         if (j.w.tq && !(j.epi == EPI_ARGMAX && T != 1)) fast.push_back(j);
         else slow.push_back(j);
     }
+    // group the fast matrices by weight type (one launch per group, at most 4 matrices each)
+    std::vector<MmaArgs> groups;
+    std::vector<int> gtype;
     std::vector<char> done(fast.size(), 0);
     for (size_t i = 0; i < fast.size(); i++) {
         if (done[i]) continue;
@@ -232,31 +236,43 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
             m.njob++;
             done[k] = 1;
         }
-        // tokens in chunks of 16 (wide launches) or 4; each token's result does not depend on the
-        // chunking (the conv epilogue carries its state across chunks, its checkpoints are indexed by
-        // absolute token)
-        const int tch = T > MMA_MAXT && wide_ok(type, K) ? MMA_WIDE_T : MMA_MAXT;
-        for (int t0 = 0; t0 < T; t0 += tch) {
+        groups.push_back(m);
+        gtype.push_back(type);
+    }
+    // tokens in chunks of 16 (wide launches on activations prepared once per chunk) or, for 4 tokens or
+    // fewer, one launch; each token's result does not depend on the chunking (the conv epilogue carries
+    // its state across chunks, its checkpoints are indexed by absolute token)
+    const int tch = T > MMA_MAXT ? MMA_WIDE_T : MMA_MAXT;
+    for (int t0 = 0; t0 < T; t0 += tch) {
+        const int Tc = T - t0 < tch ? T - t0 : tch;
+        const bool wide = Tc > MMA_MAXT;
+        if (wide && !groups.empty()) {
+            launch(im, k_prep_x, dim3(Tc), dim3(MMA_WARPS * 32), 0, (const float *)(x + t0 * ldx),
+                   (const float *)(x2 ? x2 + t0 * ldx : nullptr), ldx, K, pro, norm_w, eps, im->wide_buf, Tc);
+        }
+        for (size_t gi = 0; gi < groups.size(); gi++) {
+            const MmaArgs &m = groups[gi];
             MmaArgs c = m;
-            c.T = T - t0 < tch ? T - t0 : tch;
+            c.T = Tc;
             c.x = x + t0 * ldx;
             c.x2 = x2 ? x2 + t0 * ldx : nullptr;
             for (int j = 0; j < c.njob; j++) {
                 if (c.job[j].y) c.job[j].y = m.job[j].y + t0 * m.job[j].ldy;
                 if (c.job[j].conv_bstride) c.job[j].conv_state = m.job[j].conv_state + t0 * m.job[j].conv_bstride;
                 if (c.job[j].conv_ck) {
-                    // the chunk saves the states after its tokens t0..t0+c.T-2; the one after t0+c.T-1
+                    // the chunk saves the states after its tokens t0..t0+Tc-2; the one after t0+Tc-1
                     // (when that is not the last token) is saved by the next chunk as its "previous" state
                     c.job[j].conv_ck = m.job[j].conv_ck + (size_t)t0 * m.job[j].w.N * (m.job[j].kc - 1);
                 }
             }
-            launch_mma(c, type, im->st);
+            if (wide) launch_wide(c, gtype[gi], im->wide_buf, im->st);
+            else launch_mma(c, gtype[gi], im->st);
             im->nlaunch++;
             for (int j = 0; j < c.njob; j++)
-                if (m.job[j].conv_ck && !m.job[j].conv_bstride && t0 + c.T < T) {
-                    // state after token t0+c.T-1 = current conv state: copy it into its checkpoint slot
+                if (m.job[j].conv_ck && !m.job[j].conv_bstride && t0 + Tc < T) {
+                    // state after token t0+Tc-1 = current conv state: copy it into its checkpoint slot
                     const size_t n = (size_t)m.job[j].w.N * (m.job[j].kc - 1);
-                    cudaMemcpyAsync(m.job[j].conv_ck + (size_t)(t0 + c.T - 1) * n, m.job[j].conv_state, n * 4,
+                    cudaMemcpyAsync(m.job[j].conv_ck + (size_t)(t0 + Tc - 1) * n, m.job[j].conv_state, n * 4,
                                     cudaMemcpyDeviceToDevice, im->st);
                 }
         }
@@ -630,6 +646,7 @@ int build(xj_stage *s, char *err, size_t errlen) {
         dalloc(im, &im->u, sf, err, errlen) || dalloc(im, &im->q, sf, err, errlen) || dalloc(im, &im->k, sf, err, errlen) ||
         dalloc(im, &im->v, sf, err, errlen) || dalloc(im, &im->logits, V * (size_t)B, err, errlen) ||
         dalloc(im, &im->hn, sf, err, errlen) ||
+        dalloc(im, (uint8_t **)&im->wide_buf, wide_x_bytes(MMA_WIDE_T, MMA_KMAX), err, errlen) ||
         dalloc(im, &im->npast, 4, err, errlen) || dalloc(im, &im->step, 4, err, errlen) ||
         dalloc(im, &im->derr, 4, err, errlen) ||
         dalloc(im, &im->tok, (size_t)B, err, errlen) || dalloc(im, &im->cur, 4, err, errlen)) return -1;
@@ -1126,7 +1143,8 @@ static int gemv_diag(int type, const void *w, int k, int n, const float *x, int 
         }
     }
     if (dalloc(im, &dx, (size_t)t * k, err, errlen) || dalloc(im, &dy, (size_t)t * n, err, errlen) ||
-        dalloc(im, &im->hn, (size_t)t * k, err, errlen) || dalloc(im, &im->derr, 1, err, errlen)) goto done;
+        dalloc(im, &im->hn, (size_t)t * k, err, errlen) || dalloc(im, &im->derr, 1, err, errlen) ||
+        dalloc(im, (uint8_t **)&im->wide_buf, wide_x_bytes(MMA_WIDE_T, MMA_KMAX), err, errlen)) goto done;
     cudaMemset(im->derr, 0, sizeof(int));
     if (cudaMemcpy(dx, x, sizeof(float) * (size_t)t * k, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) { seterr(err, errlen, "copy failed"); goto done; }
