@@ -229,6 +229,57 @@ def run_batch(args, cfg, model, rank, world, barrier, xjcuda):
     }
 
 
+def run_pipeline(args, rank, local, world):
+    """Layer pipeline over the ranks (rank r holds layers split_layers(L, world)[r], the last the head):
+    --batch sequences in --micro-batches groups, greedy decode; device-timed per step, max over ranks."""
+    import datetime
+    import torch
+    import torch.distributed as dist
+    from xjb200 import pipeline as pl, synth, xjcuda
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    gx, gt = dist.new_group(list(range(world))), dist.new_group(list(range(world)))
+    cfg = synth.CONFIG3
+    model = xjcuda.Model(synth.cached_gguf(cfg, os.environ.get("XJ_MODEL_DIR", f"/tmp/xj_models_r{local}")))
+    B = max(args.batch, 1)
+    n_ctx = args.prompt + 2 * args.steps + 16
+    l0, l1 = pl.split_layers(model.n_layer, world)[rank]
+    st = pl.CudaStage(model, l0, l1, rank == world - 1, B, n_ctx, dev)
+    p = pl.Pipeline(st, rank, world, B, args.micro_batches, gx, gt)
+    prompts = np.random.default_rng(4321).integers(0, cfg.n_vocab, (B, args.prompt)).astype(np.int32)
+    p.decode(prompts if rank == 0 else None, max(args.warmup, 3))          # prompt + warm-up (untimed)
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    ids = None
+    for i in range(args.steps):                                            # K steps of every sequence
+        if rank == 0:
+            ids = ids if ids is not None else [p._ids_from(np.zeros(n, np.int32)) for (r0, n) in p.mbs]
+        got = p.step(ids, True)
+        if rank == 0:
+            ids = got
+    e1.record()
+    torch.cuda.synchronize()
+    dist.barrier()
+    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    st.close()
+    if rank == 0:
+        print(json.dumps({
+            "metric": "pipelined batched decode tok/s (config 3, Q4_K_M)", "value": round(B * args.steps / (ms / 1e3), 1),
+            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
+            "vs_baseline": None, "dtype": "q4_k/q6_k weights, f32 accumulate", "data": "synthetic",
+            "config": {"workload": f"{cfg.name} greedy decode, {B} sequences", "prompt": args.prompt,
+                       "parallelism": f"layer pipeline x{world}", "micro_batches": args.micro_batches,
+                       "layers": pl.split_layers(model.n_layer, world)},
+            "exchange_bytes_per_step": {"activations": int(B * cfg.n_embd * 4 * (world - 1)), "ids": 4 * B},
+        }))
+    dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -238,6 +289,9 @@ def main():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched-decode measurement (0: skip)")
+    ap.add_argument("--pipeline", action="store_true",
+                    help="under torchrun: one layer range per GPU (NCCL layer pipeline) on --batch sequences")
+    ap.add_argument("--micro-batches", type=int, default=2)
     args = ap.parse_args()
     rank, local, world = dist_env()
     load_pkg()
@@ -246,6 +300,8 @@ def main():
 
     import torch
     torch.cuda.set_device(local)
+    if args.pipeline:
+        return run_pipeline(args, rank, local, world)
     if world > 1:
         import datetime
         import torch.distributed as dist

@@ -118,6 +118,20 @@ int xj_cuda_batch_decode(xj_cuda_batch *b, const int32_t *prompts, int n_prompt,
 // the decode steps after them. Returns their sum.
 long long xj_cuda_batch_last_launches(const xj_cuda_batch *b, long long *launches);
 
+// Pipeline stages (layer pipeline across GPUs: each GPU holds a batch over its layer range [l0, l1),
+// the last one with the head). Device buffers belong to the batch's device; calls return after the work
+// is done. Rows [row0, row0+nrows) of the batch form a micro-batch; x_dev holds its nrows rows of
+// [n_embd] fp32 activations.
+xj_cuda_batch *xj_cuda_batch_new_range(const xj_model *m, int l0, int l1, bool has_head, int n_seq, int n_ctx, char *err,
+                                       size_t errlen);
+// x_dev[i] = embedding row of tok_dev[i] (batches whose range starts at layer 0).
+int xj_cuda_batch_embed_rows(xj_cuda_batch *b, const int32_t *tok_dev, float *x_dev, int nrows, char *err, size_t errlen);
+// The batch's layers on the micro-batch in place; each of its sequences advances one position.
+int xj_cuda_batch_forward_rows(xj_cuda_batch *b, float *x_dev, int row0, int nrows, char *err, size_t errlen);
+// Output norm, LM head and greedy pick of the micro-batch: tok_dev[i] = next id of sequence row0+i.
+int xj_cuda_batch_pick_rows(xj_cuda_batch *b, const float *x_dev, int row0, int nrows, int32_t *tok_dev, char *err,
+                            size_t errlen);
+
 // Capacity, in floats, of the fixed device scratch used by xj_cuda_norm_gemv_noalloc (256 KiB).
 #define XJC_NOALLOC_MAX_FLOATS 65536
 

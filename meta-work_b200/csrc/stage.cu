@@ -859,7 +859,7 @@ struct BatchImpl {
     int B = 0, n_ctx = 0, n_past = 0;
     std::vector<float *> ssm, conv;        // per layer: [B][h_v][s_v][s_k], [B][conv_dim][conv_k-1]
     std::vector<void *> kc, vc;            // per layer: [B][n_ctx][n_head_kv * head_dim]
-    int *npast = nullptr, *step = nullptr;
+    int *npast = nullptr, *step = nullptr, *np_scratch = nullptr;
     int32_t *cur = nullptr, *prompts = nullptr, *out_tok = nullptr;
     float *margin = nullptr, *pbest = nullptr, *psecond = nullptr;
     int *pidx = nullptr;
@@ -869,24 +869,26 @@ struct BatchImpl {
     long long last_launches[2] = {0, 0};
 };
 
-void run_layers_batch(BatchImpl *bi) {
+// Layers of the batch's stage on rows x[0..nr) = sequences r0..r0+nr-1 (their own states and positions).
+void run_layers_batch(BatchImpl *bi, float *x, int r0, int nr) {
     xj_stage *s = bi->s;
     Impl *im = I(s);
     const xj_hparams *hp = &s->m->hp;
-    const int E = hp->n_embd, FF = hp->n_ff, B = bi->B;
+    const int E = hp->n_embd, FF = hp->n_ff, B = nr;
     const float eps = hp->eps;
+    const int *npast = bi->npast + r0;
     for (int il = s->l0; il < s->l1; il++) {
         Layer &Ly = im->L[il - s->l0];
         const int li = il - s->l0;
         if (Ly.rec) {
             const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v;
             Job qkv{Ly.qkv, im->qkvb, CD};
-            qkv.epi = EPI_CONV; qkv.conv_state = bi->conv[li]; qkv.conv_w = Ly.conv_w; qkv.kc = hp->conv_k;
+            qkv.epi = EPI_CONV; qkv.conv_state = bi->conv[li] + (size_t)r0 * hp->conv_dim * (hp->conv_k - 1); qkv.conv_w = Ly.conv_w; qkv.kc = hp->conv_k;
             qkv.conv_bstride = (long long)CD * (hp->conv_k - 1);
-            gemv(im, im->x, nullptr, E, B, PRO_NORM, Ly.attn_norm, eps,
+            gemv(im, x, nullptr, E, B, PRO_NORM, Ly.attn_norm, eps,
                  {qkv, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
             GdnArgs g = gdn_args(im, hp, Ly, 1, false);
-            g.ssm = bi->ssm[li];
+            g.ssm = bi->ssm[li] + (size_t)r0 * hp->h_v * hp->s_v * hp->s_k;
             const long long ss = (long long)hp->h_v * hp->s_v * hp->s_k;
             switch (hp->s_k) {
             case 16: launch(im, k_gdn_batch<16>, dim3(Hv, B), dim3(64), 0, g, ss); break;
@@ -895,7 +897,7 @@ void run_layers_batch(BatchImpl *bi) {
             case 128: launch(im, k_gdn_batch<128>, dim3(Hv, B), dim3(512), 0, g, ss); break;
             default: launch(im, k_gdn_batch<256>, dim3(Hv, B), dim3(1024), 0, g, ss); break;
             }
-            Job out{Ly.out, im->x, E};
+            Job out{Ly.out, x, E};
             out.epi = EPI_ADD;
             gemv(im, im->o, nullptr, DI, B, PRO_NONE, nullptr, eps, {out});
         } else {
@@ -903,55 +905,58 @@ void run_layers_batch(BatchImpl *bi) {
             const float *q, *k, *v;
             long long ldq, ldkv;
             if (Ly.fused) {
-                gemv(im, im->x, nullptr, E, B, PRO_NORM, Ly.attn_norm, eps, {{Ly.wqkv, im->qkvb, nq + 2 * nk}});
+                gemv(im, x, nullptr, E, B, PRO_NORM, Ly.attn_norm, eps, {{Ly.wqkv, im->qkvb, nq + 2 * nk}});
                 q = im->qkvb; k = im->qkvb + nq; v = im->qkvb + nq + nk; ldq = ldkv = nq + 2 * nk;
             } else {
-                gemv(im, im->x, nullptr, E, B, PRO_NORM, Ly.attn_norm, eps,
+                gemv(im, x, nullptr, E, B, PRO_NORM, Ly.attn_norm, eps,
                      {{Ly.wq, im->q, nq}, {Ly.wk, im->k, nk}, {Ly.wv, im->v, nk}});
                 q = im->q; k = im->k; v = im->v; ldq = nq; ldkv = nk;
             }
             AttnArgs a = attn_args(im, hp, Ly, q, ldq, k, v, ldkv);
-            a.kc = bi->kc[li]; a.vc = bi->vc[li];
             const long long kvs = (long long)bi->n_ctx * nk;
+            const size_t kvoff = (size_t)r0 * kvs * (im->kv_f32 ? 4 : 2);
+            a.kc = (uint8_t *)bi->kc[li] + kvoff; a.vc = (uint8_t *)bi->vc[li] + kvoff;
             const int dpl = (D + 31) / 32;
             if (im->kv_f32) {
-                launch(im, k_attn_prep_batch<float>, dim3(H + Hkv, B), dim3((D + 31) / 32 * 32), 0, a, (const int *)bi->npast, kvs);
-                if (dpl == 1) launch(im, k_attn_batch<float, 1>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
-                else if (dpl == 2) launch(im, k_attn_batch<float, 2>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
-                else if (dpl <= 4) launch(im, k_attn_batch<float, 4>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
-                else launch(im, k_attn_batch<float, 8>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                launch(im, k_attn_prep_batch<float>, dim3(H + Hkv, B), dim3((D + 31) / 32 * 32), 0, a, npast, kvs);
+                if (dpl == 1) launch(im, k_attn_batch<float, 1>, dim3(H, B), dim3(128), 0, a, npast, kvs);
+                else if (dpl == 2) launch(im, k_attn_batch<float, 2>, dim3(H, B), dim3(128), 0, a, npast, kvs);
+                else if (dpl <= 4) launch(im, k_attn_batch<float, 4>, dim3(H, B), dim3(128), 0, a, npast, kvs);
+                else launch(im, k_attn_batch<float, 8>, dim3(H, B), dim3(128), 0, a, npast, kvs);
             } else {
-                launch(im, k_attn_prep_batch<__half>, dim3(H + Hkv, B), dim3((D + 31) / 32 * 32), 0, a, (const int *)bi->npast, kvs);
-                if (dpl == 1) launch(im, k_attn_batch<__half, 1>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
-                else if (dpl == 2) launch(im, k_attn_batch<__half, 2>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
-                else if (dpl <= 4) launch(im, k_attn_batch<__half, 4>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
-                else launch(im, k_attn_batch<__half, 8>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                launch(im, k_attn_prep_batch<__half>, dim3(H + Hkv, B), dim3((D + 31) / 32 * 32), 0, a, npast, kvs);
+                if (dpl == 1) launch(im, k_attn_batch<__half, 1>, dim3(H, B), dim3(128), 0, a, npast, kvs);
+                else if (dpl == 2) launch(im, k_attn_batch<__half, 2>, dim3(H, B), dim3(128), 0, a, npast, kvs);
+                else if (dpl <= 4) launch(im, k_attn_batch<__half, 4>, dim3(H, B), dim3(128), 0, a, npast, kvs);
+                else launch(im, k_attn_batch<__half, 8>, dim3(H, B), dim3(128), 0, a, npast, kvs);
             }
-            Job o{Ly.wo, im->x, E};
+            Job o{Ly.wo, x, E};
             o.epi = EPI_ADD;
             gemv(im, im->o, nullptr, (long long)H * D, B, PRO_NONE, nullptr, eps, {o});
         }
-        gemv(im, im->x, nullptr, E, B, PRO_NORM, Ly.post_norm, eps, {{Ly.ffn_gate, im->g, FF}, {Ly.ffn_up, im->u, FF}});
-        Job down{Ly.ffn_down, im->x, E};
+        gemv(im, x, nullptr, E, B, PRO_NORM, Ly.post_norm, eps, {{Ly.ffn_gate, im->g, FF}, {Ly.ffn_up, im->u, FF}});
+        Job down{Ly.ffn_down, x, E};
         down.epi = EPI_ADD;
         gemv(im, im->g, im->u, FF, B, PRO_SWIGLU, nullptr, eps, {down});
     }
 }
 
-// Output norm + LM head for all B rows, then each sequence's greedy pick: out_tok[b][step_b], the next
-// token's embedding into row b of x, position + 1.
-void head_batch(BatchImpl *bi) {
+// Output norm + LM head for rows x[0..nr) = sequences r0.., then each sequence's greedy pick: out_tok of
+// sequence r0+i at its step, the token into cur[i], its embedding into row i of emb_x, emb_np[i] + 1.
+// The whole-batch decode passes x itself and the positions; a pipeline's last stage passes scratch.
+void head_batch(BatchImpl *bi, const float *x, int r0, int nr, int32_t *cur, float *emb_x, int *emb_np) {
     xj_stage *s = bi->s;
     Impl *im = I(s);
     const xj_hparams *hp = &s->m->hp;
-    const int V = im->output.N, B = bi->B;
-    gemv(im, im->x, nullptr, hp->n_embd, B, PRO_NORM, im->output_norm, hp->eps, {{im->output, im->logits, V}});
+    const int V = im->output.N, B = nr;
+    gemv(im, x, nullptr, hp->n_embd, B, PRO_NORM, im->output_norm, hp->eps, {{im->output, im->logits, V}});
     launch(im, k_argmax_rows_batch, dim3(bi->ntiles, B), dim3(32), 0, (const float *)im->logits, V, bi->pbest, bi->psecond,
            bi->pidx, bi->ntiles);
     ArgmaxArgs a;
     a.pbest = bi->pbest; a.psecond = bi->psecond; a.pidx = bi->pidx; a.ntiles = bi->ntiles;
-    a.out_tok = bi->out_tok; a.margin = bi->margin; a.cur = bi->cur; a.step = bi->step;
-    a.emb = im->tok_embd; a.x = im->x; a.npast = bi->npast;
+    a.out_tok = bi->out_tok + (size_t)r0 * bi->out_cap; a.margin = bi->margin + (size_t)r0 * bi->out_cap;
+    a.cur = cur; a.step = bi->step + r0;
+    a.emb = im->tok_embd; a.x = emb_x; a.npast = emb_np;
     launch(im, k_argmax_final_batch, dim3(B), dim3(1024), 0, a, (long long)bi->out_cap, hp->n_embd);
 }
 
@@ -1272,10 +1277,12 @@ struct xj_cuda_batch {
     BatchImpl impl;
 };
 
-xj_cuda_batch *xj_cuda_batch_new(const xj_model *m, int n_seq, int n_ctx, char *err, size_t errlen) {
+xj_cuda_batch *xj_cuda_batch_new_range(const xj_model *m, int l0, int l1, bool has_head, int n_seq, int n_ctx, char *err,
+                                       size_t errlen) {
     if (!m || n_seq < 1 || n_seq > 1024 || n_ctx < 1) { seterr(err, errlen, "need 1 <= n_seq <= 1024 and n_ctx >= 1"); return nullptr; }
-    // the stage holds the weights and B-row activation buffers; its own single-sequence state is minimal
-    xj_stage *s = xj_cuda_stage_new(m, 0, m->hp.n_layer, 1, n_seq, true, err, errlen);
+    if (l0 < 0 || l1 > m->hp.n_layer || l0 >= l1) { seterr(err, errlen, "bad layer range [%d,%d)", l0, l1); return nullptr; }
+    // the stage holds the weights and n_seq-row activation buffers; its own single-sequence state is minimal
+    xj_stage *s = xj_cuda_stage_new(m, l0, l1, 1, n_seq, has_head, err, errlen);
     if (!s) return nullptr;
     xj_cuda_batch *b = new xj_cuda_batch();
     BatchImpl *bi = &b->impl;
@@ -1288,24 +1295,32 @@ xj_cuda_batch *xj_cuda_batch_new(const xj_model *m, int n_seq, int n_ctx, char *
     auto fail = [&]() { cuda_destroy(s); delete b; return (xj_cuda_batch *)nullptr; };
     const size_t ns = (size_t)n_seq * hp->h_v * hp->s_v * hp->s_k, nc = (size_t)n_seq * hp->conv_dim * (hp->conv_k - 1);
     const size_t nkv = (size_t)n_seq * n_ctx * hp->n_head_kv * hp->head_dim, es = im->kv_f32 ? 4 : 2;
-    for (int il = 0; il < hp->n_layer; il++) {
+    for (int il = l0; il < l1; il++) {
         float *a = nullptr, *c = nullptr;
         uint8_t *k = nullptr, *v = nullptr;
-        if (im->L[il].rec) {
+        if (im->L[il - l0].rec) {
             if (dalloc(im, &a, ns, err, errlen) || dalloc(im, &c, nc, err, errlen)) return fail();
         } else if (dalloc(im, &k, nkv * es, err, errlen) || dalloc(im, &v, nkv * es, err, errlen)) return fail();
         bi->ssm.push_back(a); bi->conv.push_back(c); bi->kc.push_back(k); bi->vc.push_back(v);
     }
-    bi->ntiles = (im->output.N + 15) / 16;
+    bi->ntiles = has_head ? (im->output.N + 15) / 16 : 1;
+    bi->out_cap = 1024;
     if (dalloc(im, &bi->npast, (size_t)n_seq, err, errlen) || dalloc(im, &bi->step, (size_t)n_seq, err, errlen) ||
-        dalloc(im, &bi->cur, (size_t)n_seq, err, errlen) ||
+        dalloc(im, &bi->np_scratch, (size_t)n_seq, err, errlen) || dalloc(im, &bi->cur, (size_t)n_seq, err, errlen) ||
         dalloc(im, &bi->pbest, (size_t)n_seq * bi->ntiles, err, errlen) ||
         dalloc(im, &bi->psecond, (size_t)n_seq * bi->ntiles, err, errlen) ||
-        dalloc(im, &bi->pidx, (size_t)n_seq * bi->ntiles, err, errlen)) return fail();
-    if (!im->tok_embd.p && upload(im, m->tok_embd, &im->tok_embd, err, errlen, true)) return fail();
+        dalloc(im, &bi->pidx, (size_t)n_seq * bi->ntiles, err, errlen) ||
+        dalloc(im, &bi->out_tok, (size_t)n_seq * bi->out_cap, err, errlen) ||
+        dalloc(im, &bi->margin, (size_t)n_seq * bi->out_cap, err, errlen)) return fail();
+    if ((l0 == 0 || has_head) && !im->tok_embd.p && upload(im, m->tok_embd, &im->tok_embd, err, errlen, true)) return fail();
     if (cudaDeviceSynchronize() != cudaSuccess) { seterr(err, errlen, "CUDA error while creating the batch"); return fail(); }
     if (batch_reset_state(bi, err, errlen)) return fail();
     return b;
+}
+
+xj_cuda_batch *xj_cuda_batch_new(const xj_model *m, int n_seq, int n_ctx, char *err, size_t errlen) {
+    if (!m) { seterr(err, errlen, "null model"); return nullptr; }
+    return xj_cuda_batch_new_range(m, 0, m->hp.n_layer, true, n_seq, n_ctx, err, errlen);
 }
 
 void xj_cuda_batch_free(xj_cuda_batch *b) {
@@ -1335,11 +1350,12 @@ int xj_cuda_batch_decode(xj_cuda_batch *b, const int32_t *prompts, int n_prompt,
     Impl *im = I(s);
     DevGuard dg(im->dev);
     const int B = bi->B, E = s->m->hp.n_embd;
+    if (s->l0 != 0 || s->l1 != s->m->hp.n_layer || !s->has_head) { seterr(err, errlen, "decode needs a batch over all layers with the head"); return -1; }
     if (n_prompt <= 0 || n_gen <= 0) { seterr(err, errlen, "need at least one prompt token and one generated token"); return -1; }
     if (bi->n_past + n_prompt + n_gen - 1 > bi->n_ctx) { seterr(err, errlen, "context is full (%d)", bi->n_ctx); return -1; }
     if (n_gen > bi->out_cap) {
         if (bi->step_graph) { cudaGraphExecDestroy(bi->step_graph); bi->step_graph = nullptr; }
-        const int cap = n_gen > 1024 ? n_gen : 1024;
+        const int cap = n_gen;
         if (dalloc(im, &bi->out_tok, (size_t)B * cap, err, errlen) || dalloc(im, &bi->margin, (size_t)B * cap, err, errlen)) return -1;
         bi->out_cap = cap;
     }
@@ -1359,9 +1375,9 @@ int xj_cuda_batch_decode(xj_cuda_batch *b, const int32_t *prompts, int n_prompt,
     for (int i = 0; i < n_prompt; i++) {
         launch(im, k_embed, dim3((E / 8 + 127) / 128, B), dim3(128), 0, im->tok_embd, (const int32_t *)(bi->prompts + (size_t)i * B), B,
                im->x, E);
-        run_layers_batch(bi);
+        run_layers_batch(bi, im->x, 0, B);
         if (i + 1 < n_prompt) launch(im, k_advance_batch, dim3(1), dim3(256), 0, bi->npast, B, 1);
-        else head_batch(bi);   // out[:, 0], its embedding into x, position + 1
+        else head_batch(bi, im->x, 0, B, bi->cur, im->x, bi->npast);   // out[:, 0], its embedding into x, position + 1
     }
     CK(cudaEventRecord(im->ev[1], im->st));
     bi->last_launches[0] = im->nlaunch - nl0;
@@ -1370,8 +1386,8 @@ int xj_cuda_batch_decode(xj_cuda_batch *b, const int32_t *prompts, int n_prompt,
         if (!bi->step_graph) {
             cudaGraph_t g;
             CK(cudaStreamBeginCapture(im->st, cudaStreamCaptureModeThreadLocal));
-            run_layers_batch(bi);
-            head_batch(bi);
+            run_layers_batch(bi, im->x, 0, B);
+            head_batch(bi, im->x, 0, B, bi->cur, im->x, bi->npast);
             CK(cudaStreamEndCapture(im->st, &g));
             bi->step_kernels = count_kernels(g);
             cudaError_t e = cudaGraphInstantiate(&bi->step_graph, g, 0);
@@ -1394,6 +1410,43 @@ int xj_cuda_batch_decode(xj_cuda_batch *b, const int32_t *prompts, int n_prompt,
     }
     bi->n_past += n_prompt + n_gen - 1;
     return 0;
+}
+
+// ---- pipeline-stage entry points: device buffers of the batch's device, rows = a micro-batch
+int xj_cuda_batch_embed_rows(xj_cuda_batch *b, const int32_t *tok_dev, float *x_dev, int nrows, char *err, size_t errlen) {
+    if (!b || !tok_dev || !x_dev || nrows < 1 || nrows > b->impl.B) { seterr(err, errlen, "bad arguments"); return -1; }
+    BatchImpl *bi = &b->impl;
+    Impl *im = I(bi->s);
+    DevGuard dg(im->dev);
+    if (!im->tok_embd.p) { seterr(err, errlen, "this batch has no embedding table (layer range does not start at 0)"); return -1; }
+    const int E = bi->s->m->hp.n_embd;
+    launch(im, k_embed, dim3((E / 8 + 127) / 128, nrows), dim3(128), 0, im->tok_embd, tok_dev, nrows, x_dev, E);
+    return sync_check(im, err, errlen);
+}
+
+int xj_cuda_batch_forward_rows(xj_cuda_batch *b, float *x_dev, int row0, int nrows, char *err, size_t errlen) {
+    if (!b || !x_dev || row0 < 0 || nrows < 1 || row0 + nrows > b->impl.B) { seterr(err, errlen, "bad row range"); return -1; }
+    BatchImpl *bi = &b->impl;
+    Impl *im = I(bi->s);
+    DevGuard dg(im->dev);
+    if (bi->n_past + 1 > bi->n_ctx) { seterr(err, errlen, "context is full (%d)", bi->n_ctx); return -1; }
+    run_layers_batch(bi, x_dev, row0, nrows);
+    launch(im, k_advance_batch, dim3(1), dim3(256), 0, bi->npast + row0, nrows, 1);
+    if (sync_check(im, err, errlen)) return -1;
+    if (row0 + nrows == bi->B) bi->n_past++;   // the host mirror follows the last micro-batch of a step
+    return 0;
+}
+
+int xj_cuda_batch_pick_rows(xj_cuda_batch *b, const float *x_dev, int row0, int nrows, int32_t *tok_dev, char *err,
+                            size_t errlen) {
+    if (!b || !x_dev || !tok_dev || row0 < 0 || nrows < 1 || row0 + nrows > b->impl.B) { seterr(err, errlen, "bad row range"); return -1; }
+    BatchImpl *bi = &b->impl;
+    Impl *im = I(bi->s);
+    DevGuard dg(im->dev);
+    if (!bi->s->has_head) { seterr(err, errlen, "this batch has no head"); return -1; }
+    // the pick's embedding and position update go to scratch: the pipeline's first stage embeds the ids
+    head_batch(bi, x_dev, row0, nrows, tok_dev, im->h, bi->np_scratch + row0);
+    return sync_check(im, err, errlen);
 }
 
 long long xj_cuda_batch_last_launches(const xj_cuda_batch *b, long long *launches) {
