@@ -84,11 +84,12 @@ int xj_cuda_graph_kernels(const xj_stage *s);
 long long xj_cuda_last_decode_launches(const xj_stage *s, long long *launches);
 
 // Phase timing of the persistent kernel's last traced step (XJC_OPT_TRACE): for each phase p < cap,
-// out[9p..9p+8] = {kind (0 matrix-vector, 1 Gated DeltaNet, 2 attention, 3 token pick), longest CTA
+// out[13p..13p+12] = {kind (0 matrix-vector, 1 Gated DeltaNet, 2 attention, 3 token pick), longest CTA
 // time in the phase (us), mean CTA time (us), first start to last end over CTAs (us), first start
 // (us, device clock), mean time a CTA's consumers waited for weight chunks (us), mean lead of the
 // first chunk request before the phase started (us), mean prologue time (us), mean time of the first
-// tile after the prologue (us)}. Returns the number of phases, or -1.
+// tile after the prologue (us), and of that first tile (warp 0): chunk wait, tensor-core work, tile
+// barrier, epilogue (us)}. Returns the number of phases, or -1.
 int xj_cuda_phase_trace(const xj_stage *s, double *out, int cap);
 
 // Dequantise n_rows rows of k elements of GGUF type `type` (host bytes in, host fp32 out) with the

@@ -329,6 +329,110 @@ XJ_DEV float mk_prologue(const MkPhase &p, __half *xs, float *xsum, int tid) {
     return sc;
 }
 
+// ------------------------------------------------------------------ K-quant units at T = 1
+// One warp's half of a Q4_K / Q6_K unit (16 rows x 128 codes: k-steps 8*HH .. 8*HH+7 of the super-block)
+// from a staged chunk, with unit_compute's arithmetic for the token's columns (lanes c = 0: columns 0
+// and 1 = hi and lo). Leaner than unit_compute at T = 1: the half index HH is a compile-time constant,
+// so each header byte is one byte-permute; and no lane predicate guards the operand loads: lanes whose
+// B-fragment column is not the token's (g >= 2) read the token's own columns again and lanes c != 0
+// read its block sums, which only changes D columns and partial rows that are never stored.
+XJ_DEV uint32_t byte_sel(uint32_t w, int j) { return __byte_perm(w, 0u, 0x4440u | (uint32_t)j); }   // byte j of w
+
+template <int HH>
+XJ_DEV void mk_q4k(const uint8_t *stage, int ui, int u, int lane, const __half *xb, const float *xsum, float *scw,
+                   float &yg, float &yg8) {
+    using G = Geo<XJ_Q4_K>;
+    const int g = lane >> 2;
+    const uint8_t *qs = stage + ui * G::QB;
+    const uint8_t *ss = stage + G::CU * G::QB + ui * G::SB;
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + ((2 * HH) * 32 + lane) * 16);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + ((2 * HH + 1) * 32 + lane) * 16);
+    {   // (d*sc, 64*d*sc + dmin*m) for row r, sub-blocks 4HH + 2*(lane>>4) + {0,1} (core/xj_quant.h:49-52)
+        const int r = lane & 15;
+        const uint4 hdr = *reinterpret_cast<const uint4 *>(ss + r * 16);
+        const float d = h2f((uint16_t)(hdr.x & 0xffff)), dmin = h2f((uint16_t)(hdr.x >> 16));
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int sbl = 2 * (lane >> 4) + e;          // sub-block within this half = header byte index
+            int s_, m_;
+            if (HH == 0) { s_ = (int)(byte_sel(hdr.y, sbl) & 63); m_ = (int)(byte_sel(hdr.z, sbl) & 63); }
+            else {
+                const uint32_t b8 = byte_sel(hdr.w, sbl), b0 = byte_sel(hdr.y, sbl), b4 = byte_sel(hdr.z, sbl);
+                s_ = (int)((b8 & 0xF) | ((b0 >> 6) << 4));
+                m_ = (int)((b8 >> 4) | ((b4 >> 6) << 4));
+            }
+            const float d1 = d * (float)s_, m1 = dmin * (float)m_;
+            float *o = scw + ((sbl * 8 + (r & 7)) * 4 + (r >> 3) * 2);
+            o[0] = d1;
+            o[1] = 64.0f * d1 + m1;
+        }
+    }
+    __syncwarp();
+    const int kb = u * 256;
+    const __half *xk = xb + kb + 128 * HH;
+    const float *sk = xsum + (kb >> 5) + 4 * HH;
+#pragma unroll
+    for (int sbl = 0; sbl < 4; sbl++) {
+        float d4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            uint32_t af[4];
+            nib_frag64(word_of(e + 2 * sbl < 4 ? q0 : q1, (2 * sbl + e) & 3), af);
+            const uint2 bv = *reinterpret_cast<const uint2 *>(xk + 16 * (2 * sbl + e));
+            mma16816(d4, af, bv.x, bv.y);
+        }
+        const float4 sc4 = *reinterpret_cast<const float4 *>(scw + (sbl * 8 + g) * 4);
+        const float S = sk[sbl];
+        yg = fmaf(sc4.x, d4[0] + d4[1], yg);
+        yg = fmaf(-sc4.y, S, yg);
+        yg8 = fmaf(sc4.z, d4[2] + d4[3], yg8);
+        yg8 = fmaf(-sc4.w, S, yg8);
+    }
+    __syncwarp();
+}
+
+template <int HH>
+XJ_DEV void mk_q6k(const uint8_t *stage, int ui, int u, int lane, const __half *xb, float *scw, float &yg, float &yg8) {
+    using G = Geo<XJ_Q6_K>;
+    const int g = lane >> 2;
+    const uint8_t *qs = stage + ui * G::QB;
+    const uint8_t *hs = stage + G::CU * G::QB + ui * G::HB;
+    const uint8_t *ss = stage + G::CU * (G::QB + G::HB) + ui * G::SB;
+    const uint8_t *ds = stage + G::CU * (G::QB + G::HB + G::SB) + ui * G::DB;
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + ((2 * HH) * 32 + lane) * 16);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + ((2 * HH + 1) * 32 + lane) * 16);
+    const uint4 hq = *reinterpret_cast<const uint4 *>(hs + (HH * 32 + lane) * 16);
+    {   // d*sc for row r, k-steps 8HH + 4*(lane>>4) + {0..3} (core/xj_quant.h:106-118)
+        const int r = lane & 15;
+        const uint4 sc = *reinterpret_cast<const uint4 *>(ss + r * 16);
+        const float d = h2f(*reinterpret_cast<const uint16_t *>(ds + r * 2));
+        const uint32_t wsel = (lane >> 4) ? (HH ? sc.w : sc.y) : (HH ? sc.z : sc.x);   // bytes 8HH + 4*(lane>>4) ..
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            const int sl = 4 * (lane >> 4) + e;
+            scw[(sl * 8 + (r & 7)) * 2 + (r >> 3)] = d * (float)(int)(int8_t)(wsel >> (8 * e));
+        }
+    }
+    __syncwarp();
+    const __half *xk = xb + u * 256 + 128 * HH;
+#pragma unroll
+    for (int sl = 0; sl < 8; sl++) {
+        float d4[4] = {0.f, 0.f, 0.f, 0.f};
+        uint32_t af[4], ah[4];
+        nib_frag(word_of(sl < 4 ? q0 : q1, sl & 3), af);
+        uint32_t hw = word_of(hq, sl >> 1);
+        if (sl & 1) hw >>= 8;
+        hi_frag(hw, ah);
+        const uint2 bv = *reinterpret_cast<const uint2 *>(xk + 16 * sl);
+        mma16816(d4, af, bv.x, bv.y);
+        mma16816(d4, ah, bv.x, bv.y);
+        const float2 sc2 = *reinterpret_cast<const float2 *>(scw + (sl * 8 + g) * 2);
+        yg = fmaf(sc2.x, d4[0] + d4[1], yg);
+        yg8 = fmaf(sc2.y, d4[2] + d4[3], yg8);
+    }
+    __syncwarp();
+}
+
 // Global operands of a tile's epilogue, loaded when the tile starts so the load latency overlaps the
 // tile's tensor-core work (threads tid < 16, one output row each).
 constexpr int MK_KC = 4;   // longest causal conv the persistent kernel takes (the models' conv_k)
@@ -697,7 +801,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                 const MkStream &S = sst[gk & 1];
                 const int kn = k + 1 < A.nstream ? k + 1 : 0;
                 copy_desc_async(&sst[(gk + 1) & 1], &A.stream[kn], (int)sizeof(MkStream), lane);
-                unsigned long long *trp = A.trace && step == A.nsteps - 1 ? A.trace + ((size_t)cta * A.nphase + S.ph) * 8 : nullptr;
+                unsigned long long *trp = A.trace && step == A.nsteps - 1 ? A.trace + ((size_t)cta * A.nphase + S.ph) * 12 : nullptr;
                 if (lane < 6 && S.pf[lane]) {
                     // this CTA's slice of the side-data range (16-byte granules)
                     const unsigned bytes = S.pf_bytes[lane];
@@ -751,16 +855,17 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                 copy_desc_async(&sph[(gp + 1) & 1], &A.prog[pn], (int)sizeof(MkPhase), tid);
                 const bool tr = A.trace && step == A.nsteps - 1 && tid == 0;
                 unsigned long long wait_ns = 0;
-                if (tr) A.trace[((size_t)cta * A.nphase + ph) * 8] = globaltimer();
+                if (tr) A.trace[((size_t)cta * A.nphase + ph) * 12] = globaltimer();
                 if (p.op == MK_GEMV && cta < p.ntiles) {
                     ArgRun ar;
                     const float tsc = mk_prologue(p, xs, xsum, tid);
-                    if (tr) A.trace[((size_t)cta * A.nphase + ph) * 8 + 5] = globaltimer();
+                    if (tr) A.trace[((size_t)cta * A.nphase + ph) * 12 + 5] = globaltimer();
                     int ntile_done = 0;
                     const int xstride = p.K + 16;
                     const bool bcol = g < 2;
                     const __half *xb = xs + (size_t)g * xstride + 4 * c;
                     const float *xsum_t = c == 0 ? xsum : nullptr;
+                    const __half *xb2 = xs + (size_t)(g & 1) * xstride + 4 * c;   // always a staged column
                     for (int tg = cta; tg < p.ntiles; tg += G) {
                         const int j = mk_job_of(p, tg);
                         const MmaJob &jb = p.job[j];
@@ -773,15 +878,21 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                             const int slot = consumed % MK_NS;
                             const unsigned long long w0 = tr ? globaltimer() : 0;
                             const bool got = mk_wait(&full[slot], (consumed / MK_NS) & 1, A.err, 1, A.diag, step, ph, (int)consumed, 32);
-                            if (tr) wait_ns += globaltimer() - w0;
+                            if (tr) { const unsigned long long w1 = globaltimer(); wait_ns += w1 - w0; if (ntile_done == 0 && u0 == 0) A.trace[((size_t)cta * A.nphase + ph) * 12 + 8] = w1; }
                             const uint8_t *st = ring + (size_t)slot * MK_SLOT;
                             const int cu = W.nu - u0 < CU ? W.nu - u0 : CU;
                             if (W.type == XJ_Q4_K) {
                                 const int ui = warp >> 1;
-                                if (ui < cu) unit_compute<XJ_Q4_K>(st, ui, u0 + ui, warp & 1, lane, bcol, xb, xsum_t, scw, yg, yg8);
+                                if (ui < cu) {
+                                    if (warp & 1) mk_q4k<1>(st, ui, u0 + ui, lane, xb2, xsum, scw, yg, yg8);
+                                    else mk_q4k<0>(st, ui, u0 + ui, lane, xb2, xsum, scw, yg, yg8);
+                                }
                             } else if (W.type == XJ_Q6_K) {
                                 const int ui = warp >> 1;
-                                if (ui < cu) unit_compute<XJ_Q6_K>(st, ui, u0 + ui, warp & 1, lane, bcol, xb, xsum_t, scw, yg, yg8);
+                                if (ui < cu) {
+                                    if (warp & 1) mk_q6k<1>(st, ui, u0 + ui, lane, xb2, scw, yg, yg8);
+                                    else mk_q6k<0>(st, ui, u0 + ui, lane, xb2, scw, yg, yg8);
+                                }
                             } else {
 #pragma unroll
                                 for (int k = 0; k < Geo<XJ_Q8_0>::CU / MK_CWARPS; k++) {
@@ -795,13 +906,16 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                         }
                         float *rr = red + rb * (MK_CWARPS * 16);
                         if (c == 0) { rr[warp * 16 + g] = yg; rr[warp * 16 + g + 8] = yg8; }
+                        if (tr && ntile_done == 0) A.trace[((size_t)cta * A.nphase + ph) * 12 + 9] = globaltimer();
                         BarC::sync();
+                        if (tr && ntile_done == 0) A.trace[((size_t)cta * A.nphase + ph) * 12 + 10] = globaltimer();
                         mk_epilogue(jb, tile, rr, tsc, tid, e, ar);
+                        if (tr && ntile_done == 0) A.trace[((size_t)cta * A.nphase + ph) * 12 + 11] = globaltimer();
                         rb ^= 1;
-                        if (tr && ntile_done == 0) A.trace[((size_t)cta * A.nphase + ph) * 8 + 6] = globaltimer();
+                        if (tr && ntile_done == 0) A.trace[((size_t)cta * A.nphase + ph) * 12 + 6] = globaltimer();
                         ntile_done++;
                     }
-                    if (tr) A.trace[((size_t)cta * A.nphase + ph) * 8 + 7] = ntile_done;
+                    if (tr) A.trace[((size_t)cta * A.nphase + ph) * 12 + 7] = ntile_done;
                     if (tid == 0 && p.job[0].epi == EPI_ARGMAX) {
                         // one greedy-pick partial per CTA (CTA c holds tiles c, c + G, ...)
                         p.job[0].pbest[cta] = ar.b; p.job[0].psecond[cta] = ar.b2; p.job[0].pidx[cta] = ar.bi;
@@ -822,8 +936,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                     if (cta == 0) argmax_final_dev<BarC>(p.am, tid, MK_CTHREADS);
                 }
                 if (tr) {
-                    A.trace[((size_t)cta * A.nphase + ph) * 8 + 1] = globaltimer();
-                    A.trace[((size_t)cta * A.nphase + ph) * 8 + 2] = wait_ns;
+                    A.trace[((size_t)cta * A.nphase + ph) * 12 + 1] = globaltimer();
+                    A.trace[((size_t)cta * A.nphase + ph) * 12 + 2] = wait_ns;
                 }
                 cp_async_wait_all();   // the next descriptor has landed (visible after the barrier below)
                 if (step == A.nsteps - 1 && ph == A.nphase - 1) break;

@@ -814,7 +814,7 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
     // the program's size is fixed for a stage: a rebuild (after the output buffers moved) reuses these
     if (!im->mk_prog &&
         (dalloc(im, &im->mk_prog, prog.size(), err, errlen) || dalloc(im, &im->mk_stream, stream.size(), err, errlen) ||
-         dalloc(im, &im->mk_trace, (size_t)sms * prog.size() * 8, err, errlen) || dalloc(im, &im->mk_bar, 4, err, errlen) ||
+         dalloc(im, &im->mk_trace, (size_t)sms * prog.size() * 12, err, errlen) || dalloc(im, &im->mk_bar, 4, err, errlen) ||
          dalloc(im, &im->mk_diag, 8, err, errlen) || dalloc(im, &im->mk_acnt, (size_t)hp->n_head, err, errlen) ||
          dalloc(im, &im->mk_apart, (size_t)hp->n_head * im->mk_max_split * (hp->head_dim + 2), err, errlen))) return -1;
     CK(cudaMemcpy(im->mk_prog, prog.data(), prog.size() * sizeof(MkPhase), cudaMemcpyHostToDevice));
@@ -1199,15 +1199,23 @@ int xj_cuda_phase_trace(const xj_stage *s, double *out, int cap) {
     if (!im || im->mk_state != 1 || !g_opt_trace) return -1;
     DevGuard dg(im->dev);
     const int np = im->mk_nphase, G = im->mk_ctas;
-    std::vector<unsigned long long> t((size_t)G * np * 8);
+    std::vector<unsigned long long> t((size_t)G * np * 12);
     if (cudaMemcpy(t.data(), im->mk_trace, t.size() * 8, cudaMemcpyDeviceToHost) != cudaSuccess) return -1;
     for (int ph = 0; ph < np && ph < cap; ph++) {
         unsigned long long s0 = ~0ull, e1 = 0;
-        double wmax = 0, wsum = 0, wait = 0, lead = 0, pro = 0, first = 0;
+        double wmax = 0, wsum = 0, wait = 0, lead = 0, pro = 0, first = 0, f1 = 0, f2 = 0, f3 = 0, f4 = 0;
         int nlead = 0, ntl = 0;
         for (int c = 0; c < G; c++) {
-            const unsigned long long *r = &t[((size_t)c * np + ph) * 8];
-            if (r[7]) { pro += ((double)r[5] - (double)r[0]) * 1e-3; first += ((double)r[6] - (double)r[5]) * 1e-3; ntl++; }
+            const unsigned long long *r = &t[((size_t)c * np + ph) * 12];
+            if (r[7]) {
+                pro += ((double)r[5] - (double)r[0]) * 1e-3;
+                first += ((double)r[6] - (double)r[5]) * 1e-3;
+                f1 += ((double)r[8] - (double)r[5]) * 1e-3;    // prologue end -> first chunk ready
+                f2 += ((double)r[9] - (double)r[8]) * 1e-3;    // tensor-core work of the first tile (warp 0)
+                f3 += ((double)r[10] - (double)r[9]) * 1e-3;   // tile barrier (waiting for the other warps)
+                f4 += ((double)r[11] - (double)r[10]) * 1e-3;  // epilogue
+                ntl++;
+            }
             if (r[0] < s0) s0 = r[0];
             if (r[1] > e1) e1 = r[1];
             const double w = r[1] > r[0] ? (double)(r[1] - r[0]) * 1e-3 : 0.0;
@@ -1216,7 +1224,7 @@ int xj_cuda_phase_trace(const xj_stage *s, double *out, int cap) {
             wait += (double)r[2] * 1e-3;
             if (r[3]) { lead += ((double)r[0] - (double)r[3]) * 1e-3; nlead++; }
         }
-        double *o = out + (size_t)ph * 9;
+        double *o = out + (size_t)ph * 13;
         o[0] = im->mk_ops[ph];
         o[1] = wmax;
         o[2] = wsum / G;
@@ -1226,6 +1234,10 @@ int xj_cuda_phase_trace(const xj_stage *s, double *out, int cap) {
         o[6] = nlead ? lead / nlead : 0.0;
         o[7] = ntl ? pro / ntl : 0.0;
         o[8] = ntl ? first / ntl : 0.0;
+        o[9] = ntl ? f1 / ntl : 0.0;
+        o[10] = ntl ? f2 / ntl : 0.0;
+        o[11] = ntl ? f3 / ntl : 0.0;
+        o[12] = ntl ? f4 / ntl : 0.0;
     }
     return np;
 }

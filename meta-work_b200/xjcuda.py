@@ -291,8 +291,9 @@ class Stage:
     def phase_trace(self):
         """Per-phase timing of the last traced persistent decode (OPT_TRACE): array [phases, 5] of
         kind, max CTA us, mean CTA us, span us, start us, mean weight wait us, mean request lead us,
-        mean prologue us, mean first-tile us."""
-        out = np.zeros((4096, 9), np.float64)
+        mean prologue us, mean first-tile us, and the first tile's chunk wait, tensor-core work, tile barrier
+        and epilogue us."""
+        out = np.zeros((4096, 13), np.float64)
         n = lib().xj_cuda_phase_trace(self.addr, out.ctypes.data, 4096)
         if n < 0:
             raise XjError("no phase trace (enable OPT_TRACE before decode)")
