@@ -65,8 +65,9 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
                    float *gpu_ms, char *err, size_t errlen);
 
 // Matrix-vector product on host buffers with the decode kernels: y[t][n] = W[n] . x[t] for t < T
-// (1 <= T <= 16), W an [n][k] matrix in GGUF block layout of `type`. path 0 = fastest available
-// kernel, 1 = generic per-element kernel. For parity tests of the kernel that dominates decode.
+// (1 <= T <= 64; more than 16 tokens take the 64-token kernel of batched decode), W an [n][k] matrix
+// in GGUF block layout of `type`. path 0 = fastest available kernel, 1 = generic per-element kernel.
+// For parity tests of the kernels that dominate decode.
 int xj_cuda_gemv(int type, const void *w, int k, int n, const float *x, int T, float *y, int path, char *err,
                  size_t errlen);
 // Average device time (ms) of one such launch over `iters` launches that rotate through `copies`

@@ -715,9 +715,24 @@ __host__ __device__ inline WideX wide_x_of(void *buf, int T, int K) {
     return w;
 }
 
-// Grid T, MMA_WARPS*32 threads: f(x[t]) -> range scale -> hi/lo columns + block sums of token t.
-static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_x(const float *x, const float *x2, long long ldx, int K, int pro,
-                                                                  const float *norm_w, float eps, void *buf, int T) {
+// Layout of a 64-token launch's activations (k_gemv_b64): K in chunks of B64_CK = 128; chunk c is one
+// record: per token a row of B64_XROW bytes holding each element as the pair (hi, lo) of fp16 halves,
+// each 16-element group as four 16-byte lane quads (quad c: elements 2c, 2c+1, 2c+8, 2c+9, the B
+// fragments of two MMA k-steps), then the 32-wide block sums [4][64] (sub-block major); the T range
+// scales follow the last record. One bulk copy moves a whole record into shared memory.
+constexpr int B64_T = 64;           // tokens of one launch, at most
+constexpr int B64_CK = 128;         // K per chunk: half a K-quant super-block, four Q8_0 blocks
+constexpr int B64_XROW = B64_CK * 4 + 64;   // bytes per token row (the pad makes B-fragment loads conflict-free)
+__host__ __device__ inline int b64_rec_bytes(int T) { return T * B64_XROW + 4 * B64_T * 4; }
+inline size_t b64_x_bytes(int T, int K) { return (size_t)(K / B64_CK) * b64_rec_bytes(T) + (size_t)T * 4 + 256; }
+// position (in halves) of element e (0..15) of a 16-element group in its 64-byte lane-quad layout
+__host__ __device__ inline int b64_pos(int e) { return ((e & 7) >> 1) * 8 + ((e & 1) + 2 * (e >> 3)) * 2; }
+
+// Grid T, MMA_WARPS*32 threads: f(x[t]) -> range scale -> hi/lo columns + block sums of token t, in the
+// wide layout (B64 = false) or the 64-token chunk layout (B64 = true); the values are the same.
+template <bool B64>
+static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_xt(const float *x, const float *x2, long long ldx, int K, int pro,
+                                                                   const float *norm_w, float eps, void *buf, int T) {
     griddep_wait();
     __shared__ float pred[MMA_WARPS][2];
     __shared__ float s_scale, s_nsc;
@@ -754,7 +769,8 @@ static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_x(const float *x
         const float m = tam * nsc;
         s_nsc = nsc;
         s_scale = ldexpf(1.0f, 14 - (m > 0.0f ? ilogbf(m) : 0));
-        W.scale[t] = s_scale;
+        if (B64) reinterpret_cast<float *>((uint8_t *)buf + (size_t)(K / B64_CK) * b64_rec_bytes(T))[t] = s_scale;
+        else W.scale[t] = s_scale;
     }
     __syncthreads();
     const float sc = s_scale, nsc = s_nsc;
@@ -766,11 +782,19 @@ static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_x(const float *x
             const float val = (pro == PRO_NORM ? (v[k] * nsc) * norm_w[i] : v[k]) * sc;
             const __half hi = __float2half_rn(val);
             const __half lo = __float2half_rn(val - __half2float(hi));
-            const int pos = (i & ~15) + bperm(i & 15);
-            col_hi[pos] = hi;
-            col_lo[pos] = lo;
             const float bs = warp_sum(__half2float(hi) + __half2float(lo));
-            if (lane == 0) W.xsum[t * W.sstride + (i >> 5)] = bs;
+            if (B64) {
+                const int ci = i & (B64_CK - 1);
+                uint8_t *rec = (uint8_t *)buf + (size_t)(i / B64_CK) * b64_rec_bytes(T);
+                __half *row = reinterpret_cast<__half *>(rec + (size_t)t * B64_XROW) + (ci & ~15) * 2 + b64_pos(ci & 15);
+                *reinterpret_cast<__half2 *>(row) = __halves2half2(hi, lo);
+                if (lane == 0) reinterpret_cast<float *>(rec + (size_t)T * B64_XROW)[(ci >> 5) * B64_T + t] = bs;
+            } else {
+                const int pos = (i & ~15) + bperm(i & 15);
+                col_hi[pos] = hi;
+                col_lo[pos] = lo;
+                if (lane == 0) W.xsum[t * W.sstride + (i >> 5)] = bs;
+            }
         }
     }
 }
@@ -972,6 +996,447 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 1) k_gemv_wide(MmaArgs a, cons
     }
 }
 
+
+// ------------------------------------------------------------------ 64-token launches (batches of sequences)
+// 17..64 independent tokens (one per sequence of a batch): the weights stream once per launch and every
+// decoded A fragment feeds all 2T columns. A CTA of B64_WARPS warps owns a block of 16 row tiles (warp
+// w: tiles w and w + 8, sharing each B fragment) and a range of K chunks; the chunk's activations (all
+// tokens, one 128-wide K slice) and the 16 tiles' weights for it arrive together in one stage. When a
+// block's K is split over several CTAs, those CTAs form one thread-block cluster: CTA r owns rows
+// [r*256/ns, (r+1)*256/ns) of the block; every CTA stages its partial sums in its own shared memory and
+// sends each owner its rows with one bulk copy into the owner's receive buffer (distributed shared
+// memory, completion on the owner's mbarrier); CTA r then adds the ns partials in rank order and runs
+// the epilogue, so the result is deterministic. Per block and split the
+// arithmetic is unit_compute's (same fragments, same per-block scale terms); only the summation order
+// over K differs from the 1..16-token kernels.
+constexpr int B64_WARPS = 8;
+constexpr int B64_TILES = 2 * B64_WARPS;          // row tiles per block
+constexpr int B64_ROWS = 16 * B64_TILES;          // 256
+constexpr int B64_RS = B64_T + 4;                 // partial-sum row stride (floats): rows stay 16-byte aligned
+constexpr int B64_MAXSPLIT = 8;                   // CTAs per block: a portable cluster
+constexpr int B64_RECV_ROWS = B64_ROWS + B64_MAXSPLIT;   // >= ns * ceil(256 / ns) for every ns <= 8
+template <int TYPE> struct B64Geo;                // weight bytes per tile and chunk, and their layout
+template <> struct B64Geo<XJ_Q4_K> { static constexpr int Q = 1024, H = 0, S = 256, D = 0; };
+template <> struct B64Geo<XJ_Q6_K> { static constexpr int Q = 1024, H = 512, S = 256, D = 32; };
+template <> struct B64Geo<XJ_Q8_0> { static constexpr int Q = 2048, H = 0, S = 0, D = 128; };
+template <int TYPE> constexpr int b64_wbytes() { return B64Geo<TYPE>::Q + B64Geo<TYPE>::H + B64Geo<TYPE>::S + B64Geo<TYPE>::D; }
+constexpr int B64_ACT = B64_T * B64_XROW + 4 * B64_T * 4;       // largest activation record
+template <int TYPE> constexpr int b64_stage() { return B64_ACT + B64_TILES * b64_wbytes<TYPE>(); }
+constexpr int B64_STAGES = 2;
+constexpr size_t B64_RECV = (size_t)B64_RECV_ROWS * B64_RS * 4;
+template <int TYPE> constexpr size_t b64_smem() {
+    return (size_t)B64_STAGES * b64_stage<TYPE>() + (size_t)B64_WARPS * 2 * 128 * 4 + B64_RECV;
+}
+static_assert(b64_smem<XJ_Q8_0>() <= 227 * 1024, "fits one SM");
+
+struct B64Args {
+    MmaJob job[4];
+    int njob, T, K;
+    int nsplit;            // CTAs per block (= cluster size), each a contiguous range of K chunks
+    int blk_start[5];      // prefix sums of 256-row blocks over jobs
+    const void *xbuf;      // activations in the 64-token chunk layout (k_prep_xt<true>)
+    int *err;
+};
+
+XJ_DEV void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+XJ_DEV uint32_t cluster_rank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+XJ_DEV void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+XJ_DEV void cluster_wait() { asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory"); }
+// Address of this CTA's shared variable p in the shared memory of cluster CTA `rank`.
+XJ_DEV uint32_t peer_addr(const void *p, uint32_t rank) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(smem_u32(p)), "r"(rank));
+    return ra;
+}
+// Bulk copy of `bytes` (multiple of 16, both ends 16-byte aligned) from this CTA's shared memory into
+// cluster CTA memory at dst (a peer address), completing on the peer's mbarrier at bar (peer address).
+XJ_DEV void bulk_s2peer(uint32_t dst, const void *src, uint32_t bytes, uint32_t bar) {
+    asm volatile("cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
+                 :: "r"(dst), "r"(smem_u32(src)), "r"(bytes), "r"(bar) : "memory");
+}
+
+// D = A.B with C = 0 (the first k-step of a fresh accumulator).
+XJ_DEV void mma16816_z(float *d, const uint32_t *a, uint32_t b0, uint32_t b1) {
+    const float z = 0.0f;
+    asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};"
+                 : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(z));
+}
+// The A registers of the two hi/lo k-steps of one 16-wide fragment f (f[0..3] = rows g / g+8 at
+// elements (2c, 2c+1) and (2c+8, 2c+9)): k-step s pairs K slots (2j, 2j+1) = (hi, lo) of one element,
+// so each register holds that element's code twice.
+XJ_DEV void b64_dup(const uint32_t *f, uint32_t (&a)[2][4]) {
+    a[0][0] = __byte_perm(f[0], 0u, 0x1010); a[0][1] = __byte_perm(f[1], 0u, 0x1010);
+    a[0][2] = __byte_perm(f[0], 0u, 0x3232); a[0][3] = __byte_perm(f[1], 0u, 0x3232);
+    a[1][0] = __byte_perm(f[2], 0u, 0x1010); a[1][1] = __byte_perm(f[3], 0u, 0x1010);
+    a[1][2] = __byte_perm(f[2], 0u, 0x3232); a[1][3] = __byte_perm(f[3], 0u, 0x3232);
+}
+
+// One chunk of this warp's NQ row tiles against the 8-token n-tiles. The K dimension of each MMA holds
+// 8 elements as (hi, lo) pairs, so an accumulator sums code * (hi + lo) directly: per element group of
+// 16, two k-steps whose B fragments come from one 16-byte load (see b64_pos). wst[q]: tile q's weights
+// in the stage; xs: the stage's token rows; xsum: its block sums [4][64]; hh: which half of the
+// super-block. Each per-block scale term is applied to the fresh accumulator of its block, as in
+// unit_compute.
+template <int TYPE, int NQ>
+XJ_DEV void b64_chunk(const uint8_t *const *wst, int hh, int lane, int T, int ntl, const uint8_t *xs, const float *xsum,
+                      float *scw, float (&y)[2][8][4]) {
+    using BG = B64Geo<TYPE>;
+    const int g = lane >> 2, c = lane & 3;
+    const uint8_t *xb = xs + (size_t)g * B64_XROW + c * 16;      // this lane's quad of group 0, token g of n-tile 0
+    if constexpr (TYPE == XJ_Q4_K) {
+        uint4 q0[NQ], q1[NQ];
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            q0[q] = *reinterpret_cast<const uint4 *>(wst[q] + lane * 16);
+            q1[q] = *reinterpret_cast<const uint4 *>(wst[q] + (32 + lane) * 16);
+            const int r = lane & 15;
+            const uint4 hdr = *reinterpret_cast<const uint4 *>(wst[q] + BG::Q + r * 16);
+            const float d = h2f((uint16_t)(hdr.x & 0xffff)), dmin = h2f((uint16_t)(hdr.x >> 16));
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                const int sbl = 2 * (lane >> 4) + e, sb = 4 * hh + sbl;
+                int s_, m_;
+                if (sb < 4) { s_ = byte_of(hdr, 4 + sb) & 63; m_ = byte_of(hdr, 8 + sb) & 63; }
+                else {
+                    s_ = (byte_of(hdr, 8 + sb) & 0xF) | ((byte_of(hdr, sb) >> 6) << 4);
+                    m_ = (byte_of(hdr, 8 + sb) >> 4) | ((byte_of(hdr, 4 + sb) >> 6) << 4);
+                }
+                const float d1 = d * (float)s_, m1 = dmin * (float)m_;
+                float *o = scw + q * 128 + ((sbl * 8 + (r & 7)) * 4 + (r >> 3) * 2);
+                o[0] = d1;
+                o[1] = 64.0f * d1 + m1;
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int sbl = 0; sbl < 4; sbl++) {
+            uint32_t af[NQ][2][2][4];            // tile, 16-group, k-step
+            float4 sc4[NQ];
+#pragma unroll
+            for (int q = 0; q < NQ; q++) {
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    uint32_t f[4];
+                    nib_frag64(word_of(e + 2 * sbl < 4 ? q0[q] : q1[q], (2 * sbl + e) & 3), f);
+                    b64_dup(f, af[q][e]);
+                }
+                sc4[q] = *reinterpret_cast<const float4 *>(scw + q * 128 + (sbl * 8 + g) * 4);
+            }
+#pragma unroll
+            for (int n = 0; n < 8; n++) {
+                if (n < ntl) {
+                    uint4 b[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+                    if (8 * n + g < T) {
+                        b[0] = *reinterpret_cast<const uint4 *>(xb + (size_t)(8 * n) * B64_XROW + (2 * sbl) * 64);
+                        b[1] = *reinterpret_cast<const uint4 *>(xb + (size_t)(8 * n) * B64_XROW + (2 * sbl + 1) * 64);
+                    }
+                    const float2 S = *reinterpret_cast<const float2 *>(xsum + sbl * B64_T + 8 * n + 2 * c);
+#pragma unroll
+                    for (int q = 0; q < NQ; q++) {
+                        float d4[4];
+                        mma16816_z(d4, af[q][0][0], b[0].x, b[0].y);
+                        mma16816(d4, af[q][0][1], b[0].z, b[0].w);
+                        mma16816(d4, af[q][1][0], b[1].x, b[1].y);
+                        mma16816(d4, af[q][1][1], b[1].z, b[1].w);
+                        y[q][n][0] = fmaf(sc4[q].x, d4[0], y[q][n][0]); y[q][n][0] = fmaf(-sc4[q].y, S.x, y[q][n][0]);
+                        y[q][n][1] = fmaf(sc4[q].x, d4[1], y[q][n][1]); y[q][n][1] = fmaf(-sc4[q].y, S.y, y[q][n][1]);
+                        y[q][n][2] = fmaf(sc4[q].z, d4[2], y[q][n][2]); y[q][n][2] = fmaf(-sc4[q].w, S.x, y[q][n][2]);
+                        y[q][n][3] = fmaf(sc4[q].z, d4[3], y[q][n][3]); y[q][n][3] = fmaf(-sc4[q].w, S.y, y[q][n][3]);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else if constexpr (TYPE == XJ_Q6_K) {
+        uint4 q0[NQ], q1[NQ], hq[NQ];
+#pragma unroll
+        for (int q = 0; q < NQ; q++) {
+            q0[q] = *reinterpret_cast<const uint4 *>(wst[q] + lane * 16);
+            q1[q] = *reinterpret_cast<const uint4 *>(wst[q] + (32 + lane) * 16);
+            hq[q] = *reinterpret_cast<const uint4 *>(wst[q] + BG::Q + lane * 16);
+            const int r = lane & 15;
+            const uint4 sc = *reinterpret_cast<const uint4 *>(wst[q] + BG::Q + BG::H + r * 16);
+            const float d = h2f(*reinterpret_cast<const uint16_t *>(wst[q] + BG::Q + BG::H + BG::S + r * 2));
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int sl = 4 * (lane >> 4) + e;
+                scw[q * 128 + (sl * 8 + (r & 7)) * 2 + (r >> 3)] = d * (float)(int8_t)byte_of(sc, 8 * hh + sl);
+            }
+        }
+        __syncwarp();
+#pragma unroll
+        for (int sl = 0; sl < 8; sl++) {
+            uint32_t af[NQ][2][4], ah[NQ][2][4];
+            float2 sc2[NQ];
+#pragma unroll
+            for (int q = 0; q < NQ; q++) {
+                uint32_t f[4], fh[4];
+                nib_frag(word_of(sl < 4 ? q0[q] : q1[q], sl & 3), f);
+                uint32_t hw = word_of(hq[q], sl >> 1);
+                if (sl & 1) hw >>= 8;
+                hi_frag(hw, fh);
+                b64_dup(f, af[q]);
+                b64_dup(fh, ah[q]);
+                sc2[q] = *reinterpret_cast<const float2 *>(scw + q * 128 + (sl * 8 + g) * 2);
+            }
+#pragma unroll
+            for (int n = 0; n < 8; n++) {
+                if (n < ntl) {
+                    uint4 b = make_uint4(0u, 0u, 0u, 0u);
+                    if (8 * n + g < T) b = *reinterpret_cast<const uint4 *>(xb + (size_t)(8 * n) * B64_XROW + sl * 64);
+#pragma unroll
+                    for (int q = 0; q < NQ; q++) {
+                        float d4[4];
+                        mma16816_z(d4, af[q][0], b.x, b.y);
+                        mma16816(d4, af[q][1], b.z, b.w);
+                        mma16816(d4, ah[q][0], b.x, b.y);
+                        mma16816(d4, ah[q][1], b.z, b.w);
+                        y[q][n][0] = fmaf(sc2[q].x, d4[0], y[q][n][0]);
+                        y[q][n][1] = fmaf(sc2[q].x, d4[1], y[q][n][1]);
+                        y[q][n][2] = fmaf(sc2[q].y, d4[2], y[q][n][2]);
+                        y[q][n][3] = fmaf(sc2[q].y, d4[3], y[q][n][3]);
+                    }
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+#pragma unroll 1
+        for (int ui = 0; ui < 4; ui++) {
+            uint32_t af[NQ][2][2][4];
+            float dg[NQ], dg8[NQ];
+#pragma unroll
+            for (int q = 0; q < NQ; q++) {
+                const uint4 qv = *reinterpret_cast<const uint4 *>(wst[q] + ui * 512 + lane * 16);
+                const float dv = lane < 16 ? h2f(*reinterpret_cast<const uint16_t *>(wst[q] + BG::Q + ui * 32 + lane * 2)) : 0.0f;
+                dg[q] = __shfl_sync(0xffffffffu, dv, g);
+                dg8[q] = __shfl_sync(0xffffffffu, dv, g + 8);
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    uint32_t f[4];
+                    q8_frag(word_of(qv, 2 * e), word_of(qv, 2 * e + 1), f);
+                    b64_dup(f, af[q][e]);
+                }
+            }
+#pragma unroll
+            for (int n = 0; n < 8; n++) {
+                if (n < ntl) {
+                    uint4 b[2] = {make_uint4(0u, 0u, 0u, 0u), make_uint4(0u, 0u, 0u, 0u)};
+                    if (8 * n + g < T) {
+                        b[0] = *reinterpret_cast<const uint4 *>(xb + (size_t)(8 * n) * B64_XROW + (2 * ui) * 64);
+                        b[1] = *reinterpret_cast<const uint4 *>(xb + (size_t)(8 * n) * B64_XROW + (2 * ui + 1) * 64);
+                    }
+#pragma unroll
+                    for (int q = 0; q < NQ; q++) {
+                        float d4[4];
+                        mma16816_z(d4, af[q][0][0], b[0].x, b[0].y);
+                        mma16816(d4, af[q][0][1], b[0].z, b[0].w);
+                        mma16816(d4, af[q][1][0], b[1].x, b[1].y);
+                        mma16816(d4, af[q][1][1], b[1].z, b[1].w);
+                        y[q][n][0] = fmaf(dg[q], d4[0], y[q][n][0]);
+                        y[q][n][1] = fmaf(dg[q], d4[1], y[q][n][1]);
+                        y[q][n][2] = fmaf(dg8[q], d4[2], y[q][n][2]);
+                        y[q][n][3] = fmaf(dg8[q], d4[3], y[q][n][3]);
+                    }
+                }
+            }
+        }
+    }
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(B64_WARPS * 32, 1) k_gemv_b64(B64Args a) {
+    using BG = B64Geo<TYPE>;
+    constexpr int WB = b64_wbytes<TYPE>(), SBY = b64_stage<TYPE>();
+    constexpr bool KQ = TYPE != XJ_Q8_0;
+    constexpr int NTH = B64_WARPS * 32;
+    extern __shared__ __align__(128) uint8_t smem[];
+    float *scs = reinterpret_cast<float *>(smem + (size_t)B64_STAGES * SBY);
+    float *recv = scs + B64_WARPS * 2 * 128;               // [ns][ceil(256/ns)][B64_RS] partials of this CTA's rows
+    __shared__ __align__(8) uint64_t bars[B64_STAGES];
+    __shared__ __align__(8) uint64_t rbar;                  // partials of this CTA's rows from the other splits
+    __shared__ float tok_inv[B64_T];                        // 1 / range scale (a power of two: exact)
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
+    const int T = a.T, K = a.K, ntl = (T + 7) / 8, ns = a.nsplit;
+    const int blk = blockIdx.x / ns;
+    const int split = ns > 1 ? (int)cluster_rank() : 0;       // = blockIdx.x % ns (1-D clusters of ns CTAs)
+    int j = 0;
+    while (blk >= a.blk_start[j + 1]) j++;
+    const MmaJob &jb = a.job[j];
+    const Tiled &W = jb.w;
+    const int ntiles = (W.N + 15) / 16;
+    const int t0 = (blk - a.blk_start[j]) * B64_TILES;
+    const int nt = ntiles - t0 < B64_TILES ? ntiles - t0 : B64_TILES;
+    const int nch = K / B64_CK;
+    const int c0 = (int)((long long)split * nch / ns), c1 = (int)((long long)(split + 1) * nch / ns);
+    const int nc = c1 - c0;
+    const int nrmax = (B64_ROWS + ns - 1) / ns;
+    const uint32_t act_bytes = (uint32_t)b64_rec_bytes(T);
+    auto issue_w = [&](int i) {       // warp 0: weights of chunk c0 + i for the block's tiles into stage i % B64_STAGES,
+        const int ch = c0 + i;         // one tile per lane (lane 0 also declares the stage's bytes)
+        uint8_t *st = smem + (size_t)(i % B64_STAGES) * SBY + B64_ACT;
+        uint64_t *bar = &bars[i % B64_STAGES];
+        if (lane == 0) mbar_expect_tx(bar, act_bytes + (uint32_t)(nt * WB));
+        __syncwarp();
+        for (int tl = lane; tl < nt; tl += 32) {
+            uint8_t *dst = st + tl * WB;
+            const size_t tile = (size_t)(t0 + tl);
+            if (KQ) {
+                constexpr int QB = Geo<TYPE>::QB, HB = Geo<TYPE>::HB, SB = Geo<TYPE>::SB, DB = Geo<TYPE>::DB;
+                const size_t tu = tile * W.nu + (ch >> 1);
+                const int hh = ch & 1;
+                bulk_g2s(dst, W.q + tu * QB + hh * (QB / 2), QB / 2, bar);
+                if (HB) bulk_g2s(dst + BG::Q, W.h + tu * HB + hh * (HB / 2), HB / 2, bar);
+                bulk_g2s(dst + BG::Q + BG::H, W.s + tu * SB, SB, bar);
+                if (DB) bulk_g2s(dst + BG::Q + BG::H + BG::S, W.d + tu * DB, DB, bar);
+            } else {
+                const size_t tu = tile * W.nu + (size_t)ch * 4;
+                bulk_g2s(dst, W.q + tu * Geo<TYPE>::QB, 4 * Geo<TYPE>::QB, bar);
+                bulk_g2s(dst + BG::Q, W.d + tu * Geo<TYPE>::DB, 4 * Geo<TYPE>::DB, bar);
+            }
+        }
+    };
+    auto issue_x = [&](int i) {       // activation record of chunk c0 + i (after the predecessor finished)
+        bulk_g2s(smem + (size_t)(i % B64_STAGES) * SBY, (const uint8_t *)a.xbuf + (size_t)(c0 + i) * act_bytes, act_bytes,
+                 &bars[i % B64_STAGES]);
+    };
+    const int rb = split * B64_ROWS / ns, nr = (split + 1) * B64_ROWS / ns - rb;   // the rows this CTA finishes
+    if (tid == 0) {
+        for (int q = 0; q < B64_STAGES; q++) mbar_init(&bars[q], 1);
+        mbar_init(&rbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (ns > 1) mbar_expect_tx(&rbar, (uint32_t)((ns - 1) * nr * B64_RS * 4));
+    }
+    if (ns > 1) cluster_arrive();                          // every CTA's receive barrier is armed before any send
+    if (warp == 0) {
+        __syncwarp();
+        for (int i = 0; i < B64_STAGES && i < nc; i++) issue_w(i);
+    }
+    griddep_launch();
+    griddep_wait();
+    if (tid == 0)
+        for (int i = 0; i < B64_STAGES && i < nc; i++) issue_x(i);
+    if (tid < T) tok_inv[tid] = 1.0f / reinterpret_cast<const float *>((const uint8_t *)a.xbuf + (size_t)nch * act_bytes)[tid];
+    const int nq = (warp < nt) + (warp + B64_WARPS < nt);
+    float y[2][8][4];                                      // tile q, n-tile n: rows g / g+8 x tokens 8n+2c, 8n+2c+1
+#pragma unroll
+    for (int q = 0; q < 2; q++)
+#pragma unroll
+        for (int n = 0; n < 8; n++) y[q][n][0] = y[q][n][1] = y[q][n][2] = y[q][n][3] = 0.0f;
+    float *scw = scs + warp * 256;
+    for (int i = 0; i < nc; i++) {
+        const int slot = i % B64_STAGES;
+        uint8_t *st = smem + (size_t)slot * SBY;
+        mbar_wait(&bars[slot], (uint32_t)((i / B64_STAGES) & 1), a.err);
+        const float *xsum = reinterpret_cast<const float *>(st + (size_t)T * B64_XROW);
+        const uint8_t *wst[2] = {st + B64_ACT + warp * WB, st + B64_ACT + (warp + B64_WARPS) * WB};
+        const int hh = (c0 + i) & 1;
+        if (nq == 2) b64_chunk<TYPE, 2>(wst, hh, lane, T, ntl, st, xsum, scw, y);
+        else if (nq == 1) b64_chunk<TYPE, 1>(wst, hh, lane, T, ntl, st, xsum, scw, y);
+        __syncthreads();                                   // the stage is free
+        if (warp == 0 && i + B64_STAGES < nc) {
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            issue_w(i + B64_STAGES);
+            if (lane == 0) issue_x(i + B64_STAGES);
+        }
+    }
+    // ---- partial sums of all 256 rows into this CTA's staging area (idle now), [row][B64_RS]
+    float *part = reinterpret_cast<float *>(smem);
+#pragma unroll
+    for (int q = 0; q < 2; q++) {
+        if (q < nq) {
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                float *dst = part + ((warp + q * B64_WARPS) * 16 + g + 8 * h) * B64_RS;
+#pragma unroll
+                for (int n = 0; n < 8; n++)
+                    if (n < ntl) *reinterpret_cast<float2 *>(dst + 8 * n + 2 * c) = make_float2(y[q][n][2 * h], y[q][n][2 * h + 1]);
+            }
+        }
+    }
+    __syncthreads();
+    if (ns > 1) {
+        // each owner's rows to slot `split` of its receive buffer, one bulk copy per owner
+        cluster_wait();                                    // the owners' receive barriers are armed
+        if (tid < ns && tid != split) {
+            const int o = tid, orb = o * B64_ROWS / ns, onr = (o + 1) * B64_ROWS / ns - orb;
+            asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+            bulk_s2peer(peer_addr(recv + (size_t)split * nrmax * B64_RS, (uint32_t)o), part + (size_t)orb * B64_RS,
+                        (uint32_t)(onr * B64_RS * 4), peer_addr(&rbar, (uint32_t)o));
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // the source may be reused / freed
+        }
+        mbar_wait(&rbar, 0u, a.err);                       // every other split's partials of this CTA's rows
+    }
+    // ---- rows [rb, rb + nr): sum over splits in rank order, epilogue. Thread -> one row, every
+    // tstep-th token (consecutive threads take consecutive rows).
+    const int epi = jb.epi, ldy = (int)jb.ldy, kc = jb.kc;
+    float *yb = jb.y;
+    const int tstep = NTH / nr, rl = tid % nr, tt = tid / nr;
+    const int row = rb + rl, ch = t0 * 16 + row;
+    if (tt < tstep && ch < W.N) {
+        const float *own = part + (size_t)row * B64_RS;
+        const float *rcv = recv + (size_t)rl * B64_RS;
+        auto total = [&](int t) {
+            float sv = 0.0f;
+#pragma unroll
+            for (int r = 0; r < B64_MAXSPLIT; r++)
+                if (r < ns) sv += r == split ? own[t] : rcv[(size_t)r * nrmax * B64_RS + t];
+            return sv * tok_inv[t];
+        };
+        if (epi == EPI_CONV) {
+            // kc <= 9 (b64_ok): fixed-size, predicated loops keep the state in registers
+            float wc[9], wl = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 9; k++) wc[k] = k < kc ? jb.conv_w[(size_t)ch * kc + k] : 0.0f;
+#pragma unroll
+            for (int k = 0; k < 9; k++)
+                if (k == kc - 1) wl = wc[k];
+            for (int t = tt; t < T; t += tstep) {
+                float *stt = jb.conv_state + t * jb.conv_bstride + (size_t)ch * (kc - 1);
+                float cs[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++) cs[k] = k < kc - 1 ? stt[k] : 0.0f;
+                const float v = total(t);
+                float acc = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if (k < kc - 1) acc = fmaf(cs[k], wc[k], acc);
+                acc = fmaf(v, wl, acc);
+#pragma unroll
+                for (int k = 0; k < 7; k++)
+                    if (k < kc - 2) stt[k] = cs[k + 1];
+                stt[kc - 2] = v;
+                yb[(size_t)t * ldy + ch] = silu_f(acc);
+            }
+        } else if (epi == EPI_ADD) {
+            constexpr int U = 4;
+            for (int t0u = tt; t0u < T; t0u += U * tstep) {
+                float yv[U];
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int t = t0u + u * tstep;
+                    yv[u] = t < T ? yb[(size_t)t * ldy + ch] : 0.0f;
+                }
+#pragma unroll
+                for (int u = 0; u < U; u++) {
+                    const int t = t0u + u * tstep;
+                    if (t < T) yb[(size_t)t * ldy + ch] = yv[u] + total(t);
+                }
+            }
+        } else {
+            for (int t = tt; t < T; t += tstep) yb[(size_t)t * ldy + ch] = total(t);
+        }
+    }
+}
+
 // ------------------------------------------------------------------ host: launch
 constexpr size_t MMA_SMEM_MAX = 200 * 1024;              // 4-token launches
 constexpr int MMA_KMAX = MMA_KMAX_PT * MMA_WARPS * 32;   // longest row the prologue stages
@@ -1069,6 +1534,91 @@ inline cudaError_t launch_wide_t(MmaArgs a, const void *xbuf, cudaStream_t st) {
     if (nsl > 1 && a.tiles_per_cta > WIDE_MAXTILES) a.tiles_per_cta = WIDE_MAXTILES;   // carried accumulators
     const dim3 grid((tiles + a.tiles_per_cta - 1) / a.tiles_per_cta), block(MMA_WARPS * 32);
     return launch_pdl(k_gemv_wide<TYPE>, grid, block, smem, st, a, xbuf);
+}
+// 64-token launch on activations prepared by k_prep_xt<true> into a.xbuf. Blocks of 256 rows; when
+// there are fewer blocks than SMs, each block's K chunks are split over a cluster of ns <= B64_MAXSPLIT
+// CTAs, ns chosen (per device, type and block count) to minimise waves x chunks per CTA with the
+// number of clusters that fit the GPU at once.
+template <int TYPE>
+inline cudaError_t launch_b64_t(B64Args a, cudaStream_t st) {
+    constexpr int MAXDEV = 64;
+    static int sms_dev[MAXDEV] = {0};
+    static int occ[MAXDEV][B64_MAXSPLIT + 1] = {};      // clusters of ns CTAs resident at once
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= MAXDEV) dev = 0;
+    constexpr size_t smem = b64_smem<TYPE>();
+    if (!sms_dev[dev]) {
+        cudaFuncSetAttribute(k_gemv_b64<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaDeviceGetAttribute(&sms_dev[dev], cudaDevAttrMultiProcessorCount, dev);
+        occ[dev][1] = sms_dev[dev];
+        for (int ns = 2; ns <= B64_MAXSPLIT; ns++) {
+            cudaLaunchConfig_t q{};
+            q.gridDim = dim3(ns * 64);
+            q.blockDim = dim3(B64_WARPS * 32);
+            q.dynamicSmemBytes = smem;
+            cudaLaunchAttribute ca[1];
+            ca[0].id = cudaLaunchAttributeClusterDimension;
+            ca[0].val.clusterDim.x = (unsigned)ns;
+            ca[0].val.clusterDim.y = 1;
+            ca[0].val.clusterDim.z = 1;
+            q.attrs = ca;
+            q.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, k_gemv_b64<TYPE>, &q) != cudaSuccess) { cudaGetLastError(); n = 0; }
+            occ[dev][ns] = n;
+        }
+    }
+    a.blk_start[0] = 0;
+    for (int j = 0; j < a.njob; j++) a.blk_start[j + 1] = a.blk_start[j] + ((a.job[j].w.N + 15) / 16 + B64_TILES - 1) / B64_TILES;
+    const int nblk = a.blk_start[a.njob], nch = a.K / B64_CK;
+    int best = 1;
+    long long best_cost = (long long)((nblk + occ[dev][1] - 1) / occ[dev][1]) * nch;
+    for (int ns = 2; ns <= B64_MAXSPLIT && ns <= nch; ns++) {
+        if (occ[dev][ns] < 1) continue;
+        const long long cost = (long long)((nblk + occ[dev][ns] - 1) / occ[dev][ns]) * ((nch + ns - 1) / ns);
+        if (cost < best_cost) { best_cost = cost; best = ns; }
+    }
+    const int ns = best;
+    a.nsplit = ns;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(nblk * ns);
+    cfg.blockDim = dim3(B64_WARPS * 32);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (g_pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (ns > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = (unsigned)ns;
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = 1;
+        na++;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, k_gemv_b64<TYPE>, a);
+}
+inline cudaError_t launch_b64(const B64Args &a, int type, cudaStream_t st) {
+    switch (type) {
+    case XJ_Q4_K: return launch_b64_t<XJ_Q4_K>(a, st);
+    case XJ_Q6_K: return launch_b64_t<XJ_Q6_K>(a, st);
+    case XJ_Q8_0: return launch_b64_t<XJ_Q8_0>(a, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+// Matrices and epilogues the 64-token kernel takes: tiled types with K a multiple of the chunk, and no
+// epilogue that runs across tokens (the sequential conv of one sequence's prompt) or picks an argmax.
+inline bool b64_ok(const MmaJob &j, int K) {
+    if (K % B64_CK || K > MMA_KMAX_PT * MMA_WARPS * 32) return false;
+    if (j.w.type != XJ_Q4_K && j.w.type != XJ_Q6_K && j.w.type != XJ_Q8_0) return false;
+    if (j.epi == EPI_ARGMAX || (j.epi == EPI_CONV && (!j.conv_bstride || j.kc > 9 || j.conv_ck))) return false;
+    return true;
 }
 inline cudaError_t launch_wide(const MmaArgs &a, int type, const void *xbuf, cudaStream_t st) {
     switch (type) {

@@ -191,9 +191,15 @@ template <int S, class Bar>
 XJ_DEV void gdn_head(const GdnArgs &a, int hv, int tid) {
     constexpr int P = S / 4, NT = 4 * S;
     __shared__ float qs[S], ks[S];
-    __shared__ double red[32];
+    __shared__ double red[32], red2[32];
     const int hk = hv % a.Hk;
-    const int j = tid >> 2, qq = tid & 3;
+    const int j = tid >> 2, qq = tid & 3, lane = tid & 31, w = tid >> 5;
+    // this token's operands first (independent of the state), then the state slice
+    const float dtv = a.dt[hv], Av = a.A[hv], nwj = a.nw[j];
+    const float *x = a.qkv;
+    float qv = tid < S ? lda(x + hk * S + tid) : 0.0f, kv = tid < S ? lda(x + a.key_dim + hk * S + tid) : 0.0f;
+    float vj = lda(x + 2 * a.key_dim + hv * S + j), zj = lda(a.z + hv * S + j);
+    float bt = lda(a.beta + hv), al = lda(a.alpha + hv);
     float row[P];
     float *M = a.ssm + (size_t)hv * S * S + (size_t)j * S + qq * P;
 #pragma unroll
@@ -203,25 +209,38 @@ XJ_DEV void gdn_head(const GdnArgs &a, int hv, int tid) {
     }
     const float qscale = 1.0f / sqrtf((float)S);
     for (int t = 0; t < a.T; t++) {
-        const float *x = a.qkv + t * a.ldq;
-        // L2 norms of q and k (sums in double, core/xj_cpu.c:185-193)
-        const float qv = tid < S ? lda(x + hk * S + tid) : 0.0f, kv = tid < S ? lda(x + a.key_dim + hk * S + tid) : 0.0f;
-        const double sq = group_sum_d<Bar>((double)qv * qv, red, tid, NT);
-        const double sk2 = group_sum_d<Bar>((double)kv * kv, red, tid, NT);
+        if (t > 0) {
+            x = a.qkv + t * a.ldq;
+            qv = tid < S ? lda(x + hk * S + tid) : 0.0f;
+            kv = tid < S ? lda(x + a.key_dim + hk * S + tid) : 0.0f;
+            vj = lda(x + 2 * a.key_dim + hv * S + j);
+            zj = lda(a.z + t * a.ldz + hv * S + j);
+            bt = lda(a.beta + t * a.ldg + hv);
+            al = lda(a.alpha + t * a.ldg + hv);
+        }
+        // L2 norms of q and k (sums in double, core/xj_cpu.c:185-193): both in one pass, each with the
+        // warp-then-warps order of group_sum_d
+        double sq = warp_sum_d((double)qv * qv), sk2 = warp_sum_d((double)kv * kv);
+        Bar::sync();
+        if (lane == 0) { red[w] = sq; red2[w] = sk2; }
+        Bar::sync();
+        sq = 0.0; sk2 = 0.0;
+        for (int i = 0; i < NT / 32; i++) sq += red[i];
+        for (int i = 0; i < NT / 32; i++) sk2 += red2[i];
         if (tid < S) {
             qs[tid] = qv * (1.0f / sqrtf((float)sq + a.eps));
             ks[tid] = kv * (1.0f / sqrtf((float)sk2 + a.eps));
         }
         Bar::sync();
-        const float b = sigm_f(lda(a.beta + t * a.ldg + hv));
-        const float g = softplus_f(lda(a.alpha + t * a.ldg + hv) + a.dt[hv]) * a.A[hv];
+        const float b = sigm_f(bt);
+        const float g = softplus_f(al + dtv) * Av;
         const float eg = expf(g);
         float sk = 0.0f;
 #pragma unroll
         for (int i = 0; i < P; i++) { row[i] *= eg; sk = fmaf(row[i], ks[qq * P + i], sk); }
         sk += __shfl_xor_sync(0xffffffffu, sk, 1);
         sk += __shfl_xor_sync(0xffffffffu, sk, 2);
-        const float delta = (lda(x + 2 * a.key_dim + hv * S + j) - sk) * b;
+        const float delta = (vj - sk) * b;
         float acc = 0.0f;
 #pragma unroll
         for (int i = 0; i < P; i++) { row[i] = fmaf(ks[qq * P + i], delta, row[i]); acc = fmaf(row[i], qs[qq * P + i], acc); }
@@ -231,7 +250,7 @@ XJ_DEV void gdn_head(const GdnArgs &a, int hv, int tid) {
         const double so = group_sum_d<Bar>(qq == 0 ? (double)o * o : 0.0, red, tid, NT);
         if (qq == 0) {
             const float sc = 1.0f / sqrtf((float)(so / S) + a.eps);
-            a.out[t * a.ldo + hv * S + j] = o * sc * a.nw[j] * silu_f(lda(a.z + t * a.ldz + hv * S + j));
+            a.out[t * a.ldo + hv * S + j] = o * sc * nwj * silu_f(zj);
         }
         if (a.ck_ssm && t < a.T - 1) {
             float *C = a.ck_ssm + ((size_t)t * a.Hv + hv) * S * S + (size_t)j * S + qq * P;
@@ -557,7 +576,7 @@ static __global__ void __launch_bounds__(1024) k_argmax_final(ArgmaxArgs a) {
 
 // Grid (Hv, B), 4*S threads; state of sequence b at ssm + b*state_stride.
 template <int S>
-__global__ void __launch_bounds__(4 * S) k_gdn_batch(GdnArgs a, long long state_stride) {
+__global__ void __launch_bounds__(4 * S, 2) k_gdn_batch(GdnArgs a, long long state_stride) {
     griddep_wait();
     const int b = blockIdx.y;
     GdnArgs c = a;
@@ -591,10 +610,12 @@ static __global__ void __launch_bounds__(128) k_attn_batch(AttnArgs a, const int
     attn_head<KV, DPL, BarBlock>(attn_seq<KV>(a, npast_b, kv_stride, blockIdx.y), blockIdx.x, 0, threadIdx.x);
 }
 
-// Grid (ceil(V/16), B), 32 threads: per-tile argmax partials of each sequence's logits row.
-static __global__ void k_argmax_rows_batch(const float *logits, int V, float *pbest, float *psecond, int *pidx, int ntiles) {
+// Grid (ceil(ntiles/16), B), 256 threads: per-tile (16-row) argmax partials of each sequence's logits row.
+static __global__ void __launch_bounds__(256) k_argmax_rows_batch(const float *logits, int V, float *pbest, float *psecond,
+                                                                   int *pidx, int ntiles) {
     griddep_wait();
-    const int b = blockIdx.y, tile = blockIdx.x, row = threadIdx.x & 15, r = tile * 16 + row;
+    // 16 tiles per block, one per half-warp (the shuffles below stay inside a half-warp)
+    const int b = blockIdx.y, tile = blockIdx.x * 16 + (threadIdx.x >> 4), row = threadIdx.x & 15, r = tile * 16 + row;
     const float *lg = logits + (size_t)b * V;
     float v = r < V ? lg[r] : -INFINITY, v2 = -INFINITY;
     int vi = r < V ? r : 0x7fffffff;
@@ -605,7 +626,7 @@ static __global__ void k_argmax_rows_batch(const float *logits, int V, float *pb
         if (ov > v || (ov == v && oi < vi)) { v2 = fmaxf(v, ov2); v = ov; vi = oi; }
         else v2 = fmaxf(v2, ov);
     }
-    if (threadIdx.x == 0) {
+    if (row == 0 && tile < ntiles) {
         const size_t o = (size_t)b * ntiles + tile;
         pbest[o] = v; psecond[o] = v2; pidx[o] = vi;
     }

@@ -72,7 +72,8 @@ struct Impl {
     float *x = nullptr, *xin = nullptr, *h = nullptr, *qkvb = nullptr, *z = nullptr, *beta = nullptr, *alpha = nullptr;
     float *o = nullptr, *qrot = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
     float *q = nullptr, *k = nullptr, *v = nullptr, *hn = nullptr;
-    void *wide_buf = nullptr;   // activations of a wide (5..16-token) GEMV launch, prepared by k_prep_x
+    void *wide_buf = nullptr;   // activations of a wide (5..16-token) GEMV launch, prepared by k_prep_xt<false>
+    void *b64_buf = nullptr;    // activations of a 64-token GEMV launch (stages taking more than 16 tokens)
     float *pbest = nullptr, *psecond = nullptr;
     int *pidx = nullptr;
     int *derr = nullptr;       // device error word: set when a kernel's bounded wait gives up
@@ -198,6 +199,11 @@ void launch(Impl *im, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
     im->nlaunch++;
 }
 
+// Activations of the 64-token GEMV: 64 tokens at the longest K.
+int alloc_b64(Impl *im, char *err, size_t errlen) {
+    return dalloc(im, (uint8_t **)&im->b64_buf, b64_x_bytes(B64_T, MMA_KMAX), err, errlen);
+}
+
 void rmsnorm(Impl *im, const float *x, long long ldx, const float *w, float *y, long long ldy, int n, int rows, float eps) {
     launch(im, k_rmsnorm, dim3(rows), dim3(256), 0, x, ldx, w, y, ldy, n, eps);
 }
@@ -239,6 +245,32 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
         groups.push_back(m);
         gtype.push_back(type);
     }
+    // more than 16 tokens and every matrix fit for it: 64-token launches (weights streamed once per 64
+    // tokens; each token's result depends only on the matrix shapes, not on the other tokens)
+    bool use64 = T > MMA_WIDE_T && im->b64_buf && !groups.empty();
+    for (const MmaArgs &m : groups)
+        for (int j = 0; j < m.njob; j++) use64 = use64 && b64_ok(m.job[j], K);
+    if (use64) {
+        for (int t0 = 0; t0 < T; t0 += B64_T) {
+            const int Tc = T - t0 < B64_T ? T - t0 : B64_T;
+            launch(im, k_prep_xt<true>, dim3(Tc), dim3(MMA_WARPS * 32), 0, (const float *)(x + t0 * ldx),
+                   (const float *)(x2 ? x2 + t0 * ldx : nullptr), ldx, K, pro, norm_w, eps, im->b64_buf, Tc);
+            for (size_t gi = 0; gi < groups.size(); gi++) {
+                const MmaArgs &m = groups[gi];
+                B64Args b{};
+                b.njob = m.njob; b.T = Tc; b.K = K;
+                b.xbuf = im->b64_buf; b.err = im->derr;
+                for (int j = 0; j < m.njob; j++) {
+                    b.job[j] = m.job[j];
+                    if (b.job[j].y) b.job[j].y = m.job[j].y + t0 * m.job[j].ldy;
+                    if (b.job[j].conv_bstride) b.job[j].conv_state = m.job[j].conv_state + t0 * m.job[j].conv_bstride;
+                }
+                launch_b64(b, gtype[gi], im->st);
+                im->nlaunch++;
+            }
+        }
+        groups.clear();
+    }
     // tokens in chunks of 16 (wide launches on activations prepared once per chunk) or, for 4 tokens or
     // fewer, one launch; each token's result does not depend on the chunking (the conv epilogue carries
     // its state across chunks, its checkpoints are indexed by absolute token)
@@ -247,7 +279,7 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
         const int Tc = T - t0 < tch ? T - t0 : tch;
         const bool wide = Tc > MMA_MAXT;
         if (wide && !groups.empty()) {
-            launch(im, k_prep_x, dim3(Tc), dim3(MMA_WARPS * 32), 0, (const float *)(x + t0 * ldx),
+            launch(im, k_prep_xt<false>, dim3(Tc), dim3(MMA_WARPS * 32), 0, (const float *)(x + t0 * ldx),
                    (const float *)(x2 ? x2 + t0 * ldx : nullptr), ldx, K, pro, norm_w, eps, im->wide_buf, Tc);
         }
         for (size_t gi = 0; gi < groups.size(); gi++) {
@@ -650,6 +682,7 @@ int build(xj_stage *s, char *err, size_t errlen) {
         dalloc(im, &im->npast, 4, err, errlen) || dalloc(im, &im->step, 4, err, errlen) ||
         dalloc(im, &im->derr, 4, err, errlen) ||
         dalloc(im, &im->tok, (size_t)B, err, errlen) || dalloc(im, &im->cur, 4, err, errlen)) return -1;
+    if (B > MMA_WIDE_T && alloc_b64(im, err, errlen)) return -1;
     if (s->has_head) {
         const size_t nt = (size_t)(m->output.ne1 + 15) / 16;
         if (dalloc(im, &im->pbest, nt, err, errlen) || dalloc(im, &im->psecond, nt, err, errlen) ||
@@ -950,7 +983,7 @@ void head_batch(BatchImpl *bi, const float *x, int r0, int nr, int32_t *cur, flo
     const xj_hparams *hp = &s->m->hp;
     const int V = im->output.N, B = nr;
     gemv(im, x, nullptr, hp->n_embd, B, PRO_NORM, im->output_norm, hp->eps, {{im->output, im->logits, V}});
-    launch(im, k_argmax_rows_batch, dim3(bi->ntiles, B), dim3(32), 0, (const float *)im->logits, V, bi->pbest, bi->psecond,
+    launch(im, k_argmax_rows_batch, dim3((bi->ntiles + 15) / 16, B), dim3(256), 0, (const float *)im->logits, V, bi->pbest, bi->psecond,
            bi->pidx, bi->ntiles);
     ArgmaxArgs a;
     a.pbest = bi->pbest; a.psecond = bi->psecond; a.pidx = bi->pidx; a.ntiles = bi->ntiles;
@@ -1123,7 +1156,7 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
 // `copies` device copies of W (so L2 cannot serve the weights) when ms != nullptr.
 static int gemv_diag(int type, const void *w, int k, int n, const float *x, int t, float *y, int path, int copies,
                      int iters, float *ms, char *err, size_t errlen) {
-    if (t < 1 || t > MAXT) { seterr(err, errlen, "t must be in 1..%d", MAXT); return -1; }
+    if (t < 1 || t > B64_T) { seterr(err, errlen, "t must be in 1..%d", B64_T); return -1; }
     if (k % 8) { seterr(err, errlen, "k must be a multiple of 8"); return -1; }
     Impl tmp;
     Impl *im = &tmp;
@@ -1149,7 +1182,8 @@ static int gemv_diag(int type, const void *w, int k, int n, const float *x, int 
     }
     if (dalloc(im, &dx, (size_t)t * k, err, errlen) || dalloc(im, &dy, (size_t)t * n, err, errlen) ||
         dalloc(im, &im->hn, (size_t)t * k, err, errlen) || dalloc(im, &im->derr, 1, err, errlen) ||
-        dalloc(im, (uint8_t **)&im->wide_buf, wide_x_bytes(MMA_WIDE_T, MMA_KMAX), err, errlen)) goto done;
+        dalloc(im, (uint8_t **)&im->wide_buf, wide_x_bytes(MMA_WIDE_T, MMA_KMAX), err, errlen) ||
+        (t > MMA_WIDE_T && alloc_b64(im, err, errlen))) goto done;
     cudaMemset(im->derr, 0, sizeof(int));
     if (cudaMemcpy(dx, x, sizeof(float) * (size_t)t * k, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) { seterr(err, errlen, "copy failed"); goto done; }

@@ -2,9 +2,11 @@
 
 Every matrix-vector product computes each token's column independently in a fixed order, and the
 attention / Gated-DeltaNet / greedy-pick kernels of the batch run the single-sequence device code on
-each sequence's own state, so sequence b of a batch must produce exactly (bit for bit, margins
-included) what xj_cuda_decode produces for that sequence alone through the per-phase kernels; one of
-the sequences is the golden prompt, whose ids are the reference's.
+each sequence's own state. Up to 16 sequences the matrix-vector kernels are the single-sequence
+arithmetic, so sequence b of a batch must produce exactly (bit for bit, margins included) what
+xj_cuda_decode produces for that sequence alone; above 16 the 64-token kernel adds K in another order
+(fp32-level differences), so the ids must still agree and the margins to fp32 accuracy. One of the
+sequences is the golden prompt, whose ids are the reference's.
 """
 from __future__ import annotations
 
@@ -40,7 +42,8 @@ def single(xc, m, prompt, n_gen):
     return out
 
 
-@pytest.mark.parametrize("which,n_seq", [("config0", 1), ("config0", 5), ("mid", 3), ("mid", 20)])
+@pytest.mark.parametrize("which,n_seq", [("config0", 1), ("config0", 5), ("mid", 3), ("config0", 24), ("mid", 20),
+                                         ("mid", 64)])
 def test_batch_matches_single_sequence_decode(xc, golden, config0_path, mid_path, which, n_seq):
     xc.set_option(xc.OPT_KV_F32, 0)
     m = xc.Model(config0_path if which == "config0" else mid_path)
@@ -53,7 +56,11 @@ def test_batch_matches_single_sequence_decode(xc, golden, config0_path, mid_path
     for i in range(min(n_seq, 3)):
         t1, m1, _ = single(xc, m, P[i], n_gen)
         assert toks[i].tolist() == t1.tolist(), i
-        assert np.array_equal(mar[i], m1), i
+        if n_seq <= 16:
+            assert np.array_equal(mar[i], m1), i
+        else:
+            d = np.abs(mar[i] - m1).max()
+            assert d <= 1e-4 * max(1.0, float(np.abs(m1).max())), (i, d)
     pre, dec = b.last_launches()
     assert pre > 0 and dec > 0
     b.close()
