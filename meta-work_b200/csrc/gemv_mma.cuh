@@ -141,6 +141,12 @@ XJ_DEV uint32_t hsub2(uint32_t a, uint32_t b) {
     return r;
 }
 
+XJ_DEV uint32_t hadd2(uint32_t a, uint32_t b) {
+    uint32_t r;
+    asm("add.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
+    return r;
+}
+
 XJ_DEV uint32_t hfma2(uint32_t a, uint32_t b, uint32_t c) {
     uint32_t r;
     asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
@@ -1173,17 +1179,19 @@ XJ_DEV void b64_chunk(const uint8_t *const *wst, int hh, int lane, int T, int nt
         __syncwarp();
 #pragma unroll
         for (int sl = 0; sl < 8; sl++) {
-            uint32_t af[NQ][2][4], ah[NQ][2][4];
+            uint32_t af[NQ][2][4];
             float2 sc2[NQ];
 #pragma unroll
             for (int q = 0; q < NQ; q++) {
+                // code q - 32 = low nibble + (16*high - 32), in [-32, 31]: the fp16 sum is exact
                 uint32_t f[4], fh[4];
                 nib_frag(word_of(sl < 4 ? q0[q] : q1[q], sl & 3), f);
                 uint32_t hw = word_of(hq[q], sl >> 1);
                 if (sl & 1) hw >>= 8;
                 hi_frag(hw, fh);
+#pragma unroll
+                for (int k = 0; k < 4; k++) f[k] = hadd2(f[k], fh[k]);
                 b64_dup(f, af[q]);
-                b64_dup(fh, ah[q]);
                 sc2[q] = *reinterpret_cast<const float2 *>(scw + q * 128 + (sl * 8 + g) * 2);
             }
 #pragma unroll
@@ -1196,8 +1204,6 @@ XJ_DEV void b64_chunk(const uint8_t *const *wst, int hh, int lane, int T, int nt
                         float d4[4];
                         mma16816_z(d4, af[q][0], b.x, b.y);
                         mma16816(d4, af[q][1], b.z, b.w);
-                        mma16816(d4, ah[q][0], b.x, b.y);
-                        mma16816(d4, ah[q][1], b.z, b.w);
                         y[q][n][0] = fmaf(sc2[q].x, d4[0], y[q][n][0]);
                         y[q][n][1] = fmaf(sc2[q].x, d4[1], y[q][n][1]);
                         y[q][n][2] = fmaf(sc2[q].y, d4[2], y[q][n][2]);
@@ -1572,11 +1578,13 @@ inline cudaError_t launch_b64_t(B64Args a, cudaStream_t st) {
     a.blk_start[0] = 0;
     for (int j = 0; j < a.njob; j++) a.blk_start[j + 1] = a.blk_start[j] + ((a.job[j].w.N + 15) / 16 + B64_TILES - 1) / B64_TILES;
     const int nblk = a.blk_start[a.njob], nch = a.K / B64_CK;
+    // cost in chunk times: waves x (chunks per CTA + ~2 for the start and the split exchange / epilogue)
+    constexpr int FIXED = 2;
     int best = 1;
-    long long best_cost = (long long)((nblk + occ[dev][1] - 1) / occ[dev][1]) * nch;
+    long long best_cost = (long long)((nblk + occ[dev][1] - 1) / occ[dev][1]) * (nch + FIXED);
     for (int ns = 2; ns <= B64_MAXSPLIT && ns <= nch; ns++) {
         if (occ[dev][ns] < 1) continue;
-        const long long cost = (long long)((nblk + occ[dev][ns] - 1) / occ[dev][ns]) * ((nch + ns - 1) / ns);
+        const long long cost = (long long)((nblk + occ[dev][ns] - 1) / occ[dev][ns]) * ((nch + ns - 1) / ns + FIXED);
         if (cost < best_cost) { best_cost = cost; best = ns; }
     }
     const int ns = best;

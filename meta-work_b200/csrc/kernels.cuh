@@ -181,11 +181,12 @@ struct GdnArgs {
 };
 
 // Gated DeltaNet for value head hv over T tokens, 4*S threads (tid < 4*S); thread (j, q) keeps key
-// dims [q*S/4, (q+1)*S/4) of row j of the head's state M in registers (core/xj_cpu.c:194-219):
+// dims {16m + 4q + e : m < S/16, e < 4} of row j of the head's state M in registers, so the four
+// threads of a row read and write 64 contiguous bytes per access (core/xj_cpu.c:194-219):
 //   q, k <- L2-normalised key head hv % Hk;  b = sigmoid(beta);  g = softplus(alpha + dt) * A
 //   M *= exp(g);  delta_j = (v_j - M_j.k) * b;  M_j += delta_j k;  o_j = M_j.q / sqrt(S)
 //   out = rmsnorm(o) * norm_w * silu(z)
-// State layout [Hv][S(j)][S(i)] as the CPU oracle; each thread's slice is contiguous.
+// State layout [Hv][S(j)][S(i)] as the CPU oracle.
 // ck_ssm != nullptr saves M after token t < T-1 into ck_ssm[t][Hv][S][S].
 template <int S, class Bar>
 XJ_DEV void gdn_head(const GdnArgs &a, int hv, int tid) {
@@ -200,11 +201,11 @@ XJ_DEV void gdn_head(const GdnArgs &a, int hv, int tid) {
     float qv = tid < S ? lda(x + hk * S + tid) : 0.0f, kv = tid < S ? lda(x + a.key_dim + hk * S + tid) : 0.0f;
     float vj = lda(x + 2 * a.key_dim + hv * S + j), zj = lda(a.z + hv * S + j);
     float bt = lda(a.beta + hv), al = lda(a.alpha + hv);
-    float row[P];
-    float *M = a.ssm + (size_t)hv * S * S + (size_t)j * S + qq * P;
+    float row[P];                       // row[4m + e] = M[j][16m + 4qq + e]
+    float *M = a.ssm + (size_t)hv * S * S + (size_t)j * S + 4 * qq;
 #pragma unroll
     for (int i = 0; i < P; i += 4) {
-        const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(M + i));
+        const float4 v4 = __ldcg(reinterpret_cast<const float4 *>(M + 4 * i));
         row[i] = v4.x; row[i + 1] = v4.y; row[i + 2] = v4.z; row[i + 3] = v4.w;
     }
     const float qscale = 1.0f / sqrtf((float)S);
@@ -237,13 +238,17 @@ XJ_DEV void gdn_head(const GdnArgs &a, int hv, int tid) {
         const float eg = expf(g);
         float sk = 0.0f;
 #pragma unroll
-        for (int i = 0; i < P; i++) { row[i] *= eg; sk = fmaf(row[i], ks[qq * P + i], sk); }
+        for (int i = 0; i < P; i++) { row[i] *= eg; sk = fmaf(row[i], ks[4 * (i & ~3) + 4 * qq + (i & 3)], sk); }
         sk += __shfl_xor_sync(0xffffffffu, sk, 1);
         sk += __shfl_xor_sync(0xffffffffu, sk, 2);
         const float delta = (vj - sk) * b;
         float acc = 0.0f;
 #pragma unroll
-        for (int i = 0; i < P; i++) { row[i] = fmaf(ks[qq * P + i], delta, row[i]); acc = fmaf(row[i], qs[qq * P + i], acc); }
+        for (int i = 0; i < P; i++) {
+            const int col = 4 * (i & ~3) + 4 * qq + (i & 3);
+            row[i] = fmaf(ks[col], delta, row[i]);
+            acc = fmaf(row[i], qs[col], acc);
+        }
         acc += __shfl_xor_sync(0xffffffffu, acc, 1);
         acc += __shfl_xor_sync(0xffffffffu, acc, 2);
         const float o = acc * qscale;
@@ -253,14 +258,14 @@ XJ_DEV void gdn_head(const GdnArgs &a, int hv, int tid) {
             a.out[t * a.ldo + hv * S + j] = o * sc * nwj * silu_f(zj);
         }
         if (a.ck_ssm && t < a.T - 1) {
-            float *C = a.ck_ssm + ((size_t)t * a.Hv + hv) * S * S + (size_t)j * S + qq * P;
+            float *C = a.ck_ssm + ((size_t)t * a.Hv + hv) * S * S + (size_t)j * S + 4 * qq;
 #pragma unroll
-            for (int i = 0; i < P; i += 4) *reinterpret_cast<float4 *>(C + i) = make_float4(row[i], row[i + 1], row[i + 2], row[i + 3]);
+            for (int i = 0; i < P; i += 4) *reinterpret_cast<float4 *>(C + 4 * i) = make_float4(row[i], row[i + 1], row[i + 2], row[i + 3]);
         }
         Bar::sync();
     }
 #pragma unroll
-    for (int i = 0; i < P; i += 4) *reinterpret_cast<float4 *>(M + i) = make_float4(row[i], row[i + 1], row[i + 2], row[i + 3]);
+    for (int i = 0; i < P; i += 4) *reinterpret_cast<float4 *>(M + 4 * i) = make_float4(row[i], row[i + 1], row[i + 2], row[i + 3]);
 }
 
 // One block of 4*S threads per value head.
