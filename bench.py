@@ -182,6 +182,62 @@ def cpu_baseline(K_cap=24):
             "sample": f"{cfg.name}: 32-token prompt, {K_cap} greedy decode steps at batch 1 (oracle/_ref, {threads} threads)"}
 
 
+def run_gdn(xjcuda, peak, peak_kind):
+    """BASELINE config 2, decode: one Gated DeltaNet step of 16 heads x 128x128 fp32 state per sequence
+    at batch 1 and 64 (the batch kernel of batched decode), states rotated over >= 256 MiB so that L2
+    cannot serve them. Bytes = state read + written."""
+    out = {"workload": "config2 GDN decode, 16 heads, S=128, fp32 state", "unit": "GB/s"}
+    for B in (1, 64):
+        ms = xjcuda.gdn_time(128, 16, B, iters=50)
+        nbytes = 2 * B * 16 * 128 * 128 * 4
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[f"b{B}"] = {"us": round(ms * 1e3, 2), "state_bytes": nbytes, "achieved": round(gbs, 1),
+                        "frac": round(gbs / peak, 4)}
+    out["peak"] = peak
+    out["peak_kind"] = peak_kind
+    return out
+
+
+def run_spec(args, model, rank, world, barrier, xjcuda, synth, local):
+    """greedy speculative decoding, target = config 3, draft = the E=1024 8-layer Q8_0
+    model with the target's vocabulary, k = 4; args.spec seeded 256-token prompts per GPU, 256 tokens each.
+    Output ids equal plain greedy decoding by construction (tested); reports emitted tokens/s and target
+    forwards/s over the whole job (prompt processing included), and the acceptance of drafted tokens."""
+    import torch
+    dpath = synth.cached_gguf(synth.DRAFT, os.environ.get("XJ_MODEL_DIR", f"/tmp/xj_models_r{local}"))
+    dmodel = xjcuda.Model(dpath)
+    n_prompt, n_gen, k = 256, 256, 4
+    rng = np.random.default_rng(777 + rank)
+    prompts = rng.integers(0, model.n_vocab, (args.spec, n_prompt)).astype(np.int32)
+    stats = np.zeros(4, np.int64)
+    barrier()
+    t0 = time.perf_counter()
+    for i in range(args.spec):
+        t = xjcuda.Stage(model, 0, model.n_layer, n_prompt + n_gen + 16, 16)
+        d = xjcuda.Stage(dmodel, 0, dmodel.n_layer, n_prompt + n_gen + 16, 16)
+        _, st = t.spec_decode(d, prompts[i], n_gen, k)
+        stats += np.array(st, np.int64)
+        t.close()
+        d.close()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    w = wall
+    if world > 1:
+        import torch.distributed as dist
+        x = torch.tensor([wall], device="cuda")
+        dist.all_reduce(x, op=dist.ReduceOp.MAX)
+        w = float(x[0])
+    if rank != 0:
+        return None
+    return {"workload": "config4 speculative: target config3, draft 1024x8 Q8_0 (vocab 151936), k=4",
+            "prompts_per_gpu": args.spec, "prompt": n_prompt, "gen": n_gen,
+            "value": round(world * args.spec * n_gen / w, 1), "unit": "emitted tok/s",
+            "target_forwards_per_s": round(world * int(stats[0]) / w, 1),
+            "acceptance": round(int(stats[2]) / max(1, int(stats[1])), 4),
+            "rounds": int(stats[0]), "drafted": int(stats[1]), "accepted": int(stats[2]),
+            "timing": "host wall clock per GPU, max over ranks, stages built and prompts processed inside"}
+
+
 def run_batch(args, cfg, model, rank, world, barrier, xjcuda):
     """Batched greedy decode: args.batch independent sequences per GPU in lockstep (xj_cuda_batch_*),
     each with its own seeded prompt of args.prompt tokens; K timed steps = one token of every sequence."""
@@ -292,6 +348,8 @@ def main():
     ap.add_argument("--pipeline", action="store_true",
                     help="under torchrun: one layer range per GPU (NCCL layer pipeline) on --batch sequences")
     ap.add_argument("--micro-batches", type=int, default=2)
+    ap.add_argument("--spec", type=int, default=0,
+                    help="BASELINE config 4: speculative decoding of this many 256-token prompts per GPU (0: skip)")
     args = ap.parse_args()
     rank, local, world = dist_env()
     load_pkg()
@@ -351,6 +409,7 @@ def main():
     e2e = world * args.steps / (e2e_max / 1e3)
     stage.close()
     batch_line = run_batch(args, cfg, model, rank, world, barrier, xjcuda) if args.batch > 0 else None
+    spec_line = run_spec(args, model, rank, world, barrier, xjcuda, synth, local) if args.spec > 0 else None
     if rank == 0:
         peak, peak_kind = hbm_peak()
         b = step_bytes(cfg, pos0 + args.steps // 2)
@@ -380,6 +439,9 @@ def main():
         }
         if batch_line:
             line["batch"] = batch_line
+        line["gdn"] = run_gdn(xjcuda, peak, peak_kind)
+        if spec_line:
+            line["spec"] = spec_line
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline()
         print(json.dumps(line))

@@ -74,6 +74,21 @@ int xj_cuda_gemv(int type, const void *w, int k, int n, const float *x, int T, f
 // distinct device copies of W, so the last-level cache cannot serve the weights (GEMV microbenchmark).
 int xj_cuda_gemv_time(int type, const void *w, int k, int n, int T, int copies, int iters, int path, float *ms,
                       char *err, size_t errlen);
+// Greedy speculative decoding with a separate draft model: both stages take the
+// prompt, then each round the draft proposes k tokens (device greedy decode), the target verifies the
+// last emitted token and the k drafts in one forward (k + 1 rows of logits, device greedy picks), the
+// longest agreeing prefix plus the target's own next pick are emitted, the target rolls back through its
+// checkpoints and the draft's recurrent state is restored and re-fed. out[0..n_gen) equals plain greedy
+// decoding of the target. stats (may be NULL): target verify forwards, drafted tokens, accepted drafted
+// tokens, draft re-feeds. Both stages span all layers with the head, share the vocabulary, and take
+// k + 1 tokens per forward.
+int xj_cuda_spec_decode(xj_stage *target, xj_stage *draft, const int32_t *prompt, int n_prompt, int n_gen, int k,
+                        int32_t *out, long long *stats, char *err, size_t errlen);
+
+// Gated DeltaNet decode microbenchmark: average device time (ms) of one decode step
+// of B sequences x Hv heads with an S x S fp32 state each (S in 16, 32, 64, 128), the batch kernel of
+// batched decode, states rotated over >= 256 MiB of copies so the last-level cache cannot serve them.
+int xj_cuda_gdn_time(int S, int Hv, int B, int iters, float *ms, char *err, size_t errlen);
 
 // Number of kernel launches in one replay of the stage's cached decode-step graph (0 before the first
 // xj_cuda_decode call that generated more than one token).

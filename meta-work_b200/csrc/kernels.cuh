@@ -650,4 +650,37 @@ static __global__ void __launch_bounds__(1024) k_argmax_final_batch(ArgmaxArgs a
     argmax_final_dev<BarBlock>(c, threadIdx.x, blockDim.x);
 }
 
+// Grid (T), 1024 threads: ids[t] = argmax of logits row t, the lowest index among equal maxima (the
+// strict '>' of core/xj_spec.c:12-16).
+static __global__ void __launch_bounds__(1024) k_argmax_pick_rows(const float *logits, int V, int32_t *ids) {
+    griddep_wait();
+    __shared__ float sb[32];
+    __shared__ int si[32];
+    const float *lg = logits + (size_t)blockIdx.x * V;
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float v = lg[i];
+        if (v > best) { best = v; bi = i; }
+    }
+    for (int o = 16; o; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+    }
+    const int w = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    if (lane == 0) { sb[w] = best; si[w] = bi; }
+    __syncthreads();
+    if (w == 0) {
+        best = lane < (int)(blockDim.x >> 5) ? sb[lane] : -INFINITY;
+        bi = lane < (int)(blockDim.x >> 5) ? si[lane] : 0x7fffffff;
+        for (int o = 16; o; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, best, o);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (ov > best || (ov == best && oi < bi)) { best = ov; bi = oi; }
+        }
+        if (lane == 0) ids[blockIdx.x] = bi == 0x7fffffff ? 0 : bi;
+    }
+}
+
 }  // namespace xjk

@@ -97,6 +97,9 @@ struct Impl {
     int *mk_diag = nullptr;
     float *mk_apart = nullptr;
     int *mk_acnt = nullptr;
+    // recurrent-state snapshot (draft stage of speculative decoding): conv and GDN state per layer
+    std::vector<float *> snap_conv, snap_ssm;
+    int snap_np = -1;
     long long nlaunch = 0;                   // kernels launched on the stage stream so far
     long long last_launches[2] = {0, 0};     // last xj_cuda_decode: prompt, decode steps
 };
@@ -1221,6 +1224,210 @@ int xj_cuda_gemv_time(int type, const void *w, int k, int n, int t, int copies, 
                       char *err, size_t errlen) {
     std::vector<float> x((size_t)t * k, 0.5f);
     return gemv_diag(type, w, k, n, x.data(), t, nullptr, path, copies, iters, ms, err, errlen);
+}
+
+// ------------------------------------------------------------------ speculative decoding with a draft model
+// Tokens -> embeddings -> layers on the device (no output head); n_past += T.
+static int feed_tokens(xj_stage *s, const int32_t *toks, int T, bool keep, char *err, size_t errlen) {
+    Impl *im = I(s);
+    const int E = s->m->hp.n_embd;
+    if (T < 1 || T > s->max_batch || s->n_past + T > s->n_ctx) { seterr(err, errlen, "cannot feed %d tokens", T); return -1; }
+    if (keep && ensure_ck(s, T - 1, err, errlen)) return -1;
+    s->ck_start = s->n_past;
+    s->ck_T = keep ? T : 0;
+    CK(cudaMemcpyAsync(im->tok, toks, sizeof(int32_t) * T, cudaMemcpyHostToDevice, im->st));
+    launch(im, k_embed, dim3((E / 8 + 127) / 128, T), dim3(128), 0, im->tok_embd, (const int32_t *)im->tok, T, im->x, E);
+    run_layers(s, T, keep, T);
+    return 0;
+}
+
+// Recurrent state (conv + GDN state of every layer) and position of a stage: save / restore. KV rows
+// beyond a restored position are simply overwritten later.
+static int snapshot(xj_stage *s, char *err, size_t errlen) {
+    Impl *im = I(s);
+    const xj_hparams *hp = &s->m->hp;
+    const size_t nc = (size_t)hp->conv_dim * (hp->conv_k - 1), ns = (size_t)hp->h_v * hp->s_v * hp->s_k;
+    if (im->snap_conv.empty()) {
+        im->snap_conv.assign(im->L.size(), nullptr);
+        im->snap_ssm.assign(im->L.size(), nullptr);
+        for (size_t li = 0; li < im->L.size(); li++) {
+            if (!im->L[li].rec) continue;
+            if (dalloc(im, &im->snap_conv[li], nc, err, errlen) || dalloc(im, &im->snap_ssm[li], ns, err, errlen)) return -1;
+        }
+    }
+    for (size_t li = 0; li < im->L.size(); li++) {
+        if (!im->L[li].rec) continue;
+        CK(cudaMemcpyAsync(im->snap_conv[li], im->L[li].conv, nc * 4, cudaMemcpyDeviceToDevice, im->st));
+        CK(cudaMemcpyAsync(im->snap_ssm[li], im->L[li].ssm, ns * 4, cudaMemcpyDeviceToDevice, im->st));
+    }
+    im->snap_np = s->n_past;
+    return 0;
+}
+static int restore(xj_stage *s, char *err, size_t errlen) {
+    Impl *im = I(s);
+    const xj_hparams *hp = &s->m->hp;
+    const size_t nc = (size_t)hp->conv_dim * (hp->conv_k - 1), ns = (size_t)hp->h_v * hp->s_v * hp->s_k;
+    if (im->snap_np < 0) { seterr(err, errlen, "no snapshot"); return -1; }
+    for (size_t li = 0; li < im->L.size(); li++) {
+        if (!im->L[li].rec) continue;
+        CK(cudaMemcpyAsync(im->L[li].conv, im->snap_conv[li], nc * 4, cudaMemcpyDeviceToDevice, im->st));
+        CK(cudaMemcpyAsync(im->L[li].ssm, im->snap_ssm[li], ns * 4, cudaMemcpyDeviceToDevice, im->st));
+    }
+    int np = im->snap_np;
+    CK(cudaMemcpyAsync(im->npast, &np, sizeof(int), cudaMemcpyHostToDevice, im->st));
+    CK(cudaStreamSynchronize(im->st));   // np is a host local
+    s->n_past = im->snap_np;
+    s->ck_T = 0;
+    return 0;
+}
+
+int xj_cuda_spec_decode(xj_stage *target, xj_stage *draft, const int32_t *prompt, int n_prompt, int n_gen, int k,
+                        int32_t *out, long long *stats, char *err, size_t errlen) {
+    for (xj_stage *s : {target, draft})
+        if (!s || !s->backend || strcmp(s->backend, "cuda") != 0 || s->mtp || s->l0 != 0 || s->l1 != s->m->hp.n_layer ||
+            !s->has_head) {
+            seterr(err, errlen, "speculative decoding needs two CUDA stages over all layers with the head");
+            return -1;
+        }
+    if (target == draft) { seterr(err, errlen, "the draft must be its own stage"); return -1; }
+    if (target->m->hp.n_vocab != draft->m->hp.n_vocab) { seterr(err, errlen, "draft and target vocabularies differ"); return -1; }
+    if (k < 1 || k + 1 > target->max_batch || k + 1 > draft->max_batch) {
+        seterr(err, errlen, "k must be in 1..max_batch-1 of both stages"); return -1;
+    }
+    if (n_prompt < 1 || n_gen < 1) { seterr(err, errlen, "need at least one prompt token and one generated token"); return -1; }
+    if (target->n_past + n_prompt + n_gen + k > target->n_ctx || draft->n_past + n_prompt + n_gen + k > draft->n_ctx) {
+        seterr(err, errlen, "context is too short for %d + %d tokens", n_prompt, n_gen); return -1;
+    }
+    Impl *ti = I(target), *di = I(draft);
+    long long st[4] = {0, 0, 0, 0};   // verify forwards, drafted, accepted, draft re-feeds
+    // the prompt through both models; the target picks out[0]
+    int32_t first = 0;
+    if (xj_cuda_decode(target, prompt, n_prompt, 1, out, nullptr, nullptr, err, errlen)) return -1;
+    if (xj_cuda_decode(draft, prompt, n_prompt, 1, &first, nullptr, nullptr, err, errlen)) return -1;
+    const int V = target->m->hp.n_vocab;
+    int produced = 1;
+    std::vector<int32_t> toks(k + 1), ids(k + 1), dr(k);
+    while (produced < n_gen) {
+        const int32_t last = out[produced - 1];           // emitted, not yet fed to either model
+        const int kk = k < n_gen - produced ? k : n_gen - produced;
+        // draft kk tokens greedily from its state before `last`
+        {
+            DevGuard dg(di->dev);
+            if (snapshot(draft, err, errlen)) return -1;
+        }
+        if (xj_cuda_decode(draft, &last, 1, kk, dr.data(), nullptr, nullptr, err, errlen)) return -1;
+        st[1] += kk;
+        // the target verifies [last, d0 .. d_{kk-1}] in one forward (checkpoints kept for the rollback)
+        const int T = kk + 1;
+        toks[0] = last;
+        for (int i = 0; i < kk; i++) toks[i + 1] = dr[i];
+        {
+            DevGuard dg(ti->dev);
+            const int P = target->n_past;
+            if (feed_tokens(target, toks.data(), T, true, err, errlen)) return -1;
+            head(target, ti->x, T);
+            launch(ti, k_argmax_pick_rows, dim3(T), dim3(1024), 0, (const float *)ti->logits, V, ti->out_tok);
+            CK(cudaMemcpyAsync(ids.data(), ti->out_tok, sizeof(int32_t) * T, cudaMemcpyDeviceToHost, ti->st));
+            if (sync_check(ti, err, errlen)) return -1;
+            target->n_past = P + T;
+            st[0]++;
+            int a = 0;
+            while (a < kk && ids[a] == dr[a]) a++;
+            st[2] += a;
+            // emit the accepted drafts, then the target's own pick after them when there is room; every
+            // emitted token but the final one of the call is fed
+            const bool pick = produced + a < n_gen;
+            for (int i = 0; i < a; i++) out[produced++] = dr[i];
+            if (pick) out[produced++] = ids[a];
+            const int fed = pick ? a + 1 : a;                  // last, d0 .. d_{fed-2}
+            if (fed < T && cuda_rollback(target, P + fed, err, errlen)) return -1;
+            // the draft consumed last, d0 .. d_{kk-2} (kk tokens): bring it to `fed` tokens
+            DevGuard dd(di->dev);
+            if (fed == kk + 1) {
+                if (feed_tokens(draft, &dr[kk - 1], 1, false, err, errlen)) return -1;
+                draft->n_past += 1;
+                st[3]++;
+            } else if (fed < kk) {
+                if (restore(draft, err, errlen)) return -1;
+                if (feed_tokens(draft, toks.data(), fed, false, err, errlen)) return -1;
+                draft->n_past += fed;
+                st[3]++;
+            }
+            if (sync_check(di, err, errlen)) return -1;
+        }
+    }
+    if (stats) for (int i = 0; i < 4; i++) stats[i] = st[i];
+    return 0;
+}
+
+// Gated DeltaNet decode step on synthetic operands: B sequences x Hv heads of an
+// S x S fp32 state, one token each, with the batch kernel of batched decode (k_gdn_batch; B = 1 is the
+// single-sequence case). The states rotate over enough copies that the last-level cache cannot serve
+// them (>= 256 MiB in total); *ms = average device time per launch over `iters` launches.
+int xj_cuda_gdn_time(int S, int Hv, int B, int iters, float *ms, char *err, size_t errlen) {
+    if (S != 16 && S != 32 && S != 64 && S != 128) { seterr(err, errlen, "S must be 16, 32, 64 or 128"); return -1; }
+    if (Hv < 1 || B < 1 || iters < 1 || !ms) { seterr(err, errlen, "need Hv, B, iters >= 1 and ms"); return -1; }
+    Impl tmp;
+    Impl *im = &tmp;
+    int rc = -1;
+    const size_t state = (size_t)B * Hv * S * S;                 // floats per copy
+    const int copies = (int)std::max<size_t>(1, ((size_t)256 << 20) / (state * 4) + 1);
+    const int key_dim = Hv * S, ldq = 2 * key_dim + Hv * S;
+    float *ssm = nullptr, *qkv = nullptr, *z = nullptr, *ba = nullptr, *par = nullptr, *out = nullptr;
+    if (cudaStreamCreateWithFlags(&im->st, cudaStreamNonBlocking) != cudaSuccess) { seterr(err, errlen, "no stream"); return -1; }
+    if (dalloc(im, &ssm, state * copies, err, errlen) || dalloc(im, &qkv, (size_t)B * ldq, err, errlen) ||
+        dalloc(im, &z, (size_t)B * Hv * S, err, errlen) || dalloc(im, &ba, (size_t)2 * B * Hv, err, errlen) ||
+        dalloc(im, &par, (size_t)2 * Hv + S, err, errlen) || dalloc(im, &out, (size_t)B * Hv * S, err, errlen)) goto done;
+    {
+        // small deterministic operands: decays below 1, state and inputs of unit scale
+        std::vector<float> h((size_t)B * ldq);
+        for (size_t i = 0; i < h.size(); i++) h[i] = (float)((i * 2654435761u) % 2001) / 1000.0f - 1.0f;
+        std::vector<float> hp(2 * Hv + S);
+        for (int i = 0; i < Hv; i++) { hp[i] = 0.5f; hp[Hv + i] = -1.0f; }
+        for (int i = 0; i < S; i++) hp[2 * Hv + i] = 1.0f;
+        if (cudaMemcpy(qkv, h.data(), h.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(z, h.data(), (size_t)B * Hv * S * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(ba, h.data(), (size_t)2 * B * Hv * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(par, hp.data(), hp.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemset(ssm, 0, state * copies * 4) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+            seterr(err, errlen, "setup failed");
+            goto done;
+        }
+    }
+    {
+        GdnArgs g{};
+        g.qkv = qkv; g.ldq = ldq; g.z = z; g.ldz = Hv * S; g.beta = ba; g.alpha = ba + (size_t)B * Hv; g.ldg = Hv;
+        g.dt = par; g.A = par + Hv; g.nw = par + 2 * Hv; g.ck_ssm = nullptr; g.out = out; g.ldo = Hv * S;
+        g.T = 1; g.Hk = Hv; g.Hv = Hv; g.key_dim = key_dim; g.eps = 1e-6f;
+        const long long sstride = (long long)Hv * S * S;
+        auto run = [&](int i) {
+            g.ssm = ssm + (size_t)(i % copies) * state;
+            switch (S) {
+            case 16: launch(im, k_gdn_batch<16>, dim3(Hv, B), dim3(64), 0, g, sstride); break;
+            case 32: launch(im, k_gdn_batch<32>, dim3(Hv, B), dim3(128), 0, g, sstride); break;
+            case 64: launch(im, k_gdn_batch<64>, dim3(Hv, B), dim3(256), 0, g, sstride); break;
+            default: launch(im, k_gdn_batch<128>, dim3(Hv, B), dim3(512), 0, g, sstride); break;
+            }
+        };
+        for (int i = 0; i < 3; i++) run(i);
+        cudaEvent_t e0, e1;
+        cudaEventCreate(&e0); cudaEventCreate(&e1);
+        cudaEventRecord(e0, im->st);
+        for (int i = 0; i < iters; i++) run(i + 3);
+        cudaEventRecord(e1, im->st);
+        cudaEventSynchronize(e1);
+        cudaEventElapsedTime(ms, e0, e1);
+        *ms /= iters;
+        cudaEventDestroy(e0); cudaEventDestroy(e1);
+    }
+    if (cudaStreamSynchronize(im->st) != cudaSuccess || cudaGetLastError() != cudaSuccess) { seterr(err, errlen, "GDN launch failed"); goto done; }
+    rc = 0;
+done:
+    cudaStreamSynchronize(im->st);
+    for (void *p : im->allocs) cudaFree(p);
+    im->allocs.clear();
+    cudaStreamDestroy(im->st);
+    return rc;
 }
 
 int xj_cuda_graph_kernels(const xj_stage *s) {

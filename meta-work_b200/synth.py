@@ -84,6 +84,9 @@ CONFIG3 = ModelConfig(
     head_dim=128, n_rot=32, s_k=128, h_k=16, h_v=16, wtype=Q4_K)
 MID = ModelConfig("mid-q4_k_m", n_layer=8, n_embd=512, n_ff=1536, n_vocab=4096, n_head=4, n_head_kv=2,
                   head_dim=128, n_rot=32, s_k=128, h_k=4, h_v=4, wtype=Q4_K)
+# a small draft for MID (same vocabulary), for the speculative-decoding tests
+MID_DRAFT = ModelConfig("mid-draft-q8_0", n_layer=4, n_embd=256, n_ff=512, n_vocab=4096, n_head=2, n_head_kv=1,
+                        head_dim=128, n_rot=32, s_k=64, h_k=2, h_v=4, wtype=Q8_0, seed=20261202)
 DRAFT = ModelConfig("draft-1024-q8_0", n_layer=8, n_embd=1024, n_ff=2816, n_vocab=151936, n_head=8,
                     n_head_kv=2, head_dim=128, n_rot=32, s_k=128, h_k=4, h_v=8, wtype=Q8_0)
 

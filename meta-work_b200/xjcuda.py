@@ -108,6 +108,8 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_batch_last_launches": (ctypes.c_longlong, [vp, vp]),
         "xj_cuda_gemv": (ip, [ip, vp, ip, ip, vp, ip, vp, ip, cp, sz]),
         "xj_cuda_gemv_time": (ip, [ip, vp, ip, ip, ip, ip, ip, ip, vp, cp, sz]),
+        "xj_cuda_gdn_time": (ip, [ip, ip, ip, ip, vp, cp, sz]),
+        "xj_cuda_spec_decode": (ip, [vp, vp, vp, ip, ip, ip, vp, vp, cp, sz]),
         "xj_cuda_norm_gemv_noalloc": (ip, [ip, vp, ip, ip, vp, vp, ctypes.c_float, ip, vp, cp, sz]),
     }
     for name, (res, args) in sig.items():
@@ -160,6 +162,15 @@ def gemv_time(type_id: int, raw: bytes, k: int, n: int, T: int = 1, copies: int 
     ms = ctypes.c_float(0)
     e = _err()
     if lib().xj_cuda_gemv_time(type_id, w.ctypes.data, k, n, T, copies, iters, path, ctypes.byref(ms), e, 512):
+        _raise(e)
+    return ms.value
+
+
+def gdn_time(S: int, Hv: int, B: int, iters: int = 50) -> float:
+    """Average ms per Gated DeltaNet decode step of B sequences x Hv heads (xj_cuda_gdn_time)."""
+    ms = ctypes.c_float(0)
+    e = _err()
+    if lib().xj_cuda_gdn_time(S, Hv, B, iters, ctypes.byref(ms), e, 512):
         _raise(e)
     return ms.value
 
@@ -280,6 +291,17 @@ class Stage:
         if rc:
             _raise(e)
         return out, mar, ms
+
+    def spec_decode(self, draft: "Stage", prompt, n_gen: int, k: int = 4):
+        """Greedy speculative decode with a draft-model stage (xj_cuda_spec_decode). Returns (ids, stats)
+        with stats = (target verify forwards, drafted, accepted, draft re-feeds)."""
+        p = np.ascontiguousarray(prompt, dtype=np.int32)
+        out = np.zeros(n_gen, np.int32)
+        st = (ctypes.c_longlong * 4)()
+        e = _err()
+        if lib().xj_cuda_spec_decode(self.addr, draft.addr, p.ctypes.data, p.size, n_gen, k, out.ctypes.data, st, e, 512):
+            _raise(e)
+        return out, tuple(int(v) for v in st)
 
     def last_decode_launches(self) -> tuple[int, int]:
         """Kernel launches of the last decode() call: (prompt, decode steps after it); the persistent

@@ -56,6 +56,12 @@ def mid_path(tmp_path_factory):
 
 
 @pytest.fixture(scope="session")
+def mid_draft_path(tmp_path_factory):
+    from xjb200 import synth
+    return synth.cached_gguf(synth.MID_DRAFT, tmp_path_factory.mktemp("models"))
+
+
+@pytest.fixture(scope="session")
 def ref_lib():
     from oracle import ref
     if not ref.available() and not ref.build():

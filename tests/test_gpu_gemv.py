@@ -122,3 +122,11 @@ def test_gemv_microbench_runs():
     raw = _w(xo.Q4_K, 2048, 2048, 9)
     ms = xjcuda.gemv_time(xo.Q4_K, raw, 2048, 2048, T=1, copies=4, iters=20)
     assert 0 < ms < 5
+
+
+def test_gdn_decode_microbench_runs():
+    """BASELINE config 2 decode: 16 heads, S = 128, B = 1 and 64 (state 2 MiB per sequence)."""
+    from xjb200 import xjcuda
+    for B in (1, 64):
+        ms = xjcuda.gdn_time(128, 16, B, iters=10)
+        assert 0 < ms < 50, (B, ms)
