@@ -89,6 +89,10 @@ int xj_cuda_spec_decode(xj_stage *target, xj_stage *draft, const int32_t *prompt
 // of B sequences x Hv heads with an S x S fp32 state each (S in 16, 32, 64, 128), the batch kernel of
 // batched decode, states rotated over >= 256 MiB of copies so the last-level cache cannot serve them.
 int xj_cuda_gdn_time(int S, int Hv, int B, int iters, float *ms, char *err, size_t errlen);
+// Gated DeltaNet over a prompt of T tokens (prefill): the chunked kernels that prompt
+// forwards of 32 or more tokens use, against the token-by-token kernel on the same synthetic operands.
+// res[4] = max relative difference of the outputs, of the final state, chunked ms, token-by-token ms.
+int xj_cuda_gdn_prefill_check(int S, int Hk, int Hv, int T, float *res, char *err, size_t errlen);
 
 // Number of kernel launches in one replay of the stage's cached decode-step graph (0 before the first
 // xj_cuda_decode call that generated more than one token).

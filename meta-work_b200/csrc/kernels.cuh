@@ -268,6 +268,244 @@ XJ_DEV void gdn_head(const GdnArgs &a, int hv, int tid) {
     for (int i = 0; i < P; i += 4) *reinterpret_cast<float4 *>(M + 4 * i) = make_float4(row[i], row[i + 1], row[i + 2], row[i + 3]);
 }
 
+// ---------------------------------------------------------------- chunked Gated DeltaNet (prompts)
+// The recurrence of gdn_head over T tokens, chunk by chunk (GC_C tokens), for prompt forwards without
+// checkpoints. Each value row j of a head's state evolves on its own, so a head's S rows are split
+// over S / 16 CTAs. Within a chunk with state M0 at its start, cumulative log decay G_i = g_1 + .. + g_i
+// (g = softplus(alpha + dt) * A <= 0) and normalised q, k:
+//   u_i = b_i (v_i - e^G_i M0 k_i) - sum_{l<i} b_i e^(G_i - G_l) (k_i . k_l) u_l     (forward substitution)
+//   o_i = (e^G_i M0 q_i + sum_{l<=i} e^(G_i - G_l) (q_i . k_l) u_l) / sqrt(S)
+//   M_C = e^G_C M0 + sum_l e^(G_C - G_l) u_l k_l^T
+// which is the token-by-token update M = e^g M; u = (v - M k) b; M += u k^T; o = M q / sqrt(S) of
+// core/xj_cpu.c:194-219 regrouped (fp32 throughout; sums in another order, so results agree with the
+// sequential kernel to rounding). The gated RMSNorm of the outputs is a separate pass (k_gdn_gnorm).
+constexpr int GC_C = 64;          // tokens per chunk
+constexpr int GC_MIN_T = 32;      // forwards of at least this many tokens take the chunked path
+
+// Grid (Hk, nchunks), 256 threads: q, k of key head hk for the chunk's tokens, L2-normalised (sums in
+// double, core/xj_cpu.c:185-193) into qn, kn [T][Hk][S]; kk[i][l] = k_i . k_l (l < i) and
+// qk[i][l] = q_i . k_l (l <= i) into [Hk][nchunks][GC_C][GC_C].
+template <int S>
+__global__ void __launch_bounds__(256) k_gdn_chunk_prep(GdnArgs a, float *qn, float *kn, float *kk, float *qk) {
+    griddep_wait();
+    extern __shared__ __align__(16) float gsm[];
+    constexpr int CP = GC_C + 4;                           // transposed rows [S][CP]
+    float *qt = gsm, *kt = gsm + S * CP;
+    const int hk = blockIdx.x, ch = blockIdx.y, t0 = ch * GC_C, n = a.T - t0 < GC_C ? a.T - t0 : GC_C;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    // normalise: one warp per token
+    for (int i = warp; i < GC_C; i += 8) {
+        const int t = t0 + i;
+        float qv[S / 32], kv[S / 32];
+        double sq = 0.0, sk = 0.0;
+#pragma unroll
+        for (int e = 0; e < S / 32; e++) {
+            const int c = lane + 32 * e;
+            qv[e] = i < n ? lda(a.qkv + (size_t)t * a.ldq + hk * S + c) : 0.0f;
+            kv[e] = i < n ? lda(a.qkv + (size_t)t * a.ldq + a.key_dim + hk * S + c) : 0.0f;
+            sq += (double)qv[e] * qv[e];
+            sk += (double)kv[e] * kv[e];
+        }
+        sq = warp_sum_d(sq);
+        sk = warp_sum_d(sk);
+        const float rq = 1.0f / sqrtf((float)sq + a.eps), rk = 1.0f / sqrtf((float)sk + a.eps);
+#pragma unroll
+        for (int e = 0; e < S / 32; e++) {
+            const int c = lane + 32 * e;
+            const float q = qv[e] * rq, k = kv[e] * rk;
+            qt[c * CP + i] = q;
+            kt[c * CP + i] = k;
+            if (i < n) {
+                qn[((size_t)t * a.Hk + hk) * S + c] = q;
+                kn[((size_t)t * a.Hk + hk) * S + c] = k;
+            }
+        }
+    }
+    __syncthreads();
+    // 4x4 output blocks: thread (bi, bl) = (tid / 16, tid % 16) takes rows 4bi.., columns 4bl..
+    const int bi = tid >> 4, bl = tid & 15;
+    if (bl > bi) return;                                   // strictly above the diagonal: unused
+    float ak[4][4] = {}, aq[4][4] = {};
+    for (int c = 0; c < S; c++) {
+        const float4 ki = *reinterpret_cast<const float4 *>(kt + c * CP + 4 * bi);
+        const float4 qi = *reinterpret_cast<const float4 *>(qt + c * CP + 4 * bi);
+        const float4 kl = *reinterpret_cast<const float4 *>(kt + c * CP + 4 * bl);
+        const float kiv[4] = {ki.x, ki.y, ki.z, ki.w}, qiv[4] = {qi.x, qi.y, qi.z, qi.w}, klv[4] = {kl.x, kl.y, kl.z, kl.w};
+#pragma unroll
+        for (int x = 0; x < 4; x++)
+#pragma unroll
+            for (int y = 0; y < 4; y++) {
+                ak[x][y] = fmaf(kiv[x], klv[y], ak[x][y]);
+                aq[x][y] = fmaf(qiv[x], klv[y], aq[x][y]);
+            }
+    }
+    float *KK = kk + ((size_t)hk * gridDim.y + ch) * GC_C * GC_C, *QK = qk + ((size_t)hk * gridDim.y + ch) * GC_C * GC_C;
+#pragma unroll
+    for (int x = 0; x < 4; x++)
+#pragma unroll
+        for (int y = 0; y < 4; y++) {
+            KK[(4 * bi + x) * GC_C + 4 * bl + y] = ak[x][y];
+            QK[(4 * bi + x) * GC_C + 4 * bl + y] = aq[x][y];
+        }
+}
+
+template <int S> constexpr size_t gdn_chunk_smem() { return ((size_t)2 * GC_C * (S + 4) + 3 * GC_C * (GC_C + 1) + 4 * GC_C * 17) * 4; }
+template <int S> constexpr size_t gdn_prep_smem() { return (size_t)2 * S * (GC_C + 4) * 4; }
+
+// Grid (Hv, S / 16), 256 threads: rows [16 r, 16 r + 16) of value head hv's state over all chunks;
+// thread (row rr = tid / 16, column block cb = tid % 16) keeps state columns [cb*S/16, (cb+1)*S/16) of
+// its row in registers. Raw outputs o (scaled by 1/sqrt(S), before the gated norm) to out[t][hv*S + j].
+template <int S>
+__global__ void __launch_bounds__(256) k_gdn_chunk(GdnArgs a, const float *qn, const float *kn, const float *kk,
+                                                   const float *qk) {
+    griddep_wait();
+    constexpr int P = S / 16, SP = S + 4, CP = GC_C + 1;
+    extern __shared__ __align__(16) float gsm[];
+    float *qs = gsm, *ks = qs + GC_C * SP;                 // [C][SP]
+    float *dec = ks + GC_C * SP;                           // [C][CP]: e^(G_i - G_l), l <= i
+    float *KKs = dec + GC_C * CP, *QKs = KKs + GC_C * CP;  // [C][CP]
+    float *Mk = QKs + GC_C * CP, *Mq = Mk + GC_C * 17, *U = Mq + GC_C * 17, *Vs = U + GC_C * 17;   // [C][17]
+    __shared__ float G[GC_C], bv[GC_C], eG[GC_C];
+    const int hv = blockIdx.x, hk = hv % a.Hk, r0 = blockIdx.y * 16;
+    const int tid = threadIdx.x, rr = tid >> 4, cb = tid & 15, lane = tid & 31, warp = tid >> 5;
+    const int j = r0 + rr;
+    const int nch = (a.T + GC_C - 1) / GC_C;
+    float m[P];
+    float *Mrow = a.ssm + (size_t)hv * S * S + (size_t)j * S + cb * P;
+#pragma unroll
+    for (int e = 0; e < P; e++) m[e] = __ldcg(Mrow + e);
+    const float dtv = a.dt[hv], Av = a.A[hv], qscale = 1.0f / sqrtf((float)S);
+    for (int ch = 0; ch < nch; ch++) {
+        const int t0 = ch * GC_C, n = a.T - t0 < GC_C ? a.T - t0 : GC_C;
+        __syncthreads();                                   // the previous chunk's shared data is consumed
+        for (int x = tid; x < GC_C * (S / 4); x += 256) {
+            const int i = x / (S / 4), c = (x % (S / 4)) * 4;
+            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f), k4 = q4;
+            if (i < n) {
+                q4 = __ldcg(reinterpret_cast<const float4 *>(qn + ((size_t)(t0 + i) * a.Hk + hk) * S + c));
+                k4 = __ldcg(reinterpret_cast<const float4 *>(kn + ((size_t)(t0 + i) * a.Hk + hk) * S + c));
+            }
+            *reinterpret_cast<float4 *>(qs + i * SP + c) = q4;
+            *reinterpret_cast<float4 *>(ks + i * SP + c) = k4;
+        }
+        for (int x = tid; x < GC_C * 16; x += 256) {
+            const int i = x >> 4, row = x & 15;
+            Vs[i * 17 + row] = i < n ? lda(a.qkv + (size_t)(t0 + i) * a.ldq + 2 * a.key_dim + hv * S + r0 + row) : 0.0f;
+        }
+        const float *KKg = kk + ((size_t)hk * nch + ch) * GC_C * GC_C, *QKg = qk + ((size_t)hk * nch + ch) * GC_C * GC_C;
+        for (int x = tid; x < GC_C * GC_C; x += 256) {
+            const int i = x / GC_C, l = x % GC_C;
+            KKs[i * CP + l] = l < i ? __ldcg(KKg + x) : 0.0f;
+            QKs[i * CP + l] = l <= i ? __ldcg(QKg + x) : 0.0f;
+        }
+        if (warp == 0) {
+            // g, b per token; G by a sequential prefix sum (fp32)
+            for (int i = lane; i < GC_C; i += 32) {
+                const int t = t0 + i;
+                const float gi = i < n ? softplus_f(lda(a.alpha + (size_t)t * a.ldg + hv) + dtv) * Av : 0.0f;
+                G[i] = gi;
+                bv[i] = i < n ? sigm_f(lda(a.beta + (size_t)t * a.ldg + hv)) : 0.0f;
+            }
+            __syncwarp();
+            if (lane == 0) {
+                float acc = 0.0f;
+                for (int i = 0; i < GC_C; i++) { acc += G[i]; G[i] = acc; }
+            }
+            __syncwarp();
+            for (int i = lane; i < GC_C; i += 32) eG[i] = expf(G[i]);
+        }
+        __syncthreads();
+        for (int x = tid; x < GC_C * GC_C; x += 256) {
+            const int i = x / GC_C, l = x % GC_C;
+            dec[i * CP + l] = l <= i ? expf(G[i] - G[l]) : 0.0f;
+        }
+        // M0 k_i and M0 q_i for this CTA's rows: partial over the thread's columns, summed over the 16
+        // threads of the row (a half-warp)
+        for (int i = 0; i < n; i++) {
+            float pk = 0.0f, pq = 0.0f;
+            float kv[P], qv[P];
+            if constexpr (P % 4 == 0) {
+#pragma unroll
+                for (int e = 0; e < P; e += 4) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(ks + i * SP + cb * P + e);
+                    const float4 q4 = *reinterpret_cast<const float4 *>(qs + i * SP + cb * P + e);
+                    kv[e] = k4.x; kv[e + 1] = k4.y; kv[e + 2] = k4.z; kv[e + 3] = k4.w;
+                    qv[e] = q4.x; qv[e + 1] = q4.y; qv[e + 2] = q4.z; qv[e + 3] = q4.w;
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < P; e++) { kv[e] = ks[i * SP + cb * P + e]; qv[e] = qs[i * SP + cb * P + e]; }
+            }
+#pragma unroll
+            for (int e = 0; e < P; e++) {
+                pk = fmaf(m[e], kv[e], pk);
+                pq = fmaf(m[e], qv[e], pq);
+            }
+#pragma unroll
+            for (int o = 8; o; o >>= 1) {
+                pk += __shfl_xor_sync(0xffffffffu, pk, o);
+                pq += __shfl_xor_sync(0xffffffffu, pq, o);
+            }
+            if (cb == 0) { Mk[i * 17 + rr] = pk; Mq[i * 17 + rr] = pq; }
+        }
+        __syncthreads();
+        // forward substitution for u: warp w solves rows 2w, 2w+1; lane p of a row sums l = p, p+16, ..
+        {
+            const int row = 2 * warp + (lane >> 4), p = lane & 15;
+            for (int i = 0; i < n; i++) {
+                float s = 0.0f;
+                for (int l = p; l < i; l += 16) s = fmaf(dec[i * CP + l] * KKs[i * CP + l], U[l * 17 + row], s);
+#pragma unroll
+                for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+                if (p == 0) U[i * 17 + row] = bv[i] * (Vs[i * 17 + row] - eG[i] * Mk[i * 17 + row]) - bv[i] * s;
+                __syncwarp();
+            }
+        }
+        __syncthreads();
+        // outputs o_i for this CTA's rows
+        for (int x = tid; x < n * 16; x += 256) {
+            const int i = x >> 4, row = x & 15;
+            float acc = eG[i] * Mq[i * 17 + row];
+            for (int l = 0; l <= i; l++) acc = fmaf(dec[i * CP + l] * QKs[i * CP + l], U[l * 17 + row], acc);
+            a.out[(size_t)(t0 + i) * a.ldo + hv * S + r0 + row] = acc * qscale;
+        }
+        // state at the chunk's end
+        const float eGC = eG[n - 1];
+#pragma unroll
+        for (int e = 0; e < P; e++) m[e] *= eGC;
+        for (int i = 0; i < n; i++) {
+            const float w = dec[(n - 1) * CP + i] * U[i * 17 + rr];
+            if constexpr (P % 4 == 0) {
+#pragma unroll
+                for (int e = 0; e < P; e += 4) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(ks + i * SP + cb * P + e);
+                    m[e] = fmaf(w, k4.x, m[e]); m[e + 1] = fmaf(w, k4.y, m[e + 1]);
+                    m[e + 2] = fmaf(w, k4.z, m[e + 2]); m[e + 3] = fmaf(w, k4.w, m[e + 3]);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < P; e++) m[e] = fmaf(w, ks[i * SP + cb * P + e], m[e]);
+            }
+        }
+    }
+#pragma unroll
+    for (int e = 0; e < P; e++) Mrow[e] = m[e];
+}
+
+// Grid (T, Hv), S threads (S <= 1024): out[t][hv*S + j] = o * rsqrt(mean_j o^2 + eps) * norm_w[j] * silu(z),
+// in place on the raw outputs of k_gdn_chunk (the gated RMSNorm of gdn_head, sum in double).
+template <int S>
+__global__ void __launch_bounds__(S) k_gdn_gnorm(GdnArgs a) {
+    griddep_wait();
+    __shared__ double red[32];
+    const int t = blockIdx.x, hv = blockIdx.y, j = threadIdx.x;
+    float *op = a.out + (size_t)t * a.ldo + hv * S + j;
+    const float o = *op;
+    const double so = group_sum_d<BarBlock>((double)o * o, red, j, S);
+    const float sc = 1.0f / sqrtf((float)(so / S) + a.eps);
+    *op = o * sc * a.nw[j] * silu_f(lda(a.z + (size_t)t * a.ldz + hv * S + j));
+}
+
 // One block of 4*S threads per value head.
 template <int S>
 __global__ void __launch_bounds__(4 * S) k_gdn(GdnArgs a) {

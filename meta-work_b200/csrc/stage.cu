@@ -74,6 +74,8 @@ struct Impl {
     float *q = nullptr, *k = nullptr, *v = nullptr, *hn = nullptr;
     void *wide_buf = nullptr;   // activations of a wide (5..16-token) GEMV launch, prepared by k_prep_xt<false>
     void *b64_buf = nullptr;    // activations of a 64-token GEMV launch (stages taking more than 16 tokens)
+    // chunked GDN (prompt forwards of >= GC_MIN_T tokens): normalised q, k and the chunk products
+    float *gc_qn = nullptr, *gc_kn = nullptr, *gc_kk = nullptr, *gc_qk = nullptr;
     float *pbest = nullptr, *psecond = nullptr;
     int *pidx = nullptr;
     int *derr = nullptr;       // device error word: set when a kernel's bounded wait gives up
@@ -361,8 +363,35 @@ GdnArgs gdn_args(Impl *im, const xj_hparams *hp, Layer &Ly, int T, bool ck) {
     return g;
 }
 
+// Chunked GDN over T tokens (no checkpoints): prep (per key head and chunk), state walk (per value head
+// and 16-row block), gated RMSNorm. Scratch: qn, kn [T][Hk][S], kk, qk [Hk][chunks][GC_C][GC_C].
+template <int S>
+void launch_gdn_chunked(Impl *im, const GdnArgs &g, float *qn, float *kn, float *kk, float *qk) {
+    static bool attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr[dev & 63]) {
+        cudaFuncSetAttribute(k_gdn_chunk_prep<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_prep_smem<S>());
+        cudaFuncSetAttribute(k_gdn_chunk<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_chunk_smem<S>());
+        attr[dev & 63] = true;
+    }
+    const int nch = (g.T + GC_C - 1) / GC_C;
+    launch(im, k_gdn_chunk_prep<S>, dim3(g.Hk, nch), dim3(256), gdn_prep_smem<S>(), g, qn, kn, kk, qk);
+    launch(im, k_gdn_chunk<S>, dim3(g.Hv, S / 16), dim3(256), gdn_chunk_smem<S>(), g, (const float *)qn, (const float *)kn,
+           (const float *)kk, (const float *)qk);
+    launch(im, k_gdn_gnorm<S>, dim3(g.T, g.Hv), dim3(S), 0, g);
+}
+bool gdn_chunked_ok(const xj_hparams *hp) { return hp->s_v == hp->s_k && (hp->s_k == 32 || hp->s_k == 64 || hp->s_k == 128); }
+
 void launch_gdn(Impl *im, const xj_hparams *hp, Layer &Ly, int T, bool ck) {
     const GdnArgs g = gdn_args(im, hp, Ly, T, ck);
+    if (!ck && T >= GC_MIN_T && im->gc_qn && gdn_chunked_ok(hp)) {
+        switch (hp->s_k) {
+        case 32: launch_gdn_chunked<32>(im, g, im->gc_qn, im->gc_kn, im->gc_kk, im->gc_qk); return;
+        case 64: launch_gdn_chunked<64>(im, g, im->gc_qn, im->gc_kn, im->gc_kk, im->gc_qk); return;
+        default: launch_gdn_chunked<128>(im, g, im->gc_qn, im->gc_kn, im->gc_kk, im->gc_qk); return;
+        }
+    }
     switch (hp->s_k) {
     case 16: launch(im, k_gdn<16>, dim3(hp->h_v), dim3(64), 0, g); break;
     case 32: launch(im, k_gdn<32>, dim3(hp->h_v), dim3(128), 0, g); break;
@@ -686,6 +715,12 @@ int build(xj_stage *s, char *err, size_t errlen) {
         dalloc(im, &im->derr, 4, err, errlen) ||
         dalloc(im, &im->tok, (size_t)B, err, errlen) || dalloc(im, &im->cur, 4, err, errlen)) return -1;
     if (B > MMA_WIDE_T && alloc_b64(im, err, errlen)) return -1;
+    if (B >= GC_MIN_T && gdn_chunked_ok(hp)) {
+        const size_t nch = (size_t)(B + GC_C - 1) / GC_C;
+        if (dalloc(im, &im->gc_qn, (size_t)B * hp->key_dim, err, errlen) || dalloc(im, &im->gc_kn, (size_t)B * hp->key_dim, err, errlen) ||
+            dalloc(im, &im->gc_kk, (size_t)hp->h_k * nch * GC_C * GC_C, err, errlen) ||
+            dalloc(im, &im->gc_qk, (size_t)hp->h_k * nch * GC_C * GC_C, err, errlen)) return -1;
+    }
     if (s->has_head) {
         const size_t nt = (size_t)(m->output.ne1 + 15) / 16;
         if (dalloc(im, &im->pbest, nt, err, errlen) || dalloc(im, &im->psecond, nt, err, errlen) ||
@@ -1421,6 +1456,104 @@ int xj_cuda_gdn_time(int S, int Hv, int B, int iters, float *ms, char *err, size
         cudaEventDestroy(e0); cudaEventDestroy(e1);
     }
     if (cudaStreamSynchronize(im->st) != cudaSuccess || cudaGetLastError() != cudaSuccess) { seterr(err, errlen, "GDN launch failed"); goto done; }
+    rc = 0;
+done:
+    cudaStreamSynchronize(im->st);
+    for (void *p : im->allocs) cudaFree(p);
+    im->allocs.clear();
+    cudaStreamDestroy(im->st);
+    return rc;
+}
+
+// Gated DeltaNet over a prompt of T tokens (prefill): the chunked kernels against the
+// token-by-token kernel on the same synthetic operands (Hk key heads, Hv value heads, S x S state from a
+// nonzero start). res[0] = max |o_chunked - o_seq| / max |o_seq| (after the gated norm), res[1] = the same
+// for the final state, res[2] / res[3] = device ms of the chunked / token-by-token path.
+int xj_cuda_gdn_prefill_check(int S, int Hk, int Hv, int T, float *res, char *err, size_t errlen) {
+    if (S != 32 && S != 64 && S != 128) { seterr(err, errlen, "S must be 32, 64 or 128"); return -1; }
+    if (Hk < 1 || Hv < Hk || Hv % Hk || T < 1 || !res) { seterr(err, errlen, "need 1 <= Hk, Hk | Hv, T >= 1 and res"); return -1; }
+    Impl tmp;
+    Impl *im = &tmp;
+    int rc = -1;
+    const int key_dim = Hk * S, ldq = 2 * key_dim + Hv * S, nch = (T + GC_C - 1) / GC_C;
+    const size_t ns = (size_t)Hv * S * S;
+    float *qkv = nullptr, *z = nullptr, *ba = nullptr, *par = nullptr, *o1 = nullptr, *o2 = nullptr, *m1 = nullptr, *m2 = nullptr;
+    float *qn = nullptr, *kn = nullptr, *kk = nullptr, *qk = nullptr;
+    std::vector<float> h1, h2, s1, s2;
+    if (cudaStreamCreateWithFlags(&im->st, cudaStreamNonBlocking) != cudaSuccess) { seterr(err, errlen, "no stream"); return -1; }
+    if (dalloc(im, &qkv, (size_t)T * ldq, err, errlen) || dalloc(im, &z, (size_t)T * Hv * S, err, errlen) ||
+        dalloc(im, &ba, (size_t)2 * T * Hv, err, errlen) || dalloc(im, &par, (size_t)2 * Hv + S, err, errlen) ||
+        dalloc(im, &o1, (size_t)T * Hv * S, err, errlen) || dalloc(im, &o2, (size_t)T * Hv * S, err, errlen) ||
+        dalloc(im, &m1, ns, err, errlen) || dalloc(im, &m2, ns, err, errlen) ||
+        dalloc(im, &qn, (size_t)T * key_dim, err, errlen) || dalloc(im, &kn, (size_t)T * key_dim, err, errlen) ||
+        dalloc(im, &kk, (size_t)Hk * nch * GC_C * GC_C, err, errlen) || dalloc(im, &qk, (size_t)Hk * nch * GC_C * GC_C, err, errlen))
+        goto done;
+    {
+        // deterministic operands: q, k, v, z ~ U(-1, 1); beta, alpha logits ~ U(-2, 2); dt = 0.5;
+        // A = -exp(U(-1, 1)) (decays below 1); norm weights 1 + U(-0.1, 0.1); start state ~ U(-0.1, 0.1)
+        uint64_t x = 0x9E3779B97F4A7C15ull;
+        auto u = [&]() { x ^= x << 13; x ^= x >> 7; x ^= x << 17; return (float)((x >> 11) * (1.0 / 9007199254740992.0)) * 2.0f - 1.0f; };
+        std::vector<float> q((size_t)T * ldq), zz((size_t)T * Hv * S), bb((size_t)2 * T * Hv), pp(2 * Hv + S), mm(ns);
+        for (auto &v : q) v = u();
+        for (auto &v : zz) v = u();
+        for (auto &v : bb) v = 2.0f * u();
+        for (int i = 0; i < Hv; i++) { pp[i] = 0.5f; pp[Hv + i] = -expf(u()); }
+        for (int i = 0; i < S; i++) pp[2 * Hv + i] = 1.0f + 0.1f * u();
+        for (auto &v : mm) v = 0.1f * u();
+        if (cudaMemcpy(qkv, q.data(), q.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(z, zz.data(), zz.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(ba, bb.data(), bb.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(par, pp.data(), pp.size() * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(m1, mm.data(), ns * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+            cudaMemcpy(m2, mm.data(), ns * 4, cudaMemcpyHostToDevice) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+            seterr(err, errlen, "setup failed");
+            goto done;
+        }
+    }
+    {
+        GdnArgs g{};
+        g.qkv = qkv; g.ldq = ldq; g.z = z; g.ldz = Hv * S; g.beta = ba; g.alpha = ba + (size_t)T * Hv; g.ldg = Hv;
+        g.dt = par; g.A = par + Hv; g.nw = par + 2 * Hv; g.ck_ssm = nullptr; g.ldo = Hv * S;
+        g.T = T; g.Hk = Hk; g.Hv = Hv; g.key_dim = key_dim; g.eps = 1e-6f;
+        cudaEvent_t e[3];
+        for (auto &ev : e) cudaEventCreate(&ev);
+        GdnArgs gs = g, gc = g;
+        gs.ssm = m1; gs.out = o1;
+        gc.ssm = m2; gc.out = o2;
+        cudaEventRecord(e[0], im->st);
+        switch (S) {
+        case 32: launch(im, k_gdn<32>, dim3(Hv), dim3(128), 0, gs); break;
+        case 64: launch(im, k_gdn<64>, dim3(Hv), dim3(256), 0, gs); break;
+        default: launch(im, k_gdn<128>, dim3(Hv), dim3(512), 0, gs); break;
+        }
+        cudaEventRecord(e[1], im->st);
+        switch (S) {
+        case 32: launch_gdn_chunked<32>(im, gc, qn, kn, kk, qk); break;
+        case 64: launch_gdn_chunked<64>(im, gc, qn, kn, kk, qk); break;
+        default: launch_gdn_chunked<128>(im, gc, qn, kn, kk, qk); break;
+        }
+        cudaEventRecord(e[2], im->st);
+        if (cudaStreamSynchronize(im->st) != cudaSuccess || cudaGetLastError() != cudaSuccess) {
+            seterr(err, errlen, "GDN launch failed");
+            for (auto &ev : e) cudaEventDestroy(ev);
+            goto done;
+        }
+        cudaEventElapsedTime(&res[3], e[0], e[1]);
+        cudaEventElapsedTime(&res[2], e[1], e[2]);
+        for (auto &ev : e) cudaEventDestroy(ev);
+        h1.resize((size_t)T * Hv * S); h2.resize(h1.size()); s1.resize(ns); s2.resize(ns);
+        cudaMemcpy(h1.data(), o1, h1.size() * 4, cudaMemcpyDeviceToHost);
+        cudaMemcpy(h2.data(), o2, h2.size() * 4, cudaMemcpyDeviceToHost);
+        cudaMemcpy(s1.data(), m1, ns * 4, cudaMemcpyDeviceToHost);
+        cudaMemcpy(s2.data(), m2, ns * 4, cudaMemcpyDeviceToHost);
+        auto rel = [](const std::vector<float> &a, const std::vector<float> &b) {
+            double d = 0.0, mx = 0.0;
+            for (size_t i = 0; i < a.size(); i++) { d = std::max(d, (double)fabsf(a[i] - b[i])); mx = std::max(mx, (double)fabsf(a[i])); }
+            return (float)(mx > 0 ? d / mx : d);
+        };
+        res[0] = rel(h1, h2);
+        res[1] = rel(s1, s2);
+    }
     rc = 0;
 done:
     cudaStreamSynchronize(im->st);

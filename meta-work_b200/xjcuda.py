@@ -110,6 +110,7 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_gemv_time": (ip, [ip, vp, ip, ip, ip, ip, ip, ip, vp, cp, sz]),
         "xj_cuda_gdn_time": (ip, [ip, ip, ip, ip, vp, cp, sz]),
         "xj_cuda_spec_decode": (ip, [vp, vp, vp, ip, ip, ip, vp, vp, cp, sz]),
+        "xj_cuda_gdn_prefill_check": (ip, [ip, ip, ip, ip, vp, cp, sz]),
         "xj_cuda_norm_gemv_noalloc": (ip, [ip, vp, ip, ip, vp, vp, ctypes.c_float, ip, vp, cp, sz]),
     }
     for name, (res, args) in sig.items():
@@ -173,6 +174,16 @@ def gdn_time(S: int, Hv: int, B: int, iters: int = 50) -> float:
     if lib().xj_cuda_gdn_time(S, Hv, B, iters, ctypes.byref(ms), e, 512):
         _raise(e)
     return ms.value
+
+
+def gdn_prefill_check(S: int, Hk: int, Hv: int, T: int):
+    """Chunked vs token-by-token Gated DeltaNet over T tokens (xj_cuda_gdn_prefill_check):
+    (max rel diff of outputs, of the final state, chunked ms, token-by-token ms)."""
+    r = np.zeros(4, np.float32)
+    e = _err()
+    if lib().xj_cuda_gdn_prefill_check(S, Hk, Hv, T, r.ctypes.data, e, 512):
+        _raise(e)
+    return tuple(float(v) for v in r)
 
 
 def _err():
