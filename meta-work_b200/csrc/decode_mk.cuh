@@ -147,12 +147,15 @@ XJ_DEV bool mk_wait(uint64_t *bar, uint32_t parity, int *err, int code, int *dia
 }
 
 // All consumer threads of all CTAs: returns false (uniformly) when the grid records an error.
+// Ordering: the CTA barrier orders every consumer thread's writes before thread 0's release add, and
+// thread 0's acquire load before the other threads' reads after the second CTA barrier (release and
+// acquire are cumulative in the PTX memory model), so no separate fences are needed; the add returns
+// nothing, so the arriving CTA does not wait for it.
 XJ_DEV bool mk_grid_sync(unsigned *bar, unsigned target, int *err, int tid, int *diag, int step, int ph) {
     __shared__ int s_ok;
     BarC::sync();
     if (tid == 0) {
-        __threadfence();
-        atomicAdd(bar, 1u);
+        asm volatile("red.release.gpu.global.add.u32 [%0], 1;" :: "l"(bar) : "memory");
         int ok = 1;
         const unsigned long long t0 = globaltimer();
         for (int it = 0; ld_acquire(bar) < target; it++) {
@@ -165,7 +168,6 @@ XJ_DEV bool mk_grid_sync(unsigned *bar, unsigned target, int *err, int tid, int 
             }
             __nanosleep(20);
         }
-        __threadfence();
         if (ok && ld_volatile(err)) ok = 0;
         s_ok = ok;
     }
