@@ -58,6 +58,60 @@ def hbm_peak():
         return FALLBACK_HBM_GBS, "fallback"
 
 
+class NvmlClocks:
+    """NVML sampling (every ~2 ms, read-only queries) during the timed region: SM clock, max SM clock,
+    throttle reasons; the same counters nvidia-smi reports, at a rate that covers a ~100 ms region."""
+
+    NAMES = [("hw_slowdown", "nvmlClocksThrottleReasonHwSlowdown"),
+             ("hw_thermal_slowdown", "nvmlClocksThrottleReasonHwThermalSlowdown"),
+             ("sw_thermal_slowdown", "nvmlClocksThrottleReasonSwThermalSlowdown"),
+             ("sw_power_cap", "nvmlClocksThrottleReasonSwPowerCap")]
+
+    def __init__(self, gpu: int):
+        import threading
+        import pynvml as nv
+        self.nv = nv
+        nv.nvmlInit()
+        h = None
+        try:   # the CUDA device's own NVML handle (CUDA and NVML may number GPUs differently)
+            import torch
+            pr = torch.cuda.get_device_properties(gpu)
+            bus = f"{pr.pci_domain_id:08x}:{pr.pci_bus_id:02x}:{pr.pci_device_id:02x}.0"
+            h = nv.nvmlDeviceGetHandleByPciBusId(bus)
+        except Exception:
+            h = nv.nvmlDeviceGetHandleByIndex(gpu)
+        self.h = h
+        self.max = nv.nvmlDeviceGetMaxClockInfo(h, nv.NVML_CLOCK_SM)
+        self.bits = [(n, getattr(nv, c, 0)) for n, c in self.NAMES]
+        reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        self.samples, self.stopping = [], False
+
+        def run():
+            while not self.stopping:
+                self.samples.append((nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM), reasons(h)))
+                time.sleep(0.002)
+        self.t = threading.Thread(target=run, daemon=True)
+        self.t.start()
+        while not self.samples:
+            time.sleep(0.001)
+
+    def stop(self):
+        self.stopping = True
+        self.t.join()
+        sm = [float(c) for c, _ in self.samples]
+        reasons = sorted({n for _, r in self.samples for n, b in self.bits if b and (r & b)})
+        self.nv.nvmlShutdown()
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": float(self.max), "reasons": reasons,
+                "samples": len(sm), "source": "nvml"}
+
+
+def clocks_sampler(gpu: int):
+    try:
+        return NvmlClocks(gpu)
+    except Exception:
+        return Clocks(gpu)
+
+
 class Clocks:
     """nvidia-smi sampling during the timed region (SM clock, throttle reasons)."""
 
@@ -389,7 +443,7 @@ def main():
     pos0 = stage.n_past
     # timed region: exactly K decode steps, device-timed with CUDA events on the stage stream
     barrier()
-    clocks = Clocks(local)
+    clocks = clocks_sampler(local)
     toks, _, ms = stage.decode(last, args.steps)
     barrier()
     clk = clocks.stop()
