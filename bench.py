@@ -448,7 +448,7 @@ def main():
     barrier()
     clk = clocks.stop()
     dev_ms = float(ms[0] + ms[1])
-    kern_ms = float(ms[1])                     # the decode steps after the 1-token prompt (one launch)
+    kern_ms = float(ms[1])                     # the persistent launch: all K steps (one launch)
     launches = stage.last_decode_launches()
     last = toks[-1:]
     # end to end through the public C ABI with host buffers (token ids in, ids out), host wall clock
@@ -472,8 +472,8 @@ def main():
     if rank == 0:
         peak, peak_kind = hbm_peak()
         b = step_bytes(cfg, pos0 + args.steps // 2)
-        n_kern = args.steps - 1
         persistent = launches[1] == 1
+        n_kern = args.steps if persistent else args.steps - 1   # the persistent launch runs every step
         achieved = b["total"] * n_kern / (kern_ms / 1e3) / 1e9
         line = {
             "metric": METRIC, "value": round(value, 2), "unit": "tok/s", "n_gpus": world, "steps": args.steps,

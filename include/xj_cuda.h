@@ -60,7 +60,8 @@ int xj_cuda_set_options(int which, int value);
 // chunks of max_batch, continuing from the stage's n_past), then emits n_gen ids into out (out[0] is
 // the argmax after the prompt). Each emitted id except the last is fed back, so the stage's n_past
 // grows by n_prompt + n_gen - 1. margins (may be NULL) receives each step's top-2 logit gap.
-// gpu_ms (may be NULL) receives [prefill ms, decode ms] measured with CUDA events on the stage stream.
+// gpu_ms (may be NULL) receives [prefill ms, decode ms] measured with CUDA events on the stage stream;
+// with the persistent decode kernel the prompt's last token is the kernel's first step (decode ms).
 int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, int32_t *out, float *margins,
                    float *gpu_ms, char *err, size_t errlen);
 

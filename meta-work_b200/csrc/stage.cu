@@ -1129,29 +1129,37 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
         im->out_cap = cap;
     }
     CK(cudaMemsetAsync(im->step, 0, sizeof(int), im->st));
+    int persist = 0;
+    if (g_opt_persist) {
+        char why[256];
+        persist = mk_build(s, why, sizeof why) == 1;
+    }
     CK(cudaEventRecord(im->ev[0], im->st));
     const long long nl0 = im->nlaunch;
     const int B = s->max_batch;
-    for (int i = 0; i < n_prompt; i += B) {
-        const int T = n_prompt - i < B ? n_prompt - i : B;
+    // with the persistent kernel the prompt's last token is its first step (it picks out[0]); otherwise
+    // the last prompt chunk ends with the head and the greedy pick
+    const int n_pre = persist ? n_prompt - 1 : n_prompt;
+    for (int i = 0; i < n_pre; i += B) {
+        const int T = n_pre - i < B ? n_pre - i : B;
         CK(cudaMemcpyAsync(im->tok, prompt + i, sizeof(int32_t) * T, cudaMemcpyHostToDevice, im->st));
         launch(im, k_embed, dim3((E / 8 + 127) / 128, T), dim3(128), 0, im->tok_embd, (const int32_t *)im->tok, T, im->x, E);
-        const bool last = i + T == n_prompt;
+        const bool last = !persist && i + T == n_prompt;
         run_layers(s, T, false, last ? T - 1 : T);
         if (last) head_argmax(s, im->x + (size_t)(T - 1) * E);   // picks out[0], embeds it, position +1
+    }
+    if (persist) {
+        CK(cudaMemcpyAsync(im->tok, prompt + n_prompt - 1, sizeof(int32_t), cudaMemcpyHostToDevice, im->st));
+        launch(im, k_embed, dim3((E / 8 + 127) / 128, 1), dim3(128), 0, im->tok_embd, (const int32_t *)im->tok, 1, im->x, E);
     }
     CK(cudaEventRecord(im->ev[1], im->st));
     im->last_launches[0] = im->nlaunch - nl0;
     im->last_launches[1] = 0;
-    int persist = 0;
-    if (n_gen > 1 && g_opt_persist) {
-        char why[256];
-        persist = mk_build(s, why, sizeof why) == 1;
-    }
-    if (n_gen > 1 && persist) {
-        // segments of at most 8192 steps keep the grid barrier's 32-bit counter far from wrapping
-        for (int done = 0; done < n_gen - 1; done += 8192) {
-            if (mk_launch(s, n_gen - 1 - done < 8192 ? n_gen - 1 - done : 8192, err, errlen)) return -1;
+    if (persist) {
+        // every step in the persistent kernel (step 0 = the last prompt token); segments of at most 8192
+        // steps keep the grid barrier's 32-bit counter far from wrapping
+        for (int done = 0; done < n_gen; done += 8192) {
+            if (mk_launch(s, n_gen - done < 8192 ? n_gen - done : 8192, err, errlen)) return -1;
             im->last_launches[1]++;
         }
     } else if (n_gen > 1) {
