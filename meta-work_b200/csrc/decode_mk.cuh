@@ -43,7 +43,9 @@ static_assert(MK_ATTN_SCR * 4 <= MK_XS_BYTES, "attention scratch lives in the ac
 using BarC = BarNamed<1, MK_CTHREADS>;           // the consumer warps only
 
 enum { MK_GEMV = 0, MK_GDN = 1, MK_ATTN = 2, MK_ARGMAX = 3 };
-enum { PRO_GNORM = 3 };                          // per-head RMSNorm(ssm_norm) * silu(z), core/xj_cpu.c:218-224
+enum { PRO_GNORM = 3,                             // per-head RMSNorm(ssm_norm) * silu(z), core/xj_cpu.c:218-224
+       PRO_GNORM_S = 4 };                         // the same with x2 = silu(z) already (MK_EPI_SILU)
+enum { MK_EPI_SILU = 4 };                         // store silu(row) (the gate rows z of a GDN layer)
 
 struct alignas(16) MkPhase {
     int op;
@@ -237,8 +239,9 @@ XJ_DEV float mk_prologue(const MkPhase &p, __half *xs, float *xsum, int tid) {
         const int i = r * 4 * MK_CTHREADS + 4 * tid;
         const bool in = i < K;
         v[r] = in ? ldcg4(px + i) : z4;
-        w[r] = in && pro == PRO_NORM ? ld4(pw + i) : in && pro == PRO_GNORM ? ld4(pw + i % gs) : z4;
-        v2[r] = in && (pro == PRO_SWIGLU || pro == PRO_GNORM) ? ldcg4(px2 + i) : z4;
+        const bool gn = pro == PRO_GNORM || pro == PRO_GNORM_S;
+        w[r] = in && pro == PRO_NORM ? ld4(pw + i) : in && gn ? ld4(pw + i % gs) : z4;
+        v2[r] = in && (pro == PRO_SWIGLU || gn) ? ldcg4(px2 + i) : z4;
     }
     double ss = 0.0;
     float am = 0.0f;
@@ -250,10 +253,10 @@ XJ_DEV float mk_prologue(const MkPhase &p, __half *xs, float *xsum, int tid) {
             const float xv = f4(v[r], e);
             if (pro == PRO_NORM) { ss += (double)xv * xv; am = fmaxf(am, fabsf(xv * f4(w[r], e))); }
             else if (pro == PRO_SWIGLU) { const float y = silu_f(xv) * f4(v2[r], e); f4set(v[r], e, y); am = fmaxf(am, fabsf(y)); }
-            else if (pro != PRO_GNORM) am = fmaxf(am, fabsf(xv));
+            else if (pro != PRO_GNORM && pro != PRO_GNORM_S) am = fmaxf(am, fabsf(xv));
         }
     }
-    if (pro == PRO_GNORM) {
+    if (pro == PRO_GNORM || pro == PRO_GNORM_S) {
         // o * (1/sqrt(mean_head(o^2) + eps)) * w[j] * silu(z): head sums (exact, in double) over the
         // gs/4 lanes of a head, across warps through shared memory for heads wider than 128
         double hd[NG];
@@ -284,19 +287,20 @@ XJ_DEV float mk_prologue(const MkPhase &p, __half *xs, float *xsum, int tid) {
             const float sc = 1.0f / sqrtf((float)(so / gs) + eps);
 #pragma unroll
             for (int e = 0; e < 4; e++) {
-                const float y = f4(v[r], e) * sc * f4(w[r], e) * silu_f(f4(v2[r], e));
+                const float z = f4(v2[r], e);
+                const float y = f4(v[r], e) * sc * f4(w[r], e) * (pro == PRO_GNORM_S ? z : silu_f(z));
                 f4set(v[r], e, y);
                 am = fmaxf(am, fabsf(y));
             }
         }
     }
-    ss = warp_sum_d(ss);
+    if (pro == PRO_NORM) ss = warp_sum_d(ss);
     am = warp_max(am);
     if (lane == 0) { s_ss[warp] = ss; s_am[warp] = am; }
     BarC::sync();
     double tss = lane < MK_CWARPS ? s_ss[lane] : 0.0;
     float tam = lane < MK_CWARPS ? s_am[lane] : 0.0f;
-    tss = warp_sum_d(tss);
+    if (pro == PRO_NORM) tss = warp_sum_d(tss);
     tam = warp_max(tam);
     const float nsc = pro == PRO_NORM ? 1.0f / sqrtf((float)(tss / K) + eps) : 1.0f;
     const float m = tam * nsc;
@@ -518,7 +522,7 @@ XJ_DEV void mk_epilogue(const MmaJob &jb, int tile, const float *red, float tsca
 #pragma unroll
         for (int w = 0; w < MK_CWARPS; w++) s += red[w * 16 + tid];
         s /= tscale;
-        jb.y[(size_t)tile * 16 + tid] = jb.epi == EPI_ADD ? e.y + s : s;
+        jb.y[(size_t)tile * 16 + tid] = jb.epi == EPI_ADD ? e.y + s : jb.epi == MK_EPI_SILU ? silu_f(s) : s;
     }
 }
 

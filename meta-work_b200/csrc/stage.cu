@@ -801,14 +801,17 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
             const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v;
             Job qkv{Ly.qkv, im->qkvb, CD};
             qkv.epi = EPI_CONV; qkv.conv_state = Ly.conv; qkv.conv_w = Ly.conv_w; qkv.kc = hp->conv_k;
+            // the gate rows z are stored as silu(z) (MK_EPI_SILU): only the gated norm below reads them
+            Job zj{Ly.gate, im->z, DI};
+            zj.epi = MK_EPI_SILU;
             ok = ok && mk_gemv(prog, stream, E, PRO_NORM, im->x, nullptr, Ly.attn_norm, eps, 0,
-                               {qkv, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
+                               {qkv, zj, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
             MkPhase g{};
             g.op = MK_GDN; g.gdn = gdn_args(im, hp, Ly, 1, false); g.gs = hp->s_k;
             prog.push_back(g);
             Job out{Ly.out, im->x, E};
             out.epi = EPI_ADD;
-            ok = ok && mk_gemv(prog, stream, DI, PRO_GNORM, im->o, im->z, Ly.ssm_norm, eps, hp->s_k, {out});
+            ok = ok && mk_gemv(prog, stream, DI, PRO_GNORM_S, im->o, im->z, Ly.ssm_norm, eps, hp->s_k, {out});
         } else {
             const int H = hp->n_head, Hkv = hp->n_head_kv, D = hp->head_dim, nq = 2 * H * D, nk = Hkv * D;
             const float *q, *k, *v;
@@ -849,7 +852,7 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
         };
         const MkPhase &g = prog[ms.ph];
         if (g.pro == PRO_NORM) add(g.norm_w, (size_t)g.K * 4);
-        if (g.pro == PRO_GNORM) add(g.norm_w, (size_t)g.gs * 4);
+        if (g.pro == PRO_GNORM || g.pro == PRO_GNORM_S) add(g.norm_w, (size_t)g.gs * 4);
         for (int j = 0; j < g.njob; j++)
             if (g.job[j].epi == EPI_CONV) {
                 add(g.job[j].conv_w, (size_t)g.job[j].w.N * g.job[j].kc * 4);
