@@ -740,6 +740,7 @@ template <bool B64>
 static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_xt(const float *x, const float *x2, long long ldx, int K, int pro,
                                                                    const float *norm_w, float eps, void *buf, int T) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     __shared__ float pred[MMA_WARPS][2];
     __shared__ float s_scale, s_nsc;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = blockIdx.x;

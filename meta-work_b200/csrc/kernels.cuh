@@ -56,6 +56,7 @@ static __global__ void k_dequant(DevMat w, int row0, int nrows, float *out) {
 // x[t] = row tok[t] of the embedding table; out-of-range ids give zeros (core/xj_cpu.c:369-373).
 static __global__ void k_embed(DevMat w, const int32_t *tok, int T, float *x, int ldx) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     const int t = blockIdx.y;
     if (t >= T) return;
     const int id = tok[t];
@@ -75,6 +76,7 @@ static __global__ void k_embed(DevMat w, const int32_t *tok, int T, float *x, in
 // y[r] = x[r] * w / sqrt(mean(x[r]^2) + eps), sum in double (core/xj_cpu.c:56-61). One block per row.
 static __global__ void k_rmsnorm(const float *x, long long ldx, const float *w, float *y, long long ldy, int n, float eps) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     __shared__ double red[32];
     const float *xr = x + blockIdx.x * ldx;
     float *yr = y + blockIdx.x * ldy;
@@ -151,6 +153,7 @@ static __global__ void __launch_bounds__(256) k_gemv_generic(GemvArgs a) {
 // after token t (t < T-1) is saved to ck[t][CD][KC-1] (core/xj_cpu.c:220).
 static __global__ void k_conv_silu(float *qkv, long long ldq, int T, int CD, int KC, float *state, const float *cw, float *ck) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     const int c = blockIdx.x * blockDim.x + threadIdx.x;
     if (c >= CD) return;
     float cs[8];
@@ -288,6 +291,7 @@ constexpr int GC_MIN_T = 32;      // forwards of at least this many tokens take 
 template <int S>
 __global__ void __launch_bounds__(256) k_gdn_chunk_prep(GdnArgs a, float *qn, float *kn, float *kk, float *qk) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     extern __shared__ __align__(16) float gsm[];
     constexpr int CP = GC_C + 4;                           // transposed rows [S][CP]
     float *qt = gsm, *kt = gsm + S * CP;
@@ -359,6 +363,7 @@ template <int S>
 __global__ void __launch_bounds__(256) k_gdn_chunk(GdnArgs a, const float *qn, const float *kn, const float *kk,
                                                    const float *qk) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     constexpr int P = S / 16, SP = S + 4, CP = GC_C + 1;
     extern __shared__ __align__(16) float gsm[];
     float *qs = gsm, *ks = qs + GC_C * SP;                 // [C][SP]
@@ -497,6 +502,7 @@ __global__ void __launch_bounds__(256) k_gdn_chunk(GdnArgs a, const float *qn, c
 template <int S>
 __global__ void __launch_bounds__(S) k_gdn_gnorm(GdnArgs a) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     __shared__ double red[32];
     const int t = blockIdx.x, hv = blockIdx.y, j = threadIdx.x;
     float *op = a.out + (size_t)t * a.ldo + hv * S + j;
@@ -510,6 +516,7 @@ __global__ void __launch_bounds__(S) k_gdn_gnorm(GdnArgs a) {
 template <int S>
 __global__ void __launch_bounds__(4 * S) k_gdn(GdnArgs a) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     gdn_head<S, BarBlock>(a, blockIdx.x, threadIdx.x);
 }
 
@@ -576,6 +583,7 @@ XJ_DEV void attn_prep_slot(const AttnArgs &a, int slot, int t, int tid) {
 template <typename KV>
 static __global__ void k_attn_prep(AttnArgs a) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     attn_prep_slot<KV, BarBlock>(a, blockIdx.x, blockIdx.y, threadIdx.x);
 }
 
@@ -641,6 +649,7 @@ XJ_DEV void attn_head(const AttnArgs &a, int h, int t, int tid) {
 template <typename KV, int DPL>
 static __global__ void __launch_bounds__(128) k_attn(AttnArgs a) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     attn_head<KV, DPL, BarBlock>(a, blockIdx.x, blockIdx.y, threadIdx.x);
 }
 
@@ -648,18 +657,21 @@ static __global__ void __launch_bounds__(128) k_attn(AttnArgs a) {
 // out = silu(g) * u (core/xj_cpu.c:273).
 static __global__ void k_swiglu(const float *g, const float *u, float *out, long long n) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x)
         out[i] = silu_f(g[i]) * u[i];
 }
 
 static __global__ void k_advance(int *npast, int T) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     if (threadIdx.x == 0 && blockIdx.x == 0) *npast += T;
 }
 
 // Positions of B sequences: npast[b] += T.
 static __global__ void k_advance_batch(int *npast, int B, int T) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     for (int b = threadIdx.x; b < B; b += blockDim.x) npast[b] += T;
 }
 
@@ -809,6 +821,7 @@ XJ_DEV void argmax_final_dev(const ArgmaxArgs &a, int tid, int nthr) {
 // One block of 1024 threads.
 static __global__ void __launch_bounds__(1024) k_argmax_final(ArgmaxArgs a) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     argmax_final_dev<BarBlock>(a, threadIdx.x, blockDim.x);
 }
 
@@ -821,6 +834,7 @@ static __global__ void __launch_bounds__(1024) k_argmax_final(ArgmaxArgs a) {
 template <int S>
 __global__ void __launch_bounds__(4 * S, 2) k_gdn_batch(GdnArgs a, long long state_stride) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     const int b = blockIdx.y;
     GdnArgs c = a;
     c.qkv += b * a.ldq; c.z += b * a.ldz; c.beta += b * a.ldg; c.alpha += b * a.ldg;
@@ -843,6 +857,7 @@ XJ_DEV AttnArgs attn_seq(const AttnArgs &a, const int *npast_b, long long kv_str
 template <typename KV>
 static __global__ void k_attn_prep_batch(AttnArgs a, const int *npast_b, long long kv_stride) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     attn_prep_slot<KV, BarBlock>(attn_seq<KV>(a, npast_b, kv_stride, blockIdx.y), blockIdx.x, 0, threadIdx.x);
 }
 
@@ -850,6 +865,7 @@ static __global__ void k_attn_prep_batch(AttnArgs a, const int *npast_b, long lo
 template <typename KV, int DPL>
 static __global__ void __launch_bounds__(128) k_attn_batch(AttnArgs a, const int *npast_b, long long kv_stride) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     attn_head<KV, DPL, BarBlock>(attn_seq<KV>(a, npast_b, kv_stride, blockIdx.y), blockIdx.x, 0, threadIdx.x);
 }
 
@@ -857,6 +873,7 @@ static __global__ void __launch_bounds__(128) k_attn_batch(AttnArgs a, const int
 static __global__ void __launch_bounds__(256) k_argmax_rows_batch(const float *logits, int V, float *pbest, float *psecond,
                                                                    int *pidx, int ntiles) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     // 16 tiles per block, one per half-warp (the shuffles below stay inside a half-warp)
     const int b = blockIdx.y, tile = blockIdx.x * 16 + (threadIdx.x >> 4), row = threadIdx.x & 15, r = tile * 16 + row;
     const float *lg = logits + (size_t)b * V;
@@ -879,6 +896,7 @@ static __global__ void __launch_bounds__(256) k_argmax_rows_batch(const float *l
 // written to out_tok[b*out_stride + step_b], with the next token's embedding into row b of x.
 static __global__ void __launch_bounds__(1024) k_argmax_final_batch(ArgmaxArgs a, long long out_stride, int E) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     const int b = blockIdx.x;
     ArgmaxArgs c = a;
     c.pbest += (size_t)b * a.ntiles; c.psecond += (size_t)b * a.ntiles; c.pidx += (size_t)b * a.ntiles;
@@ -892,6 +910,7 @@ static __global__ void __launch_bounds__(1024) k_argmax_final_batch(ArgmaxArgs a
 // strict '>' of core/xj_spec.c:12-16).
 static __global__ void __launch_bounds__(1024) k_argmax_pick_rows(const float *logits, int V, int32_t *ids) {
     griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     __shared__ float sb[32];
     __shared__ int si[32];
     const float *lg = logits + (size_t)blockIdx.x * V;
