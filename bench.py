@@ -366,15 +366,16 @@ def run_pipeline(args, rank, local, world):
     dist.barrier()
     torch.cuda.synchronize()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record()
-    ids = None
-    for i in range(args.steps):                                            # K steps of every sequence
+    with st.context():                     # stage kernels and transfers on the stage's stream
+        first = [p._ids_from(np.zeros(n, np.int32)) for (r0, n) in p.mbs] if rank == 0 else None
+        e0.record()
+        for i in range(args.steps):        # K steps of every sequence; after the first, the picks are fed back
+            p.step(first if i == 0 else None, True)
         if rank == 0:
-            ids = ids if ids is not None else [p._ids_from(np.zeros(n, np.int32)) for (r0, n) in p.mbs]
-        got = p.step(ids, True)
-        if rank == 0:
-            ids = got
-    e1.record()
+            p.drain()                      # the last step's picks reach rank 0
+        if rank == world - 1:
+            p.finish()
+        e1.record()
     torch.cuda.synchronize()
     dist.barrier()
     t = torch.tensor([e0.elapsed_time(e1)], device=dev)

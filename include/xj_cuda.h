@@ -153,6 +153,13 @@ int xj_cuda_batch_forward_rows(xj_cuda_batch *b, float *x_dev, int row0, int nro
 // Output norm, LM head and greedy pick of the micro-batch: tok_dev[i] = next id of sequence row0+i.
 int xj_cuda_batch_pick_rows(xj_cuda_batch *b, const float *x_dev, int row0, int nrows, int32_t *tok_dev, char *err,
                             size_t errlen);
+// The CUDA stream (cudaStream_t) the batch's kernels run on, so that a caller's transfers (e.g. NCCL
+// send/recv of the activations) can be ordered with them on the device.
+void *xj_cuda_batch_stream(xj_cuda_batch *b);
+// on != 0: the *_rows calls return as soon as their kernels are queued (launch errors are still
+// reported); xj_cuda_batch_sync waits for the stream and reports errors of queued work.
+int xj_cuda_batch_set_async(xj_cuda_batch *b, int on);
+int xj_cuda_batch_sync(xj_cuda_batch *b, char *err, size_t errlen);
 
 // Capacity, in floats, of the fixed device scratch used by xj_cuda_norm_gemv_noalloc (256 KiB).
 #define XJC_NOALLOC_MAX_FLOATS 65536

@@ -941,6 +941,7 @@ struct BatchImpl {
     cudaGraphExec_t step_graph = nullptr;
     int step_kernels = 0;
     long long last_launches[2] = {0, 0};
+    bool async_rows = false;               // *_rows calls return without waiting for the stream
 };
 
 // Layers of the batch's stage on rows x[0..nr) = sequences r0..r0+nr-1 (their own states and positions).
@@ -1810,6 +1811,16 @@ int xj_cuda_batch_decode(xj_cuda_batch *b, const int32_t *prompts, int n_prompt,
 }
 
 // ---- pipeline-stage entry points: device buffers of the batch's device, rows = a micro-batch
+// End of a *_rows call: wait for the stream and check errors, or in async mode only check the launches
+// (errors then surface at xj_cuda_batch_sync).
+static int rows_check(BatchImpl *bi, char *err, size_t errlen) {
+    Impl *im = I(bi->s);
+    if (!bi->async_rows) return sync_check(im, err, errlen);
+    const cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) { seterr(err, errlen, "GPU error: %s", cudaGetErrorString(e)); return -1; }
+    return 0;
+}
+
 int xj_cuda_batch_embed_rows(xj_cuda_batch *b, const int32_t *tok_dev, float *x_dev, int nrows, char *err, size_t errlen) {
     if (!b || !tok_dev || !x_dev || nrows < 1 || nrows > b->impl.B) { seterr(err, errlen, "bad arguments"); return -1; }
     BatchImpl *bi = &b->impl;
@@ -1818,7 +1829,7 @@ int xj_cuda_batch_embed_rows(xj_cuda_batch *b, const int32_t *tok_dev, float *x_
     if (!im->tok_embd.p) { seterr(err, errlen, "this batch has no embedding table (layer range does not start at 0)"); return -1; }
     const int E = bi->s->m->hp.n_embd;
     launch(im, k_embed, dim3((E / 8 + 127) / 128, nrows), dim3(128), 0, im->tok_embd, tok_dev, nrows, x_dev, E);
-    return sync_check(im, err, errlen);
+    return rows_check(bi, err, errlen);
 }
 
 int xj_cuda_batch_forward_rows(xj_cuda_batch *b, float *x_dev, int row0, int nrows, char *err, size_t errlen) {
@@ -1829,7 +1840,7 @@ int xj_cuda_batch_forward_rows(xj_cuda_batch *b, float *x_dev, int row0, int nro
     if (bi->n_past + 1 > bi->n_ctx) { seterr(err, errlen, "context is full (%d)", bi->n_ctx); return -1; }
     run_layers_batch(bi, x_dev, row0, nrows);
     launch(im, k_advance_batch, dim3(1), dim3(256), 0, bi->npast + row0, nrows, 1);
-    if (sync_check(im, err, errlen)) return -1;
+    if (rows_check(bi, err, errlen)) return -1;
     if (row0 + nrows == bi->B) bi->n_past++;   // the host mirror follows the last micro-batch of a step
     return 0;
 }
@@ -1843,6 +1854,21 @@ int xj_cuda_batch_pick_rows(xj_cuda_batch *b, const float *x_dev, int row0, int 
     if (!bi->s->has_head) { seterr(err, errlen, "this batch has no head"); return -1; }
     // the pick's embedding and position update go to scratch: the pipeline's first stage embeds the ids
     head_batch(bi, x_dev, row0, nrows, tok_dev, im->h, bi->np_scratch + row0);
+    return rows_check(bi, err, errlen);
+}
+
+void *xj_cuda_batch_stream(xj_cuda_batch *b) { return b ? (void *)I(b->impl.s)->st : nullptr; }
+
+int xj_cuda_batch_set_async(xj_cuda_batch *b, int on) {
+    if (!b) return -1;
+    b->impl.async_rows = on != 0;
+    return 0;
+}
+
+int xj_cuda_batch_sync(xj_cuda_batch *b, char *err, size_t errlen) {
+    if (!b) { seterr(err, errlen, "no batch"); return -1; }
+    Impl *im = I(b->impl.s);
+    DevGuard dg(im->dev);
     return sync_check(im, err, errlen);
 }
 

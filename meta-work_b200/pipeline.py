@@ -13,6 +13,12 @@ Micro-batches keep the stages busy at the same time: while the last stage works 
 step s, the first stage already runs micro-batch k+1. Activations ([rows][n_embd] fp32) and ids go
 over NCCL (NVLink) on GPUs and over gloo in the CPU tests; they travel on two process groups, one per
 direction, so a send in one direction never waits behind a receive in the other on one communicator.
+On GPUs every stage call and every transfer is queued on the stage's own CUDA stream (the library's
+stream, wrapped as a torch external stream), so they are ordered on the device and the host never waits
+inside a step. The last rank sends each micro-batch's picks as soon as they are made, without waiting
+for the send; rank 0 receives them only when the next step's micro-batch needs them. So the first
+stage starts micro-batch k of the next step as soon as that micro-batch's picks exist, and no stream
+ever holds a receive of activations behind a send of ids (which could deadlock the two communicators).
 KV caches and recurrent state stay on the rank that owns the layer.
 
 The per-stage compute is behind a small interface (``embed``, ``forward``, ``pick``) so that the
@@ -20,6 +26,7 @@ schedule itself is tested on CPU with a stand-in stage (tests/test_pipeline_cpu.
 """
 from __future__ import annotations
 
+import contextlib
 import ctypes
 from dataclasses import dataclass
 
@@ -63,6 +70,9 @@ class CudaStage:
             ("xj_cuda_batch_embed_rows", ip, [vp, vp, vp, ip, cp, sz]),
             ("xj_cuda_batch_forward_rows", ip, [vp, vp, ip, ip, cp, sz]),
             ("xj_cuda_batch_pick_rows", ip, [vp, vp, ip, ip, vp, cp, sz]),
+            ("xj_cuda_batch_stream", vp, [vp]),
+            ("xj_cuda_batch_set_async", ip, [vp, ip]),
+            ("xj_cuda_batch_sync", ip, [vp, cp, sz]),
         ]:
             getattr(lib, name).restype = res
             getattr(lib, name).argtypes = args
@@ -74,6 +84,9 @@ class CudaStage:
         self.E = model.n_embd
         self.has_head = has_head
         self.first = l0 == 0
+        # queue-only stage calls, ordered with the caller's transfers on the library's stream
+        lib.xj_cuda_batch_set_async(self.p, 1)
+        self.stream = torch.cuda.ExternalStream(lib.xj_cuda_batch_stream(self.p), device=device)
 
     def _check(self, rc, e):
         if rc:
@@ -82,10 +95,18 @@ class CudaStage:
     def new_x(self, nrows):
         return self.torch.empty((nrows, self.E), dtype=self.torch.float32, device=self.device)
 
+    def context(self):
+        """Everything of a step runs on the stage's stream (transfers included)."""
+        return self.torch.cuda.stream(self.stream)
+
     def sync(self):
-        # received tensors are written on torch's streams; the library's kernels run on the stage's own
-        # stream, so the data must have landed before a pointer is handed over
-        self.torch.cuda.synchronize(self.device)
+        # transfers run on the stage's own stream (see context), so a received tensor is ordered before
+        # the kernels that read it without waiting on the host
+        pass
+
+    def host_sync(self):
+        e = ctypes.create_string_buffer(512)
+        self._check(self.lib.xj_cuda_batch_sync(self.p, e, 512), e)
 
     def new_ids(self, nrows):
         return self.torch.empty(nrows, dtype=self.torch.int32, device=self.device)
@@ -125,6 +146,8 @@ class Pipeline:
         self.mbs = micro_batches(n_seq, n_mb)
         self.gx, self.gt = gx, gt
         self.stats = PipelineStats()
+        self._pending = []           # last rank: (work, ids) of picks sent to rank 0
+        self._local = None           # one rank only: the last step's picks
 
     def _send_x(self, x):
         self.dist.send(x, self.rank + 1, group=self.gx)
@@ -134,15 +157,29 @@ class Pipeline:
         self.dist.recv(x, self.rank - 1, group=self.gx)
         self.stage.sync()
 
+    def _recv_ids(self, n):
+        ids = self.stage.new_ids(n)
+        self.dist.recv(ids, self.world - 1, group=self.gt)
+        return ids
+
     def step(self, ids_by_mb, pick: bool):
-        """One token of every sequence. Rank 0 passes ids_by_mb (one id tensor per micro-batch) and,
-        when pick, receives the next ids from the last rank; returns them (rank 0 and last rank)."""
-        out = []
+        """One token of every sequence. Rank 0 passes ids_by_mb (one id tensor per micro-batch), or None
+        to feed the previous step's picks, each received from the last rank just before its micro-batch
+        needs it. The last rank, when pick, sends each micro-batch's picks to rank 0 as soon as they are
+        made (non-blocking; see finish). Returns the ids rank 0 fed, the picks on the last rank."""
+        fed, out = [], []
         last = self.rank == self.world - 1
         for k, (r0, n) in enumerate(self.mbs):
             x = self.stage.new_x(n)
             if self.rank == 0:
-                self.stage.embed(ids_by_mb[k], x)
+                if ids_by_mb is not None:
+                    ids = ids_by_mb[k]
+                elif self.world > 1:
+                    ids = self._recv_ids(n)
+                else:
+                    ids = self._local[k]
+                fed.append(ids)
+                self.stage.embed(ids, x)
             else:
                 self._recv_x(x)
             self.stage.forward(x, r0, n)
@@ -152,27 +189,37 @@ class Pipeline:
                 ids = self.stage.new_ids(n)
                 self.stage.pick(x, r0, n, ids)
                 out.append(ids)
-        # the ids go back to rank 0 after every micro-batch of the step has been sent forward, on their
-        # own group: rank 0 receives them in micro-batch order
-        if pick and self.world > 1:
-            if last:
-                for ids in out:
-                    self.dist.send(ids, 0, group=self.gt)
+                if self.world > 1:
+                    # to rank 0 right away, on its own group; nothing waits for it before finish(), so a
+                    # device-ordered stream never holds a receive of activations behind this send
+                    self._pending.append((self.dist.isend(ids, 0, group=self.gt), ids))
                     self.stats.sent_id_bytes += ids.numel() * ids.element_size()
-            elif self.rank == 0:
-                out = []
-                for (r0, n) in self.mbs:
-                    ids = self.stage.new_ids(n)
-                    self.dist.recv(ids, self.world - 1, group=self.gt)
-                    out.append(ids)
-                self.stage.sync()
+        if last and pick:
+            self._local = out
         self.stats.steps += 1
-        return out
+        return fed if self.rank == 0 else out
+
+    def drain(self):
+        """Rank 0: the picks of the last step (not fed to any step)."""
+        if self.world == 1:
+            return self._local
+        return [self._recv_ids(n) for (r0, n) in self.mbs]
+
+    def finish(self):
+        """Last rank: wait for the picks sent to rank 0."""
+        for w, _ in self._pending:
+            w.wait()
+        self._pending = []
 
     def decode(self, prompts, n_gen: int):
         """Greedy decode: prompts [n_seq][P] (numpy, used on rank 0). Returns ids [n_seq][n_gen] on rank 0
         (None elsewhere): the prompt goes through in P lockstep steps, the last of which picks out[:, 0];
         each generated id but the last is fed back."""
+        ctx = getattr(self.stage, "context", None)
+        with (ctx() if ctx else contextlib.nullcontext()):
+            return self._decode(prompts, n_gen)
+
+    def _decode(self, prompts, n_gen: int):
         P = int(prompts.shape[1]) if self.rank == 0 else None
         if self.world > 1:
             import torch
@@ -180,19 +227,21 @@ class Pipeline:
             self.dist.broadcast(t, 0, group=self.gx)
             P = int(t.item())
         gen = []
-        ids = None
         for i in range(P + n_gen - 1):
             pick = i >= P - 1
-            if self.rank == 0:
-                if i < P:
-                    ids = [self._ids_from(prompts[r0:r0 + n, i]) for (r0, n) in self.mbs]
-                # else: ids are the previous step's picks
+            ids = None
+            if self.rank == 0 and i < P:
+                ids = [self._ids_from(prompts[r0:r0 + n, i]) for (r0, n) in self.mbs]
             got = self.step(ids, pick)
-            if pick and self.rank == 0:
-                ids = got
-                gen.append(np.concatenate([g.cpu().numpy() for g in got]))
+            if self.rank == 0 and i >= P:
+                gen.append(got)          # the ids fed at step i are the picks of step i - 1 (on the device)
+        if self.rank == 0:
+            gen.append(self.drain())
+        if self.rank == self.world - 1:
+            self.finish()
         if self.rank != 0:
             return None
+        gen = [np.concatenate([g.cpu().numpy() for g in got]) for got in gen]   # copies on the stage's stream
         return np.stack(gen, axis=1).astype(np.int32)
 
     def _ids_from(self, arr):
