@@ -1020,8 +1020,8 @@ constexpr int B64_WARPS = 8;
 constexpr int B64_TILES = 2 * B64_WARPS;          // row tiles per block
 constexpr int B64_ROWS = 16 * B64_TILES;          // 256
 constexpr int B64_RS = B64_T + 4;                 // partial-sum row stride (floats): rows stay 16-byte aligned
-constexpr int B64_MAXSPLIT = 8;                   // CTAs per block: a portable cluster
-constexpr int B64_RECV_ROWS = B64_ROWS + B64_MAXSPLIT;   // >= ns * ceil(256 / ns) for every ns <= 8
+constexpr int B64_MAXSPLIT = 16;                  // CTAs per block: up to a (non-portable) 16-CTA cluster
+constexpr int B64_RECV_ROWS = B64_ROWS + B64_MAXSPLIT;   // >= ns * ceil(256 / ns) for every ns <= B64_MAXSPLIT
 template <int TYPE> struct B64Geo;                // weight bytes per tile and chunk, and their layout
 template <> struct B64Geo<XJ_Q4_K> { static constexpr int Q = 1024, H = 0, S = 256, D = 0; };
 template <> struct B64Geo<XJ_Q6_K> { static constexpr int Q = 1024, H = 512, S = 256, D = 32; };
@@ -1557,6 +1557,7 @@ inline cudaError_t launch_b64_t(B64Args a, cudaStream_t st) {
     constexpr size_t smem = b64_smem<TYPE>();
     if (!sms_dev[dev]) {
         cudaFuncSetAttribute(k_gemv_b64<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_gemv_b64<TYPE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         cudaDeviceGetAttribute(&sms_dev[dev], cudaDevAttrMultiProcessorCount, dev);
         occ[dev][1] = sms_dev[dev];
         for (int ns = 2; ns <= B64_MAXSPLIT; ns++) {
