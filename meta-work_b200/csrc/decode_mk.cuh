@@ -7,11 +7,13 @@
 // in a loop and the phases are separated by a grid barrier instead (a counter in global memory; every
 // wait bounded).
 //
-// Each CTA has 16 consumer warps and one producer warp. The producer walks the same phase program and,
-// for every matrix-vector phase, requests this CTA's weight chunks into a shared-memory ring with bulk
-// asynchronous copies (one mbarrier per slot for "full", one for "empty"; no multicast). Weights do not
-// depend on activations, so the producer runs ahead of the consumers across phase boundaries and the
-// grid barriers: the HBM stream of the next phases overlaps the barrier and the small phases.
+// Each CTA has 16 compute warps, one producer warp and one epilogue warp. The producer walks the same
+// phase program and, for every matrix-vector phase, requests this CTA's weight chunks into a
+// shared-memory ring with bulk asynchronous copies (one mbarrier per slot for "full", one for "empty";
+// no multicast). Weights do not depend on activations, so the producer runs ahead of the consumers
+// across phase boundaries and the grid barriers: the HBM stream of the next phases overlaps the barrier
+// and the small phases. The compute warps hand each tile's partial rows to the epilogue warp through a
+// small ring of buffers (mbarriers again) and go straight on to the next tile.
 //
 // Phases (one decode step, core/xj_cpu.c:161-291 for the layer math):
 //   GEMV   y_j (+)= W_j . f(x) for up to 4 matrices sharing x (the tensor-core unit code of
@@ -31,16 +33,19 @@
 
 namespace xjk {
 
-constexpr int MK_CWARPS = 16;                    // consumer warps
+constexpr int MK_CWARPS = 16;                    // consumer (compute) warps
 constexpr int MK_CTHREADS = MK_CWARPS * 32;      // 512
-constexpr int MK_THREADS = MK_CTHREADS + 32;     // + the producer warp
+constexpr int MK_EWARP = MK_CWARPS + 1;          // the epilogue warp (after the producer warp)
+constexpr int MK_THREADS = MK_CTHREADS + 64;     // + the producer and the epilogue warp
+constexpr int MK_NR = 4;                         // tile partial buffers between compute and epilogue warps
 constexpr int MK_SLOT = 26880;                   // largest chunk: 8 Q6_K units
 constexpr int MK_NS = 6;                         // ring slots
 constexpr int MK_KMAX = MMA_KMAX_PT * MK_CTHREADS;
 constexpr int MK_XS_BYTES = 2 * (MK_KMAX + 16) * 2;   // hi/lo fp16 columns (also GDN / attention scratch)
 constexpr int MK_ATTN_SCR = 5440;                     // floats of attention scratch (split merge: nsplit*(D+2))
 static_assert(MK_ATTN_SCR * 4 <= MK_XS_BYTES, "attention scratch lives in the activation staging area");
-using BarC = BarNamed<1, MK_CTHREADS>;           // the consumer warps only
+using BarC = BarNamed<1, MK_CTHREADS>;           // the compute warps only
+using BarP = BarNamed<2, MK_CTHREADS + 32>;      // compute + epilogue warps (descriptor hand-over, phase ends)
 
 enum { MK_GEMV = 0, MK_GDN = 1, MK_ATTN = 2, MK_ARGMAX = 3 };
 enum { PRO_GNORM = 3,                             // per-head RMSNorm(ssm_norm) * silu(z), core/xj_cpu.c:218-224
@@ -92,7 +97,7 @@ struct MkArgs {
 };
 
 constexpr size_t MK_SMEM = (size_t)MK_NS * MK_SLOT + MK_XS_BYTES + (MK_KMAX / 32) * 4 + MK_CWARPS * 128 * 4 +
-                           2 * MK_CWARPS * 16 * 4;
+                           MK_NR * MK_CWARPS * 16 * 4;
 
 XJ_DEV unsigned long long globaltimer() {
     unsigned long long t;
@@ -148,14 +153,14 @@ XJ_DEV bool mk_wait(uint64_t *bar, uint32_t parity, int *err, int code, int *dia
     return false;
 }
 
-// All consumer threads of all CTAs: returns false (uniformly) when the grid records an error.
-// Ordering: the CTA barrier orders every consumer thread's writes before thread 0's release add, and
-// thread 0's acquire load before the other threads' reads after the second CTA barrier (release and
-// acquire are cumulative in the PTX memory model), so no separate fences are needed; the add returns
-// nothing, so the arriving CTA does not wait for it.
+// All compute and epilogue threads of all CTAs: returns false (uniformly) when the grid records an
+// error. Ordering: the CTA barrier orders every participating thread's writes before thread 0's release
+// add, and thread 0's acquire load before the other threads' reads after the second CTA barrier
+// (release and acquire are cumulative in the PTX memory model), so no separate fences are needed; the
+// add returns nothing, so the arriving CTA does not wait for it.
 XJ_DEV bool mk_grid_sync(unsigned *bar, unsigned target, int *err, int tid, int *diag, int step, int ph) {
     __shared__ int s_ok;
-    BarC::sync();
+    BarP::sync();
     if (tid == 0) {
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" :: "l"(bar) : "memory");
         int ok = 1;
@@ -173,7 +178,7 @@ XJ_DEV bool mk_grid_sync(unsigned *bar, unsigned target, int *err, int tid, int 
         if (ok && ld_volatile(err)) ok = 0;
         s_ok = ok;
     }
-    BarC::sync();
+    BarP::sync();
     return s_ok != 0;
 }
 
@@ -217,7 +222,8 @@ XJ_DEV void mk_issue_t(const MkStream &S, int j, int tile, int u0, int cu, uint8
 // sums, as k_gemv_mma's prologue at T = 1 computes them. Thread t takes the 4 consecutive elements
 // 2048r + 4t .. +3 (r < 3): one vector load per operand (all issued before the first use, so the
 // prologue costs one memory round trip), two half2 stores per column, and block sums over 8 lanes.
-// Sums of squares are accumulated in double, where they are exact, so their order does not matter.
+// Sums of squares are accumulated in double (as core/xj_cpu.c:56-61 does); a different summation order
+// changes the double sum only near 1e-16 relative, far below the float scale derived from it.
 // Returns the range scale.
 XJ_DEV float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
 XJ_DEV float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
@@ -257,7 +263,7 @@ XJ_DEV float mk_prologue(const MkPhase &p, __half *xs, float *xsum, int tid) {
         }
     }
     if (pro == PRO_GNORM || pro == PRO_GNORM_S) {
-        // o * (1/sqrt(mean_head(o^2) + eps)) * w[j] * silu(z): head sums (exact, in double) over the
+        // o * (1/sqrt(mean_head(o^2) + eps)) * w[j] * silu(z): head sums (in double) over the
         // gs/4 lanes of a head, across warps through shared memory for heads wider than 128
         double hd[NG];
 #pragma unroll
@@ -775,7 +781,9 @@ XJ_DEV void mk_gdn_phase(const GdnArgs &a, float *scr, int tid) {
 __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[MK_NS], empty[MK_NS];
+    __shared__ __align__(8) uint64_t rfull[MK_NR], rfree[MK_NR];   // tile partials: ready / consumed
     __shared__ unsigned s_issued;
+    __shared__ float s_tsc;        // the running GEMV phase's range scale (compute -> epilogue warp)
     __shared__ MkPhase sph[2];     // consumers: this phase's descriptor and the next one (prefetched)
     __shared__ MkStream sst[2];    // producer: same for its GEMV stream
     uint8_t *ring = smem;
@@ -788,6 +796,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
     const int G = gridDim.x, cta = blockIdx.x;
     if (tid == 0) {
         for (int s = 0; s < MK_NS; s++) { mbar_init(&full[s], 1); mbar_init(&empty[s], MK_CWARPS); }
+        for (int s = 0; s < MK_NR; s++) { mbar_init(&rfull[s], MK_CWARPS); mbar_init(&rfree[s], 1); }
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         s_issued = 0;
     }
@@ -845,46 +854,71 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
         cp_async_wait_all();
         __syncwarp();
     } else {
-        // ---------------- consumers
+        // ---------------- compute warps (warp < MK_CWARPS) and the epilogue warp (warp == MK_EWARP)
+        // Per tile the compute warps leave their partial rows in one of MK_NR buffers and go on to the
+        // next tile; the epilogue warp sums the partials (fixed warp order), applies the epilogue and
+        // hands the buffer back. So no CTA-wide barrier separates the tiles of a phase.
+        const bool ew = warp == MK_EWARP;
         const int g = lane >> 2, c = lane & 3;
-        float *scw = scs + warp * 128;
-        unsigned nbar = 0;
-        int rb = 0, gp = 0;         // gp: phases run so far (selects the descriptor buffer)
-        copy_desc_async(&sph[0], &A.prog[0], (int)sizeof(MkPhase), tid);
+        float *scw = scs + (ew ? 0 : warp) * 128;
+        unsigned nbar = 0, ntile = 0;   // ntile: GEMV tiles of this CTA so far (counted alike by both roles)
+        int gp = 0;                 // gp: phases run so far (selects the descriptor buffer)
+        if (!ew) copy_desc_async(&sph[0], &A.prog[0], (int)sizeof(MkPhase), tid);
         cp_async_wait_all();
-        BarC::sync();
+        BarP::sync();
         for (int step = 0; step < A.nsteps; step++) {
             bool ok = true;
             for (int ph = 0; ph < A.nphase; ph++, gp++) {
                 const MkPhase &p = sph[gp & 1];
                 const int pn = ph + 1 < A.nphase ? ph + 1 : 0;
-                copy_desc_async(&sph[(gp + 1) & 1], &A.prog[pn], (int)sizeof(MkPhase), tid);
-                const bool tr = A.trace && step == A.nsteps - 1 && tid == 0;
+                if (!ew) copy_desc_async(&sph[(gp + 1) & 1], &A.prog[pn], (int)sizeof(MkPhase), tid);
+                const bool last_step = A.trace && step == A.nsteps - 1;
+                const bool tr = last_step && tid == 0, tre = last_step && tid == MK_EWARP * 32;
+                unsigned long long *trow = A.trace ? A.trace + ((size_t)cta * A.nphase + ph) * 12 : nullptr;
                 unsigned long long wait_ns = 0;
-                if (tr) A.trace[((size_t)cta * A.nphase + ph) * 12] = globaltimer();
-                if (p.op == MK_GEMV && cta < p.ntiles) {
+                if (tr) trow[0] = globaltimer();
+                if (p.op == MK_GEMV && cta < p.ntiles && ew) {
+                    // ---- epilogues of this CTA's tiles, in the compute warps' order
                     ArgRun ar;
+                    int ntile_done = 0;
+                    for (int tg = cta; tg < p.ntiles; tg += G, ntile++, ntile_done++) {
+                        const int j = mk_job_of(p, tg);
+                        const MmaJob &jb = p.job[j];
+                        const int tile = tg - p.tile_start[j];
+                        EpiPre e;
+                        mk_epi_load(jb, tile, lane, e);    // overlaps the wait for the partials
+                        const int b = (int)(ntile % MK_NR);
+                        if (!mk_wait(&rfull[b], (ntile / MK_NR) & 1, A.err, 3, A.diag, step, ph, (int)ntile, 32)) continue;
+                        if (tre && ntile_done == 0) trow[10] = globaltimer();
+                        mk_epilogue(jb, tile, red + b * (MK_CWARPS * 16), s_tsc, lane, e, ar);
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&rfree[b]);
+                        if (tre && ntile_done == 0) { trow[11] = globaltimer(); trow[6] = trow[11]; }
+                    }
+                    if (lane == 0 && p.job[0].epi == EPI_ARGMAX) {
+                        // one greedy-pick partial per CTA (CTA c holds tiles c, c + G, ...)
+                        p.job[0].pbest[cta] = ar.b; p.job[0].psecond[cta] = ar.b2; p.job[0].pidx[cta] = ar.bi;
+                    }
+                } else if (p.op == MK_GEMV && cta < p.ntiles) {
                     const float tsc = mk_prologue(p, xs, xsum, tid);
-                    if (tr) A.trace[((size_t)cta * A.nphase + ph) * 12 + 5] = globaltimer();
+                    if (tid == 0) s_tsc = tsc;     // read by the epilogue warp after this warp's first hand-over
+                    if (tr) trow[5] = globaltimer();
                     int ntile_done = 0;
                     const int xstride = p.K + 16;
                     const bool bcol = g < 2;
                     const __half *xb = xs + (size_t)g * xstride + 4 * c;
                     const float *xsum_t = c == 0 ? xsum : nullptr;
                     const __half *xb2 = xs + (size_t)(g & 1) * xstride + 4 * c;   // always a staged column
-                    for (int tg = cta; tg < p.ntiles; tg += G) {
+                    for (int tg = cta; tg < p.ntiles; tg += G, ntile++, ntile_done++) {
                         const int j = mk_job_of(p, tg);
-                        const MmaJob &jb = p.job[j];
-                        const Tiled &W = jb.w;
-                        const int tile = tg - p.tile_start[j], CU = mk_cu(W.type);
+                        const Tiled &W = p.job[j].w;
+                        const int CU = mk_cu(W.type);
                         float yg = 0.0f, yg8 = 0.0f;
-                        EpiPre e;
-                        mk_epi_load(jb, tile, tid, e);
                         for (int u0 = 0; u0 < W.nu; u0 += CU, consumed++) {
                             const int slot = consumed % MK_NS;
                             const unsigned long long w0 = tr ? globaltimer() : 0;
                             const bool got = mk_wait(&full[slot], (consumed / MK_NS) & 1, A.err, 1, A.diag, step, ph, (int)consumed, 32);
-                            if (tr) { const unsigned long long w1 = globaltimer(); wait_ns += w1 - w0; if (ntile_done == 0 && u0 == 0) A.trace[((size_t)cta * A.nphase + ph) * 12 + 8] = w1; }
+                            if (tr) { const unsigned long long w1 = globaltimer(); wait_ns += w1 - w0; if (ntile_done == 0 && u0 == 0) trow[8] = w1; }
                             const uint8_t *st = ring + (size_t)slot * MK_SLOT;
                             const int cu = W.nu - u0 < CU ? W.nu - u0 : CU;
                             if (W.type == XJ_Q4_K) {
@@ -910,23 +944,19 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                             if (lane == 0 && got) mbar_arrive(&empty[slot]);
                             if (!got && drain_from == 0xffffffffu) drain_from = consumed;
                         }
-                        float *rr = red + rb * (MK_CWARPS * 16);
+                        // hand the tile's partial rows to the epilogue warp (its buffer free again first)
+                        const int b = (int)(ntile % MK_NR);
+                        if (ntile >= MK_NR && lane == 0)
+                            mk_wait(&rfree[b], ((ntile / MK_NR) - 1) & 1, A.err, 3, A.diag, step, ph, (int)ntile, 32);
+                        __syncwarp();
+                        float *rr = red + b * (MK_CWARPS * 16);
                         if (c == 0) { rr[warp * 16 + g] = yg; rr[warp * 16 + g + 8] = yg8; }
-                        if (tr && ntile_done == 0) A.trace[((size_t)cta * A.nphase + ph) * 12 + 9] = globaltimer();
-                        BarC::sync();
-                        if (tr && ntile_done == 0) A.trace[((size_t)cta * A.nphase + ph) * 12 + 10] = globaltimer();
-                        mk_epilogue(jb, tile, rr, tsc, tid, e, ar);
-                        if (tr && ntile_done == 0) A.trace[((size_t)cta * A.nphase + ph) * 12 + 11] = globaltimer();
-                        rb ^= 1;
-                        if (tr && ntile_done == 0) A.trace[((size_t)cta * A.nphase + ph) * 12 + 6] = globaltimer();
-                        ntile_done++;
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&rfull[b]);
+                        if (tr && ntile_done == 0) trow[9] = globaltimer();
                     }
-                    if (tr) A.trace[((size_t)cta * A.nphase + ph) * 12 + 7] = ntile_done;
-                    if (tid == 0 && p.job[0].epi == EPI_ARGMAX) {
-                        // one greedy-pick partial per CTA (CTA c holds tiles c, c + G, ...)
-                        p.job[0].pbest[cta] = ar.b; p.job[0].psecond[cta] = ar.b2; p.job[0].pidx[cta] = ar.bi;
-                    }
-                } else if (p.op == MK_GDN) {
+                    if (tr) trow[7] = ntile_done;
+                } else if (!ew && p.op == MK_GDN) {
                     switch (p.gs) {
                     case 16: mk_gdn_phase<16>(p.gdn, scr, tid); break;
                     case 32: mk_gdn_phase<32>(p.gdn, scr, tid); break;
@@ -935,15 +965,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                     case 256: mk_gdn_phase<256>(p.gdn, scr, tid); break;
                     default: break;
                     }
-                } else if (p.op == MK_ATTN) {
+                } else if (!ew && p.op == MK_ATTN) {
                     if (A.kv_f32) mk_attn_phase<float>(A, p.attn, scr, tid);
                     else mk_attn_phase<__half>(A, p.attn, scr, tid);
-                } else if (p.op == MK_ARGMAX) {
+                } else if (!ew && p.op == MK_ARGMAX) {
                     if (cta == 0) argmax_final_dev<BarC>(p.am, tid, MK_CTHREADS);
                 }
                 if (tr) {
-                    A.trace[((size_t)cta * A.nphase + ph) * 12 + 1] = globaltimer();
-                    A.trace[((size_t)cta * A.nphase + ph) * 12 + 2] = wait_ns;
+                    trow[1] = globaltimer();
+                    trow[2] = wait_ns;
                 }
                 cp_async_wait_all();   // the next descriptor has landed (visible after the barrier below)
                 if (step == A.nsteps - 1 && ph == A.nphase - 1) break;

@@ -517,7 +517,8 @@ int sync_check(Impl *im, char *err, size_t errlen) {
     int flag = 0;
     if (im->derr && cudaMemcpy(&flag, im->derr, sizeof(int), cudaMemcpyDeviceToHost) == cudaSuccess && flag) {
         cudaMemset(im->derr, 0, sizeof(int));
-        seterr(err, errlen, "a bounded wait on the GPU gave up (%s)", flag == 2 ? "grid barrier" : "weight stream");
+        seterr(err, errlen, "a bounded wait on the GPU gave up (%s)",
+               flag == 2 ? "grid barrier" : flag == 3 ? "tile partial hand-over" : "weight stream");
         return -1;
     }
     return 0;
@@ -1598,8 +1599,8 @@ int xj_cuda_phase_trace(const xj_stage *s, double *out, int cap) {
                 first += ((double)r[6] - (double)r[5]) * 1e-3;
                 f1 += ((double)r[8] - (double)r[5]) * 1e-3;    // prologue end -> first chunk ready
                 f2 += ((double)r[9] - (double)r[8]) * 1e-3;    // tensor-core work of the first tile (warp 0)
-                f3 += ((double)r[10] - (double)r[9]) * 1e-3;   // tile barrier (waiting for the other warps)
-                f4 += ((double)r[11] - (double)r[10]) * 1e-3;  // epilogue
+                f3 += ((double)r[10] - (double)r[9]) * 1e-3;   // warp 0's hand-over -> all partials with the epilogue warp
+                f4 += ((double)r[11] - (double)r[10]) * 1e-3;  // epilogue (epilogue warp)
                 ntl++;
             }
             if (r[0] < s0) s0 = r[0];
