@@ -49,8 +49,9 @@ using BarP = BarNamed<2, MK_CTHREADS + 32>;      // compute + epilogue warps (de
 
 enum { MK_GEMV = 0, MK_GDN = 1, MK_ATTN = 2, MK_ARGMAX = 3 };
 enum { PRO_GNORM = 3,                             // per-head RMSNorm(ssm_norm) * silu(z), core/xj_cpu.c:218-224
-       PRO_GNORM_S = 4 };                         // the same with x2 = silu(z) already (MK_EPI_SILU)
-enum { MK_EPI_SILU = 4 };                         // store silu(row) (the gate rows z of a GDN layer)
+       PRO_GNORM_S = 4,                           // the same with x2 = silu(z) already (MK_EPI_SILU)
+       PRO_SWIGLU_S = 5 };                        // x * up with x = silu(gate) already (MK_EPI_SILU)
+enum { MK_EPI_SILU = 4 };                         // store silu(row) (GDN gate rows z, FFN gate rows)
 
 struct alignas(16) MkPhase {
     int op;
@@ -96,7 +97,7 @@ struct MkArgs {
     int *diag;                   // first wait that gave up: kind, cta, tid, step, phase, index, extra
 };
 
-constexpr size_t MK_SMEM = (size_t)MK_NS * MK_SLOT + MK_XS_BYTES + (MK_KMAX / 32) * 4 + MK_CWARPS * 128 * 4 +
+constexpr size_t MK_SMEM = (size_t)MK_NS * MK_SLOT + MK_XS_BYTES + 2 * (MK_KMAX / 32) * 4 + MK_CWARPS * 128 * 4 +
                            MK_NR * MK_CWARPS * 16 * 4;
 
 XJ_DEV unsigned long long globaltimer() {
@@ -218,51 +219,55 @@ XJ_DEV void mk_issue_t(const MkStream &S, int j, int tile, int u0, int cu, uint8
     if (G::DB) bulk_g2s(st + G::CU * (G::QB + G::HB + G::SB), S.d[j] + tu0 * G::DB, cu * G::DB, bar);
 }
 
-// f(x) for one token -> exact power-of-two range scale -> fp16 hi/lo columns (B operand) + 32-wide block
-// sums, as k_gemv_mma's prologue at T = 1 computes them. Thread t takes the 4 consecutive elements
+// f(x) for one token -> fp16 hi/lo columns (B operand) with a power-of-two range scale per 32-element
+// block, the block sums and the blocks' inverse scales. Thread t takes the 4 consecutive elements
 // 2048r + 4t .. +3 (r < 3): one vector load per operand (all issued before the first use, so the
-// prologue costs one memory round trip), two half2 stores per column, and block sums over 8 lanes.
-// Sums of squares are accumulated in double (as core/xj_cpu.c:56-61 does); a different summation order
-// changes the double sum only near 1e-16 relative, far below the float scale derived from it.
-// Returns the range scale.
+// prologue costs one memory round trip), two half2 stores per column; a block is 8 consecutive lanes,
+// so its largest magnitude, scale and sum are warp shuffles. Only RMSNorm needs a CTA-wide sum (of
+// squares, in double as core/xj_cpu.c:56-61 does; a different summation order changes it only near
+// 1e-16 relative, far below the float scale derived from it).
+//
+// Scaling a block by a power of two is exact and the unit code multiplies the block's weight scales by
+// the inverse (exact again), so every product and partial sum equals the one computed with one scale
+// for the whole vector (as the standalone kernels do) times a power of two: the results are the same
+// bits unless an element is small enough (about 2^-17 of the vector's largest) that its fp16 low part
+// turns subnormal under the whole-vector scale.
 XJ_DEV float4 ldcg4(const float *p) { return __ldcg(reinterpret_cast<const float4 *>(p)); }
 XJ_DEV float4 ld4(const float *p) { return *reinterpret_cast<const float4 *>(p); }
 XJ_DEV float f4(const float4 &v, int e) { return e == 0 ? v.x : e == 1 ? v.y : e == 2 ? v.z : v.w; }
 XJ_DEV void f4set(float4 &v, int e, float x) { if (e == 0) v.x = x; else if (e == 1) v.y = x; else if (e == 2) v.z = x; else v.w = x; }
 
-XJ_DEV float mk_prologue(const MkPhase &p, __half *xs, float *xsum, int tid) {
+XJ_DEV void mk_prologue(const MkPhase &p, __half *xs, float *xsum, float *xinv, int tid) {
     __shared__ double s_ss[MK_CWARPS];
-    __shared__ float s_am[MK_CWARPS];
     __shared__ double s_hd[MK_KMAX / 128];
     const int lane = tid & 31, warp = tid >> 5, K = p.K, xstride = K + 16, pro = p.pro, gs = p.gs;
     const float *px = p.x, *px2 = p.x2, *pw = p.norm_w;
     const float eps = p.eps;
     constexpr int NG = MK_KMAX / (4 * MK_CTHREADS);   // groups of 2048 elements
     const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+    const bool gn = pro == PRO_GNORM || pro == PRO_GNORM_S;
     float4 v[NG], w[NG], v2[NG];
 #pragma unroll
     for (int r = 0; r < NG; r++) {
         const int i = r * 4 * MK_CTHREADS + 4 * tid;
         const bool in = i < K;
         v[r] = in ? ldcg4(px + i) : z4;
-        const bool gn = pro == PRO_GNORM || pro == PRO_GNORM_S;
         w[r] = in && pro == PRO_NORM ? ld4(pw + i) : in && gn ? ld4(pw + i % gs) : z4;
-        v2[r] = in && (pro == PRO_SWIGLU || gn) ? ldcg4(px2 + i) : z4;
+        v2[r] = in && (pro == PRO_SWIGLU || pro == PRO_SWIGLU_S || gn) ? ldcg4(px2 + i) : z4;
     }
     double ss = 0.0;
-    float am = 0.0f;
 #pragma unroll
     for (int r = 0; r < NG; r++) {
         if (r * 4 * MK_CTHREADS + 4 * tid >= K) continue;
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             const float xv = f4(v[r], e);
-            if (pro == PRO_NORM) { ss += (double)xv * xv; am = fmaxf(am, fabsf(xv * f4(w[r], e))); }
-            else if (pro == PRO_SWIGLU) { const float y = silu_f(xv) * f4(v2[r], e); f4set(v[r], e, y); am = fmaxf(am, fabsf(y)); }
-            else if (pro != PRO_GNORM && pro != PRO_GNORM_S) am = fmaxf(am, fabsf(xv));
+            if (pro == PRO_NORM) ss += (double)xv * xv;
+            else if (pro == PRO_SWIGLU) f4set(v[r], e, silu_f(xv) * f4(v2[r], e));
+            else if (pro == PRO_SWIGLU_S) f4set(v[r], e, xv * f4(v2[r], e));
         }
     }
-    if (pro == PRO_GNORM || pro == PRO_GNORM_S) {
+    if (gn) {
         // o * (1/sqrt(mean_head(o^2) + eps)) * w[j] * silu(z): head sums (in double) over the
         // gs/4 lanes of a head, across warps through shared memory for heads wider than 128
         double hd[NG];
@@ -294,34 +299,42 @@ XJ_DEV float mk_prologue(const MkPhase &p, __half *xs, float *xsum, int tid) {
 #pragma unroll
             for (int e = 0; e < 4; e++) {
                 const float z = f4(v2[r], e);
-                const float y = f4(v[r], e) * sc * f4(w[r], e) * (pro == PRO_GNORM_S ? z : silu_f(z));
-                f4set(v[r], e, y);
-                am = fmaxf(am, fabsf(y));
+                f4set(v[r], e, f4(v[r], e) * sc * f4(w[r], e) * (pro == PRO_GNORM_S ? z : silu_f(z)));
             }
         }
     }
-    if (pro == PRO_NORM) ss = warp_sum_d(ss);
-    am = warp_max(am);
-    if (lane == 0) { s_ss[warp] = ss; s_am[warp] = am; }
-    BarC::sync();
-    double tss = lane < MK_CWARPS ? s_ss[lane] : 0.0;
-    float tam = lane < MK_CWARPS ? s_am[lane] : 0.0f;
-    if (pro == PRO_NORM) tss = warp_sum_d(tss);
-    tam = warp_max(tam);
-    const float nsc = pro == PRO_NORM ? 1.0f / sqrtf((float)(tss / K) + eps) : 1.0f;
-    const float m = tam * nsc;
-    const float sc = ldexpf(1.0f, 14 - (m > 0.0f ? ilogbf(m) : 0));
+    float nsc = 1.0f;
+    if (pro == PRO_NORM) {
+        ss = warp_sum_d(ss);
+        if (lane == 0) s_ss[warp] = ss;
+        BarC::sync();
+        double tss = lane < MK_CWARPS ? s_ss[lane] : 0.0;
+        tss = warp_sum_d(tss);
+        nsc = 1.0f / sqrtf((float)(tss / K) + eps);
+    }
 #pragma unroll
     for (int r = 0; r < NG; r++) {
         const int i = r * 4 * MK_CTHREADS + 4 * tid;
         if (r * 4 * MK_CTHREADS >= K) break;          // uniform: whole groups beyond K
+        float val[4], m = 0.0f;
+#pragma unroll
+        for (int e = 0; e < 4; e++) {
+            val[e] = pro == PRO_NORM ? (f4(v[r], e) * nsc) * f4(w[r], e) : f4(v[r], e);
+            m = fmaxf(m, fabsf(val[e]));
+        }
+        // the block's largest magnitude (8 lanes; K is a multiple of 32, so a block is all in or all out)
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 1));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 2));
+        m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, 4));
+        const int ex = m > 0.0f ? ilogbf(m) : 14;
+        const float sc = ldexpf(1.0f, 14 - ex);
         float bs = 0.0f;
         __half hi[4], lo[4];
 #pragma unroll
         for (int e = 0; e < 4; e++) {
-            const float val = (pro == PRO_NORM ? (f4(v[r], e) * nsc) * f4(w[r], e) : f4(v[r], e)) * sc;
-            hi[e] = __float2half_rn(val);
-            lo[e] = __float2half_rn(val - __half2float(hi[e]));
+            const float vs = val[e] * sc;
+            hi[e] = __float2half_rn(vs);
+            lo[e] = __float2half_rn(vs - __half2float(hi[e]));
             bs += __half2float(hi[e]) + __half2float(lo[e]);
         }
         // block sums of the 32 elements of 8 consecutive lanes
@@ -334,11 +347,10 @@ XJ_DEV float mk_prologue(const MkPhase &p, __half *xs, float *xsum, int tid) {
             *reinterpret_cast<__half2 *>(xs + pos + 4) = __halves2half2(hi[2], hi[3]);
             *reinterpret_cast<__half2 *>(xs + xstride + pos) = __halves2half2(lo[0], lo[1]);
             *reinterpret_cast<__half2 *>(xs + xstride + pos + 4) = __halves2half2(lo[2], lo[3]);
-            if ((lane & 7) == 0) xsum[i >> 5] = bs;
+            if ((lane & 7) == 0) { xsum[i >> 5] = bs; xinv[i >> 5] = ldexpf(1.0f, ex - 14); }
         }
     }
     BarC::sync();
-    return sc;
 }
 
 // ------------------------------------------------------------------ K-quant units at T = 1
@@ -351,8 +363,8 @@ XJ_DEV float mk_prologue(const MkPhase &p, __half *xs, float *xsum, int tid) {
 XJ_DEV uint32_t byte_sel(uint32_t w, int j) { return __byte_perm(w, 0u, 0x4440u | (uint32_t)j); }   // byte j of w
 
 template <int HH>
-XJ_DEV void mk_q4k(const uint8_t *stage, int ui, int u, int lane, const __half *xb, const float *xsum, float *scw,
-                   float &yg, float &yg8) {
+XJ_DEV void mk_q4k(const uint8_t *stage, int ui, int u, int lane, const __half *xb, const float *xsum, const float *xinv,
+                   float *scw, float &yg, float &yg8) {
     using G = Geo<XJ_Q4_K>;
     const int g = lane >> 2;
     const uint8_t *qs = stage + ui * G::QB;
@@ -374,9 +386,10 @@ XJ_DEV void mk_q4k(const uint8_t *stage, int ui, int u, int lane, const __half *
                 m_ = (int)((b8 >> 4) | ((b4 >> 6) << 4));
             }
             const float d1 = d * (float)s_, m1 = dmin * (float)m_;
+            const float iv = xinv[u * 8 + 4 * HH + sbl];   // the activation block's inverse range scale
             float *o = scw + ((sbl * 8 + (r & 7)) * 4 + (r >> 3) * 2);
-            o[0] = d1;
-            o[1] = 64.0f * d1 + m1;
+            o[0] = d1 * iv;
+            o[1] = (64.0f * d1 + m1) * iv;
         }
     }
     __syncwarp();
@@ -404,7 +417,8 @@ XJ_DEV void mk_q4k(const uint8_t *stage, int ui, int u, int lane, const __half *
 }
 
 template <int HH>
-XJ_DEV void mk_q6k(const uint8_t *stage, int ui, int u, int lane, const __half *xb, float *scw, float &yg, float &yg8) {
+XJ_DEV void mk_q6k(const uint8_t *stage, int ui, int u, int lane, const __half *xb, const float *xinv, float *scw,
+                   float &yg, float &yg8) {
     using G = Geo<XJ_Q6_K>;
     const int g = lane >> 2;
     const uint8_t *qs = stage + ui * G::QB;
@@ -422,7 +436,8 @@ XJ_DEV void mk_q6k(const uint8_t *stage, int ui, int u, int lane, const __half *
 #pragma unroll
         for (int e = 0; e < 4; e++) {
             const int sl = 4 * (lane >> 4) + e;
-            scw[(sl * 8 + (r & 7)) * 2 + (r >> 3)] = d * (float)(int)(int8_t)(wsel >> (8 * e));
+            const float ds = d * (float)(int)(int8_t)(wsel >> (8 * e));
+            scw[(sl * 8 + (r & 7)) * 2 + (r >> 3)] = ds * xinv[u * 8 + 4 * HH + (sl >> 1)];
         }
     }
     __syncwarp();
@@ -443,6 +458,32 @@ XJ_DEV void mk_q6k(const uint8_t *stage, int ui, int u, int lane, const __half *
         yg8 = fmaf(sc2.y, d4[2] + d4[3], yg8);
     }
     __syncwarp();
+}
+
+// One Q8_0 unit (16 rows x 32 codes) at T = 1, unit_compute's arithmetic with the block's scale
+// multiplied by the activation block's inverse range scale.
+XJ_DEV void mk_q80(const uint8_t *stage, int ui, int u, int lane, bool bcol, const __half *xb, const float *xinv,
+                   float &yg, float &yg8) {
+    using G = Geo<XJ_Q8_0>;
+    const int g = lane >> 2;
+    const uint8_t *qs = stage + ui * G::QB;
+    const uint8_t *ds = stage + G::CU * G::QB + ui * G::DB;
+    const uint4 q = *reinterpret_cast<const uint4 *>(qs + lane * 16);
+    const float dv = lane < 16 ? h2f(*reinterpret_cast<const uint16_t *>(ds + lane * 2)) : 0.0f;
+    const float iv = xinv[u];
+    const float dg = __shfl_sync(0xffffffffu, dv, g) * iv, dg8 = __shfl_sync(0xffffffffu, dv, g + 8) * iv;
+    float d4[4] = {0.f, 0.f, 0.f, 0.f};
+    const int kb = u * 32;
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        uint32_t af[4];
+        q8_frag(word_of(q, 2 * e), word_of(q, 2 * e + 1), af);
+        uint2 bv = make_uint2(0u, 0u);
+        if (bcol) bv = *reinterpret_cast<const uint2 *>(xb + kb + 16 * e);
+        mma16816(d4, af, bv.x, bv.y);
+    }
+    yg = fmaf(dg, d4[0] + d4[1], yg);
+    yg8 = fmaf(dg8, d4[2] + d4[3], yg8);
 }
 
 // Global operands of a tile's epilogue, loaded when the tile starts so the load latency overlaps the
@@ -476,7 +517,7 @@ struct ArgRun {
 };
 
 // Epilogue of one 16-row tile from the per-warp partials red[warp][16] (fixed-order sum over warps).
-XJ_DEV void mk_epilogue(const MmaJob &jb, int tile, const float *red, float tscale, int tid, const EpiPre &e, ArgRun &ar) {
+XJ_DEV void mk_epilogue(const MmaJob &jb, int tile, const float *red, int tid, const EpiPre &e, ArgRun &ar) {
     const bool real = tile * 16 + (tid & 15) < jb.w.N;   // rows past N pad the last tile
     if (jb.epi == EPI_CONV) {
         if (tid < 16 && real) {
@@ -484,7 +525,6 @@ XJ_DEV void mk_epilogue(const MmaJob &jb, int tile, const float *red, float tsca
             float s = 0.0f;
 #pragma unroll
             for (int w = 0; w < MK_CWARPS; w++) s += red[w * 16 + tid];
-            s /= tscale;
             float acc = 0.0f;
 #pragma unroll
             for (int k = 0; k < MK_KC - 1; k++)
@@ -507,7 +547,6 @@ XJ_DEV void mk_epilogue(const MmaJob &jb, int tile, const float *red, float tsca
             float s = 0.0f;
 #pragma unroll
             for (int w = 0; w < MK_CWARPS; w++) s += red[w * 16 + row];
-            s /= tscale;
             if (jb.y && tid < 16 && real) jb.y[(size_t)tile * 16 + row] = s;
             if (!real) s = -INFINITY;
             float b = s, b2 = -INFINITY;
@@ -527,7 +566,6 @@ XJ_DEV void mk_epilogue(const MmaJob &jb, int tile, const float *red, float tsca
         float s = 0.0f;
 #pragma unroll
         for (int w = 0; w < MK_CWARPS; w++) s += red[w * 16 + tid];
-        s /= tscale;
         jb.y[(size_t)tile * 16 + tid] = jb.epi == EPI_ADD ? e.y + s : jb.epi == MK_EPI_SILU ? silu_f(s) : s;
     }
 }
@@ -783,13 +821,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
     __shared__ __align__(8) uint64_t full[MK_NS], empty[MK_NS];
     __shared__ __align__(8) uint64_t rfull[MK_NR], rfree[MK_NR];   // tile partials: ready / consumed
     __shared__ unsigned s_issued;
-    __shared__ float s_tsc;        // the running GEMV phase's range scale (compute -> epilogue warp)
     __shared__ MkPhase sph[2];     // consumers: this phase's descriptor and the next one (prefetched)
     __shared__ MkStream sst[2];    // producer: same for its GEMV stream
     uint8_t *ring = smem;
     __half *xs = reinterpret_cast<__half *>(smem + (size_t)MK_NS * MK_SLOT);
     float *xsum = reinterpret_cast<float *>(smem + (size_t)MK_NS * MK_SLOT + MK_XS_BYTES);
-    float *scs = xsum + MK_KMAX / 32;
+    float *xinv = xsum + MK_KMAX / 32;   // per 32-element activation block: 1 / its range scale
+    float *scs = xinv + MK_KMAX / 32;
     float *red = scs + MK_CWARPS * 128;
     float *scr = reinterpret_cast<float *>(xs);     // GDN / attention scratch (xs is dead between GEMVs)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -890,7 +928,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                         const int b = (int)(ntile % MK_NR);
                         if (!mk_wait(&rfull[b], (ntile / MK_NR) & 1, A.err, 3, A.diag, step, ph, (int)ntile, 32)) continue;
                         if (tre && ntile_done == 0) trow[10] = globaltimer();
-                        mk_epilogue(jb, tile, red + b * (MK_CWARPS * 16), s_tsc, lane, e, ar);
+                        mk_epilogue(jb, tile, red + b * (MK_CWARPS * 16), lane, e, ar);
                         __syncwarp();
                         if (lane == 0) mbar_arrive(&rfree[b]);
                         if (tre && ntile_done == 0) { trow[11] = globaltimer(); trow[6] = trow[11]; }
@@ -900,14 +938,12 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                         p.job[0].pbest[cta] = ar.b; p.job[0].psecond[cta] = ar.b2; p.job[0].pidx[cta] = ar.bi;
                     }
                 } else if (p.op == MK_GEMV && cta < p.ntiles) {
-                    const float tsc = mk_prologue(p, xs, xsum, tid);
-                    if (tid == 0) s_tsc = tsc;     // read by the epilogue warp after this warp's first hand-over
+                    mk_prologue(p, xs, xsum, xinv, tid);
                     if (tr) trow[5] = globaltimer();
                     int ntile_done = 0;
                     const int xstride = p.K + 16;
                     const bool bcol = g < 2;
                     const __half *xb = xs + (size_t)g * xstride + 4 * c;
-                    const float *xsum_t = c == 0 ? xsum : nullptr;
                     const __half *xb2 = xs + (size_t)(g & 1) * xstride + 4 * c;   // always a staged column
                     for (int tg = cta; tg < p.ntiles; tg += G, ntile++, ntile_done++) {
                         const int j = mk_job_of(p, tg);
@@ -924,20 +960,20 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                             if (W.type == XJ_Q4_K) {
                                 const int ui = warp >> 1;
                                 if (ui < cu) {
-                                    if (warp & 1) mk_q4k<1>(st, ui, u0 + ui, lane, xb2, xsum, scw, yg, yg8);
-                                    else mk_q4k<0>(st, ui, u0 + ui, lane, xb2, xsum, scw, yg, yg8);
+                                    if (warp & 1) mk_q4k<1>(st, ui, u0 + ui, lane, xb2, xsum, xinv, scw, yg, yg8);
+                                    else mk_q4k<0>(st, ui, u0 + ui, lane, xb2, xsum, xinv, scw, yg, yg8);
                                 }
                             } else if (W.type == XJ_Q6_K) {
                                 const int ui = warp >> 1;
                                 if (ui < cu) {
-                                    if (warp & 1) mk_q6k<1>(st, ui, u0 + ui, lane, xb2, scw, yg, yg8);
-                                    else mk_q6k<0>(st, ui, u0 + ui, lane, xb2, scw, yg, yg8);
+                                    if (warp & 1) mk_q6k<1>(st, ui, u0 + ui, lane, xb2, xinv, scw, yg, yg8);
+                                    else mk_q6k<0>(st, ui, u0 + ui, lane, xb2, xinv, scw, yg, yg8);
                                 }
                             } else {
 #pragma unroll
                                 for (int k = 0; k < Geo<XJ_Q8_0>::CU / MK_CWARPS; k++) {
                                     const int ui = warp + k * MK_CWARPS;
-                                    if (ui < cu) unit_compute<XJ_Q8_0>(st, ui, u0 + ui, 0, lane, bcol, xb, xsum_t, scw, yg, yg8);
+                                    if (ui < cu) mk_q80(st, ui, u0 + ui, lane, bcol, xb, xinv, yg, yg8);
                                 }
                             }
                             __syncwarp();

@@ -832,10 +832,13 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
             o.epi = EPI_ADD;
             ok = ok && mk_gemv(prog, stream, H * D, PRO_NONE, im->o, nullptr, nullptr, eps, 0, {o});
         }
-        ok = ok && mk_gemv(prog, stream, E, PRO_NORM, im->x, nullptr, Ly.post_norm, eps, 0, {{Ly.ffn_gate, im->g, FF}, {Ly.ffn_up, im->u, FF}});
+        // the gate rows are stored as silu(gate) (MK_EPI_SILU), once, instead of in every CTA's prologue
+        Job gate{Ly.ffn_gate, im->g, FF};
+        gate.epi = MK_EPI_SILU;
+        ok = ok && mk_gemv(prog, stream, E, PRO_NORM, im->x, nullptr, Ly.post_norm, eps, 0, {gate, {Ly.ffn_up, im->u, FF}});
         Job down{Ly.ffn_down, im->x, E};
         down.epi = EPI_ADD;
-        ok = ok && mk_gemv(prog, stream, FF, PRO_SWIGLU, im->g, im->u, nullptr, eps, 0, {down});
+        ok = ok && mk_gemv(prog, stream, FF, PRO_SWIGLU_S, im->g, im->u, nullptr, eps, 0, {down});
     }
     Job h{im->output, nullptr, im->output.N};
     h.epi = EPI_ARGMAX; h.pbest = im->pbest; h.psecond = im->psecond; h.pidx = im->pidx;
