@@ -134,49 +134,59 @@ XJ_DEV void mk_record(int *diag, int kind, int step, int ph, int idx, int extra)
     }
 }
 
-// Wait for an mbarrier phase; gives up (recording `code`) after MK_WAIT_NS (or 2^24 rounds of polls,
-// should the clock not advance) or as soon as another part of the grid has recorded an error. Between
-// rounds of polls the thread sleeps `nap` ns, so a waiting warp does not take issue slots from the
-// warps that compute.
+// Wait for an mbarrier phase; gives up (recording `code`) after MK_WAIT_NS (or 2^26 polls, should the
+// clock not advance) or once another part of the grid has recorded an error. mbarrier.try_wait suspends
+// the thread in hardware until the phase completes (or a short time limit), so the loop polls it back to
+// back and wakes as soon as the phase completes. The grid's error word is a global load of about a
+// microsecond: it is issued every 16 polls and its value read 16 polls later, so the wait never stalls on
+// it; the same polls read the clock and, if `nap` is set, sleep that many ns.
 XJ_DEV bool mk_wait(uint64_t *bar, uint32_t parity, int *err, int code, int *diag = nullptr, int step = 0,
                     int ph = 0, int idx = 0, int nap = 0) {
     if (mbar_try_wait(bar, parity)) return true;
     const unsigned long long t0 = globaltimer();
-    for (int it = 0; it < (1 << 24); it++) {
-        for (int i = 0; i < 4; i++)
-            if (mbar_try_wait(bar, parity)) return true;
-        if (nap) __nanosleep(nap);
-        if (ld_volatile(err)) return false;
-        if (globaltimer() - t0 > MK_WAIT_NS) break;
+    int ev = ld_volatile(err);
+    for (int it = 1; it < (1 << 26); it++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 15) == 0) {
+            if (ev) return false;
+            ev = ld_volatile(err);
+            if (globaltimer() - t0 > MK_WAIT_NS) break;
+            if (nap) __nanosleep(nap);
+        }
     }
     mk_record(diag, code == 1 ? 10 + (int)parity : code, step, ph, idx, (int)(globaltimer() - t0) / 1000);
     atomicExch(err, code);
     return false;
 }
 
-// All compute and epilogue threads of all CTAs: returns false (uniformly) when the grid records an
-// error. Ordering: the CTA barrier orders every participating thread's writes before thread 0's release
-// add, and thread 0's acquire load before the other threads' reads after the second CTA barrier
-// (release and acquire are cumulative in the PTX memory model), so no separate fences are needed; the
-// add returns nothing, so the arriving CTA does not wait for it.
+// All compute and epilogue threads of all CTAs: returns false (uniformly within the CTA) when the grid
+// records an error. Ordering: the CTA barrier orders every participating thread's writes before thread
+// 0's release add, and thread 0's acquire load before the other threads' reads after the second CTA
+// barrier (release and acquire are cumulative in the PTX memory model), so no separate fences are
+// needed; the add returns nothing, so the arriving CTA does not wait for it. Thread 0 polls the counter
+// back to back (one acquire load in flight); the error word is loaded alongside every 16 polls and its
+// value used at the next check, so it adds no round trip to the barrier. A CTA that passes a barrier
+// while another records an error stops at its next wait instead (every wait also reads the error word).
 XJ_DEV bool mk_grid_sync(unsigned *bar, unsigned target, int *err, int tid, int *diag, int step, int ph) {
     __shared__ int s_ok;
     BarP::sync();
     if (tid == 0) {
         asm volatile("red.release.gpu.global.add.u32 [%0], 1;" :: "l"(bar) : "memory");
-        int ok = 1;
+        int ok = 1, ev = ld_volatile(err);
         const unsigned long long t0 = globaltimer();
-        for (int it = 0; ld_acquire(bar) < target; it++) {
-            if (ld_volatile(err)) { ok = 0; break; }
-            if (globaltimer() - t0 > MK_WAIT_NS || it > (1 << 27)) {
-                mk_record(diag, 2, step, ph, (int)target, (int)ld_acquire(bar));
-                atomicExch(err, 2);
-                ok = 0;
-                break;
+        for (unsigned it = 1; ld_acquire(bar) < target; it++) {
+            if ((it & 15) == 0) {
+                if (ev) { ok = 0; break; }
+                ev = ld_volatile(err);
+                if (globaltimer() - t0 > MK_WAIT_NS || it > (1u << 24)) {
+                    mk_record(diag, 2, step, ph, (int)target, (int)ld_acquire(bar));
+                    atomicExch(err, 2);
+                    ok = 0;
+                    break;
+                }
             }
-            __nanosleep(20);
         }
-        if (ok && ld_volatile(err)) ok = 0;
+        if (ev) ok = 0;
         s_ok = ok;
     }
     BarP::sync();
