@@ -118,6 +118,11 @@ int xj_cuda_phase_trace(const xj_stage *s, double *out, int cap);
 // (core/xj_quant.h:55-122). Runs on the current device.
 int xj_cuda_dequant_rows(int type, const void *src, int k, int n_rows, float *out, char *err, size_t errlen);
 
+/* Tensor-core (tcgen05) self-test: d[128][64] = a[128][k] . b[64][k]^T with a, b fp16 (bit patterns) in
+ * host memory, k a positive multiple of 64, f32 accumulation in tensor memory. Checks the shared-memory
+ * descriptors, the MMA and the tensor-memory read-back used by the batched kernels. 0 or -1 + message. */
+int xj_cuda_tc_selftest(const uint16_t *a, const uint16_t *b, int k, float *d, char *err, size_t errlen);
+
 // Batch of n_seq independent sequences decoded in lockstep (no counterpart in the reference, which has
 // no multi-sequence API; additive). The batch owns a stage over all layers with the head (weights,
 // n_seq-row activation buffers) plus each sequence's KV caches, Gated-DeltaNet/conv states and

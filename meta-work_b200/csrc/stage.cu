@@ -22,6 +22,7 @@
 #include "kernels.cuh"
 #include "gemv_mma.cuh"
 #include "decode_mk.cuh"
+#include "tc_gemm.cuh"
 
 using namespace xjk;
 
@@ -1656,6 +1657,31 @@ int xj_cuda_dequant_rows(int type, const void *src, int k, int n_rows, float *ou
     cudaFree(d_src);
     cudaFree(d_out);
     if (e != cudaSuccess) { seterr(err, errlen, "CUDA error: %s", cudaGetErrorString(e)); return -1; }
+    return 0;
+}
+
+int xj_cuda_tc_selftest(const uint16_t *a, const uint16_t *b, int k, float *d, char *err, size_t errlen) {
+    if (k <= 0 || k % TCS_KC) { seterr(err, errlen, "K must be a positive multiple of %d", TCS_KC); return -1; }
+    __half *da = nullptr, *db = nullptr;
+    float *dd = nullptr;
+    int *derr = nullptr, herr = 0;
+    cudaError_t e = cudaMalloc(&da, sizeof(__half) * TCS_M * (size_t)k);
+    if (e == cudaSuccess) e = cudaMalloc(&db, sizeof(__half) * TCS_N * (size_t)k);
+    if (e == cudaSuccess) e = cudaMalloc(&dd, sizeof(float) * TCS_M * TCS_N);
+    if (e == cudaSuccess) e = cudaMalloc(&derr, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(derr, 0, sizeof(int));
+    if (e == cudaSuccess) e = cudaMemset(dd, 0, sizeof(float) * TCS_M * TCS_N);
+    if (e == cudaSuccess) e = cudaMemcpy(da, a, sizeof(__half) * TCS_M * (size_t)k, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) e = cudaMemcpy(db, b, sizeof(__half) * TCS_N * (size_t)k, cudaMemcpyHostToDevice);
+    if (e == cudaSuccess) {
+        k_tc_selftest<<<1, 128>>>(da, db, k, dd, derr);
+        e = cudaGetLastError();
+    }
+    if (e == cudaSuccess) e = cudaMemcpy(d, dd, sizeof(float) * TCS_M * TCS_N, cudaMemcpyDeviceToHost);
+    if (e == cudaSuccess) e = cudaMemcpy(&herr, derr, sizeof(int), cudaMemcpyDeviceToHost);
+    cudaFree(da); cudaFree(db); cudaFree(dd); cudaFree(derr);
+    if (e != cudaSuccess) { seterr(err, errlen, "CUDA error: %s", cudaGetErrorString(e)); return -1; }
+    if (herr) { seterr(err, errlen, "a bounded wait on the GPU gave up (tensor-core completion)"); return -1; }
     return 0;
 }
 

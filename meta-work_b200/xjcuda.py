@@ -97,6 +97,7 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_set_options": (ip, [ip, ip]),
         "xj_cuda_decode": (ip, [vp, vp, ip, ip, vp, vp, vp, cp, sz]),
         "xj_cuda_dequant_rows": (ip, [ip, vp, ip, ip, vp, cp, sz]),
+        "xj_cuda_tc_selftest": (ip, [vp, vp, ip, vp, cp, sz]),
         "xj_cuda_graph_kernels": (ip, [vp]),
         "xj_cuda_last_decode_launches": (ctypes.c_longlong, [vp, vp]),
         "xj_cuda_phase_trace": (ip, [vp, vp, ip]),
@@ -143,6 +144,18 @@ def dequant_rows(type_id: int, raw: bytes, k: int, n_rows: int) -> np.ndarray:
     if lib().xj_cuda_dequant_rows(type_id, src.ctypes.data, k, n_rows, out.ctypes.data, e, 512):
         _raise(e)
     return out
+
+
+def tc_selftest(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """d[128][64] = a[128][k] . b[64][k]^T on the tcgen05 tensor cores (a, b float16; xj_cuda_tc_selftest)."""
+    a = np.ascontiguousarray(a, np.float16)
+    b = np.ascontiguousarray(b, np.float16)
+    assert a.shape[0] == 128 and b.shape[0] == 64 and a.shape[1] == b.shape[1]
+    d = np.zeros((128, 64), np.float32)
+    e = _err()
+    if lib().xj_cuda_tc_selftest(a.ctypes.data, b.ctypes.data, a.shape[1], d.ctypes.data, e, 512):
+        _raise(e)
+    return d
 
 
 def gemv(type_id: int, raw: bytes, k: int, n: int, x: np.ndarray, path: int = 0) -> np.ndarray:
