@@ -52,8 +52,10 @@ uint64_t xjc_stage_state_bytes(const xj_model *m, int l0, int l1, int n_ctx, int
 //   XJC_OPT_TRACE    1 = the persistent kernel records when each CTA starts and ends each phase of
 //                    its last step (read with xj_cuda_phase_trace), 0 = off (default).
 //   XJC_OPT_GEMV_CTAS  CTAs per SM of the standalone tensor-core GEMV kernel: 2 (default) or 1.
+//   XJC_OPT_TC       1 = matrix products of 17..64 tokens (batched decode, prompt chunks) on the tcgen05
+//                    tensor cores (default), 0 = on the mma.sync 64-token kernel.
 enum { XJC_OPT_KV_F32 = 1, XJC_OPT_GEMV = 2, XJC_OPT_PDL = 3, XJC_OPT_PERSIST = 4, XJC_OPT_TRACE = 5,
-       XJC_OPT_GEMV_CTAS = 6 };
+       XJC_OPT_GEMV_CTAS = 6, XJC_OPT_TC = 7 };
 int xj_cuda_set_options(int which, int value);
 
 // Greedy decode on a stage covering [0, n_layer) with the head. Feeds n_prompt ids (prefill in

@@ -734,9 +734,23 @@ inline size_t b64_x_bytes(int T, int K) { return (size_t)(K / B64_CK) * b64_rec_
 // position (in halves) of element e (0..15) of a 16-element group in its 64-byte lane-quad layout
 __host__ __device__ inline int b64_pos(int e) { return ((e & 7) >> 1) * 8 + ((e & 1) + 2 * (e >> 3)) * 2; }
 
+// Layout of a tensor-core (tcgen05) launch's activations (k_gemm_tc, up to 64 tokens): K in chunks of
+// 128; chunk c is one 32 KB record of two planes (hi, then lo), each [64 tokens][128 halves] in the
+// core-matrix layout of a K-major MMA operand (8 x 8 blocks of 128 bytes, block (i, j) at byte
+// (i * 16 + j) * 128); the 64 range scales follow the last record.
+constexpr int TC_T = 64, TC_CK = 128;
+constexpr int TC_PLANE_X = TC_T * TC_CK * 2;
+constexpr int TC_REC = 2 * TC_PLANE_X;
+inline size_t tc_x_bytes(int K) { return (size_t)(K / TC_CK) * TC_REC + TC_T * 4 + 256; }
+__host__ __device__ inline uint32_t tc_xoff(int t, int k) {   // byte of (token t, element k) in a plane
+    return (uint32_t)((((t >> 3) * (TC_CK >> 3) + (k >> 3)) << 7) + ((t & 7) << 4) + ((k & 7) << 1));
+}
+enum { PREP_WIDE = 0, PREP_B64 = 1, PREP_TC = 2 };
+
 // Grid T, MMA_WARPS*32 threads: f(x[t]) -> range scale -> hi/lo columns + block sums of token t, in the
-// wide layout (B64 = false) or the 64-token chunk layout (B64 = true); the values are the same.
-template <bool B64>
+// wide layout (PREP_WIDE), the 64-token chunk layout (PREP_B64) or the tensor-core operand layout
+// (PREP_TC, no block sums); the values are the same.
+template <int L>
 static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_xt(const float *x, const float *x2, long long ldx, int K, int pro,
                                                                    const float *norm_w, float eps, void *buf, int T) {
     griddep_wait();
@@ -776,7 +790,8 @@ static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_xt(const float *
         const float m = tam * nsc;
         s_nsc = nsc;
         s_scale = ldexpf(1.0f, 14 - (m > 0.0f ? ilogbf(m) : 0));
-        if (B64) reinterpret_cast<float *>((uint8_t *)buf + (size_t)(K / B64_CK) * b64_rec_bytes(T))[t] = s_scale;
+        if (L == PREP_B64) reinterpret_cast<float *>((uint8_t *)buf + (size_t)(K / B64_CK) * b64_rec_bytes(T))[t] = s_scale;
+        else if (L == PREP_TC) reinterpret_cast<float *>((uint8_t *)buf + (size_t)(K / TC_CK) * TC_REC)[t] = s_scale;
         else W.scale[t] = s_scale;
     }
     __syncthreads();
@@ -789,8 +804,15 @@ static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_xt(const float *
             const float val = (pro == PRO_NORM ? (v[k] * nsc) * norm_w[i] : v[k]) * sc;
             const __half hi = __float2half_rn(val);
             const __half lo = __float2half_rn(val - __half2float(hi));
+            if (L == PREP_TC) {
+                uint8_t *rec = (uint8_t *)buf + (size_t)(i / TC_CK) * TC_REC;
+                const uint32_t o = tc_xoff(t, i & (TC_CK - 1));
+                *reinterpret_cast<__half *>(rec + o) = hi;
+                *reinterpret_cast<__half *>(rec + TC_PLANE_X + o) = lo;
+                continue;
+            }
             const float bs = warp_sum(__half2float(hi) + __half2float(lo));
-            if (B64) {
+            if (L == PREP_B64) {
                 const int ci = i & (B64_CK - 1);
                 uint8_t *rec = (uint8_t *)buf + (size_t)(i / B64_CK) * b64_rec_bytes(T);
                 __half *row = reinterpret_cast<__half *>(rec + (size_t)t * B64_XROW) + (ci & ~15) * 2 + b64_pos(ci & 15);
@@ -1041,7 +1063,7 @@ struct B64Args {
     int njob, T, K;
     int nsplit;            // CTAs per block (= cluster size), each a contiguous range of K chunks
     int blk_start[5];      // prefix sums of 256-row blocks over jobs
-    const void *xbuf;      // activations in the 64-token chunk layout (k_prep_xt<true>)
+    const void *xbuf;      // activations in the 64-token chunk layout (k_prep_xt<PREP_B64>)
     int *err;
 };
 
@@ -1539,7 +1561,7 @@ inline cudaError_t launch_wide_t(MmaArgs a, const void *xbuf, cudaStream_t st) {
     const dim3 grid((tiles + a.tiles_per_cta - 1) / a.tiles_per_cta), block(MMA_WARPS * 32);
     return launch_pdl(k_gemv_wide<TYPE>, grid, block, smem, st, a, xbuf);
 }
-// 64-token launch on activations prepared by k_prep_xt<true> into a.xbuf. Blocks of 256 rows; when
+// 64-token launch on activations prepared by k_prep_xt<PREP_B64> into a.xbuf. Blocks of 256 rows; when
 // there are fewer blocks than SMs, each block's K chunks are split over a cluster of ns <= B64_MAXSPLIT
 // CTAs, ns chosen (per device, type and block count) to minimise waves x chunks per CTA with the
 // number of clusters that fit the GPU at once.

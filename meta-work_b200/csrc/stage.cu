@@ -32,6 +32,7 @@ int g_opt_kv_f32 = 0;
 int g_opt_gemv = 0;
 int g_opt_persist = 1;
 int g_opt_trace = 0;
+int g_opt_tc = 1;
 
 void seterr(char *err, size_t errlen, const char *fmt, ...) {
     if (!err || !errlen) return;
@@ -73,8 +74,9 @@ struct Impl {
     float *x = nullptr, *xin = nullptr, *h = nullptr, *qkvb = nullptr, *z = nullptr, *beta = nullptr, *alpha = nullptr;
     float *o = nullptr, *qrot = nullptr, *g = nullptr, *u = nullptr, *logits = nullptr;
     float *q = nullptr, *k = nullptr, *v = nullptr, *hn = nullptr;
-    void *wide_buf = nullptr;   // activations of a wide (5..16-token) GEMV launch, prepared by k_prep_xt<false>
+    void *wide_buf = nullptr;   // activations of a wide (5..16-token) GEMV launch, prepared by k_prep_xt<PREP_WIDE>
     void *b64_buf = nullptr;    // activations of a 64-token GEMV launch (stages taking more than 16 tokens)
+    void *tc_buf = nullptr;     // the same in the tensor-core operand layout (k_gemm_tc)
     // chunked GDN (prompt forwards of >= GC_MIN_T tokens): normalised q, k and the chunk products
     float *gc_qn = nullptr, *gc_kn = nullptr, *gc_kk = nullptr, *gc_qk = nullptr;
     float *pbest = nullptr, *psecond = nullptr;
@@ -207,7 +209,8 @@ void launch(Impl *im, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
 
 // Activations of the 64-token GEMV: 64 tokens at the longest K.
 int alloc_b64(Impl *im, char *err, size_t errlen) {
-    return dalloc(im, (uint8_t **)&im->b64_buf, b64_x_bytes(B64_T, MMA_KMAX), err, errlen);
+    return dalloc(im, (uint8_t **)&im->b64_buf, b64_x_bytes(B64_T, MMA_KMAX), err, errlen) ||
+           dalloc(im, (uint8_t **)&im->tc_buf, tc_x_bytes(MMA_KMAX), err, errlen);
 }
 
 void rmsnorm(Impl *im, const float *x, long long ldx, const float *w, float *y, long long ldy, int n, int rows, float eps) {
@@ -256,10 +259,34 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
     bool use64 = T > MMA_WIDE_T && im->b64_buf && !groups.empty();
     for (const MmaArgs &m : groups)
         for (int j = 0; j < m.njob; j++) use64 = use64 && b64_ok(m.job[j], K);
-    if (use64) {
+    bool usetc = use64 && g_opt_tc && im->tc_buf;
+    for (const MmaArgs &m : groups)
+        for (int j = 0; j < m.njob; j++) usetc = usetc && tc_ok(m.job[j], K);
+    if (usetc) {
+        // tcgen05 tensor cores: weights decoded to fp16 pairs in shared memory, accumulators in TMEM
+        for (int t0 = 0; t0 < T; t0 += TC_T) {
+            const int Tc = T - t0 < TC_T ? T - t0 : TC_T;
+            launch(im, k_prep_xt<PREP_TC>, dim3(Tc), dim3(MMA_WARPS * 32), 0, (const float *)(x + t0 * ldx),
+                   (const float *)(x2 ? x2 + t0 * ldx : nullptr), ldx, K, pro, norm_w, eps, im->tc_buf, Tc);
+            for (size_t gi = 0; gi < groups.size(); gi++) {
+                const MmaArgs &m = groups[gi];
+                B64Args b{};
+                b.njob = m.njob; b.T = Tc; b.K = K;
+                b.xbuf = im->tc_buf; b.err = im->derr;
+                for (int j = 0; j < m.njob; j++) {
+                    b.job[j] = m.job[j];
+                    if (b.job[j].y) b.job[j].y = m.job[j].y + t0 * m.job[j].ldy;
+                    if (b.job[j].conv_bstride) b.job[j].conv_state = m.job[j].conv_state + t0 * m.job[j].conv_bstride;
+                }
+                launch_tc(b, gtype[gi], im->st);
+                im->nlaunch++;
+            }
+        }
+        groups.clear();
+    } else if (use64) {
         for (int t0 = 0; t0 < T; t0 += B64_T) {
             const int Tc = T - t0 < B64_T ? T - t0 : B64_T;
-            launch(im, k_prep_xt<true>, dim3(Tc), dim3(MMA_WARPS * 32), 0, (const float *)(x + t0 * ldx),
+            launch(im, k_prep_xt<PREP_B64>, dim3(Tc), dim3(MMA_WARPS * 32), 0, (const float *)(x + t0 * ldx),
                    (const float *)(x2 ? x2 + t0 * ldx : nullptr), ldx, K, pro, norm_w, eps, im->b64_buf, Tc);
             for (size_t gi = 0; gi < groups.size(); gi++) {
                 const MmaArgs &m = groups[gi];
@@ -285,7 +312,7 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
         const int Tc = T - t0 < tch ? T - t0 : tch;
         const bool wide = Tc > MMA_MAXT;
         if (wide && !groups.empty()) {
-            launch(im, k_prep_xt<false>, dim3(Tc), dim3(MMA_WARPS * 32), 0, (const float *)(x + t0 * ldx),
+            launch(im, k_prep_xt<PREP_WIDE>, dim3(Tc), dim3(MMA_WARPS * 32), 0, (const float *)(x + t0 * ldx),
                    (const float *)(x2 ? x2 + t0 * ldx : nullptr), ldx, K, pro, norm_w, eps, im->wide_buf, Tc);
         }
         for (size_t gi = 0; gi < groups.size(); gi++) {
@@ -1072,6 +1099,7 @@ int xj_cuda_set_options(int which, int value) {
     case XJC_OPT_PDL: g_pdl = value ? 1 : 0; return 0;
     case XJC_OPT_PERSIST: g_opt_persist = value; return 0;
     case XJC_OPT_TRACE: g_opt_trace = value; return 0;
+    case XJC_OPT_TC: g_opt_tc = value ? 1 : 0; return 0;
     case XJC_OPT_GEMV_CTAS: if (value < 1 || value > 2) return -1; g_mma_ctas_per_sm = value; return 0;
     default: return -1;
     }

@@ -124,4 +124,429 @@ __global__ void __launch_bounds__(128, 1) k_tc_selftest(const __half *A, const _
     if (warp == 0) tc_dealloc(tmem, 64);
 }
 
+// ------------------------------------------------------------------ quantised GEMM, 17..64 tokens
+// y[t][r] (epilogue)= sum_k W[r][k] x[t][k] for up to 64 tokens on the tcgen05 tensor cores. A CTA owns
+// 128 rows (8 tiles of the tiled weight layout) and a contiguous range of 128-wide K chunks; when a
+// matrix has fewer 128-row blocks than SMs, a block's chunks are split over a thread-block cluster
+// exactly as in k_gemv_b64 (partials exchanged through distributed shared memory, summed by the owner
+// in rank order, so the result does not depend on timing).
+//
+// Per chunk a producer warp bulk-copies the 8 tiles' quantised bytes and the activation record (two
+// fp16 planes hi / lo, k_prep_xt<PREP_TC>) into a stage. The 8 compute warps (one tile each) decode
+// the weights of one 64-wide half chunk into fp16 planes Wh / Wl (Wh = w rounded, Wl = w - Wh
+// rounded; w is the reference's dequantised float, core/xj_quant.h:55-122) in the MMA's core-matrix
+// layout, and thread 0 issues, per 16-wide k-step, D += Wh.Xh + Wh.Xl + Wl.Xh (kind::f16, f32
+// accumulator [128 rows][64 tokens] in tensor memory), then commits to an mbarrier that frees the half
+// chunk's weight planes (double-buffered) and, after the second half, the stage. The products that
+// remain dropped (Wl.Xl) are below 2^-22 relative, so the result is fp32-level like the mma.sync path.
+constexpr int TC_SUB = 64;                          // K of one dequantised weight buffer
+constexpr int TC_ROWS = 128, TC_TILES = 8, TC_WARPS = 8;
+constexpr int TC_THREADS = TC_WARPS * 32 + 32;      // + the producer warp
+constexpr int TC_PLANE_A = TC_ROWS * TC_SUB * 2;    // one weight plane of a half chunk: 16 KB
+constexpr int TC_ABUF = 2 * TC_PLANE_A;             // Wh + Wl
+constexpr int TC_STAGES = 2;
+constexpr int TC_MAXSPLIT = 16;
+constexpr int TC_RS = TC_T + 4;                     // row stride (floats) of the partial sums
+constexpr size_t TC_RECV = (size_t)(TC_ROWS + TC_MAXSPLIT) * TC_RS * 4;
+template <int TYPE> constexpr int tc_stage() { return TC_REC + TC_TILES * b64_wbytes<TYPE>(); }
+template <int TYPE> constexpr size_t tc_smem() { return (size_t)TC_STAGES * tc_stage<TYPE>() + 2 * TC_ABUF + TC_RECV; }
+static_assert(tc_smem<XJ_Q8_0>() <= 227 * 1024, "fits one SM");
+static_assert(tc_stage<XJ_Q4_K>() % 128 == 0 && tc_stage<XJ_Q6_K>() % 128 == 0 && tc_stage<XJ_Q8_0>() % 128 == 0, "aligned stages");
+static_assert(TC_ROWS * TC_RS * 4 <= TC_STAGES * tc_stage<XJ_Q4_K>(), "partials fit the stage area");
+using BarTc = BarNamed<1, TC_WARPS * 32>;
+
+// Byte of (row r, element k) in a weight plane ([128 rows][64 halves], core-matrix layout).
+XJ_DEV uint32_t tc_aoff(int r, int k) { return (uint32_t)((((r >> 3) * (TC_SUB >> 3) + (k >> 3)) << 7) + ((r & 7) << 4) + ((k & 7) << 1)); }
+
+// Stores w0, w1 (elements k, k+1 of row r) as Wh / Wl pairs.
+XJ_DEV void tc_put2(uint8_t *ab, int r, int k, float w0, float w1) {
+    const __half2 h = __floats2half2_rn(w0, w1);
+    const float2 hf = __half22float2(h);
+    const __half2 l = __floats2half2_rn(w0 - hf.x, w1 - hf.y);
+    const uint32_t o = tc_aoff(r, k);
+    *reinterpret_cast<__half2 *>(ab + o) = h;
+    *reinterpret_cast<__half2 *>(ab + TC_PLANE_A + o) = l;
+}
+
+// Warp `tl` decodes its tile's 16 rows x 64 elements (half `h` of the staged 128-wide chunk; `hh`: which
+// half of the K-quant super-block the chunk is) into the weight planes at ab. Lane (g, c) holds, per
+// k-step, the codes of rows g, g+8 and elements 2c, 2c+1, 2c+8, 2c+9 (the mma.sync A-fragment order of
+// the tiled layout); each pair of consecutive elements becomes one Wh and one Wl store.
+template <int TYPE>
+XJ_DEV void tc_dequant(const uint8_t *wst, int tl, int lane, int hh, int h, uint8_t *ab) {
+    using BG = B64Geo<TYPE>;
+    const int g = lane >> 2, c = lane & 3, r0 = tl * 16 + g;
+    if constexpr (TYPE == XJ_Q4_K || TYPE == XJ_Q6_K) {
+        const uint4 q = *reinterpret_cast<const uint4 *>(wst + (h * 32 + lane) * 16);   // k-steps 4h .. 4h+3
+        float sa[2][4], sb[2][4];   // per row (g, g+8): Q4_K (d1, m1) of the two sub-blocks; Q6_K d*sc per k-step
+        uint2 hq = make_uint2(0u, 0u);
+#pragma unroll
+        for (int rr = 0; rr < 2; rr++) {
+            const int row = g + 8 * rr;
+            if constexpr (TYPE == XJ_Q4_K) {
+                const uint8_t *hdr = wst + BG::Q + row * 16;
+                const float d = h2f(ld_u16(hdr)), dmin = h2f(ld_u16(hdr + 2));
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    int s_, m_;
+                    k4_scale_min(4 * hh + 2 * h + e, hdr + 4, s_, m_);
+                    sa[rr][e] = __fmul_rn(d, (float)s_);
+                    sb[rr][e] = __fmul_rn(dmin, (float)m_);
+                }
+            } else {
+                const float d = h2f(ld_u16(wst + BG::Q + BG::H + BG::S + row * 2));
+                const int8_t *sc = reinterpret_cast<const int8_t *>(wst + BG::Q + BG::H + row * 16);
+#pragma unroll
+                for (int kk = 0; kk < 4; kk++) sa[rr][kk] = __fmul_rn(d, (float)sc[8 * hh + 4 * h + kk]);
+            }
+        }
+        if constexpr (TYPE == XJ_Q6_K) hq = *reinterpret_cast<const uint2 *>(wst + BG::Q + lane * 16 + 8 * h);
+#pragma unroll
+        for (int kk = 0; kk < 4; kk++) {
+            const uint32_t w = word_of(q, kk);
+            uint32_t hw = 0;
+            if constexpr (TYPE == XJ_Q6_K) hw = ((kk >> 1) ? hq.y : hq.x) >> ((kk & 1) * 8);
+#pragma unroll
+            for (int r = 0; r < 4; r++) {
+                const int rr = r & 1, k = 16 * kk + 2 * c + 8 * (r >> 1);
+                float v[2];
+#pragma unroll
+                for (int e = 0; e < 2; e++) {
+                    const int code = (int)((w >> (4 * r + 16 * e)) & 0xF);
+                    if constexpr (TYPE == XJ_Q4_K) {
+                        v[e] = __fsub_rn(__fmul_rn(sa[rr][kk >> 1], (float)code), sb[rr][kk >> 1]);
+                    } else {
+                        const int q6 = (code | (int)(((hw >> (2 * r + 16 * e)) & 3) << 4)) - 32;
+                        v[e] = __fmul_rn(sa[rr][kk], (float)q6);
+                    }
+                }
+                tc_put2(ab, r0 + 8 * rr, k, v[0], v[1]);
+            }
+        }
+    } else {   // Q8_0: units 2h, 2h+1 of the chunk, two k-steps each
+#pragma unroll
+        for (int uu = 0; uu < 2; uu++) {
+            const int u = 2 * h + uu;
+            const uint4 q = *reinterpret_cast<const uint4 *>(wst + (u * 32 + lane) * 16);
+            float dq[2];
+#pragma unroll
+            for (int rr = 0; rr < 2; rr++) dq[rr] = h2f(ld_u16(wst + BG::Q + (u * 16 + g + 8 * rr) * 2));
+#pragma unroll
+            for (int ss = 0; ss < 2; ss++)
+#pragma unroll
+                for (int hw = 0; hw < 2; hw++) {
+                    const uint32_t w = word_of(q, 2 * ss + hw);
+#pragma unroll
+                    for (int rp = 0; rp < 2; rp++) {         // bytes 2rp, 2rp+1: r = 2hw + rp, e = 0, 1
+                        const int r = 2 * hw + rp, rr = r & 1, k = 32 * uu + 16 * ss + 2 * c + 8 * (r >> 1);
+                        const float v0 = __fmul_rn(dq[rr], (float)(int8_t)(w >> (16 * rp)));
+                        const float v1 = __fmul_rn(dq[rr], (float)(int8_t)(w >> (16 * rp + 8)));
+                        tc_put2(ab, tl * 16 + g + 8 * rr, k, v0, v1);
+                    }
+                }
+        }
+    }
+}
+
+// Bounded mbarrier wait: gives up (setting *err) after about a second, or at once when *err is set
+// (read every 64 polls, one load in flight), so an error anywhere ends every wait of the grid quickly.
+XJ_DEV bool tc_wait(uint64_t *bar, uint32_t parity, int *err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    unsigned long long t0;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
+    int ev = *(volatile int *)err;
+    for (int it = 1; it < (1 << 26); it++) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if ((it & 63) == 0) {
+            if (ev) return false;
+            ev = *(volatile int *)err;
+            unsigned long long t;
+            asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+            if (t - t0 > 1000000000ull) break;
+        }
+    }
+    atomicExch(err, 1);
+    return false;
+}
+
+template <int TYPE>
+__global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
+    constexpr int WB = b64_wbytes<TYPE>(), SBY = tc_stage<TYPE>();
+    constexpr bool KQ = TYPE != XJ_Q8_0;
+    constexpr uint32_t IDESC = tc_idesc_f16(TC_ROWS, TC_T);
+    extern __shared__ __align__(1024) uint8_t smem[];
+    uint8_t *abuf = smem + (size_t)TC_STAGES * SBY;
+    float *recv = reinterpret_cast<float *>(abuf + 2 * TC_ABUF);   // [ns][ceil(128/ns)][TC_RS] partials of this CTA's rows
+    __shared__ __align__(8) uint64_t full[TC_STAGES], mdone[2], rbar;
+    __shared__ uint32_t s_tmem;
+    __shared__ float tok_inv[TC_T];                    // 1 / range scale (a power of two: exact)
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int T = a.T, K = a.K, ns = a.nsplit;
+    const int blk = blockIdx.x / ns;
+    const int split = ns > 1 ? (int)cluster_rank() : 0;
+    int j = 0;
+    while (blk >= a.blk_start[j + 1]) j++;
+    const MmaJob &jb = a.job[j];
+    const Tiled &W = jb.w;
+    const int ntiles = (W.N + 15) / 16;
+    const int t0 = (blk - a.blk_start[j]) * TC_TILES;
+    const int nt = ntiles - t0 < TC_TILES ? ntiles - t0 : TC_TILES;
+    const int nch = K / TC_CK;
+    const int c0 = (int)((long long)split * nch / ns), c1 = (int)((long long)(split + 1) * nch / ns);
+    const int nc = c1 - c0;
+    const int nrmax = (TC_ROWS + ns - 1) / ns;
+    const int rb = split * TC_ROWS / ns, nr = (split + 1) * TC_ROWS / ns - rb;   // the rows this CTA finishes
+    auto issue_w = [&](int i) {       // producer warp: weights of chunk c0 + i, one tile per lane
+        const int ch = c0 + i;
+        uint8_t *st = smem + (size_t)(i % TC_STAGES) * SBY + TC_REC;
+        uint64_t *bar = &full[i % TC_STAGES];
+        if (lane == 0) mbar_expect_tx(bar, (uint32_t)(TC_REC + nt * WB));
+        __syncwarp();
+        if (lane < nt) {
+            uint8_t *dst = st + lane * WB;
+            const size_t tile = (size_t)(t0 + lane);
+            if (KQ) {
+                constexpr int QB = Geo<TYPE>::QB, HB = Geo<TYPE>::HB, SB = Geo<TYPE>::SB, DB = Geo<TYPE>::DB;
+                const size_t tu = tile * W.nu + (ch >> 1);
+                const int hh = ch & 1;
+                bulk_g2s(dst, W.q + tu * QB + hh * (QB / 2), QB / 2, bar);
+                if (HB) bulk_g2s(dst + B64Geo<TYPE>::Q, W.h + tu * HB + hh * (HB / 2), HB / 2, bar);
+                bulk_g2s(dst + B64Geo<TYPE>::Q + B64Geo<TYPE>::H, W.s + tu * SB, SB, bar);
+                if (DB) bulk_g2s(dst + B64Geo<TYPE>::Q + B64Geo<TYPE>::H + B64Geo<TYPE>::S, W.d + tu * DB, DB, bar);
+            } else {
+                const size_t tu = tile * W.nu + (size_t)ch * 4;
+                bulk_g2s(dst, W.q + tu * Geo<TYPE>::QB, 4 * Geo<TYPE>::QB, bar);
+                bulk_g2s(dst + B64Geo<TYPE>::Q, W.d + tu * Geo<TYPE>::DB, 4 * Geo<TYPE>::DB, bar);
+            }
+        }
+    };
+    auto issue_x = [&](int i) {       // activation record of chunk c0 + i (after the predecessor finished)
+        bulk_g2s(smem + (size_t)(i % TC_STAGES) * SBY, (const uint8_t *)a.xbuf + (size_t)(c0 + i) * TC_REC, TC_REC,
+                 &full[i % TC_STAGES]);
+    };
+    if (tid == 0) {
+        for (int q = 0; q < TC_STAGES; q++) mbar_init(&full[q], 1);
+        mbar_init(&mdone[0], 1);
+        mbar_init(&mdone[1], 1);
+        mbar_init(&rbar, 1);
+        asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+        if (ns > 1) mbar_expect_tx(&rbar, (uint32_t)((ns - 1) * nr * TC_RS * 4));
+    }
+    if (warp == 0) tc_alloc(&s_tmem, TC_T);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = s_tmem;
+    if (ns > 1) cluster_arrive();                          // every CTA's receive barrier is armed before any send
+    bool ok = true;
+    if (warp == TC_WARPS) {
+        // ---- producer: weights do not depend on the predecessor kernel, the activations do
+        for (int i = 0; i < TC_STAGES && i < nc; i++) issue_w(i);
+        griddep_launch();
+        griddep_wait();
+        if (lane == 0)
+            for (int i = 0; i < TC_STAGES && i < nc; i++) issue_x(i);
+        for (int i = TC_STAGES; i < nc && ok; i++) {
+            // stage i % 2 is free once the MMAs of chunk i - 2 (its second half: sub-chunk 2i - 3) are done
+            if (lane == 0) ok = tc_wait(&mdone[1], (uint32_t)((i - 2) & 1), a.err);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            issue_w(i);
+            if (lane == 0) issue_x(i);
+        }
+    } else {
+        griddep_launch();
+        griddep_wait();
+        // every compute thread runs all iterations and meets every named barrier (a failed wait only
+        // skips work), so no thread can be left waiting at a barrier
+        for (int i = 0; i < nc; i++) {
+            const int s = i % TC_STAGES;
+            uint8_t *st = smem + (size_t)s * SBY;
+            if (ok) ok = tc_wait(&full[s], (uint32_t)((i / TC_STAGES) & 1), a.err);
+            const int hh = (c0 + i) & 1;
+            for (int h = 0; h < 2; h++) {
+                const int q = 2 * i + h, ab = q & 1;
+                if (q >= 2 && ok) ok = tc_wait(&mdone[ab], (uint32_t)(((q - 2) >> 1) & 1), a.err);   // buffer ab is free
+                uint8_t *abp = abuf + (size_t)ab * TC_ABUF;
+                if (ok && warp < nt) tc_dequant<TYPE>(st + TC_REC + warp * WB, warp, lane, hh, h, abp);
+                fence_async_smem();
+                BarTc::sync();
+                if (tid == 0 && ok) {
+                    tc_fence_after();
+#pragma unroll
+                    for (int kk = 0; kk < TC_SUB / 16; kk++) {
+                        const uint32_t ao = smem_u32(abp) + kk * 256, bo = smem_u32(st) + (8 * h + 2 * kk) * 128;
+                        const uint64_t ah = tc_desc(ao, 128, (TC_SUB / 8) * 128), al = tc_desc(ao + TC_PLANE_A, 128, (TC_SUB / 8) * 128);
+                        const uint64_t bh = tc_desc(bo, 128, (TC_CK / 8) * 128), bl = tc_desc(bo + TC_PLANE_X, 128, (TC_CK / 8) * 128);
+                        tc_mma_f16(tmem, ah, bh, IDESC, (i > 0 || h > 0 || kk > 0) ? 1u : 0u);
+                        tc_mma_f16(tmem, ah, bl, IDESC, 1u);
+                        tc_mma_f16(tmem, al, bh, IDESC, 1u);
+                    }
+                    tc_commit(&mdone[ab]);
+                }
+            }
+        }
+        // the last MMAs (sub-chunk 2nc - 1, buffer 1) are done: the accumulator is final
+        if (ok) ok = tc_wait(&mdone[1], (uint32_t)((nc - 1) & 1), a.err);
+    }
+    if (tid < T) tok_inv[tid] = 1.0f / reinterpret_cast<const float *>((const uint8_t *)a.xbuf + (size_t)nch * TC_REC)[tid];
+    const bool allok = __syncthreads_and(ok) != 0;
+    tc_fence_after();
+    // ---- accumulator (row = TMEM lane, token = column) -> partials [row][TC_RS] in the stage area
+    float *part = reinterpret_cast<float *>(smem);
+    if (warp < TC_WARPS && allok) {
+        const int quarter = warp & 3, row = 32 * quarter + lane;
+#pragma unroll
+        for (int cc = 0; cc < 2; cc++) {
+            const int col = 32 * (warp >> 2) + 16 * cc;
+            float v[16];
+            tc_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)col, v);
+#pragma unroll
+            for (int e = 0; e < 16; e += 4)
+                *reinterpret_cast<float4 *>(part + (size_t)row * TC_RS + col + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
+        }
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) tc_dealloc(tmem, TC_T);
+    if (ns > 1) {
+        // each owner's rows to slot `split` of its receive buffer, one bulk copy per owner
+        cluster_wait();                                    // the owners' receive barriers are armed
+        if (tid < ns && tid != split) {
+            const int o = tid, orb = o * TC_ROWS / ns, onr = (o + 1) * TC_ROWS / ns - orb;
+            fence_async_smem();
+            bulk_s2peer(peer_addr(recv + (size_t)split * nrmax * TC_RS, (uint32_t)o), part + (size_t)orb * TC_RS,
+                        (uint32_t)(onr * TC_RS * 4), peer_addr(&rbar, (uint32_t)o));
+            asm volatile("cp.async.bulk.commit_group;" ::: "memory");
+            asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");   // the source may be reused / freed
+        }
+        tc_wait(&rbar, 0u, a.err);                         // every other split's partials of this CTA's rows
+    }
+    // ---- rows [rb, rb + nr): sum over splits in rank order, epilogue (k_gemv_b64's)
+    const int epi = jb.epi, ldy = (int)jb.ldy, kc = jb.kc;
+    float *yb = jb.y;
+    const int tstep = TC_THREADS / nr, rl = tid % nr, tt = tid / nr;
+    const int row = rb + rl, ch = t0 * 16 + row;
+    if (allok && tt < tstep && ch < W.N) {
+        const float *own = part + (size_t)row * TC_RS;
+        const float *rcv = recv + (size_t)rl * TC_RS;
+        auto total = [&](int t) {
+            float sv = 0.0f;
+#pragma unroll
+            for (int r = 0; r < TC_MAXSPLIT; r++)
+                if (r < ns) sv += r == split ? own[t] : rcv[(size_t)r * nrmax * TC_RS + t];
+            return sv * tok_inv[t];
+        };
+        if (epi == EPI_CONV) {
+            float wc[9], wl = 0.0f;
+#pragma unroll
+            for (int k = 0; k < 9; k++) wc[k] = k < kc ? jb.conv_w[(size_t)ch * kc + k] : 0.0f;
+#pragma unroll
+            for (int k = 0; k < 9; k++)
+                if (k == kc - 1) wl = wc[k];
+            for (int t = tt; t < T; t += tstep) {
+                float *stt = jb.conv_state + t * jb.conv_bstride + (size_t)ch * (kc - 1);
+                float cs[8];
+#pragma unroll
+                for (int k = 0; k < 8; k++) cs[k] = k < kc - 1 ? stt[k] : 0.0f;
+                const float v = total(t);
+                float acc = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 8; k++)
+                    if (k < kc - 1) acc = fmaf(cs[k], wc[k], acc);
+                acc = fmaf(v, wl, acc);
+#pragma unroll
+                for (int k = 0; k < 7; k++)
+                    if (k < kc - 2) stt[k] = cs[k + 1];
+                stt[kc - 2] = v;
+                yb[(size_t)t * ldy + ch] = silu_f(acc);
+            }
+        } else if (epi == EPI_ADD) {
+            for (int t = tt; t < T; t += tstep) yb[(size_t)t * ldy + ch] += total(t);
+        } else {
+            for (int t = tt; t < T; t += tstep) yb[(size_t)t * ldy + ch] = total(t);
+        }
+    }
+}
+
+// Launch on activations prepared by k_prep_xt<PREP_TC> into a.xbuf: blocks of 128 rows, each block's K
+// chunks split over a cluster of ns CTAs when that lowers (waves x chunks per CTA).
+template <int TYPE>
+inline cudaError_t launch_tc_t(B64Args a, cudaStream_t st) {
+    constexpr int MAXDEV = 64;
+    static int sms_dev[MAXDEV] = {0};
+    static int occ[MAXDEV][TC_MAXSPLIT + 1] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (dev < 0 || dev >= MAXDEV) dev = 0;
+    constexpr size_t smem = tc_smem<TYPE>();
+    if (!sms_dev[dev]) {
+        cudaFuncSetAttribute(k_gemm_tc<TYPE>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        cudaFuncSetAttribute(k_gemm_tc<TYPE>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        cudaDeviceGetAttribute(&sms_dev[dev], cudaDevAttrMultiProcessorCount, dev);
+        occ[dev][1] = sms_dev[dev];
+        for (int ns = 2; ns <= TC_MAXSPLIT; ns++) {
+            cudaLaunchConfig_t q{};
+            q.gridDim = dim3(ns * 64);
+            q.blockDim = dim3(TC_THREADS);
+            q.dynamicSmemBytes = smem;
+            cudaLaunchAttribute ca[1];
+            ca[0].id = cudaLaunchAttributeClusterDimension;
+            ca[0].val.clusterDim.x = (unsigned)ns;
+            ca[0].val.clusterDim.y = 1;
+            ca[0].val.clusterDim.z = 1;
+            q.attrs = ca;
+            q.numAttrs = 1;
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, k_gemm_tc<TYPE>, &q) != cudaSuccess) { cudaGetLastError(); n = 0; }
+            occ[dev][ns] = n;
+        }
+    }
+    a.blk_start[0] = 0;
+    for (int j = 0; j < a.njob; j++) a.blk_start[j + 1] = a.blk_start[j] + ((a.job[j].w.N + 15) / 16 + TC_TILES - 1) / TC_TILES;
+    const int nblk = a.blk_start[a.njob], nch = a.K / TC_CK;
+    constexpr int FIXED = 2;
+    int best = 1;
+    long long best_cost = (long long)((nblk + occ[dev][1] - 1) / occ[dev][1]) * (nch + FIXED);
+    for (int ns = 2; ns <= TC_MAXSPLIT && ns <= nch; ns++) {
+        if (occ[dev][ns] < 1) continue;
+        const long long cost = (long long)((nblk + occ[dev][ns] - 1) / occ[dev][ns]) * ((nch + ns - 1) / ns + FIXED);
+        if (cost < best_cost) { best_cost = cost; best = ns; }
+    }
+    const int ns = best;
+    a.nsplit = ns;
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3(nblk * ns);
+    cfg.blockDim = dim3(TC_THREADS);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute at[2];
+    int na = 0;
+    if (g_pdl) {
+        at[na].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+        at[na].val.programmaticStreamSerializationAllowed = 1;
+        na++;
+    }
+    if (ns > 1) {
+        at[na].id = cudaLaunchAttributeClusterDimension;
+        at[na].val.clusterDim.x = (unsigned)ns;
+        at[na].val.clusterDim.y = 1;
+        at[na].val.clusterDim.z = 1;
+        na++;
+    }
+    cfg.attrs = at;
+    cfg.numAttrs = na;
+    return cudaLaunchKernelEx(&cfg, k_gemm_tc<TYPE>, a);
+}
+inline cudaError_t launch_tc(const B64Args &a, int type, cudaStream_t st) {
+    switch (type) {
+    case XJ_Q4_K: return launch_tc_t<XJ_Q4_K>(a, st);
+    case XJ_Q6_K: return launch_tc_t<XJ_Q6_K>(a, st);
+    case XJ_Q8_0: return launch_tc_t<XJ_Q8_0>(a, st);
+    default: return cudaErrorInvalidValue;
+    }
+}
+// Matrices the tensor-core kernel takes: those of the 64-token kernel (b64_ok).
+inline bool tc_ok(const MmaJob &j, int K) { return b64_ok(j, K) && K % TC_CK == 0; }
+
 }  // namespace xjk

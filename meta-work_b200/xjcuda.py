@@ -19,7 +19,7 @@ LIB = HERE / "csrc" / "libxj_cuda.so"
 _lib = None
 
 F32, F16, Q8_0, Q4_K, Q5_K, Q6_K, BF16 = 0, 1, 8, 12, 13, 14, 30
-OPT_KV_F32, OPT_GEMV, OPT_PDL, OPT_PERSIST, OPT_TRACE, OPT_GEMV_CTAS = 1, 2, 3, 4, 5, 6
+OPT_KV_F32, OPT_GEMV, OPT_PDL, OPT_PERSIST, OPT_TRACE, OPT_GEMV_CTAS, OPT_TC = 1, 2, 3, 4, 5, 6, 7
 
 
 class XjError(RuntimeError):

@@ -79,41 +79,57 @@ def test_wide_dynamic_range(t):
 
 @pytest.mark.parametrize("t", [xo.Q4_K, xo.Q6_K, xo.Q8_0])
 @pytest.mark.parametrize("k,n", [(256, 16), (512, 48), (2048, 2048), (6144, 2048), (2048, 6160)])
-def test_gemv64_matches_float64(t, k, n):
-    """17..64 tokens: the 64-token kernel (weights once per launch, K split over CTAs when the matrix
-    has fewer 256-row blocks than SMs, partial sums added in split order)."""
+@pytest.mark.parametrize("tc", [1, 0])
+def test_gemv64_matches_float64(t, k, n, tc):
+    """17..64 tokens: the tcgen05 kernel (tc = 1: weights decoded to fp16 hi/lo pairs, f32 accumulator
+    in tensor memory) and the mma.sync 64-token kernel (tc = 0); weights once per launch, K split over
+    a cluster when the matrix has fewer row blocks than SMs, partial sums added in split order."""
     from xjb200 import xjcuda
     raw = _w(t, k, n, k * 5 + n + t)
     rng = np.random.default_rng(4)
-    for T in (17, 40, 64):
-        x = rng.standard_normal((T, k)).astype(np.float32)
-        want = _ref(t, raw, k, n, x)
-        y = xjcuda.gemv(t, raw, k, n, x)
-        err = np.abs(y - want).max() / np.abs(want).max()
-        assert err < 1e-5, (t, k, n, T, err)
+    xjcuda.set_option(xjcuda.OPT_TC, tc)
+    try:
+        for T in (17, 40, 64):
+            x = rng.standard_normal((T, k)).astype(np.float32)
+            want = _ref(t, raw, k, n, x)
+            y = xjcuda.gemv(t, raw, k, n, x)
+            err = np.abs(y - want).max() / np.abs(want).max()
+            assert err < 1e-5, (t, k, n, T, tc, err)
+    finally:
+        xjcuda.set_option(xjcuda.OPT_TC, 1)
 
 
-def test_gemv64_unsplit_many_blocks():
-    """More 256-row blocks than SMs: one CTA per block over the whole K (the LM-head case)."""
+@pytest.mark.parametrize("tc", [1, 0])
+def test_gemv64_unsplit_many_blocks(tc):
+    """More row blocks than SMs: one CTA per block over the whole K (the LM-head case)."""
     from xjb200 import xjcuda
     k, n = 256, 38400
     raw = _w(xo.Q4_K, k, n, 21)
     x = np.random.default_rng(5).standard_normal((33, k)).astype(np.float32)
     want = _ref(xo.Q4_K, raw, k, n, x)
-    y = xjcuda.gemv(xo.Q4_K, raw, k, n, x)
+    xjcuda.set_option(xjcuda.OPT_TC, tc)
+    try:
+        y = xjcuda.gemv(xo.Q4_K, raw, k, n, x)
+    finally:
+        xjcuda.set_option(xjcuda.OPT_TC, 1)
     assert np.abs(y - want).max() / np.abs(want).max() < 1e-5
 
 
 @pytest.mark.parametrize("t", [xo.Q4_K, xo.Q6_K, xo.Q8_0])
-def test_gemv64_token_results_independent_of_batch(t):
-    """In the 64-token kernel a token's column depends only on the matrix shape, not on the other
+@pytest.mark.parametrize("tc", [1, 0])
+def test_gemv64_token_results_independent_of_batch(t, tc):
+    """In both 64-token kernels a token's column depends only on the matrix shape, not on the other
     tokens: the first rows of a 64-token launch equal a 17-token launch bit for bit."""
     from xjb200 import xjcuda
     k, n = 2048, 2048
     raw = _w(t, k, n, 8)
     x = np.random.default_rng(6).standard_normal((64, k)).astype(np.float32)
-    y64 = xjcuda.gemv(t, raw, k, n, x)
-    y17 = xjcuda.gemv(t, raw, k, n, x[:17])
+    xjcuda.set_option(xjcuda.OPT_TC, tc)
+    try:
+        y64 = xjcuda.gemv(t, raw, k, n, x)
+        y17 = xjcuda.gemv(t, raw, k, n, x[:17])
+    finally:
+        xjcuda.set_option(xjcuda.OPT_TC, 1)
     assert y17.view(np.uint32).tolist() == y64[:17].view(np.uint32).tolist()
 
 
