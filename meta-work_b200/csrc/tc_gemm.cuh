@@ -140,7 +140,7 @@ __global__ void __launch_bounds__(128, 1) k_tc_selftest(const __half *A, const _
 // chunk's weight planes (double-buffered) and, after the second half, the stage. The products that
 // remain dropped (Wl.Xl) are below 2^-22 relative, so the result is fp32-level like the mma.sync path.
 constexpr int TC_SUB = 64;                          // K of one dequantised weight buffer
-constexpr int TC_ROWS = 128, TC_TILES = 8, TC_WARPS = 8;
+constexpr int TC_ROWS = 128, TC_TILES = 8, TC_WARPS = 16;   // two compute warps per tile
 constexpr int TC_THREADS = TC_WARPS * 32 + 32;      // + the producer warp
 constexpr int TC_PLANE_A = TC_ROWS * TC_SUB * 2;    // one weight plane of a half chunk: 16 KB
 constexpr int TC_ABUF = 2 * TC_PLANE_A;             // Wh + Wl
@@ -158,106 +158,118 @@ using BarTc = BarNamed<1, TC_WARPS * 32>;
 // Byte of (row r, element k) in a weight plane ([128 rows][64 halves], core-matrix layout).
 XJ_DEV uint32_t tc_aoff(int r, int k) { return (uint32_t)((((r >> 3) * (TC_SUB >> 3) + (k >> 3)) << 7) + ((r & 7) << 4) + ((k & 7) << 1)); }
 
+// w rounded to its 11 leading significant bits (Veltkamp's split with the factor 2^13 + 1): exactly
+// representable in fp16 for weights in fp16's normal range, and w - hi is exact. Three FMA-pipe
+// operations instead of an fp16 round trip through the conversion unit.
+XJ_DEV float split_hi11(float w) {
+    const float c = __fmul_rn(w, 8193.0f);
+    return __fsub_rn(c, __fsub_rn(c, w));
+}
+// Exact float of a small non-negative integer code (< 2^23) without an integer-to-float conversion.
+XJ_DEV float code_f(uint32_t code) { return __fsub_rn(__uint_as_float(0x4B000000u | code), 8388608.0f); }
+
 // Stores w0, w1 (elements k, k+1 of row r) as Wh / Wl pairs.
 XJ_DEV void tc_put2(uint8_t *ab, int r, int k, float w0, float w1) {
-    const __half2 h = __floats2half2_rn(w0, w1);
-    const float2 hf = __half22float2(h);
-    const __half2 l = __floats2half2_rn(w0 - hf.x, w1 - hf.y);
+    const float h0 = split_hi11(w0), h1 = split_hi11(w1);
+    const __half2 h = __floats2half2_rn(h0, h1);
+    const __half2 l = __floats2half2_rn(__fsub_rn(w0, h0), __fsub_rn(w1, h1));
     const uint32_t o = tc_aoff(r, k);
     *reinterpret_cast<__half2 *>(ab + o) = h;
     *reinterpret_cast<__half2 *>(ab + TC_PLANE_A + o) = l;
 }
 
-// Warp `tl` decodes its tile's 16 rows x 64 elements (half `h` of the staged 128-wide chunk; `hh`: which
-// half of the K-quant super-block the chunk is) into the weight planes at ab. Lane (g, c) holds, per
-// k-step, the codes of rows g, g+8 and elements 2c, 2c+1, 2c+8, 2c+9 (the mma.sync A-fragment order of
-// the tiled layout); each pair of consecutive elements becomes one Wh and one Wl store.
+// Warp `tl` (+ 8 * part) decodes part `part` (k-steps 2 part, 2 part + 1) of its tile's 16 rows x 64
+// elements (half `h` of the staged 128-wide chunk; `hh`: which half of the K-quant super-block the chunk
+// is) into the weight planes at ab. Lane (g, c) holds, per k-step, the codes of rows g, g+8 and elements
+// 2c, 2c+1, 2c+8, 2c+9 (the mma.sync A-fragment order of the tiled layout); each pair of consecutive
+// elements becomes one Wh and one Wl store. A weight is d1 * q - m1 (Q4_K), d*sc * (q - 32) (Q6_K) or
+// d * q (Q8_0) in f32 (one rounding off the reference's value at most, far below the 22 bits kept).
 template <int TYPE>
-XJ_DEV void tc_dequant(const uint8_t *wst, int tl, int lane, int hh, int h, uint8_t *ab) {
+XJ_DEV void tc_dequant(const uint8_t *wst, int tl, int part, int lane, int hh, int h, uint8_t *ab) {
     using BG = B64Geo<TYPE>;
     const int g = lane >> 2, c = lane & 3, r0 = tl * 16 + g;
     if constexpr (TYPE == XJ_Q4_K || TYPE == XJ_Q6_K) {
-        const uint4 q = *reinterpret_cast<const uint4 *>(wst + (h * 32 + lane) * 16);   // k-steps 4h .. 4h+3
-        float sa[2][4], sb[2][4];   // per row (g, g+8): Q4_K (d1, m1) of the two sub-blocks; Q6_K d*sc per k-step
-        uint2 hq = make_uint2(0u, 0u);
+        const uint2 q = *reinterpret_cast<const uint2 *>(wst + (h * 32 + lane) * 16 + 8 * part);   // k-steps 4h + 2part + {0,1}
+        float sa[2][2], sb[2];      // per row (g, g+8): Q4_K (d1, m1) of the k-steps' sub-block; Q6_K d*sc per k-step
+        uint32_t hq = 0;
 #pragma unroll
         for (int rr = 0; rr < 2; rr++) {
             const int row = g + 8 * rr;
             if constexpr (TYPE == XJ_Q4_K) {
                 const uint8_t *hdr = wst + BG::Q + row * 16;
                 const float d = h2f(ld_u16(hdr)), dmin = h2f(ld_u16(hdr + 2));
-#pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    int s_, m_;
-                    k4_scale_min(4 * hh + 2 * h + e, hdr + 4, s_, m_);
-                    sa[rr][e] = __fmul_rn(d, (float)s_);
-                    sb[rr][e] = __fmul_rn(dmin, (float)m_);
-                }
+                int s_, m_;
+                k4_scale_min(4 * hh + 2 * h + part, hdr + 4, s_, m_);
+                sa[rr][0] = __fmul_rn(d, (float)s_);
+                sb[rr] = -__fmul_rn(dmin, (float)m_);
             } else {
                 const float d = h2f(ld_u16(wst + BG::Q + BG::H + BG::S + row * 2));
                 const int8_t *sc = reinterpret_cast<const int8_t *>(wst + BG::Q + BG::H + row * 16);
 #pragma unroll
-                for (int kk = 0; kk < 4; kk++) sa[rr][kk] = __fmul_rn(d, (float)sc[8 * hh + 4 * h + kk]);
+                for (int kk = 0; kk < 2; kk++) sa[rr][kk] = __fmul_rn(d, (float)sc[8 * hh + 4 * h + 2 * part + kk]);
             }
         }
-        if constexpr (TYPE == XJ_Q6_K) hq = *reinterpret_cast<const uint2 *>(wst + BG::Q + lane * 16 + 8 * h);
+        if constexpr (TYPE == XJ_Q6_K) hq = *reinterpret_cast<const uint32_t *>(wst + BG::Q + lane * 16 + 8 * h + 4 * part);
 #pragma unroll
-        for (int kk = 0; kk < 4; kk++) {
-            const uint32_t w = word_of(q, kk);
-            uint32_t hw = 0;
-            if constexpr (TYPE == XJ_Q6_K) hw = ((kk >> 1) ? hq.y : hq.x) >> ((kk & 1) * 8);
+        for (int kk = 0; kk < 2; kk++) {
+            const uint32_t w = kk ? q.y : q.x;
+            const uint32_t hw = hq >> (kk * 8);
 #pragma unroll
             for (int r = 0; r < 4; r++) {
-                const int rr = r & 1, k = 16 * kk + 2 * c + 8 * (r >> 1);
+                const int rr = r & 1, k = 16 * (2 * part + kk) + 2 * c + 8 * (r >> 1);
                 float v[2];
 #pragma unroll
                 for (int e = 0; e < 2; e++) {
-                    const int code = (int)((w >> (4 * r + 16 * e)) & 0xF);
+                    const uint32_t code = (w >> (4 * r + 16 * e)) & 0xFu;
                     if constexpr (TYPE == XJ_Q4_K) {
-                        v[e] = __fsub_rn(__fmul_rn(sa[rr][kk >> 1], (float)code), sb[rr][kk >> 1]);
+                        v[e] = fmaf(sa[rr][0], code_f(code), sb[rr]);
                     } else {
-                        const int q6 = (code | (int)(((hw >> (2 * r + 16 * e)) & 3) << 4)) - 32;
-                        v[e] = __fmul_rn(sa[rr][kk], (float)q6);
+                        const uint32_t q6 = code | (((hw >> (2 * r + 16 * e)) & 3u) << 4);   // value + 32
+                        v[e] = __fmul_rn(sa[rr][kk], __fsub_rn(code_f(q6), 32.0f));
                     }
                 }
                 tc_put2(ab, r0 + 8 * rr, k, v[0], v[1]);
             }
         }
-    } else {   // Q8_0: units 2h, 2h+1 of the chunk, two k-steps each
+    } else {   // Q8_0: unit 2h + part of the chunk, two k-steps
+        const int u = 2 * h + part;
+        const uint4 q = *reinterpret_cast<const uint4 *>(wst + (u * 32 + lane) * 16);
+        float dq[2];
 #pragma unroll
-        for (int uu = 0; uu < 2; uu++) {
-            const int u = 2 * h + uu;
-            const uint4 q = *reinterpret_cast<const uint4 *>(wst + (u * 32 + lane) * 16);
-            float dq[2];
+        for (int rr = 0; rr < 2; rr++) dq[rr] = h2f(ld_u16(wst + BG::Q + (u * 16 + g + 8 * rr) * 2));
 #pragma unroll
-            for (int rr = 0; rr < 2; rr++) dq[rr] = h2f(ld_u16(wst + BG::Q + (u * 16 + g + 8 * rr) * 2));
+        for (int ss = 0; ss < 2; ss++)
 #pragma unroll
-            for (int ss = 0; ss < 2; ss++)
+            for (int hw = 0; hw < 2; hw++) {
+                const uint32_t w = word_of(q, 2 * ss + hw) ^ 0x80808080u;   // q + 128 per byte
 #pragma unroll
-                for (int hw = 0; hw < 2; hw++) {
-                    const uint32_t w = word_of(q, 2 * ss + hw);
-#pragma unroll
-                    for (int rp = 0; rp < 2; rp++) {         // bytes 2rp, 2rp+1: r = 2hw + rp, e = 0, 1
-                        const int r = 2 * hw + rp, rr = r & 1, k = 32 * uu + 16 * ss + 2 * c + 8 * (r >> 1);
-                        const float v0 = __fmul_rn(dq[rr], (float)(int8_t)(w >> (16 * rp)));
-                        const float v1 = __fmul_rn(dq[rr], (float)(int8_t)(w >> (16 * rp + 8)));
-                        tc_put2(ab, tl * 16 + g + 8 * rr, k, v0, v1);
-                    }
+                for (int rp = 0; rp < 2; rp++) {         // bytes 2rp, 2rp+1: r = 2hw + rp, e = 0, 1
+                    const int r = 2 * hw + rp, rr = r & 1, k = 32 * part + 16 * ss + 2 * c + 8 * (r >> 1);
+                    const float v0 = __fmul_rn(dq[rr], __fsub_rn(code_f((w >> (16 * rp)) & 0xFFu), 128.0f));
+                    const float v1 = __fmul_rn(dq[rr], __fsub_rn(code_f((w >> (16 * rp + 8)) & 0xFFu), 128.0f));
+                    tc_put2(ab, tl * 16 + g + 8 * rr, k, v0, v1);
                 }
-        }
+            }
     }
 }
 
-// Bounded mbarrier wait: gives up (setting *err) after about a second, or at once when *err is set
-// (read every 64 polls, one load in flight), so an error anywhere ends every wait of the grid quickly.
+// Bounded mbarrier wait: the thread sleeps in hardware until the phase completes; gives up (setting
+// *err) after about a second, or at once when *err is set (read every 8 polls, one load in flight), so
+// an error anywhere ends every wait of the grid quickly.
+XJ_DEV bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {   // the thread sleeps until the phase completes (or ~0.1 ms)
+    uint32_t ok;
+    asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 100000;\n selp.u32 %0, 1, 0, p;\n}"
+                 : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
+    return ok != 0;
+}
 XJ_DEV bool tc_wait(uint64_t *bar, uint32_t parity, int *err) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     unsigned long long t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
     int ev = *(volatile int *)err;
     for (int it = 1; it < (1 << 26); it++) {
-        if (mbar_try_wait(bar, parity)) return true;
-        if ((it & 63) == 0) {
+        if (mbar_try_wait_sleep(bar, parity)) return true;
+        if ((it & 7) == 0) {
             if (ev) return false;
             ev = *(volatile int *)err;
             unsigned long long t;
@@ -368,7 +380,8 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
                 const int q = 2 * i + h, ab = q & 1;
                 if (q >= 2 && ok) ok = tc_wait(&mdone[ab], (uint32_t)(((q - 2) >> 1) & 1), a.err);   // buffer ab is free
                 uint8_t *abp = abuf + (size_t)ab * TC_ABUF;
-                if (ok && warp < nt) tc_dequant<TYPE>(st + TC_REC + warp * WB, warp, lane, hh, h, abp);
+                const int tl = warp & (TC_TILES - 1);
+                if (ok && tl < nt) tc_dequant<TYPE>(st + TC_REC + tl * WB, tl, warp >> 3, lane, hh, h, abp);
                 fence_async_smem();
                 BarTc::sync();
                 if (tid == 0 && ok) {
@@ -395,10 +408,9 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
     // ---- accumulator (row = TMEM lane, token = column) -> partials [row][TC_RS] in the stage area
     float *part = reinterpret_cast<float *>(smem);
     if (warp < TC_WARPS && allok) {
-        const int quarter = warp & 3, row = 32 * quarter + lane;
-#pragma unroll
-        for (int cc = 0; cc < 2; cc++) {
-            const int col = 32 * (warp >> 2) + 16 * cc;
+        const int quarter = warp & 3, row = 32 * quarter + lane;   // warp w reads TMEM lanes 32 (w % 4) ..
+        {
+            const int col = 16 * (warp >> 2);
             float v[16];
             tc_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)col, v);
 #pragma unroll
