@@ -735,15 +735,22 @@ inline size_t b64_x_bytes(int T, int K) { return (size_t)(K / B64_CK) * b64_rec_
 __host__ __device__ inline int b64_pos(int e) { return ((e & 7) >> 1) * 8 + ((e & 1) + 2 * (e >> 3)) * 2; }
 
 // Layout of a tensor-core (tcgen05) launch's activations (k_gemm_tc, up to 64 tokens): K in chunks of
-// 128; chunk c is one 32 KB record of two planes (hi, then lo), each [64 tokens][128 halves] in the
+// 128; chunk c is one 36 KB record: two planes (hi, then lo), each [64 tokens][128 halves] in the
 // core-matrix layout of a K-major MMA operand (8 x 8 blocks of 128 bytes, block (i, j) at byte
-// (i * 16 + j) * 128); the 64 range scales follow the last record.
+// (i * 16 + j) * 128), then per 64-wide half a block-sum plane [64 tokens][16 halves] (same layout):
+// for the half's two 32-element blocks b, columns 3b, 3b+1, 3b+2 = (Sh, Sl, Sh) with Sh + Sl = 2^-6 *
+// (the block's sum of hi + lo), columns 6..15 zero (the Q4_K minimum term as one MMA). The 64 range
+// scales follow the last record.
 constexpr int TC_T = 64, TC_CK = 128;
 constexpr int TC_PLANE_X = TC_T * TC_CK * 2;
-constexpr int TC_REC = 2 * TC_PLANE_X;
+constexpr int TC_PLANE_S = TC_T * 16 * 2;            // one block-sum plane (2 KB)
+constexpr int TC_REC = 2 * TC_PLANE_X + 2 * TC_PLANE_S;
 inline size_t tc_x_bytes(int K) { return (size_t)(K / TC_CK) * TC_REC + TC_T * 4 + 256; }
 __host__ __device__ inline uint32_t tc_xoff(int t, int k) {   // byte of (token t, element k) in a plane
     return (uint32_t)((((t >> 3) * (TC_CK >> 3) + (k >> 3)) << 7) + ((t & 7) << 4) + ((k & 7) << 1));
+}
+__host__ __device__ inline uint32_t tc_soff(int t, int k) {   // byte of (token t, column k < 16) in a block-sum plane
+    return (uint32_t)((((t >> 3) * 2 + (k >> 3)) << 7) + ((t & 7) << 4) + ((k & 7) << 1));
 }
 enum { PREP_WIDE = 0, PREP_B64 = 1, PREP_TC = 2 };
 
@@ -804,14 +811,24 @@ static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_xt(const float *
             const float val = (pro == PRO_NORM ? (v[k] * nsc) * norm_w[i] : v[k]) * sc;
             const __half hi = __float2half_rn(val);
             const __half lo = __float2half_rn(val - __half2float(hi));
+            const float bs = warp_sum(__half2float(hi) + __half2float(lo));
             if (L == PREP_TC) {
                 uint8_t *rec = (uint8_t *)buf + (size_t)(i / TC_CK) * TC_REC;
-                const uint32_t o = tc_xoff(t, i & (TC_CK - 1));
+                const int ci = i & (TC_CK - 1);
+                const uint32_t o = tc_xoff(t, ci);
                 *reinterpret_cast<__half *>(rec + o) = hi;
                 *reinterpret_cast<__half *>(rec + TC_PLANE_X + o) = lo;
+                if (lane == 0) {   // this warp's 32 elements are one block: its scaled sum as (Sh, Sl, Sh)
+                    uint8_t *sp = rec + 2 * TC_PLANE_X + (ci >> 6) * TC_PLANE_S;
+                    const int b = (ci >> 5) & 1;
+                    const float sv = bs * 0.015625f;
+                    const __half sh = __float2half_rn(sv), sl = __float2half_rn(sv - __half2float(sh));
+                    *reinterpret_cast<__half *>(sp + tc_soff(t, 3 * b)) = sh;
+                    *reinterpret_cast<__half *>(sp + tc_soff(t, 3 * b + 1)) = sl;
+                    *reinterpret_cast<__half *>(sp + tc_soff(t, 3 * b + 2)) = sh;
+                }
                 continue;
             }
-            const float bs = warp_sum(__half2float(hi) + __half2float(lo));
             if (L == PREP_B64) {
                 const int ci = i & (B64_CK - 1);
                 uint8_t *rec = (uint8_t *)buf + (size_t)(i / B64_CK) * b64_rec_bytes(T);

@@ -209,8 +209,12 @@ void launch(Impl *im, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
 
 // Activations of the 64-token GEMV: 64 tokens at the longest K.
 int alloc_b64(Impl *im, char *err, size_t errlen) {
-    return dalloc(im, (uint8_t **)&im->b64_buf, b64_x_bytes(B64_T, MMA_KMAX), err, errlen) ||
-           dalloc(im, (uint8_t **)&im->tc_buf, tc_x_bytes(MMA_KMAX), err, errlen);
+    if (dalloc(im, (uint8_t **)&im->b64_buf, b64_x_bytes(B64_T, MMA_KMAX), err, errlen) ||
+        dalloc(im, (uint8_t **)&im->tc_buf, tc_x_bytes(MMA_KMAX), err, errlen))
+        return -1;
+    // the block-sum planes' unused columns stay zero (the tensor cores multiply them)
+    CK(cudaMemset(im->tc_buf, 0, tc_x_bytes(MMA_KMAX)));
+    return 0;
 }
 
 void rmsnorm(Impl *im, const float *x, long long ldx, const float *w, float *y, long long ldy, int n, int rows, float eps) {

@@ -131,132 +131,126 @@ __global__ void __launch_bounds__(128, 1) k_tc_selftest(const __half *A, const _
 // exactly as in k_gemv_b64 (partials exchanged through distributed shared memory, summed by the owner
 // in rank order, so the result does not depend on timing).
 //
-// Per chunk a producer warp bulk-copies the 8 tiles' quantised bytes and the activation record (two
-// fp16 planes hi / lo, k_prep_xt<PREP_TC>) into a stage. The 8 compute warps (one tile each) decode
-// the weights of one 64-wide half chunk into fp16 planes Wh / Wl (Wh = w rounded, Wl = w - Wh
-// rounded; w is the reference's dequantised float, core/xj_quant.h:55-122) in the MMA's core-matrix
-// layout, and thread 0 issues, per 16-wide k-step, D += Wh.Xh + Wh.Xl + Wl.Xh (kind::f16, f32
-// accumulator [128 rows][64 tokens] in tensor memory), then commits to an mbarrier that frees the half
-// chunk's weight planes (double-buffered) and, after the second half, the stage. The products that
-// remain dropped (Wl.Xl) are below 2^-22 relative, so the result is fp32-level like the mma.sync path.
-constexpr int TC_SUB = 64;                          // K of one dequantised weight buffer
+// The weights enter the MMA as their exact integer codes in fp16 (Q4_K q, Q6_K q - 32, Q8_0 q: a few
+// logic operations per 8 weights from the tiled layout), the activations as fp16 hi / lo planes. Each
+// scale block of the weights (Q4_K / Q8_0: 32 elements, Q6_K: 16) of a 64-wide half chunk accumulates
+// code . (hi + lo) into its own f32 accumulator [128 rows][64 tokens] in tensor memory (exact products,
+// f32 sums); when a half's MMAs are done, the compute warps read its accumulators back and add
+// scale * accumulator into per-thread partial sums (one row, 16 tokens), in block order. The Q4_K
+// minimum term -dmin*m * (block sum of x) is one more MMA per half into a separate accumulator: A holds
+// -64 dmin*m as fp16 (hi, hi, lo) per block, B the block sums 2^-6 S as (Sh, Sl, Sh). So the result is
+// fp32-level like the mma.sync path, and a token's column does not depend on the other tokens.
+//
+// Pipeline: a producer warp bulk-copies each chunk's 8 tiles of quantised bytes and its activation
+// record into a 2-stage ring; per half chunk, 16 compute warps (two per tile) write the code plane
+// (double-buffered), the half's scales (triple-buffered) and the Q4_K minimum plane, thread 0 issues
+// the MMAs and commits to the half's mbarrier, and the warps fold the half two steps earlier into
+// their partial sums while the tensor cores work.
+constexpr int TC_SUB = 64;                          // K of one half chunk
 constexpr int TC_ROWS = 128, TC_TILES = 8, TC_WARPS = 16;   // two compute warps per tile
 constexpr int TC_THREADS = TC_WARPS * 32 + 32;      // + the producer warp
-constexpr int TC_PLANE_A = TC_ROWS * TC_SUB * 2;    // one weight plane of a half chunk: 16 KB
-constexpr int TC_ABUF = 2 * TC_PLANE_A;             // Wh + Wl
+constexpr int TC_PLANE_A = TC_ROWS * TC_SUB * 2;    // code plane of a half chunk: 16 KB
+constexpr int TC_PLANE_M = TC_ROWS * 16 * 2;        // Q4_K minimum plane of a half chunk: 4 KB
 constexpr int TC_STAGES = 2;
 constexpr int TC_MAXSPLIT = 16;
 constexpr int TC_RS = TC_T + 4;                     // row stride (floats) of the partial sums
 constexpr size_t TC_RECV = (size_t)(TC_ROWS + TC_MAXSPLIT) * TC_RS * 4;
+constexpr int TC_DBUF = TC_ROWS * 4;                // floats of one half's block scales (<= 4 blocks)
+template <int TYPE> constexpr int tc_nacc() { return TYPE == XJ_Q6_K ? 4 : 2; }   // scale blocks per half
+template <int TYPE> constexpr uint32_t tc_cols() { return TYPE == XJ_Q8_0 ? 256u : 512u; }   // TMEM columns
 template <int TYPE> constexpr int tc_stage() { return TC_REC + TC_TILES * b64_wbytes<TYPE>(); }
-template <int TYPE> constexpr size_t tc_smem() { return (size_t)TC_STAGES * tc_stage<TYPE>() + 2 * TC_ABUF + TC_RECV; }
-static_assert(tc_smem<XJ_Q8_0>() <= 227 * 1024, "fits one SM");
+template <int TYPE> constexpr size_t tc_smem() {
+    return (size_t)TC_STAGES * tc_stage<TYPE>() + 2 * TC_PLANE_A + 2 * TC_PLANE_M + 3 * TC_DBUF * 4 + TC_RECV;
+}
+static_assert(tc_smem<XJ_Q8_0>() <= 227 * 1024 && tc_smem<XJ_Q6_K>() <= 227 * 1024, "fits one SM");
 static_assert(tc_stage<XJ_Q4_K>() % 128 == 0 && tc_stage<XJ_Q6_K>() % 128 == 0 && tc_stage<XJ_Q8_0>() % 128 == 0, "aligned stages");
 static_assert(TC_ROWS * TC_RS * 4 <= TC_STAGES * tc_stage<XJ_Q4_K>(), "partials fit the stage area");
+static_assert(2 * 2 * 64 + 64 <= 512 && 2 * 4 * 64 <= 512, "accumulators fit tensor memory");
 using BarTc = BarNamed<1, TC_WARPS * 32>;
 
-// Byte of (row r, element k) in a weight plane ([128 rows][64 halves], core-matrix layout).
+// Byte of (row r, element k) in a code plane ([128 rows][64 halves], core-matrix layout).
 XJ_DEV uint32_t tc_aoff(int r, int k) { return (uint32_t)((((r >> 3) * (TC_SUB >> 3) + (k >> 3)) << 7) + ((r & 7) << 4) + ((k & 7) << 1)); }
+// Byte of (row r, column k < 16) in a minimum plane.
+XJ_DEV uint32_t tc_moff(int r, int k) { return (uint32_t)((((r >> 3) * 2 + (k >> 3)) << 7) + ((r & 7) << 4) + ((k & 7) << 1)); }
 
-// w rounded to its 11 leading significant bits (Veltkamp's split with the factor 2^13 + 1): exactly
-// representable in fp16 for weights in fp16's normal range, and w - hi is exact. Three FMA-pipe
-// operations instead of an fp16 round trip through the conversion unit.
-XJ_DEV float split_hi11(float w) {
-    const float c = __fmul_rn(w, 8193.0f);
-    return __fsub_rn(c, __fsub_rn(c, w));
-}
-// Exact float of a small non-negative integer code (< 2^23) without an integer-to-float conversion.
-XJ_DEV float code_f(uint32_t code) { return __fsub_rn(__uint_as_float(0x4B000000u | code), 8388608.0f); }
-
-// Stores w0, w1 (elements k, k+1 of row r) as Wh / Wl pairs.
-XJ_DEV void tc_put2(uint8_t *ab, int r, int k, float w0, float w1) {
-    const float h0 = split_hi11(w0), h1 = split_hi11(w1);
-    const __half2 h = __floats2half2_rn(h0, h1);
-    const __half2 l = __floats2half2_rn(__fsub_rn(w0, h0), __fsub_rn(w1, h1));
-    const uint32_t o = tc_aoff(r, k);
-    *reinterpret_cast<__half2 *>(ab + o) = h;
-    *reinterpret_cast<__half2 *>(ab + TC_PLANE_A + o) = l;
-}
-
-// Warp `tl` (+ 8 * part) decodes part `part` (k-steps 2 part, 2 part + 1) of its tile's 16 rows x 64
-// elements (half `h` of the staged 128-wide chunk; `hh`: which half of the K-quant super-block the chunk
-// is) into the weight planes at ab. Lane (g, c) holds, per k-step, the codes of rows g, g+8 and elements
-// 2c, 2c+1, 2c+8, 2c+9 (the mma.sync A-fragment order of the tiled layout); each pair of consecutive
-// elements becomes one Wh and one Wl store. A weight is d1 * q - m1 (Q4_K), d*sc * (q - 32) (Q6_K) or
-// d * q (Q8_0) in f32 (one rounding off the reference's value at most, far below the 22 bits kept).
+// Warp `tl` (+ 8 * part) writes the codes of k-steps (2 part, 2 part + 1) of its tile's 16 rows in half
+// `h` of the staged chunk into the code plane ab. Lane (g, c) holds, per k-step, the codes of rows g,
+// g+8 and elements 2c, 2c+1, 2c+8, 2c+9 (the mma.sync A-fragment order of the tiled layout): register
+// r of the fragment is the pair (row g + 8 (r & 1), elements 2c + 8 (r >> 1) + {0, 1}).
 template <int TYPE>
-XJ_DEV void tc_dequant(const uint8_t *wst, int tl, int part, int lane, int hh, int h, uint8_t *ab) {
+XJ_DEV void tc_codes(const uint8_t *wst, int tl, int part, int lane, int h, uint8_t *ab) {
     using BG = B64Geo<TYPE>;
     const int g = lane >> 2, c = lane & 3, r0 = tl * 16 + g;
-    if constexpr (TYPE == XJ_Q4_K || TYPE == XJ_Q6_K) {
-        const uint2 q = *reinterpret_cast<const uint2 *>(wst + (h * 32 + lane) * 16 + 8 * part);   // k-steps 4h + 2part + {0,1}
-        float sa[2][2], sb[2];      // per row (g, g+8): Q4_K (d1, m1) of the k-steps' sub-block; Q6_K d*sc per k-step
-        uint32_t hq = 0;
 #pragma unroll
-        for (int rr = 0; rr < 2; rr++) {
-            const int row = g + 8 * rr;
-            if constexpr (TYPE == XJ_Q4_K) {
-                const uint8_t *hdr = wst + BG::Q + row * 16;
-                const float d = h2f(ld_u16(hdr)), dmin = h2f(ld_u16(hdr + 2));
-                int s_, m_;
-                k4_scale_min(4 * hh + 2 * h + part, hdr + 4, s_, m_);
-                sa[rr][0] = __fmul_rn(d, (float)s_);
-                sb[rr] = -__fmul_rn(dmin, (float)m_);
-            } else {
-                const float d = h2f(ld_u16(wst + BG::Q + BG::H + BG::S + row * 2));
-                const int8_t *sc = reinterpret_cast<const int8_t *>(wst + BG::Q + BG::H + row * 16);
+    for (int kk = 0; kk < 2; kk++) {
+        const int ks = 2 * part + kk;                      // k-step within the half
+        uint32_t a[4];
+        if constexpr (TYPE == XJ_Q4_K || TYPE == XJ_Q6_K) {
+            const uint32_t w = *reinterpret_cast<const uint32_t *>(wst + ((h * 32 + lane) * 16) + 4 * ks);
+            nib_frag(w, a);
+            if constexpr (TYPE == XJ_Q6_K) {               // + 16 * high - 32: the signed code, exact
+                uint32_t hw = *reinterpret_cast<const uint32_t *>(wst + BG::Q + lane * 16 + 4 * ((4 * h + ks) >> 1));
+                if (ks & 1) hw >>= 8;
+                uint32_t ah[4];
+                hi_frag(hw, ah);
 #pragma unroll
-                for (int kk = 0; kk < 2; kk++) sa[rr][kk] = __fmul_rn(d, (float)sc[8 * hh + 4 * h + 2 * part + kk]);
+                for (int r = 0; r < 4; r++) a[r] = hadd2(a[r], ah[r]);
             }
+        } else {                                           // Q8_0: unit 2h + part, k-step kk
+            const uint8_t *qs = wst + ((2 * h + part) * 32 + lane) * 16 + 8 * kk;
+            q8_frag(*reinterpret_cast<const uint32_t *>(qs), *reinterpret_cast<const uint32_t *>(qs + 4), a);
         }
-        if constexpr (TYPE == XJ_Q6_K) hq = *reinterpret_cast<const uint32_t *>(wst + BG::Q + lane * 16 + 8 * h + 4 * part);
 #pragma unroll
-        for (int kk = 0; kk < 2; kk++) {
-            const uint32_t w = kk ? q.y : q.x;
-            const uint32_t hw = hq >> (kk * 8);
-#pragma unroll
-            for (int r = 0; r < 4; r++) {
-                const int rr = r & 1, k = 16 * (2 * part + kk) + 2 * c + 8 * (r >> 1);
-                float v[2];
-#pragma unroll
-                for (int e = 0; e < 2; e++) {
-                    const uint32_t code = (w >> (4 * r + 16 * e)) & 0xFu;
-                    if constexpr (TYPE == XJ_Q4_K) {
-                        v[e] = fmaf(sa[rr][0], code_f(code), sb[rr]);
-                    } else {
-                        const uint32_t q6 = code | (((hw >> (2 * r + 16 * e)) & 3u) << 4);   // value + 32
-                        v[e] = __fmul_rn(sa[rr][kk], __fsub_rn(code_f(q6), 32.0f));
-                    }
-                }
-                tc_put2(ab, r0 + 8 * rr, k, v[0], v[1]);
-            }
-        }
-    } else {   // Q8_0: unit 2h + part of the chunk, two k-steps
-        const int u = 2 * h + part;
-        const uint4 q = *reinterpret_cast<const uint4 *>(wst + (u * 32 + lane) * 16);
-        float dq[2];
-#pragma unroll
-        for (int rr = 0; rr < 2; rr++) dq[rr] = h2f(ld_u16(wst + BG::Q + (u * 16 + g + 8 * rr) * 2));
-#pragma unroll
-        for (int ss = 0; ss < 2; ss++)
-#pragma unroll
-            for (int hw = 0; hw < 2; hw++) {
-                const uint32_t w = word_of(q, 2 * ss + hw) ^ 0x80808080u;   // q + 128 per byte
-#pragma unroll
-                for (int rp = 0; rp < 2; rp++) {         // bytes 2rp, 2rp+1: r = 2hw + rp, e = 0, 1
-                    const int r = 2 * hw + rp, rr = r & 1, k = 32 * part + 16 * ss + 2 * c + 8 * (r >> 1);
-                    const float v0 = __fmul_rn(dq[rr], __fsub_rn(code_f((w >> (16 * rp)) & 0xFFu), 128.0f));
-                    const float v1 = __fmul_rn(dq[rr], __fsub_rn(code_f((w >> (16 * rp + 8)) & 0xFFu), 128.0f));
-                    tc_put2(ab, tl * 16 + g + 8 * rr, k, v0, v1);
-                }
-            }
+        for (int r = 0; r < 4; r++)
+            *reinterpret_cast<uint32_t *>(ab + tc_aoff(r0 + 8 * (r & 1), 16 * ks + 2 * c + 8 * (r >> 1))) = a[r];
+    }
+}
+
+// The block scales of half `h` (`hh`: which half of the K-quant super-block the chunk is) for the rows
+// this thread covers (Q4_K, Q8_0: thread = (row, block) for tid < 256; Q6_K: (row, block) for all 512),
+// into db[row * 4 + block]; Q4_K also writes the row's minimum plane entries (-64 dmin*m as hi, hi, lo
+// per block; columns 6..15 zero).
+template <int TYPE>
+XJ_DEV void tc_scales(const uint8_t *wst0, int tid, int nt, int hh, int h, float *db, uint8_t *mp) {
+    using BG = B64Geo<TYPE>;
+    constexpr int WB = b64_wbytes<TYPE>();
+    constexpr int NB = tc_nacc<TYPE>();
+    const int row = tid / NB, b = tid % NB;
+    if (row >= TC_ROWS) return;
+    const int tl = row >> 4, rt = row & 15;
+    if (tl >= nt) {                                        // rows past the matrix: zeros (never stored)
+        db[row * 4 + b] = 0.0f;
+        if (TYPE == XJ_Q4_K)
+            for (int k = 3 * b; k < (b ? 16 : 3); k++) *reinterpret_cast<__half *>(mp + tc_moff(row, k)) = __float2half_rn(0.0f);
+        return;
+    }
+    const uint8_t *wst = wst0 + tl * WB;
+    if constexpr (TYPE == XJ_Q4_K) {
+        const uint8_t *hdr = wst + BG::Q + rt * 16;
+        const float d = h2f(ld_u16(hdr)), dmin = h2f(ld_u16(hdr + 2));
+        int s_, m_;
+        k4_scale_min(4 * hh + 2 * h + b, hdr + 4, s_, m_);
+        db[row * 4 + b] = __fmul_rn(d, (float)s_);
+        const float mm = -64.0f * __fmul_rn(dmin, (float)m_);
+        const __half mh = __float2half_rn(mm), ml = __float2half_rn(mm - __half2float(mh));
+        *reinterpret_cast<__half *>(mp + tc_moff(row, 3 * b)) = mh;
+        *reinterpret_cast<__half *>(mp + tc_moff(row, 3 * b + 1)) = mh;
+        *reinterpret_cast<__half *>(mp + tc_moff(row, 3 * b + 2)) = ml;
+        if (b == 1)
+            for (int k = 6; k < 16; k++) *reinterpret_cast<__half *>(mp + tc_moff(row, k)) = __float2half_rn(0.0f);
+    } else if constexpr (TYPE == XJ_Q6_K) {
+        const float d = h2f(ld_u16(wst + BG::Q + BG::H + BG::S + rt * 2));
+        const int8_t sc = reinterpret_cast<const int8_t *>(wst + BG::Q + BG::H + rt * 16)[8 * hh + 4 * h + b];
+        db[row * 4 + b] = __fmul_rn(d, (float)sc);
+    } else {
+        db[row * 4 + b] = h2f(ld_u16(wst + BG::Q + ((2 * h + b) * 16 + rt) * 2));
     }
 }
 
 // Bounded mbarrier wait: the thread sleeps in hardware until the phase completes; gives up (setting
 // *err) after about a second, or at once when *err is set (read every 8 polls, one load in flight), so
 // an error anywhere ends every wait of the grid quickly.
-XJ_DEV bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {   // the thread sleeps until the phase completes (or ~0.1 ms)
+XJ_DEV bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {   // sleeps until the phase completes (or ~0.1 ms)
     uint32_t ok;
     asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 100000;\n selp.u32 %0, 1, 0, p;\n}"
                  : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
@@ -283,12 +277,14 @@ XJ_DEV bool tc_wait(uint64_t *bar, uint32_t parity, int *err) {
 
 template <int TYPE>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
-    constexpr int WB = b64_wbytes<TYPE>(), SBY = tc_stage<TYPE>();
+    constexpr int WB = b64_wbytes<TYPE>(), SBY = tc_stage<TYPE>(), NB = tc_nacc<TYPE>();
     constexpr bool KQ = TYPE != XJ_Q8_0;
-    constexpr uint32_t IDESC = tc_idesc_f16(TC_ROWS, TC_T);
+    constexpr uint32_t IDESC = tc_idesc_f16(TC_ROWS, TC_T), NCOL = tc_cols<TYPE>();
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t *abuf = smem + (size_t)TC_STAGES * SBY;
-    float *recv = reinterpret_cast<float *>(abuf + 2 * TC_ABUF);   // [ns][ceil(128/ns)][TC_RS] partials of this CTA's rows
+    uint8_t *aplane = smem + (size_t)TC_STAGES * SBY;                   // [2] code planes
+    uint8_t *mplane = aplane + 2 * TC_PLANE_A;                          // [2] Q4_K minimum planes
+    float *dbuf = reinterpret_cast<float *>(mplane + 2 * TC_PLANE_M);   // [3][128][4] block scales
+    float *recv = dbuf + 3 * TC_DBUF;                                   // [ns][ceil(128/ns)][TC_RS] partials of this CTA's rows
     __shared__ __align__(8) uint64_t full[TC_STAGES], mdone[2], rbar;
     __shared__ uint32_t s_tmem;
     __shared__ float tok_inv[TC_T];                    // 1 / range scale (a power of two: exact)
@@ -305,7 +301,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
     const int nt = ntiles - t0 < TC_TILES ? ntiles - t0 : TC_TILES;
     const int nch = K / TC_CK;
     const int c0 = (int)((long long)split * nch / ns), c1 = (int)((long long)(split + 1) * nch / ns);
-    const int nc = c1 - c0;
+    const int nc = c1 - c0, nsub = 2 * nc;
     const int nrmax = (TC_ROWS + ns - 1) / ns;
     const int rb = split * TC_ROWS / ns, nr = (split + 1) * TC_ROWS / ns - rb;   // the rows this CTA finishes
     auto issue_w = [&](int i) {       // producer warp: weights of chunk c0 + i, one tile per lane
@@ -344,13 +340,30 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         if (ns > 1) mbar_expect_tx(&rbar, (uint32_t)((ns - 1) * nr * TC_RS * 4));
     }
-    if (warp == 0) tc_alloc(&s_tmem, TC_T);
+    if (warp == 0) tc_alloc(&s_tmem, NCOL);
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
     if (ns > 1) cluster_arrive();                          // every CTA's receive barrier is armed before any send
     bool ok = true;
+    float y[16];                                           // compute threads: row crow, tokens 16 tb .. 16 tb + 15
+#pragma unroll
+    for (int i = 0; i < 16; i++) y[i] = 0.0f;
+    const int quarter = warp & 3, tb = (warp >> 2) & 3, crow = 32 * quarter + lane;
+    const uint32_t tlane = (uint32_t)(32 * quarter) << 16;
+    // fold half qq's accumulators (buffer qq & 1) into y, scale block by scale block
+    auto fold = [&](int qq) {
+        const float *db = dbuf + (qq % 3) * TC_DBUF + crow * 4;
+#pragma unroll
+        for (int b = 0; b < NB; b++) {
+            float v[16];
+            tc_ld16(tmem + tlane + (uint32_t)(((qq & 1) * NB + b) * 64 + 16 * tb), v);
+            const float sc = db[b];
+#pragma unroll
+            for (int i = 0; i < 16; i++) y[i] = fmaf(sc, v[i], y[i]);
+        }
+    };
     if (warp == TC_WARPS) {
         // ---- producer: weights do not depend on the predecessor kernel, the activations do
         for (int i = 0; i < TC_STAGES && i < nc; i++) issue_w(i);
@@ -359,7 +372,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
         if (lane == 0)
             for (int i = 0; i < TC_STAGES && i < nc; i++) issue_x(i);
         for (int i = TC_STAGES; i < nc && ok; i++) {
-            // stage i % 2 is free once the MMAs of chunk i - 2 (its second half: sub-chunk 2i - 3) are done
+            // stage i % 2 is free once the MMAs of chunk i - 2 (its second half: half 2i - 3) are done
             if (lane == 0) ok = tc_wait(&mdone[1], (uint32_t)((i - 2) & 1), a.err);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
@@ -370,57 +383,78 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
         griddep_launch();
         griddep_wait();
         // every compute thread runs all iterations and meets every named barrier (a failed wait only
-        // skips work), so no thread can be left waiting at a barrier
+        // skips work; `ok` is kept warp-uniform for the warp-wide tensor-memory loads)
+        const int tl = warp & (TC_TILES - 1), part = warp >> 3;
         for (int i = 0; i < nc; i++) {
             const int s = i % TC_STAGES;
             uint8_t *st = smem + (size_t)s * SBY;
             if (ok) ok = tc_wait(&full[s], (uint32_t)((i / TC_STAGES) & 1), a.err);
+            ok = __all_sync(0xffffffffu, ok);
             const int hh = (c0 + i) & 1;
             for (int h = 0; h < 2; h++) {
                 const int q = 2 * i + h, ab = q & 1;
-                if (q >= 2 && ok) ok = tc_wait(&mdone[ab], (uint32_t)(((q - 2) >> 1) & 1), a.err);   // buffer ab is free
-                uint8_t *abp = abuf + (size_t)ab * TC_ABUF;
-                const int tl = warp & (TC_TILES - 1);
-                if (ok && tl < nt) tc_dequant<TYPE>(st + TC_REC + tl * WB, tl, warp >> 3, lane, hh, h, abp);
+                if (q >= 2) {
+                    // half q - 2 is done: its planes are free and its accumulators final
+                    if (ok) ok = tc_wait(&mdone[ab], (uint32_t)(((q - 2) >> 1) & 1), a.err);
+                    ok = __all_sync(0xffffffffu, ok);
+                    tc_fence_after();
+                    if (ok) fold(q - 2);
+                    tc_fence_before();
+                }
+                uint8_t *ap = aplane + (size_t)ab * TC_PLANE_A, *mp = mplane + (size_t)ab * TC_PLANE_M;
+                if (ok && tl < nt) tc_codes<TYPE>(st + TC_REC + tl * WB, tl, part, lane, h, ap);
+                if (ok) tc_scales<TYPE>(st + TC_REC, tid, nt, hh, h, dbuf + (q % 3) * TC_DBUF, mp);
                 fence_async_smem();
                 BarTc::sync();
                 if (tid == 0 && ok) {
                     tc_fence_after();
+                    const uint32_t ao = smem_u32(ap), bo = smem_u32(st);
 #pragma unroll
-                    for (int kk = 0; kk < TC_SUB / 16; kk++) {
-                        const uint32_t ao = smem_u32(abp) + kk * 256, bo = smem_u32(st) + (8 * h + 2 * kk) * 128;
-                        const uint64_t ah = tc_desc(ao, 128, (TC_SUB / 8) * 128), al = tc_desc(ao + TC_PLANE_A, 128, (TC_SUB / 8) * 128);
-                        const uint64_t bh = tc_desc(bo, 128, (TC_CK / 8) * 128), bl = tc_desc(bo + TC_PLANE_X, 128, (TC_CK / 8) * 128);
-                        tc_mma_f16(tmem, ah, bh, IDESC, (i > 0 || h > 0 || kk > 0) ? 1u : 0u);
-                        tc_mma_f16(tmem, ah, bl, IDESC, 1u);
-                        tc_mma_f16(tmem, al, bh, IDESC, 1u);
+                    for (int ks = 0; ks < TC_SUB / 16; ks++) {
+                        const int b = TYPE == XJ_Q6_K ? ks : ks >> 1;       // scale block of the k-step
+                        const bool first = TYPE == XJ_Q6_K ? true : (ks & 1) == 0;
+                        const uint32_t acc = tmem + (uint32_t)((ab * NB + b) * 64);
+                        const uint64_t ad = tc_desc(ao + ks * 256, 128, (TC_SUB / 8) * 128);
+                        const uint32_t bk = bo + (8 * h + 2 * ks) * 128;
+                        const uint64_t bh = tc_desc(bk, 128, (TC_CK / 8) * 128), bl = tc_desc(bk + TC_PLANE_X, 128, (TC_CK / 8) * 128);
+                        tc_mma_f16(acc, ad, bh, IDESC, first ? 0u : 1u);
+                        tc_mma_f16(acc, ad, bl, IDESC, 1u);
+                    }
+                    if constexpr (TYPE == XJ_Q4_K) {
+                        const uint64_t md = tc_desc(smem_u32(mp), 128, 256);
+                        const uint64_t sd = tc_desc(bo + 2 * TC_PLANE_X + h * TC_PLANE_S, 128, 256);
+                        tc_mma_f16(tmem + (uint32_t)(2 * NB * 64), md, sd, IDESC, q > 0 ? 1u : 0u);
                     }
                     tc_commit(&mdone[ab]);
                 }
             }
         }
-        // the last MMAs (sub-chunk 2nc - 1, buffer 1) are done: the accumulator is final
-        if (ok) ok = tc_wait(&mdone[1], (uint32_t)((nc - 1) & 1), a.err);
+        // the last two halves
+        for (int qq = nsub >= 2 ? nsub - 2 : 0; qq < nsub; qq++) {
+            if (ok) ok = tc_wait(&mdone[qq & 1], (uint32_t)((qq >> 1) & 1), a.err);
+            ok = __all_sync(0xffffffffu, ok);
+            tc_fence_after();
+            if (ok) fold(qq);
+        }
+        if (TYPE == XJ_Q4_K && ok) {                       // the minimum term, unscaled
+            float v[16];
+            tc_ld16(tmem + tlane + (uint32_t)(2 * NB * 64 + 16 * tb), v);
+#pragma unroll
+            for (int i = 0; i < 16; i++) y[i] += v[i];
+        }
     }
     if (tid < T) tok_inv[tid] = 1.0f / reinterpret_cast<const float *>((const uint8_t *)a.xbuf + (size_t)nch * TC_REC)[tid];
     const bool allok = __syncthreads_and(ok) != 0;
-    tc_fence_after();
-    // ---- accumulator (row = TMEM lane, token = column) -> partials [row][TC_RS] in the stage area
+    // ---- partial sums [row][TC_RS] in the stage area (free: every load landed, every MMA is done)
     float *part = reinterpret_cast<float *>(smem);
     if (warp < TC_WARPS && allok) {
-        const int quarter = warp & 3, row = 32 * quarter + lane;   // warp w reads TMEM lanes 32 (w % 4) ..
-        {
-            const int col = 16 * (warp >> 2);
-            float v[16];
-            tc_ld16(tmem + ((uint32_t)(32 * quarter) << 16) + (uint32_t)col, v);
 #pragma unroll
-            for (int e = 0; e < 16; e += 4)
-                *reinterpret_cast<float4 *>(part + (size_t)row * TC_RS + col + e) = make_float4(v[e], v[e + 1], v[e + 2], v[e + 3]);
-        }
+        for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4 *>(part + (size_t)crow * TC_RS + 16 * tb + e) = make_float4(y[e], y[e + 1], y[e + 2], y[e + 3]);
     }
     tc_fence_before();
     __syncthreads();
-    if (warp == 0) tc_dealloc(tmem, TC_T);
+    if (warp == 0) tc_dealloc(tmem, NCOL);
     if (ns > 1) {
         // each owner's rows to slot `split` of its receive buffer, one bulk copy per owner
         cluster_wait();                                    // the owners' receive barriers are armed
