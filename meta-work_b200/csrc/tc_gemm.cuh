@@ -142,7 +142,7 @@ __global__ void __launch_bounds__(128, 1) k_tc_selftest(const __half *A, const _
 // fp32-level like the mma.sync path, and a token's column does not depend on the other tokens.
 //
 // Pipeline: a producer warp bulk-copies each chunk's 8 tiles of quantised bytes and its activation
-// record into a 2-stage ring; per half chunk, 16 compute warps (two per tile) write the code plane
+// record into a 3-stage ring; per half chunk, 16 compute warps (two per tile) write the code plane
 // (double-buffered), the half's scales (triple-buffered) and the Q4_K minimum plane, thread 0 issues
 // the MMAs and commits to the half's mbarrier, and the warps fold the half two steps earlier into
 // their partial sums while the tensor cores work.
@@ -151,20 +151,21 @@ constexpr int TC_ROWS = 128, TC_TILES = 8, TC_WARPS = 16;   // two compute warps
 constexpr int TC_THREADS = TC_WARPS * 32 + 32;      // + the producer warp
 constexpr int TC_PLANE_A = TC_ROWS * TC_SUB * 2;    // code plane of a half chunk: 16 KB
 constexpr int TC_PLANE_M = TC_ROWS * 16 * 2;        // Q4_K minimum plane of a half chunk: 4 KB
-constexpr int TC_STAGES = 2;
+constexpr int TC_STAGES = 3;
 constexpr int TC_MAXSPLIT = 16;
 constexpr int TC_RS = TC_T + 4;                     // row stride (floats) of the partial sums
-constexpr size_t TC_RECV = (size_t)(TC_ROWS + TC_MAXSPLIT) * TC_RS * 4;
+constexpr size_t TC_PART = (size_t)TC_ROWS * TC_RS * 4;   // this CTA's partial sums (stage area, after the K loop)
+constexpr size_t TC_RECV = (size_t)(TC_ROWS + TC_MAXSPLIT) * TC_RS * 4;   // other splits' partials (stage area, after it)
 constexpr int TC_DBUF = TC_ROWS * 4;                // floats of one half's block scales (<= 4 blocks)
 template <int TYPE> constexpr int tc_nacc() { return TYPE == XJ_Q6_K ? 4 : 2; }   // scale blocks per half
 template <int TYPE> constexpr uint32_t tc_cols() { return TYPE == XJ_Q8_0 ? 256u : 512u; }   // TMEM columns
 template <int TYPE> constexpr int tc_stage() { return TC_REC + TC_TILES * b64_wbytes<TYPE>(); }
 template <int TYPE> constexpr size_t tc_smem() {
-    return (size_t)TC_STAGES * tc_stage<TYPE>() + 2 * TC_PLANE_A + 2 * TC_PLANE_M + 3 * TC_DBUF * 4 + TC_RECV;
+    return (size_t)TC_STAGES * tc_stage<TYPE>() + 2 * TC_PLANE_A + 2 * TC_PLANE_M + 3 * TC_DBUF * 4;
 }
 static_assert(tc_smem<XJ_Q8_0>() <= 227 * 1024 && tc_smem<XJ_Q6_K>() <= 227 * 1024, "fits one SM");
 static_assert(tc_stage<XJ_Q4_K>() % 128 == 0 && tc_stage<XJ_Q6_K>() % 128 == 0 && tc_stage<XJ_Q8_0>() % 128 == 0, "aligned stages");
-static_assert(TC_ROWS * TC_RS * 4 <= TC_STAGES * tc_stage<XJ_Q4_K>(), "partials fit the stage area");
+static_assert(TC_PART + TC_RECV <= TC_STAGES * tc_stage<XJ_Q4_K>(), "partials fit the stage area");
 static_assert(2 * 2 * 64 + 64 <= 512 && 2 * 4 * 64 <= 512, "accumulators fit tensor memory");
 using BarTc = BarNamed<1, TC_WARPS * 32>;
 
@@ -256,6 +257,11 @@ XJ_DEV bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {   // sleeps un
                  : "=r"(ok) : "r"(smem_u32(bar)), "r"(parity) : "memory");
     return ok != 0;
 }
+XJ_DEV unsigned long long globaltimer_ns() {
+    unsigned long long t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
 XJ_DEV bool tc_wait(uint64_t *bar, uint32_t parity, int *err) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
     unsigned long long t0;
@@ -284,8 +290,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
     uint8_t *aplane = smem + (size_t)TC_STAGES * SBY;                   // [2] code planes
     uint8_t *mplane = aplane + 2 * TC_PLANE_A;                          // [2] Q4_K minimum planes
     float *dbuf = reinterpret_cast<float *>(mplane + 2 * TC_PLANE_M);   // [3][128][4] block scales
-    float *recv = dbuf + 3 * TC_DBUF;                                   // [ns][ceil(128/ns)][TC_RS] partials of this CTA's rows
-    __shared__ __align__(8) uint64_t full[TC_STAGES], mdone[2], rbar;
+    // after the K loop, in the stage area: this CTA's partials, then [ns][ceil(128/ns)][TC_RS] partials
+    // of its rows from the other splits (peers send only after every CTA of the cluster left its loop)
+    float *recv = reinterpret_cast<float *>(smem + TC_PART);
+    __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], mdone[2], rbar;
     __shared__ uint32_t s_tmem;
     __shared__ float tok_inv[TC_T];                    // 1 / range scale (a power of two: exact)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -333,7 +341,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
                  &full[i % TC_STAGES]);
     };
     if (tid == 0) {
-        for (int q = 0; q < TC_STAGES; q++) mbar_init(&full[q], 1);
+        for (int q = 0; q < TC_STAGES; q++) { mbar_init(&full[q], 1); mbar_init(&empty[q], 1); }
         mbar_init(&mdone[0], 1);
         mbar_init(&mdone[1], 1);
         mbar_init(&rbar, 1);
@@ -345,7 +353,6 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
     __syncthreads();
     tc_fence_after();
     const uint32_t tmem = s_tmem;
-    if (ns > 1) cluster_arrive();                          // every CTA's receive barrier is armed before any send
     bool ok = true;
     float y[16];                                           // compute threads: row crow, tokens 16 tb .. 16 tb + 15
 #pragma unroll
@@ -366,19 +373,28 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
     };
     if (warp == TC_WARPS) {
         // ---- producer: weights do not depend on the predecessor kernel, the activations do
-        for (int i = 0; i < TC_STAGES && i < nc; i++) issue_w(i);
+        int issued = nc < TC_STAGES ? nc : TC_STAGES;
+        for (int i = 0; i < issued; i++) issue_w(i);
         griddep_launch();
         griddep_wait();
         if (lane == 0)
             for (int i = 0; i < TC_STAGES && i < nc; i++) issue_x(i);
         for (int i = TC_STAGES; i < nc && ok; i++) {
-            // stage i % 2 is free once the MMAs of chunk i - 2 (its second half: half 2i - 3) are done
-            if (lane == 0) ok = tc_wait(&mdone[1], (uint32_t)((i - 2) & 1), a.err);
+            // the stage is free once the MMAs of chunk i - TC_STAGES are done
+            if (lane == 0) ok = tc_wait(&empty[i % TC_STAGES], (uint32_t)(((i / TC_STAGES) - 1) & 1), a.err);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             issue_w(i);
             if (lane == 0) issue_x(i);
+            issued = i + 1;
         }
+        // copies in flight must land before the stage area is reused (they all have, unless a wait gave up)
+        if (lane == 0)
+            for (int i = issued > TC_STAGES ? issued - TC_STAGES : 0; i < issued; i++) {
+                const unsigned long long t0 = globaltimer_ns();
+                while (!mbar_try_wait_sleep(&full[i % TC_STAGES], (uint32_t)((i / TC_STAGES) & 1)))
+                    if (globaltimer_ns() - t0 > 100000000ull) break;
+            }
     } else {
         griddep_launch();
         griddep_wait();
@@ -426,6 +442,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
                         tc_mma_f16(tmem + (uint32_t)(2 * NB * 64), md, sd, IDESC, q > 0 ? 1u : 0u);
                     }
                     tc_commit(&mdone[ab]);
+                    if (h == 1) tc_commit(&empty[s]);
                 }
             }
         }
@@ -456,8 +473,10 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
     __syncthreads();
     if (warp == 0) tc_dealloc(tmem, NCOL);
     if (ns > 1) {
-        // each owner's rows to slot `split` of its receive buffer, one bulk copy per owner
-        cluster_wait();                                    // the owners' receive barriers are armed
+        // every CTA of the cluster has left its K loop (its stage area now holds partials): each owner's
+        // rows to slot `split` of its receive buffer, one bulk copy per owner
+        cluster_arrive();
+        cluster_wait();
         if (tid < ns && tid != split) {
             const int o = tid, orb = o * TC_ROWS / ns, onr = (o + 1) * TC_ROWS / ns - orb;
             fence_async_smem();
