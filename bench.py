@@ -29,8 +29,8 @@ import numpy as np
 ROOT = pathlib.Path(__file__).resolve().parent
 PEAKS = ROOT / "MEASURED_PEAKS.json"
 # DRAM bytes (read + write) per decode step of k_decode_persistent on this workload, from an ncu capture
-# of a 3-step launch (profiles/k_decode_persistent_config3.md); a launch of n steps moves n times this.
-TRAFFIC_PER_STEP = 1.2557e9
+# of a 4-step launch (profiles/k_decode_persistent_config3.md); a launch of n steps moves n times this.
+TRAFFIC_PER_STEP = 1.2543e9
 FALLBACK_HBM_GBS = 6650.0
 METRIC = "decode tok/s at batch 1 & 64 (Qwen3.5-style Q4_K_M); GEMV HBM GB/s vs 8 TB/s"
 
