@@ -148,7 +148,7 @@ __global__ void __launch_bounds__(128, 1) k_tc_selftest(const __half *A, const _
 // their partial sums while the tensor cores work.
 constexpr int TC_SUB = 64;                          // K of one half chunk
 constexpr int TC_ROWS = 128, TC_TILES = 8, TC_WARPS = 16;   // two compute warps per tile
-constexpr int TC_THREADS = TC_WARPS * 32 + 32;      // + the producer warp
+constexpr int TC_THREADS = TC_WARPS * 32 + 64;      // + the producer warp and the MMA warp
 constexpr int TC_PLANE_A = TC_ROWS * TC_SUB * 2;    // code plane of a half chunk: 16 KB
 constexpr int TC_PLANE_M = TC_ROWS * 16 * 2;        // Q4_K minimum plane of a half chunk: 4 KB
 constexpr int TC_STAGES = 3;
@@ -159,15 +159,20 @@ constexpr size_t TC_RECV = (size_t)(TC_ROWS + TC_MAXSPLIT) * TC_RS * 4;   // oth
 constexpr int TC_DBUF = TC_ROWS * 4;                // floats of one half's block scales (<= 4 blocks)
 template <int TYPE> constexpr int tc_nacc() { return TYPE == XJ_Q6_K ? 4 : 2; }   // scale blocks per half
 template <int TYPE> constexpr uint32_t tc_cols() { return TYPE == XJ_Q8_0 ? 256u : 512u; }   // TMEM columns
+// half chunks in flight (code planes, accumulator sets): as many as tensor memory and shared memory allow
+template <int TYPE> constexpr int tc_nbuf() { return TYPE == XJ_Q4_K ? 3 : 2; }
 template <int TYPE> constexpr int tc_stage() { return TC_REC + TC_TILES * b64_wbytes<TYPE>(); }
 template <int TYPE> constexpr size_t tc_smem() {
-    return (size_t)TC_STAGES * tc_stage<TYPE>() + 2 * TC_PLANE_A + 2 * TC_PLANE_M + 3 * TC_DBUF * 4;
+    return (size_t)TC_STAGES * tc_stage<TYPE>() + tc_nbuf<TYPE>() * (TC_PLANE_A + TC_PLANE_M + 2 * TC_DBUF * 4);
 }
 static_assert(tc_smem<XJ_Q8_0>() <= 227 * 1024 && tc_smem<XJ_Q6_K>() <= 227 * 1024, "fits one SM");
 static_assert(tc_stage<XJ_Q4_K>() % 128 == 0 && tc_stage<XJ_Q6_K>() % 128 == 0 && tc_stage<XJ_Q8_0>() % 128 == 0, "aligned stages");
 static_assert(TC_PART + TC_RECV <= TC_STAGES * tc_stage<XJ_Q4_K>(), "partials fit the stage area");
-static_assert(2 * 2 * 64 + 64 <= 512 && 2 * 4 * 64 <= 512, "accumulators fit tensor memory");
-using BarTc = BarNamed<1, TC_WARPS * 32>;
+static_assert(3 * 2 * 64 + 64 <= 512 && 2 * 4 * 64 <= 512 && 2 * 2 * 64 <= 256, "accumulators fit tensor memory");
+static_assert(tc_smem<XJ_Q4_K>() <= 227 * 1024, "fits one SM");
+XJ_DEV void tc_arrive(uint64_t *bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" :: "r"(smem_u32(bar)) : "memory");
+}
 
 // Byte of (row r, element k) in a code plane ([128 rows][64 halves], core-matrix layout).
 XJ_DEV uint32_t tc_aoff(int r, int k) { return (uint32_t)((((r >> 3) * (TC_SUB >> 3) + (k >> 3)) << 7) + ((r & 7) << 4) + ((k & 7) << 1)); }
@@ -207,22 +212,21 @@ XJ_DEV void tc_codes(const uint8_t *wst, int tl, int part, int lane, int h, uint
     }
 }
 
-// The block scales of half `h` (`hh`: which half of the K-quant super-block the chunk is) for the rows
-// this thread covers (Q4_K, Q8_0: thread = (row, block) for tid < 256; Q6_K: (row, block) for all 512),
-// into db[row * 4 + block]; Q4_K also writes the row's minimum plane entries (-64 dmin*m as hi, hi, lo
-// per block; columns 6..15 zero).
+// The block scale of item (row, block) = (item / NB, item % NB) of half `h` (`hh`: which half of the
+// K-quant super-block the chunk is) into db[row * 4 + block]; Q4_K also writes the row's minimum plane
+// entries of the block (-64 dmin*m as hi, hi, lo in columns 3b .. 3b + 2; columns 6..15 stay zero).
 template <int TYPE>
-XJ_DEV void tc_scales(const uint8_t *wst0, int tid, int nt, int hh, int h, float *db, uint8_t *mp) {
+XJ_DEV void tc_scales(const uint8_t *wst0, int item, int nt, int hh, int h, float *db, uint8_t *mp) {
     using BG = B64Geo<TYPE>;
     constexpr int WB = b64_wbytes<TYPE>();
     constexpr int NB = tc_nacc<TYPE>();
-    const int row = tid / NB, b = tid % NB;
+    const int row = item / NB, b = item % NB;
     if (row >= TC_ROWS) return;
     const int tl = row >> 4, rt = row & 15;
     if (tl >= nt) {                                        // rows past the matrix: zeros (never stored)
         db[row * 4 + b] = 0.0f;
         if (TYPE == XJ_Q4_K)
-            for (int k = 3 * b; k < (b ? 16 : 3); k++) *reinterpret_cast<__half *>(mp + tc_moff(row, k)) = __float2half_rn(0.0f);
+            for (int k = 3 * b; k < 3 * b + 3; k++) *reinterpret_cast<__half *>(mp + tc_moff(row, k)) = __float2half_rn(0.0f);
         return;
     }
     const uint8_t *wst = wst0 + tl * WB;
@@ -237,8 +241,6 @@ XJ_DEV void tc_scales(const uint8_t *wst0, int tid, int nt, int hh, int h, float
         *reinterpret_cast<__half *>(mp + tc_moff(row, 3 * b)) = mh;
         *reinterpret_cast<__half *>(mp + tc_moff(row, 3 * b + 1)) = mh;
         *reinterpret_cast<__half *>(mp + tc_moff(row, 3 * b + 2)) = ml;
-        if (b == 1)
-            for (int k = 6; k < 16; k++) *reinterpret_cast<__half *>(mp + tc_moff(row, k)) = __float2half_rn(0.0f);
     } else if constexpr (TYPE == XJ_Q6_K) {
         const float d = h2f(ld_u16(wst + BG::Q + BG::H + BG::S + rt * 2));
         const int8_t sc = reinterpret_cast<const int8_t *>(wst + BG::Q + BG::H + rt * 16)[8 * hh + 4 * h + b];
@@ -250,7 +252,9 @@ XJ_DEV void tc_scales(const uint8_t *wst0, int tid, int nt, int hh, int h, float
 
 // Bounded mbarrier wait: the thread sleeps in hardware until the phase completes; gives up (setting
 // *err) after about a second, or at once when *err is set (read every 8 polls, one load in flight), so
-// an error anywhere ends every wait of the grid quickly.
+// an error anywhere ends every wait of the grid quickly. `nap` (ns) > 0 sleeps between polls: the
+// producer and MMA warps share their SM sub-partitions with compute warps, whose issue slots a
+// polling warp would take.
 XJ_DEV bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity) {   // sleeps until the phase completes (or ~0.1 ms)
     uint32_t ok;
     asm volatile("{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, 100000;\n selp.u32 %0, 1, 0, p;\n}"
@@ -262,12 +266,13 @@ XJ_DEV unsigned long long globaltimer_ns() {
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
-XJ_DEV bool tc_wait(uint64_t *bar, uint32_t parity, int *err) {
+XJ_DEV bool tc_wait(uint64_t *bar, uint32_t parity, int *err, int nap = 0) {
     if (mbar_try_wait_sleep(bar, parity)) return true;
     unsigned long long t0;
     asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t0));
     int ev = *(volatile int *)err;
     for (int it = 1; it < (1 << 26); it++) {
+        if (nap) __nanosleep(nap);
         if (mbar_try_wait_sleep(bar, parity)) return true;
         if ((it & 7) == 0) {
             if (ev) return false;
@@ -284,16 +289,17 @@ XJ_DEV bool tc_wait(uint64_t *bar, uint32_t parity, int *err) {
 template <int TYPE>
 __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
     constexpr int WB = b64_wbytes<TYPE>(), SBY = tc_stage<TYPE>(), NB = tc_nacc<TYPE>();
+    constexpr int NBUF = tc_nbuf<TYPE>(), ND = 2 * NBUF;   // plane / accumulator sets, scale buffers
     constexpr bool KQ = TYPE != XJ_Q8_0;
     constexpr uint32_t IDESC = tc_idesc_f16(TC_ROWS, TC_T), NCOL = tc_cols<TYPE>();
     extern __shared__ __align__(1024) uint8_t smem[];
-    uint8_t *aplane = smem + (size_t)TC_STAGES * SBY;                   // [2] code planes
-    uint8_t *mplane = aplane + 2 * TC_PLANE_A;                          // [2] Q4_K minimum planes
-    float *dbuf = reinterpret_cast<float *>(mplane + 2 * TC_PLANE_M);   // [3][128][4] block scales
+    uint8_t *aplane = smem + (size_t)TC_STAGES * SBY;                   // [NBUF] code planes
+    uint8_t *mplane = aplane + NBUF * TC_PLANE_A;                       // [NBUF] Q4_K minimum planes
+    float *dbuf = reinterpret_cast<float *>(mplane + NBUF * TC_PLANE_M);   // [ND][128][4] block scales
     // after the K loop, in the stage area: this CTA's partials, then [ns][ceil(128/ns)][TC_RS] partials
     // of its rows from the other splits (peers send only after every CTA of the cluster left its loop)
     float *recv = reinterpret_cast<float *>(smem + TC_PART);
-    __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], mdone[2], rbar;
+    __shared__ __align__(8) uint64_t full[TC_STAGES], empty[TC_STAGES], mdone[3], ready[3], rbar;
     __shared__ uint32_t s_tmem;
     __shared__ float tok_inv[TC_T];                    // 1 / range scale (a power of two: exact)
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
@@ -342,8 +348,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
     };
     if (tid == 0) {
         for (int q = 0; q < TC_STAGES; q++) { mbar_init(&full[q], 1); mbar_init(&empty[q], 1); }
-        mbar_init(&mdone[0], 1);
-        mbar_init(&mdone[1], 1);
+        for (int q = 0; q < NBUF; q++) { mbar_init(&mdone[q], 1); mbar_init(&ready[q], TC_WARPS); }
         mbar_init(&rbar, 1);
         asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
         if (ns > 1) mbar_expect_tx(&rbar, (uint32_t)((ns - 1) * nr * TC_RS * 4));
@@ -359,13 +364,13 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
     for (int i = 0; i < 16; i++) y[i] = 0.0f;
     const int quarter = warp & 3, tb = (warp >> 2) & 3, crow = 32 * quarter + lane;
     const uint32_t tlane = (uint32_t)(32 * quarter) << 16;
-    // fold half qq's accumulators (buffer qq & 1) into y, scale block by scale block
+    // fold half qq's accumulators (set qq % NBUF) into y, scale block by scale block
     auto fold = [&](int qq) {
-        const float *db = dbuf + (qq % 3) * TC_DBUF + crow * 4;
+        const float *db = dbuf + (qq % ND) * TC_DBUF + crow * 4;
 #pragma unroll
         for (int b = 0; b < NB; b++) {
             float v[16];
-            tc_ld16(tmem + tlane + (uint32_t)(((qq & 1) * NB + b) * 64 + 16 * tb), v);
+            tc_ld16(tmem + tlane + (uint32_t)(((qq % NBUF) * NB + b) * 64 + 16 * tb), v);
             const float sc = db[b];
 #pragma unroll
             for (int i = 0; i < 16; i++) y[i] = fmaf(sc, v[i], y[i]);
@@ -381,7 +386,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
             for (int i = 0; i < TC_STAGES && i < nc; i++) issue_x(i);
         for (int i = TC_STAGES; i < nc && ok; i++) {
             // the stage is free once the MMAs of chunk i - TC_STAGES are done
-            if (lane == 0) ok = tc_wait(&empty[i % TC_STAGES], (uint32_t)(((i / TC_STAGES) - 1) & 1), a.err);
+            if (lane == 0) ok = tc_wait(&empty[i % TC_STAGES], (uint32_t)(((i / TC_STAGES) - 1) & 1), a.err, 256);
             ok = __shfl_sync(0xffffffffu, ok, 0);
             if (!ok) break;
             issue_w(i);
@@ -395,12 +400,62 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
                 while (!mbar_try_wait_sleep(&full[i % TC_STAGES], (uint32_t)((i / TC_STAGES) & 1)))
                     if (globaltimer_ns() - t0 > 100000000ull) break;
             }
+    } else if (warp == TC_WARPS + 1) {
+        // ---- MMA warp (lane 0): per half chunk, once the 16 compute warps have written its code plane
+        // and scales (and folded the half two steps earlier out of the accumulators it reuses), issue its
+        // MMAs with descriptors precomputed here (a descriptor's start address is its low 14 bits, in
+        // 16-byte units, so an offset into the same buffer is an addition).
+        griddep_launch();
+        if (lane == 0) {
+            const uint64_t A0 = tc_desc(smem_u32(aplane), 128, (TC_SUB / 8) * 128);
+            const uint64_t M0 = tc_desc(smem_u32(mplane), 128, 256);
+            const uint64_t B0 = tc_desc(smem_u32(smem), 128, (TC_CK / 8) * 128);
+            const uint64_t S0 = tc_desc(smem_u32(smem) + 2 * TC_PLANE_X, 128, 256);
+            for (int i = 0; i < nc && ok; i++) {
+                const int s = i % TC_STAGES;
+                ok = tc_wait(&full[s], (uint32_t)((i / TC_STAGES) & 1), a.err, 64);
+                for (int h = 0; h < 2 && ok; h++) {
+                    const int q = 2 * i + h, ab = q % NBUF;
+                    ok = tc_wait(&ready[ab], (uint32_t)((q / NBUF) & 1), a.err, 64);
+                    if (!ok) break;
+                    tc_fence_after();
+                    const uint64_t ad0 = A0 + (uint64_t)(ab * (TC_PLANE_A >> 4));
+                    const uint64_t bd0 = B0 + (uint64_t)((s * SBY + 8 * h * 128) >> 4);
+#pragma unroll
+                    for (int ks = 0; ks < TC_SUB / 16; ks++) {
+                        const int b = TYPE == XJ_Q6_K ? ks : ks >> 1;       // scale block of the k-step
+                        const bool first = TYPE == XJ_Q6_K ? true : (ks & 1) == 0;
+                        const uint32_t acc = tmem + (uint32_t)((ab * NB + b) * 64);
+                        const uint64_t ad = ad0 + (uint64_t)(ks * 16), bh = bd0 + (uint64_t)(ks * 16);
+                        tc_mma_f16(acc, ad, bh, IDESC, first ? 0u : 1u);
+                        tc_mma_f16(acc, ad, bh + (uint64_t)(TC_PLANE_X >> 4), IDESC, 1u);
+                    }
+                    if constexpr (TYPE == XJ_Q4_K) {
+                        const uint64_t md = M0 + (uint64_t)(ab * (TC_PLANE_M >> 4));
+                        const uint64_t sd = S0 + (uint64_t)((s * SBY + h * TC_PLANE_S) >> 4);
+                        tc_mma_f16(tmem + (uint32_t)(NBUF * NB * 64), md, sd, IDESC, q > 0 ? 1u : 0u);
+                    }
+                    tc_commit(&mdone[ab]);
+                    if (h == 1) tc_commit(&empty[s]);
+                }
+            }
+        }
+        ok = __shfl_sync(0xffffffffu, ok, 0);
     } else {
         griddep_launch();
         griddep_wait();
-        // every compute thread runs all iterations and meets every named barrier (a failed wait only
-        // skips work; `ok` is kept warp-uniform for the warp-wide tensor-memory loads)
+        // compute warps: per half chunk, fold the half NBUF steps earlier (its MMAs are done), write this
+        // half's code plane and scales, and tell the MMA warp (a failed wait only skips work; `ok` is kept
+        // warp-uniform for the warp-wide tensor-memory loads). A half's MMAs need every warp's arrival,
+        // so warps run at most NBUF halves apart and 2 * NBUF scale buffers never collide.
         const int tl = warp & (TC_TILES - 1), part = warp >> 3;
+        // the minimum planes' columns 6..15 are zero for good (the MMA multiplies them)
+        if (TYPE == XJ_Q4_K)
+            for (int e = tid; e < NBUF * TC_ROWS * 10; e += TC_WARPS * 32)
+                *reinterpret_cast<__half *>(mplane + (e / (TC_ROWS * 10)) * TC_PLANE_M + tc_moff((e / 10) % TC_ROWS, 6 + e % 10)) =
+                    __float2half_rn(0.0f);
+        // scale items: NB per row; Q6_K one per thread, Q4_K / Q8_0 lanes 0..15 of every warp
+        const int item = NB == 4 ? tid : (lane < 16 ? warp * 16 + lane : TC_ROWS * NB);
         for (int i = 0; i < nc; i++) {
             const int s = i % TC_STAGES;
             uint8_t *st = smem + (size_t)s * SBY;
@@ -408,54 +463,34 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
             ok = __all_sync(0xffffffffu, ok);
             const int hh = (c0 + i) & 1;
             for (int h = 0; h < 2; h++) {
-                const int q = 2 * i + h, ab = q & 1;
-                if (q >= 2) {
-                    // half q - 2 is done: its planes are free and its accumulators final
-                    if (ok) ok = tc_wait(&mdone[ab], (uint32_t)(((q - 2) >> 1) & 1), a.err);
+                const int q = 2 * i + h, ab = q % NBUF;
+                if (q >= NBUF) {
+                    // half q - NBUF is done: its planes are free and its accumulators final
+                    if (ok) ok = tc_wait(&mdone[ab], (uint32_t)(((q / NBUF) - 1) & 1), a.err);
                     ok = __all_sync(0xffffffffu, ok);
                     tc_fence_after();
-                    if (ok) fold(q - 2);
+                    if (ok) fold(q - NBUF);
                     tc_fence_before();
                 }
                 uint8_t *ap = aplane + (size_t)ab * TC_PLANE_A, *mp = mplane + (size_t)ab * TC_PLANE_M;
                 if (ok && tl < nt) tc_codes<TYPE>(st + TC_REC + tl * WB, tl, part, lane, h, ap);
-                if (ok) tc_scales<TYPE>(st + TC_REC, tid, nt, hh, h, dbuf + (q % 3) * TC_DBUF, mp);
+                if (ok) tc_scales<TYPE>(st + TC_REC, item, nt, hh, h, dbuf + (q % ND) * TC_DBUF, mp);
                 fence_async_smem();
-                BarTc::sync();
-                if (tid == 0 && ok) {
-                    tc_fence_after();
-                    const uint32_t ao = smem_u32(ap), bo = smem_u32(st);
-#pragma unroll
-                    for (int ks = 0; ks < TC_SUB / 16; ks++) {
-                        const int b = TYPE == XJ_Q6_K ? ks : ks >> 1;       // scale block of the k-step
-                        const bool first = TYPE == XJ_Q6_K ? true : (ks & 1) == 0;
-                        const uint32_t acc = tmem + (uint32_t)((ab * NB + b) * 64);
-                        const uint64_t ad = tc_desc(ao + ks * 256, 128, (TC_SUB / 8) * 128);
-                        const uint32_t bk = bo + (8 * h + 2 * ks) * 128;
-                        const uint64_t bh = tc_desc(bk, 128, (TC_CK / 8) * 128), bl = tc_desc(bk + TC_PLANE_X, 128, (TC_CK / 8) * 128);
-                        tc_mma_f16(acc, ad, bh, IDESC, first ? 0u : 1u);
-                        tc_mma_f16(acc, ad, bl, IDESC, 1u);
-                    }
-                    if constexpr (TYPE == XJ_Q4_K) {
-                        const uint64_t md = tc_desc(smem_u32(mp), 128, 256);
-                        const uint64_t sd = tc_desc(bo + 2 * TC_PLANE_X + h * TC_PLANE_S, 128, 256);
-                        tc_mma_f16(tmem + (uint32_t)(2 * NB * 64), md, sd, IDESC, q > 0 ? 1u : 0u);
-                    }
-                    tc_commit(&mdone[ab]);
-                    if (h == 1) tc_commit(&empty[s]);
-                }
+                tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc_arrive(&ready[ab]);
             }
         }
-        // the last two halves
-        for (int qq = nsub >= 2 ? nsub - 2 : 0; qq < nsub; qq++) {
-            if (ok) ok = tc_wait(&mdone[qq & 1], (uint32_t)((qq >> 1) & 1), a.err);
+        // the last NBUF halves
+        for (int qq = nsub >= NBUF ? nsub - NBUF : 0; qq < nsub; qq++) {
+            if (ok) ok = tc_wait(&mdone[qq % NBUF], (uint32_t)((qq / NBUF) & 1), a.err);
             ok = __all_sync(0xffffffffu, ok);
             tc_fence_after();
             if (ok) fold(qq);
         }
         if (TYPE == XJ_Q4_K && ok) {                       // the minimum term, unscaled
             float v[16];
-            tc_ld16(tmem + tlane + (uint32_t)(2 * NB * 64 + 16 * tb), v);
+            tc_ld16(tmem + tlane + (uint32_t)(NBUF * NB * 64 + 16 * tb), v);
 #pragma unroll
             for (int i = 0; i < 16; i++) y[i] += v[i];
         }
