@@ -444,6 +444,7 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
     } else {
         griddep_launch();
         griddep_wait();
+        if (tid < T) tok_inv[tid] = 1.0f / reinterpret_cast<const float *>((const uint8_t *)a.xbuf + (size_t)nch * TC_REC)[tid];
         // compute warps: per half chunk, fold the half NBUF steps earlier (its MMAs are done), write this
         // half's code plane and scales, and tell the MMA warp (a failed wait only skips work; `ok` is kept
         // warp-uniform for the warp-wide tensor-memory loads). A half's MMAs need every warp's arrival,
@@ -495,8 +496,58 @@ __global__ void __launch_bounds__(TC_THREADS, 1) k_gemm_tc(B64Args a) {
             for (int i = 0; i < 16; i++) y[i] += v[i];
         }
     }
-    if (tid < T) tok_inv[tid] = 1.0f / reinterpret_cast<const float *>((const uint8_t *)a.xbuf + (size_t)nch * TC_REC)[tid];
     const bool allok = __syncthreads_and(ok) != 0;
+    if (ns == 1) {
+        // one CTA per block: the epilogue straight from the partial sums in registers (row crow, tokens
+        // 16 tb .. 16 tb + 15; a warp's lanes are 32 consecutive rows, so each store is coalesced), with
+        // the arithmetic of the split path below
+        const int ch = t0 * 16 + crow;
+        if (warp < TC_WARPS && allok && ch < W.N) {
+            const int epi = jb.epi, ldy = (int)jb.ldy, kc = jb.kc;
+            float *yb = jb.y;
+            if (epi == EPI_CONV) {
+                float wc[9], wl = 0.0f;
+#pragma unroll
+                for (int k = 0; k < 9; k++) wc[k] = k < kc ? jb.conv_w[(size_t)ch * kc + k] : 0.0f;
+#pragma unroll
+                for (int k = 0; k < 9; k++)
+                    if (k == kc - 1) wl = wc[k];
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const int t = 16 * tb + i;
+                    if (t >= T) break;
+                    float *stt = jb.conv_state + t * jb.conv_bstride + (size_t)ch * (kc - 1);
+                    float cs[8];
+#pragma unroll
+                    for (int k = 0; k < 8; k++) cs[k] = k < kc - 1 ? stt[k] : 0.0f;
+                    const float v = (0.0f + y[i]) * tok_inv[t];
+                    float acc = 0.0f;
+#pragma unroll
+                    for (int k = 0; k < 8; k++)
+                        if (k < kc - 1) acc = fmaf(cs[k], wc[k], acc);
+                    acc = fmaf(v, wl, acc);
+#pragma unroll
+                    for (int k = 0; k < 7; k++)
+                        if (k < kc - 2) stt[k] = cs[k + 1];
+                    stt[kc - 2] = v;
+                    yb[(size_t)t * ldy + ch] = silu_f(acc);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; i++) {
+                    const int t = 16 * tb + i;
+                    if (t >= T) break;
+                    const float v = (0.0f + y[i]) * tok_inv[t];
+                    if (epi == EPI_ADD) yb[(size_t)t * ldy + ch] += v;
+                    else yb[(size_t)t * ldy + ch] = v;
+                }
+            }
+        }
+        tc_fence_before();
+        __syncthreads();
+        if (warp == 0) tc_dealloc(tmem, NCOL);
+        return;
+    }
     // ---- partial sums [row][TC_RS] in the stage area (free: every load landed, every MMA is done)
     float *part = reinterpret_cast<float *>(smem);
     if (warp < TC_WARPS && allok) {
