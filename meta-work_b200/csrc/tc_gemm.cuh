@@ -142,10 +142,11 @@ __global__ void __launch_bounds__(128, 1) k_tc_selftest(const __half *A, const _
 // fp32-level like the mma.sync path, and a token's column does not depend on the other tokens.
 //
 // Pipeline: a producer warp bulk-copies each chunk's 8 tiles of quantised bytes and its activation
-// record into a 3-stage ring; per half chunk, 16 compute warps (two per tile) write the code plane
-// (double-buffered), the half's scales (triple-buffered) and the Q4_K minimum plane, thread 0 issues
-// the MMAs and commits to the half's mbarrier, and the warps fold the half two steps earlier into
-// their partial sums while the tensor cores work.
+// record into a 3-stage ring (full / empty mbarriers); per half chunk, 16 compute warps (two per tile)
+// fold the half NBUF steps earlier into their partial sums, write this half's code plane, block scales
+// and Q4_K minimum plane (NBUF = 3 sets for Q4_K, 2 otherwise) and arrive on the half's "ready"
+// mbarrier; an MMA warp waits for it, issues the half's MMAs with precomputed descriptors and commits
+// to the half's "done" mbarrier (and, after a chunk's second half, to the stage's "empty" one).
 constexpr int TC_SUB = 64;                          // K of one half chunk
 constexpr int TC_ROWS = 128, TC_TILES = 8, TC_WARPS = 16;   // two compute warps per tile
 constexpr int TC_THREADS = TC_WARPS * 32 + 64;      // + the producer warp and the MMA warp
