@@ -21,6 +21,7 @@ import importlib.util
 import pathlib
 import subprocess
 import sys
+import tempfile
 
 import numpy as np
 
@@ -112,8 +113,8 @@ def main():
     st, _ = m.spec(p, TINY_N_GEN, 0, max_batch=8, n_ctx=512, s1=3)
     g["tiny_split3"] = st
     # ---- synthetic config 0 ----
-    c0 = HERE.parent.parent / "_work" / "golden_config0.gguf"
-    c0.parent.mkdir(exist_ok=True)
+    tmp = pathlib.Path(tempfile.mkdtemp(prefix="xj_golden_"))   # the synthetic models are not fixtures
+    c0 = tmp / "golden_config0.gguf"
     synth.write_gguf(c0, synth.CONFIG0)
     g["config0_sha256"] = np.frombuffer(hashlib.sha256(c0.read_bytes()).digest(), np.uint8)
     m0 = ref.Model(c0)
@@ -123,7 +124,7 @@ def main():
     g.update(config0_prompt=p0, config0_tokens=tok0, config0_margins=mar0, config0_first_logits=first0,
              config0_trace_hid=hid0, config0_trace_logits=lg0, config0_fingerprint=np.uint64(m0.fingerprint))
     # ---- synthetic mid model (Q4_K / Q6_K, 128-wide heads) ----
-    cm = HERE.parent.parent / "_work" / "golden_mid.gguf"
+    cm = tmp / "golden_mid.gguf"
     synth.write_gguf(cm, synth.MID)
     g["mid_sha256"] = np.frombuffer(hashlib.sha256(cm.read_bytes()).digest(), np.uint8)
     mm = ref.Model(cm)
