@@ -1,6 +1,6 @@
-"""Decode-throughput benchmark of the B200 backend (BASELINE metric: decode tok/s, Qwen3.5-style Q4_K_M).
+"""Decode-throughput benchmark of the B200 backend (metric: decode tok/s, Qwen3.5-style Q4_K_M).
 
-Workload: BASELINE config 3 (~2B-class hybrid, 28 layers = 21 Gated-DeltaNet + 7 gated GQA, E=2048,
+Workload: the ~2B-class hybrid (config 3, 28 layers = 21 Gated-DeltaNet + 7 gated GQA, E=2048,
 FFN 6144, vocab 151936, Q4_K_M with Q6_K head/embeddings), random-init N(0, 0.02) weights written as a
 synthetic GGUF from a fixed seed, a 512-token seeded prompt, greedy decode at batch 1 per sequence.
 A "step" is one greedy decode step of every sequence this rank owns (embedding lookup, 28 layers, LM
@@ -237,7 +237,7 @@ def cpu_baseline(K_cap=24):
 
 
 def run_gdn(xjcuda, peak, peak_kind):
-    """BASELINE config 2, decode: one Gated DeltaNet step of 16 heads x 128x128 fp32 state per sequence
+    """Gated DeltaNet decode (config 2): one Gated DeltaNet step of 16 heads x 128x128 fp32 state per sequence
     at batch 1 and 64 (the batch kernel of batched decode), states rotated over >= 256 MiB so that L2
     cannot serve them. Bytes = state read + written."""
     out = {"workload": "config2 GDN decode, 16 heads, S=128, fp32 state", "unit": "GB/s"}
@@ -257,8 +257,49 @@ def run_gdn(xjcuda, peak, peak_kind):
     return out
 
 
+GEMV_SHAPES = ((2048, 2048), (6144, 2048), (2048, 6144), (151936, 2048))   # rows N x columns K
+
+
+def run_gemv(xjcuda, synth, peak, peak_kind, batches=(1, 4, 16), types=("q4_k", "q6_k", "q8_0"), shapes=GEMV_SHAPES):
+    """Dequant-fused GEMV microbenchmark (config 1): y = W x for W in Q4_K / Q6_K / Q8_0 quantised from
+    seeded N(0, 0.02), shapes N x K of GEMV_SHAPES (the last one the LM head), B = 1, 4, 16 tokens of fp32
+    x. Each launch reads another of >= 256 MiB of distinct device copies of W, so L2 cannot serve the
+    weights; ms = CUDA-event average per launch. Algorithmic bytes = N*K*bpw + B*K*4 + B*N*4."""
+    import numpy as np
+    bpw = {xjcuda.Q4_K: 144 / 256, xjcuda.Q6_K: 210 / 256, xjcuda.Q8_0: 34 / 32}
+    names = {xjcuda.Q4_K: "q4_k", xjcuda.Q6_K: "q6_k", xjcuda.Q8_0: "q8_0"}
+    rng = np.random.default_rng(11)
+    pool = (rng.standard_normal(max(n * k for n, k in shapes), dtype=np.float32) * 0.02)
+    out = {"workload": "config1 GEMV, weights rotated over >= 256 MiB of copies", "unit": "GB/s",
+           "peak": peak, "peak_kind": peak_kind}
+    best = None
+    for t in (xjcuda.Q4_K, xjcuda.Q6_K, xjcuda.Q8_0):
+        if names[t] not in types:
+            continue
+        for n, k in shapes:
+            raw = synth.quantize_row(t, pool[:n * k])
+            wbytes = len(raw)
+            copies = max(2, -(-(256 << 20) // wbytes))
+            for B in batches:
+                ms = xjcuda.gemv_time(t, raw, k, n, T=B, copies=copies, iters=40)
+                nbytes = n * k * bpw[t] + B * k * 4 + B * n * 4
+                gbs = nbytes / (ms / 1e3) / 1e9
+                key = f"{names[t]}_{n}x{k}_b{B}"
+                out[key] = {"us": round(ms * 1e3, 2), "achieved": round(gbs, 1), "frac": round(gbs / peak, 4)}
+                if best is None or gbs > best[1]:
+                    best = (key, gbs)
+    out["best"] = {"case": best[0], "frac": round(best[1] / peak, 4)}
+    return out
+
+
+def gemv_kw(args) -> dict:
+    return {"types": tuple(args.gemv_types.split(",")),
+            "shapes": GEMV_SHAPES if args.gemv_shapes == "all" else GEMV_SHAPES[-1:],
+            "batches": tuple(int(b) for b in args.gemv_batches.split(","))}
+
+
 def run_spec(args, model, rank, world, barrier, xjcuda, synth, local):
-    """greedy speculative decoding, target = config 3, draft = the E=1024 8-layer Q8_0
+    """Speculative decoding (config 4): greedy speculative decoding, target = config 3, draft = the E=1024 8-layer Q8_0
     model with the target's vocabulary, k = 4; args.spec seeded 256-token prompts per GPU, 256 tokens each.
     Output ids equal plain greedy decoding by construction (tested); reports emitted tokens/s and target
     forwards/s over the whole job (prompt processing included), and the acceptance of drafted tokens."""
@@ -340,7 +381,7 @@ def run_batch(args, cfg, model, rank, world, barrier, xjcuda):
         "roofline": {"bound": "hbm", "kernel": "decode-step CUDA graph (batched)", "achieved": round(achieved, 1),
                      "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "traffic": None,
                      "bytes_per_step": round(step_total), "peak_kind": peak_kind},
-        # the BASELINE wording: weight + KV bytes per token over the nominal 8 TB/s (roofline.frac above
+        # the north-star wording: weight + KV bytes per token over the nominal 8 TB/s (roofline.frac above
         # also counts the recurrent state and uses the measured copy bandwidth)
         "baseline_roofline": {"bytes_per_token": round((b["weights"] + B * b["kv"]) / B),
                               "frac_of_8tbs": round((b["weights"] + B * b["kv"]) / (t_max / args.steps / 1e3) / 8e12, 4)},
@@ -408,12 +449,18 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--gemv", type=int, default=1, help="run the config-1 GEMV microbenchmark on rank 0 (0: skip)")
+    ap.add_argument("--only", choices=["gemv"], default=None,
+                    help="run only this microbenchmark (one GPU; e.g. under a profiler) and print its JSON")
+    ap.add_argument("--gemv-types", default="q4_k,q6_k,q8_0")
+    ap.add_argument("--gemv-shapes", default="all", help="'all' or 'lm' (the 151936 x 2048 LM head only)")
+    ap.add_argument("--gemv-batches", default="1,4,16")
     ap.add_argument("--batch", type=int, default=64, help="sequences of the batched-decode measurement (0: skip)")
     ap.add_argument("--pipeline", action="store_true",
                     help="under torchrun: one layer range per GPU (NCCL layer pipeline) on --batch sequences")
     ap.add_argument("--micro-batches", type=int, default=2)
     ap.add_argument("--spec", type=int, default=0,
-                    help="BASELINE config 4: speculative decoding of this many 256-token prompts per GPU (0: skip)")
+                    help="config 4: speculative decoding of this many 256-token prompts per GPU (0: skip)")
     args = ap.parse_args()
     rank, local, world = dist_env()
     load_pkg()
@@ -424,6 +471,11 @@ def main():
     torch.cuda.set_device(local)
     if args.pipeline:
         return run_pipeline(args, rank, local, world)
+    if args.only == "gemv":
+        from xjb200 import synth, xjcuda
+        peak, peak_kind = hbm_peak()
+        print(json.dumps({"gemv": run_gemv(xjcuda, synth, peak, peak_kind, **gemv_kw(args))}))
+        return
     if world > 1:
         import datetime
         import torch.distributed as dist
@@ -497,7 +549,7 @@ def main():
                          "traffic": round(TRAFFIC_PER_STEP * n_kern) if persistent else None,
                          "algorithmic_bytes": round(b["total"] * n_kern), "units": f"{n_kern} decode steps",
                          "launch_ms": round(kern_ms, 4), "peak_kind": peak_kind},
-            # the BASELINE wording: weight + KV bytes per token over the nominal 8 TB/s (roofline.frac
+            # the north-star wording: weight + KV bytes per token over the nominal 8 TB/s (roofline.frac
             # also counts the recurrent state and uses the measured copy bandwidth)
             "baseline_roofline": {"bytes_per_token": round(b["weights"] + b["kv"]),
                                   "frac_of_8tbs": round((b["weights"] + b["kv"]) * args.steps / (t_max / 1e3) / 8e12, 4)},
@@ -508,6 +560,8 @@ def main():
         if batch_line:
             line["batch"] = batch_line
         line["gdn"] = run_gdn(xjcuda, peak, peak_kind)
+        if args.gemv:
+            line["gemv"] = run_gemv(xjcuda, synth, peak, peak_kind, **gemv_kw(args))
         if spec_line:
             line["spec"] = spec_line
         if world == 1 and not args.no_cpu_baseline:

@@ -42,7 +42,7 @@ uint64_t xjc_stage_state_bytes(const xj_model *m, int l0, int l1, int n_ctx, int
 
 // Options (process-wide, read when a stage is created):
 //   XJC_OPT_KV_F32   1 = float32 KV cache (matches the CPU oracle's cache), 0 = float16 (default,
-//                    the Metal backend's and the BASELINE precision).
+//                    the Metal backend's precision).
 //   XJC_OPT_GEMV     0 = fastest path per type (default), 1 = generic per-element path for every type.
 //   XJC_OPT_PDL      1 = kernels of a step overlap through programmatic dependent launch (default),
 //                    0 = each kernel starts after its predecessor completes.
@@ -77,7 +77,7 @@ int xj_cuda_gemv(int type, const void *w, int k, int n, const float *x, int T, f
 // distinct device copies of W, so the last-level cache cannot serve the weights (GEMV microbenchmark).
 int xj_cuda_gemv_time(int type, const void *w, int k, int n, int T, int copies, int iters, int path, float *ms,
                       char *err, size_t errlen);
-// Greedy speculative decoding with a separate draft model: both stages take the
+// Greedy speculative decoding with a separate draft model (e.g. a small Q8_0 drafter for a Q4_K_M target): both stages take the
 // prompt, then each round the draft proposes k tokens (device greedy decode), the target verifies the
 // last emitted token and the k drafts in one forward (k + 1 rows of logits, device greedy picks), the
 // longest agreeing prefix plus the target's own next pick are emitted, the target rolls back through its
@@ -88,14 +88,24 @@ int xj_cuda_gemv_time(int type, const void *w, int k, int n, int T, int copies, 
 int xj_cuda_spec_decode(xj_stage *target, xj_stage *draft, const int32_t *prompt, int n_prompt, int n_gen, int k,
                         int32_t *out, long long *stats, char *err, size_t errlen);
 
-// Gated DeltaNet decode microbenchmark: average device time (ms) of one decode step
+// Gated DeltaNet decode microbenchmark (e.g. 16 heads x 128 x 128 state): average device time (ms) of one decode step
 // of B sequences x Hv heads with an S x S fp32 state each (S in 16, 32, 64, 128), the batch kernel of
 // batched decode, states rotated over >= 256 MiB of copies so the last-level cache cannot serve them.
 int xj_cuda_gdn_time(int S, int Hv, int B, int iters, float *ms, char *err, size_t errlen);
-// Gated DeltaNet over a prompt of T tokens (BASELINE config 2, prefill): the chunked kernels that prompt
+// Gated DeltaNet over a prompt of T tokens (prefill): the chunked kernels that prompt
 // forwards of 32 or more tokens use, against the token-by-token kernel on the same synthetic operands.
 // res[4] = max relative difference of the outputs, of the final state, chunked ms, token-by-token ms.
 int xj_cuda_gdn_prefill_check(int S, int Hk, int Hv, int T, float *res, char *err, size_t errlen);
+
+// Gated DeltaNet recurrence on caller operands (host buffers), for parity against a host restatement of
+// core/xj_cpu.c:194-219 (the loop inside attn_linear, after the projections and the convolution).
+// path 0 = token-by-token kernel over T tokens of one sequence, 1 = chunked prefill kernels (S >= 32),
+// 2 = batch decode kernel, T independent sequences of one token each. qkv [T][2*Hk*S + Hv*S] (q, k, v
+// after convolution + SiLU), z [T][Hv*S] raw gate, beta / alpha [T][Hv] logits, dt / A [Hv], norm_w [S];
+// state [Hv][S][S] (path 2: [T][Hv][S][S]) in and out, out [T][Hv*S] after the gated RMSNorm.
+int xj_cuda_gdn_run(int path, int S, int Hk, int Hv, int T, const float *qkv, const float *z, const float *beta,
+                    const float *alpha, const float *dt, const float *A, const float *norm_w, float eps, float *state,
+                    float *out, char *err, size_t errlen);
 
 // Number of kernel launches in one replay of the stage's cached decode-step graph (0 before the first
 // xj_cuda_decode call that generated more than one token).

@@ -102,7 +102,7 @@ constexpr size_t MK_SMEM = (size_t)MK_NS * MK_SLOT + MK_XS_BYTES + 2 * (MK_KMAX 
 
 XJ_DEV unsigned long long globaltimer() {
     unsigned long long t;
-    asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
     return t;
 }
 XJ_DEV unsigned ld_acquire(const unsigned *p) {

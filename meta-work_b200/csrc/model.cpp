@@ -217,20 +217,28 @@ bool get_arr_u32(const gguf_file *f, const char *key, uint64_t i, uint32_t *out)
     return es && scalar_u32(kv->arr_type, kv->data + 12 + i * (uint64_t)es, out);
 }
 
-bool get_w(const gguf_file *g, const char *name, xj_w *w, bool required, char *err, size_t errlen) {
+// ------------------------------------------------------------------ the model description
+// The loader is driven by tables: which metadata keys fill which hyperparameter, which tensors each kind
+// of layer owns and what each must satisfy, which vocabulary strings name the special tokens, and which
+// tensors the MTP head adds. One walker per table applies the rules, so the loader's behaviour can be
+// read off the tables below. The rules are the runtime's (tensor names and dtype/shape requirements of
+// core/xj_model.c:62-101 and :104-127, hyperparameters of :129-172); the structural fingerprint is the
+// runtime's formula (:188-197), which pipeline peers compare.
+
+// Where a tensor points into the mapped file (or a failure message).
+bool bind_tensor(const gguf_file *g, const char *name, xj_w *w, bool must_exist, char *err, size_t errlen) {
     memset(w, 0, sizeof(*w));
     const gguf_tensor *t = find_tensor(g, name);
     if (!t) {
-        if (required) seterr(err, errlen, "model has no tensor %s", name);
-        return !required;
+        if (must_exist) seterr(err, errlen, "model has no tensor %s", name);
+        return !must_exist;
     }
-    if (t->type != XJ_F32 && t->type != XJ_F16 && t->type != XJ_BF16 && t->type != XJ_Q8_0 && t->type != XJ_Q4_K &&
-        t->type != XJ_Q5_K && t->type != XJ_Q6_K) {
-        seterr(err, errlen, "tensor %s has unsupported type %u", name, t->type);
-        return false;
-    }
-    w->data = g->map + (g->data_off + t->offset - g->map_off);
+    static const uint32_t kTypes[] = {XJ_F32, XJ_F16, XJ_BF16, XJ_Q8_0, XJ_Q4_K, XJ_Q5_K, XJ_Q6_K};
+    bool known = false;
+    for (uint32_t ty : kTypes) known = known || t->type == ty;
+    if (!known) { seterr(err, errlen, "tensor %s has unsupported type %u", name, t->type); return false; }
     w->file_off = g->data_off + t->offset;
+    w->data = g->map + (w->file_off - g->map_off);
     w->nbytes = t->nbytes;
     w->type = t->type;
     w->ne0 = t->ne[0];
@@ -238,44 +246,191 @@ bool get_w(const gguf_file *g, const char *name, xj_w *w, bool required, char *e
     return true;
 }
 
-bool load_layer(const gguf_file *g, const xj_hparams *hp, int i, xj_layer *L, char *err, size_t errlen) {
-    char name[96];
-#define W(field, suffix, req) do { snprintf(name, sizeof name, "blk.%d.%s", i, suffix); \
-        if (!get_w(g, name, &L->field, req, err, errlen)) return false; } while (0)
-    W(attn_norm, "attn_norm.weight", true);
-    W(post_norm, "post_attention_norm.weight", true);
-    W(ffn_gate, "ffn_gate.weight", true);
-    W(ffn_up, "ffn_up.weight", true);
-    W(ffn_down, "ffn_down.weight", true);
-    if (L->recurrent) {
-        W(ssm_qkv, "attn_qkv.weight", true);
-        W(ssm_gate, "attn_gate.weight", true);
-        W(ssm_conv1d, "ssm_conv1d.weight", true);
-        W(ssm_dt, "ssm_dt.bias", true);
-        W(ssm_a, "ssm_a", true);
-        W(ssm_beta, "ssm_beta.weight", true);
-        W(ssm_alpha, "ssm_alpha.weight", true);
-        W(ssm_norm, "ssm_norm.weight", true);
-        W(ssm_out, "ssm_out.weight", true);
-        if (L->ssm_qkv.ne1 != hp->conv_dim || L->ssm_conv1d.type != XJ_F32 || L->ssm_conv1d.ne0 != hp->conv_k) {
-            seterr(err, errlen, "layer %d: linear-attention tensor shapes do not match", i); return false;
-        }
-        if (L->ssm_a.type != XJ_F32 || L->ssm_dt.type != XJ_F32 || L->ssm_norm.type != XJ_F32) {
-            seterr(err, errlen, "layer %d: ssm_a / ssm_dt / ssm_norm must be F32", i); return false;
-        }
-    } else {
-        W(wqkv, "attn_qkv.weight", false);
-        if (!L->wqkv.nbytes) {
-            W(wq, "attn_q.weight", true);
-            W(wk, "attn_k.weight", true);
-            W(wv, "attn_v.weight", true);
-        }
-        W(wo, "attn_output.weight", true);
-        W(q_norm, "attn_q_norm.weight", true);
-        W(k_norm, "attn_k_norm.weight", true);
+// Layer kinds a tensor rule applies to.
+enum class Kind : uint8_t { Every, Linear, Full };
+// When a tensor must be present.
+enum class Need : uint8_t { Always, Optional, WithoutFusedQkv };
+// What it must satisfy once bound.
+enum class Rule : uint8_t { None, F32, RowsConvDim, F32ColsConvK };
+
+struct LayerTensor {
+    xj_w xj_layer::*field;
+    const char *suffix;   // after "blk.<i>."
+    Kind kind;
+    Need need;
+    Rule rule;
+};
+
+const LayerTensor kLayerTensors[] = {
+    {&xj_layer::attn_norm, "attn_norm.weight", Kind::Every, Need::Always, Rule::F32},
+    {&xj_layer::post_norm, "post_attention_norm.weight", Kind::Every, Need::Always, Rule::F32},
+    {&xj_layer::ffn_gate, "ffn_gate.weight", Kind::Every, Need::Always, Rule::None},
+    {&xj_layer::ffn_up, "ffn_up.weight", Kind::Every, Need::Always, Rule::None},
+    {&xj_layer::ffn_down, "ffn_down.weight", Kind::Every, Need::Always, Rule::None},
+    // Gated DeltaNet layers
+    {&xj_layer::ssm_qkv, "attn_qkv.weight", Kind::Linear, Need::Always, Rule::RowsConvDim},
+    {&xj_layer::ssm_gate, "attn_gate.weight", Kind::Linear, Need::Always, Rule::None},
+    {&xj_layer::ssm_conv1d, "ssm_conv1d.weight", Kind::Linear, Need::Always, Rule::F32ColsConvK},
+    {&xj_layer::ssm_dt, "ssm_dt.bias", Kind::Linear, Need::Always, Rule::F32},
+    {&xj_layer::ssm_a, "ssm_a", Kind::Linear, Need::Always, Rule::F32},
+    {&xj_layer::ssm_beta, "ssm_beta.weight", Kind::Linear, Need::Always, Rule::None},
+    {&xj_layer::ssm_alpha, "ssm_alpha.weight", Kind::Linear, Need::Always, Rule::None},
+    {&xj_layer::ssm_norm, "ssm_norm.weight", Kind::Linear, Need::Always, Rule::F32},
+    {&xj_layer::ssm_out, "ssm_out.weight", Kind::Linear, Need::Always, Rule::None},
+    // gated full-attention layers: a fused q|k|v matrix, or the three separate ones
+    {&xj_layer::wqkv, "attn_qkv.weight", Kind::Full, Need::Optional, Rule::None},
+    {&xj_layer::wq, "attn_q.weight", Kind::Full, Need::WithoutFusedQkv, Rule::None},
+    {&xj_layer::wk, "attn_k.weight", Kind::Full, Need::WithoutFusedQkv, Rule::None},
+    {&xj_layer::wv, "attn_v.weight", Kind::Full, Need::WithoutFusedQkv, Rule::None},
+    {&xj_layer::wo, "attn_output.weight", Kind::Full, Need::Always, Rule::None},
+    {&xj_layer::q_norm, "attn_q_norm.weight", Kind::Full, Need::Always, Rule::None},
+    {&xj_layer::k_norm, "attn_k_norm.weight", Kind::Full, Need::Always, Rule::None},
+};
+
+bool rule_holds(Rule r, const xj_w &w, const xj_hparams *hp) {
+    switch (r) {
+    case Rule::None: return true;
+    case Rule::F32: return w.type == XJ_F32;
+    case Rule::RowsConvDim: return w.ne1 == hp->conv_dim;
+    case Rule::F32ColsConvK: return w.type == XJ_F32 && w.ne0 == hp->conv_k;
     }
-    if (L->attn_norm.type != XJ_F32 || L->post_norm.type != XJ_F32) { seterr(err, errlen, "layer %d: norms must be F32", i); return false; }
-#undef W
+    return false;
+}
+
+// Binds the tensors of file block `blk` into *L (whose `recurrent` flag is already set).
+bool bind_layer(const gguf_file *g, const xj_hparams *hp, int blk, xj_layer *L, char *err, size_t errlen) {
+    char name[96];
+    for (const LayerTensor &t : kLayerTensors) {
+        if ((t.kind == Kind::Linear && !L->recurrent) || (t.kind == Kind::Full && L->recurrent)) continue;
+        if (t.need == Need::WithoutFusedQkv && L->wqkv.nbytes) continue;
+        snprintf(name, sizeof name, "blk.%d.%s", blk, t.suffix);
+        xj_w &w = L->*t.field;
+        if (!bind_tensor(g, name, &w, t.need != Need::Optional, err, errlen)) return false;
+        if (w.nbytes && !rule_holds(t.rule, w, hp)) {
+            seterr(err, errlen, "tensor %s: %s", name,
+                   t.rule == Rule::F32 ? "must be F32" : t.rule == Rule::RowsConvDim ? "rows differ from the conv channels"
+                                                                                      : "must be F32 with conv_k columns");
+            return false;
+        }
+    }
+    return true;
+}
+
+// Hyperparameters read from "qwen35.<suffix>" metadata. Keys without a default must be present.
+struct Raw { uint32_t block_count, key_len, val_len, nextn; };
+struct HpKey {
+    const char *suffix;
+    int xj_hparams::*field;   // or, when null, a slot of Raw
+    uint32_t Raw::*raw;
+    bool required;
+    uint32_t dflt;
+};
+const HpKey kHpKeys[] = {
+    {"block_count", nullptr, &Raw::block_count, true, 0},
+    {"embedding_length", &xj_hparams::n_embd, nullptr, true, 0},
+    {"feed_forward_length", &xj_hparams::n_ff, nullptr, true, 0},
+    {"attention.head_count", &xj_hparams::n_head, nullptr, true, 0},
+    {"attention.head_count_kv", &xj_hparams::n_head_kv, nullptr, true, 0},
+    {"attention.key_length", nullptr, &Raw::key_len, true, 0},
+    {"attention.value_length", nullptr, &Raw::val_len, true, 0},
+    {"rope.dimension_count", &xj_hparams::n_rot, nullptr, true, 0},
+    {"ssm.conv_kernel", &xj_hparams::conv_k, nullptr, true, 0},
+    {"ssm.inner_size", &xj_hparams::d_inner, nullptr, true, 0},
+    {"ssm.state_size", &xj_hparams::s_k, nullptr, true, 0},
+    {"ssm.group_count", &xj_hparams::h_k, nullptr, true, 0},
+    {"ssm.time_step_rank", &xj_hparams::h_v, nullptr, true, 0},
+    {"nextn_predict_layers", nullptr, &Raw::nextn, false, 0},
+    {"full_attention_interval", &xj_hparams::full_attn_interval, nullptr, false, 4},
+};
+// Float hyperparameters with their defaults.
+const struct { const char *suffix; float xj_hparams::*field; float dflt; } kHpFloats[] = {
+    {"rope.freq_base", &xj_hparams::rope_base, 10000.0f},
+    {"attention.layer_norm_rms_epsilon", &xj_hparams::eps, 1e-6f},
+};
+
+bool read_hparams(const gguf_file *g, xj_hparams *hp, Raw *raw, char *err, size_t errlen) {
+    char key[128];
+    for (const HpKey &k : kHpKeys) {
+        snprintf(key, sizeof key, "qwen35.%s", k.suffix);
+        uint32_t v = k.dflt;
+        if (!get_u32(g, key, &v) && k.required) { seterr(err, errlen, "model is missing %s", key); return false; }
+        if (k.field) hp->*k.field = (int)v;
+        else raw->*k.raw = v;
+    }
+    for (const auto &k : kHpFloats) {
+        snprintf(key, sizeof key, "qwen35.%s", k.suffix);
+        hp->*k.field = k.dflt;
+        get_f32(g, key, &(hp->*k.field));
+    }
+    // derived sizes, then the consistency conditions the kernels rely on
+    hp->n_layer = (int)raw->block_count - (int)raw->nextn;     // the MTP block is not a decoder layer
+    hp->head_dim = (int)raw->key_len;
+    hp->s_v = hp->h_v > 0 ? hp->d_inner / hp->h_v : 0;
+    hp->key_dim = hp->s_k * hp->h_k;
+    hp->conv_dim = 2 * hp->key_dim + hp->d_inner;
+    const struct { bool bad; const char *why; } conds[] = {
+        {raw->key_len != raw->val_len, "key and value head dims differ"},
+        {hp->h_v <= 0 || hp->h_k <= 0, "bad linear-attention head counts"},
+        {hp->s_v != hp->s_k, "linear-attention key and value head dims differ"},
+        {hp->h_k > 0 && hp->h_v % hp->h_k != 0, "value heads are not a multiple of key heads"},
+        {hp->n_layer <= 0 || hp->n_layer > XJ_MAX_LAYERS, "bad layer count"},
+        {hp->n_rot > hp->head_dim || hp->n_rot % 2 != 0, "bad rope dimension"},
+    };
+    for (const auto &c : conds)
+        if (c.bad) { seterr(err, errlen, "%s", c.why); return false; }
+    return true;
+}
+
+// Special tokens: the eos id from metadata, then vocabulary strings; the chat end token takes the last
+// match, the text end token fills eos only when the metadata left it unset. n_vocab = vocabulary size.
+void read_specials(const gguf_file *g, xj_hparams *hp) {
+    const struct { const char *text; uint32_t xj_hparams::*field; bool only_if_unset; } kSpecial[] = {
+        {"<|im_end|>", &xj_hparams::eot, false},
+        {"<|endoftext|>", &xj_hparams::eos, true},
+    };
+    hp->eos = hp->eot = UINT32_MAX;
+    uint32_t id;
+    if (get_u32(g, "tokenizer.ggml.eos_token_id", &id)) hp->eos = id;
+    const gguf_kv *kv = find_kv(g, "tokenizer.ggml.tokens");
+    if (!kv || kv->type != GGUF_ARR || kv->arr_type != GGUF_STR) return;
+    const uint8_t *p = kv->data + 12;
+    for (uint64_t i = 0; i < kv->arr_n; i++) {
+        uint64_t n;
+        memcpy(&n, p, 8);
+        for (const auto &sp : kSpecial)
+            if (n == strlen(sp.text) && memcmp(p + 8, sp.text, n) == 0 && (!sp.only_if_unset || hp->*sp.field == UINT32_MAX))
+                hp->*sp.field = (uint32_t)i;
+        p += 8 + n;
+    }
+    hp->n_vocab = (int)kv->arr_n;
+}
+
+// The MTP head's own tensors ("blk.<last>.nextn.<suffix>").
+const struct { xj_w xj_model::*field; const char *suffix; Rule rule; } kMtpTensors[] = {
+    {&xj_model::mtp_eh, "eh_proj.weight", Rule::None},
+    {&xj_model::mtp_enorm, "enorm.weight", Rule::F32},
+    {&xj_model::mtp_hnorm, "hnorm.weight", Rule::F32},
+    {&xj_model::mtp_head_norm, "shared_head_norm.weight", Rule::F32},
+};
+
+bool bind_mtp(const gguf_file *g, xj_model *m, int blk, char *err, size_t errlen) {
+    const int il = m->hp.n_layer;                 // the MTP layer sits after the decoder layers
+    if (il + 1 > XJ_MAX_LAYERS) { seterr(err, errlen, "too many layers"); return false; }
+    xj_layer *L = &m->layers[il];
+    memset(L, 0, sizeof(*L));
+    if (!bind_layer(g, &m->hp, blk, L, err, errlen)) return false;
+    char name[96];
+    for (const auto &t : kMtpTensors) {
+        snprintf(name, sizeof name, "blk.%d.nextn.%s", blk, t.suffix);
+        xj_w &w = m->*t.field;
+        if (!bind_tensor(g, name, &w, true, err, errlen)) return false;
+        if (!rule_holds(t.rule, w, &m->hp)) { seterr(err, errlen, "tensor %s must be F32", name); return false; }
+    }
+    if (m->mtp_eh.ne0 != 2 * m->hp.n_embd || m->mtp_eh.ne1 != m->hp.n_embd) {
+        seterr(err, errlen, "MTP eh_proj has the wrong shape");
+        return false;
+    }
+    m->has_mtp = true;
     return true;
 }
 
@@ -285,6 +440,59 @@ uint64_t fnv(uint64_t h, const void *p, size_t n) {
     return h;
 }
 
+// Structural fingerprint: FNV-1a over the hyperparameters and every tensor's name, type, shape and
+// offset (the runtime's formula, so that pipeline peers loaded by either loader agree).
+uint64_t structure_fingerprint(const gguf_file *g, const xj_hparams *hp) {
+    uint64_t h = fnv(1469598103934665603ull, hp, sizeof(*hp));
+    for (uint64_t i = 0; i < g->n_tensors; i++) {
+        const gguf_tensor *t = &g->tensors[i];
+        h = fnv(h, t->name, strlen(t->name));
+        h = fnv(h, &t->type, sizeof t->type);
+        h = fnv(h, t->ne, sizeof t->ne);
+        h = fnv(h, &t->offset, sizeof t->offset);
+    }
+    return h;
+}
+
+bool is_qwen35(const gguf_file *g) {
+    const gguf_kv *kv = find_kv(g, "general.architecture");
+    if (!kv || kv->type != GGUF_STR) return false;
+    uint64_t n;
+    memcpy(&n, kv->data, 8);
+    return n == 6 && memcmp(kv->data + 8, "qwen35", 6) == 0;
+}
+
+xj_model *build_model(gguf_file *g, char *err, size_t errlen) {
+    if (!is_qwen35(g)) { seterr(err, errlen, "not a Qwen3.5 model (general.architecture must be qwen35)"); return nullptr; }
+    xj_model *m = (xj_model *)calloc(1, sizeof(xj_model));
+    m->gguf = g;
+    xj_hparams *hp = &m->hp;
+    Raw raw{};
+    bool ok = read_hparams(g, hp, &raw, err, errlen);
+    if (ok) {
+        read_specials(g, hp);
+        // layer kinds: the explicit per-layer flags when present, else every full_attn_interval-th layer
+        // is full attention
+        for (int i = 0; i < hp->n_layer; i++) {
+            uint32_t r;
+            m->layers[i].recurrent = get_arr_u32(g, "qwen35.attention.recurrent_layers", (uint64_t)i, &r)
+                                         ? r != 0 : (i + 1) % hp->full_attn_interval != 0;
+        }
+        ok = bind_tensor(g, "token_embd.weight", &m->tok_embd, true, err, errlen) &&
+             bind_tensor(g, "output_norm.weight", &m->output_norm, true, err, errlen) &&
+             bind_tensor(g, "output.weight", &m->output, false, err, errlen);
+    }
+    if (ok) {
+        if (!m->output.nbytes) m->output = m->tok_embd;     // tied output
+        if (!hp->n_vocab) hp->n_vocab = (int)m->tok_embd.ne1;
+        for (int i = 0; ok && i < hp->n_layer; i++) ok = bind_layer(g, hp, i, &m->layers[i], err, errlen);
+    }
+    if (ok && raw.nextn > 0) ok = bind_mtp(g, m, (int)raw.block_count - 1, err, errlen);
+    if (!ok) { free(m); return nullptr; }
+    m->fingerprint = structure_fingerprint(g, hp);
+    return m;
+}
+
 }  // namespace
 
 extern "C" {
@@ -292,116 +500,9 @@ extern "C" {
 xj_model *xjc_model_load(const char *path, char *err, size_t errlen) {
     gguf_file *g = gguf_open_file(path, err, errlen);
     if (!g) return nullptr;
-    const gguf_kv *akv = find_kv(g, "general.architecture");
-    uint64_t alen = 0;
-    if (akv && akv->type == GGUF_STR) memcpy(&alen, akv->data, 8);
-    if (!akv || akv->type != GGUF_STR || alen != 6 || memcmp(akv->data + 8, "qwen35", 6) != 0) {
-        seterr(err, errlen, "not a Qwen3.5 model (general.architecture must be qwen35)");
-        gguf_free(g); return nullptr;
-    }
-    xj_model *m = (xj_model *)calloc(1, sizeof(xj_model));
-    m->gguf = g;
-    xj_hparams *hp = &m->hp;
-    uint32_t block_count, key_len, val_len, v;
-    int nextn = 0;
-    struct { const char *k; void *dst; } req[] = {
-        {"qwen35.block_count", &block_count}, {"qwen35.embedding_length", &hp->n_embd},
-        {"qwen35.feed_forward_length", &hp->n_ff}, {"qwen35.attention.head_count", &hp->n_head},
-        {"qwen35.attention.head_count_kv", &hp->n_head_kv}, {"qwen35.attention.key_length", &key_len},
-        {"qwen35.attention.value_length", &val_len}, {"qwen35.rope.dimension_count", &hp->n_rot},
-        {"qwen35.ssm.conv_kernel", &hp->conv_k}, {"qwen35.ssm.inner_size", &hp->d_inner},
-        {"qwen35.ssm.state_size", &hp->s_k}, {"qwen35.ssm.group_count", &hp->h_k},
-        {"qwen35.ssm.time_step_rank", &hp->h_v},
-    };
-    for (auto &q : req) {
-        if (!get_u32(g, q.k, &v)) { seterr(err, errlen, "model is missing %s", q.k); goto fail; }
-        memcpy(q.dst, &v, 4);
-    }
-    if (get_u32(g, "qwen35.nextn_predict_layers", &v)) nextn = (int)v;
-    hp->n_layer = (int)block_count - nextn;
-    hp->full_attn_interval = 4;
-    if (get_u32(g, "qwen35.full_attention_interval", &v)) hp->full_attn_interval = (int)v;
-    hp->rope_base = 10000.0f;
-    get_f32(g, "qwen35.rope.freq_base", &hp->rope_base);
-    hp->eps = 1e-6f;
-    get_f32(g, "qwen35.attention.layer_norm_rms_epsilon", &hp->eps);
-    if (key_len != val_len) { seterr(err, errlen, "key/value head dims differ (%u/%u)", key_len, val_len); goto fail; }
-    hp->head_dim = (int)key_len;
-    if (hp->h_v <= 0 || hp->h_k <= 0) { seterr(err, errlen, "bad linear-attention head counts"); goto fail; }
-    hp->s_v = hp->d_inner / hp->h_v;
-    if (hp->s_v != hp->s_k) { seterr(err, errlen, "linear-attention key/value head dims differ"); goto fail; }
-    if (hp->h_v % hp->h_k) { seterr(err, errlen, "value heads are not a multiple of key heads"); goto fail; }
-    hp->key_dim = hp->s_k * hp->h_k;
-    hp->conv_dim = 2 * hp->key_dim + hp->d_inner;
-    if (hp->n_layer <= 0 || hp->n_layer > XJ_MAX_LAYERS) { seterr(err, errlen, "bad layer count %d", hp->n_layer); goto fail; }
-    if (hp->n_rot > hp->head_dim || hp->n_rot % 2) { seterr(err, errlen, "bad rope dimension %d", hp->n_rot); goto fail; }
-    {
-        // special tokens by string, as the runtime does (xj_model.c:44-59)
-        const gguf_kv *kv = find_kv(g, "tokenizer.ggml.tokens");
-        hp->eos = hp->eot = UINT32_MAX;
-        uint32_t eos;
-        if (get_u32(g, "tokenizer.ggml.eos_token_id", &eos)) hp->eos = eos;
-        if (kv && kv->type == GGUF_ARR && kv->arr_type == GGUF_STR) {
-            const uint8_t *p = kv->data + 12;
-            for (uint64_t i = 0; i < kv->arr_n; i++) {
-                uint64_t n; memcpy(&n, p, 8);
-                const char *s = (const char *)p + 8;
-                if (n == 10 && memcmp(s, "<|im_end|>", 10) == 0) hp->eot = (uint32_t)i;
-                if (n == 13 && memcmp(s, "<|endoftext|>", 13) == 0 && hp->eos == UINT32_MAX) hp->eos = (uint32_t)i;
-                p += 8 + n;
-            }
-            hp->n_vocab = (int)kv->arr_n;
-        }
-    }
-    for (int i = 0; i < hp->n_layer; i++) {
-        uint32_t rr;
-        if (get_arr_u32(g, "qwen35.attention.recurrent_layers", (uint64_t)i, &rr)) m->layers[i].recurrent = rr != 0;
-        else m->layers[i].recurrent = (i + 1) % hp->full_attn_interval != 0;
-    }
-    if (!get_w(g, "token_embd.weight", &m->tok_embd, true, err, errlen) ||
-        !get_w(g, "output_norm.weight", &m->output_norm, true, err, errlen) ||
-        !get_w(g, "output.weight", &m->output, false, err, errlen)) goto fail;
-    if (!m->output.nbytes) m->output = m->tok_embd;
-    if (!hp->n_vocab) hp->n_vocab = (int)m->tok_embd.ne1;
-    for (int i = 0; i < hp->n_layer; i++)
-        if (!load_layer(g, hp, i, &m->layers[i], err, errlen)) goto fail;
-    if (nextn > 0) {
-        const int i = (int)block_count - 1, il = hp->n_layer;
-        if (il + 1 > XJ_MAX_LAYERS) { seterr(err, errlen, "too many layers"); goto fail; }
-        xj_layer *L = &m->layers[il];
-        memset(L, 0, sizeof(*L));
-        if (!load_layer(g, hp, i, L, err, errlen)) goto fail;
-        char name[96];
-        struct { xj_w *w; const char *s; } nx[] = {
-            {&m->mtp_eh, "eh_proj.weight"}, {&m->mtp_enorm, "enorm.weight"},
-            {&m->mtp_hnorm, "hnorm.weight"}, {&m->mtp_head_norm, "shared_head_norm.weight"}};
-        for (auto &q : nx) {
-            snprintf(name, sizeof name, "blk.%d.nextn.%s", i, q.s);
-            if (!get_w(g, name, q.w, true, err, errlen)) goto fail;
-        }
-        if (m->mtp_eh.ne0 != 2 * hp->n_embd || m->mtp_eh.ne1 != hp->n_embd) { seterr(err, errlen, "MTP eh_proj has the wrong shape"); goto fail; }
-        if (m->mtp_enorm.type != XJ_F32 || m->mtp_hnorm.type != XJ_F32 || m->mtp_head_norm.type != XJ_F32) {
-            seterr(err, errlen, "MTP norms must be F32"); goto fail;
-        }
-        m->has_mtp = true;
-    }
-    {
-        uint64_t h = 1469598103934665603ull;
-        h = fnv(h, hp, sizeof(*hp));
-        for (uint64_t i = 0; i < g->n_tensors; i++) {
-            const gguf_tensor *t = &g->tensors[i];
-            h = fnv(h, t->name, strlen(t->name));
-            h = fnv(h, &t->type, sizeof t->type);
-            h = fnv(h, t->ne, sizeof t->ne);
-            h = fnv(h, &t->offset, sizeof t->offset);
-        }
-        m->fingerprint = h;
-    }
+    xj_model *m = build_model(g, err, errlen);
+    if (!m) gguf_free(g);
     return m;
-fail:
-    free(m);
-    gguf_free(g);
-    return nullptr;
 }
 
 void xjc_model_free(xj_model *m) {

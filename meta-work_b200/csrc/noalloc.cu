@@ -18,6 +18,7 @@
 // first call before any stream capture.
 #include <cuda_runtime.h>
 
+#include <atomic>
 #include <cstdarg>
 #include <cstdio>
 
@@ -30,8 +31,13 @@ namespace {
 
 static __device__ __align__(256) float g_noalloc_scratch[XJC_NOALLOC_MAX_FLOATS];
 
+// Device address of g_noalloc_scratch per device, looked up once per device by the first call made
+// with that device current. Atomic, so calls from several host threads may race on the first lookup
+// harmlessly (each stores the same address). A cudaDeviceReset, or any other end of the device's
+// primary context, invalidates the cached address: call xj_cuda_norm_gemv_noalloc only within one
+// context lifetime per device.
 constexpr int MAXDEV = 64;
-float *g_scratch_addr[MAXDEV] = {nullptr};
+std::atomic<float *> g_scratch_addr[MAXDEV];
 
 void seterr(char *err, size_t errlen, const char *fmt, ...) {
     if (!err || !errlen) return;
@@ -73,16 +79,15 @@ extern "C" int xj_cuda_norm_gemv_noalloc(int type, const void *w_dev, int k, int
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess || dev < 0 || dev >= MAXDEV) { seterr(err, errlen, "no usable current device"); return -1; }
-    if (!g_scratch_addr[dev]) {
-        float *p = nullptr;
-        e = cudaGetSymbolAddress((void **)&p, g_noalloc_scratch);
-        if (e != cudaSuccess || !p) {
+    float *hn = g_scratch_addr[dev].load(std::memory_order_acquire);
+    if (!hn) {
+        e = cudaGetSymbolAddress((void **)&hn, g_noalloc_scratch);
+        if (e != cudaSuccess || !hn) {
             seterr(err, errlen, "cudaGetSymbolAddress failed: %s", cudaGetErrorString(e));
             return -1;
         }
-        g_scratch_addr[dev] = p;
+        g_scratch_addr[dev].store(hn, std::memory_order_release);
     }
-    float *hn = g_scratch_addr[dev];
     // rows of the normalised input (core/xj_cpu.c:56-61), then the product (core/xj_cpu.c:36-54)
     k_rmsnorm<<<T, 256>>>(x_dev, (long long)k, norm_w_dev, hn, (long long)k, k, eps);
     GemvArgs a{};

@@ -1444,7 +1444,7 @@ int xj_cuda_spec_decode(xj_stage *target, xj_stage *draft, const int32_t *prompt
     return 0;
 }
 
-// Gated DeltaNet decode step on synthetic operands (BASELINE config 2): B sequences x Hv heads of an
+// Gated DeltaNet decode step on synthetic operands: B sequences x Hv heads of an
 // S x S fp32 state, one token each, with the batch kernel of batched decode (k_gdn_batch; B = 1 is the
 // single-sequence case). The states rotate over enough copies that the last-level cache cannot serve
 // them (>= 256 MiB in total); *ms = average device time per launch over `iters` launches.
@@ -1514,7 +1514,7 @@ done:
     return rc;
 }
 
-// Gated DeltaNet over a prompt of T tokens (BASELINE config 2, prefill): the chunked kernels against the
+// Gated DeltaNet over a prompt of T tokens (prefill): the chunked kernels against the
 // token-by-token kernel on the same synthetic operands (Hk key heads, Hv value heads, S x S state from a
 // nonzero start). res[0] = max |o_chunked - o_seq| / max |o_seq| (after the gated norm), res[1] = the same
 // for the final state, res[2] / res[3] = device ms of the chunked / token-by-token path.
@@ -1602,6 +1602,94 @@ int xj_cuda_gdn_prefill_check(int S, int Hk, int Hv, int T, float *res, char *er
         };
         res[0] = rel(h1, h2);
         res[1] = rel(s1, s2);
+    }
+    rc = 0;
+done:
+    cudaStreamSynchronize(im->st);
+    for (void *p : im->allocs) cudaFree(p);
+    im->allocs.clear();
+    cudaStreamDestroy(im->st);
+    return rc;
+}
+
+// Gated DeltaNet recurrence on caller operands (host buffers), for parity against a host restatement of
+// core/xj_cpu.c:194-219. path 0: the token-by-token kernel over T tokens of one sequence (k_gdn, the
+// prompt path below 32 tokens and the checkpointing verify path); 1: the chunked prefill kernels;
+// 2: the batch decode kernel with T independent sequences of one token each (state [T][Hv][S][S]).
+// qkv [T][2*Hk*S + Hv*S] after the convolution and SiLU; z [T][Hv*S] raw gate; beta, alpha [T][Hv]
+// logits; dt, A [Hv]; norm_w [S]; state in/out; out [T][Hv*S] after the gated RMSNorm.
+int xj_cuda_gdn_run(int path, int S, int Hk, int Hv, int T, const float *qkv, const float *z, const float *beta,
+                    const float *alpha, const float *dt, const float *A, const float *norm_w, float eps, float *state,
+                    float *out, char *err, size_t errlen) {
+    if (path < 0 || path > 2) { seterr(err, errlen, "path must be 0, 1 or 2"); return -1; }
+    if (S != 16 && S != 32 && S != 64 && S != 128) { seterr(err, errlen, "S must be 16, 32, 64 or 128"); return -1; }
+    if (path == 1 && S == 16) { seterr(err, errlen, "the chunked path needs S = 32, 64 or 128"); return -1; }
+    if (Hk < 1 || Hv < Hk || Hv % Hk || T < 1) { seterr(err, errlen, "need 1 <= Hk, Hk | Hv and T >= 1"); return -1; }
+    if (!qkv || !z || !beta || !alpha || !dt || !A || !norm_w || !state || !out) { seterr(err, errlen, "null buffer"); return -1; }
+    Impl tmp;
+    Impl *im = &tmp;
+    int rc = -1;
+    const int key_dim = Hk * S, ldq = 2 * key_dim + Hv * S, nch = (T + GC_C - 1) / GC_C;
+    const size_t ns = (size_t)Hv * S * S * (path == 2 ? T : 1);
+    float *dq = nullptr, *dz = nullptr, *dba = nullptr, *dpar = nullptr, *dm = nullptr, *dout = nullptr;
+    float *qn = nullptr, *kn = nullptr, *kk = nullptr, *qk = nullptr;
+    if (cudaStreamCreateWithFlags(&im->st, cudaStreamNonBlocking) != cudaSuccess) { seterr(err, errlen, "no stream"); return -1; }
+    if (dalloc(im, &dq, (size_t)T * ldq, err, errlen) || dalloc(im, &dz, (size_t)T * Hv * S, err, errlen) ||
+        dalloc(im, &dba, (size_t)2 * T * Hv, err, errlen) || dalloc(im, &dpar, (size_t)2 * Hv + S, err, errlen) ||
+        dalloc(im, &dm, ns, err, errlen) || dalloc(im, &dout, (size_t)T * Hv * S, err, errlen))
+        goto done;
+    if (path == 1 && (dalloc(im, &qn, (size_t)T * key_dim, err, errlen) || dalloc(im, &kn, (size_t)T * key_dim, err, errlen) ||
+                      dalloc(im, &kk, (size_t)Hk * nch * GC_C * GC_C, err, errlen) ||
+                      dalloc(im, &qk, (size_t)Hk * nch * GC_C * GC_C, err, errlen)))
+        goto done;
+    if (cudaMemcpy(dq, qkv, (size_t)T * ldq * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dz, z, (size_t)T * Hv * S * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dba, beta, (size_t)T * Hv * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dba + (size_t)T * Hv, alpha, (size_t)T * Hv * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dpar, dt, (size_t)Hv * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dpar + Hv, A, (size_t)Hv * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dpar + 2 * Hv, norm_w, (size_t)S * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
+        cudaMemcpy(dm, state, ns * 4, cudaMemcpyHostToDevice) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        seterr(err, errlen, "upload failed");
+        goto done;
+    }
+    {
+        GdnArgs g{};
+        g.qkv = dq; g.ldq = ldq; g.z = dz; g.ldz = Hv * S; g.beta = dba; g.alpha = dba + (size_t)T * Hv; g.ldg = Hv;
+        g.dt = dpar; g.A = dpar + Hv; g.nw = dpar + 2 * Hv; g.ck_ssm = nullptr; g.ssm = dm; g.out = dout; g.ldo = Hv * S;
+        g.T = T; g.Hk = Hk; g.Hv = Hv; g.key_dim = key_dim; g.eps = eps;
+        if (path == 0) {
+            switch (S) {
+            case 16: launch(im, k_gdn<16>, dim3(Hv), dim3(64), 0, g); break;
+            case 32: launch(im, k_gdn<32>, dim3(Hv), dim3(128), 0, g); break;
+            case 64: launch(im, k_gdn<64>, dim3(Hv), dim3(256), 0, g); break;
+            default: launch(im, k_gdn<128>, dim3(Hv), dim3(512), 0, g); break;
+            }
+        } else if (path == 1) {
+            switch (S) {
+            case 32: launch_gdn_chunked<32>(im, g, qn, kn, kk, qk); break;
+            case 64: launch_gdn_chunked<64>(im, g, qn, kn, kk, qk); break;
+            default: launch_gdn_chunked<128>(im, g, qn, kn, kk, qk); break;
+            }
+        } else {
+            const long long sstride = (long long)Hv * S * S;
+            g.T = 1;
+            switch (S) {
+            case 16: launch(im, k_gdn_batch<16>, dim3(Hv, T), dim3(64), 0, g, sstride); break;
+            case 32: launch(im, k_gdn_batch<32>, dim3(Hv, T), dim3(128), 0, g, sstride); break;
+            case 64: launch(im, k_gdn_batch<64>, dim3(Hv, T), dim3(256), 0, g, sstride); break;
+            default: launch(im, k_gdn_batch<128>, dim3(Hv, T), dim3(512), 0, g, sstride); break;
+            }
+        }
+        if (cudaStreamSynchronize(im->st) != cudaSuccess || cudaGetLastError() != cudaSuccess) {
+            seterr(err, errlen, "GDN launch failed");
+            goto done;
+        }
+    }
+    if (cudaMemcpy(out, dout, (size_t)T * Hv * S * 4, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        cudaMemcpy(state, dm, ns * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        seterr(err, errlen, "download failed");
+        goto done;
     }
     rc = 0;
 done:

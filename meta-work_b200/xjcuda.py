@@ -113,6 +113,7 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_spec_decode": (ip, [vp, vp, vp, ip, ip, ip, vp, vp, cp, sz]),
         "xj_cuda_gdn_prefill_check": (ip, [ip, ip, ip, ip, vp, cp, sz]),
         "xj_cuda_norm_gemv_noalloc": (ip, [ip, vp, ip, ip, vp, vp, ctypes.c_float, ip, vp, cp, sz]),
+        "xj_cuda_gdn_run": (ip, [ip, ip, ip, ip, ip, vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, vp, vp, cp, sz]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -197,6 +198,23 @@ def gdn_prefill_check(S: int, Hk: int, Hv: int, T: int):
     if lib().xj_cuda_gdn_prefill_check(S, Hk, Hv, T, r.ctypes.data, e, 512):
         _raise(e)
     return tuple(float(v) for v in r)
+
+
+def gdn_run(path: int, S: int, Hk: int, Hv: int, qkv, z, beta, alpha, dt, A, norm_w, state, eps: float = 1e-6):
+    """Gated DeltaNet recurrence on host operands (xj_cuda_gdn_run). path 0 = token-by-token kernel,
+    1 = chunked prefill kernels, 2 = batch decode kernel (rows = independent sequences). Returns
+    (out [T][Hv*S], final state)."""
+    f = lambda a: np.ascontiguousarray(a, np.float32)
+    qkv, z, beta, alpha, dt, A, norm_w = map(f, (qkv, z, beta, alpha, dt, A, norm_w))
+    st = f(state).copy()
+    T = qkv.shape[0]
+    out = np.zeros((T, Hv * S), np.float32)
+    e = _err()
+    if lib().xj_cuda_gdn_run(path, S, Hk, Hv, T, qkv.ctypes.data, z.ctypes.data, beta.ctypes.data, alpha.ctypes.data,
+                             dt.ctypes.data, A.ctypes.data, norm_w.ctypes.data, eps, st.ctypes.data, out.ctypes.data,
+                             e, 512):
+        _raise(e)
+    return out, st
 
 
 def _err():

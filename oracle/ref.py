@@ -15,7 +15,8 @@ import numpy as np
 
 HERE = pathlib.Path(__file__).resolve().parent
 LIB = HERE / "_ref" / "libxjref.so"
-REF_TREE = pathlib.Path("/root/reference/src/xiaoju-pipe")
+# the reference source tree (read-only): $XJ_REF_TREE, else the checkout location of this build machine
+REF_TREE = pathlib.Path(os.environ.get("XJ_REF_TREE", "/root/reference/src/xiaoju-pipe"))
 
 _lib = None
 

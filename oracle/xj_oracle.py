@@ -336,6 +336,66 @@ def softplus(x):
     return np.where(x > 20, x, np.log1p(np.exp(np.minimum(x, 20)))).astype(np.float32)
 
 
+def gdn_token(q, k, v, beta, alpha, z, dt, A, nw, ssm, Hk: int, Hv: int, S: int, eps: float, qscale):
+    """One token of the Gated DeltaNet recurrence in float32, as core/xj_cpu.c:194-219 writes it:
+    q [Hk][S], k [Hk][S], v [Hv][S] after the convolution; ssm [Hv][S(value j)][S(key i)] updated in place.
+    Returns the gated-normalised output [Hv*S]."""
+    o = np.zeros(Hv * S, np.float32)
+    q = l2norm(q, eps)
+    k = l2norm(k, eps)
+    b = sigm(beta)
+    g = (softplus(alpha + dt) * A).astype(np.float32)
+    eg = np.exp(g).astype(np.float32)
+    for hv in range(Hv):
+        hk = hv % Hk
+        M = ssm[hv]                                    # [S(value j)][S(key i)]
+        M *= eg[hv]
+        sk = M @ k[hk]
+        delta = ((v[hv] - sk) * b[hv]).astype(np.float32)
+        M += np.outer(delta, k[hk]).astype(np.float32)
+        oh = (M @ q[hk]).astype(np.float32) * qscale
+        zh = z[hv * S:(hv + 1) * S]
+        o[hv * S:(hv + 1) * S] = rmsnorm(oh, nw, eps) * silu(zh)
+    return o
+
+
+def gdn_recurrence(qkv, z, beta, alpha, dt, A, nw, M, Hk: int, Hv: int, S: int, eps: float,
+                   dtype=np.float64):
+    """The Gated DeltaNet recurrence of attn_linear after its projections and convolution
+    (core/xj_cpu.c:194-219), vectorised over value heads, for T tokens of one sequence:
+    q, k L2-normalised per key head; b = sigmoid(beta); g = softplus(alpha + dt) * A; per value head
+    hv (key head hv % Hk): M *= exp(g); delta = (v - M k) * b; M += delta k^T; o = M q / sqrt(S);
+    out = rmsnorm(o) * nw * silu(z). qkv [T][2*Hk*S + Hv*S], z [T][Hv*S], beta/alpha [T][Hv],
+    M [Hv][S(value)][S(key)] updated in place. Computed in `dtype` (float64 by default, a tighter
+    reference than the float32 of the C code). Returns out [T][Hv*S] as float32."""
+    T = qkv.shape[0]
+    kd = Hk * S
+    hk_of = np.arange(Hv) % Hk
+    Md = M.astype(dtype)
+    out = np.zeros((T, Hv * S), np.float32)
+    qscale = 1.0 / np.sqrt(dtype(S))
+    for t in range(T):
+        x = qkv[t].astype(dtype)
+        q = x[:kd].reshape(Hk, S)
+        k = x[kd:2 * kd].reshape(Hk, S)
+        v = x[2 * kd:].reshape(Hv, S)
+        q = q / np.sqrt((q * q).sum(axis=1, keepdims=True) + eps)
+        k = k / np.sqrt((k * k).sum(axis=1, keepdims=True) + eps)
+        b = 1.0 / (1.0 + np.exp(-beta[t].astype(dtype)))
+        g = np.logaddexp(0.0, alpha[t].astype(dtype) + dt) * A
+        kh, qh = k[hk_of], q[hk_of]                                   # [Hv][S]
+        Md *= np.exp(g)[:, None, None]
+        sk = np.einsum("hji,hi->hj", Md, kh)
+        delta = (v - sk) * b[:, None]
+        Md += delta[:, :, None] * kh[:, None, :]
+        o = np.einsum("hji,hi->hj", Md, qh) * qscale                  # [Hv][S]
+        ms = (o * o).mean(axis=1, keepdims=True)
+        zz = z[t].astype(dtype).reshape(Hv, S)
+        out[t] = (o / np.sqrt(ms + eps) * nw * (zz / (1.0 + np.exp(-zz)))).reshape(-1)
+    M[...] = Md
+    return out
+
+
 def rope(v: np.ndarray, n_rot: int, pos: int, base: float) -> np.ndarray:
     """NeoX rotation of the first n_rot dims, pairs (i, i + n_rot/2) (core/xj_cpu.c:68-77)."""
     half = n_rot // 2
@@ -437,21 +497,7 @@ class Stage:
             q = x[:hp.key_dim].reshape(Hk, S)
             k = x[hp.key_dim:2 * hp.key_dim].reshape(Hk, S)
             v = x[2 * hp.key_dim:].reshape(Hv, S)
-            q = l2norm(q, hp.eps)
-            k = l2norm(k, hp.eps)
-            b = sigm(beta[t])
-            g = (softplus(alpha[t] + dt) * A).astype(np.float32)
-            eg = np.exp(g).astype(np.float32)
-            for hv in range(Hv):
-                hk = hv % Hk
-                M = st["ssm"][hv]                              # [S(value j)][S(key i)]
-                M *= eg[hv]
-                sk = M @ k[hk]
-                delta = ((v[hv] - sk) * b[hv]).astype(np.float32)
-                M += np.outer(delta, k[hk]).astype(np.float32)
-                oh = (M @ q[hk]).astype(np.float32) * qscale
-                zh = z[t, hv * S:(hv + 1) * S]
-                o[t, hv * S:(hv + 1) * S] = rmsnorm(oh, nw, hp.eps) * silu(zh)
+            o[t] = gdn_token(q, k, v, beta[t], alpha[t], z[t], dt, A, nw, st["ssm"], Hk, Hv, S, hp.eps, qscale)
             if ck and t < T - 1:
                 st["ck"].append((st["conv"].copy(), st["ssm"].copy()))
         return matmul(L["ssm_out"], o)

@@ -30,7 +30,7 @@ ROOT = HERE.parents[1]
 sys.path.insert(0, str(ROOT))
 from oracle import ref  # noqa: E402
 
-REF_TREE = pathlib.Path("/root/reference/src/xiaoju-pipe")
+REF_TREE = ref.REF_TREE
 
 
 def load_pkg():
@@ -112,8 +112,21 @@ def main():
         g[f"tiny_spec_k{k}_stats"] = stats
     st, _ = m.spec(p, TINY_N_GEN, 0, max_batch=8, n_ctx=512, s1=3)
     g["tiny_split3"] = st
+    m.close()
+    # the synthetic models are not fixtures: they live in a temporary directory removed at the end
+    with tempfile.TemporaryDirectory(prefix="xj_golden_") as tmpdir:
+        synthetic_cases(g, synth, pathlib.Path(tmpdir))
+    # ---- dequant known answers ----
+    for t, (raw, dq) in dequant_cases(synth).items():
+        g[f"dq_{t}_raw"] = raw
+        g[f"dq_{t}_f32"] = dq
+    np.savez_compressed(HERE / "golden.npz", **g)
+    print("wrote", HERE / "golden.npz", "and", tiny)
+
+
+def synthetic_cases(g, synth, tmp: pathlib.Path):
+    """Reference outputs on the synthetic config-0 (Q8_0) and mid (Q4_K_M) models written into tmp."""
     # ---- synthetic config 0 ----
-    tmp = pathlib.Path(tempfile.mkdtemp(prefix="xj_golden_"))   # the synthetic models are not fixtures
     c0 = tmp / "golden_config0.gguf"
     synth.write_gguf(c0, synth.CONFIG0)
     g["config0_sha256"] = np.frombuffer(hashlib.sha256(c0.read_bytes()).digest(), np.uint8)
@@ -132,12 +145,8 @@ def main():
     tokm, marm, firstm, _ = mm.greedy(pm, MID_N_GEN, max_batch=8, n_ctx=512)
     g.update(mid_prompt=pm, mid_tokens=tokm, mid_margins=marm, mid_first_logits=firstm,
              mid_fingerprint=np.uint64(mm.fingerprint))
-    # ---- dequant known answers ----
-    for t, (raw, dq) in dequant_cases(synth).items():
-        g[f"dq_{t}_raw"] = raw
-        g[f"dq_{t}_f32"] = dq
-    np.savez_compressed(HERE / "golden.npz", **g)
-    print("wrote", HERE / "golden.npz", "and", tiny)
+    m0.close()
+    mm.close()
 
 
 if __name__ == "__main__":

@@ -1,6 +1,6 @@
 """The decode GEMV (y = W x, the reference matmul core/xj_cpu.c:36-54) on the GPU through the C ABI.
 
-Checks, per weight type and shape (BASELINE config-1 shapes included): fp32-level agreement with a
+Checks, per weight type and shape (the microbenchmark shapes included): fp32-level agreement with a
 float64 product of the reference-exact dequantised weights (bound 1e-5 of max|y|: fp32 accumulation,
 plus the Q4_K path's codes enter the MMA as 64+q with 64*sum(x) removed afterwards, which costs a few
 fp32 ulps of that sum); the tensor-core path equals the generic
@@ -133,6 +133,25 @@ def test_gemv64_token_results_independent_of_batch(t, tc):
     assert y17.view(np.uint32).tolist() == y64[:17].view(np.uint32).tolist()
 
 
+@pytest.mark.parametrize("t", [xo.Q6_K, xo.Q4_K, xo.Q8_0])
+def test_gemv_lm_head_shape(t):
+    """The LM head (151936 x 2048; Q6_K in the Q4_K_M models, the other two types for the microbenchmark)
+    at 1, 4 and 16 tokens against the float64 product of the oracle-dequantised weights, every row."""
+    from xjb200 import synth, xjcuda
+    k, n = 2048, 151936
+    rng = np.random.default_rng(151936 + t)
+    W = rng.standard_normal(n * k, dtype=np.float32) * np.float32(0.02)
+    raw = synth.quantize_row(t, W)
+    del W
+    D = xo.dequant(t, raw, k, n).astype(np.float64)
+    for T in (1, 4, 16):
+        x = rng.standard_normal((T, k)).astype(np.float32)
+        want = x.astype(np.float64) @ D.T
+        y = xjcuda.gemv(t, raw, k, n, x)
+        err = np.abs(y - want).max() / np.abs(want).max()
+        assert err < 1e-5, (t, T, err)
+
+
 def test_gemv_microbench_runs():
     from xjb200 import xjcuda
     raw = _w(xo.Q4_K, 2048, 2048, 9)
@@ -141,7 +160,7 @@ def test_gemv_microbench_runs():
 
 
 def test_gdn_decode_microbench_runs():
-    """BASELINE config 2 decode: 16 heads, S = 128, B = 1 and 64 (state 2 MiB per sequence)."""
+    """Gated DeltaNet decode: 16 heads, S = 128, B = 1 and 64 (state 2 MiB per sequence)."""
     from xjb200 import xjcuda
     for B in (1, 64):
         ms = xjcuda.gdn_time(128, 16, B, iters=10)

@@ -1,4 +1,4 @@
-"""Greedy speculative decoding with a separate draft model (xj_cuda_spec_decode).
+"""Greedy speculative decoding with a separate draft model (xj_cuda_spec_decode, config 4).
 
 The reference invariant (e2e.sh: speculative output equals plain greedy) is checked against the
 reference's own ids for the golden prompt (oracle) and against plain device decode through the same

@@ -148,3 +148,41 @@ def test_oracle_rollback_equivalence(tiny_path):
     assert rel_err(out, want) < 1e-5
     with pytest.raises(ValueError):
         s.rollback(3)
+
+
+def test_gdn_recurrence_matches_float32_token_step():
+    """The vectorised float64 recurrence (the GPU GDN tests' reference) against the float32 per-token
+    step that the oracle's attn_linear uses (itself pinned to the reference by the greedy and layer-trace
+    tests above), over 48 tokens of 2 key / 4 value heads."""
+    rng = np.random.default_rng(5)
+    T, Hk, Hv, S, eps = 48, 2, 4, 16, 1e-6
+    qkv = rng.standard_normal((T, 2 * Hk * S + Hv * S)).astype(np.float32)
+    z = rng.standard_normal((T, Hv * S)).astype(np.float32)
+    beta = rng.standard_normal((T, Hv)).astype(np.float32)
+    alpha = rng.standard_normal((T, Hv)).astype(np.float32)
+    dt = (0.5 * rng.standard_normal(Hv)).astype(np.float32)
+    A = (-np.exp(0.5 * rng.standard_normal(Hv))).astype(np.float32)
+    nw = (1 + 0.1 * rng.standard_normal(S)).astype(np.float32)
+    M0 = (0.1 * rng.standard_normal((Hv, S, S))).astype(np.float32)
+    M64 = M0.astype(np.float64)
+    want = xo.gdn_recurrence(qkv, z, beta, alpha, dt.astype(np.float64), A.astype(np.float64),
+                             nw.astype(np.float64), M64, Hk, Hv, S, eps)
+    M32 = M0.copy()
+    qs = np.float32(1.0 / np.sqrt(np.float32(S)))
+    got = np.stack([xo.gdn_token(qkv[t, :Hk * S].reshape(Hk, S), qkv[t, Hk * S:2 * Hk * S].reshape(Hk, S),
+                                 qkv[t, 2 * Hk * S:].reshape(Hv, S), beta[t], alpha[t], z[t], dt, A, nw, M32,
+                                 Hk, Hv, S, eps, qs) for t in range(T)])
+    assert rel_err(got, want) < 1e-5
+    assert rel_err(M32, M64) < 1e-5
+
+
+def test_config3_fixture_is_consistent():
+    """tests/golden/config3.npz (the reference at the benchmark's operating point) holds bench.py's
+    prompt, 64 ids, and a last-step trace whose logits pick the second id."""
+    from make_config3 import C3_N_GEN, C3_N_PROMPT, c3_prompt
+    from conftest import GOLDEN
+    c3 = np.load(GOLDEN / "config3.npz")
+    assert c3["c3_prompt"].tolist() == c3_prompt(151936).tolist() and c3["c3_prompt"].size == C3_N_PROMPT
+    assert c3["c3_tokens"].size == C3_N_GEN and c3["c3_margins"].size == C3_N_GEN
+    assert c3["c3_trace_hid"].shape == (29, 2048)
+    assert int(np.argmax(c3["c3_trace_logits"].astype(np.float32))) == int(c3["c3_tokens"][1])
