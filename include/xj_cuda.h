@@ -107,6 +107,21 @@ int xj_cuda_gdn_run(int path, int S, int Hk, int Hv, int T, const float *qkv, co
                     const float *alpha, const float *dt, const float *A, const float *norm_w, float eps, float *state,
                     float *out, char *err, size_t errlen);
 
+// Sampling instead of the greedy pick for later xj_cuda_decode calls on this stage: the session
+// layer's sampler (ios/App/XJGlue.c:251-282: top-k 40, top-p 0.95, temperature) on the device, with a
+// reproducible draw. temperature <= 0 restores greedy decoding. 1 <= top_k <= 64, 0 < top_p <= 1. The
+// draw for each token is uniform(seed, stage position of its logits) (SplitMix64, 30 bits), so a seed
+// fixes the sampled sequence however the decode calls are split. Sampled decode runs the per-phase
+// decode step (a CUDA graph), not the persistent kernel, and reports each step's top-2 logit gap.
+int xj_cuda_set_sampler(xj_stage *s, float temperature, int top_k, double top_p, unsigned long long seed, char *err,
+                        size_t errlen);
+// The same pick on host logit rows (parity tests): out[r] = the id drawn from logits[r][0..n_vocab) with
+// uniform(seed, counter0 + r); margins (may be NULL) = each row's top-2 logit gap. temperature <= 0 (or
+// top_k = 1) = greedy, lowest id on ties.
+int xj_cuda_sample_logits(const float *logits, int rows, int n_vocab, float temperature, int top_k, double top_p,
+                          unsigned long long seed, unsigned long long counter0, int32_t *out, float *margins, char *err,
+                          size_t errlen);
+
 // Number of kernel launches in one replay of the stage's cached decode-step graph (0 before the first
 // xj_cuda_decode call that generated more than one token).
 int xj_cuda_graph_kernels(const xj_stage *s);

@@ -21,6 +21,7 @@
 #include "../../include/xj_cuda.h"
 #include "kernels.cuh"
 #include "gemv_mma.cuh"
+#include "sample.cuh"
 #include "decode_mk.cuh"
 #include "tc_gemm.cuh"
 
@@ -107,6 +108,11 @@ struct Impl {
     int snap_np = -1;
     long long nlaunch = 0;                   // kernels launched on the stage stream so far
     long long last_launches[2] = {0, 0};     // last xj_cuda_decode: prompt, decode steps
+    // sampler of xj_cuda_decode (xj_cuda_set_sampler): temperature <= 0 = greedy
+    float samp_temp = 0.0f;
+    double samp_top_p = 0.95;
+    int samp_top_k = 40;
+    unsigned long long samp_seed = 0;
 };
 
 Impl *I(xj_stage *s) { return (Impl *)s->impl; }
@@ -542,6 +548,19 @@ void head_argmax(xj_stage *s, const float *x) {
     launch(im, k_argmax_final, dim3(1), dim3(1024), 0, argmax_args(im));
 }
 
+// The pick after the last row x: greedy (head_argmax), or with a sampler set, the LM head's logits and a
+// top-k / top-p draw (k_sample_final) that also embeds the picked token and advances the position.
+void head_pick(xj_stage *s, const float *x) {
+    Impl *im = I(s);
+    if (im->samp_temp <= 0.0f) { head_argmax(s, x); return; }
+    const xj_hparams *hp = &s->m->hp;
+    gemv(im, x, nullptr, hp->n_embd, 1, PRO_NORM, im->output_norm, hp->eps, {{im->output, im->logits, im->output.N}});
+    SampleArgs a{};
+    a.logits = im->logits; a.ld = im->output.N; a.n = im->output.N;
+    a.temp = im->samp_temp; a.top_p = im->samp_top_p; a.top_k = im->samp_top_k; a.seed = im->samp_seed;
+    launch(im, k_sample_final, dim3(1), dim3(SAMPLE_THREADS), 0, a, argmax_args(im));
+}
+
 int sync_check(Impl *im, char *err, size_t errlen) {
     cudaError_t e = cudaGetLastError();
     if (e == cudaSuccess) e = cudaStreamSynchronize(im->st);
@@ -785,7 +804,7 @@ int count_kernels(cudaGraph_t g) {
 void decode_step(xj_stage *s) {
     Impl *im = I(s);
     run_layers(s, 1, false, 0);
-    head_argmax(s, im->x);
+    head_pick(s, im->x);
 }
 
 // ------------------------------------------------------------------ persistent decode kernel
@@ -1171,7 +1190,7 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
     }
     CK(cudaMemsetAsync(im->step, 0, sizeof(int), im->st));
     int persist = 0;
-    if (g_opt_persist) {
+    if (g_opt_persist && im->samp_temp <= 0.0f) {   // the persistent kernel picks greedily
         char why[256];
         persist = mk_build(s, why, sizeof why) == 1;
     }
@@ -1187,7 +1206,7 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
         launch(im, k_embed, dim3((E / 8 + 127) / 128, T), dim3(128), 0, im->tok_embd, (const int32_t *)im->tok, T, im->x, E);
         const bool last = !persist && i + T == n_prompt;
         run_layers(s, T, false, last ? T - 1 : T);
-        if (last) head_argmax(s, im->x + (size_t)(T - 1) * E);   // picks out[0], embeds it, position +1
+        if (last) head_pick(s, im->x + (size_t)(T - 1) * E);   // picks out[0], embeds it, position +1
     }
     if (persist) {
         CK(cudaMemcpyAsync(im->tok, prompt + n_prompt - 1, sizeof(int32_t), cudaMemcpyHostToDevice, im->st));
@@ -1688,6 +1707,67 @@ int xj_cuda_gdn_run(int path, int S, int Hk, int Hv, int T, const float *qkv, co
     }
     if (cudaMemcpy(out, dout, (size_t)T * Hv * S * 4, cudaMemcpyDeviceToHost) != cudaSuccess ||
         cudaMemcpy(state, dm, ns * 4, cudaMemcpyDeviceToHost) != cudaSuccess) {
+        seterr(err, errlen, "download failed");
+        goto done;
+    }
+    rc = 0;
+done:
+    cudaStreamSynchronize(im->st);
+    for (void *p : im->allocs) cudaFree(p);
+    im->allocs.clear();
+    cudaStreamDestroy(im->st);
+    return rc;
+}
+
+int xj_cuda_set_sampler(xj_stage *s, float temperature, int top_k, double top_p, unsigned long long seed, char *err,
+                        size_t errlen) {
+    if (!s || s->backend == nullptr || strcmp(s->backend, "cuda") != 0) { seterr(err, errlen, "not a CUDA stage"); return -1; }
+    if (top_k < 1 || top_k > SAMPLE_KMAX) { seterr(err, errlen, "top_k must be in 1..%d", SAMPLE_KMAX); return -1; }
+    if (!(top_p > 0.0 && top_p <= 1.0)) { seterr(err, errlen, "top_p must be in (0, 1]"); return -1; }
+    Impl *im = I(s);
+    DevGuard dg(im->dev);
+    const bool was = im->samp_temp > 0.0f, now = temperature > 0.0f;
+    im->samp_temp = now ? temperature : 0.0f;
+    im->samp_top_k = top_k;
+    im->samp_top_p = top_p;
+    im->samp_seed = seed;
+    // the cached decode-step graph holds the pick kernel and its arguments
+    if (im->step_graph && (was || now)) {
+        cudaStreamSynchronize(im->st);
+        cudaGraphExecDestroy(im->step_graph);
+        im->step_graph = nullptr;
+    }
+    return 0;
+}
+
+int xj_cuda_sample_logits(const float *logits, int rows, int n_vocab, float temperature, int top_k, double top_p,
+                          unsigned long long seed, unsigned long long counter0, int32_t *out, float *margins, char *err,
+                          size_t errlen) {
+    if (!logits || !out || rows < 1 || n_vocab < 1) { seterr(err, errlen, "need logits, out, rows >= 1 and n_vocab >= 1"); return -1; }
+    if (top_k < 1 || top_k > SAMPLE_KMAX) { seterr(err, errlen, "top_k must be in 1..%d", SAMPLE_KMAX); return -1; }
+    if (!(top_p > 0.0 && top_p <= 1.0)) { seterr(err, errlen, "top_p must be in (0, 1]"); return -1; }
+    Impl tmp;
+    Impl *im = &tmp;
+    int rc = -1;
+    float *dl = nullptr, *dm = nullptr;
+    int32_t *dout = nullptr;
+    if (cudaStreamCreateWithFlags(&im->st, cudaStreamNonBlocking) != cudaSuccess) { seterr(err, errlen, "no stream"); return -1; }
+    if (dalloc(im, &dl, (size_t)rows * n_vocab, err, errlen) || dalloc(im, &dm, (size_t)rows, err, errlen) ||
+        dalloc(im, &dout, (size_t)rows, err, errlen))
+        goto done;
+    if (cudaMemcpy(dl, logits, (size_t)rows * n_vocab * 4, cudaMemcpyHostToDevice) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess) {
+        seterr(err, errlen, "upload failed");
+        goto done;
+    }
+    {
+        SampleArgs a{};
+        a.logits = dl; a.ld = n_vocab; a.n = n_vocab; a.temp = temperature; a.top_k = top_k; a.top_p = top_p;
+        a.seed = seed; a.counter0 = counter0; a.out = dout; a.margin = dm;
+        launch(im, k_sample_rows, dim3(rows), dim3(SAMPLE_THREADS), 0, a);
+        if (cudaStreamSynchronize(im->st) != cudaSuccess || cudaGetLastError() != cudaSuccess) { seterr(err, errlen, "sampling launch failed"); goto done; }
+    }
+    if (cudaMemcpy(out, dout, (size_t)rows * 4, cudaMemcpyDeviceToHost) != cudaSuccess ||
+        (margins && cudaMemcpy(margins, dm, (size_t)rows * 4, cudaMemcpyDeviceToHost) != cudaSuccess)) {
         seterr(err, errlen, "download failed");
         goto done;
     }

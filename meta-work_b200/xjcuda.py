@@ -114,6 +114,9 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_gdn_prefill_check": (ip, [ip, ip, ip, ip, vp, cp, sz]),
         "xj_cuda_norm_gemv_noalloc": (ip, [ip, vp, ip, ip, vp, vp, ctypes.c_float, ip, vp, cp, sz]),
         "xj_cuda_gdn_run": (ip, [ip, ip, ip, ip, ip, vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, vp, vp, cp, sz]),
+        "xj_cuda_set_sampler": (ip, [vp, ctypes.c_float, ip, ctypes.c_double, ctypes.c_ulonglong, cp, sz]),
+        "xj_cuda_sample_logits": (ip, [vp, ip, ip, ctypes.c_float, ip, ctypes.c_double, ctypes.c_ulonglong,
+                                       ctypes.c_ulonglong, vp, vp, cp, sz]),
     }
     for name, (res, args) in sig.items():
         f = getattr(L, name)
@@ -215,6 +218,22 @@ def gdn_run(path: int, S: int, Hk: int, Hv: int, qkv, z, beta, alpha, dt, A, nor
                              e, 512):
         _raise(e)
     return out, st
+
+
+def sample_logits(logits, temperature: float, seed: int, counter0: int = 0, top_k: int = 40, top_p: float = 0.95):
+    """Device top-k / top-p / temperature pick per row of host logits (xj_cuda_sample_logits): row r
+    draws with uniform(seed, counter0 + r). Returns (ids, top-2 margins)."""
+    lg = np.ascontiguousarray(logits, np.float32)
+    if lg.ndim == 1:
+        lg = lg[None]
+    rows, n = lg.shape
+    out = np.zeros(rows, np.int32)
+    mar = np.zeros(rows, np.float32)
+    e = _err()
+    if lib().xj_cuda_sample_logits(lg.ctypes.data, rows, n, temperature, top_k, top_p, seed, counter0, out.ctypes.data,
+                                   mar.ctypes.data, e, 512):
+        _raise(e)
+    return out, mar
 
 
 def _err():
@@ -333,6 +352,13 @@ class Stage:
         if rc:
             _raise(e)
         return out, mar, ms
+
+    def set_sampler(self, temperature: float, seed: int = 0, top_k: int = 40, top_p: float = 0.95) -> None:
+        """Sample later decode() tokens (top-k / top-p / temperature, xj_cuda_set_sampler); temperature <= 0
+        restores greedy decoding."""
+        e = _err()
+        if lib().xj_cuda_set_sampler(self.addr, temperature, top_k, top_p, seed, e, 512):
+            _raise(e)
 
     def spec_decode(self, draft: "Stage", prompt, n_gen: int, k: int = 4):
         """Greedy speculative decode with a draft-model stage (xj_cuda_spec_decode). Returns (ids, stats)

@@ -599,3 +599,99 @@ def greedy(m: Model, prompt, n_gen: int, max_batch: int = 8, n_ctx: int = 4096):
         x = s.forward(m.embed(t)[None, :])
         lg = s.logits(x)[0]
     return np.array(out, np.int32)
+
+
+# ---------------------------------------------------------------- sampling (session layer)
+def splitmix64(z: int) -> int:
+    """SplitMix64 output function (Steele, Lea and Flood, OOPSLA 2014) on a 64-bit state value."""
+    M = (1 << 64) - 1
+    z &= M
+    z = ((z ^ (z >> 30)) * 0xBF58476D1CE4E5B9) & M
+    z = ((z ^ (z >> 27)) * 0x94D049BB133111EB) & M
+    return z ^ (z >> 31)
+
+
+def sample_uniform(seed: int, counter: int) -> float:
+    """The device sampler's draw: 30 bits of splitmix64(seed + (counter + 1) * golden gamma), times 2^-30
+    (the resolution of arc4random_uniform(1 << 30) / 2^30 in ios/App/XJGlue.c:279)."""
+    z = splitmix64((seed + (counter + 1) * 0x9E3779B97F4A7C15) & ((1 << 64) - 1))
+    return (z >> 34) / float(1 << 30)
+
+
+def sample(lg: np.ndarray, temp: float, u: float, top_k: int = 40, top_p: float = 0.95) -> int:
+    """The session layer's sampler (ios/App/XJGlue.c:251-282) with the uniform draw u supplied:
+    greedy for temp <= 0; else a running top-k selection (replace the current minimum when a larger
+    value arrives), a descending selection sort, p_i = exp((v_i - v_0) / temp) in double, the cut where
+    the normalised cumulative sum reaches top_p, r = u * (sum of kept p), first i with r - sum p <= 0."""
+    lg = np.asarray(lg, np.float32)
+    n = lg.size
+    best = int(np.argmax(lg))
+    if temp <= 0:
+        return best
+    K = top_k
+    idx, val, k, mi = [0] * K, [0.0] * K, 0, 0
+    for i in range(n):
+        v = float(lg[i])
+        if k < K:
+            idx[k], val[k] = i, v
+            if v < val[mi]:
+                mi = k
+            k += 1
+        elif v > val[mi]:
+            idx[mi], val[mi] = i, v
+            mi = min(range(K), key=lambda j: (val[j], j))
+    for i in range(k):
+        for j in range(i + 1, k):
+            if val[j] > val[i]:
+                val[i], val[j] = val[j], val[i]
+                idx[i], idx[j] = idx[j], idx[i]
+    p, s = [], 0.0
+    for i in range(k):
+        # (val[i] - val[0]) / temp is float arithmetic in the C code; exp takes it as a double
+        p.append(float(np.exp(np.float64((np.float32(val[i]) - np.float32(val[0])) / np.float32(temp)))))
+        s += p[i]
+    acc, cut = 0.0, k
+    for i in range(k):
+        acc += p[i] / s
+        if acc >= top_p:
+            cut = i + 1
+            break
+    s2 = 0.0
+    for i in range(cut):
+        s2 += p[i]
+    r = u * s2
+    for i in range(cut):
+        r -= p[i]
+        if r <= 0:
+            return idx[i]
+    return idx[0]
+
+
+def sample_fast(lg: np.ndarray, temp: float, u: float, top_k: int = 40, top_p: float = 0.95) -> int:
+    """sample() for rows without equal values at the k-th place, vectorised: the top-k set sorted by value
+    descending (index ascending on ties), then the same cut and draw arithmetic."""
+    lg = np.asarray(lg, np.float32)
+    if temp <= 0:
+        return int(np.argmax(lg))
+    K = min(top_k, lg.size)
+    order = np.lexsort((np.arange(lg.size), -lg.astype(np.float64)))[:K]
+    vals = lg[order]
+    p, s = [], 0.0
+    for i in range(K):
+        p.append(float(np.exp(np.float64((vals[i] - vals[0]) / np.float32(temp)))))
+        s += p[i]
+    acc, cut = 0.0, K
+    for i in range(K):
+        acc += p[i] / s
+        if acc >= top_p:
+            cut = i + 1
+            break
+    s2 = 0.0
+    for i in range(cut):
+        s2 += p[i]
+    r = u * s2
+    for i in range(cut):
+        r -= p[i]
+        if r <= 0:
+            return int(order[i])
+    return int(order[0])
