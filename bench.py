@@ -338,11 +338,12 @@ def run_spec(args, model, rank, world, barrier, xjcuda, synth, local):
             "timing": "host wall clock per GPU, max over ranks, stages built and prompts processed inside"}
 
 
-def run_batch(args, cfg, model, rank, world, barrier, xjcuda):
-    """Batched greedy decode: args.batch independent sequences per GPU in lockstep (xj_cuda_batch_*),
-    each with its own seeded prompt of args.prompt tokens; K timed steps = one token of every sequence."""
+def run_batch(args, cfg, model, rank, world, barrier, xjcuda, n_seq=None):
+    """Batched greedy decode: args.batch (or n_seq) independent sequences per GPU in lockstep
+    (xj_cuda_batch_*), each with its own seeded prompt of args.prompt tokens; K timed steps = one token of
+    every sequence."""
     import torch
-    B = args.batch
+    B = n_seq or args.batch
     n_ctx = args.prompt + max(args.warmup, 3) + 2 * args.steps + 16
     bt = xjcuda.Batch(model, B, n_ctx)
     P = np.random.default_rng(4321 + rank).integers(0, cfg.n_vocab, (B, args.prompt)).astype(np.int32)
@@ -389,55 +390,75 @@ def run_batch(args, cfg, model, rank, world, barrier, xjcuda):
     }
 
 
+def run_pipeline_native(args, cfg, model, rank, world, barrier, xjcuda):
+    """Layer pipeline over all ranks, native (xj_cuda_pipeline_*: NCCL send/recv of activations and ids
+    inside libxj_cuda.so): args.batch sequences in total, args.micro_batches micro-batches, rank r holding
+    an even share of the layers. The communicator identifier goes from rank 0 to the others through
+    torch.distributed (this harness's channel). Timed: K decode steps in one decode call, device time per
+    rank (CUDA events on its compute stream), max over ranks; e2e = the same call by the host clock (prompt
+    upload and id download included)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.zeros(xjcuda.PIPELINE_ID_BYTES, dtype=torch.uint8, device="cuda")
+    if rank == 0:
+        t.copy_(torch.frombuffer(bytearray(xjcuda.pipeline_id()), dtype=torch.uint8))
+    dist.broadcast(t, 0)
+    pid = bytes(t.cpu().numpy().tobytes())
+    B = args.batch
+    n_ctx = args.prompt + max(args.warmup, 3) + 2 * args.steps + 16
+    p = xjcuda.Pipeline(model, rank, world, pid, B, n_ctx, args.micro_batches)
+    prompts = np.random.default_rng(4321).integers(0, cfg.n_vocab, (B, args.prompt)).astype(np.int32)
+    out, ms_pre = p.decode(prompts if rank == 0 else args.prompt, max(args.warmup, 3))   # prompt + warm-up
+    last = out[:, -1:] if rank == 0 else 1
+    barrier()
+    out, ms = p.decode(last, args.steps)
+    barrier()
+    last = out[:, -1:] if rank == 0 else 1
+    t0 = time.perf_counter()
+    p.decode(last, args.steps)
+    e2e_ms = (time.perf_counter() - t0) * 1e3
+    barrier()
+    v = torch.tensor([ms, e2e_ms], device="cuda")
+    dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    t_max, e2e_max = float(v[0]), float(v[1])
+    p.close()
+    if rank != 0:
+        return None
+    L = model.n_layer
+    return {
+        "value": round(B * args.steps / (t_max / 1e3), 1), "unit": "tok/s", "scaling": "strong",
+        "sequences_total": B, "micro_batches": args.micro_batches, "ms_per_step": round(t_max / args.steps, 4),
+        "steps": args.steps, "prompt": args.prompt, "prompt_ms": round(ms_pre, 1),
+        "layers_per_rank": [L // world + (1 if r < L % world else 0) for r in range(world)],
+        "e2e": {"value": round(B * args.steps / (e2e_max / 1e3), 1), "unit": "tok/s",
+                "h2d_bytes_per_step": round(4 * B / args.steps, 3), "d2h_bytes_per_step": 4 * B},
+        "exchange_bytes_per_step": {"activations": int(B * cfg.n_embd * 4 * (world - 1)), "ids": 4 * B},
+        "transport": "NCCL send/recv inside libxj_cuda.so",
+    }
+
+
 def run_pipeline(args, rank, local, world):
-    """Layer pipeline over the ranks (rank r holds layers split_layers(L, world)[r], the last the head):
-    --batch sequences in --micro-batches groups, greedy decode; device-timed per step, max over ranks."""
+    """--pipeline: only the native layer pipeline over the ranks (run_pipeline_native), as its own line."""
     import datetime
     import torch
     import torch.distributed as dist
-    from xjb200 import pipeline as pl, synth, xjcuda
+    from xjb200 import synth, xjcuda
     dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
     dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
-    gx, gt = dist.new_group(list(range(world))), dist.new_group(list(range(world)))
     cfg = synth.CONFIG3
     model = xjcuda.Model(synth.cached_gguf(cfg, os.environ.get("XJ_MODEL_DIR", f"/tmp/xj_models_r{local}")))
-    B = max(args.batch, 1)
-    n_ctx = args.prompt + 2 * args.steps + 16
-    l0, l1 = pl.split_layers(model.n_layer, world)[rank]
-    st = pl.CudaStage(model, l0, l1, rank == world - 1, B, n_ctx, dev)
-    p = pl.Pipeline(st, rank, world, B, args.micro_batches, gx, gt)
-    prompts = np.random.default_rng(4321).integers(0, cfg.n_vocab, (B, args.prompt)).astype(np.int32)
-    p.decode(prompts if rank == 0 else None, max(args.warmup, 3))          # prompt + warm-up (untimed)
-    dist.barrier()
-    torch.cuda.synchronize()
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    with st.context():                     # stage kernels and transfers on the stage's stream
-        first = [p._ids_from(np.zeros(n, np.int32)) for (r0, n) in p.mbs] if rank == 0 else None
-        e0.record()
-        for i in range(args.steps):        # K steps of every sequence; after the first, the picks are fed back
-            p.step(first if i == 0 else None, True)
-        if rank == 0:
-            p.drain()                      # the last step's picks reach rank 0
-        if rank == world - 1:
-            p.finish()
-        e1.record()
-    torch.cuda.synchronize()
-    dist.barrier()
-    t = torch.tensor([e0.elapsed_time(e1)], device=dev)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    ms = float(t.item())
-    st.close()
+
+    def barrier():
+        torch.cuda.synchronize()
+        dist.barrier()
+
+    line = run_pipeline_native(args, cfg, model, rank, world, barrier, xjcuda)
     if rank == 0:
-        print(json.dumps({
-            "metric": "pipelined batched decode tok/s (config 3, Q4_K_M)", "value": round(B * args.steps / (ms / 1e3), 1),
-            "unit": "tok/s", "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(ms / args.steps, 4), "higher_is_better": True, "scaling": "strong",
-            "vs_baseline": None, "dtype": "q4_k/q6_k weights, f32 accumulate", "data": "synthetic",
-            "config": {"workload": f"{cfg.name} greedy decode, {B} sequences", "prompt": args.prompt,
-                       "parallelism": f"layer pipeline x{world}", "micro_batches": args.micro_batches,
-                       "layers": pl.split_layers(model.n_layer, world)},
-            "exchange_bytes_per_step": {"activations": int(B * cfg.n_embd * 4 * (world - 1)), "ids": 4 * B},
-        }))
+        print(json.dumps({"metric": "pipelined batched decode tok/s (config 3, Q4_K_M)", "n_gpus": world,
+                          "higher_is_better": True, "data": "synthetic", "vs_baseline": None,
+                          "config": {"workload": f"{cfg.name} greedy decode, {args.batch} sequences",
+                                     "parallelism": f"layer pipeline x{world}"}, **line}))
     dist.destroy_process_group()
 
 
@@ -459,6 +480,8 @@ def main():
     ap.add_argument("--pipeline", action="store_true",
                     help="under torchrun: one layer range per GPU (NCCL layer pipeline) on --batch sequences")
     ap.add_argument("--micro-batches", type=int, default=2)
+    ap.add_argument("--strong", type=int, default=1,
+                    help="with several GPUs, also time --batch sequences in total: sharded and through the layer pipeline")
     ap.add_argument("--spec", type=int, default=0,
                     help="config 4: speculative decoding of this many 256-token prompts per GPU (0: skip)")
     args = ap.parse_args()
@@ -525,6 +548,16 @@ def main():
     e2e = world * args.steps / (e2e_max / 1e3)
     stage.close()
     batch_line = run_batch(args, cfg, model, rank, world, barrier, xjcuda) if args.batch > 0 else None
+    # strong scaling: args.batch sequences in total over the ranks (batch sharding, no data-path
+    # collective), and the same total through the layer pipeline over all ranks
+    strong_line = None
+    pipe_line = None
+    if world > 1 and args.batch > 0 and args.strong:
+        strong_line = run_batch(args, cfg, model, rank, world, barrier, xjcuda, n_seq=max(1, args.batch // world))
+        if strong_line:
+            strong_line["scaling"] = "strong"
+            strong_line["sequences_total"] = max(1, args.batch // world) * world
+        pipe_line = run_pipeline_native(args, cfg, model, rank, world, barrier, xjcuda)
     spec_line = run_spec(args, model, rank, world, barrier, xjcuda, synth, local) if args.spec > 0 else None
     if rank == 0:
         peak, peak_kind = hbm_peak()
@@ -559,6 +592,10 @@ def main():
         }
         if batch_line:
             line["batch"] = batch_line
+        if strong_line:
+            line["strong"] = strong_line
+        if pipe_line:
+            line["pipeline"] = pipe_line
         line["gdn"] = run_gdn(xjcuda, peak, peak_kind)
         if args.gemv:
             line["gemv"] = run_gemv(xjcuda, synth, peak, peak_kind, **gemv_kw(args))

@@ -193,6 +193,30 @@ void *xj_cuda_batch_stream(xj_cuda_batch *b);
 int xj_cuda_batch_set_async(xj_cuda_batch *b, int on);
 int xj_cuda_batch_sync(xj_cuda_batch *b, char *err, size_t errlen);
 
+// Layer pipeline across GPUs over NCCL (no counterpart in the reference's API: it re-expresses the
+// runtime's stage split, core/xj_net.h:93-111, driven by xj_pipeline_eval, core/xj_net.c:527-605, as
+// one process per GPU with activations and ids sent by NCCL instead of TCP). Each rank holds a batch of
+// n_seq sequences over an even share of the layers (first rank: embedding; last rank: LM head and
+// greedy pick); a decode step is one token of every sequence, split into n_micro micro-batches of rows
+// so that the stages overlap. NCCL is loaded at run time (libnccl.so.2).
+typedef struct xj_cuda_pipeline xj_cuda_pipeline;
+// Bytes of the identifier that rank 0 creates and every rank passes to xj_cuda_pipeline_new (three
+// NCCL unique ids: the two link-parity communicators and the token-id communicator).
+#define XJC_PIPELINE_ID_BYTES 384
+int xj_cuda_pipeline_id_new(unsigned char *id, char *err, size_t errlen);
+// Collective over the world's ranks (each on its own current device); id may be NULL when world == 1.
+xj_cuda_pipeline *xj_cuda_pipeline_new(const xj_model *m, int rank, int world, const unsigned char *id, int n_seq, int n_ctx,
+                                       int n_micro, char *err, size_t errlen);
+void xj_cuda_pipeline_free(xj_cuda_pipeline *p);
+// The rank's batch (its layer range, KV caches and states).
+xj_cuda_batch *xj_cuda_pipeline_batch(xj_cuda_pipeline *p);
+// Greedy decode, collective: rank 0 passes prompts [n_seq][n_prompt] and receives out [n_seq][n_gen]
+// (other ranks pass NULL for both); the prompt goes through in n_prompt lockstep steps, the last of which
+// picks out[:, 0]; every generated id but the last is fed back; positions continue across calls.
+// gpu_ms (may be NULL): device time of the call on this rank (CUDA events on its compute stream).
+int xj_cuda_pipeline_decode(xj_cuda_pipeline *p, const int32_t *prompts, int n_prompt, int n_gen, int32_t *out, float *gpu_ms,
+                            char *err, size_t errlen);
+
 // Capacity, in floats, of the fixed device scratch used by xj_cuda_norm_gemv_noalloc (256 KiB).
 #define XJC_NOALLOC_MAX_FLOATS 65536
 

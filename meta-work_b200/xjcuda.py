@@ -115,6 +115,11 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_norm_gemv_noalloc": (ip, [ip, vp, ip, ip, vp, vp, ctypes.c_float, ip, vp, cp, sz]),
         "xj_cuda_gdn_run": (ip, [ip, ip, ip, ip, ip, vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, vp, vp, cp, sz]),
         "xj_cuda_set_sampler": (ip, [vp, ctypes.c_float, ip, ctypes.c_double, ctypes.c_ulonglong, cp, sz]),
+        "xj_cuda_pipeline_id_new": (ip, [vp, cp, sz]),
+        "xj_cuda_pipeline_new": (vp, [vp, ip, ip, vp, ip, ip, ip, cp, sz]),
+        "xj_cuda_pipeline_free": (None, [vp]),
+        "xj_cuda_pipeline_batch": (vp, [vp]),
+        "xj_cuda_pipeline_decode": (ip, [vp, vp, ip, ip, vp, vp, cp, sz]),
         "xj_cuda_sample_logits": (ip, [vp, ip, ip, ctypes.c_float, ip, ctypes.c_double, ctypes.c_ulonglong,
                                        ctypes.c_ulonglong, vp, vp, cp, sz]),
     }
@@ -442,6 +447,63 @@ class Batch:
     def close(self):
         if self.p:
             lib().xj_cuda_batch_free(self.p)
+            self.p = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+PIPELINE_ID_BYTES = 384
+
+
+def pipeline_id() -> bytes:
+    """A new identifier for the communicators of one pipeline (xj_cuda_pipeline_id_new), made on rank 0 and
+    handed to every rank by the host (any channel: a store, a pipe, a file)."""
+    buf = (ctypes.c_ubyte * PIPELINE_ID_BYTES)()
+    e = _err()
+    if lib().xj_cuda_pipeline_id_new(buf, e, 512):
+        _raise(e)
+    return bytes(buf)
+
+
+class Pipeline:
+    """This rank's part of a layer pipeline across GPUs over NCCL (xj_cuda_pipeline_*): layers split evenly
+    over the world's ranks, n_seq sequences in n_micro micro-batches. Collective: every rank constructs it
+    (on its own current device) and calls decode together."""
+
+    def __init__(self, model: Model, rank: int, world: int, pid: bytes | None, n_seq: int, n_ctx: int = 256,
+                 n_micro: int = 2):
+        e = _err()
+        idb = (ctypes.c_ubyte * PIPELINE_ID_BYTES).from_buffer_copy(pid) if pid is not None else None
+        p = lib().xj_cuda_pipeline_new(model.ptr, rank, world, idb, n_seq, n_ctx, n_micro, e, 512)
+        if not p:
+            _raise(e)
+        self.p, self.rank, self.world, self.n_seq, self.model = p, rank, world, n_seq, model
+
+    def decode(self, prompts, n_gen: int):
+        """Rank 0: prompts [n_seq][n_prompt] -> (ids [n_seq][n_gen], device ms); other ranks pass the
+        prompt length as an int and get (None, device ms)."""
+        ms = ctypes.c_float(0)
+        e = _err()
+        if self.rank == 0:
+            pr = np.ascontiguousarray(prompts, dtype=np.int32)
+            assert pr.ndim == 2 and pr.shape[0] == self.n_seq
+            out = np.zeros((self.n_seq, n_gen), np.int32)
+            rc = lib().xj_cuda_pipeline_decode(self.p, pr.ctypes.data, pr.shape[1], n_gen, out.ctypes.data,
+                                               ctypes.byref(ms), e, 512)
+        else:
+            out = None
+            rc = lib().xj_cuda_pipeline_decode(self.p, None, int(prompts), n_gen, None, ctypes.byref(ms), e, 512)
+        if rc:
+            _raise(e)
+        return out, ms.value
+
+    def close(self):
+        if self.p:
+            lib().xj_cuda_pipeline_free(self.p)
             self.p = None
 
     def __del__(self):

@@ -1,4 +1,7 @@
-"""Layer pipeline across GPUs for batched greedy decode (one process per GPU, torch.distributed).
+"""A host-side model of the layer pipeline's schedule, for CPU tests (tests/test_pipeline_cpu.py): the
+same step order as the native pipeline in libxj_cuda.so (meta-work_b200/csrc/pipeline.cpp), driven over
+torch.distributed process groups (gloo on CPU) with stand-in stages. TEST INFRASTRUCTURE: the product's
+pipeline is the native one; this model checks the schedule and the data movement without GPUs.
 
 The reference splits a model into stages by layer range (``xj_net.h:93-111``: a|r|b) and drives them
 with ``xj_pipeline_eval`` over TCP. Here every rank holds one stage: a batch of ``n_seq`` sequences
@@ -11,23 +14,20 @@ owns the LM head and the greedy pick. Per decode step and micro-batch of rows:
 
 Micro-batches keep the stages busy at the same time: while the last stage works on micro-batch k of
 step s, the first stage already runs micro-batch k+1. Activations ([rows][n_embd] fp32) and ids go
-over NCCL (NVLink) on GPUs and over gloo in the CPU tests; they travel on two process groups, one per
-direction, so a send in one direction never waits behind a receive in the other on one communicator.
-On GPUs every stage call and every transfer is queued on the stage's own CUDA stream (the library's
-stream, wrapped as a torch external stream), so they are ordered on the device and the host never waits
-inside a step. The last rank sends each micro-batch's picks as soon as they are made, without waiting
+over gloo here (NCCL in the native pipeline); they travel on two process groups, one per direction,
+so a send in one direction never waits behind a receive in the other on one communicator. The last
+rank sends each micro-batch's picks as soon as they are made, without waiting
 for the send; rank 0 receives them only when the next step's micro-batch needs them. So the first
 stage starts micro-batch k of the next step as soon as that micro-batch's picks exist, and no stream
 ever holds a receive of activations behind a send of ids (which could deadlock the two communicators).
 KV caches and recurrent state stay on the rank that owns the layer.
 
-The per-stage compute is behind a small interface (``embed``, ``forward``, ``pick``) so that the
-schedule itself is tested on CPU with a stand-in stage (tests/test_pipeline_cpu.py).
+The per-stage compute is behind a small interface (``embed``, ``forward``, ``pick``), provided here by a
+stand-in stage.
 """
 from __future__ import annotations
 
 import contextlib
-import ctypes
 from dataclasses import dataclass
 
 import numpy as np
@@ -54,79 +54,6 @@ def micro_batches(n_seq: int, n_mb: int) -> list[tuple[int, int]]:
         out.append((r0, n))
         r0 += n
     return out
-
-
-class CudaStage:
-    """One rank's stage on its GPU: xj_cuda_batch over layers [l0, l1) (head on the last rank)."""
-
-    def __init__(self, model, l0: int, l1: int, has_head: bool, n_seq: int, n_ctx: int, device):
-        import torch
-        from . import xjcuda
-        self.xc, self.torch, self.device = xjcuda, torch, device
-        lib = xjcuda.lib()
-        vp, ip, cp, sz = ctypes.c_void_p, ctypes.c_int, ctypes.c_char_p, ctypes.c_size_t
-        for name, res, args in [
-            ("xj_cuda_batch_new_range", vp, [vp, ip, ip, ctypes.c_bool, ip, ip, cp, sz]),
-            ("xj_cuda_batch_embed_rows", ip, [vp, vp, vp, ip, cp, sz]),
-            ("xj_cuda_batch_forward_rows", ip, [vp, vp, ip, ip, cp, sz]),
-            ("xj_cuda_batch_pick_rows", ip, [vp, vp, ip, ip, vp, cp, sz]),
-            ("xj_cuda_batch_stream", vp, [vp]),
-            ("xj_cuda_batch_set_async", ip, [vp, ip]),
-            ("xj_cuda_batch_sync", ip, [vp, cp, sz]),
-        ]:
-            getattr(lib, name).restype = res
-            getattr(lib, name).argtypes = args
-        self.lib = lib
-        e = ctypes.create_string_buffer(512)
-        self.p = lib.xj_cuda_batch_new_range(model.ptr, l0, l1, has_head, n_seq, n_ctx, e, 512)
-        if not self.p:
-            raise xjcuda.XjError(e.value.decode(errors="replace"))
-        self.E = model.n_embd
-        self.has_head = has_head
-        self.first = l0 == 0
-        # queue-only stage calls, ordered with the caller's transfers on the library's stream
-        lib.xj_cuda_batch_set_async(self.p, 1)
-        self.stream = torch.cuda.ExternalStream(lib.xj_cuda_batch_stream(self.p), device=device)
-
-    def _check(self, rc, e):
-        if rc:
-            raise self.xc.XjError(e.value.decode(errors="replace"))
-
-    def new_x(self, nrows):
-        return self.torch.empty((nrows, self.E), dtype=self.torch.float32, device=self.device)
-
-    def context(self):
-        """Everything of a step runs on the stage's stream (transfers included)."""
-        return self.torch.cuda.stream(self.stream)
-
-    def sync(self):
-        # transfers run on the stage's own stream (see context), so a received tensor is ordered before
-        # the kernels that read it without waiting on the host
-        pass
-
-    def host_sync(self):
-        e = ctypes.create_string_buffer(512)
-        self._check(self.lib.xj_cuda_batch_sync(self.p, e, 512), e)
-
-    def new_ids(self, nrows):
-        return self.torch.empty(nrows, dtype=self.torch.int32, device=self.device)
-
-    def embed(self, ids, x):
-        e = ctypes.create_string_buffer(512)
-        self._check(self.lib.xj_cuda_batch_embed_rows(self.p, ids.data_ptr(), x.data_ptr(), ids.numel(), e, 512), e)
-
-    def forward(self, x, row0, nrows):
-        e = ctypes.create_string_buffer(512)
-        self._check(self.lib.xj_cuda_batch_forward_rows(self.p, x.data_ptr(), row0, nrows, e, 512), e)
-
-    def pick(self, x, row0, nrows, ids):
-        e = ctypes.create_string_buffer(512)
-        self._check(self.lib.xj_cuda_batch_pick_rows(self.p, x.data_ptr(), row0, nrows, ids.data_ptr(), e, 512), e)
-
-    def close(self):
-        if self.p:
-            self.xc.lib().xj_cuda_batch_free(self.p)
-            self.p = None
 
 
 @dataclass

@@ -1,4 +1,4 @@
-"""The layer-pipeline schedule (meta-work_b200/pipeline.py) on CPU: world-size-2 and -3 gloo process
+"""The layer-pipeline schedule (tests/pipeline_schedule.py, the step order of the native pipeline) on CPU: world-size-2 and -3 gloo process
 groups, micro-batches, ids flowing back to rank 0, against the same stages run in one process.
 
 The stand-in stage has the interface of the CUDA stage (embed / forward / pick on row ranges, each
@@ -53,7 +53,7 @@ class FakeStage:
 
 
 def reference(prompts, n_gen):
-    from xjb200 import pipeline as pl  # noqa: F401  (same package import path as the workers)
+    import pipeline_schedule as pl  # noqa: F401  (same import path as the workers)
     st = FakeStage(0, L, True, prompts.shape[0])
     out = []
     ids = None
@@ -78,7 +78,7 @@ def worker(rank, world, port, prompts, n_gen, n_mb, q):
     sys.path.insert(0, str(pathlib.Path(__file__).resolve().parent))
     from conftest import load_pkg
     load_pkg()
-    from xjb200 import pipeline as pl
+    import pipeline_schedule as pl
     dist.init_process_group("gloo", rank=rank, world_size=world)
     gx, gt = dist.new_group(list(range(world))), dist.new_group(list(range(world)))
     l0, l1 = pl.split_layers(L, world)[rank]
@@ -111,7 +111,7 @@ def test_pipeline_schedule_matches_single_process(world, n_mb):
 
 
 def test_split_helpers():
-    from xjb200 import pipeline as pl
+    import pipeline_schedule as pl
     assert pl.split_layers(28, 2) == [(0, 14), (14, 28)]
     assert pl.split_layers(7, 3) == [(0, 3), (3, 5), (5, 7)]
     assert pl.micro_batches(7, 3) == [(0, 3), (3, 2), (5, 2)]
