@@ -104,3 +104,16 @@ def test_loader_errors(tmp_path, tiny_path):
     cut.write_bytes(pathlib.Path(tiny_path).read_bytes()[:5000])
     with pytest.raises(xjcuda.XjError):
         xjcuda.Model(cut)
+
+
+def test_reference_session_layer_runs_on_cpu(tiny_path):
+    """The session-layer build the GPU test compares against (XJGlue.c with CPU stages) chats here."""
+    from oracle import glue
+    if not glue.available("cpu"):
+        pytest.skip("session-layer build missing")
+    h = glue.Host("cpu", tiny_path, 256)
+    try:
+        ans, st = h.chat("hello", 0.0, 8)
+        assert st.prompt_tokens > 0 and st.gen_tokens >= 0 and st.n_past >= st.prompt_tokens
+    finally:
+        h.close()
