@@ -197,22 +197,30 @@ def run_reference(args, rank, world):
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libxjref.so was not built"}))
         return
     cfg = synth.CONFIG3
-    path = synth.cached_gguf(cfg)
+    mdir = os.environ.get("XJ_MODEL_DIR", "/tmp/xj_models_r0")          # the repo arm's rank-0 model
+    path = synth.model_path(cfg, mdir)
+    if not path.exists():
+        # the model writer (libxj_synth.so) runs in a child process, so this arm's process maps only the
+        # reference's library
+        subprocess.run([sys.executable, "-c", "import bench; bench.load_pkg(); from xjb200 import synth; "
+                        f"synth.cached_gguf(synth.CONFIG3, {str(mdir)!r})"], cwd=str(ROOT), check=True)
     m = ref.Model(path)
     threads = os.cpu_count() or 1
     ref.set_threads(threads)
-    n_prompt = 32
+    # the repo arm's operating point: its 512-token prompt (prefill untimed), then K timed decode steps
+    n_prompt = args.prompt
     K = min(args.steps, 48)
     p = np.random.default_rng(1234).integers(0, cfg.n_vocab, n_prompt)
-    m.greedy(p, 2, max_batch=8, n_ctx=2048)                         # warm-up: pages the weights in
-    _, _, _, times = m.greedy(p, K + 1, max_batch=8, n_ctx=2048)
+    _, _, _, times = m.greedy(p, K + 1, max_batch=64, n_ctx=n_prompt + K + 16)
     v = K / times[1]
-    sample = f"{cfg.name}: {n_prompt}-token prompt, {K} greedy decode steps at batch 1, {threads} threads"
+    sample = (f"{cfg.name}: {n_prompt}-token prompt (prefill untimed, {times[0]:.1f} s), {K} greedy decode steps at "
+              f"batch 1 at positions {n_prompt}..{n_prompt + K - 1}, {threads} threads")
     print(json.dumps({
         "impl": "reference", "metric": METRIC, "value": round(v, 4), "unit": "tok/s", "n_gpus": world,
         "steps": K, "warmup": args.warmup, "ms_per_step": round(1e3 / v, 3), "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": cfg.name + " decode, batch 1", "prompt": n_prompt, "batch": 1},
+        "config": {"workload": f"{cfg.name} greedy decode, batch 1 per GPU", "prompt": n_prompt, "batch": 1,
+                   "same_config": True},
         "cpu_baseline": {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "reference", "sample": sample},
         "e2e": {"value": round(v, 4), "unit": "tok/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }))
@@ -233,7 +241,8 @@ def cpu_baseline(K_cap=24):
     _, _, _, times = m.greedy(p, K_cap + 1, max_batch=8, n_ctx=2048)
     v = K_cap / times[1]
     return {"value": round(v, 4), "unit": "tok/s", "cores": threads, "kind": "reference",
-            "sample": f"{cfg.name}: 32-token prompt, {K_cap} greedy decode steps at batch 1 (oracle/_ref, {threads} threads)"}
+            "sample": f"{cfg.name}: 32-token prompt, {K_cap} greedy decode steps at batch 1 at positions 32..{32 + K_cap - 1} "
+                      f"(oracle/_ref, {threads} threads)"}
 
 
 def run_gdn(xjcuda, peak, peak_kind):
@@ -507,7 +516,8 @@ def main():
     cfg = synth.CONFIG3
     path = synth.cached_gguf(cfg, os.environ.get("XJ_MODEL_DIR", f"/tmp/xj_models_r{local}"))
     model = xjcuda.Model(path)
-    n_ctx = args.prompt + max(args.warmup, 3) + 2 * args.steps + 16   # prefill + warm-up + timed + e2e runs
+    n_vt = min(args.steps, 32)                                        # steps of the vtable e2e run
+    n_ctx = args.prompt + max(args.warmup, 3) + 2 * args.steps + n_vt + 16   # prefill + warm-up + timed + e2e runs
     stage = xjcuda.Stage(model, 0, model.n_layer, n_ctx, 8)
     prompt = np.random.default_rng(1234 + rank).integers(0, cfg.n_vocab, args.prompt).astype(np.int32)
 
@@ -537,13 +547,23 @@ def main():
     toks2, _, _ = stage.decode(last, args.steps)
     torch.cuda.synchronize()
     e2e_ms = (time.perf_counter() - t0) * 1e3
+    # end to end through the drop-in vtable with host buffers, as the runtime's pipeline drives a stage
+    # (core/xj_net.c:532-605 via xj_pipeline_eval): embed on the host (xjc_embed), forward [1][E] in,
+    # logits [1][V] out, argmax on the host; n_vt steps by the host clock
+    tok = int(toks2[-1])
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(n_vt):
+        x = stage.forward(model.embed_many([tok]))
+        tok = int(np.argmax(stage.logits(x)[0]))
+    vt_ms = (time.perf_counter() - t0) * 1e3
     t_max = dev_ms
     e2e_max = e2e_ms
     if world > 1:
         import torch.distributed as dist
-        t = torch.tensor([dev_ms, e2e_ms], device="cuda")
+        t = torch.tensor([dev_ms, e2e_ms, vt_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_max, e2e_max = float(t[0]), float(t[1])
+        t_max, e2e_max, vt_ms = float(t[0]), float(t[1]), float(t[2])
     value = world * args.steps / (t_max / 1e3)
     e2e = world * args.steps / (e2e_max / 1e3)
     stage.close()
@@ -575,6 +595,9 @@ def main():
                        "l2": "weights 1.2 GB per step > 126 MB L2"},
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": round(4 / args.steps, 3),
                     "d2h_bytes_per_step": 4},
+            "e2e_vtable": {"value": round(world * n_vt / (vt_ms / 1e3), 2), "unit": "tok/s", "steps": n_vt,
+                           "h2d_bytes_per_step": 4 * cfg.n_embd, "d2h_bytes_per_step": 4 * cfg.n_vocab + 4 * cfg.n_embd,
+                           "path": "xj_stage forward + logits with host buffers, argmax and embedding on the host"},
             "roofline": {"bound": "hbm",
                          "kernel": "k_decode_persistent" if persistent else "decode-step CUDA graph",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

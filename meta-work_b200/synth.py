@@ -113,12 +113,17 @@ def write_gguf(path: str | os.PathLike, cfg: ModelConfig, threads: int = 0) -> i
     return n
 
 
+def model_path(cfg: ModelConfig, directory: str | os.PathLike | None = None) -> pathlib.Path:
+    """Where cached_gguf keeps `cfg` (default directory: $XJ_MODEL_DIR or /tmp/xj_models); nothing is written."""
+    d = pathlib.Path(directory or os.environ.get("XJ_MODEL_DIR", "/tmp/xj_models"))
+    key = hashlib.sha1(repr(dataclasses.astuple(cfg)).encode()).hexdigest()[:12]
+    return d / f"{cfg.name}-{key}.gguf"
+
+
 def cached_gguf(cfg: ModelConfig, directory: str | os.PathLike | None = None) -> pathlib.Path:
     """Path of `cfg` written once into `directory` (default: $XJ_MODEL_DIR or /tmp/xj_models)."""
-    d = pathlib.Path(directory or os.environ.get("XJ_MODEL_DIR", "/tmp/xj_models"))
-    d.mkdir(parents=True, exist_ok=True)
-    key = hashlib.sha1(repr(dataclasses.astuple(cfg)).encode()).hexdigest()[:12]
-    p = d / f"{cfg.name}-{key}.gguf"
+    p = model_path(cfg, directory)
+    p.parent.mkdir(parents=True, exist_ok=True)
     if not p.exists():
         tmp = p.with_suffix(f".tmp{os.getpid()}")
         write_gguf(tmp, cfg)
