@@ -39,17 +39,52 @@ def lib(which: str) -> ctypes.CDLL:
     L.xjg_host_reset.argtypes = [vp, cp, ip]
     L.xjg_host_free.restype = None
     L.xjg_host_free.argtypes = [vp]
+    L.xjg_worker_new.restype = vp
+    L.xjg_worker_new.argtypes = [cp, ip, ip, ctypes.c_uint32, vp, vp, cp, ip]
+    L.xjg_worker_run.restype = ip
+    L.xjg_worker_run.argtypes = [vp, ip, cp, ip]
+    L.xjg_worker_stop.restype = None
+    L.xjg_worker_stop.argtypes = [vp]
+    L.xjg_worker_free.restype = None
+    L.xjg_worker_free.argtypes = [vp]
     return L
 
 
-class Host:
-    """One xjg_host (whole model on this machine: no worker)."""
+class Worker:
+    """xjg_worker (XJGlue.h:27-32): holds layers [l0, l1) and serves them over the reference's TCP protocol
+    (core/xj_net.c:119-292) on a background thread; the stage backend is the build's (CPU or CUDA)."""
 
-    def __init__(self, which: str, path, n_ctx: int = 512, mtp_path=None, draft: int = 0):
+    def __init__(self, which: str, path, l0: int, l1: int, port: int, pin: int):
+        import threading
         self.L = lib(which)
-        info, err = ctypes.create_string_buffer(512), ctypes.create_string_buffer(512)
-        self.h = self.L.xjg_host_new(str(path).encode(), b"", 0, 0, 0, 0, n_ctx,
-                                     str(mtp_path).encode() if mtp_path else None, draft, info, 512, err, 512)
+        err = ctypes.create_string_buffer(512)
+        self.w = self.L.xjg_worker_new(str(path).encode(), l0, l1, pin, None, None, err, 512)
+        if not self.w:
+            raise RuntimeError(err.value.decode(errors="replace"))
+        self.port, self.rc, self.err = port, None, ctypes.create_string_buffer(512)
+        self.t = threading.Thread(target=self._run, daemon=True)
+        self.t.start()
+
+    def _run(self):
+        self.rc = self.L.xjg_worker_run(self.w, self.port, self.err, 512)
+
+    def close(self):
+        if self.w:
+            self.L.xjg_worker_stop(self.w)
+            self.t.join(timeout=30)
+            self.L.xjg_worker_free(self.w)
+            self.w = None
+
+
+class Host:
+    """One xjg_host: the whole model on this machine, or layers [s1, s2) on a worker at worker:port."""
+
+    def __init__(self, which: str, path, n_ctx: int = 512, mtp_path=None, draft: int = 0, worker: str = "",
+                 port: int = 0, pin: int = 0, s1: int = 0, s2: int = 0):
+        self.L = lib(which)
+        info, err = ctypes.create_string_buffer(1024), ctypes.create_string_buffer(512)
+        self.h = self.L.xjg_host_new(str(path).encode(), worker.encode(), port, pin, s1, s2, n_ctx,
+                                     str(mtp_path).encode() if mtp_path else None, draft, info, 1024, err, 512)
         if not self.h:
             raise RuntimeError(err.value.decode(errors="replace"))
         self.info = info.value.decode(errors="replace")
