@@ -308,43 +308,50 @@ def gemv_kw(args) -> dict:
 
 
 def run_spec(args, model, rank, world, barrier, xjcuda, synth, local):
-    """Speculative decoding (config 4): greedy speculative decoding, target = config 3, draft = the E=1024 8-layer Q8_0
-    model with the target's vocabulary, k = 4; args.spec seeded 256-token prompts per GPU, 256 tokens each.
-    Output ids equal plain greedy decoding by construction (tested); reports emitted tokens/s and target
-    forwards/s over the whole job (prompt processing included), and the acceptance of drafted tokens."""
+    """Speculative decoding (config 4): target = config 3, draft = the E=1024 8-layer Q8_0 model with the
+    target's vocabulary, k = 4, greedy acceptance; args.spec seeded 256-token prompts in total, sharded
+    over the ranks (args.spec / world sequences per GPU), args.spec_gen tokens each. Every GPU decodes its
+    sequences as one batch (xj_cuda_batch_spec_decode): the draft proposes k tokens per sequence, the
+    target verifies k + 1 tokens of all its sequences in one forward on the tensor cores. Output ids equal
+    plain greedy decoding (tested). Timed: the whole call (prompts included), device time on the target's
+    stream, max over ranks; e2e = the same call by the host clock."""
     import torch
     dpath = synth.cached_gguf(synth.DRAFT, os.environ.get("XJ_MODEL_DIR", f"/tmp/xj_models_r{local}"))
     dmodel = xjcuda.Model(dpath)
-    n_prompt, n_gen, k = 256, 256, 4
-    rng = np.random.default_rng(777 + rank)
-    prompts = rng.integers(0, model.n_vocab, (args.spec, n_prompt)).astype(np.int32)
-    stats = np.zeros(4, np.int64)
+    n_prompt, n_gen, k = 256, args.spec_gen, 4
+    per = max(1, args.spec // world)
+    allp = np.random.default_rng(777).integers(0, model.n_vocab, (per * world, n_prompt)).astype(np.int32)
+    prompts = allp[rank * per:(rank + 1) * per]
+    n_ctx = n_prompt + n_gen * (k + 1) + k + 8
+    target = xjcuda.Batch(model, per, n_ctx, max_tokens=k + 1)
+    draft = xjcuda.Batch(dmodel, per, n_ctx, max_tokens=8)
     barrier()
     t0 = time.perf_counter()
-    for i in range(args.spec):
-        t = xjcuda.Stage(model, 0, model.n_layer, n_prompt + n_gen + 16, 16)
-        d = xjcuda.Stage(dmodel, 0, dmodel.n_layer, n_prompt + n_gen + 16, 16)
-        _, st = t.spec_decode(d, prompts[i], n_gen, k)
-        stats += np.array(st, np.int64)
-        t.close()
-        d.close()
+    _, st, ms = target.spec_decode(draft, prompts, n_gen, k)
     torch.cuda.synchronize()
-    wall = time.perf_counter() - t0
-    w = wall
+    wall = (time.perf_counter() - t0) * 1e3
+    target.close()
+    draft.close()
+    v = torch.tensor([ms, wall, st[0]], device="cuda", dtype=torch.float64)
     if world > 1:
         import torch.distributed as dist
-        x = torch.tensor([wall], device="cuda")
-        dist.all_reduce(x, op=dist.ReduceOp.MAX)
-        w = float(x[0])
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+    t_max, w_max, rounds_max = float(v[0]), float(v[1]), int(v[2])
     if rank != 0:
         return None
-    return {"workload": "config4 speculative: target config3, draft 1024x8 Q8_0 (vocab 151936), k=4",
-            "prompts_per_gpu": args.spec, "prompt": n_prompt, "gen": n_gen,
-            "value": round(world * args.spec * n_gen / w, 1), "unit": "emitted tok/s",
-            "target_forwards_per_s": round(world * int(stats[0]) / w, 1),
-            "acceptance": round(int(stats[2]) / max(1, int(stats[1])), 4),
-            "rounds": int(stats[0]), "drafted": int(stats[1]), "accepted": int(stats[2]),
-            "timing": "host wall clock per GPU, max over ranks, stages built and prompts processed inside"}
+    total = per * world
+    return {"workload": "config4 speculative: target config3, draft 1024x8 Q8_0 (vocab 151936), k=4, batched verify",
+            "sequences_total": total, "sequences_per_gpu": per, "prompt": n_prompt, "gen": n_gen,
+            "value": round(total * n_gen / (t_max / 1e3), 1), "unit": "emitted tok/s",
+            "accepted_tok_s_rank0": round(st[2] / (t_max / 1e3), 1),
+            "target_forwards_per_s": round(rounds_max / (t_max / 1e3), 2),
+            "target_rows_per_s": round(world * st[3] * per / (t_max / 1e3), 1),
+            "acceptance": round(st[2] / max(1, st[1]), 4),
+            "rounds_rank0": st[0], "drafted_rank0": st[1], "accepted_rank0": st[2],
+            "e2e": {"value": round(total * n_gen / (w_max / 1e3), 1), "unit": "emitted tok/s", "step": "one verify round",
+                    "h2d_bytes_per_step": round(4 * per * n_prompt / max(1, st[0]), 1),
+                    "d2h_bytes_per_step": round(4 * per + 4 * per * n_gen / max(1, st[0]), 1)},
+            "timing": "device time of one xj_cuda_batch_spec_decode call per GPU (prompts included), max over ranks"}
 
 
 def run_batch(args, cfg, model, rank, world, barrier, xjcuda, n_seq=None):
@@ -491,8 +498,9 @@ def main():
     ap.add_argument("--micro-batches", type=int, default=2)
     ap.add_argument("--strong", type=int, default=1,
                     help="with several GPUs, also time --batch sequences in total: sharded and through the layer pipeline")
-    ap.add_argument("--spec", type=int, default=0,
-                    help="config 4: speculative decoding of this many 256-token prompts per GPU (0: skip)")
+    ap.add_argument("--spec", type=int, default=64,
+                    help="config 4: batched speculative decoding of this many 256-token prompts in total (0: skip)")
+    ap.add_argument("--spec-gen", type=int, default=256, help="config 4: tokens generated per prompt")
     args = ap.parse_args()
     rank, local, world = dist_env()
     load_pkg()

@@ -172,6 +172,22 @@ int xj_cuda_batch_decode(xj_cuda_batch *b, const int32_t *prompts, int n_prompt,
 // the decode steps after them. Returns their sum.
 long long xj_cuda_batch_last_launches(const xj_cuda_batch *b, long long *launches);
 
+// A batch that also takes up to max_tokens (1..16) tokens of every sequence in one forward: prompts of
+// batches wider than 16 sequences go through in chunks of max_tokens, and the batch can be the target of
+// xj_cuda_batch_spec_decode (max_tokens >= k + 1). n_seq * max_tokens <= 4096.
+xj_cuda_batch *xj_cuda_batch_new_multi(const xj_model *m, int n_seq, int n_ctx, int max_tokens, char *err, size_t errlen);
+// Greedy speculative decoding of every sequence of a batch with a draft batch (core/xj_spec.c:131-209,
+// for all sequences at once): both take the prompts [n_seq][n_prompt]; each round the draft proposes k
+// tokens per sequence, the target verifies [last, k drafts] of all sequences in one (k+1)-token forward
+// (its matrix products on the tensor cores), each sequence keeps its agreeing prefix plus the target's
+// own next pick, and both batches roll each sequence back to what it keeps. out [n_seq][n_gen] equals
+// plain greedy decoding of the target. stats[4] (may be NULL): verify rounds, drafted tokens, accepted
+// drafted tokens, target token-rows processed. gpu_ms (may be NULL): device time of the call. Both
+// batches hold the same number of sequences at the same position on one device; the contexts need
+// n_past + n_prompt + n_gen * (k + 1) + k + 1 positions (a sequence can run ahead of the slowest).
+int xj_cuda_batch_spec_decode(xj_cuda_batch *target, xj_cuda_batch *draft, const int32_t *prompts, int n_prompt, int n_gen,
+                              int k, int32_t *out, long long *stats, float *gpu_ms, char *err, size_t errlen);
+
 // Pipeline stages (layer pipeline across GPUs: each GPU holds a batch over its layer range [l0, l1),
 // the last one with the head). Device buffers belong to the batch's device; calls return after the work
 // is done. Rows [row0, row0+nrows) of the batch form a micro-batch; x_dev holds its nrows rows of

@@ -842,6 +842,116 @@ __global__ void __launch_bounds__(4 * S, 2) k_gdn_batch(GdnArgs a, long long sta
     gdn_head<S, BarBlock>(c, blockIdx.x, threadIdx.x);
 }
 
+// ---------------------------------------------------------------- several tokens of every sequence
+// B sequences x T tokens in one forward, rows b*T + t (speculative verify of a batch, chunked prefill of
+// a batch); per token the arithmetic of the one-token kernels.
+
+// Grid (Hv, B), 4*S threads: the T tokens of sequence b in order through its own state (gdn_head's token
+// loop, as for a single-sequence prompt). ck_ssm (may be null): state after token t < T-1 at
+// ck_ssm + b*ck_stride + t*Hv*S*S.
+template <int S>
+__global__ void __launch_bounds__(4 * S, 2) k_gdn_batch_multi(GdnArgs a, long long state_stride, long long ck_stride) {
+    griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
+    const int b = blockIdx.y;
+    const long long r = (long long)b * a.T;      // the sequence's first row
+    GdnArgs c = a;
+    c.qkv += r * a.ldq; c.z += r * a.ldz; c.beta += r * a.ldg; c.alpha += r * a.ldg;
+    c.ssm += b * state_stride; c.out += r * a.ldo;
+    c.ck_ssm = a.ck_ssm ? a.ck_ssm + b * ck_stride : nullptr;
+    gdn_head<S, BarBlock>(c, blockIdx.x, threadIdx.x);
+}
+
+// Grid (ceil(CD / 128), B), 128 threads: channel ch of sequence b takes the raw projections of its T
+// tokens in order through its rolling conv state, with the arithmetic of the GEMV conv epilogue
+// (y = silu(sum_k state_k w_k + raw w_last), core/xj_cpu.c:167-176). ck (may be null): the state after
+// token t < T-1 at ck[b][t][CD][kc-1]. kc <= 9.
+static __global__ void __launch_bounds__(128) k_conv_batch_multi(const float *raw, long long ldr, float *y, long long ldy,
+                                                                 float *state, const float *w, int CD, int kc, int T,
+                                                                 float *ck) {
+    griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
+    if (ch >= CD) return;
+    float *st = state + ((size_t)b * CD + ch) * (kc - 1);
+    const float *wc = w + (size_t)ch * kc;
+    float cs[8];
+    for (int k = 0; k < kc - 1; k++) cs[k] = st[k];
+    for (int t = 0; t < T; t++) {
+        const size_t row = (size_t)b * T + t;
+        const float s = raw[row * ldr + ch];
+        float acc = 0.0f;
+        for (int k = 0; k < kc - 1; k++) acc = fmaf(cs[k], wc[k], acc);
+        acc = fmaf(s, wc[kc - 1], acc);
+        for (int k = 0; k < kc - 2; k++) cs[k] = cs[k + 1];
+        cs[kc - 2] = s;
+        y[row * ldy + ch] = silu_f(acc);
+        if (ck && t < T - 1)
+            for (int k = 0; k < kc - 1; k++) ck[(((size_t)b * (T - 1) + t) * CD + ch) * (kc - 1) + k] = cs[k];
+    }
+    for (int k = 0; k < kc - 1; k++) st[k] = cs[k];
+}
+
+// Grid (blocks, B), 256 threads: sequence b keeps the first keep[b] (1..T) tokens of its last T-token
+// forward: its n-float state becomes the copy taken after token keep[b]-1, at
+// ck + b*ck_bstride + (keep[b]-1)*ck_slot (nothing to do when keep[b] == T: the state is current).
+static __global__ void __launch_bounds__(256) k_batch_keep_state(float *state, long long n, const float *ck, long long ck_bstride,
+                                                                 long long ck_slot, const int *keep, int T) {
+    griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
+    const int b = blockIdx.y, kb = keep[b];
+    if (kb >= T || kb < 1) return;
+    const float *src = ck + b * ck_bstride + (kb - 1) * ck_slot;
+    float *dst = state + b * n;
+    const long long i0 = (long long)blockIdx.x * blockDim.x + threadIdx.x, step = (long long)gridDim.x * blockDim.x;
+    if ((n & 3) == 0 && (ck_bstride & 3) == 0 && (ck_slot & 3) == 0)
+        for (long long i = i0; i < n / 4; i += step)
+            reinterpret_cast<float4 *>(dst)[i] = __ldcg(reinterpret_cast<const float4 *>(src) + i);
+    else
+        for (long long i = i0; i < n; i += step) dst[i] = __ldcg(src + i);
+}
+
+// npast[b] -= T - keep[b] (the tokens a sequence did not keep); one block.
+static __global__ void k_batch_keep_pos(int *npast, const int *keep, int T, int B) {
+    griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
+    for (int b = threadIdx.x; b < B; b += blockDim.x) npast[b] -= T - keep[b];
+}
+
+// Greedy acceptance of one speculative round for every sequence (one thread each), the rule of
+// core/xj_spec.c:131-209: drafts d[b*ldd + i] (i < k), target picks p[b*(k+1) + t] after token t of the
+// verified [last, d_0 .. d_(k-1)]; a = the longest prefix with d_i == p_i; the round emits d_0 .. d_(a-1)
+// and p_a into out[b][n[b]..] (at most n_gen in all), keeps a + 1 tokens of the verify forward
+// (keep[b]) and feeds p_a next (next[b]). stats[0] += k (drafted), stats[1] += a (accepted).
+static __global__ void k_spec_accept_batch(const int32_t *d, int ldd, const int32_t *p, int k, int B, int32_t *out,
+                                           long long out_stride, int *n, int n_gen, int *keep, int32_t *next,
+                                           unsigned long long *stats) {
+    griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const int32_t *db = d + (size_t)b * ldd, *pb = p + (size_t)b * (k + 1);
+    int a = 0;
+    while (a < k && db[a] == pb[a]) a++;
+    int c = n[b];
+    for (int i = 0; i <= a && c < n_gen; i++, c++) out[b * out_stride + c] = i < a ? db[i] : pb[a];
+    n[b] = c;
+    keep[b] = a + 1;
+    next[b] = pb[a];
+    atomicAdd(&stats[0], (unsigned long long)k);
+    atomicAdd(&stats[1], (unsigned long long)a);
+}
+
+// The verify rows of a speculative round: row b*(k+1) = last[b], row b*(k+1) + 1 + i = d[b*ldd + i].
+static __global__ void k_spec_rows(const int32_t *last, const int32_t *d, int ldd, int k, int B, int32_t *rows) {
+    griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
+    const int i = blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= B * (k + 1)) return;
+    const int b = i / (k + 1), t = i % (k + 1);
+    rows[i] = t == 0 ? last[b] : d[(size_t)b * ldd + t - 1];
+}
+
 template <typename KV>
 XJ_DEV AttnArgs attn_seq(const AttnArgs &a, const int *npast_b, long long kv_stride, int b) {
     AttnArgs c = a;

@@ -997,6 +997,21 @@ struct BatchImpl {
     int step_kernels = 0;
     long long last_launches[2] = {0, 0};
     bool async_rows = false;               // *_rows calls return without waiting for the stream
+    // several tokens per sequence in one forward (xj_cuda_batch_new_spec): chunked prefill, speculative
+    // verify. Rows b*T + t. Buffers of B*tmax rows; checkpoints allocated on the first verify.
+    int tmax = 1;
+    float *conv_raw = nullptr;             // [B*tmax][conv_dim] raw qkv projections
+    int32_t *rows_tok = nullptr, *picks = nullptr;   // [B*tmax]
+    float *x_multi = nullptr, *x_last = nullptr;     // [B*tmax][E], [B][E]
+    std::vector<float *> ck_ssm, ck_conv;  // per layer: [B][tmax-1][state] after each verified token
+    // speculative rounds (target side): acceptance per sequence
+    int *keep = nullptr, *nout = nullptr;
+    int32_t *next = nullptr, *spec_out = nullptr;
+    int spec_out_cap = 0;
+    unsigned long long *spec_stats = nullptr;
+    // draft side: the recurrent state after each of the first k drafting steps, per layer [k][B][state]
+    std::vector<float *> snap_ssm, snap_conv;
+    int snap_k = 0;
 };
 
 // Layers of the batch's stage on rows x[0..nr) = sequences r0..r0+nr-1 (their own states and positions).
@@ -1069,6 +1084,133 @@ void run_layers_batch(BatchImpl *bi, float *x, int r0, int nr) {
         down.epi = EPI_ADD;
         gemv(im, im->g, im->u, FF, B, PRO_SWIGLU, nullptr, eps, {down});
     }
+}
+
+// Layers of the batch's stage on T tokens of every sequence at once (rows b*T + t of x, T <= tmax): the
+// one-token kernels per token (the same arithmetic), the conv through its own kernel so each sequence's
+// tokens pass its rolling state in order, attention token by token (token t at position npast[b] + t).
+// ck: checkpoints of each sequence's GDN and conv state after tokens t < T-1 (speculative verify).
+// Positions advance by `advance` at the end.
+void run_layers_batch_multi(BatchImpl *bi, float *x, int T, bool ck, int advance) {
+    xj_stage *s = bi->s;
+    Impl *im = I(s);
+    const xj_hparams *hp = &s->m->hp;
+    const int E = hp->n_embd, FF = hp->n_ff, B = bi->B, R = B * T;
+    const float eps = hp->eps;
+    for (int il = s->l0; il < s->l1; il++) {
+        Layer &Ly = im->L[il - s->l0];
+        const int li = il - s->l0;
+        if (Ly.rec) {
+            const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v, kc = hp->conv_k;
+            gemv(im, x, nullptr, E, R, PRO_NORM, Ly.attn_norm, eps,
+                 {{Ly.qkv, bi->conv_raw, CD}, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
+            launch(im, k_conv_batch_multi, dim3((CD + 127) / 128, B), dim3(128), 0, (const float *)bi->conv_raw,
+                   (long long)CD, im->qkvb, (long long)CD, bi->conv[li], (const float *)Ly.conv_w, CD, kc, T,
+                   ck ? bi->ck_conv[li] : (float *)nullptr);
+            GdnArgs g = gdn_args(im, hp, Ly, T, false);
+            g.ssm = bi->ssm[li];
+            g.ck_ssm = ck ? bi->ck_ssm[li] : nullptr;
+            const long long ss = (long long)hp->h_v * hp->s_v * hp->s_k, cks = (long long)(T - 1) * ss;
+            switch (hp->s_k) {
+            case 16: launch(im, k_gdn_batch_multi<16>, dim3(Hv, B), dim3(64), 0, g, ss, cks); break;
+            case 32: launch(im, k_gdn_batch_multi<32>, dim3(Hv, B), dim3(128), 0, g, ss, cks); break;
+            case 64: launch(im, k_gdn_batch_multi<64>, dim3(Hv, B), dim3(256), 0, g, ss, cks); break;
+            default: launch(im, k_gdn_batch_multi<128>, dim3(Hv, B), dim3(512), 0, g, ss, cks); break;
+            }
+            Job out{Ly.out, x, E};
+            out.epi = EPI_ADD;
+            gemv(im, im->o, nullptr, DI, R, PRO_NONE, nullptr, eps, {out});
+        } else {
+            const int H = hp->n_head, Hkv = hp->n_head_kv, D = hp->head_dim, nq = 2 * H * D, nk = Hkv * D;
+            const float *q, *k, *v;
+            long long ldq, ldkv;
+            if (Ly.fused) {
+                gemv(im, x, nullptr, E, R, PRO_NORM, Ly.attn_norm, eps, {{Ly.wqkv, im->qkvb, nq + 2 * nk}});
+                q = im->qkvb; k = im->qkvb + nq; v = im->qkvb + nq + nk; ldq = ldkv = nq + 2 * nk;
+            } else {
+                gemv(im, x, nullptr, E, R, PRO_NORM, Ly.attn_norm, eps,
+                     {{Ly.wq, im->q, nq}, {Ly.wk, im->k, nk}, {Ly.wv, im->v, nk}});
+                q = im->q; k = im->k; v = im->v; ldq = nq; ldkv = nk;
+            }
+            const long long kvs = (long long)bi->n_ctx * nk;
+            const int dpl = (D + 31) / 32;
+            for (int t = 0; t < T; t++) {
+                // token t of every sequence: rows t, t + T, ... (strides of T rows), position npast[b]
+                AttnArgs a = attn_args(im, hp, Ly, q + t * ldq, ldq * T, k + t * ldkv, v + t * ldkv, ldkv * T);
+                a.out = im->o + (size_t)t * H * D;
+                a.ldo = (long long)T * H * D;
+                a.kc = bi->kc[li]; a.vc = bi->vc[li];
+                if (im->kv_f32) {
+                    launch(im, k_attn_prep_batch<float>, dim3(H + Hkv, B), dim3((D + 31) / 32 * 32), 0, a, (const int *)bi->npast, kvs);
+                    if (dpl == 1) launch(im, k_attn_batch<float, 1>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                    else if (dpl == 2) launch(im, k_attn_batch<float, 2>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                    else if (dpl <= 4) launch(im, k_attn_batch<float, 4>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                    else launch(im, k_attn_batch<float, 8>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                } else {
+                    launch(im, k_attn_prep_batch<__half>, dim3(H + Hkv, B), dim3((D + 31) / 32 * 32), 0, a, (const int *)bi->npast, kvs);
+                    if (dpl == 1) launch(im, k_attn_batch<__half, 1>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                    else if (dpl == 2) launch(im, k_attn_batch<__half, 2>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                    else if (dpl <= 4) launch(im, k_attn_batch<__half, 4>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                    else launch(im, k_attn_batch<__half, 8>, dim3(H, B), dim3(128), 0, a, (const int *)bi->npast, kvs);
+                }
+                launch(im, k_advance_batch, dim3(1), dim3(256), 0, bi->npast, B, 1);
+            }
+            launch(im, k_advance_batch, dim3(1), dim3(256), 0, bi->npast, B, -T);
+            Job o{Ly.wo, x, E};
+            o.epi = EPI_ADD;
+            gemv(im, im->o, nullptr, (long long)H * D, R, PRO_NONE, nullptr, eps, {o});
+        }
+        gemv(im, x, nullptr, E, R, PRO_NORM, Ly.post_norm, eps, {{Ly.ffn_gate, im->g, FF}, {Ly.ffn_up, im->u, FF}});
+        Job down{Ly.ffn_down, x, E};
+        down.epi = EPI_ADD;
+        gemv(im, im->g, im->u, FF, R, PRO_SWIGLU, nullptr, eps, {down});
+    }
+    if (advance) launch(im, k_advance_batch, dim3(1), dim3(256), 0, bi->npast, B, advance);
+}
+
+// Prompts of every sequence (host [B][n]) through the batch in chunks of up to tmax tokens per
+// sequence, continuing from the sequences' positions, which advance by n. copy_last: the last prompt
+// token's activation row of each sequence into x_last [B][E] (for the head). Queued on the stage stream;
+// the ids go through bi->prompts (capacity B*n, grown here).
+int batch_prefill(BatchImpl *bi, const int32_t *prompts, int n, bool copy_last, char *err, size_t errlen) {
+    xj_stage *s = bi->s;
+    Impl *im = I(s);
+    const int B = bi->B, E = s->m->hp.n_embd, tm = bi->tmax;
+    if (n > bi->prompt_cap) {
+        CK(cudaStreamSynchronize(im->st));
+        if (dalloc(im, &bi->prompts, (size_t)B * n, err, errlen)) return -1;
+        bi->prompt_cap = n;
+    }
+    // chunk-major ids: chunk [i0, i0 + Tc) holds B*Tc ids at offset i0*B, rows b*Tc + t
+    std::vector<int32_t> h((size_t)B * n);
+    for (int i0 = 0; i0 < n; i0 += tm) {
+        const int Tc = n - i0 < tm ? n - i0 : tm;
+        for (int b = 0; b < B; b++)
+            for (int t = 0; t < Tc; t++) h[(size_t)i0 * B + (size_t)b * Tc + t] = prompts[(size_t)b * n + i0 + t];
+    }
+    CK(cudaMemcpyAsync(bi->prompts, h.data(), h.size() * sizeof(int32_t), cudaMemcpyHostToDevice, im->st));
+    CK(cudaStreamSynchronize(im->st));   // h is a host temporary
+    for (int i0 = 0; i0 < n; i0 += tm) {
+        const int Tc = n - i0 < tm ? n - i0 : tm;
+        launch(im, k_embed, dim3((E / 8 + 127) / 128, B * Tc), dim3(128), 0, im->tok_embd,
+               (const int32_t *)(bi->prompts + (size_t)i0 * B), B * Tc, im->x, E);
+        run_layers_batch_multi(bi, im->x, Tc, false, Tc);
+        if (copy_last && i0 + Tc == n)
+            CK(cudaMemcpy2DAsync(bi->x_last, sizeof(float) * E, im->x + (size_t)(Tc - 1) * E, sizeof(float) * E * Tc,
+                                 sizeof(float) * E, B, cudaMemcpyDeviceToDevice, im->st));
+    }
+    bi->n_past += n;
+    return 0;
+}
+
+// LM head and greedy pick of R rows of x: ids[r] (lowest id on equal logits).
+void head_pick_rows(BatchImpl *bi, const float *x, int R, int32_t *ids) {
+    xj_stage *s = bi->s;
+    Impl *im = I(s);
+    const xj_hparams *hp = &s->m->hp;
+    const int V = im->output.N;
+    gemv(im, x, nullptr, hp->n_embd, R, PRO_NORM, im->output_norm, hp->eps, {{im->output, im->logits, V}});
+    launch(im, k_argmax_pick_rows, dim3(R), dim3(1024), 0, (const float *)im->logits, V, ids);
 }
 
 // Output norm + LM head for rows x[0..nr) = sequences r0.., then each sequence's greedy pick: out_tok of
@@ -1905,12 +2047,14 @@ struct xj_cuda_batch {
     BatchImpl impl;
 };
 
-xj_cuda_batch *xj_cuda_batch_new_range(const xj_model *m, int l0, int l1, bool has_head, int n_seq, int n_ctx, char *err,
-                                       size_t errlen) {
+static xj_cuda_batch *batch_new(const xj_model *m, int l0, int l1, bool has_head, int n_seq, int n_ctx, int tmax, char *err,
+                                size_t errlen) {
     if (!m || n_seq < 1 || n_seq > 1024 || n_ctx < 1) { seterr(err, errlen, "need 1 <= n_seq <= 1024 and n_ctx >= 1"); return nullptr; }
+    if (tmax < 1 || tmax > 16 || (long long)n_seq * tmax > 4096) { seterr(err, errlen, "need 1 <= max_tokens <= 16 and n_seq * max_tokens <= 4096"); return nullptr; }
     if (l0 < 0 || l1 > m->hp.n_layer || l0 >= l1) { seterr(err, errlen, "bad layer range [%d,%d)", l0, l1); return nullptr; }
-    // the stage holds the weights and n_seq-row activation buffers; its own single-sequence state is minimal
-    xj_stage *s = xj_cuda_stage_new(m, l0, l1, 1, n_seq, has_head, err, errlen);
+    if (tmax > 1 && m->hp.conv_k > 9) { seterr(err, errlen, "multi-token forwards need conv_k <= 9"); return nullptr; }
+    // the stage holds the weights and n_seq*tmax-row activation buffers; its own single-sequence state is minimal
+    xj_stage *s = xj_cuda_stage_new(m, l0, l1, 1, n_seq * tmax, has_head, err, errlen);
     if (!s) return nullptr;
     xj_cuda_batch *b = new xj_cuda_batch();
     BatchImpl *bi = &b->impl;
@@ -1941,14 +2085,29 @@ xj_cuda_batch *xj_cuda_batch_new_range(const xj_model *m, int l0, int l1, bool h
         dalloc(im, &bi->out_tok, (size_t)n_seq * bi->out_cap, err, errlen) ||
         dalloc(im, &bi->margin, (size_t)n_seq * bi->out_cap, err, errlen)) return fail();
     if ((l0 == 0 || has_head) && !im->tok_embd.p && upload(im, m->tok_embd, &im->tok_embd, err, errlen, true)) return fail();
+    bi->tmax = tmax;
+    if (dalloc(im, &bi->conv_raw, (size_t)n_seq * tmax * hp->conv_dim, err, errlen) ||
+        dalloc(im, &bi->rows_tok, (size_t)n_seq * tmax, err, errlen) || dalloc(im, &bi->picks, (size_t)n_seq * tmax, err, errlen) ||
+        dalloc(im, &bi->x_last, (size_t)n_seq * hp->n_embd, err, errlen))
+        return fail();
     if (cudaDeviceSynchronize() != cudaSuccess) { seterr(err, errlen, "CUDA error while creating the batch"); return fail(); }
     if (batch_reset_state(bi, err, errlen)) return fail();
     return b;
 }
 
+xj_cuda_batch *xj_cuda_batch_new_range(const xj_model *m, int l0, int l1, bool has_head, int n_seq, int n_ctx, char *err,
+                                       size_t errlen) {
+    return batch_new(m, l0, l1, has_head, n_seq, n_ctx, 1, err, errlen);
+}
+
 xj_cuda_batch *xj_cuda_batch_new(const xj_model *m, int n_seq, int n_ctx, char *err, size_t errlen) {
     if (!m) { seterr(err, errlen, "null model"); return nullptr; }
-    return xj_cuda_batch_new_range(m, 0, m->hp.n_layer, true, n_seq, n_ctx, err, errlen);
+    return batch_new(m, 0, m->hp.n_layer, true, n_seq, n_ctx, 1, err, errlen);
+}
+
+xj_cuda_batch *xj_cuda_batch_new_multi(const xj_model *m, int n_seq, int n_ctx, int max_tokens, char *err, size_t errlen) {
+    if (!m) { seterr(err, errlen, "null model"); return nullptr; }
+    return batch_new(m, 0, m->hp.n_layer, true, n_seq, n_ctx, max_tokens, err, errlen);
 }
 
 void xj_cuda_batch_free(xj_cuda_batch *b) {
@@ -1991,21 +2150,33 @@ int xj_cuda_batch_decode(xj_cuda_batch *b, const int32_t *prompts, int n_prompt,
         if (dalloc(im, &bi->prompts, (size_t)B * n_prompt, err, errlen)) return -1;
         bi->prompt_cap = n_prompt;
     }
-    // prompts [B][n_prompt] -> device [n_prompt][B]: the tokens of step i are contiguous (the pageable
-    // source is consumed before the call returns; the copy is ordered on the stage stream)
-    std::vector<int32_t> tp((size_t)B * n_prompt);
-    for (int bq = 0; bq < B; bq++)
-        for (int i = 0; i < n_prompt; i++) tp[(size_t)i * B + bq] = prompts[(size_t)bq * n_prompt + i];
-    CK(cudaMemcpyAsync(bi->prompts, tp.data(), tp.size() * sizeof(int32_t), cudaMemcpyHostToDevice, im->st));
     CK(cudaMemsetAsync(bi->step, 0, sizeof(int) * B, im->st));
-    CK(cudaEventRecord(im->ev[0], im->st));
     const long long nl0 = im->nlaunch;
-    for (int i = 0; i < n_prompt; i++) {
-        launch(im, k_embed, dim3((E / 8 + 127) / 128, B), dim3(128), 0, im->tok_embd, (const int32_t *)(bi->prompts + (size_t)i * B), B,
-               im->x, E);
-        run_layers_batch(bi, im->x, 0, B);
-        if (i + 1 < n_prompt) launch(im, k_advance_batch, dim3(1), dim3(256), 0, bi->npast, B, 1);
-        else head_batch(bi, im->x, 0, B, bi->cur, im->x, bi->npast);   // out[:, 0], its embedding into x, position + 1
+    // a batch wider than 16 sequences takes its prompt in chunks of up to tmax tokens per sequence (its
+    // matrix products run on the 64-row kernels either way, where a token's result does not depend on
+    // the other rows of the launch, so the ids are those of the one-token steps); otherwise token by token
+    if (bi->tmax > 1 && B > 16) {
+        CK(cudaEventRecord(im->ev[0], im->st));
+        const int np0 = bi->n_past;
+        if (batch_prefill(bi, prompts, n_prompt, true, err, errlen)) return -1;
+        bi->n_past = np0;                                                  // counted once, below
+        launch(im, k_advance_batch, dim3(1), dim3(256), 0, bi->npast, B, -1);   // the last token's position
+        head_batch(bi, bi->x_last, 0, B, bi->cur, im->x, bi->npast);       // out[:, 0], its embedding into x, position + 1
+    } else {
+        // prompts [B][n_prompt] -> device [n_prompt][B]: the tokens of step i are contiguous
+        std::vector<int32_t> tp((size_t)B * n_prompt);
+        for (int bq = 0; bq < B; bq++)
+            for (int i = 0; i < n_prompt; i++) tp[(size_t)i * B + bq] = prompts[(size_t)bq * n_prompt + i];
+        CK(cudaMemcpyAsync(bi->prompts, tp.data(), tp.size() * sizeof(int32_t), cudaMemcpyHostToDevice, im->st));
+        CK(cudaEventRecord(im->ev[0], im->st));
+        for (int i = 0; i < n_prompt; i++) {
+            launch(im, k_embed, dim3((E / 8 + 127) / 128, B), dim3(128), 0, im->tok_embd, (const int32_t *)(bi->prompts + (size_t)i * B), B,
+                   im->x, E);
+            run_layers_batch(bi, im->x, 0, B);
+            if (i + 1 < n_prompt) launch(im, k_advance_batch, dim3(1), dim3(256), 0, bi->npast, B, 1);
+            else head_batch(bi, im->x, 0, B, bi->cur, im->x, bi->npast);   // out[:, 0], its embedding into x, position + 1
+        }
+        CK(cudaStreamSynchronize(im->st));   // tp is a host temporary
     }
     CK(cudaEventRecord(im->ev[1], im->st));
     bi->last_launches[0] = im->nlaunch - nl0;
@@ -2038,6 +2209,156 @@ int xj_cuda_batch_decode(xj_cuda_batch *b, const int32_t *prompts, int n_prompt,
     }
     bi->n_past += n_prompt + n_gen - 1;
     return 0;
+}
+
+// Greedy speculative decoding of a batch of sequences with a draft batch (core/xj_spec.c:131-209 for
+// every sequence at once). Both batches span all layers with the head, hold the same number of sequences
+// at the same position, and share the vocabulary; the target takes k + 1 tokens per sequence per forward
+// (xj_cuda_batch_new_multi). Per round: the draft runs k + 1 one-token steps from each sequence's last
+// emitted id (its picks d_0 .. d_k; its recurrent state is copied after each of the first k steps), the
+// target verifies [last, d_0 .. d_(k-1)] of every sequence in one (k+1)-token forward with per-token
+// checkpoints and greedy picks, each sequence emits its agreeing prefix plus the target's next pick, and
+// both batches roll each sequence back to what it keeps.
+int xj_cuda_batch_spec_decode(xj_cuda_batch *target, xj_cuda_batch *draft, const int32_t *prompts, int n_prompt, int n_gen,
+                              int k, int32_t *out, long long *stats, float *gpu_ms, char *err, size_t errlen) {
+    if (!target || !draft || !prompts || !out) { seterr(err, errlen, "null argument"); return -1; }
+    BatchImpl *tb = &target->impl, *db = &draft->impl;
+    xj_stage *ts = tb->s, *ds = db->s;
+    Impl *ti = I(ts), *di = I(ds);
+    DevGuard dg(ti->dev);
+    const int B = tb->B, T = k + 1;
+    const xj_hparams *thp = &ts->m->hp, *dhp = &ds->m->hp;
+    if (ti->dev != di->dev) { seterr(err, errlen, "target and draft must be on one device"); return -1; }
+    if (ts->l0 != 0 || ts->l1 != thp->n_layer || !ts->has_head || ds->l0 != 0 || ds->l1 != dhp->n_layer || !ds->has_head) {
+        seterr(err, errlen, "both batches must span all layers with the head"); return -1;
+    }
+    if (db->B != B) { seterr(err, errlen, "target and draft hold different numbers of sequences"); return -1; }
+    if (ti->output.N != di->output.N) { seterr(err, errlen, "target and draft vocabularies differ"); return -1; }
+    if (k < 1 || T > tb->tmax) { seterr(err, errlen, "need 1 <= k and k + 1 <= the target's max_tokens (%d)", tb->tmax); return -1; }
+    if (n_prompt < 1 || n_gen < 1) { seterr(err, errlen, "need at least one prompt token and one generated token"); return -1; }
+    if (tb->n_past != db->n_past) { seterr(err, errlen, "target and draft are at different positions"); return -1; }
+    const long long need = (long long)tb->n_past + n_prompt + (long long)n_gen * T + T;
+    if (need > tb->n_ctx || need > db->n_ctx) { seterr(err, errlen, "contexts too short: need %lld positions", need); return -1; }
+    if (db->out_cap < T) { seterr(err, errlen, "draft output buffer too small"); return -1; }
+    // buffers: target checkpoints, acceptance state, output; draft state copies
+    const size_t tss = (size_t)thp->h_v * thp->s_v * thp->s_k, tcs = (size_t)thp->conv_dim * (thp->conv_k - 1);
+    const size_t dss = (size_t)dhp->h_v * dhp->s_v * dhp->s_k, dcs = (size_t)dhp->conv_dim * (dhp->conv_k - 1);
+    if (tb->ck_ssm.empty()) {
+        for (size_t li = 0; li < tb->ssm.size(); li++) {
+            float *a = nullptr, *c = nullptr;
+            if (tb->ssm[li] && (dalloc(ti, &a, (size_t)B * (tb->tmax - 1) * tss, err, errlen) ||
+                                dalloc(ti, &c, (size_t)B * (tb->tmax - 1) * tcs, err, errlen))) return -1;
+            tb->ck_ssm.push_back(a); tb->ck_conv.push_back(c);
+        }
+        if (dalloc(ti, &tb->keep, (size_t)B, err, errlen) || dalloc(ti, &tb->nout, (size_t)B, err, errlen) ||
+            dalloc(ti, &tb->next, (size_t)B, err, errlen) ||
+            dalloc(ti, (uint8_t **)&tb->spec_stats, 2 * sizeof(unsigned long long), err, errlen)) return -1;
+    }
+    if (n_gen > tb->spec_out_cap) {
+        if (dalloc(ti, &tb->spec_out, (size_t)B * n_gen, err, errlen)) return -1;
+        tb->spec_out_cap = n_gen;
+    }
+    if (db->snap_k < k) {
+        db->snap_ssm.clear(); db->snap_conv.clear();
+        for (size_t li = 0; li < db->ssm.size(); li++) {
+            float *a = nullptr, *c = nullptr;
+            if (db->ssm[li] && (dalloc(di, &a, (size_t)k * B * dss, err, errlen) || dalloc(di, &c, (size_t)k * B * dcs, err, errlen)))
+                return -1;
+            db->snap_ssm.push_back(a); db->snap_conv.push_back(c);
+        }
+        db->snap_k = k;
+    }
+    cudaStream_t st = ti->st;
+    // the draft's work runs on its own stream; the two streams meet through events at each hand-over
+    cudaEvent_t ev_t, ev_d;
+    CK(cudaEventCreateWithFlags(&ev_t, cudaEventDisableTiming));
+    CK(cudaEventCreateWithFlags(&ev_d, cudaEventDisableTiming));
+    auto done = [&](int rc) { cudaEventDestroy(ev_t); cudaEventDestroy(ev_d); return rc; };
+    CK(cudaEventRecord(ti->ev[0], st));
+    CK(cudaMemsetAsync(tb->spec_stats, 0, 2 * sizeof(unsigned long long), st));
+    // prompts: the target picks each sequence's first id after its prompt; the draft only takes the prompt
+    if (batch_prefill(tb, prompts, n_prompt, true, err, errlen) || batch_prefill(db, prompts, n_prompt, false, err, errlen))
+        return done(-1);
+    head_pick_rows(tb, tb->x_last, B, tb->next);
+    CK(cudaMemcpy2DAsync(tb->spec_out, sizeof(int32_t) * n_gen, tb->next, sizeof(int32_t), sizeof(int32_t), B,
+                         cudaMemcpyDeviceToDevice, st));
+    {
+        std::vector<int> ones(B, 1);
+        CK(cudaMemcpyAsync(tb->nout, ones.data(), sizeof(int) * B, cudaMemcpyHostToDevice, st));
+        CK(cudaStreamSynchronize(st));
+        CK(cudaStreamSynchronize(di->st));
+    }
+    std::vector<int> nout(B, 1);
+    long long rounds = 0;
+    const int E = dhp->n_embd, V = ti->output.N;
+    (void)V;
+    auto min_out = [&]() { int mn = n_gen; for (int v : nout) mn = v < mn ? v : mn; return mn; };
+    while (min_out() < n_gen) {
+        // ---- draft: k + 1 one-token steps from next[b], state copies after the first k
+        CK(cudaEventRecord(ev_t, st));
+        CK(cudaStreamWaitEvent(di->st, ev_t, 0));
+        CK(cudaMemsetAsync(db->step, 0, sizeof(int) * B, di->st));
+        launch(di, k_embed, dim3((E / 8 + 127) / 128, B), dim3(128), 0, di->tok_embd, (const int32_t *)tb->next, B, di->x, E);
+        for (int i = 0; i <= k; i++) {
+            run_layers_batch(db, di->x, 0, B);
+            head_batch(db, di->x, 0, B, db->cur, di->x, db->npast);
+            if (i < k)
+                for (size_t li = 0; li < db->ssm.size(); li++) {
+                    if (!db->ssm[li]) continue;
+                    CK(cudaMemcpyAsync(db->snap_ssm[li] + (size_t)i * B * dss, db->ssm[li], sizeof(float) * B * dss,
+                                       cudaMemcpyDeviceToDevice, di->st));
+                    CK(cudaMemcpyAsync(db->snap_conv[li] + (size_t)i * B * dcs, db->conv[li], sizeof(float) * B * dcs,
+                                       cudaMemcpyDeviceToDevice, di->st));
+                }
+        }
+        CK(cudaEventRecord(ev_d, di->st));
+        CK(cudaStreamWaitEvent(st, ev_d, 0));
+        // ---- target: verify [last, d_0 .. d_(k-1)] of every sequence in one (k+1)-token forward
+        launch(ti, k_spec_rows, dim3((B * T + 127) / 128), dim3(128), 0, (const int32_t *)tb->next, (const int32_t *)db->out_tok,
+               db->out_cap, k, B, tb->rows_tok);
+        launch(ti, k_embed, dim3((thp->n_embd / 8 + 127) / 128, B * T), dim3(128), 0, ti->tok_embd, (const int32_t *)tb->rows_tok,
+               B * T, ti->x, thp->n_embd);
+        run_layers_batch_multi(tb, ti->x, T, true, T);
+        head_pick_rows(tb, ti->x, B * T, tb->picks);
+        launch(ti, k_spec_accept_batch, dim3((B + 127) / 128), dim3(128), 0, (const int32_t *)db->out_tok, db->out_cap,
+               (const int32_t *)tb->picks, k, B, tb->spec_out, (long long)n_gen, tb->nout, n_gen, tb->keep, tb->next,
+               tb->spec_stats);
+        // ---- both roll every sequence back to the tokens it keeps (target: checkpoints; draft: copies)
+        for (size_t li = 0; li < tb->ssm.size(); li++) {
+            if (!tb->ssm[li]) continue;
+            launch(ti, k_batch_keep_state, dim3(64, B), dim3(256), 0, tb->ssm[li], (long long)tss, (const float *)tb->ck_ssm[li],
+                   (long long)k * tss, (long long)tss, (const int *)tb->keep, T);
+            launch(ti, k_batch_keep_state, dim3(8, B), dim3(256), 0, tb->conv[li], (long long)tcs, (const float *)tb->ck_conv[li],
+                   (long long)k * tcs, (long long)tcs, (const int *)tb->keep, T);
+        }
+        launch(ti, k_batch_keep_pos, dim3(1), dim3(256), 0, tb->npast, (const int *)tb->keep, T, B);
+        for (size_t li = 0; li < db->ssm.size(); li++) {
+            if (!db->ssm[li]) continue;
+            launch(ti, k_batch_keep_state, dim3(32, B), dim3(256), 0, db->ssm[li], (long long)dss, (const float *)db->snap_ssm[li],
+                   (long long)dss, (long long)B * dss, (const int *)tb->keep, T);
+            launch(ti, k_batch_keep_state, dim3(8, B), dim3(256), 0, db->conv[li], (long long)dcs, (const float *)db->snap_conv[li],
+                   (long long)dcs, (long long)B * dcs, (const int *)tb->keep, T);
+        }
+        launch(ti, k_batch_keep_pos, dim3(1), dim3(256), 0, db->npast, (const int *)tb->keep, T, B);
+        CK(cudaMemcpyAsync(nout.data(), tb->nout, sizeof(int) * B, cudaMemcpyDeviceToHost, st));
+        if (sync_check(ti, err, errlen)) return done(-1);
+        rounds++;
+    }
+    CK(cudaEventRecord(ti->ev[2], st));
+    CK(cudaMemcpyAsync(out, tb->spec_out, sizeof(int32_t) * B * n_gen, cudaMemcpyDeviceToHost, st));
+    unsigned long long sst[2] = {0, 0};
+    CK(cudaMemcpyAsync(sst, tb->spec_stats, sizeof sst, cudaMemcpyDeviceToHost, st));
+    std::vector<int> tp(B), dp(B);
+    CK(cudaMemcpyAsync(tp.data(), tb->npast, sizeof(int) * B, cudaMemcpyDeviceToHost, st));
+    CK(cudaMemcpyAsync(dp.data(), db->npast, sizeof(int) * B, cudaMemcpyDeviceToHost, st));
+    if (sync_check(ti, err, errlen)) return done(-1);
+    if (gpu_ms) cudaEventElapsedTime(gpu_ms, ti->ev[0], ti->ev[2]);
+    // the sequences now sit at different positions; the host mirrors keep the furthest
+    int mt = 0, md = 0;
+    for (int b = 0; b < B; b++) { mt = tp[b] > mt ? tp[b] : mt; md = dp[b] > md ? dp[b] : md; }
+    tb->n_past = mt; db->n_past = md;
+    if (stats) { stats[0] = rounds; stats[1] = (long long)sst[0]; stats[2] = (long long)sst[1]; stats[3] = rounds * T; }
+    return done(0);
 }
 
 // ---- pipeline-stage entry points: device buffers of the batch's device, rows = a micro-batch

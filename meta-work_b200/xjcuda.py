@@ -115,6 +115,8 @@ def lib() -> ctypes.CDLL:
         "xj_cuda_norm_gemv_noalloc": (ip, [ip, vp, ip, ip, vp, vp, ctypes.c_float, ip, vp, cp, sz]),
         "xj_cuda_gdn_run": (ip, [ip, ip, ip, ip, ip, vp, vp, vp, vp, vp, vp, vp, ctypes.c_float, vp, vp, cp, sz]),
         "xj_cuda_set_sampler": (ip, [vp, ctypes.c_float, ip, ctypes.c_double, ctypes.c_ulonglong, cp, sz]),
+        "xj_cuda_batch_new_multi": (vp, [vp, ip, ip, ip, cp, sz]),
+        "xj_cuda_batch_spec_decode": (ip, [vp, vp, vp, ip, ip, ip, vp, vp, vp, cp, sz]),
         "xj_cuda_pipeline_id_new": (ip, [vp, cp, sz]),
         "xj_cuda_pipeline_new": (vp, [vp, ip, ip, vp, ip, ip, ip, cp, sz]),
         "xj_cuda_pipeline_free": (None, [vp]),
@@ -409,9 +411,14 @@ class Stage:
 class Batch:
     """n_seq independent sequences decoded in lockstep on one GPU (xj_cuda_batch_*)."""
 
-    def __init__(self, model: Model, n_seq: int, n_ctx: int = 256):
+    def __init__(self, model: Model, n_seq: int, n_ctx: int = 256, max_tokens: int = 1):
+        """max_tokens > 1 (xj_cuda_batch_new_multi): forwards of up to that many tokens per sequence (chunked
+        prompts of batches wider than 16 sequences, the target of spec_decode)."""
         e = _err()
-        p = lib().xj_cuda_batch_new(model.ptr, n_seq, n_ctx, e, 512)
+        if max_tokens > 1:
+            p = lib().xj_cuda_batch_new_multi(model.ptr, n_seq, n_ctx, max_tokens, e, 512)
+        else:
+            p = lib().xj_cuda_batch_new(model.ptr, n_seq, n_ctx, e, 512)
         if not p:
             _raise(e)
         self.model, self.p, self.n_seq = model, p, n_seq
@@ -438,6 +445,20 @@ class Batch:
         if rc:
             _raise(e)
         return out, mar, ms
+
+    def spec_decode(self, draft: "Batch", prompts, n_gen: int, k: int = 4):
+        """Greedy speculative decoding of every sequence with a draft batch (xj_cuda_batch_spec_decode).
+        Returns (ids [n_seq][n_gen], stats (rounds, drafted, accepted, target rows), device ms)."""
+        p = np.ascontiguousarray(prompts, dtype=np.int32)
+        assert p.ndim == 2 and p.shape[0] == self.n_seq
+        out = np.zeros((self.n_seq, n_gen), np.int32)
+        st = (ctypes.c_longlong * 4)()
+        ms = ctypes.c_float(0)
+        e = _err()
+        if lib().xj_cuda_batch_spec_decode(self.p, draft.p, p.ctypes.data, p.shape[1], n_gen, k, out.ctypes.data, st,
+                                           ctypes.byref(ms), e, 512):
+            _raise(e)
+        return out, tuple(int(v) for v in st), ms.value
 
     def last_launches(self) -> tuple[int, int]:
         v = (ctypes.c_longlong * 2)()

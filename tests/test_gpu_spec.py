@@ -71,3 +71,51 @@ def test_speculative_errors(xc, mid_path, config0_path):
         t.spec_decode(t, np.array([1, 2, 3], np.int32), 4, 2)    # the draft is the target stage
     for x in (t, d, d2):
         x.close()
+
+
+
+# ---- batched speculative decoding (xj_cuda_batch_spec_decode): every sequence of a batch at once
+@pytest.mark.parametrize("n_seq", [3, 20])
+@pytest.mark.parametrize("own_draft", [True, False])
+def test_batch_spec_decode_equals_plain_greedy(mid_path, mid_draft_path, n_seq, own_draft):
+    """Batched verify of k + 1 = 5 tokens per sequence: 3 sequences (15 verify rows, the wide kernel) and
+    20 (100 rows, the tcgen05 kernel; chunked prompts) against plain batch decoding; with the target as its
+    own draft every drafted token is accepted, with the small draft nearly none."""
+    from xjb200 import xjcuda
+    rng = np.random.default_rng(n_seq)
+    m = xjcuda.Model(mid_path)
+    prompts = rng.integers(0, m.n_vocab, (n_seq, 12)).astype(np.int32)
+    n_gen, k = 24, 4
+    b = xjcuda.Batch(m, n_seq, 256)
+    want, _, _ = b.decode(prompts, n_gen)
+    b.close()
+    dm = m if own_draft else xjcuda.Model(mid_draft_path)
+    target = xjcuda.Batch(m, n_seq, 256, max_tokens=k + 1)
+    draft = xjcuda.Batch(dm, n_seq, 256, max_tokens=4)
+    got, st, ms = target.spec_decode(draft, prompts, n_gen, k)
+    target.close()
+    draft.close()
+    assert np.array_equal(got, want)
+    rounds, drafted, accepted, rows = st
+    assert drafted == rounds * k * n_seq and rows == rounds * (k + 1) and ms > 0
+    if own_draft:
+        assert accepted == drafted and rounds == -(-(n_gen - 1) // (k + 1))
+    else:
+        assert rounds <= n_gen - 1
+
+
+def test_batch_chunked_prompt_equals_token_by_token(mid_path):
+    """A batch of 20 sequences taking its prompts in chunks of 8 tokens per sequence gives the ids and
+    margins of the one-token steps, bit for bit."""
+    from xjb200 import xjcuda
+    rng = np.random.default_rng(5)
+    m = xjcuda.Model(mid_path)
+    prompts = rng.integers(0, m.n_vocab, (20, 21)).astype(np.int32)
+    a = xjcuda.Batch(m, 20, 256)
+    ia, ma, _ = a.decode(prompts, 8, want_margins=True)
+    a.close()
+    c = xjcuda.Batch(m, 20, 256, max_tokens=8)
+    ic, mc, _ = c.decode(prompts, 8, want_margins=True)
+    c.close()
+    assert np.array_equal(ia, ic)
+    assert ma.view(np.uint32).tolist() == mc.view(np.uint32).tolist()
