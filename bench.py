@@ -361,7 +361,7 @@ def run_batch(args, cfg, model, rank, world, barrier, xjcuda, n_seq=None):
     import torch
     B = n_seq or args.batch
     n_ctx = args.prompt + max(args.warmup, 3) + 2 * args.steps + 16
-    bt = xjcuda.Batch(model, B, n_ctx)
+    bt = xjcuda.Batch(model, B, n_ctx, max_tokens=16)                # prompts in chunks of 16 tokens per sequence
     P = np.random.default_rng(4321 + rank).integers(0, cfg.n_vocab, (B, args.prompt)).astype(np.int32)
     toks, _, ms_pre = bt.decode(P, max(args.warmup, 3))          # prompt + warm-up steps (untimed)
     last = toks[:, -1:]
