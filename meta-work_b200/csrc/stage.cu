@@ -97,6 +97,11 @@ struct Impl {
     MkPhase *mk_prog = nullptr;
     MkStream *mk_stream = nullptr;
     int mk_nphase = 0, mk_nstream = 0, mk_ctas = 0, mk_max_split = 1;
+    // the layers-only program (one-token vtable forward): same kernel, no head or pick
+    int mkf_state = 0;
+    MkPhase *mkf_prog = nullptr;
+    MkStream *mkf_stream = nullptr;
+    int mkf_nphase = 0, mkf_nstream = 0;
     unsigned long long *mk_trace = nullptr;   // per CTA and phase: start, end (last step of a traced launch)
     std::vector<int> mk_ops;
     unsigned *mk_bar = nullptr;
@@ -592,6 +597,9 @@ int ensure_ck(xj_stage *s, int n, char *err, size_t errlen) {
 }
 
 // ------------------------------------------------------------------ vtable
+int mk_build(xj_stage *s, bool fwd, char *err, size_t errlen);
+int mk_launch(xj_stage *s, int n, bool fwd, char *err, size_t errlen);
+
 int cuda_forward(xj_stage *s, float *x, int T, char *err, size_t errlen) {
     Impl *im = I(s);
     DevGuard dg(im->dev);
@@ -608,7 +616,14 @@ int cuda_forward(xj_stage *s, float *x, int T, char *err, size_t errlen) {
         seterr(err, errlen, "host-to-device copy failed"); s->keep = 0; return -1;
     }
     if (s->mtp) run_mtp_prefix(s, T);
-    run_layers(s, T, keep, T);
+    // one token without checkpoints: the layers-only program of the persistent kernel, then the position
+    char why[256];
+    if (T == 1 && !keep && !s->mtp && g_opt_persist && mk_build(s, true, why, sizeof why) == 1) {
+        if (mk_launch(s, 1, true, err, errlen)) { s->keep = 0; return -1; }
+        launch(im, k_advance, dim3(1), dim3(32), 0, im->npast, 1);
+    } else {
+        run_layers(s, T, keep, T);
+    }
     cudaMemcpyAsync(im->hx, im->x, sizeof(float) * (size_t)T * E, cudaMemcpyDeviceToHost, im->st);
     if (sync_check(im, err, errlen)) { s->keep = 0; return -1; }
     memcpy(x, im->hx, sizeof(float) * (size_t)T * E);
@@ -838,9 +853,12 @@ bool mk_gemv(std::vector<MkPhase> &prog, std::vector<MkStream> &stream, int K, i
 }
 
 // 1: built, -1: unsupported for this stage, with the reason in err.
-int mk_build(xj_stage *s, char *err, size_t errlen) {
+// fwd: the layers-only program of a one-token forward (no head, no pick: the caller advances the
+// position); otherwise a whole greedy decode step.
+int mk_build(xj_stage *s, bool fwd, char *err, size_t errlen) {
     Impl *im = I(s);
-    if (im->mk_state) return im->mk_state;
+    int &state = fwd ? im->mkf_state : im->mk_state;
+    if (state) return state;
     const xj_hparams *hp = &s->m->hp;
     const int E = hp->n_embd, FF = hp->n_ff;
     const float eps = hp->eps;
@@ -891,13 +909,17 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
         down.epi = EPI_ADD;
         ok = ok && mk_gemv(prog, stream, FF, PRO_SWIGLU_S, im->g, im->u, nullptr, eps, 0, {down});
     }
-    Job h{im->output, nullptr, im->output.N};
-    h.epi = EPI_ARGMAX; h.pbest = im->pbest; h.psecond = im->psecond; h.pidx = im->pidx;
-    ok = ok && mk_gemv(prog, stream, E, PRO_NORM, im->x, nullptr, im->output_norm, eps, 0, {h});
-    if (!ok) { im->mk_state = -1; seterr(err, errlen, "persistent decode needs every matrix in the tiled layout"); return -1; }
-    MkPhase am{};
-    am.op = MK_ARGMAX; am.am = argmax_args(im);
-    prog.push_back(am);
+    if (!fwd) {
+        Job h{im->output, nullptr, im->output.N};
+        h.epi = EPI_ARGMAX; h.pbest = im->pbest; h.psecond = im->psecond; h.pidx = im->pidx;
+        ok = ok && mk_gemv(prog, stream, E, PRO_NORM, im->x, nullptr, im->output_norm, eps, 0, {h});
+    }
+    if (!ok) { state = -1; seterr(err, errlen, "persistent decode needs every matrix in the tiled layout"); return -1; }
+    if (!fwd) {
+        MkPhase am{};
+        am.op = MK_ARGMAX; am.am = argmax_args(im);
+        prog.push_back(am);
+    }
     // side data each GEMV phase (and the GDN / attention phase after it) reads, for the producer's
     // L2 prefetch
     for (MkStream &ms : stream) {
@@ -932,40 +954,50 @@ int mk_build(xj_stage *s, char *err, size_t errlen) {
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, im->dev));
     CK(cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
     CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent, MK_THREADS, MK_SMEM));
-    if (!coop || per_sm < 1) { im->mk_state = -1; seterr(err, errlen, "cooperative launch of the persistent decode kernel is not possible"); return -1; }
+    if (!coop || per_sm < 1) { state = -1; seterr(err, errlen, "cooperative launch of the persistent decode kernel is not possible"); return -1; }
     im->mk_ctas = sms;
     // the head phase leaves one greedy-pick partial per CTA that holds LM-head tiles
-    prog.back().am.ntiles = prog[prog.size() - 2].ntiles < sms ? prog[prog.size() - 2].ntiles : sms;
+    if (!fwd) prog.back().am.ntiles = prog[prog.size() - 2].ntiles < sms ? prog[prog.size() - 2].ntiles : sms;
     // splits per head: at most one work item per CTA, and the merge fits the attention scratch
     int ms = sms / hp->n_head;
     if (ms > MK_ATTN_SCR / (hp->head_dim + 2)) ms = MK_ATTN_SCR / (hp->head_dim + 2);
     im->mk_max_split = ms > 0 ? ms : 1;
-    // the program's size is fixed for a stage: a rebuild (after the output buffers moved) reuses these
-    if (!im->mk_prog &&
-        (dalloc(im, &im->mk_prog, prog.size(), err, errlen) || dalloc(im, &im->mk_stream, stream.size(), err, errlen) ||
-         dalloc(im, &im->mk_trace, (size_t)sms * prog.size() * 12, err, errlen) || dalloc(im, &im->mk_bar, 4, err, errlen) ||
-         dalloc(im, &im->mk_diag, 8, err, errlen) || dalloc(im, &im->mk_acnt, (size_t)hp->n_head, err, errlen) ||
+    // scratch shared by both programs (barrier counter, wait record, attention split partials)
+    if (!im->mk_bar &&
+        (dalloc(im, &im->mk_bar, 4, err, errlen) || dalloc(im, &im->mk_diag, 8, err, errlen) ||
+         dalloc(im, &im->mk_acnt, (size_t)hp->n_head, err, errlen) ||
          dalloc(im, &im->mk_apart, (size_t)hp->n_head * im->mk_max_split * (hp->head_dim + 2), err, errlen))) return -1;
-    CK(cudaMemcpy(im->mk_prog, prog.data(), prog.size() * sizeof(MkPhase), cudaMemcpyHostToDevice));
-    CK(cudaMemcpy(im->mk_stream, stream.data(), stream.size() * sizeof(MkStream), cudaMemcpyHostToDevice));
+    // the program's size is fixed for a stage: a rebuild (after the output buffers moved) reuses these
+    MkPhase *&dprog = fwd ? im->mkf_prog : im->mk_prog;
+    MkStream *&dstream = fwd ? im->mkf_stream : im->mk_stream;
+    if (!dprog && (dalloc(im, &dprog, prog.size(), err, errlen) || dalloc(im, &dstream, stream.size(), err, errlen))) return -1;
+    if (!fwd && !im->mk_trace && dalloc(im, &im->mk_trace, (size_t)sms * prog.size() * 12, err, errlen)) return -1;
+    CK(cudaMemcpy(dprog, prog.data(), prog.size() * sizeof(MkPhase), cudaMemcpyHostToDevice));
+    CK(cudaMemcpy(dstream, stream.data(), stream.size() * sizeof(MkStream), cudaMemcpyHostToDevice));
     // a pageable host-to-device cudaMemcpy may return before its DMA lands, and the stage stream does
     // not wait for the legacy stream: the program must be complete before the kernel reads it
     CK(cudaDeviceSynchronize());
-    im->mk_nphase = (int)prog.size();
-    im->mk_nstream = (int)stream.size();
-    im->mk_ops.clear();
-    for (const MkPhase &q : prog) im->mk_ops.push_back(q.op);
-    im->mk_state = 1;
+    if (fwd) {
+        im->mkf_nphase = (int)prog.size();
+        im->mkf_nstream = (int)stream.size();
+    } else {
+        im->mk_nphase = (int)prog.size();
+        im->mk_nstream = (int)stream.size();
+        im->mk_ops.clear();
+        for (const MkPhase &q : prog) im->mk_ops.push_back(q.op);
+    }
+    state = 1;
     return 1;
 }
 
 // n decode steps in one cooperative launch (k_decode_persistent).
-int mk_launch(xj_stage *s, int n, char *err, size_t errlen) {
+int mk_launch(xj_stage *s, int n, bool fwd, char *err, size_t errlen) {
     Impl *im = I(s);
     MkArgs a{};
-    a.prog = im->mk_prog; a.stream = im->mk_stream; a.nphase = im->mk_nphase; a.nstream = im->mk_nstream;
+    if (fwd) { a.prog = im->mkf_prog; a.stream = im->mkf_stream; a.nphase = im->mkf_nphase; a.nstream = im->mkf_nstream; }
+    else { a.prog = im->mk_prog; a.stream = im->mk_stream; a.nphase = im->mk_nphase; a.nstream = im->mk_nstream; }
     a.nsteps = n;
-    a.trace = g_opt_trace ? im->mk_trace : nullptr;
+    a.trace = g_opt_trace && !fwd ? im->mk_trace : nullptr;
     a.bar = im->mk_bar; a.err = im->derr; a.apart = im->mk_apart; a.acnt = im->mk_acnt;
     a.max_split = im->mk_max_split; a.kv_f32 = im->kv_f32 ? 1 : 0; a.diag = im->mk_diag;
     CK(cudaMemsetAsync(im->mk_bar, 0, sizeof(unsigned), im->st));
@@ -1334,7 +1366,7 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
     int persist = 0;
     if (g_opt_persist && im->samp_temp <= 0.0f) {   // the persistent kernel picks greedily
         char why[256];
-        persist = mk_build(s, why, sizeof why) == 1;
+        persist = mk_build(s, false, why, sizeof why) == 1;
     }
     CK(cudaEventRecord(im->ev[0], im->st));
     const long long nl0 = im->nlaunch;
@@ -1361,7 +1393,7 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
         // every step in the persistent kernel (step 0 = the last prompt token); segments of at most 8192
         // steps keep the grid barrier's 32-bit counter far from wrapping
         for (int done = 0; done < n_gen; done += 8192) {
-            if (mk_launch(s, n_gen - done < 8192 ? n_gen - done : 8192, err, errlen)) return -1;
+            if (mk_launch(s, n_gen - done < 8192 ? n_gen - done : 8192, false, err, errlen)) return -1;
             im->last_launches[1]++;
         }
     } else if (n_gen > 1) {
