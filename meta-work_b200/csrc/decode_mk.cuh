@@ -42,8 +42,7 @@ constexpr int MK_SLOT = 26880;                   // largest chunk: 8 Q6_K units
 constexpr int MK_NS = 6;                         // ring slots
 constexpr int MK_KMAX = MMA_KMAX_PT * MK_CTHREADS;
 constexpr int MK_XS_BYTES = 2 * (MK_KMAX + 16) * 2;   // hi/lo fp16 columns (also GDN / attention scratch)
-constexpr int MK_ATTN_SCR = 5440;                     // floats of attention scratch (split merge: nsplit*(D+2))
-static_assert(MK_ATTN_SCR * 4 <= MK_XS_BYTES, "attention scratch lives in the activation staging area");
+constexpr int MK_MAX_SPLIT = 64;                      // attention splits per KV head
 using BarC = BarNamed<1, MK_CTHREADS>;           // the compute warps only
 using BarP = BarNamed<2, MK_CTHREADS + 32>;      // compute + epilogue warps (descriptor hand-over, phase ends)
 
@@ -651,171 +650,283 @@ template <typename KV> XJ_DEV float kv_round(float v);
 template <> XJ_DEV float kv_round<float>(float v) { return v; }
 template <> XJ_DEV float kv_round<__half>(float v) { return __half2float(__float2half_rn(v)); }
 
-// Work item (head h, split sp of nsplit): q head h and its KV head through RMSNorm + NeoX RoPE (the
-// arithmetic of attn_prep_slot), the new K/V row stored at position npast by one item per KV head, and
-// online-softmax attention over positions [sp*n/nsplit, (sp+1)*n/nsplit) of n = npast + 1 (the new row
-// is taken from shared memory, rounded as the cache stores it). One split writes the gated output
-// directly; otherwise the last split of a head to finish merges all splits (core/xj_cpu.c:118-150).
-// Global operands are loaded in as few round trips as possible: all per-head vectors at once, then
-// the cache rows of MK_CWARPS * PB positions per batch.
-template <typename KV, int DPL>
-XJ_DEV void mk_attn_item(const AttnArgs &a, int h, int sp, int nsplit, float *apart, int *acnt, float *scr, int tid) {
-    constexpr int PB = DPL >= 8 ? 2 : 4;   // positions per warp per batch of loads
-    __shared__ int s_last;
-    const int D = a.D, group = a.H / a.Hkv, kvh = h / group, lane = tid & 31, warp = tid >> 5;
-    float *nq = scr, *rq = scr + 256, *nk = scr + 512, *rk = scr + 768, *rv = scr + 1024;
-    double *red = reinterpret_cast<double *>(scr + 1280);
-    float *sm_m = scr + 1312, *sm_l = scr + 1328, *sm_o = scr + 1344;      // [16][256]
-    const int pos = __ldcg(a.npast), n = pos + 1;
-    const bool isq = tid < 256;
-    const int i = isq ? tid : tid - 256;
-    const bool in = i < D;
-    const float *gate = a.q + (size_t)h * 2 * D + D;
-    const float xv = in ? lda(isq ? a.q + (size_t)h * 2 * D + i : a.k + (size_t)kvh * D + i) : 0.0f;
-    const float nw = in ? (isq ? a.qn[i] : a.kn[i]) : 0.0f;
-    const float vv = in && !isq ? lda(a.v + (size_t)kvh * D + i) : 0.0f;
-    const float gv = in && isq ? lda(gate + i) : 0.0f;
-    const double d = warp_sum_d((double)xv * xv);
-    if (lane == 0) red[warp] = d;
-    BarC::sync();
-    double ssq = 0, ssk = 0;
-    for (int w = 0; w < 8; w++) { ssq += red[w]; ssk += red[8 + w]; }
-    float *src = isq ? nq : nk;
-    if (in) src[i] = xv * (1.0f / sqrtf((float)((isq ? ssq : ssk) / D) + a.eps)) * nw;
-    BarC::sync();
-    if (in) {
-        float r = src[i];
-        const int half = a.n_rot / 2;
-        if (i < a.n_rot) {
-            const int p = i < half ? i : i - half;
-            const float theta = (float)pos * powf(a.base, -2.0f * (float)p / (float)a.n_rot);
-            const float c = cosf(theta), s = sinf(theta);
-            const float x0 = src[p], x1 = src[p + half];
-            r = i < half ? x0 * c - x1 * s : x0 * s + x1 * c;
-        }
-        if (isq) rq[i] = r;
-        else {
-            rk[i] = kv_round<KV>(r);
-            rv[i] = kv_round<KV>(vv);
-            if (sp == nsplit - 1 && h % group == 0) {
-                const size_t o = (size_t)pos * a.Hkv * D + (size_t)kvh * D + i;
-                store_kv<KV>((KV *)a.kc + o, r);
-                store_kv<KV>((KV *)a.vc + o, vv);
-            }
-        }
-    }
-    BarC::sync();
-    // online softmax over this split's positions: warp w takes j0 + w, j0 + w + 16, ... in order
-    const int j0 = (int)((long long)sp * n / nsplit), j1 = (int)((long long)(sp + 1) * n / nsplit);
-    const int kvd = a.Hkv * D;
-    const float scale = 1.0f / sqrtf((float)D);
-    const KV *kc = (const KV *)a.kc, *vc = (const KV *)a.vc;
-    const bool on = lane * DPL < D;
-    float qr[DPL], o[DPL];
-#pragma unroll
-    for (int e = 0; e < DPL; e++) { qr[e] = on ? rq[lane * DPL + e] : 0.0f; o[e] = 0.0f; }
-    float m = -INFINITY, l = 0.0f;
-    for (int jb = j0 + warp; jb < j1; jb += MK_CWARPS * PB) {
-        float kr[PB][DPL], vr[PB][DPL];
-#pragma unroll
-        for (int b = 0; b < PB; b++) {
-            const int j = jb + b * MK_CWARPS;
-            const bool fromsm = j == pos;
-            const bool ld = on && j < j1 && !fromsm;
-            const KV *kp = kc + (size_t)(ld ? j : 0) * kvd + (size_t)kvh * D + lane * DPL;
-            const KV *vp = vc + (size_t)(ld ? j : 0) * kvd + (size_t)kvh * D + lane * DPL;
-#pragma unroll
-            for (int e = 0; e < DPL; e++) {
-                kr[b][e] = ld ? load_kv(kp + e) : (on && fromsm ? rk[lane * DPL + e] : 0.0f);
-                vr[b][e] = ld ? load_kv(vp + e) : (on && fromsm ? rv[lane * DPL + e] : 0.0f);
-            }
-        }
-#pragma unroll
-        for (int b = 0; b < PB; b++) {
-            if (jb + b * MK_CWARPS >= j1) break;
-            float s = 0.0f;
-#pragma unroll
-            for (int e = 0; e < DPL; e++) s = fmaf(qr[e], kr[b][e], s);
-            s = warp_sum(s) * scale;
-            const float mn = fmaxf(m, s);
-            const float corr = expf(m - mn), p = expf(s - mn);
-            l = l * corr + p;
-#pragma unroll
-            for (int e = 0; e < DPL; e++) o[e] = fmaf(p, vr[b][e], o[e] * corr);
-            m = mn;
-        }
-    }
-    if (lane == 0) { sm_m[warp] = m; sm_l[warp] = l; }
-#pragma unroll
-    for (int e = 0; e < DPL; e++) sm_o[warp * 256 + lane * DPL + e] = o[e];
-    BarC::sync();
-    float *part = apart + ((size_t)h * nsplit + sp) * (D + 2);
-    if (tid < D) {
-        float M = -INFINITY;
-        for (int w = 0; w < MK_CWARPS; w++) M = fmaxf(M, sm_m[w]);
-        float L = 0.0f, acc = 0.0f;
-        for (int w = 0; w < MK_CWARPS; w++) {
-            const float c = sm_m[w] == -INFINITY ? 0.0f : expf(sm_m[w] - M);
-            L += sm_l[w] * c;
-            acc = fmaf(sm_o[w * 256 + tid], c, acc);
-        }
-        if (nsplit == 1) a.out[(size_t)h * D + tid] = (acc / L) * sigm_f(gv);
-        else {
-            part[tid] = acc;
-            if (tid == 0) { part[D] = M; part[D + 1] = L; }
-            __threadfence();
-        }
-    }
-    if (nsplit > 1) {
-        BarC::sync();
-        if (tid == 0) {
-            __threadfence();
-            const int old = atomicAdd(acnt + h, 1);
-            s_last = old == nsplit - 1;
-        }
-        BarC::sync();
-        if (s_last) {
-            __threadfence();
-            // all splits' partials into shared memory (one round trip), then the merge per dim
-            const float *p0 = apart + (size_t)h * nsplit * (D + 2);
-            const int np = nsplit * (D + 2);                  // <= MK_ATTN_SCR floats (host cap)
-            for (int q = tid; q < np; q += MK_CTHREADS) scr[q] = __ldcg(p0 + q);
-            BarC::sync();
-            if (tid < D) {
-                float M = -INFINITY;
-                for (int s = 0; s < nsplit; s++) M = fmaxf(M, scr[s * (D + 2) + D]);
-                float L = 0.0f, acc = 0.0f;
-                for (int s = 0; s < nsplit; s++) {
-                    const float c = expf(scr[s * (D + 2) + D] - M);
-                    L += scr[s * (D + 2) + D + 1] * c;
-                    acc = fmaf(scr[s * (D + 2) + tid], c, acc);
-                }
-                a.out[(size_t)h * D + tid] = (acc / L) * sigm_f(gv);
-            }
-            if (tid == 0) atomicExch(acnt + h, 0);
-        }
-    }
-    BarC::sync();   // scratch is reused by the next item
+// Cache positions per round of an attention item: the round's K and V rows (8 KB each) sit in the
+// activation staging area, which is dead between matrix-vector phases.
+template <typename KV> constexpr int mk_attn_pe() { return 8192 / (int)sizeof(KV); }
+__host__ __device__ inline int mk_attn_rows(int D, int kvsz) { const int r = 8192 / kvsz / D; return r < 64 ? r : 64; }
+// Bytes of the staging area an attention item uses (the rows, queries, scores, the new row, the
+// rotation table; the split merge's weights fit in the rows' place).
+__host__ __device__ inline int mk_attn_scratch(int group, int D, int kvsz) {
+    return 16384 + 4 * (group * D + group * mk_attn_rows(D, kvsz) + 3 * D);
 }
-
-XJ_DEV int mk_nsplit(int n, int H, int max_split) {
-    int ns = (n + 63) / 64;                    // one batch of loads per warp up to 64 positions a split
+// Splits per KV head for n positions: one round per split while the items fit the grid.
+XJ_DEV int mk_nsplit(int n, int D, int kvsz, int max_split) {
+    const int P = mk_attn_rows(D, kvsz);
+    int ns = (n + P - 1) / P;
     if (ns > max_split) ns = max_split;
     return ns < 1 ? 1 : ns;
 }
 
-template <typename KV>
-XJ_DEV void mk_attn_phase(const MkArgs &A, const AttnArgs &a, float *scr, int tid) {
-    const int n = __ldcg(a.npast) + 1, nsplit = mk_nsplit(n, a.H, A.max_split);
-    const int items = a.H * nsplit;
-    for (int it = blockIdx.x; it < items; it += gridDim.x) {
-        const int h = it / nsplit, sp = it % nsplit;
-        switch ((a.D + 31) / 32) {
-        case 1: mk_attn_item<KV, 1>(a, h, sp, nsplit, A.apart, A.acnt, scr, tid); break;
-        case 2: mk_attn_item<KV, 2>(a, h, sp, nsplit, A.apart, A.acnt, scr, tid); break;
-        case 4: mk_attn_item<KV, 4>(a, h, sp, nsplit, A.apart, A.acnt, scr, tid); break;
-        default: mk_attn_item<KV, 8>(a, h, sp, nsplit, A.apart, A.acnt, scr, tid); break;
+XJ_DEV float kv_f(float v) { return v; }
+XJ_DEV float kv_f(__half v) { return __half2float(v); }
+template <typename KV> XJ_DEV KV kv_from(float v);
+template <> XJ_DEV float kv_from<float>(float v) { return v; }
+template <> XJ_DEV __half kv_from<__half>(float v) { return __float2half_rn(v); }
+
+constexpr int MK_GQA = 8;    // query heads per KV head the persistent attention takes
+
+// Work item (KV head kvh, split sp of nsplit): every query head of the GQA group over positions
+// [sp*n/nsplit, (sp+1)*n/nsplit) of n = npast + 1, so the group's query heads share one read of each
+// cached row. The round's cache rows are requested first; meanwhile warps 0..group-1 put the query
+// heads and warp `group` the new K row through RMSNorm + NeoX RoPE (attn_prep_slot's arithmetic; the
+// new K/V row enters the round's rows from there, rounded as the cache stores it, and the last split
+// stores it at position npast). Per round: scores (warp per position, lanes over the head dim), the
+// softmax statistics (warp per query head), then o = sum p v (thread per (head, dim)). One split writes
+// the gated output directly; otherwise each split leaves (o, m, l) per query head and the last split of
+// the KV head to finish merges them (acquire/release counter, core/xj_cpu.c:118-150).
+template <typename KV, int DPL>
+XJ_DEV void mk_attn_item(const AttnArgs &a, int n, int kvh, int sp, int nsplit, float *apart, int *acnt, float *scr,
+                         int tid, unsigned long long *trow) {
+    constexpr int PE = mk_attn_pe<KV>();
+    constexpr int OPT = (MK_GQA * 32 * DPL + MK_CTHREADS - 1) / MK_CTHREADS;   // (head, dim) pairs per thread
+    __shared__ float st_m[MK_GQA], st_l[MK_GQA], st_c[MK_GQA];
+    __shared__ int s_last;
+    const int D = a.D, group = a.H / a.Hkv, lane = tid & 31, warp = tid >> 5;
+    const int P = mk_attn_rows(D, (int)sizeof(KV)), kvd = a.Hkv * D;
+    KV *sk = reinterpret_cast<KV *>(scr);                       // [P][D]
+    KV *sv = reinterpret_cast<KV *>(reinterpret_cast<uint8_t *>(scr) + 8192);
+    float *rq = scr + 4096;                                     // [group][D] normed + rotated queries
+    float *ps = rq + group * D;                                 // [group][P] scores, then probabilities
+    float *rkn = ps + group * P;                                // [D] the new K row (normed, then rotated)
+    float *rvn = rkn + D;                                       // [D] the new V row
+    const int pos = n - 1;
+    if (trow) trow[5] = globaltimer();
+    const int j0 = (int)((long long)sp * n / nsplit), j1 = (int)((long long)(sp + 1) * n / nsplit);
+    const float scale = 1.0f / sqrtf((float)D);
+    const KV *kc = (const KV *)a.kc + (size_t)kvh * D, *vc = (const KV *)a.vc + (size_t)kvh * D;
+    // this thread's (head, dim) pairs: gates and running outputs
+    float gate[OPT], o[OPT];
+#pragma unroll
+    for (int k = 0; k < OPT; k++) {
+        const int t = tid + k * MK_CTHREADS, hq = t / D, d = t - hq * D;
+        gate[k] = hq < group ? lda(a.q + (size_t)(kvh * group + hq) * 2 * D + D + d) : 0.0f;
+        o[k] = 0.0f;
+    }
+    if (tid < MK_GQA) { st_m[tid] = -INFINITY; st_l[tid] = 0.0f; }
+    for (int r0 = j0; r0 < j1; r0 += P) {
+        const int np = j1 - r0 < P ? j1 - r0 : P;
+        // the round's cached rows straight into shared memory (16-byte asynchronous copies, 8 elements
+        // per piece for fp16), all requested before any use
+        const int nchunk = np * D / 8;
+        for (int c = tid; c < nchunk; c += MK_CTHREADS) {
+            const int e = c * 8, j = e / D, d = e - j * D;
+            if (r0 + j == pos) continue;
+#pragma unroll
+            for (int i = 0; i < (int)sizeof(KV) / 2; i++) {
+                cp_async16(reinterpret_cast<uint4 *>(sk + e) + i, reinterpret_cast<const uint4 *>(kc + (size_t)(r0 + j) * kvd + d) + i);
+                cp_async16(reinterpret_cast<uint4 *>(sv + e) + i, reinterpret_cast<const uint4 *>(vc + (size_t)(r0 + j) * kvd + d) + i);
+            }
         }
+        cp_async_commit();
+        if (r0 == j0) {
+            // query heads (warps < group) and the new K row (warp group): RMSNorm, then NeoX RoPE with
+            // the rotation table (cos, sin of every pair) computed once per item by threads p < n_rot/2
+            const int half = a.n_rot / 2;
+            float *tab = rvn + D;                                   // [half][2]
+            for (int p = tid; p < half; p += MK_CTHREADS) {
+                const float theta = (float)pos * powf(a.base, -2.0f * (float)p / (float)a.n_rot);
+                tab[2 * p] = cosf(theta);
+                tab[2 * p + 1] = sinf(theta);
+            }
+            const bool isq = warp < group;
+            float *buf = isq ? rq + warp * D : rkn;
+            if (warp <= group) {
+                const float *src = isq ? a.q + (size_t)(kvh * group + warp) * 2 * D : a.k + (size_t)kvh * D;
+                const float *nw = isq ? a.qn : a.kn;
+                float x[8];
+                double ssq = 0.0;
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const int i = lane + 32 * e;
+                    x[e] = i < D ? lda(src + i) : 0.0f;
+                    ssq += (double)x[e] * x[e];
+                }
+                ssq = warp_sum_d(ssq);
+                const float sc = 1.0f / sqrtf((float)(ssq / D) + a.eps);
+#pragma unroll
+                for (int e = 0; e < 8; e++) {
+                    const int i = lane + 32 * e;
+                    if (i < D) buf[i] = x[e] * sc * nw[i];
+                }
+            }
+            BarC::sync();
+            if (trow) trow[6] = globaltimer();
+            if (warp <= group) {
+                // each lane rotates whole pairs (p, p + half) in place
+                for (int p = lane; p < half; p += 32) {
+                    const float c = tab[2 * p], sn = tab[2 * p + 1];
+                    const float x0 = buf[p], x1 = buf[p + half];
+                    buf[p] = x0 * c - x1 * sn;
+                    buf[p + half] = x0 * sn + x1 * c;
+                }
+                if (!isq && sp == nsplit - 1) {
+                    __syncwarp();
+                    const bool mine = pos < r0 + P;     // the new row is in this round
+                    for (int i = lane; i < D; i += 32) {
+                        const float kr0 = rkn[i], vv = lda(a.v + (size_t)kvh * D + i);
+                        rvn[i] = vv;
+                        const size_t og = (size_t)pos * kvd + (size_t)kvh * D + i;
+                        store_kv<KV>((KV *)a.kc + og, kr0);
+                        store_kv<KV>((KV *)a.vc + og, vv);
+                        if (mine) { sk[(pos - r0) * D + i] = kv_from<KV>(kr0); sv[(pos - r0) * D + i] = kv_from<KV>(vv); }
+                    }
+                }
+            }
+        }
+        if (r0 != j0 && pos >= r0 && pos < r0 + np)
+            // the new row in a later round of the last split (round j0 had it from the RoPE warp)
+            for (int i = tid; i < D; i += MK_CTHREADS) {
+                sk[(pos - r0) * D + i] = kv_from<KV>(rkn[i]);
+                sv[(pos - r0) * D + i] = kv_from<KV>(rvn[i]);
+            }
+        cp_async_wait_all();
+        BarC::sync();
+        if (trow && r0 == j0) trow[8] = globaltimer();
+        // scores: warp w takes positions w, w + 16, ...; lanes DPL consecutive dims
+        for (int j = warp; j < np; j += MK_CWARPS) {
+            float kv[DPL];
+#pragma unroll
+            for (int e = 0; e < DPL; e++) {
+                const int i = lane * DPL + e;
+                kv[e] = i < D ? kv_f(sk[j * D + i]) : 0.0f;
+            }
+            for (int h0 = 0; h0 < group; h0 += 4) {   // four query heads' reductions interleaved
+                float acc[4] = {0.0f, 0.0f, 0.0f, 0.0f};
+#pragma unroll
+                for (int e = 0; e < DPL; e++) {
+                    const int i = lane * DPL + e;
+#pragma unroll
+                    for (int q = 0; q < 4; q++)
+                        if (h0 + q < group && i < D) acc[q] = fmaf(rq[(h0 + q) * D + i], kv[e], acc[q]);
+                }
+#pragma unroll
+                for (int q = 0; q < 4; q++)
+                    if (h0 + q < group) {
+                        const float sc = warp_sum(acc[q]) * scale;
+                        if (lane == 0) ps[(h0 + q) * P + j] = sc;
+                    }
+            }
+        }
+        BarC::sync();
+        // softmax statistics of the round per query head (warp hq), probabilities in place
+        if (warp < group) {
+            float s0 = lane < np ? ps[warp * P + lane] : -INFINITY;
+            float s1 = lane + 32 < np ? ps[warp * P + lane + 32] : -INFINITY;
+            const float mr = warp_max(fmaxf(s0, s1)), mo = st_m[warp], mn = fmaxf(mo, mr);
+            const float p0 = lane < np ? expf(s0 - mn) : 0.0f, p1 = lane + 32 < np ? expf(s1 - mn) : 0.0f;
+            if (lane < np) ps[warp * P + lane] = p0;
+            if (lane + 32 < np) ps[warp * P + lane + 32] = p1;
+            const float psum = warp_sum(p0 + p1);
+            const float corr = mo == -INFINITY ? 0.0f : expf(mo - mn);
+            __syncwarp();
+            if (lane == 0) { st_c[warp] = corr; st_l[warp] = st_l[warp] * corr + psum; st_m[warp] = mn; }
+        }
+        BarC::sync();
+#pragma unroll
+        for (int k = 0; k < OPT; k++) {
+            const int t = tid + k * MK_CTHREADS, hq = t / D, d = t - hq * D;
+            if (hq >= group) continue;
+            float acc = o[k] * st_c[hq];
+            for (int j = 0; j < np; j++) acc = fmaf(ps[hq * P + j], kv_f(sv[j * D + d]), acc);
+            o[k] = acc;
+        }
+        BarC::sync();   // the round's rows and scores are overwritten by the next round
+    }
+    const size_t hstride = (size_t)nsplit * (D + 2);
+    if (trow) trow[9] = globaltimer();
+    if (nsplit == 1) {
+#pragma unroll
+        for (int k = 0; k < OPT; k++) {
+            const int t = tid + k * MK_CTHREADS, hq = t / D, d = t - hq * D;
+            if (hq < group) a.out[(size_t)(kvh * group + hq) * D + d] = (o[k] / st_l[hq]) * sigm_f(gate[k]);
+        }
+        BarC::sync();   // the statistics are reset by the next item
+        return;
+    }
+#pragma unroll
+    for (int k = 0; k < OPT; k++) {
+        const int t = tid + k * MK_CTHREADS, hq = t / D, d = t - hq * D;
+        if (hq < group) {
+            float *part = apart + (size_t)(kvh * group + hq) * hstride + (size_t)sp * (D + 2);
+            part[d] = o[k];
+            if (d == 0) { part[D] = st_m[hq]; part[D + 1] = st_l[hq]; }
+        }
+    }
+    BarC::sync();
+    if (tid == 0) {
+        // release: the CTA's partials (ordered before this by the barrier); acquire: the other splits'
+        int old;
+        asm volatile("atom.acq_rel.gpu.global.add.s32 %0, [%1], 1;" : "=r"(old) : "l"(acnt + kvh) : "memory");
+        s_last = old == nsplit - 1;
+        if (trow) trow[10] = globaltimer();
+    }
+    BarC::sync();
+    if (!s_last) return;
+    // merge: per query head (warp hq, lanes over splits) the weights c_s = exp(m_s - M) and L from one
+    // read of every split's (m, l); then o = sum_s c_s o_s / L by (head, dim) thread
+    float *cs = scr;                     // [group][nsplit]
+    if (warp < group) {
+        const float *p0 = apart + (size_t)(kvh * group + warp) * hstride;
+        float mv[MK_MAX_SPLIT / 32], lv[MK_MAX_SPLIT / 32];
+        float M = -INFINITY;
+#pragma unroll
+        for (int k = 0; k < MK_MAX_SPLIT / 32; k++) {
+            const int s_ = lane + 32 * k;
+            mv[k] = s_ < nsplit ? __ldcg(p0 + (size_t)s_ * (D + 2) + D) : -INFINITY;
+            lv[k] = s_ < nsplit ? __ldcg(p0 + (size_t)s_ * (D + 2) + D + 1) : 0.0f;
+            M = fmaxf(M, mv[k]);
+        }
+        M = warp_max(M);
+        float L = 0.0f;
+#pragma unroll
+        for (int k = 0; k < MK_MAX_SPLIT / 32; k++) {
+            const int s_ = lane + 32 * k;
+            if (s_ < nsplit) {
+                const float c = expf(mv[k] - M);
+                cs[warp * nsplit + s_] = c;
+                L = fmaf(lv[k], c, L);
+            }
+        }
+        L = warp_sum(L);
+        if (lane == 0) st_l[warp] = L;
+    }
+    BarC::sync();
+#pragma unroll
+    for (int k = 0; k < OPT; k++) {
+        const int t = tid + k * MK_CTHREADS, hq = t / D, d = t - hq * D;
+        if (hq >= group) continue;
+        const float *p0 = apart + (size_t)(kvh * group + hq) * hstride;
+        float acc = 0.0f;
+#pragma unroll 4
+        for (int s_ = 0; s_ < nsplit; s_++) acc = fmaf(cs[hq * nsplit + s_], __ldcg(p0 + (size_t)s_ * (D + 2) + d), acc);
+        a.out[(size_t)(kvh * group + hq) * D + d] = (acc / st_l[hq]) * sigm_f(gate[k]);
+    }
+    if (tid == 0) { atomicExch(acnt + kvh, 0); if (trow) trow[11] = globaltimer(); }
+    BarC::sync();   // scratch is reused by the next item
+}
+
+template <typename KV>
+XJ_DEV void mk_attn_phase(const MkArgs &A, const AttnArgs &a, int n, float *scr, int tid, unsigned long long *trow) {
+    if (trow)
+        for (int i = 5; i < 12; i++) trow[i] = 0;
+    const int nsplit = mk_nsplit(n, a.D, (int)sizeof(KV), A.max_split);
+    const int items = a.Hkv * nsplit;
+    for (int it = blockIdx.x; it < items; it += gridDim.x) {
+        const int kvh = it / nsplit, sp = it % nsplit;
+        // lanes take DPL consecutive dims of the head (DPL * 32 >= D; dims past D are masked)
+        if (a.D <= 64) mk_attn_item<KV, 2>(a, n, kvh, sp, nsplit, A.apart, A.acnt, scr, tid, it == (int)blockIdx.x ? trow : nullptr);
+        else if (a.D <= 128) mk_attn_item<KV, 4>(a, n, kvh, sp, nsplit, A.apart, A.acnt, scr, tid, it == (int)blockIdx.x ? trow : nullptr);
+        else mk_attn_item<KV, 8>(a, n, kvh, sp, nsplit, A.apart, A.acnt, scr, tid, it == (int)blockIdx.x ? trow : nullptr);
     }
 }
 
@@ -910,6 +1021,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
         const int g = lane >> 2, c = lane & 3;
         float *scw = scs + (ew ? 0 : warp) * 128;
         unsigned nbar = 0, ntile = 0;   // ntile: GEMV tiles of this CTA so far (counted alike by both roles)
+        int attn_n0 = -1;               // attention: positions at step 0 (npast + 1), once read
         int gp = 0;                 // gp: phases run so far (selects the descriptor buffer)
         if (!ew) copy_desc_async(&sph[0], &A.prog[0], (int)sizeof(MkPhase), tid);
         cp_async_wait_all();
@@ -1012,8 +1124,10 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                     default: break;
                     }
                 } else if (!ew && p.op == MK_ATTN) {
-                    if (A.kv_f32) mk_attn_phase<float>(A, p.attn, scr, tid);
-                    else mk_attn_phase<__half>(A, p.attn, scr, tid);
+                    // positions attended: read once per launch (every step adds one)
+                    if (attn_n0 < 0) attn_n0 = __ldcg(p.attn.npast) + 1 - step;
+                    if (A.kv_f32) mk_attn_phase<float>(A, p.attn, attn_n0 + step, scr, tid, tr ? trow : nullptr);
+                    else mk_attn_phase<__half>(A, p.attn, attn_n0 + step, scr, tid, tr ? trow : nullptr);
                 } else if (!ew && p.op == MK_ARGMAX) {
                     if (cta == 0) argmax_final_dev<BarC>(p.am, tid, MK_CTHREADS);
                 }

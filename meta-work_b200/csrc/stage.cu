@@ -864,7 +864,9 @@ int mk_build(xj_stage *s, bool fwd, char *err, size_t errlen) {
     const float eps = hp->eps;
     std::vector<MkPhase> prog;
     std::vector<MkStream> stream;
-    bool ok = hp->s_k == hp->s_v && hp->head_dim <= 256 && hp->n_head % hp->n_head_kv == 0 && hp->conv_k <= MK_KC;
+    const int group = hp->n_head / hp->n_head_kv;
+    bool ok = hp->s_k == hp->s_v && hp->head_dim <= 256 && hp->n_head % hp->n_head_kv == 0 && hp->conv_k <= MK_KC &&
+              group <= MK_GQA && mk_attn_scratch(group, hp->head_dim, im->kv_f32 ? 4 : 2) <= MK_XS_BYTES;
     for (int il = s->l0; ok && il < s->l1; il++) {
         Layer &Ly = im->L[il - s->l0];
         if (Ly.rec) {
@@ -958,9 +960,9 @@ int mk_build(xj_stage *s, bool fwd, char *err, size_t errlen) {
     im->mk_ctas = sms;
     // the head phase leaves one greedy-pick partial per CTA that holds LM-head tiles
     if (!fwd) prog.back().am.ntiles = prog[prog.size() - 2].ntiles < sms ? prog[prog.size() - 2].ntiles : sms;
-    // splits per head: at most one work item per CTA, and the merge fits the attention scratch
-    int ms = sms / hp->n_head;
-    if (ms > MK_ATTN_SCR / (hp->head_dim + 2)) ms = MK_ATTN_SCR / (hp->head_dim + 2);
+    // attention splits per KV head: at most one work item (KV head, split) per CTA
+    int ms = sms / hp->n_head_kv;
+    if (ms > MK_MAX_SPLIT) ms = MK_MAX_SPLIT;
     im->mk_max_split = ms > 0 ? ms : 1;
     // scratch shared by both programs (barrier counter, wait record, attention split partials)
     if (!im->mk_bar &&
@@ -1970,9 +1972,22 @@ int xj_cuda_phase_trace(const xj_stage *s, double *out, int cap) {
         unsigned long long s0 = ~0ull, e1 = 0;
         double wmax = 0, wsum = 0, wait = 0, lead = 0, pro = 0, first = 0, f1 = 0, f2 = 0, f3 = 0, f4 = 0;
         int nlead = 0, ntl = 0;
+        const bool attn = im->mk_ops[ph] == MK_ATTN;
+        double at[6] = {0, 0, 0, 0, 0, 0};
+        int nat = 0, nmerge = 0;
         for (int c = 0; c < G; c++) {
             const unsigned long long *r = &t[((size_t)c * np + ph) * 12];
-            if (r[7]) {
+            if (attn && r[5] && r[10]) {
+                // an attention item: position read, queries normed, rows staged, rounds, split counter, merge
+                at[0] += ((double)r[5] - (double)r[0]) * 1e-3;
+                at[1] += ((double)r[6] - (double)r[5]) * 1e-3;
+                at[2] += ((double)r[8] - (double)r[6]) * 1e-3;
+                at[3] += ((double)r[9] - (double)r[8]) * 1e-3;
+                at[4] += ((double)r[10] - (double)r[9]) * 1e-3;
+                nat++;
+                if (r[11]) { at[5] += ((double)r[11] - (double)r[10]) * 1e-3; nmerge++; }
+            }
+            if (!attn && r[7]) {
                 pro += ((double)r[5] - (double)r[0]) * 1e-3;
                 first += ((double)r[6] - (double)r[5]) * 1e-3;
                 f1 += ((double)r[8] - (double)r[5]) * 1e-3;    // prologue end -> first chunk ready
@@ -2003,6 +2018,10 @@ int xj_cuda_phase_trace(const xj_stage *s, double *out, int cap) {
         o[10] = ntl ? f2 / ntl : 0.0;
         o[11] = ntl ? f3 / ntl : 0.0;
         o[12] = ntl ? f4 / ntl : 0.0;
+        if (attn) {
+            for (int i = 0; i < 5; i++) o[7 + i] = nat ? at[i] / nat : 0.0;
+            o[12] = nmerge ? at[5] / nmerge : 0.0;
+        }
     }
     return np;
 }

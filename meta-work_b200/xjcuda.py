@@ -386,10 +386,12 @@ class Stage:
         return int(v[0]), int(v[1])
 
     def phase_trace(self):
-        """Per-phase timing of the last traced persistent decode (OPT_TRACE): array [phases, 5] of
-        kind, max CTA us, mean CTA us, span us, start us, mean weight wait us, mean request lead us,
-        mean prologue us, mean first-tile us, and the first tile's chunk wait, tensor-core work, tile barrier
-        and epilogue us."""
+        """Per-phase timing of the last traced persistent decode (OPT_TRACE): array [phases, 13] of
+        kind, max CTA us, mean CTA us, span us, start us, mean weight wait us, mean request lead us, then
+        for matrix-vector phases the mean prologue us, mean first-tile us, and the first tile's chunk
+        wait, tensor-core work, tile barrier and epilogue us; for attention phases the mean us of an
+        item's steps (position read, query/key norm, cache rows staged, rounds, split counter) and of
+        the split merge."""
         out = np.zeros((4096, 13), np.float64)
         n = lib().xj_cuda_phase_trace(self.addr, out.ctypes.data, 4096)
         if n < 0:
