@@ -478,6 +478,47 @@ def run_pipeline(args, rank, local, world):
     dist.destroy_process_group()
 
 
+def run_phase_trace(args) -> dict:
+    """Per-phase timing of the persistent decode kernel (XJC_OPT_TRACE) on config 3 after the
+    --prompt-token prompt: the last of 8 traced steps, summed per phase kind and per slot of a layer
+    (in-projection, GDN / attention, out-projection, FFN gate + up, FFN down), plus the attention items'
+    steps. Times are us on the device clock."""
+    from xjb200 import synth, xjcuda
+    cfg = synth.CONFIG3
+    model = xjcuda.Model(synth.cached_gguf(cfg, os.environ.get("XJ_MODEL_DIR", "/tmp/xj_models_r0")))
+    stage = xjcuda.Stage(model, 0, model.n_layer, args.prompt + 64, 8)
+    prompt = np.random.default_rng(1234).integers(0, cfg.n_vocab, args.prompt).astype(np.int32)
+    toks, _, _ = stage.decode(prompt, 4)
+    toks, _, _ = stage.decode(toks[-1:], 20)
+    xjcuda.set_option(xjcuda.OPT_TRACE, 1)
+    try:
+        _, _, ms = stage.decode(toks[-1:], 8)
+        t = stage.phase_trace()
+    finally:
+        xjcuda.set_option(xjcuda.OPT_TRACE, 0)
+        stage.close()
+    kinds = {0: "gemv", 1: "gdn", 2: "attn", 3: "argmax"}
+    ends = t[:, 4] + t[:, 3]
+    out = {"prompt": args.prompt, "ms_per_traced_step": round(float(ms[1]) / 8, 4), "phases": int(len(t)),
+           "step_span_us": round(float(ends[-1] - t[0, 4]), 1),
+           "barrier_gaps_us": round(float((t[1:, 4] - ends[:-1]).sum()), 1)}
+    nl = model.n_layer
+    slots = ["in_proj", "mixer", "out_proj", "ffn_gate_up", "ffn_down"]
+    for k, name in enumerate(slots):
+        sel = t[k:5 * nl:5]
+        out[name] = {"max_cta_us": round(float(sel[:, 1].sum()), 1), "span_us": round(float(sel[:, 3].sum()), 1)}
+        if k != 1:
+            out[name]["prologue_us"] = round(float(sel[:, 7].sum()), 1)
+    out["lm_head_span_us"] = round(float(t[5 * nl:-1, 3].sum()), 1)
+    at = t[t[:, 0] == 2]
+    if len(at):
+        out["attention_item_us"] = {k: round(float(at[:, i].mean()), 2) for k, i in
+                                    (("to_item", 7), ("qk_norm_rope", 8), ("rows", 9), ("rounds", 10),
+                                     ("split_counter", 11), ("merge", 12), ("phase_max", 1))}
+    out["by_kind_max_cta_us"] = {kinds.get(k, str(k)): round(float(t[t[:, 0] == k, 1].sum()), 1) for k in kinds}
+    return out
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -487,7 +528,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemv", type=int, default=1, help="run the config-1 GEMV microbenchmark on rank 0 (0: skip)")
-    ap.add_argument("--only", choices=["gemv"], default=None,
+    ap.add_argument("--only", choices=["gemv", "trace"], default=None,
                     help="run only this microbenchmark (one GPU; e.g. under a profiler) and print its JSON")
     ap.add_argument("--gemv-types", default="q4_k,q6_k,q8_0")
     ap.add_argument("--gemv-shapes", default="all", help="'all' or 'lm' (the 151936 x 2048 LM head only)")
@@ -515,6 +556,9 @@ def main():
         from xjb200 import synth, xjcuda
         peak, peak_kind = hbm_peak()
         print(json.dumps({"gemv": run_gemv(xjcuda, synth, peak, peak_kind, **gemv_kw(args))}))
+        return
+    if args.only == "trace":
+        print(json.dumps({"phase_trace": run_phase_trace(args)}))
         return
     if world > 1:
         import datetime
