@@ -210,7 +210,12 @@ XJ_DEV void copy_desc_async(void *dst, const void *src, int bytes, int tid) {
 }
 
 // ------------------------------------------------------------------ matrix-vector phases
-XJ_DEV int mk_cu(int type) { return type == XJ_Q4_K ? Geo<XJ_Q4_K>::CU : type == XJ_Q6_K ? Geo<XJ_Q6_K>::CU : Geo<XJ_Q8_0>::CU; }
+XJ_DEV int mk_cu(int type) {
+    return type == XJ_Q4_K ? Geo<XJ_Q4_K>::CU : type == XJ_Q5_K ? Geo<XJ_Q5_K>::CU : type == XJ_Q6_K ? Geo<XJ_Q6_K>::CU
+         : type == XJ_F16 ? Geo<XJ_F16>::CU : Geo<XJ_Q8_0>::CU;
+}
+static_assert(stage_bytes<XJ_Q5_K>() <= 26880 && stage_bytes<XJ_F16>() <= 26880 && stage_bytes<XJ_Q6_K>() <= 26880,
+              "every type's chunk fits a ring slot");
 XJ_DEV int mk_job_of(const MkPhase &p, int tg) {
     int j = 0;
     while (j + 1 < p.njob && tg >= p.tile_start[j + 1]) j++;
@@ -425,6 +430,63 @@ XJ_DEV void mk_q4k(const uint8_t *stage, int ui, int u, int lane, const __half *
     __syncwarp();
 }
 
+// Q5_K: mk_q4k with the high bit of every code from the 1-bit plane (codes 64 + q, q < 32).
+template <int HH>
+XJ_DEV void mk_q5k(const uint8_t *stage, int ui, int u, int lane, const __half *xb, const float *xsum, const float *xinv,
+                   float *scw, float &yg, float &yg8) {
+    using G = Geo<XJ_Q5_K>;
+    const int g = lane >> 2;
+    const uint8_t *qs = stage + ui * G::QB;
+    const uint8_t *ss = stage + G::CU * (G::QB + G::HB) + ui * G::SB;
+    // this half's two words of the lane's high-bit record (k-steps 8HH .. 8HH+3, 8HH+4 .. 8HH+7)
+    const uint2 hq = *reinterpret_cast<const uint2 *>(stage + G::CU * G::QB + ui * G::HB + lane * 16 + HH * 8);
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + ((2 * HH) * 32 + lane) * 16);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + ((2 * HH + 1) * 32 + lane) * 16);
+    {   // (d*sc, 64*d*sc + dmin*m) for row r, sub-blocks 4HH + 2*(lane>>4) + {0,1} (core/xj_quant.h:49-52)
+        const int r = lane & 15;
+        const uint4 hdr = *reinterpret_cast<const uint4 *>(ss + r * 16);
+        const float d = h2f((uint16_t)(hdr.x & 0xffff)), dmin = h2f((uint16_t)(hdr.x >> 16));
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            const int sbl = 2 * (lane >> 4) + e;          // sub-block within this half = header byte index
+            int s_, m_;
+            if (HH == 0) { s_ = (int)(byte_sel(hdr.y, sbl) & 63); m_ = (int)(byte_sel(hdr.z, sbl) & 63); }
+            else {
+                const uint32_t b8 = byte_sel(hdr.w, sbl), b0 = byte_sel(hdr.y, sbl), b4 = byte_sel(hdr.z, sbl);
+                s_ = (int)((b8 & 0xF) | ((b0 >> 6) << 4));
+                m_ = (int)((b8 >> 4) | ((b4 >> 6) << 4));
+            }
+            const float d1 = d * (float)s_, m1 = dmin * (float)m_;
+            const float iv = xinv[u * 8 + 4 * HH + sbl];   // the activation block's inverse range scale
+            float *o = scw + ((sbl * 8 + (r & 7)) * 4 + (r >> 3) * 2);
+            o[0] = d1 * iv;
+            o[1] = (64.0f * d1 + m1) * iv;
+        }
+    }
+    __syncwarp();
+    const int kb = u * 256;
+    const __half *xk = xb + kb + 128 * HH;
+    const float *sk = xsum + (kb >> 5) + 4 * HH;
+#pragma unroll
+    for (int sbl = 0; sbl < 4; sbl++) {
+        float d4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 2; e++) {
+            uint32_t af[4];
+            nib5_frag64(word_of(e + 2 * sbl < 4 ? q0 : q1, (2 * sbl + e) & 3), e + 2 * sbl < 4 ? hq.x : hq.y, (2 * sbl + e) & 3, af);
+            const uint2 bv = *reinterpret_cast<const uint2 *>(xk + 16 * (2 * sbl + e));
+            mma16816(d4, af, bv.x, bv.y);
+        }
+        const float4 sc4 = *reinterpret_cast<const float4 *>(scw + (sbl * 8 + g) * 4);
+        const float S = sk[sbl];
+        yg = fmaf(sc4.x, d4[0] + d4[1], yg);
+        yg = fmaf(-sc4.y, S, yg);
+        yg8 = fmaf(sc4.z, d4[2] + d4[3], yg8);
+        yg8 = fmaf(-sc4.w, S, yg8);
+    }
+    __syncwarp();
+}
+
 template <int HH>
 XJ_DEV void mk_q6k(const uint8_t *stage, int ui, int u, int lane, const __half *xb, const float *xinv, float *scw,
                    float &yg, float &yg8) {
@@ -490,6 +552,33 @@ XJ_DEV void mk_q80(const uint8_t *stage, int ui, int u, int lane, bool bcol, con
         uint2 bv = make_uint2(0u, 0u);
         if (bcol) bv = *reinterpret_cast<const uint2 *>(xb + kb + 16 * e);
         mma16816(d4, af, bv.x, bv.y);
+    }
+    yg = fmaf(dg, d4[0] + d4[1], yg);
+    yg8 = fmaf(dg8, d4[2] + d4[3], yg8);
+}
+
+// One F16 unit (16 rows x 32 elements, the fp16 values are the A fragments) at T = 1: mk_q80 without
+// the code conversion; the row-block scale (1 for F16, a power of two for BF16) times the activation
+// block's inverse range scale.
+XJ_DEV void mk_h32(const uint8_t *stage, int ui, int u, int lane, bool bcol, const __half *xb, const float *xinv,
+                   float &yg, float &yg8) {
+    using G = Geo<XJ_F16>;
+    const int g = lane >> 2;
+    const uint8_t *qs = stage + ui * G::QB;
+    const uint8_t *ds = stage + G::CU * G::QB + ui * G::DB;
+    const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + lane * 16);
+    const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + 512 + lane * 16);
+    const float dv = lane < 16 ? h2f(*reinterpret_cast<const uint16_t *>(ds + lane * 2)) : 0.0f;
+    const float iv = xinv[u];
+    const float dg = __shfl_sync(0xffffffffu, dv, g) * iv, dg8 = __shfl_sync(0xffffffffu, dv, g + 8) * iv;
+    const uint32_t af[2][4] = {{q0.x, q0.y, q0.z, q0.w}, {q1.x, q1.y, q1.z, q1.w}};
+    float d4[4] = {0.f, 0.f, 0.f, 0.f};
+    const int kb = u * 32;
+#pragma unroll
+    for (int e = 0; e < 2; e++) {
+        uint2 bv = make_uint2(0u, 0u);
+        if (bcol) bv = *reinterpret_cast<const uint2 *>(xb + kb + 16 * e);
+        mma16816(d4, af[e], bv.x, bv.y);
     }
     yg = fmaf(dg, d4[0] + d4[1], yg);
     yg8 = fmaf(dg8, d4[2] + d4[3], yg8);
@@ -996,6 +1085,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                             uint8_t *st = ring + (size_t)slot * MK_SLOT;
                             if (type == XJ_Q4_K) mk_issue_t<XJ_Q4_K>(S, j, tile, u0, cu, st, &full[slot]);
                             else if (type == XJ_Q6_K) mk_issue_t<XJ_Q6_K>(S, j, tile, u0, cu, st, &full[slot]);
+                            else if (type == XJ_Q5_K) mk_issue_t<XJ_Q5_K>(S, j, tile, u0, cu, st, &full[slot]);
+                            else if (type == XJ_F16) mk_issue_t<XJ_F16>(S, j, tile, u0, cu, st, &full[slot]);
                             else mk_issue_t<XJ_Q8_0>(S, j, tile, u0, cu, st, &full[slot]);
                             *(volatile unsigned *)&s_issued = i + 1;
                             if (trp) {
@@ -1091,6 +1182,15 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                                     if (warp & 1) mk_q6k<1>(st, ui, u0 + ui, lane, xb2, xinv, scw, yg, yg8);
                                     else mk_q6k<0>(st, ui, u0 + ui, lane, xb2, xinv, scw, yg, yg8);
                                 }
+                            } else if (W.type == XJ_Q5_K) {
+                                const int ui = warp >> 1;
+                                if (ui < cu) {
+                                    if (warp & 1) mk_q5k<1>(st, ui, u0 + ui, lane, xb2, xsum, xinv, scw, yg, yg8);
+                                    else mk_q5k<0>(st, ui, u0 + ui, lane, xb2, xsum, xinv, scw, yg, yg8);
+                                }
+                            } else if (W.type == XJ_F16) {
+                                static_assert(Geo<XJ_F16>::CU == MK_CWARPS, "one F16 unit per warp");
+                                if (warp < cu) mk_h32(st, warp, u0 + warp, lane, bcol, xb, xinv, yg, yg8);
                             } else {
 #pragma unroll
                                 for (int k = 0; k < Geo<XJ_Q8_0>::CU / MK_CWARPS; k++) {

@@ -28,6 +28,7 @@
 // Every token column is computed independently in a fixed order, so a token's result does not depend
 // on how many other tokens share the launch (decode T=1 and speculative verify T>1 agree bit for bit).
 #pragma once
+#include <cmath>
 #include <cstring>
 #include <vector>
 
@@ -45,20 +46,22 @@ enum { EPI_STORE = 0, EPI_ADD = 1, EPI_CONV = 2, EPI_ARGMAX = 3 };
 
 // Tiled weight (see repack_tiled below).
 struct Tiled {
-    const uint8_t *q = nullptr;   // fragment-ordered codes
-    const uint8_t *h = nullptr;   // Q6_K high 2-bit planes
+    const uint8_t *q = nullptr;   // fragment-ordered codes (F16: the fp16 values)
+    const uint8_t *h = nullptr;   // Q6_K high 2-bit planes, Q5_K high-bit plane
     const uint8_t *s = nullptr;   // per-row block headers (scales)
-    const uint8_t *d = nullptr;   // Q6_K / Q8_0 fp16 d per row-block
-    int type = 0, K = 0, N = 0;
-    int nu = 0;                   // units per row: Q4_K/Q6_K super-blocks (K/256), Q8_0 blocks (K/32)
+    const uint8_t *d = nullptr;   // Q6_K / Q8_0 fp16 d per row-block, F16 power-of-two row-block scales
+    int type = 0, K = 0, N = 0;   // type: the tiled layout (Q4_K, Q5_K, Q6_K, Q8_0 or F16)
+    int nu = 0;                   // units per row: K-quant super-blocks (K/256), Q8_0 / F16 blocks (K/32)
 };
 
 inline Tiled tiled_of(const DevMat &m) {
     Tiled t;
-    t.q = m.tq; t.h = m.th; t.s = m.ts; t.d = m.td; t.type = m.type; t.K = m.K; t.N = m.N;
-    t.nu = m.type == XJ_Q8_0 ? m.K / 32 : m.K / 256;
+    t.q = m.tq; t.h = m.th; t.s = m.ts; t.d = m.td; t.K = m.K; t.N = m.N;
+    t.type = m.type == XJ_BF16 ? XJ_F16 : m.type;   // BF16 is tiled as scaled fp16
+    t.nu = t.type == XJ_Q8_0 || t.type == XJ_F16 ? m.K / 32 : m.K / 256;
     return t;
 }
+inline int tiled_type(int gguf_type) { return gguf_type == XJ_BF16 ? XJ_F16 : gguf_type; }
 
 struct MmaJob {
     Tiled w;
@@ -98,6 +101,14 @@ template <int TYPE> struct Geo;
 template <> struct Geo<XJ_Q4_K> { static constexpr int QB = 2048, HB = 0, SB = 256, DB = 0, CU = 8, STAGES = 3; };
 template <> struct Geo<XJ_Q6_K> { static constexpr int QB = 2048, HB = 1024, SB = 256, DB = 32, CU = 8, STAGES = 2; };
 template <> struct Geo<XJ_Q8_0> { static constexpr int QB = 512, HB = 0, SB = 0, DB = 32, CU = 32, STAGES = 3; };
+// Q5_K: the low nibbles as Q4_K's, the high bits as a 1-bit plane, Q4_K's block headers
+template <> struct Geo<XJ_Q5_K> { static constexpr int QB = 2048, HB = 512, SB = 256, DB = 0, CU = 8, STAGES = 2; };
+// F16 and BF16 matrices as fp16 values in A-fragment order (16 rows x 32 elements per unit) with a
+// power-of-two fp16 scale per row and 32-element block (1 for F16)
+template <> struct Geo<XJ_F16> { static constexpr int QB = 1024, HB = 0, SB = 0, DB = 32, CU = 16, STAGES = 3; };
+// K-quant units (256 elements per row, split over two warps) or 32-element units
+template <int TYPE> constexpr bool kquant() { return TYPE == XJ_Q4_K || TYPE == XJ_Q5_K || TYPE == XJ_Q6_K; }
+template <int TYPE> constexpr int unit_k() { return kquant<TYPE>() ? 256 : 32; }
 template <int TYPE> constexpr int unit_bytes() { return Geo<TYPE>::QB + Geo<TYPE>::HB + Geo<TYPE>::SB + Geo<TYPE>::DB; }
 template <int TYPE> constexpr int stage_bytes() { return Geo<TYPE>::CU * unit_bytes<TYPE>(); }
 
@@ -198,137 +209,44 @@ XJ_DEV void nib_frag64(uint32_t w, uint32_t *a) {
     a[3] = lop3_and_or(w >> 8, 0x00F000F0u, 0x54005400u);
 }
 
+// Q5_K codes of one k-step as fp16 (64 + q, q = low nibble + 16 * high bit), exact: the nibbles as
+// nib_frag64, the high bit into mantissa bit 8 (weight 16 above 64). Word hw of the high-bit plane
+// holds k-steps 4j .. 4j+3; k-step S = s & 3 keeps register r's bits at 4S + r (first half) and
+// 16 + 4S + r (second half).
+XJ_DEV void nib5_frag64(uint32_t w, uint32_t hw, int S, uint32_t *a) {   // S: a constant after unrolling
+    nib_frag64(w, a);
+#pragma unroll
+    for (int r = 0; r < 4; r++) {
+        const int sh = 8 - 4 * S - r;
+        const uint32_t hb = sh >= 0 ? hw << sh : hw >> -sh;
+        a[r] = lop3_and_or(hb, 0x01000100u, a[r]);
+    }
+}
+
 // Position of column k (0..15) of a k-step in the staged activations: lane quad c finds columns
 // 2c, 2c+1, 2c+8, 2c+9 (its two B-fragment registers) as 4 adjacent halves.
 __host__ __device__ inline int bperm(int k) { return ((k & 7) >> 1) * 4 + (k >> 3) * 2 + (k & 1); }
 
 // ------------------------------------------------------------------ one unit from a shared-memory stage
-// Accumulate into (yg, yg8) (rows g, g+8 of the tile, token c) unit ui of the staged chunk (global unit
-// u of its tile). K-quant units are shared by two warps: half hh takes k-steps 8hh..8hh+7. xb: this
-// lane's B-fragment row (column g), valid when bcol; xsum_t: 32-wide block sums of token c (Q4_K);
-// scw: this warp's 128-float scale scratch.
-template <int TYPE>
-XJ_DEV void unit_compute(const uint8_t *stage, int ui, int u, int hh, int lane, bool bcol, const __half *xb,
-                         const float *xsum_t, float *scw, float &yg, float &yg8) {
-    using G = Geo<TYPE>;
-    const int g = lane >> 2;
-    const uint8_t *qs = stage + ui * G::QB;
-    if constexpr (TYPE == XJ_Q4_K) {
-        const uint8_t *ss = stage + G::CU * G::QB + ui * G::SB;
-        const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh) * 32 + lane) * 16);
-        const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh + 1) * 32 + lane) * 16);
-        {   // (d*sc, 64*d*sc + dmin*m) for row r, sub-blocks 4hh + 2*(lane>>4) + {0,1} (core/xj_quant.h:49-52)
-            const int r = lane & 15;
-            const uint4 hdr = *reinterpret_cast<const uint4 *>(ss + r * 16);
-            const float d = h2f((uint16_t)(hdr.x & 0xffff)), dmin = h2f((uint16_t)(hdr.x >> 16));
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int sbl = 2 * (lane >> 4) + e, sb = 4 * hh + sbl;
-                int s_, m_;
-                if (sb < 4) { s_ = byte_of(hdr, 4 + sb) & 63; m_ = byte_of(hdr, 8 + sb) & 63; }
-                else {
-                    s_ = (byte_of(hdr, 8 + sb) & 0xF) | ((byte_of(hdr, sb) >> 6) << 4);
-                    m_ = (byte_of(hdr, 8 + sb) >> 4) | ((byte_of(hdr, 4 + sb) >> 6) << 4);
-                }
-                const float d1 = d * (float)s_, m1 = dmin * (float)m_;
-                float *o = scw + ((sbl * 8 + (r & 7)) * 4 + (r >> 3) * 2);
-                o[0] = d1;
-                o[1] = 64.0f * d1 + m1;
-            }
-        }
-        __syncwarp();
-        const int kb = u * 256;
-#pragma unroll
-        for (int sbl = 0; sbl < 4; sbl++) {
-            float d4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int e = 0; e < 2; e++) {
-                const int s = 8 * hh + 2 * sbl + e;            // k-step within the super-block
-                uint32_t af[4];
-                nib_frag64(word_of(e + 2 * sbl < 4 ? q0 : q1, (2 * sbl + e) & 3), af);
-                uint2 bv = make_uint2(0u, 0u);
-                if (bcol) bv = *reinterpret_cast<const uint2 *>(xb + kb + 16 * s);
-                mma16816(d4, af, bv.x, bv.y);
-            }
-            const float4 sc4 = *reinterpret_cast<const float4 *>(scw + (sbl * 8 + g) * 4);
-            const float S = xsum_t ? xsum_t[(kb >> 5) + 4 * hh + sbl] : 0.0f;
-            yg = fmaf(sc4.x, d4[0] + d4[1], yg);
-            yg = fmaf(-sc4.y, S, yg);
-            yg8 = fmaf(sc4.z, d4[2] + d4[3], yg8);
-            yg8 = fmaf(-sc4.w, S, yg8);
-        }
-        __syncwarp();
-    } else if constexpr (TYPE == XJ_Q6_K) {
-        const uint8_t *hs = stage + G::CU * G::QB + ui * G::HB;
-        const uint8_t *ss = stage + G::CU * (G::QB + G::HB) + ui * G::SB;
-        const uint8_t *ds = stage + G::CU * (G::QB + G::HB + G::SB) + ui * G::DB;
-        const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh) * 32 + lane) * 16);
-        const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh + 1) * 32 + lane) * 16);
-        const uint4 hq = *reinterpret_cast<const uint4 *>(hs + (hh * 32 + lane) * 16);
-        {   // d*sc for row r, k-steps 8hh + 4*(lane>>4) + {0..3} (core/xj_quant.h:106-118)
-            const int r = lane & 15;
-            const uint4 sc = *reinterpret_cast<const uint4 *>(ss + r * 16);
-            const float d = h2f(*reinterpret_cast<const uint16_t *>(ds + r * 2));
-#pragma unroll
-            for (int e = 0; e < 4; e++) {
-                const int sl = 4 * (lane >> 4) + e;
-                scw[(sl * 8 + (r & 7)) * 2 + (r >> 3)] = d * (float)(int8_t)byte_of(sc, 8 * hh + sl);
-            }
-        }
-        __syncwarp();
-        const int kb = u * 256;
-#pragma unroll
-        for (int sl = 0; sl < 8; sl++) {
-            const int s = 8 * hh + sl;
-            float d4[4] = {0.f, 0.f, 0.f, 0.f};
-            uint32_t af[4], ah[4];
-            nib_frag(word_of(sl < 4 ? q0 : q1, sl & 3), af);
-            uint32_t hw = word_of(hq, sl >> 1);
-            if (sl & 1) hw >>= 8;
-            hi_frag(hw, ah);
-            uint2 bv = make_uint2(0u, 0u);
-            if (bcol) bv = *reinterpret_cast<const uint2 *>(xb + kb + 16 * s);
-            mma16816(d4, af, bv.x, bv.y);
-            mma16816(d4, ah, bv.x, bv.y);
-            const float2 sc2 = *reinterpret_cast<const float2 *>(scw + (sl * 8 + g) * 2);
-            yg = fmaf(sc2.x, d4[0] + d4[1], yg);
-            yg8 = fmaf(sc2.y, d4[2] + d4[3], yg8);
-        }
-        __syncwarp();
-    } else {
-        const uint8_t *ds = stage + G::CU * G::QB + ui * G::DB;
-        const uint4 q = *reinterpret_cast<const uint4 *>(qs + lane * 16);
-        const float dv = lane < 16 ? h2f(*reinterpret_cast<const uint16_t *>(ds + lane * 2)) : 0.0f;
-        const float dg = __shfl_sync(0xffffffffu, dv, g), dg8 = __shfl_sync(0xffffffffu, dv, g + 8);
-        float d4[4] = {0.f, 0.f, 0.f, 0.f};
-        const int kb = u * 32;
-#pragma unroll
-        for (int e = 0; e < 2; e++) {
-            uint32_t af[4];
-            q8_frag(word_of(q, 2 * e), word_of(q, 2 * e + 1), af);
-            uint2 bv = make_uint2(0u, 0u);
-            if (bcol) bv = *reinterpret_cast<const uint2 *>(xb + kb + 16 * e);
-            mma16816(d4, af, bv.x, bv.y);
-        }
-        yg = fmaf(dg, d4[0] + d4[1], yg);
-        yg8 = fmaf(dg8, d4[2] + d4[3], yg8);
-    }
-}
-
-// The same unit for up to 4*NT tokens: the A fragment is decoded once per k-step and multiplied with
-// NT B fragments (8 columns each: tokens 4n..4n+3, hi and lo). Column by column the arithmetic is
-// unit_compute's, so a token's result does not depend on NT or on the other tokens of the launch.
-// xb: this lane's B-fragment row of n-tile 0 (column g); the row of n-tile n is 8n columns further.
+// Accumulate into (yg[n], yg8[n]) (rows g, g+8 of the tile, tokens 4n + c) unit ui of the staged chunk
+// (global unit u of its tile) for up to 4*NT tokens: the A fragment is decoded once per k-step and
+// multiplied with NT B fragments (8 columns each: tokens 4n..4n+3, hi and lo), so a token's result does
+// not depend on NT or on the other tokens of the launch. K-quant units are shared by two warps: half hh
+// takes k-steps 8hh..8hh+7. xb: this lane's B-fragment row of n-tile 0 (column g); the row of n-tile n
+// is 8n columns further. xsum: 32-wide block sums [T][nblk] (Q4_K, Q5_K); scw: this warp's 128-float
+// scale scratch.
 template <int TYPE, int NT>
 XJ_DEV void unit_compute_n(const uint8_t *stage, int ui, int u, int hh, int lane, int T, const __half *xb,
                            int xstride, const float *xsum, int nblk, float *scw, float (&yg)[NT], float (&yg8)[NT]) {
     using G = Geo<TYPE>;
     const int g = lane >> 2, c = lane & 3;
     const uint8_t *qs = stage + ui * G::QB;
-    if constexpr (TYPE == XJ_Q4_K) {
-        const uint8_t *ss = stage + G::CU * G::QB + ui * G::SB;
+    if constexpr (TYPE == XJ_Q4_K || TYPE == XJ_Q5_K) {
+        const uint8_t *ss = stage + G::CU * (G::QB + G::HB) + ui * G::SB;
         const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh) * 32 + lane) * 16);
         const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + ((2 * hh + 1) * 32 + lane) * 16);
+        uint2 hq = make_uint2(0u, 0u);   // Q5_K: this half's two words of the lane's high-bit record
+        if constexpr (TYPE == XJ_Q5_K) hq = *reinterpret_cast<const uint2 *>(stage + G::CU * G::QB + ui * G::HB + lane * 16 + hh * 8);
         {
             const int r = lane & 15;
             const uint4 hdr = *reinterpret_cast<const uint4 *>(ss + r * 16);
@@ -359,7 +277,9 @@ XJ_DEV void unit_compute_n(const uint8_t *stage, int ui, int u, int hh, int lane
             for (int e = 0; e < 2; e++) {
                 const int s = 8 * hh + 2 * sbl + e;
                 uint32_t af[4];
-                nib_frag64(word_of(e + 2 * sbl < 4 ? q0 : q1, (2 * sbl + e) & 3), af);
+                const uint32_t wq = word_of(e + 2 * sbl < 4 ? q0 : q1, (2 * sbl + e) & 3);
+                if constexpr (TYPE == XJ_Q5_K) nib5_frag64(wq, (2 * sbl + e) < 4 ? hq.x : hq.y, (2 * sbl + e) & 3, af);
+                else nib_frag64(wq, af);
 #pragma unroll
                 for (int n = 0; n < NT; n++) {
                     uint2 bv = make_uint2(0u, 0u);
@@ -419,6 +339,27 @@ XJ_DEV void unit_compute_n(const uint8_t *stage, int ui, int u, int hh, int lane
             }
         }
         __syncwarp();
+    } else if constexpr (TYPE == XJ_F16) {
+        // the fp16 values are the A fragments; k-step e's 16 bytes of lane l at 512 e + 16 l
+        const uint8_t *ds = stage + G::CU * G::QB + ui * G::DB;
+        const uint4 q0 = *reinterpret_cast<const uint4 *>(qs + lane * 16);
+        const uint4 q1 = *reinterpret_cast<const uint4 *>(qs + 512 + lane * 16);
+        const float dv = lane < 16 ? h2f(*reinterpret_cast<const uint16_t *>(ds + lane * 2)) : 0.0f;
+        const float dg = __shfl_sync(0xffffffffu, dv, g), dg8 = __shfl_sync(0xffffffffu, dv, g + 8);
+        const int kb = u * 32;
+        const uint32_t af[2][4] = {{q0.x, q0.y, q0.z, q0.w}, {q1.x, q1.y, q1.z, q1.w}};
+#pragma unroll
+        for (int n = 0; n < NT; n++) {
+            float d4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int e = 0; e < 2; e++) {
+                uint2 bv = make_uint2(0u, 0u);
+                if (8 * n + g < 2 * T) bv = *reinterpret_cast<const uint2 *>(xb + (size_t)(8 * n) * xstride + kb + 16 * e);
+                mma16816(d4, af[e], bv.x, bv.y);
+            }
+            yg[n] = fmaf(dg, d4[0] + d4[1], yg[n]);
+            yg8[n] = fmaf(dg8, d4[2] + d4[3], yg8[n]);
+        }
     } else {
         const uint8_t *ds = stage + G::CU * G::QB + ui * G::DB;
         const uint4 q = *reinterpret_cast<const uint4 *>(qs + lane * 16);
@@ -465,7 +406,7 @@ template <int TYPE, int NT>
 __global__ void __launch_bounds__(MMA_WARPS * 32, NT == 1 ? 2 : 1) k_gemv_mma(MmaArgs a) {
     using G = Geo<TYPE>;
     constexpr int SB = stage_bytes<TYPE>(), NS = G::STAGES, TMAX = 4 * NT;
-    constexpr bool KQ = TYPE != XJ_Q8_0;                 // K-quant units are split over two warps
+    constexpr bool KQ = kquant<TYPE>();                  // K-quant units are split over two warps
     extern __shared__ __align__(128) uint8_t smem[];
     const MmaSmem L(a.T, a.K, SB * NS, TMAX);
     uint8_t *ring = smem + L.off_ring;
@@ -565,7 +506,7 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, NT == 1 ? 2 : 1) k_gemv_mma(Mm
                 const int pos = (i & ~15) + bperm(i & 15);
                 col_hi[pos] = hi;
                 col_lo[pos] = lo;
-                if (TYPE == XJ_Q4_K) {
+                if (TYPE == XJ_Q4_K || TYPE == XJ_Q5_K) {
                     // elements i..i+31 of a warp form one 32-wide block; sum what the MMA multiplies
                     const float bs = warp_sum(__half2float(hi) + __half2float(lo));
                     if (lane == 0) xsum[t * (K / 32) + (i >> 5)] = bs;
@@ -869,9 +810,9 @@ template <int TYPE>
 __global__ void __launch_bounds__(MMA_WARPS * 32, 1) k_gemv_wide(MmaArgs a, const void *xbuf) {
     using G = Geo<TYPE>;
     constexpr int SB = stage_bytes<TYPE>(), NS = G::STAGES, NT = MMA_WIDE_T / 4, TMAX = MMA_WIDE_T;
-    constexpr bool KQ = TYPE != XJ_Q8_0;
+    constexpr bool KQ = kquant<TYPE>();
     constexpr int USL = G::CU;                                  // units per slice: one chunk
-    constexpr int SLK = USL * (TYPE == XJ_Q8_0 ? 32 : 256);     // K per slice
+    constexpr int SLK = USL * unit_k<TYPE>();                   // K per slice
     static_assert(SLK <= WIDE_SLICE, "slice fits the staging area");
     extern __shared__ __align__(128) uint8_t smem[];
     const WideSmem L(SB * NS);
@@ -1488,6 +1429,8 @@ inline int ring_bytes(int type) {
     switch (type) {
     case XJ_Q4_K: return stage_bytes<XJ_Q4_K>() * Geo<XJ_Q4_K>::STAGES;
     case XJ_Q6_K: return stage_bytes<XJ_Q6_K>() * Geo<XJ_Q6_K>::STAGES;
+    case XJ_Q5_K: return stage_bytes<XJ_Q5_K>() * Geo<XJ_Q5_K>::STAGES;
+    case XJ_F16: case XJ_BF16: return stage_bytes<XJ_F16>() * Geo<XJ_F16>::STAGES;
     default: return stage_bytes<XJ_Q8_0>() * Geo<XJ_Q8_0>::STAGES;
     }
 }
@@ -1498,8 +1441,8 @@ inline size_t mma_smem_bytes(int type, int T, int K, int tmax = MMA_MAXT) { retu
 // Matrices the tensor-core path can take (at up to MMA_MAXT tokens).
 inline bool tiled_ok(int type, int K, int N) {
     if (N < 1 || K > MMA_KMAX) return false;
-    if (type == XJ_Q4_K || type == XJ_Q6_K) { if (K % 256) return false; }
-    else if (type == XJ_Q8_0) { if (K % 32) return false; }
+    if (type == XJ_Q4_K || type == XJ_Q5_K || type == XJ_Q6_K) { if (K % 256) return false; }
+    else if (type == XJ_Q8_0 || type == XJ_F16 || type == XJ_BF16) { if (K % 32) return false; }
     else return false;
     return mma_smem_bytes(type, MMA_MAXT, K) <= MMA_SMEM_MAX;
 }
@@ -1671,6 +1614,8 @@ inline cudaError_t launch_wide(const MmaArgs &a, int type, const void *xbuf, cud
     case XJ_Q4_K: return launch_wide_t<XJ_Q4_K>(a, xbuf, st);
     case XJ_Q6_K: return launch_wide_t<XJ_Q6_K>(a, xbuf, st);
     case XJ_Q8_0: return launch_wide_t<XJ_Q8_0>(a, xbuf, st);
+    case XJ_Q5_K: return launch_wide_t<XJ_Q5_K>(a, xbuf, st);
+    case XJ_F16: return launch_wide_t<XJ_F16>(a, xbuf, st);
     default: return cudaErrorInvalidValue;
     }
 }
@@ -1680,6 +1625,8 @@ inline cudaError_t launch_mma(const MmaArgs &a, int type, cudaStream_t st) {
     case XJ_Q4_K: return launch_mma_t<XJ_Q4_K>(a, st);
     case XJ_Q6_K: return launch_mma_t<XJ_Q6_K>(a, st);
     case XJ_Q8_0: return launch_mma_t<XJ_Q8_0>(a, st);
+    case XJ_Q5_K: return launch_mma_t<XJ_Q5_K>(a, st);
+    case XJ_F16: return launch_mma_t<XJ_F16>(a, st);
     default: return cudaErrorInvalidValue;
     }
 }
@@ -1697,6 +1644,12 @@ inline uint8_t q4k_code(const uint8_t *blk, int col) {   // Q4_K code of column 
     return (j & 1) ? (b >> 4) : (b & 0xF);
 }
 
+inline uint8_t q5k_code(const uint8_t *blk, int col) {   // Q5_K code 0..31 (core/xj_quant.h layout)
+    const int j = col / 32, l = col % 32;
+    const uint8_t ql = blk[48 + 32 * (j / 2) + l];
+    return (uint8_t)(((j & 1) ? (ql >> 4) : (ql & 0xF)) | (((blk[16 + l] >> j) & 1) << 4));
+}
+
 inline uint8_t q6k_code(const uint8_t *blk, int col) {   // Q6_K code 0..63 (value + 32)
     const int h = col / 128, r = col % 128, part = r / 32, l = r % 32;
     const uint8_t ql = blk[64 * h + (part & 1) * 32 + l], qh = blk[128 + 32 * h + l];
@@ -1707,9 +1660,41 @@ inline uint8_t q6k_code(const uint8_t *blk, int col) {   // Q6_K code 0..63 (val
 inline int frag_col(int r, int e, int c) { return 2 * c + e + 8 * (r >> 1); }
 inline int frag_row(int r, int g) { return g + 8 * (r & 1); }
 
-inline void repack_tiled(int type, const uint8_t *src_rows, int K, int N, TiledHost &o) {
+// F16 / BF16 row r, elements k0..k0+31 -> fp16 values and the block's power-of-two scale (fp16 bits);
+// false when a BF16 block cannot be carried exactly (an element more than ~2^29 below the block's
+// largest, a non-finite value, or a scale outside fp16).
+inline bool h32_block(int type, const uint8_t *row, int k0, uint16_t *v, uint16_t *scale) {
+    float f[32], m = 0.0f;
+    for (int i = 0; i < 32; i++) {
+        uint16_t u;
+        memcpy(&u, row + 2 * (k0 + i), 2);
+        if (type == XJ_F16) { v[i] = u; continue; }
+        const uint32_t w = (uint32_t)u << 16;
+        memcpy(&f[i], &w, 4);
+        if (!std::isfinite(f[i])) return false;
+        m = fabsf(f[i]) > m ? fabsf(f[i]) : m;
+    }
+    if (type == XJ_F16) { *scale = 0x3C00; return true; }
+    const int e = m > 0.0f ? ilogbf(m) - 14 : 0;    // the largest lands in [2^14, 2^15)
+    if (e < -24 || e > 15) return false;
+    const float inv = ldexpf(1.0f, -e);
+    for (int i = 0; i < 32; i++) {
+        const float x = f[i] * inv;                 // exact: a power of two
+        const __half h = __float2half_rn(x);
+        if (__half2float(h) != x) return false;
+        v[i] = __half_as_ushort(h);
+    }
+    *scale = __half_as_ushort(__float2half_rn(ldexpf(1.0f, e)));
+    return true;
+}
+
+// Re-encodes an [N][K] GGUF matrix into the tiled layout of its type; false if the matrix cannot be
+// carried exactly (BF16 only), in which case it stays row-major.
+inline bool repack_tiled(int type, const uint8_t *src_rows, int K, int N, TiledHost &o) {
     const int tiles = (N + 15) / 16;
-    const size_t rb0 = type == XJ_Q8_0 ? (size_t)(K / 32) * 34 : (size_t)(K / 256) * (type == XJ_Q4_K ? 144 : 210);
+    const bool kq = type == XJ_Q4_K || type == XJ_Q5_K || type == XJ_Q6_K;
+    const int bb = type == XJ_Q4_K ? 144 : type == XJ_Q5_K ? 176 : 210;
+    const size_t rb0 = type == XJ_Q8_0 ? (size_t)(K / 32) * 34 : kq ? (size_t)(K / 256) * bb : (size_t)K * 2;
     std::vector<uint8_t> padded;
     const uint8_t *src = src_rows;
     if (N % 16) {
@@ -1717,31 +1702,35 @@ inline void repack_tiled(int type, const uint8_t *src_rows, int K, int N, TiledH
         memcpy(padded.data(), src_rows, (size_t)N * rb0);
         src = padded.data();
     }
-    if (type == XJ_Q4_K || type == XJ_Q6_K) {
-        const int nu = K / 256, bb = type == XJ_Q4_K ? 144 : 210;
+    if (kq) {
+        const int nu = K / 256;
         const size_t rb = (size_t)nu * bb;
         o.q.assign((size_t)tiles * nu * 2048, 0);
         o.s.assign((size_t)tiles * nu * 16 * 16, 0);
         if (type == XJ_Q6_K) { o.h.assign((size_t)tiles * nu * 1024, 0); o.d.assign((size_t)tiles * nu * 16 * 2, 0); }
+        if (type == XJ_Q5_K) o.h.assign((size_t)tiles * nu * 512, 0);
         for (int t = 0; t < tiles; t++)
             for (int u = 0; u < nu; u++) {
                 const size_t tu = (size_t)t * nu + u;
                 const uint8_t *blk[16];
                 for (int i = 0; i < 16; i++) blk[i] = src + (size_t)(16 * t + i) * rb + (size_t)u * bb;
                 for (int i = 0; i < 16; i++) {
-                    if (type == XJ_Q4_K) memcpy(&o.s[(tu * 16 + i) * 16], blk[i], 16);
+                    if (type != XJ_Q6_K) memcpy(&o.s[(tu * 16 + i) * 16], blk[i], 16);   // d, dmin, scales
                     else { memcpy(&o.s[(tu * 16 + i) * 16], blk[i] + 192, 16); memcpy(&o.d[(tu * 16 + i) * 2], blk[i] + 208, 2); }
                 }
                 for (int lane = 0; lane < 32; lane++) {
                     const int g = lane >> 2, c = lane & 3;
+                    uint32_t h5[4] = {0, 0, 0, 0};   // Q5_K: the lane's high-bit record, 4 k-steps per word
                     for (int s = 0; s < 16; s++) {
                         uint32_t w = 0, hw = 0;
                         for (int r = 0; r < 4; r++)
                             for (int e = 0; e < 2; e++) {
                                 const int row = frag_row(r, g), col = 16 * s + frag_col(r, e, c);
-                                const uint8_t code = type == XJ_Q4_K ? q4k_code(blk[row], col) : q6k_code(blk[row], col);
+                                const uint8_t code = type == XJ_Q4_K ? q4k_code(blk[row], col)
+                                                   : type == XJ_Q5_K ? q5k_code(blk[row], col) : q6k_code(blk[row], col);
                                 w |= (uint32_t)(code & 0xF) << (4 * r + 16 * e);
                                 hw |= (uint32_t)(code >> 4) << (2 * r + 16 * e);
+                                if (type == XJ_Q5_K) h5[s >> 2] |= (uint32_t)(code >> 4) << (16 * e + 4 * (s & 3) + r);
                             }
                         memcpy(&o.q[((tu * 4 + s / 4) * 32 + lane) * 16 + (s % 4) * 4], &w, 4);
                         if (type == XJ_Q6_K) {
@@ -1753,9 +1742,10 @@ inline void repack_tiled(int type, const uint8_t *src_rows, int K, int N, TiledH
                             memcpy(p, &cur, 4);
                         }
                     }
+                    if (type == XJ_Q5_K) memcpy(&o.h[(tu * 32 + lane) * 16], h5, 16);
                 }
             }
-    } else {   // Q8_0
+    } else if (type == XJ_Q8_0) {
         const int nu = K / 32;
         const size_t rb = (size_t)nu * 34;
         o.q.assign((size_t)tiles * nu * 512, 0);
@@ -1777,7 +1767,32 @@ inline void repack_tiled(int type, const uint8_t *src_rows, int K, int N, TiledH
                     memcpy(&o.q[(tu * 32 + lane) * 16], out, 16);
                 }
             }
+    } else {   // F16 / BF16: fp16 values in fragment order, k-step ss of lane l at 512 ss + 16 l
+        const int nu = K / 32;
+        const size_t rb = (size_t)K * 2;
+        o.q.assign((size_t)tiles * nu * 1024, 0);
+        o.d.assign((size_t)tiles * nu * 16 * 2, 0);
+        uint16_t v[16][32];
+        for (int t = 0; t < tiles; t++)
+            for (int u = 0; u < nu; u++) {
+                const size_t tu = (size_t)t * nu + u;
+                for (int i = 0; i < 16; i++) {
+                    uint16_t sc;
+                    if (!h32_block(type, src + (size_t)(16 * t + i) * rb, 32 * u, v[i], &sc)) return false;
+                    memcpy(&o.d[(tu * 16 + i) * 2], &sc, 2);
+                }
+                for (int lane = 0; lane < 32; lane++) {
+                    const int g = lane >> 2, c = lane & 3;
+                    for (int ss = 0; ss < 2; ss++)
+                        for (int r = 0; r < 4; r++)
+                            for (int e = 0; e < 2; e++) {
+                                const int row = frag_row(r, g), col = 16 * ss + frag_col(r, e, c);
+                                memcpy(&o.q[tu * 1024 + ss * 512 + lane * 16 + r * 4 + e * 2], &v[row][col], 2);
+                            }
+                }
+            }
     }
+    return true;
 }
 
 }  // namespace xjk

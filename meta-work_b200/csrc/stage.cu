@@ -170,12 +170,13 @@ int upload(Impl *im, const xj_w &w, DevMat *out, char *err, size_t errlen, bool 
     DevMat d{nullptr, (int)w.type, (int)w.ne0, (int)w.ne1, (long long)row_bytes(w.type, w.ne0)};
     auto it = im->uploaded.find(w.data);
     if (it != im->uploaded.end()) d = it->second;
-    const bool want_tiled = im->gemv_mode == 0 && w.ne1 > 1 && tiled_ok((int)w.type, (int)w.ne0, (int)w.ne1);
+    bool want_tiled = im->gemv_mode == 0 && w.ne1 > 1 && tiled_ok((int)w.type, (int)w.ne0, (int)w.ne1);
     if (want_tiled && !d.tq) {
         TiledHost th;
-        repack_tiled((int)w.type, (const uint8_t *)w.data, (int)w.ne0, (int)w.ne1, th);
-        if (dput(im, th.q, &d.tq, err, errlen) || dput(im, th.h, &d.th, err, errlen) ||
-            dput(im, th.s, &d.ts, err, errlen) || dput(im, th.d, &d.td, err, errlen)) return -1;
+        // a BF16 matrix whose values do not all fit the scaled fp16 layout stays row-major
+        if (!repack_tiled((int)w.type, (const uint8_t *)w.data, (int)w.ne0, (int)w.ne1, th)) want_tiled = false;
+        else if (dput(im, th.q, &d.tq, err, errlen) || dput(im, th.h, &d.th, err, errlen) ||
+                 dput(im, th.s, &d.ts, err, errlen) || dput(im, th.d, &d.td, err, errlen)) return -1;
     }
     if ((need_rowmajor || !want_tiled) && !d.p) {
         uint8_t *p;
@@ -252,10 +253,10 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
         if (done[i]) continue;
         MmaArgs m{};
         m.ldx = ldx; m.K = K; m.pro = pro; m.norm_w = norm_w; m.eps = eps; m.err = im->derr;
-        const int type = fast[i].w.type;
+        const int type = tiled_type(fast[i].w.type);
         m.tile_start[0] = 0;
         for (size_t k = i; k < fast.size() && m.njob < 4; k++) {
-            if (done[k] || fast[k].w.type != type) continue;
+            if (done[k] || tiled_type(fast[k].w.type) != type) continue;
             const Job &f = fast[k];
             MmaJob &mj = m.job[m.njob];
             mj.w = tiled_of(f.w); mj.y = f.y; mj.ldy = f.ldy; mj.epi = f.epi;

@@ -50,7 +50,37 @@ def test_gemv_matches_float64(t, k, n):
             assert err < 1e-5, (t, k, n, T, path, err)
 
 
-@pytest.mark.parametrize("t", [xo.Q4_K, xo.Q6_K, xo.Q8_0])
+@pytest.mark.parametrize("t", [xo.Q5_K, xo.F16, xo.BF16])
+@pytest.mark.parametrize("k,n", [(2048, 2048), (6144, 2048), (2048, 6144)])
+def test_gemv_new_tiled_types_wide_and_chunked(t, k, n):
+    """Q5_K / F16 / BF16 at 5..16 tokens (the wide kernel) and 20 tokens (16-token chunks)."""
+    from xjb200 import xjcuda
+    raw = _w(t, k, n, k + 3 * n + t)
+    rng = np.random.default_rng(4)
+    for T in (5, 16, 20):
+        x = rng.standard_normal((T, k)).astype(np.float32)
+        want = _ref(t, raw, k, n, x)
+        y = xjcuda.gemv(t, raw, k, n, x)
+        assert np.abs(y - want).max() / np.abs(want).max() < 1e-5, (t, T)
+
+
+def test_bf16_outside_scaled_fp16_stays_exact():
+    """A BF16 block spanning more than fp16 can carry (1 and 2^-40 side by side) keeps the matrix on
+    the row-major kernel; the result still matches the float64 product."""
+    from xjb200 import xjcuda
+    k, n = 512, 32
+    rng = np.random.default_rng(9)
+    w = (rng.standard_normal((n, k)) * 0.02).astype(np.float32)
+    w[3, 5] = 1.0
+    w[3, 6] = 2.0 ** -40
+    raw = (w.view(np.uint32) >> 16).astype(np.uint16).tobytes()
+    x = rng.standard_normal((2, k)).astype(np.float32)
+    want = _ref(xo.BF16, raw, k, n, x)
+    y = xjcuda.gemv(xo.BF16, raw, k, n, x)
+    assert np.abs(y - want).max() / np.abs(want).max() < 1e-5
+
+
+@pytest.mark.parametrize("t", [xo.Q4_K, xo.Q6_K, xo.Q8_0, xo.Q5_K, xo.F16, xo.BF16])
 def test_token_results_independent_of_batch(t):
     from xjb200 import xjcuda
     k, n = 2048, 512
@@ -62,7 +92,7 @@ def test_token_results_independent_of_batch(t):
         assert y1[0].view(np.uint32).tolist() == y4[i].view(np.uint32).tolist()
 
 
-@pytest.mark.parametrize("t", [xo.Q4_K, xo.Q6_K, xo.Q8_0])
+@pytest.mark.parametrize("t", [xo.Q4_K, xo.Q6_K, xo.Q8_0, xo.Q5_K, xo.F16, xo.BF16])
 def test_wide_dynamic_range(t):
     from xjb200 import xjcuda
     k, n = 1024, 64
