@@ -154,6 +154,28 @@ def test_persistent_matches_graph_path_long_context(xc, mid_path):
     assert np.allclose(m0[:first], m1[:first], rtol=0.05, atol=2e-3)
 
 
+def test_persistent_attention_several_rounds_per_split(xc, mid_path, ref_lib):
+    """Context longer than the persistent kernel's splits hold in one round (mid: 2 KV heads, 74 splits of
+    32 positions = 2368): every attention item walks several rounds of cached rows and the new row
+    enters in a later round. The ids must equal the reference's CPU path until a near tie."""
+    xc.set_option(xc.OPT_GEMV, 0)
+    xc.set_option(xc.OPT_KV_F32, 0)
+    xc.set_option(xc.OPT_PERSIST, 1)
+    m = xc.Model(mid_path)
+    p = np.random.default_rng(21).integers(0, m.n_vocab, 2600).astype(np.int32)
+    s = xc.Stage(m, 0, m.n_layer, 2700, 64)
+    toks, mar, _ = s.decode(p, 40, want_margins=True)
+    assert s.last_decode_launches()[1] == 1
+    s.close()
+    rm = ref_lib.Model(mid_path)
+    want, want_mar, _, _ = rm.greedy(p, 40, max_batch=64, n_ctx=2700)
+    rm.close()
+    diff = np.nonzero(toks != want)[0]
+    first = int(diff[0]) if diff.size else len(toks)
+    assert first >= 20 or want_mar[first] < 5e-3, (first, want_mar[first])
+    assert np.allclose(mar[:first], want_mar[:first], rtol=0.05, atol=2e-3)
+
+
 def test_reference_driver_runs_cuda_stage(xc, ref_lib, golden, tiny_path, config0_path):
     """The reference's own loader builds the xj_model and its greedy loop drives the CUDA stage."""
     for which in ("tiny", "config0"):
