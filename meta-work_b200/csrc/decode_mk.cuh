@@ -369,8 +369,8 @@ XJ_DEV void mk_prologue(const MkPhase &p, __half *xs, float *xsum, float *xinv, 
 
 // ------------------------------------------------------------------ K-quant units at T = 1
 // One warp's half of a Q4_K / Q6_K unit (16 rows x 128 codes: k-steps 8*HH .. 8*HH+7 of the super-block)
-// from a staged chunk, with unit_compute's arithmetic for the token's columns (lanes c = 0: columns 0
-// and 1 = hi and lo). Leaner than unit_compute at T = 1: the half index HH is a compile-time constant,
+// from a staged chunk, with unit_compute_n's arithmetic for the token's columns (lanes c = 0: columns 0
+// and 1 = hi and lo). Leaner than unit_compute_n at T = 1: the half index HH is a compile-time constant,
 // so each header byte is one byte-permute; and no lane predicate guards the operand loads: lanes whose
 // B-fragment column is not the token's (g >= 2) read the token's own columns again and lanes c != 0
 // read its block sums, which only changes D columns and partial rows that are never stored.
@@ -531,7 +531,7 @@ XJ_DEV void mk_q6k(const uint8_t *stage, int ui, int u, int lane, const __half *
     __syncwarp();
 }
 
-// One Q8_0 unit (16 rows x 32 codes) at T = 1, unit_compute's arithmetic with the block's scale
+// One Q8_0 unit (16 rows x 32 codes) at T = 1, unit_compute_n's arithmetic with the block's scale
 // multiplied by the activation block's inverse range scale.
 XJ_DEV void mk_q80(const uint8_t *stage, int ui, int u, int lane, bool bcol, const __half *xb, const float *xinv,
                    float &yg, float &yg8) {

@@ -636,7 +636,7 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, NT == 1 ? 2 : 1) k_gemv_mma(Mm
 }
 
 // ------------------------------------------------------------------ wide launches (5..16 tokens)
-// Activations for a wide launch are prepared once per GEMV by k_prep_x (one block per token, the same
+// Activations for a wide launch are prepared once per GEMV by k_prep_xt (one block per token, the same
 // arithmetic as k_gemv_mma's prologue: identical hi/lo values, block sums and range scales) into a
 // global buffer laid out as k_gemv_mma stages them: per token, columns hi and lo of xstride = K + 16
 // halves (bperm order within each 16), then the 32-wide block sums, then the range scales.
@@ -994,7 +994,7 @@ __global__ void __launch_bounds__(MMA_WARPS * 32, 1) k_gemv_wide(MmaArgs a, cons
 // sends each owner its rows with one bulk copy into the owner's receive buffer (distributed shared
 // memory, completion on the owner's mbarrier); CTA r then adds the ns partials in rank order and runs
 // the epilogue, so the result is deterministic. Per block and split the
-// arithmetic is unit_compute's (same fragments, same per-block scale terms); only the summation order
+// arithmetic is unit_compute_n's (same fragments, same per-block scale terms); only the summation order
 // over K differs from the 1..16-token kernels.
 constexpr int B64_WARPS = 8;
 constexpr int B64_TILES = 2 * B64_WARPS;          // row tiles per block
@@ -1067,7 +1067,7 @@ XJ_DEV void b64_dup(const uint32_t *f, uint32_t (&a)[2][4]) {
 // 16, two k-steps whose B fragments come from one 16-byte load (see b64_pos). wst[q]: tile q's weights
 // in the stage; xs: the stage's token rows; xsum: its block sums [4][64]; hh: which half of the
 // super-block. Each per-block scale term is applied to the fresh accumulator of its block, as in
-// unit_compute.
+// unit_compute_n.
 template <int TYPE, int NQ>
 XJ_DEV void b64_chunk(const uint8_t *const *wst, int hh, int lane, int T, int ntl, const uint8_t *xs, const float *xsum,
                       float *scw, float (&y)[2][8][4]) {
@@ -1500,7 +1500,7 @@ inline cudaError_t launch_mma_t(MmaArgs a, cudaStream_t st) {
     return cudaErrorInvalidValue;   // 5..16 tokens: launch_wide
 }
 
-// Wide launch (5..16 tokens) on activations prepared by k_prep_x into xbuf.
+// Wide launch (5..16 tokens) on activations prepared by k_prep_xt into xbuf.
 template <int TYPE>
 inline cudaError_t launch_wide_t(MmaArgs a, const void *xbuf, cudaStream_t st) {
     constexpr int MAXDEV = 64;
