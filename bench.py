@@ -569,7 +569,7 @@ def main():
     path = synth.cached_gguf(cfg, os.environ.get("XJ_MODEL_DIR", f"/tmp/xj_models_r{local}"))
     model = xjcuda.Model(path)
     n_vt = min(args.steps, 32)                                        # steps of the vtable e2e run
-    n_ctx = args.prompt + max(args.warmup, 3) + 2 * args.steps + n_vt + 16   # prefill + warm-up + timed + e2e runs
+    n_ctx = args.prompt + max(args.warmup, 3) + 3 * args.steps + n_vt + 16   # prefill + warm-up + timed, e2e, sampled runs
     stage = xjcuda.Stage(model, 0, model.n_layer, n_ctx, 8)
     prompt = np.random.default_rng(1234 + rank).integers(0, cfg.n_vocab, args.prompt).astype(np.int32)
 
@@ -609,13 +609,20 @@ def main():
         x = stage.forward(model.embed_many([tok]))
         tok = int(np.argmax(stage.logits(x)[0]))
     vt_ms = (time.perf_counter() - t0) * 1e3
+    # sampled decode (top-40 / top-p 0.95 / temperature 0.9, the session's settings) on the device: the
+    # same persistent kernel with its SAMPLE phase; device time of args.steps steps
+    stage.set_sampler(0.9, 1234 + rank)
+    stoks, _, sms = stage.decode(np.array([tok], np.int32), args.steps)
+    samp_launches = stage.last_decode_launches()[1]
+    stage.set_sampler(0.0)
+    samp_ms = float(sms[0] + sms[1])
     t_max = dev_ms
     e2e_max = e2e_ms
     if world > 1:
         import torch.distributed as dist
-        t = torch.tensor([dev_ms, e2e_ms, vt_ms], device="cuda")
+        t = torch.tensor([dev_ms, e2e_ms, vt_ms, samp_ms], device="cuda")
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        t_max, e2e_max, vt_ms = float(t[0]), float(t[1]), float(t[2])
+        t_max, e2e_max, vt_ms, samp_ms = float(t[0]), float(t[1]), float(t[2]), float(t[3])
     value = world * args.steps / (t_max / 1e3)
     e2e = world * args.steps / (e2e_max / 1e3)
     stage.close()
@@ -650,6 +657,10 @@ def main():
             "e2e_vtable": {"value": round(world * n_vt / (vt_ms / 1e3), 2), "unit": "tok/s", "steps": n_vt,
                            "h2d_bytes_per_step": 4 * cfg.n_embd, "d2h_bytes_per_step": 4 * cfg.n_vocab + 4 * cfg.n_embd,
                            "path": "xj_stage forward + logits with host buffers, argmax and embedding on the host"},
+            "sampled": {"value": round(world * args.steps / (samp_ms / 1e3), 2), "unit": "tok/s",
+                        "sampler": "temperature 0.9, top-k 40, top-p 0.95, seeded per position",
+                        "decode_kernel": "persistent" if samp_launches == 1 else "graph",
+                        "timing": "device time of one xj_cuda_decode call, max over ranks"},
             "roofline": {"bound": "hbm",
                          "kernel": "k_decode_persistent" if persistent else "decode-step CUDA graph",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",

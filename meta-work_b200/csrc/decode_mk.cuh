@@ -24,12 +24,15 @@
 //   ATTN   q/k RMSNorm + RoPE, the new K/V row, and attention over one split of the positions per work
 //          item; the last split of a head to finish merges the splits (counter + fence, no barrier)
 //   ARGMAX the greedy pick from the LM head's tile partials, the next token's embedding, position + 1
+//   SAMPLE (a sampler set) a top-k / top-p / temperature draw from the LM head's logits, keyed by the
+//          position (sample_row_dev, the session sampler's arithmetic), then as ARGMAX
 //
 // Matrix-vector products give the same bits as the standalone tensor-core kernel (same unit order,
 // same prologue arithmetic, same fixed-order reductions). GDN and attention sum in a different order
 // than the standalone kernels (more threads per row and per head), within float rounding.
 #pragma once
 #include "gemv_mma.cuh"
+#include "sample.cuh"
 
 namespace xjk {
 
@@ -46,7 +49,7 @@ constexpr int MK_MAX_SPLIT = 64;                      // attention splits per KV
 using BarC = BarNamed<1, MK_CTHREADS>;           // the compute warps only
 using BarP = BarNamed<2, MK_CTHREADS + 32>;      // compute + epilogue warps (descriptor hand-over, phase ends)
 
-enum { MK_GEMV = 0, MK_GDN = 1, MK_ATTN = 2, MK_ARGMAX = 3 };
+enum { MK_GEMV = 0, MK_GDN = 1, MK_ATTN = 2, MK_ARGMAX = 3, MK_SAMPLE = 4 };
 enum { PRO_GNORM = 3,                             // per-head RMSNorm(ssm_norm) * silu(z), core/xj_cpu.c:218-224
        PRO_GNORM_S = 4,                           // the same with x2 = silu(z) already (MK_EPI_SILU)
        PRO_SWIGLU_S = 5 };                        // x * up with x = silu(gate) already (MK_EPI_SILU)
@@ -65,7 +68,8 @@ struct alignas(16) MkPhase {
     // MK_GDN / MK_ATTN / MK_ARGMAX
     GdnArgs gdn;
     AttnArgs attn;
-    ArgmaxArgs am;
+    ArgmaxArgs am;               // MK_ARGMAX, MK_SAMPLE: where the pick goes
+    SampleArgs sa;               // MK_SAMPLE: the LM head's logits and the sampler settings
 };
 
 // One GEMV phase as the producer streams it (the weight regions of each job's tiled layout).
@@ -1025,6 +1029,36 @@ XJ_DEV void mk_gdn_phase(const GdnArgs &a, float *scr, int tid) {
     for (int it = blockIdx.x; it < items; it += gridDim.x) mk_gdn_item<S>(a, it, scr, tid);
 }
 
+// The SAMPLE phase on CTA 0's compute warps: k_sample_final's pick with 512 threads, its sampler state
+// in the activation staging area and the scale scratch after it (dead outside matrix-vector phases).
+constexpr size_t MK_SCRATCH_BYTES = MK_XS_BYTES + 2 * (MK_KMAX / 32) * 4 + MK_CWARPS * 128 * 4 + MK_NR * MK_CWARPS * 16 * 4;
+static_assert(sizeof(SampleSmem) <= MK_SCRATCH_BYTES, "the sampler state fits the phase scratch");
+XJ_DEV void mk_sample_phase(const SampleArgs &a, const ArgmaxArgs &g, SampleSmem &S, int tid) {
+    const int pos = ld_volatile(g.npast);
+    float mg = 0.0f;
+    const int id = sample_row_dev<BarC>(a.logits, a.n, a.temp, a.top_k, a.top_p, sample_uniform(a.seed, (unsigned long long)pos),
+                                        S, tid, MK_CTHREADS, &mg);
+    if (tid == 0) {
+        const int s = *g.step;
+        g.out_tok[s] = id;
+        if (g.margin) g.margin[s] = mg;
+        *g.cur = id;
+        *g.step = s + 1;
+        *g.npast = pos + 1;
+    }
+    const DevMat &emb = g.emb;
+    for (int e0 = tid * 8; e0 < emb.K; e0 += MK_CTHREADS * 8) {
+        float y[8];
+        if (id >= 0 && id < emb.N) dequant8(emb.type, emb.p + id * emb.ld, e0, y);
+        else {
+#pragma unroll
+            for (int l = 0; l < 8; l++) y[l] = 0.0f;
+        }
+#pragma unroll
+        for (int l = 0; l < 8; l++) g.x[e0 + l] = y[l];
+    }
+}
+
 // ------------------------------------------------------------------ the kernel
 __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1230,6 +1264,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                     else mk_attn_phase<__half>(A, p.attn, attn_n0 + step, scr, tid, tr ? trow : nullptr);
                 } else if (!ew && p.op == MK_ARGMAX) {
                     if (cta == 0) argmax_final_dev<BarC>(p.am, tid, MK_CTHREADS);
+                } else if (!ew && p.op == MK_SAMPLE) {
+                    if (cta == 0) mk_sample_phase(p.sa, p.am, *reinterpret_cast<SampleSmem *>(xs), tid);
                 }
                 if (tr) {
                     trow[1] = globaltimer();

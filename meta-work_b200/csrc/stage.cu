@@ -912,15 +912,22 @@ int mk_build(xj_stage *s, bool fwd, char *err, size_t errlen) {
         down.epi = EPI_ADD;
         ok = ok && mk_gemv(prog, stream, FF, PRO_SWIGLU_S, im->g, im->u, nullptr, eps, 0, {down});
     }
+    // with a sampler set, the LM head also writes its logits for the SAMPLE phase
+    const bool samp = im->samp_temp > 0.0f;
     if (!fwd) {
-        Job h{im->output, nullptr, im->output.N};
+        Job h{im->output, samp ? im->logits : nullptr, im->output.N};
         h.epi = EPI_ARGMAX; h.pbest = im->pbest; h.psecond = im->psecond; h.pidx = im->pidx;
         ok = ok && mk_gemv(prog, stream, E, PRO_NORM, im->x, nullptr, im->output_norm, eps, 0, {h});
     }
     if (!ok) { state = -1; seterr(err, errlen, "persistent decode needs every matrix in the tiled layout"); return -1; }
     if (!fwd) {
         MkPhase am{};
-        am.op = MK_ARGMAX; am.am = argmax_args(im);
+        am.op = samp ? MK_SAMPLE : MK_ARGMAX; am.am = argmax_args(im);
+        if (samp) {
+            SampleArgs &a = am.sa;
+            a.logits = im->logits; a.ld = im->output.N; a.n = im->output.N;
+            a.temp = im->samp_temp; a.top_p = im->samp_top_p; a.top_k = im->samp_top_k; a.seed = im->samp_seed;
+        }
         prog.push_back(am);
     }
     // side data each GEMV phase (and the GDN / attention phase after it) reads, for the producer's
@@ -1367,7 +1374,7 @@ int xj_cuda_decode(xj_stage *s, const int32_t *prompt, int n_prompt, int n_gen, 
     }
     CK(cudaMemsetAsync(im->step, 0, sizeof(int), im->st));
     int persist = 0;
-    if (g_opt_persist && im->samp_temp <= 0.0f) {   // the persistent kernel picks greedily
+    if (g_opt_persist) {   // the persistent kernel picks greedily or samples (a sampler set)
         char why[256];
         persist = mk_build(s, false, why, sizeof why) == 1;
     }
@@ -1908,6 +1915,8 @@ int xj_cuda_set_sampler(xj_stage *s, float temperature, int top_k, double top_p,
     im->samp_top_k = top_k;
     im->samp_top_p = top_p;
     im->samp_seed = seed;
+    // the decode program of the persistent kernel holds the pick phase and the sampler settings
+    if (im->mk_state == 1 && (was || now)) im->mk_state = 0;
     // the cached decode-step graph holds the pick kernel and its arguments
     if (im->step_graph && (was || now)) {
         cudaStreamSynchronize(im->st);

@@ -93,12 +93,15 @@ def test_sampled_frequencies_follow_the_probabilities():
     assert chi2 < 3 * cut + 30, (chi2, cut)      # df = cut - 1; far beyond the 0.999 quantile only on a bug
 
 
+@pytest.mark.parametrize("persist", [1, 0])
 @pytest.mark.parametrize("which", ["tiny", "mid"])
-def test_sampled_decode_matches_reference_stage(ref_lib, golden, tiny_path, mid_path, which):
+def test_sampled_decode_matches_reference_stage(ref_lib, golden, tiny_path, mid_path, which, persist):
     """xj_cuda_decode with a sampler against the reference CPU stage's logits sampled on the host with the
     same draws (counter = position of the row that produced the logits), 24 tokens; then the same seed
-    again, split over two calls, reproduces the ids."""
+    again, split over two calls, reproduces the ids. persist=1: the mid model samples inside the
+    persistent kernel (its SAMPLE phase); the tiny model's F32 matrices keep it on the per-phase path."""
     from xjb200 import xjcuda
+    xjcuda.set_option(xjcuda.OPT_PERSIST, persist)
     path = tiny_path if which == "tiny" else mid_path
     p = golden[f"{which}_prompt"]
     temp, seed, n_gen = 0.9, 424242, 24
@@ -121,6 +124,8 @@ def test_sampled_decode_matches_reference_stage(ref_lib, golden, tiny_path, mid_
     s.set_sampler(temp, seed)
     toks, _, _ = s.decode(p, n_gen)
     assert toks.tolist() == want
+    if which == "mid":
+        assert s.last_decode_launches()[1] == (1 if persist else (n_gen - 1) * xjcuda.lib().xj_cuda_graph_kernels(s.addr))
     s.reset()
     a, _, _ = s.decode(p, 10)                  # ids 0..9; id 9 is emitted, not yet fed
     b, _, _ = s.decode(a[-1:], n_gen - 10)     # feeds id 9, emits ids 10..23
@@ -130,3 +135,4 @@ def test_sampled_decode_matches_reference_stage(ref_lib, golden, tiny_path, mid_
     g0, _, _ = s.decode(p, 8)
     assert g0.tolist() == golden[f"{which}_tokens"][:8].tolist()
     s.close()
+    xjcuda.set_option(xjcuda.OPT_PERSIST, 1)
