@@ -1060,6 +1060,10 @@ XJ_DEV void mk_sample_phase(const SampleArgs &a, const ArgmaxArgs &g, SampleSmem
 }
 
 // ------------------------------------------------------------------ the kernel
+// FULL: the Q5_K / F16 unit code and the SAMPLE phase are compiled in. The lean variant (Q4_K, Q6_K,
+// Q8_0 matrices and the greedy pick) is what a Q4_K_M model decodes with: the extra code in the unit
+// loop and the phase switch measurably slows the whole step even where it never runs.
+template <bool FULL>
 __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ __align__(8) uint64_t full[MK_NS], empty[MK_NS];
@@ -1119,8 +1123,8 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                             uint8_t *st = ring + (size_t)slot * MK_SLOT;
                             if (type == XJ_Q4_K) mk_issue_t<XJ_Q4_K>(S, j, tile, u0, cu, st, &full[slot]);
                             else if (type == XJ_Q6_K) mk_issue_t<XJ_Q6_K>(S, j, tile, u0, cu, st, &full[slot]);
-                            else if (type == XJ_Q5_K) mk_issue_t<XJ_Q5_K>(S, j, tile, u0, cu, st, &full[slot]);
-                            else if (type == XJ_F16) mk_issue_t<XJ_F16>(S, j, tile, u0, cu, st, &full[slot]);
+                            else if (FULL && type == XJ_Q5_K) mk_issue_t<XJ_Q5_K>(S, j, tile, u0, cu, st, &full[slot]);
+                            else if (FULL && type == XJ_F16) mk_issue_t<XJ_F16>(S, j, tile, u0, cu, st, &full[slot]);
                             else mk_issue_t<XJ_Q8_0>(S, j, tile, u0, cu, st, &full[slot]);
                             *(volatile unsigned *)&s_issued = i + 1;
                             if (trp) {
@@ -1216,13 +1220,13 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                                     if (warp & 1) mk_q6k<1>(st, ui, u0 + ui, lane, xb2, xinv, scw, yg, yg8);
                                     else mk_q6k<0>(st, ui, u0 + ui, lane, xb2, xinv, scw, yg, yg8);
                                 }
-                            } else if (W.type == XJ_Q5_K) {
+                            } else if (FULL && W.type == XJ_Q5_K) {
                                 const int ui = warp >> 1;
                                 if (ui < cu) {
                                     if (warp & 1) mk_q5k<1>(st, ui, u0 + ui, lane, xb2, xsum, xinv, scw, yg, yg8);
                                     else mk_q5k<0>(st, ui, u0 + ui, lane, xb2, xsum, xinv, scw, yg, yg8);
                                 }
-                            } else if (W.type == XJ_F16) {
+                            } else if (FULL && W.type == XJ_F16) {
                                 static_assert(Geo<XJ_F16>::CU == MK_CWARPS, "one F16 unit per warp");
                                 if (warp < cu) mk_h32(st, warp, u0 + warp, lane, bcol, xb, xinv, yg, yg8);
                             } else {
@@ -1264,7 +1268,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                     else mk_attn_phase<__half>(A, p.attn, attn_n0 + step, scr, tid, tr ? trow : nullptr);
                 } else if (!ew && p.op == MK_ARGMAX) {
                     if (cta == 0) argmax_final_dev<BarC>(p.am, tid, MK_CTHREADS);
-                } else if (!ew && p.op == MK_SAMPLE) {
+                } else if (FULL && !ew && p.op == MK_SAMPLE) {
                     if (cta == 0) mk_sample_phase(p.sa, p.am, *reinterpret_cast<SampleSmem *>(xs), tid);
                 }
                 if (tr) {

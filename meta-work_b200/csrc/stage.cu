@@ -94,6 +94,7 @@ struct Impl {
     int step_kernels = 0;
     // persistent decode kernel: phase program (device), barrier counter, attention split scratch
     int mk_state = 0;          // 0: not built, 1: built, -1: this stage cannot use it
+    bool mk_full = false, mkf_full = false;   // the program needs the full kernel variant (Q5_K / F16 / sampling)
     MkPhase *mk_prog = nullptr;
     MkStream *mk_stream = nullptr;
     int mk_nphase = 0, mk_nstream = 0, mk_ctas = 0, mk_max_split = 1;
@@ -962,8 +963,12 @@ int mk_build(xj_stage *s, bool fwd, char *err, size_t errlen) {
     int sms = 0, per_sm = 0, coop = 0;
     CK(cudaDeviceGetAttribute(&coop, cudaDevAttrCooperativeLaunch, im->dev));
     CK(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, im->dev));
-    CK(cudaFuncSetAttribute(k_decode_persistent, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
-    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent, MK_THREADS, MK_SMEM));
+    CK(cudaFuncSetAttribute(k_decode_persistent<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
+    CK(cudaFuncSetAttribute(k_decode_persistent<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)MK_SMEM));
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k_decode_persistent<true>, MK_THREADS, MK_SMEM));
+    int per_sm_lean = 0;
+    CK(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm_lean, k_decode_persistent<false>, MK_THREADS, MK_SMEM));
+    if (per_sm_lean < per_sm) per_sm = per_sm_lean;
     if (!coop || per_sm < 1) { state = -1; seterr(err, errlen, "cooperative launch of the persistent decode kernel is not possible"); return -1; }
     im->mk_ctas = sms;
     // the head phase leaves one greedy-pick partial per CTA that holds LM-head tiles
@@ -996,6 +1001,11 @@ int mk_build(xj_stage *s, bool fwd, char *err, size_t errlen) {
         im->mk_ops.clear();
         for (const MkPhase &q : prog) im->mk_ops.push_back(q.op);
     }
+    bool full = false;
+    for (const MkStream &q : stream)
+        for (int j = 0; j < q.njob; j++) full = full || !(q.type[j] == XJ_Q4_K || q.type[j] == XJ_Q6_K || q.type[j] == XJ_Q8_0);
+    for (const MkPhase &q : prog) full = full || q.op == MK_SAMPLE;
+    (fwd ? im->mkf_full : im->mk_full) = full;
     state = 1;
     return 1;
 }
@@ -1014,7 +1024,8 @@ int mk_launch(xj_stage *s, int n, bool fwd, char *err, size_t errlen) {
     CK(cudaMemsetAsync(im->mk_diag, 0, sizeof(int) * 8, im->st));
     CK(cudaMemsetAsync(im->mk_acnt, 0, sizeof(int) * (size_t)s->m->hp.n_head, im->st));
     void *args[] = {&a};
-    CK(cudaLaunchCooperativeKernel((const void *)k_decode_persistent, dim3(im->mk_ctas), dim3(MK_THREADS), args, MK_SMEM, im->st));
+    const void *kern = (fwd ? im->mkf_full : im->mk_full) ? (const void *)k_decode_persistent<true> : (const void *)k_decode_persistent<false>;
+    CK(cudaLaunchCooperativeKernel(kern, dim3(im->mk_ctas), dim3(MK_THREADS), args, MK_SMEM, im->st));
     return 0;
 }
 
