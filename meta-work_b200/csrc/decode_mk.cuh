@@ -1060,9 +1060,10 @@ XJ_DEV void mk_sample_phase(const SampleArgs &a, const ArgmaxArgs &g, SampleSmem
 }
 
 // ------------------------------------------------------------------ the kernel
-// FULL: the Q5_K / F16 unit code and the SAMPLE phase are compiled in. The lean variant (Q4_K, Q6_K,
-// Q8_0 matrices and the greedy pick) is what a Q4_K_M model decodes with: the extra code in the unit
-// loop and the phase switch measurably slows the whole step even where it never runs.
+// FULL: the Q5_K / F16 / Q8_0 unit code, the SAMPLE phase and the phase trace are compiled in. The lean
+// variant (Q4_K and Q6_K matrices, the greedy pick, no trace) is what a Q4_K_M model decodes with: the
+// extra code in the unit loop and the phase switch measurably slows the whole step even where it never
+// runs.
 template <bool FULL>
 __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
     extern __shared__ __align__(128) uint8_t smem[];
@@ -1102,7 +1103,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                 const MkStream &S = sst[gk & 1];
                 const int kn = k + 1 < A.nstream ? k + 1 : 0;
                 copy_desc_async(&sst[(gk + 1) & 1], &A.stream[kn], (int)sizeof(MkStream), lane);
-                unsigned long long *trp = A.trace && step == A.nsteps - 1 ? A.trace + ((size_t)cta * A.nphase + S.ph) * 12 : nullptr;
+                unsigned long long *trp = FULL && A.trace && step == A.nsteps - 1 ? A.trace + ((size_t)cta * A.nphase + S.ph) * 12 : nullptr;
                 if (lane < 6 && S.pf[lane]) {
                     // this CTA's slice of the side-data range (16-byte granules)
                     const unsigned bytes = S.pf_bytes[lane];
@@ -1125,7 +1126,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                             else if (type == XJ_Q6_K) mk_issue_t<XJ_Q6_K>(S, j, tile, u0, cu, st, &full[slot]);
                             else if (FULL && type == XJ_Q5_K) mk_issue_t<XJ_Q5_K>(S, j, tile, u0, cu, st, &full[slot]);
                             else if (FULL && type == XJ_F16) mk_issue_t<XJ_F16>(S, j, tile, u0, cu, st, &full[slot]);
-                            else mk_issue_t<XJ_Q8_0>(S, j, tile, u0, cu, st, &full[slot]);
+                            else if (FULL) mk_issue_t<XJ_Q8_0>(S, j, tile, u0, cu, st, &full[slot]);
                             *(volatile unsigned *)&s_issued = i + 1;
                             if (trp) {
                                 const unsigned long long now = globaltimer();
@@ -1161,9 +1162,9 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                 const MkPhase &p = sph[gp & 1];
                 const int pn = ph + 1 < A.nphase ? ph + 1 : 0;
                 if (!ew) copy_desc_async(&sph[(gp + 1) & 1], &A.prog[pn], (int)sizeof(MkPhase), tid);
-                const bool last_step = A.trace && step == A.nsteps - 1;
+                const bool last_step = FULL && A.trace && step == A.nsteps - 1;   // tracing: the full variant
                 const bool tr = last_step && tid == 0, tre = last_step && tid == MK_EWARP * 32;
-                unsigned long long *trow = A.trace ? A.trace + ((size_t)cta * A.nphase + ph) * 12 : nullptr;
+                unsigned long long *trow = FULL && A.trace ? A.trace + ((size_t)cta * A.nphase + ph) * 12 : nullptr;
                 unsigned long long wait_ns = 0;
                 if (tr) trow[0] = globaltimer();
                 if (p.op == MK_GEMV && cta < p.ntiles && ew) {
@@ -1229,7 +1230,7 @@ __global__ void __launch_bounds__(MK_THREADS, 1) k_decode_persistent(MkArgs A) {
                             } else if (FULL && W.type == XJ_F16) {
                                 static_assert(Geo<XJ_F16>::CU == MK_CWARPS, "one F16 unit per warp");
                                 if (warp < cu) mk_h32(st, warp, u0 + warp, lane, bcol, xb, xinv, yg, yg8);
-                            } else {
+                            } else if (FULL) {
 #pragma unroll
                                 for (int k = 0; k < Geo<XJ_Q8_0>::CU / MK_CWARPS; k++) {
                                     const int ui = warp + k * MK_CWARPS;

@@ -94,7 +94,7 @@ struct Impl {
     int step_kernels = 0;
     // persistent decode kernel: phase program (device), barrier counter, attention split scratch
     int mk_state = 0;          // 0: not built, 1: built, -1: this stage cannot use it
-    bool mk_full = false, mkf_full = false;   // the program needs the full kernel variant (Q5_K / F16 / sampling)
+    bool mk_full = false, mkf_full = false;   // the program needs the full kernel variant (Q5_K / F16 / Q8_0 / sampling)
     MkPhase *mk_prog = nullptr;
     MkStream *mk_stream = nullptr;
     int mk_nphase = 0, mk_nstream = 0, mk_ctas = 0, mk_max_split = 1;
@@ -1003,7 +1003,7 @@ int mk_build(xj_stage *s, bool fwd, char *err, size_t errlen) {
     }
     bool full = false;
     for (const MkStream &q : stream)
-        for (int j = 0; j < q.njob; j++) full = full || !(q.type[j] == XJ_Q4_K || q.type[j] == XJ_Q6_K || q.type[j] == XJ_Q8_0);
+        for (int j = 0; j < q.njob; j++) full = full || !(q.type[j] == XJ_Q4_K || q.type[j] == XJ_Q6_K);
     for (const MkPhase &q : prog) full = full || q.op == MK_SAMPLE;
     (fwd ? im->mkf_full : im->mk_full) = full;
     state = 1;
@@ -1024,7 +1024,8 @@ int mk_launch(xj_stage *s, int n, bool fwd, char *err, size_t errlen) {
     CK(cudaMemsetAsync(im->mk_diag, 0, sizeof(int) * 8, im->st));
     CK(cudaMemsetAsync(im->mk_acnt, 0, sizeof(int) * (size_t)s->m->hp.n_head, im->st));
     void *args[] = {&a};
-    const void *kern = (fwd ? im->mkf_full : im->mk_full) ? (const void *)k_decode_persistent<true> : (const void *)k_decode_persistent<false>;
+    const bool full = (fwd ? im->mkf_full : im->mk_full) || a.trace;   // the phase trace is in the full variant
+    const void *kern = full ? (const void *)k_decode_persistent<true> : (const void *)k_decode_persistent<false>;
     CK(cudaLaunchCooperativeKernel(kern, dim3(im->mk_ctas), dim3(MK_THREADS), args, MK_SMEM, im->st));
     return 0;
 }
