@@ -516,6 +516,7 @@ def run_phase_trace(args) -> dict:
                                     (("to_item", 7), ("qk_norm_rope", 8), ("rows", 9), ("rounds", 10),
                                      ("split_counter", 11), ("merge", 12), ("phase_max", 1))}
     out["by_kind_max_cta_us"] = {kinds.get(k, str(k)): round(float(t[t[:, 0] == k, 1].sum()), 1) for k in kinds}
+    out["phases_by_kind"] = {kinds.get(k, str(k)): int((t[:, 0] == k).sum()) for k in kinds}
     return out
 
 
@@ -683,6 +684,17 @@ def main():
         if pipe_line:
             line["pipeline"] = pipe_line
         line["gdn"] = run_gdn(xjcuda, peak, peak_kind)
+        # the same GDN step inside the persistent decode kernel (config 3 has 21 such layers of 16 heads x
+        # 128x128): mean over its GDN phases of the slowest CTA, from a short traced decode
+        tr = run_phase_trace(args)
+        n_gdn = tr["phases_by_kind"]["gdn"]
+        if n_gdn:
+            us = tr["by_kind_max_cta_us"]["gdn"] / n_gdn
+            nbytes = 2 * 16 * 128 * 128 * 4
+            line["gdn"]["b1_in_persistent_kernel"] = {
+                "us": round(us, 2), "state_bytes": nbytes, "achieved": round(nbytes / (us / 1e6) / 1e9, 1),
+                "frac": round(nbytes / (us / 1e6) / 1e9 / peak, 4),
+                "timing": "phase trace (device clock), slowest CTA of each GDN phase, mean over the step's 21 layers"}
         if args.gemv:
             line["gemv"] = run_gemv(xjcuda, synth, peak, peak_kind, **gemv_kw(args))
         if spec_line:
