@@ -143,9 +143,10 @@ XJ_DEV void mk_record(int *diag, int kind, int step, int ph, int idx, int extra)
 // back and wakes as soon as the phase completes. The grid's error word is a global load of about a
 // microsecond: it is issued every 16 polls and its value read 16 polls later, so the wait never stalls on
 // it; the same polls read the clock and, if `nap` is set, sleep that many ns.
-XJ_DEV bool mk_wait(uint64_t *bar, uint32_t parity, int *err, int code, int *diag = nullptr, int step = 0,
-                    int ph = 0, int idx = 0, int nap = 0) {
-    if (mbar_try_wait(bar, parity)) return true;
+// The polling part, out of line: the fast path (the phase already complete) stays a single try_wait in
+// the callers' loops, which keeps the unit loop's code short.
+__device__ __noinline__ bool mk_wait_slow(uint64_t *bar, uint32_t parity, int *err, int code, int *diag, int step,
+                                          int ph, int idx, int nap) {
     const unsigned long long t0 = globaltimer();
     int ev = ld_volatile(err);
     for (int it = 1; it < (1 << 26); it++) {
@@ -160,6 +161,11 @@ XJ_DEV bool mk_wait(uint64_t *bar, uint32_t parity, int *err, int code, int *dia
     mk_record(diag, code == 1 ? 10 + (int)parity : code, step, ph, idx, (int)(globaltimer() - t0) / 1000);
     atomicExch(err, code);
     return false;
+}
+XJ_DEV bool mk_wait(uint64_t *bar, uint32_t parity, int *err, int code, int *diag = nullptr, int step = 0,
+                    int ph = 0, int idx = 0, int nap = 0) {
+    if (mbar_try_wait(bar, parity)) return true;
+    return mk_wait_slow(bar, parity, err, code, diag, step, ph, idx, nap);
 }
 
 // All compute and epilogue threads of all CTAs: returns false (uniformly within the CTA) when the grid
