@@ -42,7 +42,7 @@ constexpr int MK_EWARP = MK_CWARPS + 1;          // the epilogue warp (after the
 constexpr int MK_THREADS = MK_CTHREADS + 64;     // + the producer and the epilogue warp
 constexpr int MK_NR = 4;                         // tile partial buffers between compute and epilogue warps
 constexpr int MK_SLOT = 26880;                   // largest chunk: 8 Q6_K units
-constexpr int MK_NS = 6;                         // ring slots
+constexpr int MK_NS = 3;                         // ring slots (3 measured faster than 2, 4 or 6)
 constexpr int MK_KMAX = MMA_KMAX_PT * MK_CTHREADS;
 constexpr int MK_XS_BYTES = 2 * (MK_KMAX + 16) * 2;   // hi/lo fp16 columns (also GDN / attention scratch)
 constexpr int MK_MAX_SPLIT = 64;                      // attention splits per KV head
