@@ -353,148 +353,275 @@ __global__ void __launch_bounds__(256) k_gdn_chunk_prep(GdnArgs a, float *qn, fl
         }
 }
 
-template <int S> constexpr size_t gdn_chunk_smem() { return ((size_t)2 * GC_C * (S + 4) + 3 * GC_C * (GC_C + 1) + 4 * GC_C * 17) * 4; }
 template <int S> constexpr size_t gdn_prep_smem() { return (size_t)2 * S * (GC_C + 4) * 4; }
 
-// Grid (Hv, S / 16), 256 threads: rows [16 r, 16 r + 16) of value head hv's state over all chunks;
-// thread (row rr = tid / 16, column block cb = tid % 16) keeps state columns [cb*S/16, (cb+1)*S/16) of
-// its row in registers. Raw outputs o (scaled by 1/sqrt(S), before the gated norm) to out[t][hv*S + j].
+// The chunk-parallel half of the recurrence. Per value head and chunk, with A[i][l] = b_i e^(G_i - G_l)
+// (k_i . k_l) for l < i, the substitution above is (I + A) u = b (v - e^G M0 k), so with
+//   W = (I + A)^-1 diag(b e^G) K,   U0 = (I + A)^-1 diag(b) V                      (state-independent)
+// u = U0 - W M0^T. Substituting into o and M_C:
+//   o = O0 + Q' M0^T,  Q' = diag(e^G) Q - D W,  O0 = D U0,  D[i][l] = e^(G_i - G_l) (q_i . k_l), l <= i
+//   M_C = e^G_C M0 + u^T Kd,  Kd[l] = e^(G_C - G_l) k_l
+// so the walk over chunks (k_gdn_chunk) is three small matrix products per chunk and this kernel runs
+// every chunk at once. Tokens past the prompt count as g = 0, b = 0, q = k = v = 0 (they change nothing).
+// Scratch wx, all [T][Hv][S]: W, Q', Kd, U0, O0; then e^(G_C) per [Hv][chunk].
+inline size_t gc_wx_floats(int T, int Hv, int S) { return (size_t)5 * T * Hv * S + (size_t)Hv * ((T + GC_C - 1) / GC_C); }
+template <int S> constexpr size_t gdn_solve_smem() { return ((size_t)2 * GC_C * (GC_C + 4) + 3 * GC_C * (S + 4)) * 4; }
+
+// Grid (Hv, nchunks), 2S threads: thread c < S takes column c of W and then of Q' (and of Kd), thread
+// S + c column c of U0 and then of O0. A column of (I + A)^-1 X needs only the same column's earlier
+// rows, so each thread solves its column on its own, in place in shared memory.
 template <int S>
-__global__ void __launch_bounds__(256) k_gdn_chunk(GdnArgs a, const float *qn, const float *kn, const float *kk,
-                                                   const float *qk) {
+__global__ void __launch_bounds__(2 * S) k_gdn_chunk_solve(GdnArgs a, const float *qn, const float *kn, const float *kk,
+                                                           const float *qk, float *wx) {
     griddep_wait();
     griddep_launch();   // successors may start their prologue; they wait for this grid before reading
-    constexpr int P = S / 16, SP = S + 4, CP = GC_C + 1;
+    constexpr int CP = GC_C + 4, SP = S + 4, NT = 2 * S;
     extern __shared__ __align__(16) float gsm[];
-    float *qs = gsm, *ks = qs + GC_C * SP;                 // [C][SP]
-    float *dec = ks + GC_C * SP;                           // [C][CP]: e^(G_i - G_l), l <= i
-    float *KKs = dec + GC_C * CP, *QKs = KKs + GC_C * CP;  // [C][CP]
-    float *Mk = QKs + GC_C * CP, *Mq = Mk + GC_C * 17, *U = Mq + GC_C * 17, *Vs = U + GC_C * 17;   // [C][17]
+    float *Am = gsm, *Dm = Am + GC_C * CP;                  // [C][CP]: A (l < i), D (l <= i)
+    float *Xk = Dm + GC_C * CP, *Xv = Xk + GC_C * SP, *Xq = Xv + GC_C * SP;   // [C][SP]: k, v, q rows of the chunk
     __shared__ float G[GC_C], bv[GC_C], eG[GC_C];
-    const int hv = blockIdx.x, hk = hv % a.Hk, r0 = blockIdx.y * 16;
-    const int tid = threadIdx.x, rr = tid >> 4, cb = tid & 15, lane = tid & 31, warp = tid >> 5;
-    const int j = r0 + rr;
-    const int nch = (a.T + GC_C - 1) / GC_C;
-    float m[P];
-    float *Mrow = a.ssm + (size_t)hv * S * S + (size_t)j * S + cb * P;
+    const int hv = blockIdx.x, hk = hv % a.Hk, ch = blockIdx.y, nch = gridDim.y;
+    const int t0 = ch * GC_C, n = a.T - t0 < GC_C ? a.T - t0 : GC_C;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const size_t plane = (size_t)a.T * a.Hv * S;
+    // every global operand first, loads batched ahead of the stores (each loop's trip count is fixed)
+    {
+        constexpr int NR = GC_C * (S / 4) / NT;            // 16-byte pieces per thread and array
+        float4 rk[NR], rq[NR];
+        float rv[4 * NR];
 #pragma unroll
-    for (int e = 0; e < P; e++) m[e] = __ldcg(Mrow + e);
-    const float dtv = a.dt[hv], Av = a.A[hv], qscale = 1.0f / sqrtf((float)S);
-    for (int ch = 0; ch < nch; ch++) {
-        const int t0 = ch * GC_C, n = a.T - t0 < GC_C ? a.T - t0 : GC_C;
-        __syncthreads();                                   // the previous chunk's shared data is consumed
-        for (int x = tid; x < GC_C * (S / 4); x += 256) {
-            const int i = x / (S / 4), c = (x % (S / 4)) * 4;
-            float4 q4 = make_float4(0.f, 0.f, 0.f, 0.f), k4 = q4;
-            if (i < n) {
-                q4 = __ldcg(reinterpret_cast<const float4 *>(qn + ((size_t)(t0 + i) * a.Hk + hk) * S + c));
-                k4 = __ldcg(reinterpret_cast<const float4 *>(kn + ((size_t)(t0 + i) * a.Hk + hk) * S + c));
-            }
-            *reinterpret_cast<float4 *>(qs + i * SP + c) = q4;
-            *reinterpret_cast<float4 *>(ks + i * SP + c) = k4;
+        for (int r = 0; r < NR; r++) {
+            const int x = tid + r * NT, i = x / (S / 4), c4 = (x % (S / 4)) * 4;
+            const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+            const size_t o = ((size_t)(t0 + i) * a.Hk + hk) * S + c4;
+            rk[r] = i < n ? __ldcg(reinterpret_cast<const float4 *>(kn + o)) : z4;
+            rq[r] = i < n ? __ldcg(reinterpret_cast<const float4 *>(qn + o)) : z4;
+            const float *vp = a.qkv + (size_t)(t0 + i) * a.ldq + 2 * a.key_dim + hv * S + c4;   // 4-byte aligned only
+#pragma unroll
+            for (int e = 0; e < 4; e++) rv[4 * r + e] = i < n ? lda(vp + e) : 0.0f;
         }
-        for (int x = tid; x < GC_C * 16; x += 256) {
-            const int i = x >> 4, row = x & 15;
-            Vs[i * 17 + row] = i < n ? lda(a.qkv + (size_t)(t0 + i) * a.ldq + 2 * a.key_dim + hv * S + r0 + row) : 0.0f;
+#pragma unroll
+        for (int r = 0; r < NR; r++) {
+            const int x = tid + r * NT, i = x / (S / 4), c4 = (x % (S / 4)) * 4;
+            *reinterpret_cast<float4 *>(Xk + i * SP + c4) = rk[r];
+            *reinterpret_cast<float4 *>(Xq + i * SP + c4) = rq[r];
+            *reinterpret_cast<float4 *>(Xv + i * SP + c4) = make_float4(rv[4 * r], rv[4 * r + 1], rv[4 * r + 2], rv[4 * r + 3]);
         }
+    }
+    if (warp == 0) {
+        // g, b per token; G by a sequential prefix sum (fp32)
+        const float dtv = a.dt[hv], Av = a.A[hv];
+        for (int i = lane; i < GC_C; i += 32) {
+            const int t = t0 + i;
+            G[i] = i < n ? softplus_f(lda(a.alpha + (size_t)t * a.ldg + hv) + dtv) * Av : 0.0f;
+            bv[i] = i < n ? sigm_f(lda(a.beta + (size_t)t * a.ldg + hv)) : 0.0f;
+        }
+        __syncwarp();
+        if (lane == 0) {
+            float acc = 0.0f;
+            for (int i = 0; i < GC_C; i++) { acc += G[i]; G[i] = acc; }
+        }
+        __syncwarp();
+        for (int i = lane; i < GC_C; i += 32) eG[i] = expf(G[i]);
+    }
+    {
+        // the chunk's k.k and q.k products (16-byte rows; the never-written upper blocks are masked)
         const float *KKg = kk + ((size_t)hk * nch + ch) * GC_C * GC_C, *QKg = qk + ((size_t)hk * nch + ch) * GC_C * GC_C;
-        for (int x = tid; x < GC_C * GC_C; x += 256) {
-            const int i = x / GC_C, l = x % GC_C;
-            KKs[i * CP + l] = l < i ? __ldcg(KKg + x) : 0.0f;
-            QKs[i * CP + l] = l <= i ? __ldcg(QKg + x) : 0.0f;
+        constexpr int NQ = GC_C * GC_C / 4 / NT;
+        float4 rkk[NQ], rqk[NQ];
+#pragma unroll
+        for (int r = 0; r < NQ; r++) {
+            const int x = (tid + r * NT) * 4;
+            rkk[r] = __ldcg(reinterpret_cast<const float4 *>(KKg + x));
+            rqk[r] = __ldcg(reinterpret_cast<const float4 *>(QKg + x));
         }
-        if (warp == 0) {
-            // g, b per token; G by a sequential prefix sum (fp32)
-            for (int i = lane; i < GC_C; i += 32) {
-                const int t = t0 + i;
-                const float gi = i < n ? softplus_f(lda(a.alpha + (size_t)t * a.ldg + hv) + dtv) * Av : 0.0f;
-                G[i] = gi;
-                bv[i] = i < n ? sigm_f(lda(a.beta + (size_t)t * a.ldg + hv)) : 0.0f;
-            }
-            __syncwarp();
-            if (lane == 0) {
-                float acc = 0.0f;
-                for (int i = 0; i < GC_C; i++) { acc += G[i]; G[i] = acc; }
-            }
-            __syncwarp();
-            for (int i = lane; i < GC_C; i += 32) eG[i] = expf(G[i]);
-        }
-        __syncthreads();
-        for (int x = tid; x < GC_C * GC_C; x += 256) {
-            const int i = x / GC_C, l = x % GC_C;
-            dec[i * CP + l] = l <= i ? expf(G[i] - G[l]) : 0.0f;
-        }
-        // M0 k_i and M0 q_i for this CTA's rows: partial over the thread's columns, summed over the 16
-        // threads of the row (a half-warp)
-        for (int i = 0; i < n; i++) {
-            float pk = 0.0f, pq = 0.0f;
-            float kv[P], qv[P];
-            if constexpr (P % 4 == 0) {
+        __syncthreads();                                   // G, bv, eG
 #pragma unroll
-                for (int e = 0; e < P; e += 4) {
-                    const float4 k4 = *reinterpret_cast<const float4 *>(ks + i * SP + cb * P + e);
-                    const float4 q4 = *reinterpret_cast<const float4 *>(qs + i * SP + cb * P + e);
-                    kv[e] = k4.x; kv[e + 1] = k4.y; kv[e + 2] = k4.z; kv[e + 3] = k4.w;
-                    qv[e] = q4.x; qv[e + 1] = q4.y; qv[e + 2] = q4.z; qv[e + 3] = q4.w;
-                }
-            } else {
+        for (int r = 0; r < NQ; r++) {
+            const int x = (tid + r * NT) * 4, i = x / GC_C, l0 = x % GC_C;
+            const float kv4[4] = {rkk[r].x, rkk[r].y, rkk[r].z, rkk[r].w}, qv4[4] = {rqk[r].x, rqk[r].y, rqk[r].z, rqk[r].w};
 #pragma unroll
-                for (int e = 0; e < P; e++) { kv[e] = ks[i * SP + cb * P + e]; qv[e] = qs[i * SP + cb * P + e]; }
-            }
-#pragma unroll
-            for (int e = 0; e < P; e++) {
-                pk = fmaf(m[e], kv[e], pk);
-                pq = fmaf(m[e], qv[e], pq);
-            }
-#pragma unroll
-            for (int o = 8; o; o >>= 1) {
-                pk += __shfl_xor_sync(0xffffffffu, pk, o);
-                pq += __shfl_xor_sync(0xffffffffu, pq, o);
-            }
-            if (cb == 0) { Mk[i * 17 + rr] = pk; Mq[i * 17 + rr] = pq; }
-        }
-        __syncthreads();
-        // forward substitution for u: warp w solves rows 2w, 2w+1; lane p of a row sums l = p, p+16, ..
-        {
-            const int row = 2 * warp + (lane >> 4), p = lane & 15;
-            for (int i = 0; i < n; i++) {
-                float s = 0.0f;
-                for (int l = p; l < i; l += 16) s = fmaf(dec[i * CP + l] * KKs[i * CP + l], U[l * 17 + row], s);
-#pragma unroll
-                for (int o = 8; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
-                if (p == 0) U[i * 17 + row] = bv[i] * (Vs[i * 17 + row] - eG[i] * Mk[i * 17 + row]) - bv[i] * s;
-                __syncwarp();
-            }
-        }
-        __syncthreads();
-        // outputs o_i for this CTA's rows
-        for (int x = tid; x < n * 16; x += 256) {
-            const int i = x >> 4, row = x & 15;
-            float acc = eG[i] * Mq[i * 17 + row];
-            for (int l = 0; l <= i; l++) acc = fmaf(dec[i * CP + l] * QKs[i * CP + l], U[l * 17 + row], acc);
-            a.out[(size_t)(t0 + i) * a.ldo + hv * S + r0 + row] = acc * qscale;
-        }
-        // state at the chunk's end
-        const float eGC = eG[n - 1];
-#pragma unroll
-        for (int e = 0; e < P; e++) m[e] *= eGC;
-        for (int i = 0; i < n; i++) {
-            const float w = dec[(n - 1) * CP + i] * U[i * 17 + rr];
-            if constexpr (P % 4 == 0) {
-#pragma unroll
-                for (int e = 0; e < P; e += 4) {
-                    const float4 k4 = *reinterpret_cast<const float4 *>(ks + i * SP + cb * P + e);
-                    m[e] = fmaf(w, k4.x, m[e]); m[e + 1] = fmaf(w, k4.y, m[e + 1]);
-                    m[e + 2] = fmaf(w, k4.z, m[e + 2]); m[e + 3] = fmaf(w, k4.w, m[e + 3]);
-                }
-            } else {
-#pragma unroll
-                for (int e = 0; e < P; e++) m[e] = fmaf(w, ks[i * SP + cb * P + e], m[e]);
+            for (int e = 0; e < 4; e++) {
+                const int l = l0 + e;
+                const float d = l <= i ? expf(G[i] - G[l]) : 0.0f;
+                Am[i * CP + l] = l < i ? bv[i] * d * kv4[e] : 0.0f;
+                Dm[i * CP + l] = l <= i ? d * qv4[e] : 0.0f;
             }
         }
     }
+    __syncthreads();
+    if (tid < S) {
+        // Kd = e^(G_C - G_l) k_l, before the W threads overwrite the k rows
+        float *kd = wx + 2 * plane;
+        for (int i = 0; i < n; i++) kd[((size_t)(t0 + i) * a.Hv + hv) * S + tid] = expf(G[GC_C - 1] - G[i]) * Xk[i * SP + tid];
+    }
+    __syncthreads();
+    const bool isw = tid < S;
+    const int c = isw ? tid : tid - S;
+    float *X = isw ? Xk : Xv;
+    // column c of W (or U0) replaces column c of X in place, row by row (rows < i of the column are
+    // final when row i starts: one thread owns the column); four partial sums per row
+    for (int i = 0; i < GC_C; i++) {
+        float s0 = bv[i] * (isw ? eG[i] : 1.0f) * X[i * SP + c], s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+        const float *ar = Am + i * CP;
+#pragma unroll 2
+        for (int l = 0; l < (i & ~3); l += 4) {
+            const float4 a4 = *reinterpret_cast<const float4 *>(ar + l);
+            s0 = fmaf(-a4.x, X[l * SP + c], s0); s1 = fmaf(-a4.y, X[(l + 1) * SP + c], s1);
+            s2 = fmaf(-a4.z, X[(l + 2) * SP + c], s2); s3 = fmaf(-a4.w, X[(l + 3) * SP + c], s3);
+        }
+        for (int l = i & ~3; l < i; l++) s0 = fmaf(-ar[l], X[l * SP + c], s0);
+        const float v = (s0 + s1) + (s2 + s3);
+        X[i * SP + c] = v;
+        if (i < n) (wx + (isw ? 0 : 3 * plane))[((size_t)(t0 + i) * a.Hv + hv) * S + c] = v;
+    }
+    // Q' = e^G q - D W (W threads), O0 = D U0 (U0 threads)
+    float *dst2 = wx + (isw ? plane : 4 * plane);
+    for (int i = 0; i < n; i++) {
+        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
+        const float *dr = Dm + i * CP;
+#pragma unroll 2
+        for (int l = 0; l < ((i + 1) & ~3); l += 4) {
+            const float4 d4 = *reinterpret_cast<const float4 *>(dr + l);
+            s0 = fmaf(d4.x, X[l * SP + c], s0); s1 = fmaf(d4.y, X[(l + 1) * SP + c], s1);
+            s2 = fmaf(d4.z, X[(l + 2) * SP + c], s2); s3 = fmaf(d4.w, X[(l + 3) * SP + c], s3);
+        }
+        for (int l = (i + 1) & ~3; l <= i; l++) s0 = fmaf(dr[l], X[l * SP + c], s0);
+        const float sv = (s0 + s1) + (s2 + s3);
+        const size_t o = ((size_t)(t0 + i) * a.Hv + hv) * S + c;
+        dst2[o] = isw ? eG[i] * Xq[i * SP + c] - sv : sv;
+    }
+    if (tid == 0) wx[5 * plane + (size_t)hv * nch + ch] = eG[GC_C - 1];
+}
+
+constexpr int GC_RP = 20;         // row stride (floats) of the walk's 16-row column tiles (16-byte rows)
+template <int S> constexpr size_t gdn_chunk_smem() { return ((size_t)5 * GC_C * (S + 4) + 16 * (S + 4) + 5 * GC_C * GC_RP) * 4; }
+// State column of element e of a walk thread's P = S / 16 (cb: the thread's column block): groups of
+// four 64 apart when P is a multiple of 4 (conflict-free 16-byte shared loads), else P consecutive.
+template <int S>
+XJ_DEV int gdn_wcol(int cb, int e) {
+    constexpr int P = S / 16;
+    if constexpr (P % 4 == 0) return (e >> 2) * 64 + cb * 4 + (e & 3);
+    else return cb * P + e;
+}
+// 16 bytes global -> shared, asynchronously (zeros when !valid; src must still be a mapped address).
+XJ_DEV void gc_cp16(float *dst, const float *src, bool valid) {
+    asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" :: "r"((uint32_t)__cvta_generic_to_shared(dst)), "l"(src),
+                 "r"(valid ? 16 : 0) : "memory");
+}
+XJ_DEV void gc_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N> XJ_DEV void gc_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
+
+// Grid (Hv, S / 16), 256 threads: rows [16 r, 16 r + 16) of value head hv's state over all chunks, each
+// thread (row rr = tid / 16, column block cb = tid % 16) keeping P state columns of its row in registers.
+// Per chunk, from the solve kernel's rows: u = U0 - W M0^T and o = O0 + Q' M0^T (thread: token tid / 4,
+// rows tid % 4 + {0, 4, 8, 12}), then M = e^G_C M0 + u^T Kd. Raw outputs o (scaled by 1/sqrt(S), before
+// the gated norm) to out[t][hv*S + j]. The rows do not depend on the state, so they are copied in ahead:
+// W, Q', U0, O0 of chunk c + 1 (double-buffered) while chunk c computes, Kd of chunk c + 1 while chunk
+// c + 1 computes u and o (one commit group each, waited for in issue order).
+template <int S>
+__global__ void __launch_bounds__(256) k_gdn_chunk(GdnArgs a, const float *wx) {
+    griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
+    constexpr int P = S / 16, SP = S + 4, RP = GC_RP;
+    extern __shared__ __align__(16) float gsm[];
+    float *Wb = gsm, *Qb = Wb + 2 * GC_C * SP, *Kc = Qb + 2 * GC_C * SP;   // [2][C][SP], [2][C][SP], [C][SP]
+    float *Ms = Kc + GC_C * SP;                                           // [16][SP]: the CTA's state rows
+    float *Ub = Ms + 16 * SP, *Ob = Ub + 2 * GC_C * RP, *Us = Ob + 2 * GC_C * RP;   // [2][C][RP] x2, [C][RP]
+    const int hv = blockIdx.x, r0 = blockIdx.y * 16;
+    const int tid = threadIdx.x, rr = tid >> 4, cb = tid & 15;
+    const int gi = tid >> 2, gr = tid & 3;
+    const int nch = (a.T + GC_C - 1) / GC_C;
+    const size_t plane = (size_t)a.T * a.Hv * S;
+    const float *Wg = wx, *Qg = wx + plane, *Kg = wx + 2 * plane, *Ug = wx + 3 * plane, *Og = wx + 4 * plane;
+    const float *eGCg = wx + 5 * plane;
+    auto stage_wq = [&](int ch, int b) {
+        const int t0 = ch * GC_C, n = a.T - t0 < GC_C ? a.T - t0 : GC_C;
+        for (int x = tid; x < GC_C * (S / 4); x += 256) {
+            const int i = x / (S / 4), c = (x % (S / 4)) * 4;
+            const size_t o = i < n ? ((size_t)(t0 + i) * a.Hv + hv) * S + c : 0;
+            gc_cp16(Wb + (b * GC_C + i) * SP + c, Wg + o, i < n);
+            gc_cp16(Qb + (b * GC_C + i) * SP + c, Qg + o, i < n);
+        }
+        for (int x = tid; x < GC_C * 4; x += 256) {
+            const int i = x >> 2, q = (x & 3) * 4;
+            const size_t o = i < n ? ((size_t)(t0 + i) * a.Hv + hv) * S + r0 + q : 0;
+            gc_cp16(Ub + (b * GC_C + i) * RP + q, Ug + o, i < n);
+            gc_cp16(Ob + (b * GC_C + i) * RP + q, Og + o, i < n);
+        }
+        gc_commit();
+    };
+    auto stage_k = [&](int ch) {
+        const int t0 = ch * GC_C, n = a.T - t0 < GC_C ? a.T - t0 : GC_C;
+        for (int x = tid; x < GC_C * (S / 4); x += 256) {
+            const int i = x / (S / 4), c = (x % (S / 4)) * 4;
+            const size_t o = i < n ? ((size_t)(t0 + i) * a.Hv + hv) * S + c : 0;
+            gc_cp16(Kc + i * SP + c, Kg + o, i < n);
+        }
+        gc_commit();
+    };
+    float m[P];
+    float *Mrow = a.ssm + (size_t)hv * S * S + (size_t)(r0 + rr) * S;
 #pragma unroll
-    for (int e = 0; e < P; e++) Mrow[e] = m[e];
+    for (int e = 0; e < P; e++) m[e] = __ldcg(Mrow + gdn_wcol<S>(cb, e));
+    const float qscale = 1.0f / sqrtf((float)S);
+    stage_wq(0, 0);
+    stage_k(0);
+    for (int ch = 0; ch < nch; ch++) {
+        const int t0 = ch * GC_C, n = a.T - t0 < GC_C ? a.T - t0 : GC_C, b = ch & 1;
+        const float *Wc = Wb + b * GC_C * SP, *Qc = Qb + b * GC_C * SP, *Uc = Ub + b * GC_C * RP, *Oc = Ob + b * GC_C * RP;
+        gc_wait<1>();                                      // this chunk's W, Q', U0, O0 (Kd may be in flight)
+#pragma unroll
+        for (int e = 0; e < P; e++) Ms[rr * SP + gdn_wcol<S>(cb, e)] = m[e];
+        const float eGC = __ldcg(eGCg + (size_t)hv * nch + ch);
+        __syncthreads();
+        if (ch + 1 < nch) stage_wq(ch + 1, b ^ 1);         // that buffer's last reader was chunk ch - 1
+        // u and o of token gi, rows gr + 4x
+        float au[4] = {0.f, 0.f, 0.f, 0.f}, ao[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll 8
+        for (int c = 0; c < S; c += 4) {
+            const float4 w4 = *reinterpret_cast<const float4 *>(Wc + gi * SP + c);
+            const float4 q4 = *reinterpret_cast<const float4 *>(Qc + gi * SP + c);
+#pragma unroll
+            for (int x = 0; x < 4; x++) {
+                const float4 m4 = *reinterpret_cast<const float4 *>(Ms + (gr + 4 * x) * SP + c);
+                au[x] = fmaf(w4.x, m4.x, fmaf(w4.y, m4.y, fmaf(w4.z, m4.z, fmaf(w4.w, m4.w, au[x]))));
+                ao[x] = fmaf(q4.x, m4.x, fmaf(q4.y, m4.y, fmaf(q4.z, m4.z, fmaf(q4.w, m4.w, ao[x]))));
+            }
+        }
+#pragma unroll
+        for (int x = 0; x < 4; x++) {
+            const int r = gr + 4 * x;
+            Us[gi * RP + r] = Uc[gi * RP + r] - au[x];
+            if (gi < n) a.out[(size_t)(t0 + gi) * a.ldo + hv * S + r0 + r] = (Oc[gi * RP + r] + ao[x]) * qscale;
+        }
+        // this chunk's Kd (issued before the next chunk's W, Q', U0, O0, if any)
+        if (ch + 1 < nch) gc_wait<1>();
+        else gc_wait<0>();
+        __syncthreads();
+        // state at the chunk's end
+#pragma unroll
+        for (int e = 0; e < P; e++) m[e] *= eGC;
+        for (int i = 0; i < n; i++) {
+            const float u = Us[i * RP + rr];
+            if constexpr (P % 4 == 0) {
+#pragma unroll
+                for (int e = 0; e < P; e += 4) {
+                    const float4 k4 = *reinterpret_cast<const float4 *>(Kc + i * SP + gdn_wcol<S>(cb, e));
+                    m[e] = fmaf(u, k4.x, m[e]); m[e + 1] = fmaf(u, k4.y, m[e + 1]);
+                    m[e + 2] = fmaf(u, k4.z, m[e + 2]); m[e + 3] = fmaf(u, k4.w, m[e + 3]);
+                }
+            } else {
+#pragma unroll
+                for (int e = 0; e < P; e++) m[e] = fmaf(u, Kc[i * SP + gdn_wcol<S>(cb, e)], m[e]);
+            }
+        }
+        __syncthreads();                                   // Kc, Us and Ms are consumed
+        if (ch + 1 < nch) stage_k(ch + 1);
+    }
+    gc_wait<0>();
+#pragma unroll
+    for (int e = 0; e < P; e++) Mrow[gdn_wcol<S>(cb, e)] = m[e];
 }
 
 // Grid (T, Hv), S threads (S <= 1024): out[t][hv*S + j] = o * rsqrt(mean_j o^2 + eps) * norm_w[j] * silu(z),

@@ -79,7 +79,7 @@ struct Impl {
     void *b64_buf = nullptr;    // activations of a 64-token GEMV launch (stages taking more than 16 tokens)
     void *tc_buf = nullptr;     // the same in the tensor-core operand layout (k_gemm_tc)
     // chunked GDN (prompt forwards of >= GC_MIN_T tokens): normalised q, k and the chunk products
-    float *gc_qn = nullptr, *gc_kn = nullptr, *gc_kk = nullptr, *gc_qk = nullptr;
+    float *gc_qn = nullptr, *gc_kn = nullptr, *gc_kk = nullptr, *gc_qk = nullptr, *gc_wx = nullptr;
     float *pbest = nullptr, *psecond = nullptr;
     int *pidx = nullptr;
     int *derr = nullptr;       // device error word: set when a kernel's bounded wait gives up
@@ -408,22 +408,25 @@ GdnArgs gdn_args(Impl *im, const xj_hparams *hp, Layer &Ly, int T, bool ck) {
     return g;
 }
 
-// Chunked GDN over T tokens (no checkpoints): prep (per key head and chunk), state walk (per value head
-// and 16-row block), gated RMSNorm. Scratch: qn, kn [T][Hk][S], kk, qk [Hk][chunks][GC_C][GC_C].
+// Chunked GDN over T tokens (no checkpoints): prep (per key head and chunk), the chunk-parallel solve
+// (per value head and chunk), the state walk (per value head and 16-row block), gated RMSNorm.
+// Scratch: qn, kn [T][Hk][S], kk, qk [Hk][chunks][GC_C][GC_C], wx gc_wx_floats(T, Hv, S).
 template <int S>
-void launch_gdn_chunked(Impl *im, const GdnArgs &g, float *qn, float *kn, float *kk, float *qk) {
+void launch_gdn_chunked(Impl *im, const GdnArgs &g, float *qn, float *kn, float *kk, float *qk, float *wx) {
     static bool attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr[dev & 63]) {
         cudaFuncSetAttribute(k_gdn_chunk_prep<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_prep_smem<S>());
+        cudaFuncSetAttribute(k_gdn_chunk_solve<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_solve_smem<S>());
         cudaFuncSetAttribute(k_gdn_chunk<S>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)gdn_chunk_smem<S>());
         attr[dev & 63] = true;
     }
     const int nch = (g.T + GC_C - 1) / GC_C;
     launch(im, k_gdn_chunk_prep<S>, dim3(g.Hk, nch), dim3(256), gdn_prep_smem<S>(), g, qn, kn, kk, qk);
-    launch(im, k_gdn_chunk<S>, dim3(g.Hv, S / 16), dim3(256), gdn_chunk_smem<S>(), g, (const float *)qn, (const float *)kn,
-           (const float *)kk, (const float *)qk);
+    launch(im, k_gdn_chunk_solve<S>, dim3(g.Hv, nch), dim3(2 * S), gdn_solve_smem<S>(), g, (const float *)qn,
+           (const float *)kn, (const float *)kk, (const float *)qk, wx);
+    launch(im, k_gdn_chunk<S>, dim3(g.Hv, S / 16), dim3(256), gdn_chunk_smem<S>(), g, (const float *)wx);
     launch(im, k_gdn_gnorm<S>, dim3(g.T, g.Hv), dim3(S), 0, g);
 }
 bool gdn_chunked_ok(const xj_hparams *hp) { return hp->s_v == hp->s_k && (hp->s_k == 32 || hp->s_k == 64 || hp->s_k == 128); }
@@ -432,9 +435,9 @@ void launch_gdn(Impl *im, const xj_hparams *hp, Layer &Ly, int T, bool ck) {
     const GdnArgs g = gdn_args(im, hp, Ly, T, ck);
     if (!ck && T >= GC_MIN_T && im->gc_qn && gdn_chunked_ok(hp)) {
         switch (hp->s_k) {
-        case 32: launch_gdn_chunked<32>(im, g, im->gc_qn, im->gc_kn, im->gc_kk, im->gc_qk); return;
-        case 64: launch_gdn_chunked<64>(im, g, im->gc_qn, im->gc_kn, im->gc_kk, im->gc_qk); return;
-        default: launch_gdn_chunked<128>(im, g, im->gc_qn, im->gc_kn, im->gc_kk, im->gc_qk); return;
+        case 32: launch_gdn_chunked<32>(im, g, im->gc_qn, im->gc_kn, im->gc_kk, im->gc_qk, im->gc_wx); return;
+        case 64: launch_gdn_chunked<64>(im, g, im->gc_qn, im->gc_kn, im->gc_kk, im->gc_qk, im->gc_wx); return;
+        default: launch_gdn_chunked<128>(im, g, im->gc_qn, im->gc_kn, im->gc_kk, im->gc_qk, im->gc_wx); return;
         }
     }
     switch (hp->s_k) {
@@ -788,7 +791,8 @@ int build(xj_stage *s, char *err, size_t errlen) {
         const size_t nch = (size_t)(B + GC_C - 1) / GC_C;
         if (dalloc(im, &im->gc_qn, (size_t)B * hp->key_dim, err, errlen) || dalloc(im, &im->gc_kn, (size_t)B * hp->key_dim, err, errlen) ||
             dalloc(im, &im->gc_kk, (size_t)hp->h_k * nch * GC_C * GC_C, err, errlen) ||
-            dalloc(im, &im->gc_qk, (size_t)hp->h_k * nch * GC_C * GC_C, err, errlen)) return -1;
+            dalloc(im, &im->gc_qk, (size_t)hp->h_k * nch * GC_C * GC_C, err, errlen) ||
+            dalloc(im, &im->gc_wx, gc_wx_floats(B, hp->h_v, hp->s_v), err, errlen)) return -1;
     }
     if (s->has_head) {
         const size_t nt = (size_t)(m->output.ne1 + 15) / 16;
@@ -1742,7 +1746,7 @@ int xj_cuda_gdn_prefill_check(int S, int Hk, int Hv, int T, float *res, char *er
     const int key_dim = Hk * S, ldq = 2 * key_dim + Hv * S, nch = (T + GC_C - 1) / GC_C;
     const size_t ns = (size_t)Hv * S * S;
     float *qkv = nullptr, *z = nullptr, *ba = nullptr, *par = nullptr, *o1 = nullptr, *o2 = nullptr, *m1 = nullptr, *m2 = nullptr;
-    float *qn = nullptr, *kn = nullptr, *kk = nullptr, *qk = nullptr;
+    float *qn = nullptr, *kn = nullptr, *kk = nullptr, *qk = nullptr, *wx = nullptr;
     std::vector<float> h1, h2, s1, s2;
     if (cudaStreamCreateWithFlags(&im->st, cudaStreamNonBlocking) != cudaSuccess) { seterr(err, errlen, "no stream"); return -1; }
     if (dalloc(im, &qkv, (size_t)T * ldq, err, errlen) || dalloc(im, &z, (size_t)T * Hv * S, err, errlen) ||
@@ -1750,7 +1754,8 @@ int xj_cuda_gdn_prefill_check(int S, int Hk, int Hv, int T, float *res, char *er
         dalloc(im, &o1, (size_t)T * Hv * S, err, errlen) || dalloc(im, &o2, (size_t)T * Hv * S, err, errlen) ||
         dalloc(im, &m1, ns, err, errlen) || dalloc(im, &m2, ns, err, errlen) ||
         dalloc(im, &qn, (size_t)T * key_dim, err, errlen) || dalloc(im, &kn, (size_t)T * key_dim, err, errlen) ||
-        dalloc(im, &kk, (size_t)Hk * nch * GC_C * GC_C, err, errlen) || dalloc(im, &qk, (size_t)Hk * nch * GC_C * GC_C, err, errlen))
+        dalloc(im, &kk, (size_t)Hk * nch * GC_C * GC_C, err, errlen) || dalloc(im, &qk, (size_t)Hk * nch * GC_C * GC_C, err, errlen) ||
+        dalloc(im, &wx, gc_wx_floats(T, Hv, S), err, errlen))
         goto done;
     {
         // deterministic operands: q, k, v, z ~ U(-1, 1); beta, alpha logits ~ U(-2, 2); dt = 0.5;
@@ -1792,9 +1797,9 @@ int xj_cuda_gdn_prefill_check(int S, int Hk, int Hv, int T, float *res, char *er
         }
         cudaEventRecord(e[1], im->st);
         switch (S) {
-        case 32: launch_gdn_chunked<32>(im, gc, qn, kn, kk, qk); break;
-        case 64: launch_gdn_chunked<64>(im, gc, qn, kn, kk, qk); break;
-        default: launch_gdn_chunked<128>(im, gc, qn, kn, kk, qk); break;
+        case 32: launch_gdn_chunked<32>(im, gc, qn, kn, kk, qk, wx); break;
+        case 64: launch_gdn_chunked<64>(im, gc, qn, kn, kk, qk, wx); break;
+        default: launch_gdn_chunked<128>(im, gc, qn, kn, kk, qk, wx); break;
         }
         cudaEventRecord(e[2], im->st);
         if (cudaStreamSynchronize(im->st) != cudaSuccess || cudaGetLastError() != cudaSuccess) {
@@ -1847,7 +1852,7 @@ int xj_cuda_gdn_run(int path, int S, int Hk, int Hv, int T, const float *qkv, co
     const int key_dim = Hk * S, ldq = 2 * key_dim + Hv * S, nch = (T + GC_C - 1) / GC_C;
     const size_t ns = (size_t)Hv * S * S * (path == 2 ? T : 1);
     float *dq = nullptr, *dz = nullptr, *dba = nullptr, *dpar = nullptr, *dm = nullptr, *dout = nullptr;
-    float *qn = nullptr, *kn = nullptr, *kk = nullptr, *qk = nullptr;
+    float *qn = nullptr, *kn = nullptr, *kk = nullptr, *qk = nullptr, *wx = nullptr;
     if (cudaStreamCreateWithFlags(&im->st, cudaStreamNonBlocking) != cudaSuccess) { seterr(err, errlen, "no stream"); return -1; }
     if (dalloc(im, &dq, (size_t)T * ldq, err, errlen) || dalloc(im, &dz, (size_t)T * Hv * S, err, errlen) ||
         dalloc(im, &dba, (size_t)2 * T * Hv, err, errlen) || dalloc(im, &dpar, (size_t)2 * Hv + S, err, errlen) ||
@@ -1855,7 +1860,8 @@ int xj_cuda_gdn_run(int path, int S, int Hk, int Hv, int T, const float *qkv, co
         goto done;
     if (path == 1 && (dalloc(im, &qn, (size_t)T * key_dim, err, errlen) || dalloc(im, &kn, (size_t)T * key_dim, err, errlen) ||
                       dalloc(im, &kk, (size_t)Hk * nch * GC_C * GC_C, err, errlen) ||
-                      dalloc(im, &qk, (size_t)Hk * nch * GC_C * GC_C, err, errlen)))
+                      dalloc(im, &qk, (size_t)Hk * nch * GC_C * GC_C, err, errlen) ||
+                      dalloc(im, &wx, gc_wx_floats(T, Hv, S), err, errlen)))
         goto done;
     if (cudaMemcpy(dq, qkv, (size_t)T * ldq * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaMemcpy(dz, z, (size_t)T * Hv * S * 4, cudaMemcpyHostToDevice) != cudaSuccess ||
@@ -1882,9 +1888,9 @@ int xj_cuda_gdn_run(int path, int S, int Hk, int Hv, int T, const float *qkv, co
             }
         } else if (path == 1) {
             switch (S) {
-            case 32: launch_gdn_chunked<32>(im, g, qn, kn, kk, qk); break;
-            case 64: launch_gdn_chunked<64>(im, g, qn, kn, kk, qk); break;
-            default: launch_gdn_chunked<128>(im, g, qn, kn, kk, qk); break;
+            case 32: launch_gdn_chunked<32>(im, g, qn, kn, kk, qk, wx); break;
+            case 64: launch_gdn_chunked<64>(im, g, qn, kn, kk, qk, wx); break;
+            default: launch_gdn_chunked<128>(im, g, qn, kn, kk, qk, wx); break;
             }
         } else {
             const long long sstride = (long long)Hv * S * S;
