@@ -365,6 +365,33 @@ template <int S> constexpr size_t gdn_prep_smem() { return (size_t)2 * S * (GC_C
 // every chunk at once. Tokens past the prompt count as g = 0, b = 0, q = k = v = 0 (they change nothing).
 // Scratch wx, all [T][Hv][S]: W, Q', Kd, U0, O0; then e^(G_C) per [Hv][chunk].
 inline size_t gc_wx_floats(int T, int Hv, int S) { return (size_t)5 * T * Hv * S + (size_t)Hv * ((T + GC_C - 1) / GC_C); }
+// fp32 x = hi + lo with hi, lo tf32 (round to nearest): products of the two parts (hi*hi + hi*lo +
+// lo*hi, the lo*lo term dropped) carry about the precision of an fp32 product ("3xTF32").
+XJ_DEV uint32_t tf32_of(float x) {
+    uint32_t r;
+    asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+    return r;
+}
+XJ_DEV void tf32_split(float x, uint32_t &hi, uint32_t &lo) {
+    hi = tf32_of(x);
+    lo = tf32_of(x - __uint_as_float(hi));
+}
+// D (16 x 8, f32) += A (16 x 8, tf32, row) . B (8 x 8, tf32, col); fragments in the PTX ISA's m16n8k8
+// layout (lane = 4 g + c: a = A[g][c], A[g+8][c], A[g][c+4], A[g+8][c+4]; b = B[c][g], B[c+4][g];
+// d = D[g][2c], D[g][2c+1], D[g+8][2c], D[g+8][2c+1]).
+XJ_DEV void mma_tf32(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.tf32.tf32.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};"
+                 : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+                 : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+// The two small terms into ds, the large one into d (two accumulators: shorter dependent MMA chains).
+XJ_DEV void mma_3xtf32(float (&d)[4], float (&ds)[4], const uint32_t (&ah)[4], const uint32_t (&al)[4], uint32_t bh0,
+                       uint32_t bh1, uint32_t bl0, uint32_t bl1) {
+    mma_tf32(ds, al, bh0, bh1);
+    mma_tf32(d, ah, bh0, bh1);
+    mma_tf32(ds, ah, bl0, bl1);
+}
+
 template <int S> constexpr size_t gdn_solve_smem() { return ((size_t)2 * GC_C * (GC_C + 4) + 3 * GC_C * (S + 4)) * 4; }
 
 // Grid (Hv, nchunks), 2S threads: thread c < S takes column c of W and then of Q' (and of Kd), thread
@@ -475,34 +502,55 @@ __global__ void __launch_bounds__(2 * S) k_gdn_chunk_solve(GdnArgs a, const floa
         X[i * SP + c] = v;
         if (i < n) (wx + (isw ? 0 : 3 * plane))[((size_t)(t0 + i) * a.Hv + hv) * S + c] = v;
     }
-    // Q' = e^G q - D W (W threads), O0 = D U0 (U0 threads)
-    float *dst2 = wx + (isw ? plane : 4 * plane);
-    for (int i = 0; i < n; i++) {
-        float s0 = 0.0f, s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-        const float *dr = Dm + i * CP;
-#pragma unroll 2
-        for (int l = 0; l < ((i + 1) & ~3); l += 4) {
-            const float4 d4 = *reinterpret_cast<const float4 *>(dr + l);
-            s0 = fmaf(d4.x, X[l * SP + c], s0); s1 = fmaf(d4.y, X[(l + 1) * SP + c], s1);
-            s2 = fmaf(d4.z, X[(l + 2) * SP + c], s2); s3 = fmaf(d4.w, X[(l + 3) * SP + c], s3);
+    __syncthreads();                                       // every column of W and U0 is final
+    // Q' = e^G q - D W and O0 = D U0 on tensor cores (mma.sync m16n8k8 tf32, 3xTF32): task (product pr,
+    // 16-token tile mt) per warp in turn, 8 column tiles at a time; D is lower triangular, so the k-steps
+    // stop at the tile's diagonal block
+    {
+        constexpr int NWS = NT / 32, NTL = S / 8, NB = NTL < 8 ? NTL : 8;
+        const int g = lane >> 2, cq = lane & 3;
+        for (int task = warp; task < 8; task += NWS) {
+            const int pr = task >> 2, mt = task & 3;
+            const float *Xs = pr ? Xv : Xk;
+            float *dst = wx + (pr ? 4 * plane : plane);
+            for (int nb = 0; nb < NTL; nb += NB) {
+                float acc[NB][4] = {};
+                for (int k0 = 0; k0 < 16 * mt + 16; k0 += 8) {
+                    uint32_t ah[4], al[4];
+                    const int o0 = (16 * mt + g) * CP + k0 + cq, o1 = o0 + 8 * CP;
+                    tf32_split(Dm[o0], ah[0], al[0]);
+                    tf32_split(Dm[o1], ah[1], al[1]);
+                    tf32_split(Dm[o0 + 4], ah[2], al[2]);
+                    tf32_split(Dm[o1 + 4], ah[3], al[3]);
+#pragma unroll
+                    for (int j = 0; j < NB; j++) {
+                        const int col = 8 * (nb + j) + g;
+                        uint32_t bh0, bl0, bh1, bl1;
+                        tf32_split(Xs[(k0 + cq) * SP + col], bh0, bl0);
+                        tf32_split(Xs[(k0 + cq + 4) * SP + col], bh1, bl1);
+                        mma_tf32(acc[j], al, bh0, bh1);
+                        mma_tf32(acc[j], ah, bl0, bl1);
+                        mma_tf32(acc[j], ah, bh0, bh1);
+                    }
+                }
+#pragma unroll
+                for (int j = 0; j < NB; j++)
+#pragma unroll
+                    for (int e = 0; e < 4; e++) {
+                        const int i = 16 * mt + g + 8 * (e >> 1), col = 8 * (nb + j) + 2 * cq + (e & 1);
+                        if (i < n)
+                            dst[((size_t)(t0 + i) * a.Hv + hv) * S + col] = pr ? acc[j][e] : eG[i] * Xq[i * SP + col] - acc[j][e];
+                    }
+            }
         }
-        for (int l = (i + 1) & ~3; l <= i; l++) s0 = fmaf(dr[l], X[l * SP + c], s0);
-        const float sv = (s0 + s1) + (s2 + s3);
-        const size_t o = ((size_t)(t0 + i) * a.Hv + hv) * S + c;
-        dst2[o] = isw ? eG[i] * Xq[i * SP + c] - sv : sv;
     }
     if (tid == 0) wx[5 * plane + (size_t)hv * nch + ch] = eG[GC_C - 1];
 }
 
-constexpr int GC_RP = 20;         // row stride (floats) of the walk's 16-row column tiles (16-byte rows)
-template <int S> constexpr size_t gdn_chunk_smem() { return ((size_t)5 * GC_C * (S + 4) + 16 * (S + 4) + 5 * GC_C * GC_RP) * 4; }
-// State column of element e of a walk thread's P = S / 16 (cb: the thread's column block): groups of
-// four 64 apart when P is a multiple of 4 (conflict-free 16-byte shared loads), else P consecutive.
-template <int S>
-XJ_DEV int gdn_wcol(int cb, int e) {
-    constexpr int P = S / 16;
-    if constexpr (P % 4 == 0) return (e >> 2) * 64 + cb * 4 + (e & 3);
-    else return cb * P + e;
+constexpr int GC_RP = 20;         // row stride (floats) of the walk's U0 / O0 column tiles (16-byte rows)
+constexpr int GC_UP = GC_C + 4;   // row stride of u^T (16 state rows x the chunk's tokens)
+template <int S> constexpr size_t gdn_chunk_smem() {
+    return ((size_t)5 * GC_C * (S + 4) + 2 * 16 * (S + 4) + 4 * GC_C * GC_RP + 2 * 16 * GC_UP) * 4;
 }
 // 16 bytes global -> shared, asynchronously (zeros when !valid; src must still be a mapped address).
 XJ_DEV void gc_cp16(float *dst, const float *src, bool valid) {
@@ -512,25 +560,30 @@ XJ_DEV void gc_cp16(float *dst, const float *src, bool valid) {
 XJ_DEV void gc_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
 template <int N> XJ_DEV void gc_wait() { asm volatile("cp.async.wait_group %0;" :: "n"(N) : "memory"); }
 
-// Grid (Hv, S / 16), 256 threads: rows [16 r, 16 r + 16) of value head hv's state over all chunks, each
-// thread (row rr = tid / 16, column block cb = tid % 16) keeping P state columns of its row in registers.
-// Per chunk, from the solve kernel's rows: u = U0 - W M0^T and o = O0 + Q' M0^T (thread: token tid / 4,
-// rows tid % 4 + {0, 4, 8, 12}), then M = e^G_C M0 + u^T Kd. Raw outputs o (scaled by 1/sqrt(S), before
-// the gated norm) to out[t][hv*S + j]. The rows do not depend on the state, so they are copied in ahead:
-// W, Q', U0, O0 of chunk c + 1 (double-buffered) while chunk c computes, Kd of chunk c + 1 while chunk
-// c + 1 computes u and o (one commit group each, waited for in issue order).
+// Grid (Hv, S / 16), 256 threads (8 warps): rows [16 r, 16 r + 16) of value head hv's state over all
+// chunks, on tensor cores (mma.sync m16n8k8 tf32, 3xTF32 for fp32-level products). Per chunk, from the
+// solve kernel's rows:
+//   u = U0 - W M0^T, o = O0 + Q' M0^T   ([64 tokens x S] x [S x 16 rows]: warp w takes tokens 16 (w % 4)..
+//                                         of W (w < 4) or of Q' (w >= 4), both 8-row tiles)
+//   M = e^G_C M0 + u^T Kd               ([16 rows x 64 tokens] x [64 x S]: warp w < S / 16 takes state
+//                                         columns 16 w .. 16 w + 15 and keeps them as its accumulators)
+// The state's hi / lo tf32 parts and those of u^T go through shared memory once per chunk (every warp
+// reads them). Raw outputs o (scaled by 1/sqrt(S), before the gated norm) to out[t][hv*S + j]. The rows
+// do not depend on the state, so they are copied in ahead: W, Q', U0, O0 of chunk c + 1 (double-
+// buffered) while chunk c computes, Kd of chunk c + 1 while chunk c + 1 computes u and o (one commit
+// group each, waited for in issue order).
 template <int S>
 __global__ void __launch_bounds__(256) k_gdn_chunk(GdnArgs a, const float *wx) {
     griddep_wait();
     griddep_launch();   // successors may start their prologue; they wait for this grid before reading
-    constexpr int P = S / 16, SP = S + 4, RP = GC_RP;
+    constexpr int SP = S + 4, RP = GC_RP, UP = GC_UP, NW3 = S / 16;
     extern __shared__ __align__(16) float gsm[];
     float *Wb = gsm, *Qb = Wb + 2 * GC_C * SP, *Kc = Qb + 2 * GC_C * SP;   // [2][C][SP], [2][C][SP], [C][SP]
-    float *Ms = Kc + GC_C * SP;                                           // [16][SP]: the CTA's state rows
-    float *Ub = Ms + 16 * SP, *Ob = Ub + 2 * GC_C * RP, *Us = Ob + 2 * GC_C * RP;   // [2][C][RP] x2, [C][RP]
+    float *Mh = Kc + GC_C * SP, *Ml = Mh + 16 * SP;                      // [16][SP]: the state rows, tf32 hi / lo
+    float *Ub = Ml + 16 * SP, *Ob = Ub + 2 * GC_C * RP;                  // [2][C][RP]: U0, O0 (the CTA's rows)
+    float *Th = Ob + 2 * GC_C * RP, *Tl = Th + 16 * UP;                  // [16][UP]: u^T, tf32 hi / lo
     const int hv = blockIdx.x, r0 = blockIdx.y * 16;
-    const int tid = threadIdx.x, rr = tid >> 4, cb = tid & 15;
-    const int gi = tid >> 2, gr = tid & 3;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, g = lane >> 2, c = lane & 3;
     const int nch = (a.T + GC_C - 1) / GC_C;
     const size_t plane = (size_t)a.T * a.Hv * S;
     const float *Wg = wx, *Qg = wx + plane, *Kg = wx + 2 * plane, *Ug = wx + 3 * plane, *Og = wx + 4 * plane;
@@ -538,10 +591,10 @@ __global__ void __launch_bounds__(256) k_gdn_chunk(GdnArgs a, const float *wx) {
     auto stage_wq = [&](int ch, int b) {
         const int t0 = ch * GC_C, n = a.T - t0 < GC_C ? a.T - t0 : GC_C;
         for (int x = tid; x < GC_C * (S / 4); x += 256) {
-            const int i = x / (S / 4), c = (x % (S / 4)) * 4;
-            const size_t o = i < n ? ((size_t)(t0 + i) * a.Hv + hv) * S + c : 0;
-            gc_cp16(Wb + (b * GC_C + i) * SP + c, Wg + o, i < n);
-            gc_cp16(Qb + (b * GC_C + i) * SP + c, Qg + o, i < n);
+            const int i = x / (S / 4), cc = (x % (S / 4)) * 4;
+            const size_t o = i < n ? ((size_t)(t0 + i) * a.Hv + hv) * S + cc : 0;
+            gc_cp16(Wb + (b * GC_C + i) * SP + cc, Wg + o, i < n);
+            gc_cp16(Qb + (b * GC_C + i) * SP + cc, Qg + o, i < n);
         }
         for (int x = tid; x < GC_C * 4; x += 256) {
             const int i = x >> 2, q = (x & 3) * 4;
@@ -554,74 +607,139 @@ __global__ void __launch_bounds__(256) k_gdn_chunk(GdnArgs a, const float *wx) {
     auto stage_k = [&](int ch) {
         const int t0 = ch * GC_C, n = a.T - t0 < GC_C ? a.T - t0 : GC_C;
         for (int x = tid; x < GC_C * (S / 4); x += 256) {
-            const int i = x / (S / 4), c = (x % (S / 4)) * 4;
-            const size_t o = i < n ? ((size_t)(t0 + i) * a.Hv + hv) * S + c : 0;
-            gc_cp16(Kc + i * SP + c, Kg + o, i < n);
+            const int i = x / (S / 4), cc = (x % (S / 4)) * 4;
+            const size_t o = i < n ? ((size_t)(t0 + i) * a.Hv + hv) * S + cc : 0;
+            gc_cp16(Kc + i * SP + cc, Kg + o, i < n);
         }
         gc_commit();
     };
-    float m[P];
-    float *Mrow = a.ssm + (size_t)hv * S * S + (size_t)(r0 + rr) * S;
+    // the state columns of warp w < NW3 as m16n8 accumulators: tile j holds rows g, g + 8 and columns
+    // 16 w + 8 j + 2 c, + 1
+    float st[2][4];
+    float *Mbase = a.ssm + (size_t)hv * S * S + (size_t)r0 * S;
+    auto put_state = [&]() {   // hi / lo parts into Mh / Ml
 #pragma unroll
-    for (int e = 0; e < P; e++) m[e] = __ldcg(Mrow + gdn_wcol<S>(cb, e));
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const int o = (g + 8 * h) * SP + 16 * warp + 8 * j + 2 * c;
+                uint32_t h0, l0, h1, l1;
+                tf32_split(st[j][2 * h], h0, l0);
+                tf32_split(st[j][2 * h + 1], h1, l1);
+                *reinterpret_cast<float2 *>(Mh + o) = make_float2(__uint_as_float(h0), __uint_as_float(h1));
+                *reinterpret_cast<float2 *>(Ml + o) = make_float2(__uint_as_float(l0), __uint_as_float(l1));
+            }
+    };
+    if (warp < NW3) {
+#pragma unroll
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+                const float2 v = __ldcg(reinterpret_cast<const float2 *>(Mbase + (size_t)(g + 8 * h) * S + 16 * warp + 8 * j + 2 * c));
+                st[j][2 * h] = v.x;
+                st[j][2 * h + 1] = v.y;
+            }
+        put_state();
+    }
     const float qscale = 1.0f / sqrtf((float)S);
+    const int mt = warp & 3, pr = warp >> 2;            // products: token tile mt of W (pr 0) or Q' (pr 1)
     stage_wq(0, 0);
     stage_k(0);
     for (int ch = 0; ch < nch; ch++) {
         const int t0 = ch * GC_C, n = a.T - t0 < GC_C ? a.T - t0 : GC_C, b = ch & 1;
-        const float *Wc = Wb + b * GC_C * SP, *Qc = Qb + b * GC_C * SP, *Uc = Ub + b * GC_C * RP, *Oc = Ob + b * GC_C * RP;
+        const float *Xc = (pr ? Qb : Wb) + (b * GC_C + 16 * mt) * SP;
+        const float *Uc = Ub + b * GC_C * RP, *Oc = Ob + b * GC_C * RP;
         gc_wait<1>();                                      // this chunk's W, Q', U0, O0 (Kd may be in flight)
-#pragma unroll
-        for (int e = 0; e < P; e++) Ms[rr * SP + gdn_wcol<S>(cb, e)] = m[e];
         const float eGC = __ldcg(eGCg + (size_t)hv * nch + ch);
         __syncthreads();
         if (ch + 1 < nch) stage_wq(ch + 1, b ^ 1);         // that buffer's last reader was chunk ch - 1
-        // u and o of token gi, rows gr + 4x
-        float au[4] = {0.f, 0.f, 0.f, 0.f}, ao[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll 8
-        for (int c = 0; c < S; c += 4) {
-            const float4 w4 = *reinterpret_cast<const float4 *>(Wc + gi * SP + c);
-            const float4 q4 = *reinterpret_cast<const float4 *>(Qc + gi * SP + c);
+        // [16 tokens x S] x [S x 16 rows]; accumulators per k-step parity and term size, summed after
+        float acc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+        {
+            float pa[2][2][2][4] = {};
+#pragma unroll 2
+            for (int k0 = 0; k0 < S; k0 += 16) {
 #pragma unroll
-            for (int x = 0; x < 4; x++) {
-                const float4 m4 = *reinterpret_cast<const float4 *>(Ms + (gr + 4 * x) * SP + c);
-                au[x] = fmaf(w4.x, m4.x, fmaf(w4.y, m4.y, fmaf(w4.z, m4.z, fmaf(w4.w, m4.w, au[x]))));
-                ao[x] = fmaf(q4.x, m4.x, fmaf(q4.y, m4.y, fmaf(q4.z, m4.z, fmaf(q4.w, m4.w, ao[x]))));
+                for (int p = 0; p < 2; p++) {
+                    const int k = k0 + 8 * p;
+                    uint32_t ah[4], al[4];
+                    tf32_split(Xc[g * SP + k + c], ah[0], al[0]);
+                    tf32_split(Xc[(g + 8) * SP + k + c], ah[1], al[1]);
+                    tf32_split(Xc[g * SP + k + c + 4], ah[2], al[2]);
+                    tf32_split(Xc[(g + 8) * SP + k + c + 4], ah[3], al[3]);
+#pragma unroll
+                    for (int j = 0; j < 2; j++) {
+                        const int o = (8 * j + g) * SP + k + c;
+                        mma_3xtf32(pa[p][0][j], pa[p][1][j], ah, al, __float_as_uint(Mh[o]), __float_as_uint(Mh[o + 4]),
+                                   __float_as_uint(Ml[o]), __float_as_uint(Ml[o + 4]));
+                    }
+                }
             }
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) acc[j][e] = (pa[0][1][j][e] + pa[1][1][j][e]) + (pa[0][0][j][e] + pa[1][0][j][e]);
         }
 #pragma unroll
-        for (int x = 0; x < 4; x++) {
-            const int r = gr + 4 * x;
-            Us[gi * RP + r] = Uc[gi * RP + r] - au[x];
-            if (gi < n) a.out[(size_t)(t0 + gi) * a.ldo + hv * S + r0 + r] = (Oc[gi * RP + r] + ao[x]) * qscale;
-        }
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+            for (int e = 0; e < 4; e++) {
+                const int tok = 16 * mt + g + 8 * (e >> 1), row = 8 * j + 2 * c + (e & 1);
+                if (pr == 0) {
+                    uint32_t h, l;
+                    tf32_split(Uc[tok * RP + row] - acc[j][e], h, l);
+                    Th[row * UP + tok] = __uint_as_float(h);
+                    Tl[row * UP + tok] = __uint_as_float(l);
+                } else if (tok < n) {
+                    a.out[(size_t)(t0 + tok) * a.ldo + hv * S + r0 + row] = (Oc[tok * RP + row] + acc[j][e]) * qscale;
+                }
+            }
         // this chunk's Kd (issued before the next chunk's W, Q', U0, O0, if any)
         if (ch + 1 < nch) gc_wait<1>();
         else gc_wait<0>();
         __syncthreads();
-        // state at the chunk's end
+        // M = e^G_C M + u^T Kd: [16 rows x 64 tokens] x [64 tokens x 16 columns] per warp (rows and columns
+        // of u and Kd past the prompt are zero)
+        if (warp < NW3) {
+            float sm[2][4] = {};                           // the small terms of the 3xTF32 products
 #pragma unroll
-        for (int e = 0; e < P; e++) m[e] *= eGC;
-        for (int i = 0; i < n; i++) {
-            const float u = Us[i * RP + rr];
-            if constexpr (P % 4 == 0) {
+            for (int j = 0; j < 2; j++)
 #pragma unroll
-                for (int e = 0; e < P; e += 4) {
-                    const float4 k4 = *reinterpret_cast<const float4 *>(Kc + i * SP + gdn_wcol<S>(cb, e));
-                    m[e] = fmaf(u, k4.x, m[e]); m[e + 1] = fmaf(u, k4.y, m[e + 1]);
-                    m[e + 2] = fmaf(u, k4.z, m[e + 2]); m[e + 3] = fmaf(u, k4.w, m[e + 3]);
+                for (int e = 0; e < 4; e++) st[j][e] *= eGC;
+#pragma unroll 2
+            for (int k0 = 0; k0 < GC_C; k0 += 8) {
+                uint32_t ah[4], al[4];
+                const int o0 = g * UP + k0 + c, o1 = (g + 8) * UP + k0 + c;
+                ah[0] = __float_as_uint(Th[o0]); ah[1] = __float_as_uint(Th[o1]);
+                ah[2] = __float_as_uint(Th[o0 + 4]); ah[3] = __float_as_uint(Th[o1 + 4]);
+                al[0] = __float_as_uint(Tl[o0]); al[1] = __float_as_uint(Tl[o1]);
+                al[2] = __float_as_uint(Tl[o0 + 4]); al[3] = __float_as_uint(Tl[o1 + 4]);
+#pragma unroll
+                for (int j = 0; j < 2; j++) {
+                    const int col = 16 * warp + 8 * j + g;
+                    uint32_t bh0, bl0, bh1, bl1;
+                    tf32_split(Kc[(k0 + c) * SP + col], bh0, bl0);
+                    tf32_split(Kc[(k0 + c + 4) * SP + col], bh1, bl1);
+                    mma_3xtf32(st[j], sm[j], ah, al, bh0, bh1, bl0, bl1);
                 }
-            } else {
-#pragma unroll
-                for (int e = 0; e < P; e++) m[e] = fmaf(u, Kc[i * SP + gdn_wcol<S>(cb, e)], m[e]);
             }
+#pragma unroll
+            for (int j = 0; j < 2; j++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) st[j][e] += sm[j][e];
         }
-        __syncthreads();                                   // Kc, Us and Ms are consumed
+        __syncthreads();                                   // Kc, u^T and the old state parts are consumed
+        if (warp < NW3) put_state();
         if (ch + 1 < nch) stage_k(ch + 1);
     }
     gc_wait<0>();
+    if (warp < NW3)
 #pragma unroll
-    for (int e = 0; e < P; e++) Mrow[gdn_wcol<S>(cb, e)] = m[e];
+        for (int j = 0; j < 2; j++)
+#pragma unroll
+            for (int h = 0; h < 2; h++)
+                *reinterpret_cast<float2 *>(Mbase + (size_t)(g + 8 * h) * S + 16 * warp + 8 * j + 2 * c) =
+                    make_float2(st[j][2 * h], st[j][2 * h + 1]);
 }
 
 // Grid (T, Hv), S threads (S <= 1024): out[t][hv*S + j] = o * rsqrt(mean_j o^2 + eps) * norm_w[j] * silu(z),
