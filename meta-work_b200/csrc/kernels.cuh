@@ -392,11 +392,11 @@ XJ_DEV void mma_3xtf32(float (&d)[4], float (&ds)[4], const uint32_t (&ah)[4], c
     mma_tf32(ds, ah, bl0, bl1);
 }
 
-template <int S> constexpr size_t gdn_solve_smem() { return ((size_t)2 * GC_C * (GC_C + 4) + 3 * GC_C * (S + 4)) * 4; }
+template <int S> constexpr size_t gdn_solve_smem() { return ((size_t)3 * GC_C * (GC_C + 4) + 3 * GC_C * (S + 4)) * 4; }
 
-// Grid (Hv, nchunks), 2S threads: thread c < S takes column c of W and then of Q' (and of Kd), thread
-// S + c column c of U0 and then of O0. A column of (I + A)^-1 X needs only the same column's earlier
-// rows, so each thread solves its column on its own, in place in shared memory.
+// Grid (Hv, nchunks), 2S threads (S / 16 warps): the chunk's operands into shared memory, Kd, then
+// T = (I + A)^-1 by forward substitution (S / 32 threads per column), then the four products W, U0, Q',
+// O0 on tensor cores.
 template <int S>
 __global__ void __launch_bounds__(2 * S) k_gdn_chunk_solve(GdnArgs a, const float *qn, const float *kn, const float *kk,
                                                            const float *qk, float *wx) {
@@ -405,7 +405,8 @@ __global__ void __launch_bounds__(2 * S) k_gdn_chunk_solve(GdnArgs a, const floa
     constexpr int CP = GC_C + 4, SP = S + 4, NT = 2 * S;
     extern __shared__ __align__(16) float gsm[];
     float *Am = gsm, *Dm = Am + GC_C * CP;                  // [C][CP]: A (l < i), D (l <= i)
-    float *Xk = Dm + GC_C * CP, *Xv = Xk + GC_C * SP, *Xq = Xv + GC_C * SP;   // [C][SP]: k, v, q rows of the chunk
+    float *Tm = Dm + GC_C * CP;                             // [C][CP]: (I + A)^-1
+    float *Xk = Tm + GC_C * CP, *Xv = Xk + GC_C * SP, *Xq = Xv + GC_C * SP;   // [C][SP]: k, v, q rows of the chunk
     __shared__ float G[GC_C], bv[GC_C], eG[GC_C];
     const int hv = blockIdx.x, hk = hv % a.Hk, ch = blockIdx.y, nch = gridDim.y;
     const int t0 = ch * GC_C, n = a.T - t0 < GC_C ? a.T - t0 : GC_C;
@@ -483,24 +484,77 @@ __global__ void __launch_bounds__(2 * S) k_gdn_chunk_solve(GdnArgs a, const floa
         for (int i = 0; i < n; i++) kd[((size_t)(t0 + i) * a.Hv + hv) * S + tid] = expf(G[GC_C - 1] - G[i]) * Xk[i * SP + tid];
     }
     __syncthreads();
-    const bool isw = tid < S;
-    const int c = isw ? tid : tid - S;
-    float *X = isw ? Xk : Xv;
-    // column c of W (or U0) replaces column c of X in place, row by row (rows < i of the column are
-    // final when row i starts: one thread owns the column); four partial sums per row
-    for (int i = 0; i < GC_C; i++) {
-        float s0 = bv[i] * (isw ? eG[i] : 1.0f) * X[i * SP + c], s1 = 0.0f, s2 = 0.0f, s3 = 0.0f;
-        const float *ar = Am + i * CP;
-#pragma unroll 2
-        for (int l = 0; l < (i & ~3); l += 4) {
-            const float4 a4 = *reinterpret_cast<const float4 *>(ar + l);
-            s0 = fmaf(-a4.x, X[l * SP + c], s0); s1 = fmaf(-a4.y, X[(l + 1) * SP + c], s1);
-            s2 = fmaf(-a4.z, X[(l + 2) * SP + c], s2); s3 = fmaf(-a4.w, X[(l + 3) * SP + c], s3);
+    // T = (I + A)^-1 (unit lower triangular), row by row: T[i][cc] = -sum_{cc <= l < i} A[i][l] T[l][cc];
+    // TPC consecutive lanes per column split the sum (column cc's rows are written and read by its own
+    // lanes only, so a warp barrier orders them)
+    {
+        constexpr int TPC = NT / GC_C;
+        const int cc = tid / TPC, q = tid % TPC;
+        for (int i = 0; i < GC_C; i++) {
+            float s0 = 0.0f, s1 = 0.0f;
+            const float *ar = Am + i * CP;
+            int l = cc + q;
+            for (; l + TPC < i; l += 2 * TPC) {
+                s0 = fmaf(ar[l], Tm[l * CP + cc], s0);
+                s1 = fmaf(ar[l + TPC], Tm[(l + TPC) * CP + cc], s1);
+            }
+            if (l < i) s0 = fmaf(ar[l], Tm[l * CP + cc], s0);
+            float sum = s0 + s1;
+#pragma unroll
+            for (int o = TPC >> 1; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+            if (q == 0) Tm[i * CP + cc] = cc < i ? -sum : (cc == i ? 1.0f : 0.0f);
+            __syncwarp();
         }
-        for (int l = i & ~3; l < i; l++) s0 = fmaf(-ar[l], X[l * SP + c], s0);
-        const float v = (s0 + s1) + (s2 + s3);
-        X[i * SP + c] = v;
-        if (i < n) (wx + (isw ? 0 : 3 * plane))[((size_t)(t0 + i) * a.Hv + hv) * S + c] = v;
+    }
+    __syncthreads();
+    // W = T diag(b e^G) K and U0 = T diag(b) V on tensor cores (mma.sync m16n8k8 tf32, 3xTF32): task
+    // (product pr, 16-token tile mt); the row scales go into T's columns as the A fragments are formed.
+    // Every warp holds its tasks' whole rows (64 accumulators a thread) until all warps have read the k
+    // and v rows, then the results replace them in place.
+    {
+        constexpr int NWS = NT / 32, TPW = 8 / NWS, NTL = S / 8;
+        const int g = lane >> 2, cq = lane & 3;
+        float acc[TPW][NTL][4] = {};
+#pragma unroll
+        for (int tt = 0; tt < TPW; tt++) {
+            const int task = warp + tt * NWS, pr = task >> 2, mt = task & 3;
+            const float *Xs = pr ? Xv : Xk;
+            for (int k0 = 0; k0 < 16 * mt + 16; k0 += 8) {
+                const float sc0 = pr ? bv[k0 + cq] : bv[k0 + cq] * eG[k0 + cq];
+                const float sc1 = pr ? bv[k0 + cq + 4] : bv[k0 + cq + 4] * eG[k0 + cq + 4];
+                uint32_t ah[4], al[4];
+                const int o0 = (16 * mt + g) * CP + k0 + cq, o1 = o0 + 8 * CP;
+                tf32_split(Tm[o0] * sc0, ah[0], al[0]);
+                tf32_split(Tm[o1] * sc0, ah[1], al[1]);
+                tf32_split(Tm[o0 + 4] * sc1, ah[2], al[2]);
+                tf32_split(Tm[o1 + 4] * sc1, ah[3], al[3]);
+#pragma unroll
+                for (int j = 0; j < NTL; j++) {
+                    const int col = 8 * j + g;
+                    uint32_t bh0, bl0, bh1, bl1;
+                    tf32_split(Xs[(k0 + cq) * SP + col], bh0, bl0);
+                    tf32_split(Xs[(k0 + cq + 4) * SP + col], bh1, bl1);
+                    mma_tf32(acc[tt][j], al, bh0, bh1);
+                    mma_tf32(acc[tt][j], ah, bl0, bl1);
+                    mma_tf32(acc[tt][j], ah, bh0, bh1);
+                }
+            }
+        }
+        __syncthreads();                                   // every k and v row has been read
+#pragma unroll
+        for (int tt = 0; tt < TPW; tt++) {
+            const int task = warp + tt * NWS, pr = task >> 2, mt = task & 3;
+            float *Xs = pr ? Xv : Xk;
+            float *dst = wx + (pr ? 3 * plane : 0);
+#pragma unroll
+            for (int j = 0; j < NTL; j++)
+#pragma unroll
+                for (int e = 0; e < 4; e++) {
+                    const int i = 16 * mt + g + 8 * (e >> 1), col = 8 * j + 2 * cq + (e & 1);
+                    Xs[i * SP + col] = acc[tt][j][e];
+                    if (i < n) dst[((size_t)(t0 + i) * a.Hv + hv) * S + col] = acc[tt][j][e];
+                }
+        }
     }
     __syncthreads();                                       // every column of W and U0 is final
     // Q' = e^G q - D W and O0 = D U0 on tensor cores (mma.sync m16n8k8 tf32, 3xTF32): task (product pr,
