@@ -531,7 +531,7 @@ def main():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemv", type=int, default=1, help="run the config-1 GEMV microbenchmark on rank 0 (0: skip)")
-    ap.add_argument("--only", choices=["gemv", "trace"], default=None,
+    ap.add_argument("--only", choices=["gemv", "trace", "gdn"], default=None,
                     help="run only this microbenchmark (one GPU; e.g. under a profiler) and print its JSON")
     ap.add_argument("--gemv-types", default="q4_k,q6_k,q8_0")
     ap.add_argument("--gemv-shapes", default="all", help="'all' or 'lm' (the 151936 x 2048 LM head only)")
@@ -562,6 +562,11 @@ def main():
         return
     if args.only == "trace":
         print(json.dumps({"phase_trace": run_phase_trace(args)}))
+        return
+    if args.only == "gdn":
+        from xjb200 import xjcuda
+        peak, peak_kind = hbm_peak()
+        print(json.dumps({"gdn": run_gdn(xjcuda, peak, peak_kind)}))
         return
     if world > 1:
         import datetime
