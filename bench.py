@@ -268,6 +268,24 @@ def run_gdn(xjcuda, peak, peak_kind):
     return out
 
 
+def run_prefill(xjcuda, model, n_prompt):
+    """Prompt processing of one sequence (config 3, the bench's n_prompt-token prompt) on stages that take
+    the prompt in chunks of 8 tokens (the decode bench's stage: wide mma.sync GEMVs, token-by-token GDN)
+    and of 64 tokens (tcgen05 GEMMs, the chunked tensor-core GDN). Device time of the prompt's first
+    n_prompt - 1 tokens (the last one is the first decode step), second of two runs."""
+    p = np.random.default_rng(1234).integers(0, model.n_vocab, n_prompt).astype(np.int32)
+    out = {"prompt": n_prompt, "unit": "tok/s"}
+    for mb in (8, 64):
+        st = xjcuda.Stage(model, 0, model.n_layer, n_prompt + 16, mb)
+        ms = None
+        for _ in range(2):
+            st.reset()
+            _, _, ms = st.decode(p, 1)
+        st.close()
+        out[f"chunk_{mb}"] = {"ms": round(float(ms[0]), 3), "tok_s": round((n_prompt - 1) / (float(ms[0]) / 1e3), 1)}
+    return out
+
+
 GEMV_SHAPES = ((2048, 2048), (6144, 2048), (2048, 6144), (151936, 2048))   # rows N x columns K
 
 
@@ -691,6 +709,7 @@ def main():
         if pipe_line:
             line["pipeline"] = pipe_line
         line["gdn"] = run_gdn(xjcuda, peak, peak_kind)
+        line["prefill"] = run_prefill(xjcuda, model, args.prompt)
         # the same GDN step inside the persistent decode kernel (config 3 has 21 such layers of 16 heads x
         # 128x128): mean over its GDN phases of the slowest CTA, from a short traced decode
         tr = run_phase_trace(args)
