@@ -268,14 +268,14 @@ def run_gdn(xjcuda, peak, peak_kind):
     return out
 
 
-def run_prefill(xjcuda, model, n_prompt):
+def run_prefill(xjcuda, model, n_prompt, chunks=(8, 64)):
     """Prompt processing of one sequence (config 3, the bench's n_prompt-token prompt) on stages that take
     the prompt in chunks of 8 tokens (the decode bench's stage: wide mma.sync GEMVs, token-by-token GDN)
     and of 64 tokens (tcgen05 GEMMs, the chunked tensor-core GDN). Device time of the prompt's first
     n_prompt - 1 tokens (the last one is the first decode step), second of two runs."""
     p = np.random.default_rng(1234).integers(0, model.n_vocab, n_prompt).astype(np.int32)
     out = {"prompt": n_prompt, "unit": "tok/s"}
-    for mb in (8, 64):
+    for mb in chunks:
         st = xjcuda.Stage(model, 0, model.n_layer, n_prompt + 16, mb)
         ms = None
         for _ in range(2):
@@ -549,8 +549,9 @@ def main():
     ap.add_argument("--prompt", type=int, default=512)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--gemv", type=int, default=1, help="run the config-1 GEMV microbenchmark on rank 0 (0: skip)")
-    ap.add_argument("--only", choices=["gemv", "trace", "gdn"], default=None,
+    ap.add_argument("--only", choices=["gemv", "trace", "gdn", "prefill"], default=None,
                     help="run only this microbenchmark (one GPU; e.g. under a profiler) and print its JSON")
+    ap.add_argument("--prefill-chunks", default="8,64", help="prompt chunk sizes (stage max_batch) of the prefill leg")
     ap.add_argument("--gemv-types", default="q4_k,q6_k,q8_0")
     ap.add_argument("--gemv-shapes", default="all", help="'all' or 'lm' (the 151936 x 2048 LM head only)")
     ap.add_argument("--gemv-batches", default="1,4,16")
@@ -580,6 +581,12 @@ def main():
         return
     if args.only == "trace":
         print(json.dumps({"phase_trace": run_phase_trace(args)}))
+        return
+    if args.only == "prefill":
+        from xjb200 import synth, xjcuda
+        model = xjcuda.Model(synth.cached_gguf(synth.CONFIG3, os.environ.get("XJ_MODEL_DIR", f"/tmp/xj_models_r{local}")))
+        chunks = tuple(int(c) for c in args.prefill_chunks.split(","))
+        print(json.dumps({"prefill": run_prefill(xjcuda, model, args.prompt, chunks)}))
         return
     if args.only == "gdn":
         from xjb200 import xjcuda
@@ -709,7 +716,7 @@ def main():
         if pipe_line:
             line["pipeline"] = pipe_line
         line["gdn"] = run_gdn(xjcuda, peak, peak_kind)
-        line["prefill"] = run_prefill(xjcuda, model, args.prompt)
+        line["prefill"] = run_prefill(xjcuda, model, args.prompt, tuple(int(c) for c in args.prefill_chunks.split(",")))
         # the same GDN step inside the persistent decode kernel (config 3 has 21 such layers of 16 heads x
         # 128x128): mean over its GDN phases of the slowest CTA, from a short traced decode
         tr = run_phase_trace(args)

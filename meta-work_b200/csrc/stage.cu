@@ -485,12 +485,22 @@ void run_layers(xj_stage *s, int T, bool keep, int advance) {
     for (int il = s->l0; il < s->l1; il++) {
         Layer &Ly = im->L[il - s->l0];
         if (Ly.rec) {
-            const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v;
-            Job qkv{Ly.qkv, im->qkvb, CD};
-            qkv.epi = EPI_CONV; qkv.conv_state = Ly.conv; qkv.conv_w = Ly.conv_w; qkv.kc = hp->conv_k;
-            qkv.conv_ck = keep ? Ly.ck_conv : nullptr;
-            gemv(im, im->x, nullptr, E, T, PRO_NORM, Ly.attn_norm, eps,
-                 {qkv, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
+            const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v, kc = hp->conv_k;
+            if (T > MMA_WIDE_T && kc <= 9) {
+                // more than 16 tokens: the raw projections from the 17..64-token kernels (their epilogue
+                // has no conv carried across one sequence's tokens), then the conv over the tokens in place
+                gemv(im, im->x, nullptr, E, T, PRO_NORM, Ly.attn_norm, eps,
+                     {{Ly.qkv, im->qkvb, CD}, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
+                launch(im, k_conv_batch_multi, dim3((CD + 127) / 128, 1), dim3(128), 0, (const float *)im->qkvb,
+                       (long long)CD, im->qkvb, (long long)CD, Ly.conv, (const float *)Ly.conv_w, CD, kc, T,
+                       keep ? Ly.ck_conv : (float *)nullptr);
+            } else {
+                Job qkv{Ly.qkv, im->qkvb, CD};
+                qkv.epi = EPI_CONV; qkv.conv_state = Ly.conv; qkv.conv_w = Ly.conv_w; qkv.kc = kc;
+                qkv.conv_ck = keep ? Ly.ck_conv : nullptr;
+                gemv(im, im->x, nullptr, E, T, PRO_NORM, Ly.attn_norm, eps,
+                     {qkv, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
+            }
             launch_gdn(im, hp, Ly, T, keep);
             Job out{Ly.out, im->x, E};
             out.epi = EPI_ADD;
