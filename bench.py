@@ -268,11 +268,12 @@ def run_gdn(xjcuda, peak, peak_kind):
     return out
 
 
-def run_prefill(xjcuda, model, n_prompt, chunks=(8, 64)):
+def run_prefill(xjcuda, model, n_prompt, chunks=(8, 64, 512)):
     """Prompt processing of one sequence (config 3, the bench's n_prompt-token prompt) on stages that take
     the prompt in chunks of 8 tokens (the decode bench's stage: wide mma.sync GEMVs, token-by-token GDN)
-    and of 64 tokens (tcgen05 GEMMs, the chunked tensor-core GDN). Device time of the prompt's first
-    n_prompt - 1 tokens (the last one is the first decode step), second of two runs."""
+    and of 64 or 512 tokens (tcgen05 GEMMs in 64-token launches, the chunked tensor-core GDN). Device
+    time of the prompt's first n_prompt - 1 tokens (the last one is the first decode step), second of
+    two runs."""
     p = np.random.default_rng(1234).integers(0, model.n_vocab, n_prompt).astype(np.int32)
     out = {"prompt": n_prompt, "unit": "tok/s"}
     for mb in chunks:
@@ -551,7 +552,7 @@ def main():
     ap.add_argument("--gemv", type=int, default=1, help="run the config-1 GEMV microbenchmark on rank 0 (0: skip)")
     ap.add_argument("--only", choices=["gemv", "trace", "gdn", "prefill"], default=None,
                     help="run only this microbenchmark (one GPU; e.g. under a profiler) and print its JSON")
-    ap.add_argument("--prefill-chunks", default="8,64", help="prompt chunk sizes (stage max_batch) of the prefill leg")
+    ap.add_argument("--prefill-chunks", default="8,64,512", help="prompt chunk sizes (stage max_batch) of the prefill leg")
     ap.add_argument("--gemv-types", default="q4_k,q6_k,q8_0")
     ap.add_argument("--gemv-shapes", default="all", help="'all' or 'lm' (the 151936 x 2048 LM head only)")
     ap.add_argument("--gemv-batches", default="1,4,16")

@@ -4,7 +4,7 @@ bench.py's 512-token batch-1 prompt). The expected values are the reference's CP
 
 * 64 greedy ids after the 512-token prompt, through device decode with the persistent kernel and with the
   per-phase kernels, on a stage shaped like the bench's (prompt chunks of 8), and with the prompt in
-  chunks of 64 (tensor-core prompt path);
+  chunks of 64 or 512 (tensor-core prompt path);
 * activations after every layer and the logits of the first decode step (position 512) through chained
   one-layer stages driven by the vtable with host buffers, within 1e-2 relative (the fp16 KV cache);
 * a batch of 64 sequences whose sequence 0 holds the same prompt.
@@ -58,12 +58,13 @@ def test_config3_64_greedy_steps_after_512_prompt(c3, model, persist):
     assert np.allclose(mar, c3["c3_margins"], rtol=0.05, atol=5e-3), (persist, np.abs(mar - c3["c3_margins"]).max())
 
 
-def test_config3_prompt_in_64_token_chunks(c3, model):
-    """The same prompt on a stage taking it 64 tokens at a time: the tcgen05 GEMMs and the chunked
+@pytest.mark.parametrize("chunk", [64, 512])
+def test_config3_prompt_in_large_chunks(c3, model, chunk):
+    """The same prompt on a stage taking it 64 or 512 tokens at a time: the tcgen05 GEMMs and the chunked
     tensor-core Gated DeltaNet for the prompt, then the persistent kernel, with the reference's 64 ids."""
     from xjb200 import xjcuda
     xjcuda.set_option(xjcuda.OPT_PERSIST, 1)
-    s = xjcuda.Stage(model, 0, model.n_layer, C3_N_CTX, 64)
+    s = xjcuda.Stage(model, 0, model.n_layer, C3_N_CTX, chunk)
     toks, mar, _ = s.decode(c3["c3_prompt"], C3_N_GEN, want_margins=True)
     s.close()
     assert toks.tolist() == c3["c3_tokens"].tolist()
