@@ -1161,34 +1161,72 @@ __global__ void __launch_bounds__(4 * S, 2) k_gdn_batch_multi(GdnArgs a, long lo
     gdn_head<S, BarBlock>(c, blockIdx.x, threadIdx.x);
 }
 
-// Grid (ceil(CD / 128), B), 128 threads: channel ch of sequence b takes the raw projections of its T
-// tokens in order through its rolling conv state, with the arithmetic of the GEMV conv epilogue
-// (y = silu(sum_k state_k w_k + raw w_last), core/xj_cpu.c:167-176). ck (may be null): the state after
-// token t < T-1 at ck[b][t][CD][kc-1]. kc <= 9.
-static __global__ void __launch_bounds__(128) k_conv_batch_multi(const float *raw, long long ldr, float *y, long long ldy,
-                                                                 float *state, const float *w, int CD, int kc, int T,
-                                                                 float *ck) {
+// The conv + SiLU of T tokens of each of B sequences (rows b*T + t) from their raw projections, with the
+// arithmetic of the GEMV conv epilogue (y = silu(sum_k state_k w_k + raw w_last), core/xj_cpu.c:167-176).
+// y_t depends only on the raw projections of tokens t - kc + 1 .. t (the conv state stands for the
+// tokens before the forward), so every token is computed at once. Grid (ceil(CD / 128), B, ceil(T /
+// GC_CT)), 128 threads: channel ch of sequence b, tokens t0 .. t0 + GC_CT - 1. ck (may be null): the
+// state after token t < T-1 at ck[b][t][CD][kc-1]. kc <= 9. The state is only read here; k_conv_state
+// then moves it past the forward's tokens.
+constexpr int GC_CT = 16;
+static __global__ void __launch_bounds__(128) k_conv_tokens(const float *raw, long long ldr, float *y, long long ldy,
+                                                            const float *state, const float *w, int CD, int kc, int T,
+                                                            float *ck) {
+    griddep_wait();
+    griddep_launch();   // successors may start their prologue; they wait for this grid before reading
+    const int ch = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y, t0 = blockIdx.z * GC_CT;
+    if (ch >= CD) return;
+    const float *st = state + ((size_t)b * CD + ch) * (kc - 1);
+    float wc[9], win[GC_CT + 8];       // win[j]: raw value of token t0 - (kc - 1) + j
+#pragma unroll
+    for (int k = 0; k < 9; k++) wc[k] = k < kc ? w[(size_t)ch * kc + k] : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 8; j++) {
+        const int tt = t0 - (kc - 1) + j;
+        win[j] = j >= kc - 1 ? 0.0f : tt >= 0 ? raw[((size_t)b * T + tt) * ldr + ch] : st[tt + kc - 1];
+    }
+#pragma unroll
+    for (int i = 0; i < GC_CT; i++) {
+        const int t = t0 + i;
+        const float v = t < T ? raw[((size_t)b * T + t) * ldr + ch] : 0.0f;
+#pragma unroll
+        for (int j = 0; j < 9; j++)
+            if (j == kc - 1) win[i + j] = v;
+    }
+#pragma unroll
+    for (int i = 0; i < GC_CT; i++) {
+        const int t = t0 + i;
+        if (t >= T) break;
+        float acc = 0.0f;
+#pragma unroll
+        for (int k = 0; k < 8; k++)
+            if (k < kc - 1) acc = fmaf(win[i + k], wc[k], acc);
+        float wl = wc[0], xl = win[i];
+#pragma unroll
+        for (int k = 1; k < 9; k++)
+            if (k == kc - 1) { wl = wc[k]; xl = win[i + k]; }
+        acc = fmaf(xl, wl, acc);
+        y[((size_t)b * T + t) * ldy + ch] = silu_f(acc);
+        if (ck && t < T - 1)
+#pragma unroll
+            for (int k = 0; k < 8; k++)
+                if (k < kc - 1) ck[(((size_t)b * (T - 1) + t) * CD + ch) * (kc - 1) + k] = win[i + 1 + k];
+    }
+}
+
+// Grid (ceil(CD / 128), B), 128 threads: the conv state of channel ch of sequence b after the forward's
+// T tokens (the last kc - 1 raw projections, older state entries when T < kc - 1).
+static __global__ void __launch_bounds__(128) k_conv_state(const float *raw, long long ldr, float *state, int CD, int kc,
+                                                           int T) {
     griddep_wait();
     griddep_launch();   // successors may start their prologue; they wait for this grid before reading
     const int ch = blockIdx.x * blockDim.x + threadIdx.x, b = blockIdx.y;
     if (ch >= CD) return;
     float *st = state + ((size_t)b * CD + ch) * (kc - 1);
-    const float *wc = w + (size_t)ch * kc;
-    float cs[8];
-    for (int k = 0; k < kc - 1; k++) cs[k] = st[k];
-    for (int t = 0; t < T; t++) {
-        const size_t row = (size_t)b * T + t;
-        const float s = raw[row * ldr + ch];
-        float acc = 0.0f;
-        for (int k = 0; k < kc - 1; k++) acc = fmaf(cs[k], wc[k], acc);
-        acc = fmaf(s, wc[kc - 1], acc);
-        for (int k = 0; k < kc - 2; k++) cs[k] = cs[k + 1];
-        cs[kc - 2] = s;
-        y[row * ldy + ch] = silu_f(acc);
-        if (ck && t < T - 1)
-            for (int k = 0; k < kc - 1; k++) ck[(((size_t)b * (T - 1) + t) * CD + ch) * (kc - 1) + k] = cs[k];
+    for (int k = 0; k < kc - 1; k++) {                     // ascending: st[k + T] is read before it is written
+        const int tt = T - (kc - 1) + k;
+        st[k] = tt >= 0 ? raw[((size_t)b * T + tt) * ldr + ch] : st[k + T];
     }
-    for (int k = 0; k < kc - 1; k++) st[k] = cs[k];
 }
 
 // Grid (blocks, B), 256 threads: sequence b keeps the first keep[b] (1..T) tokens of its last T-token

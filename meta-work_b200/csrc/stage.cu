@@ -80,6 +80,7 @@ struct Impl {
     void *tc_buf = nullptr;     // the same in the tensor-core operand layout (k_gemm_tc)
     // chunked GDN (prompt forwards of >= GC_MIN_T tokens): normalised q, k and the chunk products
     float *gc_qn = nullptr, *gc_kn = nullptr, *gc_kk = nullptr, *gc_qk = nullptr, *gc_wx = nullptr;
+    float *conv_raw = nullptr;    // [max_batch][conv_dim] raw qkv projections of prompts of 17+ tokens
     float *pbest = nullptr, *psecond = nullptr;
     int *pidx = nullptr;
     int *derr = nullptr;       // device error word: set when a kernel's bounded wait gives up
@@ -486,14 +487,16 @@ void run_layers(xj_stage *s, int T, bool keep, int advance) {
         Layer &Ly = im->L[il - s->l0];
         if (Ly.rec) {
             const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v, kc = hp->conv_k;
-            if (T > MMA_WIDE_T && kc <= 9) {
+            if (T > MMA_WIDE_T && kc <= 9 && im->conv_raw) {
                 // more than 16 tokens: the raw projections from the 17..64-token kernels (their epilogue
-                // has no conv carried across one sequence's tokens), then the conv over the tokens in place
+                // has no conv carried across one sequence's tokens), then the conv over all tokens at once
                 gemv(im, im->x, nullptr, E, T, PRO_NORM, Ly.attn_norm, eps,
-                     {{Ly.qkv, im->qkvb, CD}, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
-                launch(im, k_conv_batch_multi, dim3((CD + 127) / 128, 1), dim3(128), 0, (const float *)im->qkvb,
-                       (long long)CD, im->qkvb, (long long)CD, Ly.conv, (const float *)Ly.conv_w, CD, kc, T,
-                       keep ? Ly.ck_conv : (float *)nullptr);
+                     {{Ly.qkv, im->conv_raw, CD}, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
+                launch(im, k_conv_tokens, dim3((CD + 127) / 128, 1, (T + GC_CT - 1) / GC_CT), dim3(128), 0,
+                       (const float *)im->conv_raw, (long long)CD, im->qkvb, (long long)CD, (const float *)Ly.conv,
+                       (const float *)Ly.conv_w, CD, kc, T, keep ? Ly.ck_conv : (float *)nullptr);
+                launch(im, k_conv_state, dim3((CD + 127) / 128, 1), dim3(128), 0, (const float *)im->conv_raw,
+                       (long long)CD, Ly.conv, CD, kc, T);
             } else {
                 Job qkv{Ly.qkv, im->qkvb, CD};
                 qkv.epi = EPI_CONV; qkv.conv_state = Ly.conv; qkv.conv_w = Ly.conv_w; qkv.kc = kc;
@@ -796,7 +799,8 @@ int build(xj_stage *s, char *err, size_t errlen) {
         dalloc(im, &im->npast, 4, err, errlen) || dalloc(im, &im->step, 4, err, errlen) ||
         dalloc(im, &im->derr, 4, err, errlen) ||
         dalloc(im, &im->tok, (size_t)B, err, errlen) || dalloc(im, &im->cur, 4, err, errlen)) return -1;
-    if (B > MMA_WIDE_T && alloc_b64(im, err, errlen)) return -1;
+    if (B > MMA_WIDE_T && (alloc_b64(im, err, errlen) ||
+                           (hp->conv_dim > 0 && dalloc(im, &im->conv_raw, (size_t)B * hp->conv_dim, err, errlen)))) return -1;
     if (B >= GC_MIN_T && gdn_chunked_ok(hp)) {
         const size_t nch = (size_t)(B + GC_C - 1) / GC_C;
         if (dalloc(im, &im->gc_qn, (size_t)B * hp->key_dim, err, errlen) || dalloc(im, &im->gc_kn, (size_t)B * hp->key_dim, err, errlen) ||
@@ -1172,9 +1176,11 @@ void run_layers_batch_multi(BatchImpl *bi, float *x, int T, bool ck, int advance
             const int CD = hp->conv_dim, DI = hp->d_inner, Hv = hp->h_v, kc = hp->conv_k;
             gemv(im, x, nullptr, E, R, PRO_NORM, Ly.attn_norm, eps,
                  {{Ly.qkv, bi->conv_raw, CD}, {Ly.gate, im->z, DI}, {Ly.beta, im->beta, Hv}, {Ly.alpha, im->alpha, Hv}});
-            launch(im, k_conv_batch_multi, dim3((CD + 127) / 128, B), dim3(128), 0, (const float *)bi->conv_raw,
-                   (long long)CD, im->qkvb, (long long)CD, bi->conv[li], (const float *)Ly.conv_w, CD, kc, T,
-                   ck ? bi->ck_conv[li] : (float *)nullptr);
+            launch(im, k_conv_tokens, dim3((CD + 127) / 128, B, (T + GC_CT - 1) / GC_CT), dim3(128), 0,
+                   (const float *)bi->conv_raw, (long long)CD, im->qkvb, (long long)CD, (const float *)bi->conv[li],
+                   (const float *)Ly.conv_w, CD, kc, T, ck ? bi->ck_conv[li] : (float *)nullptr);
+            launch(im, k_conv_state, dim3((CD + 127) / 128, B), dim3(128), 0, (const float *)bi->conv_raw, (long long)CD,
+                   bi->conv[li], CD, kc, T);
             GdnArgs g = gdn_args(im, hp, Ly, T, false);
             g.ssm = bi->ssm[li];
             g.ck_ssm = ck ? bi->ck_ssm[li] : nullptr;
