@@ -687,6 +687,9 @@ constexpr int TC_PLANE_X = TC_T * TC_CK * 2;
 constexpr int TC_PLANE_S = TC_T * 16 * 2;            // one block-sum plane (2 KB)
 constexpr int TC_REC = 2 * TC_PLANE_X + 2 * TC_PLANE_S;
 inline size_t tc_x_bytes(int K) { return (size_t)(K / TC_CK) * TC_REC + TC_T * 4 + 256; }
+// A forward of more than 64 tokens prepares all of them in one launch: token t goes to 64-token chunk
+// t / 64, whose records start TC_XSTRIDE bytes after the previous chunk's (room for the longest row).
+constexpr size_t TC_XSTRIDE = (((size_t)(MMA_KMAX_PT * MMA_WARPS * 32 / TC_CK) * TC_REC + TC_T * 4 + 256) + 1023) / 1024 * 1024;
 __host__ __device__ inline uint32_t tc_xoff(int t, int k) {   // byte of (token t, element k) in a plane
     return (uint32_t)((((t >> 3) * (TC_CK >> 3) + (k >> 3)) << 7) + ((t & 7) << 4) + ((k & 7) << 1));
 }
@@ -697,7 +700,8 @@ enum { PREP_WIDE = 0, PREP_B64 = 1, PREP_TC = 2 };
 
 // Grid T, MMA_WARPS*32 threads: f(x[t]) -> range scale -> hi/lo columns + block sums of token t, in the
 // wide layout (PREP_WIDE), the 64-token chunk layout (PREP_B64) or the tensor-core operand layout
-// (PREP_TC, no block sums); the values are the same.
+// (PREP_TC, no block sums; token t in 64-token chunk t / 64 at TC_XSTRIDE bytes per chunk); the values
+// are the same.
 template <int L>
 static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_xt(const float *x, const float *x2, long long ldx, int K, int pro,
                                                                    const float *norm_w, float eps, void *buf, int T) {
@@ -707,6 +711,8 @@ static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_xt(const float *
     __shared__ float s_scale, s_nsc;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, t = blockIdx.x;
     const WideX W = wide_x_of(buf, T, K);
+    uint8_t *tcb = (uint8_t *)buf + (size_t)(t / TC_T) * TC_XSTRIDE;   // PREP_TC: this token's chunk
+    const int tt = t % TC_T;                                          // PREP_TC: its row in the chunk
     const int xstride = K + 16;
     constexpr int XPT = MMA_KMAX_PT;
     const float *xr = x + t * ldx;
@@ -739,7 +745,7 @@ static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_xt(const float *
         s_nsc = nsc;
         s_scale = ldexpf(1.0f, 14 - (m > 0.0f ? ilogbf(m) : 0));
         if (L == PREP_B64) reinterpret_cast<float *>((uint8_t *)buf + (size_t)(K / B64_CK) * b64_rec_bytes(T))[t] = s_scale;
-        else if (L == PREP_TC) reinterpret_cast<float *>((uint8_t *)buf + (size_t)(K / TC_CK) * TC_REC)[t] = s_scale;
+        else if (L == PREP_TC) reinterpret_cast<float *>(tcb + (size_t)(K / TC_CK) * TC_REC)[tt] = s_scale;
         else W.scale[t] = s_scale;
     }
     __syncthreads();
@@ -754,9 +760,9 @@ static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_xt(const float *
             const __half lo = __float2half_rn(val - __half2float(hi));
             const float bs = warp_sum(__half2float(hi) + __half2float(lo));
             if (L == PREP_TC) {
-                uint8_t *rec = (uint8_t *)buf + (size_t)(i / TC_CK) * TC_REC;
+                uint8_t *rec = tcb + (size_t)(i / TC_CK) * TC_REC;
                 const int ci = i & (TC_CK - 1);
-                const uint32_t o = tc_xoff(t, ci);
+                const uint32_t o = tc_xoff(tt, ci);
                 *reinterpret_cast<__half *>(rec + o) = hi;
                 *reinterpret_cast<__half *>(rec + TC_PLANE_X + o) = lo;
                 if (lane == 0) {   // this warp's 32 elements are one block: its scaled sum as (Sh, Sl, Sh)
@@ -764,9 +770,9 @@ static __global__ void __launch_bounds__(MMA_WARPS * 32) k_prep_xt(const float *
                     const int b = (ci >> 5) & 1;
                     const float sv = bs * 0.015625f;
                     const __half sh = __float2half_rn(sv), sl = __float2half_rn(sv - __half2float(sh));
-                    *reinterpret_cast<__half *>(sp + tc_soff(t, 3 * b)) = sh;
-                    *reinterpret_cast<__half *>(sp + tc_soff(t, 3 * b + 1)) = sl;
-                    *reinterpret_cast<__half *>(sp + tc_soff(t, 3 * b + 2)) = sh;
+                    *reinterpret_cast<__half *>(sp + tc_soff(tt, 3 * b)) = sh;
+                    *reinterpret_cast<__half *>(sp + tc_soff(tt, 3 * b + 1)) = sl;
+                    *reinterpret_cast<__half *>(sp + tc_soff(tt, 3 * b + 2)) = sh;
                 }
                 continue;
             }

@@ -77,7 +77,8 @@ struct Impl {
     float *q = nullptr, *k = nullptr, *v = nullptr, *hn = nullptr;
     void *wide_buf = nullptr;   // activations of a wide (5..16-token) GEMV launch, prepared by k_prep_xt<PREP_WIDE>
     void *b64_buf = nullptr;    // activations of a 64-token GEMV launch (stages taking more than 16 tokens)
-    void *tc_buf = nullptr;     // the same in the tensor-core operand layout (k_gemm_tc)
+    void *tc_buf = nullptr;     // the same in the tensor-core operand layout (k_gemm_tc), tc_nchunk chunks
+    int tc_nchunk = 0;
     // chunked GDN (prompt forwards of >= GC_MIN_T tokens): normalised q, k and the chunk products
     float *gc_qn = nullptr, *gc_kn = nullptr, *gc_kk = nullptr, *gc_qk = nullptr, *gc_wx = nullptr;
     float *conv_raw = nullptr;    // [max_batch][conv_dim] raw qkv projections of prompts of 17+ tokens
@@ -222,12 +223,15 @@ void launch(Impl *im, void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem
 }
 
 // Activations of the 64-token GEMV: 64 tokens at the longest K.
-int alloc_b64(Impl *im, char *err, size_t errlen) {
+// ntok: the most tokens of one forward (the tensor-core operand buffer holds that many, in 64-token chunks)
+int alloc_b64(Impl *im, int ntok, char *err, size_t errlen) {
+    const int nchunk = (ntok + TC_T - 1) / TC_T;
     if (dalloc(im, (uint8_t **)&im->b64_buf, b64_x_bytes(B64_T, MMA_KMAX), err, errlen) ||
-        dalloc(im, (uint8_t **)&im->tc_buf, tc_x_bytes(MMA_KMAX), err, errlen))
+        dalloc(im, (uint8_t **)&im->tc_buf, (size_t)nchunk * TC_XSTRIDE, err, errlen))
         return -1;
+    im->tc_nchunk = nchunk;
     // the block-sum planes' unused columns stay zero (the tensor cores multiply them)
-    CK(cudaMemset(im->tc_buf, 0, tc_x_bytes(MMA_KMAX)));
+    CK(cudaMemset(im->tc_buf, 0, (size_t)nchunk * TC_XSTRIDE));
     return 0;
 }
 
@@ -282,15 +286,21 @@ void gemv(Impl *im, const float *x, const float *x2, long long ldx, int T, int p
         for (int j = 0; j < m.njob; j++) usetc = usetc && tc_ok(m.job[j], K);
     if (usetc) {
         // tcgen05 tensor cores: weights decoded to fp16 pairs in shared memory, accumulators in TMEM
+        // every token's operands in one launch when the buffer holds all chunks, else chunk by chunk
+        const bool all = (T + TC_T - 1) / TC_T <= im->tc_nchunk;
+        if (all)
+            launch(im, k_prep_xt<PREP_TC>, dim3(T), dim3(MMA_WARPS * 32), 0, x, x2, ldx, K, pro, norm_w, eps, im->tc_buf, T);
         for (int t0 = 0; t0 < T; t0 += TC_T) {
             const int Tc = T - t0 < TC_T ? T - t0 : TC_T;
-            launch(im, k_prep_xt<PREP_TC>, dim3(Tc), dim3(MMA_WARPS * 32), 0, (const float *)(x + t0 * ldx),
-                   (const float *)(x2 ? x2 + t0 * ldx : nullptr), ldx, K, pro, norm_w, eps, im->tc_buf, Tc);
+            if (!all)
+                launch(im, k_prep_xt<PREP_TC>, dim3(Tc), dim3(MMA_WARPS * 32), 0, (const float *)(x + t0 * ldx),
+                       (const float *)(x2 ? x2 + t0 * ldx : nullptr), ldx, K, pro, norm_w, eps, im->tc_buf, Tc);
             for (size_t gi = 0; gi < groups.size(); gi++) {
                 const MmaArgs &m = groups[gi];
                 B64Args b{};
                 b.njob = m.njob; b.T = Tc; b.K = K;
-                b.xbuf = im->tc_buf; b.err = im->derr;
+                b.xbuf = all ? (void *)((uint8_t *)im->tc_buf + (size_t)(t0 / TC_T) * TC_XSTRIDE) : im->tc_buf;
+                b.err = im->derr;
                 for (int j = 0; j < m.njob; j++) {
                     b.job[j] = m.job[j];
                     if (b.job[j].y) b.job[j].y = m.job[j].y + t0 * m.job[j].ldy;
@@ -799,7 +809,7 @@ int build(xj_stage *s, char *err, size_t errlen) {
         dalloc(im, &im->npast, 4, err, errlen) || dalloc(im, &im->step, 4, err, errlen) ||
         dalloc(im, &im->derr, 4, err, errlen) ||
         dalloc(im, &im->tok, (size_t)B, err, errlen) || dalloc(im, &im->cur, 4, err, errlen)) return -1;
-    if (B > MMA_WIDE_T && (alloc_b64(im, err, errlen) ||
+    if (B > MMA_WIDE_T && (alloc_b64(im, B, err, errlen) ||
                            (hp->conv_dim > 0 && dalloc(im, &im->conv_raw, (size_t)B * hp->conv_dim, err, errlen)))) return -1;
     if (B >= GC_MIN_T && gdn_chunked_ok(hp)) {
         const size_t nch = (size_t)(B + GC_C - 1) / GC_C;
@@ -1505,7 +1515,7 @@ static int gemv_diag(int type, const void *w, int k, int n, const float *x, int 
     if (dalloc(im, &dx, (size_t)t * k, err, errlen) || dalloc(im, &dy, (size_t)t * n, err, errlen) ||
         dalloc(im, &im->hn, (size_t)t * k, err, errlen) || dalloc(im, &im->derr, 1, err, errlen) ||
         dalloc(im, (uint8_t **)&im->wide_buf, wide_x_bytes(MMA_WIDE_T, MMA_KMAX), err, errlen) ||
-        (t > MMA_WIDE_T && alloc_b64(im, err, errlen))) goto done;
+        (t > MMA_WIDE_T && alloc_b64(im, t, err, errlen))) goto done;
     cudaMemset(im->derr, 0, sizeof(int));
     if (cudaMemcpy(dx, x, sizeof(float) * (size_t)t * k, cudaMemcpyHostToDevice) != cudaSuccess ||
         cudaDeviceSynchronize() != cudaSuccess) { seterr(err, errlen, "copy failed"); goto done; }
