@@ -280,8 +280,11 @@ XJ_DEV void gdn_head(const GdnArgs &a, int hv, int tid) {
 //   o_i = (e^G_i M0 q_i + sum_{l<=i} e^(G_i - G_l) (q_i . k_l) u_l) / sqrt(S)
 //   M_C = e^G_C M0 + sum_l e^(G_C - G_l) u_l k_l^T
 // which is the token-by-token update M = e^g M; u = (v - M k) b; M += u k^T; o = M q / sqrt(S) of
-// core/xj_cpu.c:194-219 regrouped (fp32 throughout; sums in another order, so results agree with the
-// sequential kernel to rounding). The gated RMSNorm of the outputs is a separate pass (k_gdn_gnorm).
+// core/xj_cpu.c:194-219 regrouped. The substitution is solved once per chunk and value head, for all
+// chunks at once, as a triangular inverse (k_gdn_chunk_solve), which leaves the walk over chunks
+// (k_gdn_chunk) three small matrix products per chunk. fp32 values, products as 3xTF32 on tensor cores,
+// sums in another order: results agree with the sequential kernel to rounding. The gated RMSNorm of the
+// outputs is a separate pass (k_gdn_gnorm).
 constexpr int GC_C = 64;          // tokens per chunk
 constexpr int GC_MIN_T = 32;      // forwards of at least this many tokens take the chunked path
 
